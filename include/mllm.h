@@ -1,0 +1,126 @@
+/*
+ * mllm.h — C ABI of the B200 Q4 decode backend for MicroLLM lab (libmllm_cuda.so).
+ *
+ * Plain pointers and sizes only.  Every entry point returns an mllm_status code; a message for the
+ * last failure is available from mllm_last_error(handle) (or mllm_last_error(NULL) for failures that
+ * happen before a handle exists).  The library never falls back to a CPU path: with no usable CUDA
+ * device mllm_create fails with MLLM_ERR_CUDA.
+ *
+ * Each entry point names the reference interface it replaces (paths relative to the reference
+ * project root).  The JavaScript engine surface those bind to is PetitGPT (engine/infer.js:289-647)
+ * and GpuPetitGPT (engine/webgpu.js:867-1297); INTEGRATION.md shows the Node-API binding.
+ */
+#ifndef MLLM_H
+#define MLLM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct mllm_engine mllm_engine;
+
+typedef enum {
+  MLLM_OK = 0,
+  MLLM_ERR_FORMAT = -1,      /* bad magic, truncated file, malformed tensor table */
+  MLLM_ERR_UNSUPPORTED = -2, /* dtype other than q4, head_dim != 64, shape beyond the kernel limits */
+  MLLM_ERR_ARG = -3,         /* token id out of range, position beyond maxSeqLen, bad slot, null pointer */
+  MLLM_ERR_OOM = -4,         /* device allocation failed */
+  MLLM_ERR_CUDA = -5,        /* CUDA runtime error (no device, launch failure, ...) */
+  MLLM_ERR_TIMEOUT = -6      /* a device-side wait ran out its time limit; the handle stays usable */
+} mllm_status;
+
+typedef enum { MLLM_STOP_EOS = 0, MLLM_STOP_MAX_NEW = 1, MLLM_STOP_CONTEXT = 2 } mllm_stop;
+
+/* Result of a generate call: engine/infer.js:617-645 and engine/webgpu.js:1272-1281. */
+typedef struct {
+  int32_t n_generated;  /* ids written to out_ids */
+  int32_t stop_reason;  /* mllm_stop */
+  int32_t spec_hits;    /* accepted draft tokens (specHits) */
+  int32_t spec_tries;   /* verify forwards that carried a draft (specTries) */
+  int32_t forwards;     /* forward passes run on the device, prefill chunks included */
+  int32_t prompt_len;   /* prompt length after truncation (engine/infer.js:604-608) */
+  float ttft_ms;        /* device time from launch to the first generated id */
+  float total_ms;       /* device time of the whole call */
+} mllm_stats;
+
+/*
+ * Load a PGW1 Q4 file and upload it to `device`.  Replaces parsePgw + new PetitGPT(bundle)
+ * (engine/weights.js:5-40, engine/infer.js:290-311) and GpuPetitGPT.init (engine/webgpu.js:892-1106).
+ * The buffer is only borrowed for the call.  `max_slots` independent sequences (KV caches) are
+ * allocated; `kv_len` caps each cache's positions (0 = the file's maxSeqLen).
+ */
+int mllm_create(int device, const uint8_t* pgw, size_t len, int max_slots, int kv_len, mllm_engine** out);
+
+/* engine/webgpu.js:1284-1297 (destroy). */
+void mllm_destroy(mllm_engine* e);
+
+/* Message of the last failure on this handle, or of the last failed mllm_create when e is NULL. */
+const char* mllm_last_error(const mllm_engine* e);
+
+/*
+ * Model configuration as parsed from the header (engine/weights.js:17-29):
+ * cfg[0..9] = arch (0 llama, 1 gpt2), vocabSize, nLayers, dModel, nHeads, nKvHeads, dFf, maxSeqLen,
+ * kv_len, max_tokens_per_forward.
+ */
+int mllm_config(const mllm_engine* e, int32_t* cfg10);
+
+/* Device bytes held by the handle (GpuPetitGPT.bytesAllocated, engine/webgpu.js:1047-1065). */
+size_t mllm_bytes_allocated(const mllm_engine* e);
+
+/* engine/infer.js:348-358 (resetCache) for one slot. */
+int mllm_reset(mllm_engine* e, int slot);
+
+/* engine/infer.js:357 (cacheLen) for one slot. */
+int mllm_cache_len(const mllm_engine* e, int slot);
+
+/*
+ * One forward over n host token ids at positions pos0 .. pos0+n-1 of `slot`, writing their K/V into
+ * the slot's cache and setting cacheLen = pos0 + n.  forwardPrompt(ids) is pos0 = 0
+ * (engine/infer.js:553-577); forwardDecode(id) is n = 1, pos0 = cacheLen (engine/infer.js:579-601);
+ * logits_each = 1 is the verify forward of engine/webgpu.js:1248 (one logits row per token).
+ * logits (nullable, host): [vocab] for the last token, or [n][vocab] when logits_each.
+ * argmax (nullable, host): greedy ids per returned logits row (engine/infer.js:240-250, lowest index
+ * on ties).
+ */
+int mllm_forward(mllm_engine* e, int slot, const int32_t* ids, int n, int pos0, int logits_each, float* logits,
+                 int32_t* argmax);
+
+/*
+ * Whole greedy generation in one device launch: engine/infer.js:603-646 when spec_k == 0, and the
+ * fused path with prompt-lookup speculation of engine/webgpu.js:1164-1282 (lookupDraft
+ * engine/webgpu.js:846-865) when spec_k > 0 (n-gram size `ngram`).  GPT-2 files use the penalised
+ * argmax of engine/infer.js:252-287.  eos = -1 disables the EOS stop.  ids/out_ids are host arrays;
+ * out_ids has room for max_new ids.  stats (nullable) receives the counters.
+ */
+int mllm_generate(mllm_engine* e, int slot, const int32_t* ids, int n, int max_new, int32_t eos, int spec_k,
+                  int ngram, int32_t* out_ids, mllm_stats* stats);
+
+/* mllm_generate with the prompt and the output already in device memory (d_ids: int32 [n],
+ * d_out: int32 [max_new]); stats stay host-side.  Used to time the device path without copies. */
+int mllm_generate_device(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max_new, int32_t eos,
+                         int spec_k, int ngram, int32_t* d_out, mllm_stats* stats);
+
+/*
+ * Failure-detection self-test (no counterpart in the reference): launches the decode kernel in a
+ * mode where every CTA waits for a word that nothing writes, with a `wait_ms` limit.  Expected
+ * result: MLLM_ERR_TIMEOUT, after which the handle keeps working.  Nothing faults or traps.
+ */
+int mllm_selftest_timeout(mllm_engine* e, int wait_ms);
+
+/*
+ * Q4 group-32 matrix-vector / skinny-matrix product y[m][r] = sum_g sc[r][g] * sum_k (q[r][32g+k]-8) x[m][32g+k]
+ * for m < n_act (engine/infer.js:88-116, engine/kernels.rs:60-97) on device pointers in the PGW
+ * layout: packed [rows][cols/2] bytes, scales [rows][cols/32] f32, x [n_act][cols], y [n_act][rows].
+ * fp32 accumulation.  n_act <= 16.  stream is a cudaStream_t (NULL = the device's default stream).
+ */
+int mllm_gemv_q4(const uint8_t* d_packed, const float* d_scales, const float* d_x, float* d_y, int rows, int cols,
+                 int n_act, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLLM_H */

@@ -1,0 +1,94 @@
+// Device helpers shared by the decode kernels: flag-in-data exchange words, bounded waits, Q4 dequant.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace mllm {
+
+constexpr int kThreads = 256;  // 8 warps per CTA
+constexpr int kWarps = kThreads / 32;
+constexpr int kHeadDim = 64;   // every supported model (PetitGPT, SmolLM2, GPT-2) uses 64
+constexpr unsigned long long kWaitNs = 500ull * 1000 * 1000;  // default per-wait limit: 0.5 s
+
+// ---------------------------------------------------------------------------------------------
+// Exchange words.  A produced value travels with a 32-bit tag in one 8-byte word; a consumer spins
+// until the tag equals the forward's tag.  8-byte aligned accesses are single-copy atomic, so no
+// fence or separate flag is needed between value and tag.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t ll_load(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void ll_store_word(uint64_t* p, uint64_t w) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ void ll_store(uint64_t* p, uint32_t tag, float v) {
+  ll_store_word(p, ((uint64_t)tag << 32) | __float_as_uint(v));
+}
+__device__ __forceinline__ void ll_store_u32(uint64_t* p, uint32_t tag, uint32_t v) {
+  ll_store_word(p, ((uint64_t)tag << 32) | v);
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait state of one CTA.  Every spin checks the clock every few rounds; when the limit passes, or
+// another CTA has raised the error flag, the wait gives up and the kernel returns.
+struct Waiter {
+  int* err;           // device-wide error flag (0 = ok)
+  uint64_t limit_ns;  // per-wait limit
+  __device__ __forceinline__ bool give_up(uint64_t start) const {
+    if (*(volatile int*)err) return true;
+    if (globaltimer() - start > limit_ns) {
+      atomicCAS(err, 0, 1);
+      return true;
+    }
+    return false;
+  }
+};
+
+// ---------------------------------------------------------------------------------------------
+// Q4 group-32 dequant.  A u32 word of a packed row holds 8 consecutive elements: byte b carries
+// element 2b in its low nibble and 2b+1 in its high nibble (tools/convert_hf_to_pgw.py:33).
+// (q - 8) is produced exactly in fp32 from the bit pattern 0x4B000000 | q (= 2^23 + q).
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float nib_at(uint32_t bytes4, int j) {
+  return __uint_as_float(__byte_perm(bytes4, 0x4B000000u, 0x7440u | (unsigned)j)) - 8388616.0f;
+}
+
+// sum_{e<8} (q_e - 8) * x[e], accumulated in element order.
+__device__ __forceinline__ float word_dot(uint32_t u, const float* x) {
+  const uint32_t lo = u & 0x0F0F0F0Fu, hi = (u >> 4) & 0x0F0F0F0Fu;
+  const float4 xa = *reinterpret_cast<const float4*>(x);
+  const float4 xb = *reinterpret_cast<const float4*>(x + 4);
+  float s = nib_at(lo, 0) * xa.x;
+  s = fmaf(nib_at(hi, 0), xa.y, s);
+  s = fmaf(nib_at(lo, 1), xa.z, s);
+  s = fmaf(nib_at(hi, 1), xa.w, s);
+  s = fmaf(nib_at(lo, 2), xb.x, s);
+  s = fmaf(nib_at(hi, 2), xb.y, s);
+  s = fmaf(nib_at(lo, 3), xb.z, s);
+  s = fmaf(nib_at(hi, 3), xb.w, s);
+  return s;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+}  // namespace mllm

@@ -1,0 +1,531 @@
+// Host runtime of the B200 Q4 decode backend: the C ABI declared in include/mllm.h.
+//
+// mllm_create  : engine/weights.js:5-40 parsePgw + engine/infer.js:290-336 binding + GpuPetitGPT.init
+//                (engine/webgpu.js:892-1106): Q4 matrices are uploaded in their PGW layout, f32 norms,
+//                biases and wpe as they are; the RoPE table is built like engine/infer.js:185-206.
+// mllm_forward : forwardPrompt / forwardDecode / the verify forward (engine/infer.js:553-601,
+//                engine/webgpu.js:1248).
+// mllm_generate: engine/infer.js:603-646 and engine/webgpu.js:1164-1282 in one device launch.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/mllm.h"
+#include "device_common.cuh"
+#include "engine.cuh"
+#include "pgw.hpp"
+
+namespace mllm {
+size_t decode_smem_bytes(const ModelDev& md, int mmax, int grid);
+typedef void (*DecodeFn)(const RunArgs);
+DecodeFn pick_decode_kernel(int D, int FF);
+}  // namespace mllm
+
+using namespace mllm;
+
+namespace {
+
+thread_local std::string g_create_error;
+
+struct Slot {
+  float* k = nullptr;
+  float* v = nullptr;
+  int cache_len = 0;
+};
+
+}  // namespace
+
+struct mllm_engine {
+  int device = 0;
+  PgwModel pgw;
+  ModelDev md{};
+  ExchangeDev ex{};
+  DecodeFn kernel = nullptr;
+  int grid = 0, mmax = 0;
+  size_t smem = 0;
+  cudaStream_t stream = nullptr;
+  std::vector<void*> allocs;
+  size_t bytes = 0;
+  std::vector<Slot> slots;
+  int32_t* d_ids = nullptr;   // [kv_len + 16]
+  int32_t* d_out = nullptr;   // [kv_len + 16]
+  int32_t* d_status = nullptr;
+  int* d_err = nullptr;
+  float* d_logits = nullptr;
+  size_t logits_cap = 0;      // floats
+  int32_t* d_argmax = nullptr;
+  int32_t* h_status = nullptr;  // pinned [ST_WORDS + 1]
+  uint32_t tag = 1;
+  std::string err;
+};
+
+namespace {
+
+int fail(mllm_engine* e, int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (e) e->err = buf;
+  else g_create_error = buf;
+  return code;
+}
+
+#define CUDA_TRY(e, call)                                                                             \
+  do {                                                                                                \
+    cudaError_t _st = (call);                                                                         \
+    if (_st != cudaSuccess) return fail(e, MLLM_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(_st)); \
+  } while (0)
+
+template <class T>
+int dev_alloc(mllm_engine* e, T** p, size_t bytes) {
+  void* q = nullptr;
+  bytes = std::max<size_t>(bytes, 16);
+  cudaError_t st = cudaMalloc(&q, bytes);
+  if (st != cudaSuccess) return fail(e, MLLM_ERR_OOM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(st));
+  e->allocs.push_back(q);
+  e->bytes += bytes;
+  *p = (T*)q;
+  return MLLM_OK;
+}
+
+#define TRY(x)                \
+  do {                        \
+    int _rc = (x);            \
+    if (_rc != MLLM_OK) return _rc; \
+  } while (0)
+
+const PgwTensor* tensor(const PgwModel& m, const std::string& name) {
+  auto it = m.tensors.find(name);
+  return it == m.tensors.end() ? nullptr : &it->second;
+}
+
+int upload_q4(mllm_engine* e, const uint8_t* buf, const std::string& name, int rows, int cols, Q4* out) {
+  const PgwTensor* t = tensor(e->pgw, name);
+  if (!t) return fail(e, MLLM_ERR_FORMAT, "missing tensor %s", name.c_str());
+  if (t->storage != "q4") return fail(e, MLLM_ERR_UNSUPPORTED, "%s is %s; this backend runs q4 only", name.c_str(), t->storage.c_str());
+  if (t->shape.size() != 2 || t->shape[0] != rows || t->shape[1] != cols)
+    return fail(e, MLLM_ERR_FORMAT, "%s has an unexpected shape", name.c_str());
+  if (t->group != 32) return fail(e, MLLM_ERR_UNSUPPORTED, "%s uses group %d; only 32 is supported", name.c_str(), t->group);
+  if (t->nbytes != (int64_t)rows * cols / 2 || t->scale_nbytes != (int64_t)rows * (cols / 32) * 4)
+    return fail(e, MLLM_ERR_FORMAT, "%s: byte counts do not match its shape", name.c_str());
+  uint32_t* w;
+  float* s;
+  TRY(dev_alloc(e, &w, t->nbytes));
+  TRY(dev_alloc(e, &s, t->scale_nbytes));
+  CUDA_TRY(e, cudaMemcpy(w, buf + e->pgw.payload_off + t->offset, t->nbytes, cudaMemcpyHostToDevice));
+  CUDA_TRY(e, cudaMemcpy(s, buf + e->pgw.payload_off + t->scale_offset, t->scale_nbytes, cudaMemcpyHostToDevice));
+  out->w = w;
+  out->s = s;
+  return MLLM_OK;
+}
+
+int upload_f32(mllm_engine* e, const uint8_t* buf, const std::string& name, int64_t count, const float** out,
+               bool optional = false) {
+  const PgwTensor* t = tensor(e->pgw, name);
+  if (!t) {
+    if (optional) {
+      *out = nullptr;
+      return MLLM_OK;
+    }
+    return fail(e, MLLM_ERR_FORMAT, "missing tensor %s", name.c_str());
+  }
+  if (t->storage != "f32") return fail(e, MLLM_ERR_UNSUPPORTED, "%s is %s, expected f32", name.c_str(), t->storage.c_str());
+  if (t->nbytes < count * 4) return fail(e, MLLM_ERR_FORMAT, "%s is shorter than expected", name.c_str());
+  float* d;
+  TRY(dev_alloc(e, &d, count * 4));
+  CUDA_TRY(e, cudaMemcpy(d, buf + e->pgw.payload_off + t->offset, count * 4, cudaMemcpyHostToDevice));
+  *out = d;
+  return MLLM_OK;
+}
+
+// engine/infer.js:185-206: f32 inverse frequencies, f64 cos/sin, f32 tables duplicated over halves.
+void build_rope(int max_seq, int head_dim, double theta, double pct, std::vector<float>* cs, std::vector<float>* sn,
+                int* rope_dim) {
+  int rd = (int)std::floor(head_dim * pct);
+  rd -= rd % 2;
+  const int half = rd / 2;
+  std::vector<float> inv(half);
+  for (int i = 0; i < half; ++i) inv[i] = (float)(1.0 / std::pow(theta, (double)(2 * i) / rd));
+  cs->assign((size_t)max_seq * std::max(rd, 1), 0.f);
+  sn->assign((size_t)max_seq * std::max(rd, 1), 0.f);
+  for (int t = 0; t < max_seq; ++t)
+    for (int i = 0; i < half; ++i) {
+      const double f = (double)t * inv[i];
+      const float c = (float)std::cos(f), s = (float)std::sin(f);
+      (*cs)[(size_t)t * rd + i] = c;
+      (*cs)[(size_t)t * rd + half + i] = c;
+      (*sn)[(size_t)t * rd + i] = s;
+      (*sn)[(size_t)t * rd + half + i] = s;
+    }
+  *rope_dim = rd;
+}
+
+int check_slot(mllm_engine* e, int slot) {
+  if (slot < 0 || slot >= (int)e->slots.size()) return fail(e, MLLM_ERR_ARG, "slot %d out of range [0, %zu)", slot, e->slots.size());
+  return MLLM_OK;
+}
+
+int launch(mllm_engine* e, RunArgs& a, int max_forwards) {
+  a.m = e->md;
+  a.x = e->ex;
+  a.mmax = e->mmax;
+  a.status = e->d_status;
+  a.err = e->d_err;
+  // Tags only grow; when the 32-bit space would wrap, clear every exchange word and restart at 1.
+  if ((uint64_t)e->tag + (uint64_t)max_forwards + 2 >= 0xFFFFFFF0ull) {
+    CUDA_TRY(e, cudaStreamSynchronize(e->stream));
+    const size_t L = e->md.n_layers, M = e->mmax;
+    CUDA_TRY(e, cudaMemset(e->ex.qkv, 0, L * M * e->ex.s_qkv * 8));
+    CUDA_TRY(e, cudaMemset(e->ex.att, 0, L * M * e->ex.s_d * 8));
+    CUDA_TRY(e, cudaMemset(e->ex.x1, 0, L * M * e->ex.s_d * 8));
+    CUDA_TRY(e, cudaMemset(e->ex.a, 0, L * M * e->ex.s_ff * 8));
+    CUDA_TRY(e, cudaMemset(e->ex.x2, 0, L * M * e->ex.s_d * 8));
+    CUDA_TRY(e, cudaMemset(e->ex.cand, 0, (size_t)2 * e->grid * M * 4 * 8));
+    e->tag = 1;
+  }
+  a.base_tag = e->tag;
+  e->tag += (uint32_t)max_forwards + 2;
+  CUDA_TRY(e, cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream));
+  CUDA_TRY(e, cudaMemsetAsync(e->d_status, 0, ST_WORDS * sizeof(int32_t), e->stream));
+  void* args[] = {&a};
+  CUDA_TRY(e, cudaLaunchCooperativeKernel((void*)e->kernel, e->grid, kThreads, args, e->smem, e->stream));
+  CUDA_TRY(e, cudaMemcpyAsync(e->h_status, e->d_status, ST_WORDS * sizeof(int32_t), cudaMemcpyDeviceToHost, e->stream));
+  CUDA_TRY(e, cudaMemcpyAsync(e->h_status + ST_WORDS, e->d_err, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+  return MLLM_OK;
+}
+
+int finish(mllm_engine* e) {
+  CUDA_TRY(e, cudaStreamSynchronize(e->stream));
+  if (e->h_status[ST_WORDS] == 2) return fail(e, MLLM_ERR_ARG, "a prompt token id is out of range");
+  if (e->h_status[ST_WORDS] != 0)
+    return fail(e, MLLM_ERR_TIMEOUT, "a device-side wait exceeded its time limit; the call was abandoned");
+  return MLLM_OK;
+}
+
+uint64_t u64_at(const int32_t* s, int i) { return (uint64_t)(uint32_t)s[i] | ((uint64_t)(uint32_t)s[i + 1] << 32); }
+
+int generate_impl(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max_new, int32_t eos, int spec_k,
+                  int ngram, int32_t* d_out, mllm_stats* st) {
+  TRY(check_slot(e, slot));
+  if (n <= 0 || max_new <= 0) return fail(e, MLLM_ERR_ARG, "empty prompt or max_new <= 0");
+  if (n > e->md.kv_len - 1)
+    return fail(e, MLLM_ERR_ARG, "prompt of %d ids does not fit the %d-position cache", n, e->md.kv_len);
+  if (spec_k < 0 || (spec_k > 0 && ngram <= 0)) return fail(e, MLLM_ERR_ARG, "bad speculation settings");
+  if (spec_k > 0 && e->md.arch == 1)
+    return fail(e, MLLM_ERR_UNSUPPORTED, "prompt-lookup speculation runs on llama-arch files only");
+  Slot& s = e->slots[slot];
+  RunArgs a{};
+  a.kc = s.k;
+  a.vc = s.v;
+  a.mode = MODE_GENERATE;
+  a.ids = d_ids;
+  a.n_ids = n;
+  a.max_new = max_new;
+  a.eos = eos;
+  a.spec_k = spec_k;
+  a.ngram = ngram;
+  a.out_ids = d_out;
+  TRY(launch(e, a, (n + e->mmax - 1) / e->mmax + max_new + 1));
+  TRY(finish(e));
+  const int32_t* hs = e->h_status;
+  const int gen = hs[ST_NGEN];
+  // engine/webgpu.js:1215-1218 style cache bookkeeping: every accepted id has its K/V in the cache
+  // except the last one generated.
+  s.cache_len = std::min(n + gen - 1, e->md.kv_len);
+  if (st) {
+    st->n_generated = gen;
+    st->stop_reason = hs[ST_STOP];
+    st->spec_hits = hs[ST_HITS];
+    st->spec_tries = hs[ST_TRIES];
+    st->forwards = hs[ST_FORWARDS];
+    st->prompt_len = n;
+    const uint64_t t0 = u64_at(hs, ST_T0), t1 = u64_at(hs, ST_TFIRST), t2 = u64_at(hs, ST_TEND);
+    st->ttft_ms = t1 > t0 ? (float)((t1 - t0) * 1e-6) : 0.f;
+    st->total_ms = t2 > t0 ? (float)((t2 - t0) * 1e-6) : 0.f;
+  }
+  return MLLM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mllm_last_error(const mllm_engine* e) { return e ? e->err.c_str() : g_create_error.c_str(); }
+
+void mllm_destroy(mllm_engine* e) {
+  if (!e) return;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  for (void* p : e->allocs) cudaFree(p);
+  if (e->h_status) cudaFreeHost(e->h_status);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}
+
+int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int kv_len, mllm_engine** out) {
+  if (!out) return fail(nullptr, MLLM_ERR_ARG, "out is null");
+  *out = nullptr;
+  std::unique_ptr<mllm_engine, void (*)(mllm_engine*)> e(new mllm_engine(), mllm_destroy);
+  std::string perr;
+  if (!parse_pgw(buf, len, &e->pgw, &perr)) return fail(nullptr, MLLM_ERR_FORMAT, "%s", perr.c_str());
+  PgwModel& p = e->pgw;
+  auto bad = [&](int code, const char* msg) { return fail(nullptr, code, "%s", msg); };
+  if (p.kind != "q4") return bad(MLLM_ERR_UNSUPPORTED, "only q4 PGW files are supported by this backend");
+  if (p.n_layers <= 0 || p.d_model <= 0 || p.n_heads <= 0 || p.n_kv_heads <= 0 || p.vocab <= 0 || p.max_seq <= 1)
+    return bad(MLLM_ERR_FORMAT, "header holds a zero dimension");
+  if (p.d_model % p.n_heads || p.d_model / p.n_heads != kHeadDim)
+    return bad(MLLM_ERR_UNSUPPORTED, "head_dim must be 64");
+  if (p.n_heads % p.n_kv_heads) return bad(MLLM_ERR_FORMAT, "nHeads is not a multiple of nKvHeads");
+  if (p.d_model % 32 || p.d_ff % 32) return bad(MLLM_ERR_UNSUPPORTED, "dModel and dFf must be multiples of 32");
+  if (max_slots <= 0) return bad(MLLM_ERR_ARG, "max_slots must be positive");
+  e->device = device;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return bad(MLLM_ERR_CUDA, "no CUDA device available");
+  if (device < 0 || device >= ndev) return bad(MLLM_ERR_ARG, "device index out of range");
+  if (cudaSetDevice(device) != cudaSuccess) return bad(MLLM_ERR_CUDA, "cudaSetDevice failed");
+  ModelDev& md = e->md;
+  md.arch = p.arch;
+  md.vocab = p.vocab;
+  md.n_layers = p.n_layers;
+  md.D = p.d_model;
+  md.NH = p.n_heads;
+  md.NKV = p.n_kv_heads;
+  md.FF = p.d_ff;
+  md.QKV = md.D + 2 * md.NKV * kHeadDim;
+  md.max_seq = p.max_seq;
+  md.kv_len = kv_len > 0 ? std::min(kv_len, p.max_seq) : p.max_seq;
+  e->kernel = pick_decode_kernel(md.D, md.FF);
+  if (!e->kernel) return bad(MLLM_ERR_UNSUPPORTED, "dModel/dFf beyond the kernel limits (1024 / 4096)");
+  mllm_engine* E = e.get();
+  auto relay = [&](int rc) {
+    if (rc != MLLM_OK) g_create_error = E->err;
+    return rc;
+  };
+  // ---- weights
+  const int D = md.D, FF = md.FF, L = md.n_layers;
+  std::vector<LayerDev> layers(L);
+  for (int l = 0; l < L; ++l) {
+    const std::string b = "blocks." + std::to_string(l) + ".";
+    LayerDev& ld = layers[l];
+    int rc;
+    if ((rc = upload_q4(E, buf, b + "attn.qkv", md.QKV, D, &ld.qkv))) return relay(rc);
+    if ((rc = upload_q4(E, buf, b + "attn.proj", D, D, &ld.proj))) return relay(rc);
+    if (md.arch == 0) {
+      if ((rc = upload_q4(E, buf, b + "mlp.w1", FF, D, &ld.w1))) return relay(rc);
+      if ((rc = upload_q4(E, buf, b + "mlp.w3", FF, D, &ld.w3))) return relay(rc);
+      if ((rc = upload_q4(E, buf, b + "mlp.w2", D, FF, &ld.w2))) return relay(rc);
+      if ((rc = upload_f32(E, buf, b + "norm1", D, &ld.norm1))) return relay(rc);
+      if ((rc = upload_f32(E, buf, b + "norm2", D, &ld.norm2))) return relay(rc);
+    } else {
+      if ((rc = upload_q4(E, buf, b + "mlp.fc", FF, D, &ld.w1))) return relay(rc);
+      if ((rc = upload_q4(E, buf, b + "mlp.proj", D, FF, &ld.w2))) return relay(rc);
+      if ((rc = upload_f32(E, buf, b + "ln1", 2 * D, &ld.norm1))) return relay(rc);
+      if ((rc = upload_f32(E, buf, b + "ln2", 2 * D, &ld.norm2))) return relay(rc);
+      // engine/infer.js:173-176: a missing bias is skipped
+      if ((rc = upload_f32(E, buf, b + "attn.qkv_bias", md.QKV, &ld.qkv_b, true))) return relay(rc);
+      if ((rc = upload_f32(E, buf, b + "attn.proj_bias", D, &ld.proj_b, true))) return relay(rc);
+      if ((rc = upload_f32(E, buf, b + "mlp.fc_bias", FF, &ld.fc_b, true))) return relay(rc);
+      if ((rc = upload_f32(E, buf, b + "mlp.proj_bias", D, &ld.mproj_b, true))) return relay(rc);
+    }
+  }
+  {
+    int rc;
+    if ((rc = upload_q4(E, buf, "lm_head", md.vocab, D, &md.lm))) return relay(rc);
+    if (md.arch == 0) {
+      if ((rc = upload_f32(E, buf, "norm_f", D, &md.norm_f))) return relay(rc);
+    } else {
+      if ((rc = upload_f32(E, buf, "ln_f", 2 * D, &md.norm_f))) return relay(rc);
+      if ((rc = upload_f32(E, buf, "wpe", (int64_t)md.max_seq * D, &md.wpe))) return relay(rc);
+      if ((rc = upload_f32(E, buf, "scale_factors", D, &md.sf, true))) return relay(rc);
+    }
+    LayerDev* dl;
+    if ((rc = dev_alloc(E, &dl, sizeof(LayerDev) * L))) return relay(rc);
+    if (cudaMemcpy(dl, layers.data(), sizeof(LayerDev) * L, cudaMemcpyHostToDevice) != cudaSuccess)
+      return bad(MLLM_ERR_CUDA, "upload of layer table failed");
+    md.layers = dl;
+    if (md.arch == 0) {
+      std::vector<float> cs, sn;
+      build_rope(md.max_seq, kHeadDim, p.rope_theta, p.rope_pct, &cs, &sn, &md.rope_dim);
+      float *dc, *ds;
+      if ((rc = dev_alloc(E, &dc, cs.size() * 4)) || (rc = dev_alloc(E, &ds, sn.size() * 4))) return relay(rc);
+      cudaMemcpy(dc, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+      cudaMemcpy(ds, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+      md.rope_cos = dc;
+      md.rope_sin = ds;
+    }
+  }
+  // ---- launch geometry: one CTA per SM, co-resident (cooperative launch)
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return bad(MLLM_ERR_CUDA, "cudaGetDeviceProperties failed");
+  if (!prop.cooperativeLaunch) return bad(MLLM_ERR_CUDA, "device lacks cooperative launch");
+  e->grid = prop.multiProcessorCount;
+  const size_t smem_cap = prop.sharedMemPerBlockOptin;
+  int mmax = 16;
+  while (mmax > 1 && decode_smem_bytes(md, mmax, e->grid) > smem_cap) --mmax;
+  e->mmax = mmax;
+  e->smem = decode_smem_bytes(md, mmax, e->grid);
+  if (e->smem > smem_cap) return bad(MLLM_ERR_UNSUPPORTED, "model does not fit the shared-memory budget");
+  if (cudaFuncSetAttribute((const void*)e->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)e->smem) != cudaSuccess)
+    return bad(MLLM_ERR_CUDA, "cudaFuncSetAttribute failed");
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, e->kernel, kThreads, e->smem);
+  if (per_sm < 1) return bad(MLLM_ERR_CUDA, "decode kernel cannot be resident with its shared memory");
+  // ---- exchange buffers
+  {
+    auto pad = [](int n) { return (n + 31) & ~31; };
+    ExchangeDev& x = e->ex;
+    x.s_qkv = pad(md.QKV);
+    x.s_d = pad(D);
+    x.s_ff = pad(FF);
+    const size_t LM = (size_t)L * mmax;
+    int rc;
+    if ((rc = dev_alloc(E, &x.qkv, LM * x.s_qkv * 8)) || (rc = dev_alloc(E, &x.att, LM * x.s_d * 8)) ||
+        (rc = dev_alloc(E, &x.x1, LM * x.s_d * 8)) || (rc = dev_alloc(E, &x.a, LM * x.s_ff * 8)) ||
+        (rc = dev_alloc(E, &x.x2, LM * x.s_d * 8)) || (rc = dev_alloc(E, &x.cand, (size_t)2 * e->grid * mmax * 4 * 8)))
+      return relay(rc);
+    cudaMemset(x.qkv, 0, LM * x.s_qkv * 8);
+    cudaMemset(x.att, 0, LM * x.s_d * 8);
+    cudaMemset(x.x1, 0, LM * x.s_d * 8);
+    cudaMemset(x.a, 0, LM * x.s_ff * 8);
+    cudaMemset(x.x2, 0, LM * x.s_d * 8);
+    cudaMemset(x.cand, 0, (size_t)2 * e->grid * mmax * 4 * 8);
+  }
+  // ---- per-slot KV caches (engine/infer.js:348-358 layout per layer: [nKv][maxSeq][hd])
+  e->slots.resize(max_slots);
+  const size_t kvn = (size_t)L * md.NKV * md.kv_len * kHeadDim;
+  for (auto& s : e->slots) {
+    int rc;
+    if ((rc = dev_alloc(E, &s.k, kvn * 4)) || (rc = dev_alloc(E, &s.v, kvn * 4))) return relay(rc);
+    cudaMemset(s.k, 0, kvn * 4);
+    cudaMemset(s.v, 0, kvn * 4);
+  }
+  int rc;
+  if ((rc = dev_alloc(E, &e->d_ids, (size_t)(md.kv_len + 16) * 4)) || (rc = dev_alloc(E, &e->d_out, (size_t)(md.kv_len + 16) * 4)) ||
+      (rc = dev_alloc(E, &e->d_status, ST_WORDS * 4)) || (rc = dev_alloc(E, &e->d_err, 16)) ||
+      (rc = dev_alloc(E, &e->d_argmax, (size_t)(md.kv_len + 16) * 4)))
+    return relay(rc);
+  if (cudaMallocHost(&e->h_status, (ST_WORDS + 1) * 4) != cudaSuccess) return bad(MLLM_ERR_OOM, "cudaMallocHost failed");
+  if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) return bad(MLLM_ERR_CUDA, "stream creation failed");
+  if (cudaDeviceSynchronize() != cudaSuccess) return bad(MLLM_ERR_CUDA, "device error during upload");
+  *out = e.release();
+  return MLLM_OK;
+}
+
+int mllm_config(const mllm_engine* e, int32_t* c) {
+  if (!e || !c) return MLLM_ERR_ARG;
+  const ModelDev& m = e->md;
+  const int32_t v[10] = {m.arch, m.vocab, m.n_layers, m.D, m.NH, m.NKV, m.FF, m.max_seq, m.kv_len, e->mmax};
+  memcpy(c, v, sizeof v);
+  return MLLM_OK;
+}
+
+size_t mllm_bytes_allocated(const mllm_engine* e) { return e ? e->bytes : 0; }
+
+int mllm_reset(mllm_engine* e, int slot) {
+  if (!e) return MLLM_ERR_ARG;
+  TRY(check_slot(e, slot));
+  e->slots[slot].cache_len = 0;
+  return MLLM_OK;
+}
+
+int mllm_cache_len(const mllm_engine* e, int slot) {
+  if (!e || slot < 0 || slot >= (int)e->slots.size()) return MLLM_ERR_ARG;
+  return e->slots[slot].cache_len;
+}
+
+int mllm_forward(mllm_engine* e, int slot, const int32_t* ids, int n, int pos0, int logits_each, float* logits,
+                 int32_t* argmax) {
+  if (!e) return MLLM_ERR_ARG;
+  cudaSetDevice(e->device);
+  TRY(check_slot(e, slot));
+  if (!ids || n <= 0) return fail(e, MLLM_ERR_ARG, "empty token list");
+  if (pos0 < 0 || pos0 + n > e->md.kv_len)
+    return fail(e, MLLM_ERR_ARG, "positions %d..%d exceed the %d-position cache", pos0, pos0 + n - 1, e->md.kv_len);
+  if (pos0 > e->slots[slot].cache_len)
+    return fail(e, MLLM_ERR_ARG, "pos0 %d leaves a gap after cacheLen %d", pos0, e->slots[slot].cache_len);
+  for (int i = 0; i < n; ++i)
+    if (ids[i] < 0 || ids[i] >= e->md.vocab) return fail(e, MLLM_ERR_ARG, "token id %d out of range", ids[i]);
+  const size_t need = (size_t)(logits_each ? n : 1) * e->md.vocab;
+  if (logits && need > e->logits_cap) {
+    float* p;
+    TRY(dev_alloc(e, &p, need * 4));
+    e->d_logits = p;
+    e->logits_cap = need;
+  }
+  CUDA_TRY(e, cudaMemcpyAsync(e->d_ids, ids, n * 4, cudaMemcpyHostToDevice, e->stream));
+  Slot& s = e->slots[slot];
+  RunArgs a{};
+  a.kc = s.k;
+  a.vc = s.v;
+  a.mode = MODE_FORWARD;
+  a.ids = e->d_ids;
+  a.n_ids = n;
+  a.pos0 = pos0;
+  a.logits_each = logits_each ? 1 : 0;
+  a.logits = logits ? e->d_logits : nullptr;
+  a.argmax_out = e->d_argmax;
+  TRY(launch(e, a, (n + e->mmax - 1) / e->mmax));
+  if (logits) CUDA_TRY(e, cudaMemcpyAsync(logits, e->d_logits, need * 4, cudaMemcpyDeviceToHost, e->stream));
+  if (argmax)
+    CUDA_TRY(e, cudaMemcpyAsync(argmax, e->d_argmax, (logits_each ? n : 1) * 4, cudaMemcpyDeviceToHost, e->stream));
+  TRY(finish(e));
+  s.cache_len = pos0 + n;
+  return MLLM_OK;
+}
+
+int mllm_generate(mllm_engine* e, int slot, const int32_t* ids, int n, int max_new, int32_t eos, int spec_k, int ngram,
+                  int32_t* out_ids, mllm_stats* st) {
+  if (!e) return MLLM_ERR_ARG;
+  cudaSetDevice(e->device);
+  if (!ids || !out_ids) return fail(e, MLLM_ERR_ARG, "null ids/out_ids");
+  if (max_new <= 0) return fail(e, MLLM_ERR_ARG, "max_new must be positive");
+  // engine/infer.js:604-608
+  const int max_prompt = std::max(1, e->md.max_seq - max_new - 1);
+  if (n > max_prompt) {
+    ids += n - max_prompt;
+    n = max_prompt;
+  }
+  if (n <= 0) return fail(e, MLLM_ERR_ARG, "empty prompt");
+  if (n > e->md.kv_len - 1) return fail(e, MLLM_ERR_ARG, "prompt of %d ids does not fit the cache", n);
+  for (int i = 0; i < n; ++i)
+    if (ids[i] < 0 || ids[i] >= e->md.vocab) return fail(e, MLLM_ERR_ARG, "token id %d out of range", ids[i]);
+  if (max_new > e->md.kv_len + 16) return fail(e, MLLM_ERR_ARG, "max_new exceeds the cache length");
+  CUDA_TRY(e, cudaMemcpyAsync(e->d_ids, ids, n * 4, cudaMemcpyHostToDevice, e->stream));
+  TRY(generate_impl(e, slot, e->d_ids, n, max_new, eos, spec_k, ngram, e->d_out, st));
+  const int gen = e->h_status[ST_NGEN];
+  CUDA_TRY(e, cudaMemcpy(out_ids, e->d_out, std::max(gen, 0) * 4, cudaMemcpyDeviceToHost));
+  return MLLM_OK;
+}
+
+int mllm_selftest_timeout(mllm_engine* e, int wait_ms) {
+  if (!e || wait_ms <= 0) return MLLM_ERR_ARG;
+  cudaSetDevice(e->device);
+  RunArgs a{};
+  a.kc = e->slots[0].k;
+  a.vc = e->slots[0].v;
+  a.mode = MODE_SELFTEST_WAIT;
+  a.wait_ns = (uint64_t)wait_ms * 1000000ull;
+  TRY(launch(e, a, 1));
+  return finish(e);
+}
+
+int mllm_generate_device(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max_new, int32_t eos, int spec_k,
+                         int ngram, int32_t* d_out, mllm_stats* st) {
+  if (!e) return MLLM_ERR_ARG;
+  cudaSetDevice(e->device);
+  if (!d_ids || !d_out) return fail(e, MLLM_ERR_ARG, "null device pointers");
+  if (n <= 0 || n > std::max(1, e->md.max_seq - max_new - 1) || n > e->md.kv_len - 1)
+    return fail(e, MLLM_ERR_ARG, "prompt length %d does not fit (truncate on the host first)", n);
+  return generate_impl(e, slot, d_ids, n, max_new, eos, spec_k, ngram, d_out, st);
+}
+
+}  // extern "C"

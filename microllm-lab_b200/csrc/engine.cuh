@@ -1,0 +1,89 @@
+// Device-side descriptors shared by the host runtime (engine.cu) and the decode kernel (decode.cu).
+#pragma once
+#include <cstdint>
+
+namespace mllm {
+
+// One Q4 matrix in the PGW layout: `w` = packed rows as u32 words ([rows][cols/8]),
+// `s` = f32 scales ([rows][cols/32]).
+struct Q4 {
+  const uint32_t* w;
+  const float* s;
+};
+
+struct LayerDev {
+  Q4 qkv, proj, w1, w3, w2;  // GPT-2: w1 = mlp.fc, w2 = mlp.proj, w3 unused
+  const float* norm1;        // llama: gain [D]; GPT-2: ln1 [gain; bias] (2D)
+  const float* norm2;
+  const float* qkv_b;        // GPT-2 biases (null for llama)
+  const float* proj_b;
+  const float* fc_b;
+  const float* mproj_b;
+};
+
+struct ModelDev {
+  int arch;  // 0 llama, 1 gpt2
+  int vocab, n_layers, D, NH, NKV, FF, QKV, max_seq, kv_len, rope_dim;
+  const LayerDev* layers;  // device array [n_layers]
+  Q4 lm;                   // tied lm_head, also the token embedding (engine/infer.js:360-420)
+  const float* norm_f;     // llama norm_f [D]; GPT-2 ln_f [2D]
+  const float* wpe;        // GPT-2 [max_seq][D]
+  const float* sf;         // GPT-2 scale_factors [D] (null when absent)
+  const float* rope_cos;   // [max_seq][rope_dim] (engine/infer.js:185-206)
+  const float* rope_sin;
+};
+
+// Exchange buffers (8-byte tagged words).  Each is [n_layers][mmax][stride] with strides padded to
+// 32 words; `cand` is [2][grid][mmax][4].
+struct ExchangeDev {
+  uint64_t* qkv;
+  uint64_t* att;
+  uint64_t* x1;
+  uint64_t* a;
+  uint64_t* x2;
+  uint64_t* cand;
+  int s_qkv, s_d, s_ff;  // row strides in words
+};
+
+enum RunMode { MODE_FORWARD = 0, MODE_GENERATE = 1, MODE_SELFTEST_WAIT = 2 };
+
+// Status words written by CTA 0 (int32 view): see the layout in engine.cu.
+enum StatusIdx {
+  ST_NGEN = 0,
+  ST_STOP = 1,
+  ST_HITS = 2,
+  ST_TRIES = 3,
+  ST_FORWARDS = 4,
+  ST_ERR = 5,
+  ST_T0 = 6,      // u64 globaltimer at kernel start (2 words)
+  ST_TFIRST = 8,  // u64 at the first generated id
+  ST_TEND = 10,   // u64 at the end
+  ST_WORDS = 16
+};
+
+struct RunArgs {
+  ModelDev m;
+  ExchangeDev x;
+  float* kc;  // slot K cache [n_layers][NKV][kv_len][64]
+  float* vc;
+  int mmax;   // tokens per forward
+  int mode;
+  // request
+  const int32_t* ids;  // device prompt / forward ids
+  int n_ids;
+  int pos0;            // MODE_FORWARD: position of ids[0]
+  int logits_each;     // MODE_FORWARD
+  float* logits;       // MODE_FORWARD, nullable: [rows][vocab]
+  int32_t* argmax_out; // MODE_FORWARD, nullable
+  int max_new;         // MODE_GENERATE
+  int eos;
+  int spec_k;
+  int ngram;
+  int32_t* out_ids;    // MODE_GENERATE: [max_new]
+  int32_t* status;     // [ST_WORDS]
+  uint32_t base_tag;
+  int* err;
+  uint64_t wait_ns;    // per-wait limit (0 = kWaitNs)
+};
+
+}  // namespace mllm

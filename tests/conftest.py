@@ -1,0 +1,31 @@
+import importlib
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200); run with -m gpu")
+
+
+def pkg():
+    return importlib.import_module("microllm-lab_b200")
+
+
+@pytest.fixture(scope="session")
+def mllm():
+    return pkg()
+
+
+@pytest.fixture(scope="session")
+def cuda_ok():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return True
