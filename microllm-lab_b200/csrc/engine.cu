@@ -197,7 +197,18 @@ int launch(mllm_engine* e, RunArgs& a, int max_forwards) {
   CUDA_TRY(e, cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream));
   CUDA_TRY(e, cudaMemsetAsync(e->d_status, 0, ST_WORDS * sizeof(int32_t), e->stream));
   void* args[] = {&a};
-  CUDA_TRY(e, cudaLaunchCooperativeKernel((void*)e->kernel, e->grid, kThreads, args, e->smem, e->stream));
+  cudaError_t lst = cudaLaunchCooperativeKernel((void*)e->kernel, e->grid, kThreads, args, e->smem, e->stream);
+  if (lst != cudaSuccess) {
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, (const void*)e->kernel);
+    int per_sm = -1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, e->kernel, kThreads, e->smem);
+    return fail(e, MLLM_ERR_CUDA,
+                "cooperative launch failed: %s (grid %d, smem %zu, regs %d, maxThreads %d, maxDynSmem %d, "
+                "static smem %zu, local %zu, params %zu B, blocks/SM %d)",
+                cudaGetErrorString(lst), e->grid, e->smem, fa.numRegs, fa.maxThreadsPerBlock,
+                fa.maxDynamicSharedSizeBytes, fa.sharedSizeBytes, fa.localSizeBytes, sizeof(RunArgs), per_sm);
+  }
   CUDA_TRY(e, cudaMemcpyAsync(e->h_status, e->d_status, ST_WORDS * sizeof(int32_t), cudaMemcpyDeviceToHost, e->stream));
   CUDA_TRY(e, cudaMemcpyAsync(e->h_status + ST_WORDS, e->d_err, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
   return MLLM_OK;
@@ -374,7 +385,9 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   e->mmax = mmax;
   e->smem = decode_smem_bytes(md, mmax, e->grid);
   if (e->smem > smem_cap) return bad(MLLM_ERR_UNSUPPORTED, "model does not fit the shared-memory budget");
-  if (cudaFuncSetAttribute((const void*)e->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)e->smem) != cudaSuccess)
+  // The limit is an attribute of the kernel function, shared by every engine that uses the same
+  // instantiation, so it is set to the device maximum rather than to this engine's need.
+  if (cudaFuncSetAttribute((const void*)e->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_cap) != cudaSuccess)
     return bad(MLLM_ERR_CUDA, "cudaFuncSetAttribute failed");
   int per_sm = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, e->kernel, kThreads, e->smem);
