@@ -67,6 +67,13 @@ const char* mllm_last_error(const mllm_engine* e);
  */
 int mllm_config(const mllm_engine* e, int32_t* cfg10);
 
+/*
+ * Launch on the caller's CUDA stream (a cudaStream_t; NULL restores the handle's own stream).  The
+ * reference engine submits to its WebGPU device queue (engine/webgpu.js:1120-1138); this is the
+ * equivalent hook, so that callers can order, overlap and time the launches with their own events.
+ */
+int mllm_set_stream(mllm_engine* e, void* stream);
+
 /* Device bytes held by the handle (GpuPetitGPT.bytesAllocated, engine/webgpu.js:1047-1065). */
 size_t mllm_bytes_allocated(const mllm_engine* e);
 

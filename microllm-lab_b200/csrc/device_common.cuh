@@ -50,6 +50,36 @@ struct Waiter {
   }
 };
 
+// Read-only loads issued exactly where written.  The compiler treats __ldg as an invariant load that
+// it may sink below a later wait; these volatile forms keep a prefetch ahead of the wait it overlaps.
+__device__ __forceinline__ uint32_t ldv_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float ldv_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 ldcg_f4(const float* p) {
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+
+// Read-only load with an L2 cache policy (createpolicy); policy 0 means the default path.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint32_t ld_hint_u32(const uint32_t* ptr, uint64_t pol) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(v) : "l"(ptr), "l"(pol));
+  return v;
+}
+
 // ---------------------------------------------------------------------------------------------
 // Q4 group-32 dequant.  A u32 word of a packed row holds 8 consecutive elements: byte b carries
 // element 2b in its low nibble and 2b+1 in its high nibble (tools/convert_hf_to_pgw.py:33).

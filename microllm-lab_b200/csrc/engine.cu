@@ -12,6 +12,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -23,9 +24,9 @@
 #include "pgw.hpp"
 
 namespace mllm {
-size_t decode_smem_bytes(const ModelDev& md, int mmax, int grid);
+size_t decode_smem_bytes(const ModelDev& md, int srows, int grid);
 typedef void (*DecodeFn)(const RunArgs);
-DecodeFn pick_decode_kernel(int D, int FF);
+DecodeFn pick_decode_kernel(int D, int FF, bool multi);
 }  // namespace mllm
 
 using namespace mllm;
@@ -47,10 +48,12 @@ struct mllm_engine {
   PgwModel pgw;
   ModelDev md{};
   ExchangeDev ex{};
-  DecodeFn kernel = nullptr;
+  DecodeFn kernel_multi = nullptr;   // prefill chunks, verify forwards, speculation
+  DecodeFn kernel_single = nullptr;  // one token per forward: the greedy decode loop
   int grid = 0, mmax = 0;
-  size_t smem = 0;
-  cudaStream_t stream = nullptr;
+  size_t smem_multi = 0, smem_single = 0;
+  cudaStream_t stream = nullptr;     // launches go here
+  cudaStream_t own_stream = nullptr; // created with the handle
   std::vector<void*> allocs;
   size_t bytes = 0;
   std::vector<Slot> slots;
@@ -64,6 +67,10 @@ struct mllm_engine {
   int32_t* h_status = nullptr;  // pinned [ST_WORDS + 1]
   uint32_t tag = 1;
   std::string err;
+  uint64_t* d_prof = nullptr;  // stage timestamps when MLLM_STAGE_PROFILE is set
+  int prof_forward = -1;
+  int poll_sleep_ns = 0;       // MLLM_POLL_SLEEP_NS
+  int weight_policy = 0;       // MLLM_WEIGHT_EVICT_LAST
 };
 
 namespace {
@@ -174,10 +181,13 @@ int check_slot(mllm_engine* e, int slot) {
   return MLLM_OK;
 }
 
-int launch(mllm_engine* e, RunArgs& a, int max_forwards) {
+// Launch one of the two decode kernels.  `resume` continues an earlier launch on the same stream:
+// its status words and error flag are kept (the earlier launch's error stops this one at entry).
+int launch(mllm_engine* e, RunArgs& a, int max_forwards, bool multi, bool resume = false) {
   a.m = e->md;
   a.x = e->ex;
   a.mmax = e->mmax;
+  a.srows = multi ? e->mmax : 1;
   a.status = e->d_status;
   a.err = e->d_err;
   // Tags only grow; when the 32-bit space would wrap, clear every exchange word and restart at 1.
@@ -194,21 +204,33 @@ int launch(mllm_engine* e, RunArgs& a, int max_forwards) {
   }
   a.base_tag = e->tag;
   e->tag += (uint32_t)max_forwards + 2;
-  CUDA_TRY(e, cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream));
-  CUDA_TRY(e, cudaMemsetAsync(e->d_status, 0, ST_WORDS * sizeof(int32_t), e->stream));
+  a.prof = e->d_prof;
+  a.prof_forward = e->prof_forward;
+  a.poll_sleep_ns = e->poll_sleep_ns;
+  a.weight_policy = e->weight_policy;
+  if (!resume) {
+    CUDA_TRY(e, cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream));
+    CUDA_TRY(e, cudaMemsetAsync(e->d_status, 0, ST_WORDS * sizeof(int32_t), e->stream));
+  }
+  DecodeFn k = multi ? e->kernel_multi : e->kernel_single;
+  const size_t smem = multi ? e->smem_multi : e->smem_single;
   void* args[] = {&a};
-  cudaError_t lst = cudaLaunchCooperativeKernel((void*)e->kernel, e->grid, kThreads, args, e->smem, e->stream);
+  cudaError_t lst = cudaLaunchCooperativeKernel((void*)k, e->grid, kThreads, args, smem, e->stream);
   if (lst != cudaSuccess) {
     cudaFuncAttributes fa{};
-    cudaFuncGetAttributes(&fa, (const void*)e->kernel);
+    cudaFuncGetAttributes(&fa, (const void*)k);
     int per_sm = -1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, e->kernel, kThreads, e->smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem);
     return fail(e, MLLM_ERR_CUDA,
                 "cooperative launch failed: %s (grid %d, smem %zu, regs %d, maxThreads %d, maxDynSmem %d, "
                 "static smem %zu, local %zu, params %zu B, blocks/SM %d)",
-                cudaGetErrorString(lst), e->grid, e->smem, fa.numRegs, fa.maxThreadsPerBlock,
+                cudaGetErrorString(lst), e->grid, smem, fa.numRegs, fa.maxThreadsPerBlock,
                 fa.maxDynamicSharedSizeBytes, fa.sharedSizeBytes, fa.localSizeBytes, sizeof(RunArgs), per_sm);
   }
+  return MLLM_OK;
+}
+
+int fetch_status(mllm_engine* e) {
   CUDA_TRY(e, cudaMemcpyAsync(e->h_status, e->d_status, ST_WORDS * sizeof(int32_t), cudaMemcpyDeviceToHost, e->stream));
   CUDA_TRY(e, cudaMemcpyAsync(e->h_status + ST_WORDS, e->d_err, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
   return MLLM_OK;
@@ -216,6 +238,15 @@ int launch(mllm_engine* e, RunArgs& a, int max_forwards) {
 
 int finish(mllm_engine* e) {
   CUDA_TRY(e, cudaStreamSynchronize(e->stream));
+  if (e->d_prof) {  // MLLM_STAGE_PROFILE=<forward index>, MLLM_STAGE_PROFILE_OUT=<file>: raw u64 dump
+    std::vector<uint64_t> h((size_t)e->grid * kProfStamps);
+    cudaMemcpy(h.data(), e->d_prof, h.size() * 8, cudaMemcpyDeviceToHost);
+    const char* path = getenv("MLLM_STAGE_PROFILE_OUT");
+    if (FILE* f = fopen(path ? path : "mllm_stage_profile.bin", "wb")) {
+      fwrite(h.data(), 8, h.size(), f);
+      fclose(f);
+    }
+  }
   if (e->h_status[ST_WORDS] == 2) return fail(e, MLLM_ERR_ARG, "a prompt token id is out of range");
   if (e->h_status[ST_WORDS] != 0)
     return fail(e, MLLM_ERR_TIMEOUT, "a device-side wait exceeded its time limit; the call was abandoned");
@@ -245,7 +276,22 @@ int generate_impl(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max
   a.spec_k = spec_k;
   a.ngram = ngram;
   a.out_ids = d_out;
-  TRY(launch(e, a, (n + e->mmax - 1) / e->mmax + max_new + 1));
+  const int chunks = (n + e->mmax - 1) / e->mmax;
+  if (spec_k > 0) {
+    TRY(launch(e, a, chunks + max_new + 1, true));
+  } else {
+    // Prefill on the general kernel, then the greedy loop on the single-token kernel; the second
+    // launch follows on the same stream and picks up the first id from out_ids.
+    a.prefill_only = 1;
+    TRY(launch(e, a, chunks, true));
+    if (max_new > 1) {
+      RunArgs b = a;
+      b.prefill_only = 0;
+      b.start_gen = 1;
+      TRY(launch(e, b, max_new, false, true));
+    }
+  }
+  TRY(fetch_status(e));
   TRY(finish(e));
   const int32_t* hs = e->h_status;
   const int gen = hs[ST_NGEN];
@@ -278,7 +324,7 @@ void mllm_destroy(mllm_engine* e) {
   if (e->stream) cudaStreamSynchronize(e->stream);
   for (void* p : e->allocs) cudaFree(p);
   if (e->h_status) cudaFreeHost(e->h_status);
-  if (e->stream) cudaStreamDestroy(e->stream);
+  if (e->own_stream) cudaStreamDestroy(e->own_stream);
   delete e;
 }
 
@@ -314,8 +360,9 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   md.QKV = md.D + 2 * md.NKV * kHeadDim;
   md.max_seq = p.max_seq;
   md.kv_len = kv_len > 0 ? std::min(kv_len, p.max_seq) : p.max_seq;
-  e->kernel = pick_decode_kernel(md.D, md.FF);
-  if (!e->kernel) return bad(MLLM_ERR_UNSUPPORTED, "dModel/dFf beyond the kernel limits (1024 / 4096)");
+  e->kernel_multi = pick_decode_kernel(md.D, md.FF, true);
+  e->kernel_single = pick_decode_kernel(md.D, md.FF, false);
+  if (!e->kernel_multi || !e->kernel_single) return bad(MLLM_ERR_UNSUPPORTED, "dModel/dFf beyond the kernel limits (1024 / 4096)");
   mllm_engine* E = e.get();
   auto relay = [&](int rc) {
     if (rc != MLLM_OK) g_create_error = E->err;
@@ -383,15 +430,18 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   int mmax = 16;
   while (mmax > 1 && decode_smem_bytes(md, mmax, e->grid) > smem_cap) --mmax;
   e->mmax = mmax;
-  e->smem = decode_smem_bytes(md, mmax, e->grid);
-  if (e->smem > smem_cap) return bad(MLLM_ERR_UNSUPPORTED, "model does not fit the shared-memory budget");
-  // The limit is an attribute of the kernel function, shared by every engine that uses the same
-  // instantiation, so it is set to the device maximum rather than to this engine's need.
-  if (cudaFuncSetAttribute((const void*)e->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_cap) != cudaSuccess)
-    return bad(MLLM_ERR_CUDA, "cudaFuncSetAttribute failed");
-  int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, e->kernel, kThreads, e->smem);
-  if (per_sm < 1) return bad(MLLM_ERR_CUDA, "decode kernel cannot be resident with its shared memory");
+  e->smem_multi = decode_smem_bytes(md, mmax, e->grid);
+  e->smem_single = decode_smem_bytes(md, 1, e->grid);
+  if (e->smem_multi > smem_cap) return bad(MLLM_ERR_UNSUPPORTED, "model does not fit the shared-memory budget");
+  for (DecodeFn k : {e->kernel_multi, e->kernel_single}) {
+    // The limit is an attribute of the kernel function, shared by every engine that uses the same
+    // instantiation, so it is set to the device maximum rather than to this engine's need.
+    if (cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_cap) != cudaSuccess)
+      return bad(MLLM_ERR_CUDA, "cudaFuncSetAttribute failed");
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, k == e->kernel_multi ? e->smem_multi : e->smem_single);
+    if (per_sm < 1) return bad(MLLM_ERR_CUDA, "decode kernel cannot be resident with its shared memory");
+  }
   // ---- exchange buffers
   {
     auto pad = [](int n) { return (n + 31) & ~31; };
@@ -427,7 +477,15 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
       (rc = dev_alloc(E, &e->d_argmax, (size_t)(md.kv_len + 16) * 4)))
     return relay(rc);
   if (cudaMallocHost(&e->h_status, (ST_WORDS + 1) * 4) != cudaSuccess) return bad(MLLM_ERR_OOM, "cudaMallocHost failed");
-  if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) return bad(MLLM_ERR_CUDA, "stream creation failed");
+  if (const char* v = getenv("MLLM_POLL_SLEEP_NS")) e->poll_sleep_ns = atoi(v);
+  if (const char* v = getenv("MLLM_WEIGHT_EVICT_LAST")) e->weight_policy = atoi(v) ? 1 : 0;
+  if (const char* pf = getenv("MLLM_STAGE_PROFILE")) {
+    e->prof_forward = atoi(pf);
+    if ((rc = dev_alloc(E, &e->d_prof, (size_t)e->grid * kProfStamps * 8))) return relay(rc);
+    cudaMemset(e->d_prof, 0, (size_t)e->grid * kProfStamps * 8);
+  }
+  if (cudaStreamCreateWithFlags(&e->own_stream, cudaStreamNonBlocking) != cudaSuccess) return bad(MLLM_ERR_CUDA, "stream creation failed");
+  e->stream = e->own_stream;
   if (cudaDeviceSynchronize() != cudaSuccess) return bad(MLLM_ERR_CUDA, "device error during upload");
   *out = e.release();
   return MLLM_OK;
@@ -442,6 +500,14 @@ int mllm_config(const mllm_engine* e, int32_t* c) {
 }
 
 size_t mllm_bytes_allocated(const mllm_engine* e) { return e ? e->bytes : 0; }
+
+int mllm_set_stream(mllm_engine* e, void* stream) {
+  if (!e) return MLLM_ERR_ARG;
+  cudaSetDevice(e->device);
+  CUDA_TRY(e, cudaStreamSynchronize(e->stream));
+  e->stream = stream ? (cudaStream_t)stream : e->own_stream;
+  return MLLM_OK;
+}
 
 int mllm_reset(mllm_engine* e, int slot) {
   if (!e) return MLLM_ERR_ARG;
@@ -486,7 +552,8 @@ int mllm_forward(mllm_engine* e, int slot, const int32_t* ids, int n, int pos0, 
   a.logits_each = logits_each ? 1 : 0;
   a.logits = logits ? e->d_logits : nullptr;
   a.argmax_out = e->d_argmax;
-  TRY(launch(e, a, (n + e->mmax - 1) / e->mmax));
+  TRY(launch(e, a, (n + e->mmax - 1) / e->mmax, n > 1));
+  TRY(fetch_status(e));
   if (logits) CUDA_TRY(e, cudaMemcpyAsync(logits, e->d_logits, need * 4, cudaMemcpyDeviceToHost, e->stream));
   if (argmax)
     CUDA_TRY(e, cudaMemcpyAsync(argmax, e->d_argmax, (logits_each ? n : 1) * 4, cudaMemcpyDeviceToHost, e->stream));
@@ -515,7 +582,8 @@ int mllm_generate(mllm_engine* e, int slot, const int32_t* ids, int n, int max_n
   CUDA_TRY(e, cudaMemcpyAsync(e->d_ids, ids, n * 4, cudaMemcpyHostToDevice, e->stream));
   TRY(generate_impl(e, slot, e->d_ids, n, max_new, eos, spec_k, ngram, e->d_out, st));
   const int gen = e->h_status[ST_NGEN];
-  CUDA_TRY(e, cudaMemcpy(out_ids, e->d_out, std::max(gen, 0) * 4, cudaMemcpyDeviceToHost));
+  CUDA_TRY(e, cudaMemcpyAsync(out_ids, e->d_out, std::max(gen, 0) * 4, cudaMemcpyDeviceToHost, e->stream));
+  CUDA_TRY(e, cudaStreamSynchronize(e->stream));
   return MLLM_OK;
 }
 
@@ -527,7 +595,8 @@ int mllm_selftest_timeout(mllm_engine* e, int wait_ms) {
   a.vc = e->slots[0].v;
   a.mode = MODE_SELFTEST_WAIT;
   a.wait_ns = (uint64_t)wait_ms * 1000000ull;
-  TRY(launch(e, a, 1));
+  TRY(launch(e, a, 1, false));
+  TRY(fetch_status(e));
   return finish(e);
 }
 

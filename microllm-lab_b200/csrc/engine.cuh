@@ -45,6 +45,8 @@ struct ExchangeDev {
   int s_qkv, s_d, s_ff;  // row strides in words
 };
 
+constexpr int kProfStamps = 256;  // stage timestamps per CTA (opt-in profiling)
+
 enum RunMode { MODE_FORWARD = 0, MODE_GENERATE = 1, MODE_SELFTEST_WAIT = 2 };
 
 // Status words written by CTA 0 (int32 view): see the layout in engine.cu.
@@ -66,7 +68,8 @@ struct RunArgs {
   ExchangeDev x;
   float* kc;  // slot K cache [n_layers][NKV][kv_len][64]
   float* vc;
-  int mmax;   // tokens per forward
+  int mmax;   // token rows per layer in the exchange buffers (tokens per forward of the general kernel)
+  int srows;  // token rows held in shared memory: mmax for the general kernel, 1 for the single-token one
   int mode;
   // request
   const int32_t* ids;  // device prompt / forward ids
@@ -84,6 +87,12 @@ struct RunArgs {
   uint32_t base_tag;
   int* err;
   uint64_t wait_ns;    // per-wait limit (0 = kWaitNs)
+  uint64_t* prof;      // nullable: [grid][kProfStamps] stage timestamps of forward `prof_forward`
+  int prof_forward;
+  int start_gen;       // MODE_GENERATE: ids already generated (in out_ids) by an earlier launch; 0 = prefill first
+  int prefill_only;    // MODE_GENERATE: stop after the first generated id
+  int poll_sleep_ns;   // back-off between unsuccessful poll rounds (0 = spin)
+  int weight_policy;   // 0: default L2 policy for weights, 1: evict_last
 };
 
 }  // namespace mllm

@@ -24,7 +24,8 @@ LIB_PATH = os.path.join(_HERE, "libmllm_cuda.so")
 SPECIAL = {"PAD": 0, "UNK": 1, "BOS": 2, "EOS": 3, "SYSTEM": 4, "USER": 5, "ASSISTANT": 6}  # engine/tokenizer.js:188-196
 STOP_NAMES = {0: "eos", 1: "max_new_tokens", 2: "context_limit"}
 
-EXPORTS = ["mllm_create", "mllm_destroy", "mllm_last_error", "mllm_config", "mllm_bytes_allocated", "mllm_reset",
+EXPORTS = ["mllm_create", "mllm_destroy", "mllm_last_error", "mllm_config", "mllm_set_stream", "mllm_bytes_allocated",
+           "mllm_reset",
            "mllm_cache_len", "mllm_forward", "mllm_generate", "mllm_generate_device", "mllm_selftest_timeout",
            "mllm_gemv_q4"]
 
@@ -70,6 +71,7 @@ def load_library(path: str = LIB_PATH):
     L.mllm_generate_device.argtypes = [P, I, P, I, I, ctypes.c_int32, I, I, P, ctypes.POINTER(Stats)]
     L.mllm_gemv_q4.argtypes = [P, P, P, P, I, I, I, P]
     L.mllm_selftest_timeout.argtypes = [P, I]
+    L.mllm_set_stream.argtypes = [P, P]
     _LIB = L
     return L
 
@@ -131,6 +133,10 @@ class CudaPetitGPT:
             self.destroy()
         except Exception:
             pass
+
+    def set_stream(self, stream_ptr: int):
+        """Launch on the caller's cudaStream_t (0 = the handle's own stream)."""
+        self._check(self._lib.mllm_set_stream(self._h, stream_ptr or None))
 
     @property
     def bytesAllocated(self) -> int:
