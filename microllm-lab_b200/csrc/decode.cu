@@ -126,6 +126,17 @@ struct Ctx {
 
 __device__ __forceinline__ bool cta_has_rows(int rows) { return (int)blockIdx.x * kWarps < rows; }
 
+// L2 prefetch of the rows [r0, r0 + 8) and [r0 + NW, r0 + NW + 8) of a Q4 matrix (the rows this CTA's
+// warps own in a GEMV stage) so that the register loads issued before the stage's wait hit L2.
+__device__ __forceinline__ void prefetch_rows(const Q4& q, int R, int n, int r0, int NW) {
+  for (int base = r0; base < R; base += NW) {
+    const int cnt = min(kWarps, R - base);
+    prefetch_l2(reinterpret_cast<const uint8_t*>(q.w) + (size_t)base * (n / 2), (uint32_t)cnt * (n / 2));
+    prefetch_l2(q.s + (size_t)base * (n / 32), (uint32_t)cnt * (n / 32) * 4);
+    if (base + NW >= R) break;
+  }
+}
+
 // Opt-in stage timestamps: thread 0 of every CTA records globaltimer at stage ends of one forward.
 __device__ __forceinline__ void stamp(const Ctx& c, uint32_t tag, int idx) {
   if (c.a.prof && threadIdx.x == 0 && tag == c.a.base_tag + (uint32_t)c.a.prof_forward && idx < kProfStamps)
@@ -520,6 +531,24 @@ __device__ __forceinline__ bool forward(Ctx& c, int M_, int pos0, int lm, uint32
   };
   for (int l = 0; l < md.n_layers; ++l) {
     const LayerDev& L = md.layers[l];
+    if (threadIdx.x == 0 && c.a.l2_prefetch) {
+      if (l + 1 < md.n_layers) {
+        const LayerDev& Ln = md.layers[l + 1];
+        const int r0 = blockIdx.x * kWarps;
+        prefetch_rows(Ln.qkv, QKV, D, r0, c.NW);
+        prefetch_rows(Ln.proj, D, D, r0, c.NW);
+        prefetch_rows(Ln.w1, FF, D, r0, c.NW);
+        if (md.arch == 0) prefetch_rows(Ln.w3, FF, D, r0, c.NW);
+        prefetch_rows(Ln.w2, D, FF, r0, c.NW);
+      }
+      // K/V rows this CTA's attention unit will read (positions < pos0 of its kv head)
+      if ((int)blockIdx.x < md.NH && pos0 > 0) {
+        const int kvh = blockIdx.x / (md.NH / md.NKV);
+        const size_t kv_base = ((size_t)l * md.NKV + kvh) * md.kv_len;
+        prefetch_l2(c.a.kc + kv_base * 64, (uint32_t)pos0 * 256);
+        prefetch_l2(c.a.vc + kv_base * 64, (uint32_t)pos0 * 256);
+      }
+    }
     const uint64_t* x2_prev = l > 0 ? x.x2 + (size_t)(l - 1) * mmax * x.s_d : nullptr;
     // ---------------- QKV (waits for the previous layer's x2 when the CTA needs the residual stream)
     if (cta_has_rows(QKV)) {
@@ -1019,12 +1048,16 @@ typedef void (*DecodeFn)(const RunArgs);
 DecodeFn pick_decode_kernel(int D, int FF, bool multi) {
   const int nd = (D / 8 + 31) / 32, nf = (FF / 8 + 31) / 32;
 #define MLLM_PICK(A, B) \
-  if (nd <= A && nf <= B) return multi ? decode_kernel<A, B, true> : decode_kernel<A, B, false>;
+  if (nd <= A && nf <= B) return multi ? decode_kernel<A, B, true> : nullptr;
+#ifndef MLLM_FAST_BUILD
   MLLM_PICK(1, 2)
+#endif
   MLLM_PICK(3, 6)
+#ifndef MLLM_FAST_BUILD
   MLLM_PICK(3, 12)
   MLLM_PICK(4, 10)
   MLLM_PICK(4, 16)
+#endif
 #undef MLLM_PICK
   return nullptr;
 }

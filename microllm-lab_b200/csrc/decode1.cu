@@ -1,0 +1,685 @@
+// Single-token persistent decode kernel: the greedy decode loop of engine/infer.js:625-639 (and the
+// GPT-2 penalised argmax of engine/infer.js:252-287), one cooperative launch, one CTA per SM.
+//
+// Same protocol as the general kernel in decode.cu (flag-in-data exchange words, one buffer per
+// layer and stage, an all-CTA argmax exchange that closes each forward), written for a small
+// register footprint: little state lives across stages, the large stages are separate functions,
+// and weight rows are requested before the wait that precedes their use.
+//
+// Per layer: QKV rows (warp per row) -> attention (one CTA per head) -> proj rows + residual ->
+// w1/w3 rows + SiLU*mul (GPT-2: fc + bias + GELU) -> w2 rows + residual.
+#include <cuda_runtime.h>
+
+#include "device_common.cuh"
+#include "engine.cuh"
+
+namespace mllm {
+namespace d1 {
+
+// Shared-memory layout (4-byte words) for one token row.
+struct Lay {
+  float* xs;     // [D] residual stream
+  float* act;    // [actw] stage input / normalised row / scratch
+  float* wpart;  // [kWarps][68] attention partials
+  float* red;    // [2][kWarps] norm partial sums
+  int* hist;     // [kv_len + 64] prompt + generated ids
+  int* pen;      // [kv_len + 128] GPT-2 banned / recent ids
+  int* misc;     // [32]
+  double* cval;  // [kWarps]
+  int* cidx;     // [kWarps]
+};
+
+__device__ __forceinline__ int act_width(const ModelDev& md, int grid) {
+  int w = max(max(md.D, md.QKV), md.FF);
+  w = max(w, 3 * grid + 4);
+  return (w + 3) & ~3;
+}
+
+__device__ __forceinline__ Lay layout(const ModelDev& md, float* smem) {
+  Lay L;
+  float* p = smem;
+  L.xs = p; p += md.D;
+  L.act = p; p += act_width(md, gridDim.x);
+  L.wpart = p; p += kWarps * 68;
+  L.red = p; p += 2 * kWarps;
+  L.hist = reinterpret_cast<int*>(p); p += md.kv_len + 64;
+  L.pen = reinterpret_cast<int*>(p); p += md.kv_len + 128;
+  L.misc = reinterpret_cast<int*>(p); p += 32;
+  p = reinterpret_cast<float*>(((uintptr_t)p + 7) & ~(uintptr_t)7);
+  L.cval = reinterpret_cast<double*>(p); p += 2 * kWarps;
+  L.cidx = reinterpret_cast<int*>(p); p += kWarps;
+  return L;
+}
+
+// Opt-in stage timestamps (thread 0 of each CTA, one forward): same layout as the general kernel.
+__device__ __forceinline__ void stamp(const RunArgs& a, uint32_t tag, int idx) {
+  if (a.prof && threadIdx.x == 0 && tag == a.base_tag + (uint32_t)a.prof_forward && idx < kProfStamps)
+    a.prof[(size_t)blockIdx.x * kProfStamps + idx] = globaltimer();
+}
+
+// Wait for the n contiguous words src[0..n) (tag == tag) and store their values to dst[0..n).
+// Every thread of the CTA calls it; returns false (everywhere) when the wait gave up.
+__device__ __noinline__ bool poll_vec(const uint64_t* src, float* dst, int n, uint32_t tag, int* err, uint64_t limit) {
+  bool ok = true;
+  const uint64_t t0 = globaltimer();
+  for (int base = threadIdx.x; base < n && ok; base += 8 * kThreads) {
+    uint32_t pending = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (base + k * kThreads < n) pending |= 1u << k;
+    int rounds = 0;
+    while (pending) {
+      uint64_t v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (pending & (1u << k)) v[k] = ll_load(src + base + k * kThreads);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if ((pending & (1u << k)) && (uint32_t)(v[k] >> 32) == tag) {
+          dst[base + k * kThreads] = __uint_as_float((uint32_t)v[k]);
+          pending &= ~(1u << k);
+        }
+      if (pending && ((++rounds & 31) == 0)) {
+        if (*(volatile int*)err || globaltimer() - t0 > limit) {
+          atomicCAS(err, 0, 1);
+          ok = false;
+          break;
+        }
+      }
+    }
+  }
+  return __syncthreads_and(ok);
+}
+
+// RMSNorm (engine/infer.js:134-143, eps 1e-6) or LayerNorm (engine/infer.js:147-164, eps 1e-5) of
+// x[0..D) into out, with the gains (and biases) already in registers; fp32 statistics.
+__device__ __noinline__ void norm_row(const float* x, float* out, float* red, int D, bool ln, float g0, float g1, float g2,
+                                      float g3, float b0, float b1, float b2, float b3) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float g[4] = {g0, g1, g2, g3}, b[4] = {b0, b1, b2, b3};
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int k = threadIdx.x + kThreads * j;
+    if (k < D) {
+      s1 += x[k];
+      s2 = fmaf(x[k], x[k], s2);
+    }
+  }
+  s1 = warp_sum(s1);
+  s2 = warp_sum(s2);
+  if (lane == 0) {
+    red[warp] = s1;
+    red[kWarps + warp] = s2;
+  }
+  __syncthreads();
+  s1 = 0.f;
+  s2 = 0.f;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    s1 += red[w];
+    s2 += red[kWarps + w];
+  }
+  if (!ln) {
+    const float inv = 1.f / sqrtf(s2 / D + 1e-6f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k = threadIdx.x + kThreads * j;
+      if (k < D) out[k] = x[k] * inv * g[j];
+    }
+  } else {
+    const float mean = s1 / D;
+    const float inv = 1.f / sqrtf(fmaxf(s2 / D - mean * mean, 0.f) + 1e-5f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k = threadIdx.x + kThreads * j;
+      if (k < D) out[k] = fmaf((x[k] - mean) * inv, g[j], b[j]);
+    }
+  }
+  __syncthreads();
+}
+
+// One Q4 row's words for this lane: words lane + 32 j of the row (u32 = 8 elements).
+template <int NWJ>
+struct Row {
+  uint32_t w[NWJ];
+  float s[NWJ];
+  __device__ __forceinline__ void load(const Q4& q, int row, int nwords, int lane) {
+    const uint32_t* wr = q.w + (size_t)row * nwords;
+    const float* sr = q.s + (size_t)row * (nwords >> 2);
+#pragma unroll
+    for (int j = 0; j < NWJ; ++j) {
+      const int k = lane + 32 * j;
+      w[j] = k < nwords ? ldv_u32(wr + k) : 0x88888888u;
+      s[j] = k < nwords ? ldv_f32(sr + (k >> 2)) : 0.f;
+    }
+  }
+  __device__ __forceinline__ float dot(const float* x, int nwords, int lane) const {
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < NWJ; ++j) {
+      const int k = lane + 32 * j;
+      if (k < nwords) acc = fmaf(word_dot(w[j], x + 8 * k), s[j], acc);
+    }
+    return warp_sum(acc);
+  }
+};
+
+__device__ __forceinline__ void load_gains(const float* g, int D, bool ln, float (&gv)[4], float (&bv)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int k = threadIdx.x + kThreads * j;
+    gv[j] = k < D ? ldv_f32(g + k) : 0.f;
+    bv[j] = (ln && k < D) ? ldv_f32(g + D + k) : 0.f;
+  }
+}
+
+// Causal attention of head h for the token at `pos` (engine/infer.js:422-495): RoPE on q and on
+// the new k, cache write by the group's first head, then online softmax over positions 0..pos with
+// 4 lanes per position (16 dims each).  Publishes the head's 64 outputs.
+__device__ __noinline__ bool attention(const RunArgs& a, const Lay& S, int l, int h, int pos, uint32_t tag) {
+  const ModelDev& md = a.m;
+  const ExchangeDev& x = a.x;
+  const int D = md.D, NKV = md.NKV, rep = md.NH / md.NKV, kvh = h / rep;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* q = S.act;       // [64]
+  float* kl = q + 64;     // [64]  new k
+  float* vl = kl + 64;    // [64]  new v
+  const bool rope = md.arch == 0 && md.rope_dim > 0;
+  const int half = rope ? md.rope_dim / 2 : 1;
+  // RoPE table values of this thread's pair (threads 0..31: q, 32..63: k), fetched before the wait.
+  float c0 = 0.f, c1 = 0.f, s0 = 0.f, s1 = 0.f;
+  if (rope && threadIdx.x < 2 * half) {
+    const int d = threadIdx.x % half;
+    const float* cs = md.rope_cos + (size_t)pos * md.rope_dim;
+    const float* sn = md.rope_sin + (size_t)pos * md.rope_dim;
+    c0 = ldv_f32(cs + d);
+    c1 = ldv_f32(cs + d + half);
+    s0 = ldv_f32(sn + d);
+    s1 = ldv_f32(sn + d + half);
+  }
+  const uint64_t* qkv_l = x.qkv + (size_t)l * a.mmax * x.s_qkv;
+  // q (64 words), k and v of the kv head (64 each): three contiguous runs
+  bool ok = true;
+  {
+    const uint64_t t0 = globaltimer();
+    const int i = threadIdx.x;  // 192 words, one per thread
+    if (i < 192) {
+      const uint64_t* src = i < 64 ? qkv_l + h * 64 + i
+                            : i < 128 ? qkv_l + D + kvh * 64 + (i - 64)
+                                      : qkv_l + D + NKV * 64 + kvh * 64 + (i - 128);
+      int rounds = 0;
+      for (;;) {
+        const uint64_t v = ll_load(src);
+        if ((uint32_t)(v >> 32) == tag) {
+          q[i] = __uint_as_float((uint32_t)v);
+          break;
+        }
+        if (((++rounds & 31) == 0) && (*(volatile int*)a.err || globaltimer() - t0 > (a.wait_ns ? a.wait_ns : kWaitNs))) {
+          atomicCAS(a.err, 0, 1);
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (!__syncthreads_and(ok)) return false;
+  }
+  if (rope && threadIdx.x < 2 * half) {
+    float* v = threadIdx.x < half ? q : kl;
+    const int d = threadIdx.x % half;
+    const float a0 = v[d], a1 = v[d + half];
+    v[d] = fmaf(-a1, s0, a0 * c0);
+    v[d + half] = fmaf(a0, s1, a1 * c1);
+  }
+  __syncthreads();
+  const size_t kv_base = ((size_t)l * NKV + kvh) * md.kv_len;
+  if (h % rep == 0 && threadIdx.x < 128) {  // engine/infer.js:457-464
+    const int d = threadIdx.x & 63;
+    if (threadIdx.x < 64) a.kc[(kv_base + pos) * 64 + d] = kl[d];
+    else a.vc[(kv_base + pos) * 64 + d] = vl[d];
+  }
+  const int qd = lane & 3, pg = lane >> 2;
+  const int npos = pos + 1;
+  float mrun = -INFINITY, lrun = 0.f, o[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i] = 0.f;
+  for (int base = warp * 8; base < npos; base += kWarps * 8) {
+    const int p = base + pg;
+    const bool valid = p < npos;
+    float4 kk[4];
+    const float* kr = p < pos ? a.kc + (kv_base + p) * 64 + qd * 16 : kl + qd * 16;
+    const float* vr = p < pos ? a.vc + (kv_base + p) * 64 + qd * 16 : vl + qd * 16;
+    if (valid && p < pos) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kk[j] = ldcg_f4(kr + 4 * j);
+    } else if (valid) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kk[j] = *reinterpret_cast<const float4*>(kr + 4 * j);
+    }
+    float part = 0.f;
+    if (valid) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 qq = *reinterpret_cast<const float4*>(q + qd * 16 + 4 * j);
+        part = fmaf(qq.x, kk[j].x, part);
+        part = fmaf(qq.y, kk[j].y, part);
+        part = fmaf(qq.z, kk[j].z, part);
+        part = fmaf(qq.w, kk[j].w, part);
+      }
+    }
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    const float sc = valid ? part * 0.125f : -INFINITY;  // 1/sqrt(64), exact (engine/infer.js:466)
+    const float newm = fmaxf(mrun, warp_max(sc));
+    const float e = valid ? expf(sc - newm) : 0.f;
+    const float corr = mrun == -INFINITY ? 0.f : expf(mrun - newm);
+    lrun = fmaf(lrun, corr, warp_sum(qd == 0 ? e : 0.f));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float4 vv = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (valid) vv = p < pos ? ldcg_f4(vr + 4 * j) : *reinterpret_cast<const float4*>(vr + 4 * j);
+      o[4 * j] = fmaf(e, vv.x, o[4 * j] * corr);
+      o[4 * j + 1] = fmaf(e, vv.y, o[4 * j + 1] * corr);
+      o[4 * j + 2] = fmaf(e, vv.z, o[4 * j + 2] * corr);
+      o[4 * j + 3] = fmaf(e, vv.w, o[4 * j + 3] * corr);
+    }
+    mrun = newm;
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    o[i] += __shfl_xor_sync(0xffffffffu, o[i], 4);
+    o[i] += __shfl_xor_sync(0xffffffffu, o[i], 8);
+    o[i] += __shfl_xor_sync(0xffffffffu, o[i], 16);
+  }
+  float* wp = S.wpart + warp * 68;
+  if (lane == 0) {
+    wp[0] = mrun;
+    wp[1] = lrun;
+  }
+  if (pg == 0) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) wp[4 + qd * 16 + i] = o[i];
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float M = -INFINITY;
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, S.wpart[w * 68]);
+    float Ls = 0.f, r0 = 0.f, r1 = 0.f;
+    for (int w = 0; w < kWarps; ++w) {
+      const float* pw = S.wpart + w * 68;
+      if (pw[1] > 0.f) {
+        const float f = expf(pw[0] - M);
+        Ls = fmaf(pw[1], f, Ls);
+        r0 = fmaf(pw[4 + 2 * lane], f, r0);
+        r1 = fmaf(pw[4 + 2 * lane + 1], f, r1);
+      }
+    }
+    const float inv = 1.f / Ls;
+    uint64_t* dst = x.att + (size_t)l * a.mmax * x.s_d + h * 64;
+    ll_store(dst + 2 * lane, tag, r0 * inv);
+    ll_store(dst + 2 * lane + 1, tag, r1 * inv);
+  }
+  __syncthreads();
+  return true;
+}
+
+// Final norm + lm_head rows + argmax candidate of this CTA (engine/infer.js:240-287); GPT-2
+// penalties use the generated ids gen_ids[0..n_past).  Publishes the candidate and closes the
+// forward with the all-CTA exchange; returns the argmax (same in every CTA) or -1 on a timeout.
+template <int NWJ>
+__device__ __noinline__ int lm_head(const RunArgs& a, const Lay& S, uint32_t tag, int parity, bool pen,
+                                    const int* gen_ids, int n_past, float* logits) {
+  const ModelDev& md = a.m;
+  const ExchangeDev& x = a.x;
+  const int D = md.D, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = gridDim.x, NW = G * kWarps, gw = blockIdx.x * kWarps + warp;
+  const int nwords = D >> 3;
+  const uint64_t limit = a.wait_ns ? a.wait_ns : kWaitNs;
+  constexpr int kG = 4;
+  Row<NWJ> rw[kG];
+#pragma unroll
+  for (int g = 0; g < kG; ++g)
+    if (gw + g * NW < md.vocab) rw[g].load(md.lm, gw + g * NW, nwords, lane);
+  {
+    float gv[4], bv[4];
+    load_gains(md.norm_f, D, md.arch == 1, gv, bv);
+    if (!poll_vec(x.x2 + (size_t)(md.n_layers - 1) * a.mmax * x.s_d, S.xs, D, tag, a.err, limit)) return -1;
+    norm_row(S.xs, S.act, S.red, D, md.arch == 1, gv[0], gv[1], gv[2], gv[3], bv[0], bv[1], bv[2], bv[3]);
+  }
+  int nban = 0, nrec = 0;
+  if (pen) {
+    if (threadIdx.x == 0) S.misc[0] = 0;
+    __syncthreads();
+    if (n_past >= 2) {
+      const int t1 = gen_ids[n_past - 2], t2 = gen_ids[n_past - 1];
+      for (int k = threadIdx.x; k < n_past - 2; k += kThreads)
+        if (gen_ids[k] == t1 && gen_ids[k + 1] == t2) S.pen[atomicAdd(&S.misc[0], 1)] = gen_ids[k + 2];
+    }
+    __syncthreads();
+    nban = S.misc[0];
+    const int rwin = max(0, n_past - 32);
+    nrec = n_past - rwin;
+    for (int k = threadIdx.x; k < nrec; k += kThreads) S.pen[nban + k] = gen_ids[rwin + k];
+    __syncthreads();
+  }
+  double best = -INFINITY;
+  int bidx = 0x7fffffff;
+  for (int r0 = gw; r0 < md.vocab; r0 += kG * NW) {
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      const int r = r0 + g * NW;
+      if (r >= md.vocab) break;
+      const float v = rw[g].dot(S.act, nwords, lane);
+      const int rn = r + kG * NW;  // next group's row for this slot
+      if (rn < md.vocab) rw[g].load(md.lm, rn, nwords, lane);
+      if (logits && lane == 0) logits[r] = v;
+      double val = v;
+      if (pen) {
+        bool banned = false, recent = false;
+        for (int k = lane; k < nban; k += 32) banned |= S.pen[k] == r;
+        for (int k = lane; k < nrec; k += 32) recent |= S.pen[nban + k] == r;
+        banned = __any_sync(0xffffffffu, banned);
+        recent = __any_sync(0xffffffffu, recent);
+        if (banned) val = -1e9;
+        if (recent && val > -1e8) val = val > 0 ? val / 1.15 : val * 1.15;
+      }
+      if (val > best) {  // rows rise within a warp: strict > keeps the lowest index on ties
+        best = val;
+        bidx = r;
+      }
+    }
+  }
+  if (lane == 0) {
+    S.cval[warp] = best;
+    S.cidx[warp] = bidx;
+  }
+  stamp(a, tag, kProfStamps - 3);
+  __threadfence();  // cache rows written in this forward become visible before the candidate
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int w = 0; w < kWarps; ++w) {
+      if (S.cval[w] > bv || (S.cval[w] == bv && S.cidx[w] < bi)) {
+        bv = S.cval[w];
+        bi = S.cidx[w];
+      }
+    }
+    const uint64_t bits = (uint64_t)__double_as_longlong(bv);
+    uint64_t* slot = x.cand + (((size_t)parity * G + blockIdx.x) * a.mmax) * 4;
+    ll_store_u32(slot + 0, tag, (uint32_t)bits);
+    ll_store_u32(slot + 1, tag, (uint32_t)(bits >> 32));
+    ll_store_u32(slot + 2, tag, (uint32_t)bi);
+  }
+  // all-CTA exchange of candidates (words 0..2 of each CTA's slot)
+  {
+    const uint64_t* base = x.cand + (size_t)parity * G * a.mmax * 4;
+    uint32_t* dst = reinterpret_cast<uint32_t*>(S.act);
+    bool ok = true;
+    const uint64_t t0 = globaltimer();
+    for (int i = threadIdx.x; i < 3 * G && ok; i += kThreads) {
+      const uint64_t* src = base + (size_t)(i / 3) * a.mmax * 4 + (i % 3);
+      int rounds = 0;
+      for (;;) {
+        const uint64_t v = ll_load(src);
+        if ((uint32_t)(v >> 32) == tag) {
+          dst[i] = (uint32_t)v;
+          break;
+        }
+        if (((++rounds & 31) == 0) && (*(volatile int*)a.err || globaltimer() - t0 > limit)) {
+          atomicCAS(a.err, 0, 1);
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (!__syncthreads_and(ok)) return -1;
+    __threadfence();
+  }
+  if (warp == 0) {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(S.act);
+    double bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int g = lane; g < G; g += 32) {
+      const double v = __longlong_as_double((long long)(((uint64_t)w[3 * g + 1] << 32) | w[3 * g]));
+      const int id = (int)w[3 * g + 2];
+      if (v > bv || (v == bv && id < bi)) {
+        bv = v;
+        bi = id;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) S.misc[2] = bi;
+  }
+  __syncthreads();
+  stamp(a, tag, kProfStamps - 2);
+  return S.misc[2];
+}
+
+// GELU tanh form (engine/infer.js:166-171), fp32.
+__device__ __forceinline__ float gelu(float v) {
+  return 0.5f * v * (1.f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
+}
+
+// One layer of the single-token forward at position `pos`.
+template <int NWJ_D, int NWJ_F>
+__device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int pos, uint32_t tag) {
+  const ModelDev& md = a.m;
+  const ExchangeDev& x = a.x;
+  const LayerDev& L = md.layers[l];
+  const int D = md.D, FF = md.FF, QKV = md.QKV;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int NW = gridDim.x * kWarps, gw = blockIdx.x * kWarps + warp;
+  const int rows0 = blockIdx.x * kWarps;  // first row of this CTA in every row-split stage
+  const bool gpt2 = md.arch == 1;
+  const uint64_t limit = a.wait_ns ? a.wait_ns : kWaitNs;
+  const size_t ofs_d = (size_t)l * a.mmax * x.s_d;
+  // ---- QKV rows (wait: previous layer's x2, then norm1)
+  if (rows0 < QKV) {
+    Row<NWJ_D> rw;
+    if (gw < QKV) rw.load(L.qkv, gw, D >> 3, lane);
+    float gv[4], bv[4];
+    load_gains(L.norm1, D, gpt2, gv, bv);
+    if (l > 0 && !poll_vec(x.x2 + ofs_d - (size_t)a.mmax * x.s_d, S.xs, D, tag, a.err, limit)) return false;
+    norm_row(S.xs, S.act, S.red, D, gpt2, gv[0], gv[1], gv[2], gv[3], bv[0], bv[1], bv[2], bv[3]);
+    uint64_t* dst = x.qkv + (size_t)l * a.mmax * x.s_qkv;
+    for (int r = gw; r < QKV; r += NW) {
+      if (r != gw) rw.load(L.qkv, r, D >> 3, lane);
+      float v = rw.dot(S.act, D >> 3, lane);
+      if (lane == 0) ll_store(dst + r, tag, L.qkv_b ? v + L.qkv_b[r] : v);
+    }
+    __syncthreads();
+  }
+  stamp(a, tag, 1 + 6 * l);
+  // ---- attention (one CTA per head)
+  for (int h = blockIdx.x; h < md.NH; h += gridDim.x)
+    if (!attention(a, S, l, h, pos, tag)) return false;
+  stamp(a, tag, 2 + 6 * l);
+  // ---- proj rows + residual (x1)
+  if (rows0 < D) {
+    Row<NWJ_D> rw;
+    if (gw < D) rw.load(L.proj, gw, D >> 3, lane);
+    if (!poll_vec(x.att + ofs_d, S.act, D, tag, a.err, limit)) return false;
+    for (int r = gw; r < D; r += NW) {
+      if (r != gw) rw.load(L.proj, r, D >> 3, lane);
+      float v = rw.dot(S.act, D >> 3, lane);
+      if (lane == 0) {
+        if (L.proj_b) v += L.proj_b[r];
+        ll_store(x.x1 + ofs_d + r, tag, S.xs[r] + v);
+      }
+    }
+    __syncthreads();
+  }
+  stamp(a, tag, 3 + 6 * l);
+  // ---- w1/w3 rows + SiLU*mul, or fc + bias + GELU (wait: x1, then norm2)
+  if (rows0 < FF) {
+    Row<NWJ_D> r1, r3;
+    if (gw < FF) {
+      r1.load(L.w1, gw, D >> 3, lane);
+      if (!gpt2) r3.load(L.w3, gw, D >> 3, lane);
+    }
+    float gv[4], bv[4];
+    load_gains(L.norm2, D, gpt2, gv, bv);
+    if (!poll_vec(x.x1 + ofs_d, S.xs, D, tag, a.err, limit)) return false;
+    norm_row(S.xs, S.act, S.red, D, gpt2, gv[0], gv[1], gv[2], gv[3], bv[0], bv[1], bv[2], bv[3]);
+    uint64_t* dst = x.a + (size_t)l * a.mmax * x.s_ff;
+    for (int r = gw; r < FF; r += NW) {
+      if (r != gw) {
+        r1.load(L.w1, r, D >> 3, lane);
+        if (!gpt2) r3.load(L.w3, r, D >> 3, lane);
+      }
+      const float u = r1.dot(S.act, D >> 3, lane);
+      if (!gpt2) {
+        const float v = r3.dot(S.act, D >> 3, lane);
+        if (lane == 0) ll_store(dst + r, tag, (u / (1.f + expf(-u))) * v);
+      } else if (lane == 0) {
+        ll_store(dst + r, tag, gelu(L.fc_b ? u + L.fc_b[r] : u));
+      }
+    }
+    __syncthreads();
+  } else if (rows0 < D) {
+    if (!poll_vec(x.x1 + ofs_d, S.xs, D, tag, a.err, limit)) return false;
+  }
+  stamp(a, tag, 4 + 6 * l);
+  // ---- w2 rows + residual (x2)
+  if (rows0 < D) {
+    Row<NWJ_F> rw;
+    if (gw < D) rw.load(L.w2, gw, FF >> 3, lane);
+    if (!poll_vec(x.a + (size_t)l * a.mmax * x.s_ff, S.act, FF, tag, a.err, limit)) return false;
+    for (int r = gw; r < D; r += NW) {
+      if (r != gw) rw.load(L.w2, r, FF >> 3, lane);
+      float v = rw.dot(S.act, FF >> 3, lane);
+      if (lane == 0) {
+        if (L.mproj_b) v += L.mproj_b[r];
+        ll_store(x.x2 + ofs_d + r, tag, S.xs[r] + v);
+      }
+    }
+    __syncthreads();
+  }
+  stamp(a, tag, 5 + 6 * l);
+  return true;
+}
+
+}  // namespace d1
+
+// The greedy decode loop on the single-token kernel.  Resumes after a prefill launch: the prompt
+// is a.ids[0..n_ids) and out_ids[0..start_gen) already holds the generated ids.  MODE_FORWARD runs
+// one forward of a.ids[0] at a.pos0 (forwardDecode).
+template <int NWJ_D, int NWJ_F>
+__global__ void __launch_bounds__(kThreads, 1) decode1_kernel(const __grid_constant__ RunArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  const ModelDev& md = a.m;
+  const d1::Lay S = d1::layout(md, smem);
+  const bool lead = blockIdx.x == 0 && threadIdx.x == 0;
+  const int n = a.n_ids, D = md.D;
+  const bool gen_mode = a.mode == MODE_GENERATE;
+  if (a.mode == MODE_SELFTEST_WAIT) {
+    // Failure-detection self-test: every CTA waits for a candidate word with a tag that no CTA
+    // writes in this launch; the wait runs out its limit, raises the error flag and returns.
+    d1::poll_vec(a.x.cand + (size_t)blockIdx.x * a.mmax * 4, S.act, 1, a.base_tag, a.err,
+                 a.wait_ns ? a.wait_ns : kWaitNs);
+    return;
+  }
+  if (!gen_mode && a.mode != MODE_FORWARD) return;
+  int gen = 0, tok = 0, stop = 1, f = 0;
+  if (gen_mode) {
+    if (*(volatile int*)a.err) return;
+    for (int t = threadIdx.x; t < n; t += kThreads) S.hist[t] = a.ids[t];
+    for (int t = threadIdx.x; t < a.start_gen; t += kThreads) S.hist[n + t] = a.out_ids[t];
+    __syncthreads();
+    gen = a.start_gen;
+    tok = S.hist[n + gen - 1];
+    if (tok == a.eos) stop = 0;
+  }
+  for (;;) {
+    int pos;
+    if (gen_mode) {
+      // engine/infer.js:625-628
+      if (stop == 0 || gen >= a.max_new || n + gen >= md.kv_len) break;
+      pos = n + gen - 1;
+    } else {
+      if (f == 1) break;
+      tok = a.ids[0];
+      pos = a.pos0;
+    }
+    const uint32_t tag = a.base_tag + f;
+    d1::stamp(a, tag, 0);
+    // embed (engine/infer.js:360-420): dequantised tied lm_head row, GPT-2 /scale_factors + wpe
+    {
+      const uint8_t* row = reinterpret_cast<const uint8_t*>(md.lm.w) + (size_t)tok * (D / 2);
+      const float* sc = md.lm.s + (size_t)tok * (D / 32);
+      for (int k = threadIdx.x; k < D; k += kThreads) {
+        const int b = row[k >> 1];
+        float v = (float)(((k & 1) ? (b >> 4) : (b & 15)) - 8) * sc[k >> 5];
+        if (md.arch == 1) {
+          if (md.sf) v = __fdiv_rn(v, md.sf[k]);
+          v += md.wpe[(size_t)min(pos, md.max_seq - 1) * D + k];
+        }
+        S.xs[k] = v;
+      }
+      __syncthreads();
+    }
+    for (int l = 0; l < md.n_layers; ++l)
+      if (!d1::layer<NWJ_D, NWJ_F>(a, S, l, pos, tag)) return;
+    const int next = d1::lm_head<NWJ_D>(a, S, tag, f & 1, gen_mode && md.arch == 1, S.hist + n, gen,
+                                          gen_mode ? nullptr : a.logits);
+    if (next < 0) return;
+    ++f;
+    if (!gen_mode) {
+      if (lead && a.argmax_out) a.argmax_out[0] = next;
+      continue;
+    }
+    tok = next;
+    if (lead) a.out_ids[gen] = tok;
+    if (threadIdx.x == 0) S.hist[n + gen] = tok;
+    ++gen;
+    __syncthreads();
+    if (tok == a.eos) stop = 0;
+  }
+  if (lead) {
+    if (gen_mode) {
+      a.status[ST_NGEN] = gen;
+      a.status[ST_STOP] = stop;
+    }
+    a.status[ST_FORWARDS] += f;
+    const uint64_t t = globaltimer();
+    a.status[ST_TEND] = (int32_t)(uint32_t)t;
+    a.status[ST_TEND + 1] = (int32_t)(uint32_t)(t >> 32);
+  }
+}
+
+size_t decode1_smem_bytes(const ModelDev& md, int grid) {
+  int actw = std::max(std::max(md.D, md.QKV), md.FF);
+  actw = std::max(actw, 3 * grid + 4);
+  actw = (actw + 3) & ~3;
+  size_t words = (size_t)md.D + actw + kWarps * 68 + 2 * kWarps + (md.kv_len + 64) + (md.kv_len + 128) + 32;
+  words = (words + 1) & ~(size_t)1;
+  words += 2 * kWarps + kWarps;
+  return words * 4;
+}
+
+typedef void (*DecodeFn)(const RunArgs);
+
+DecodeFn pick_decode1_kernel(int D, int FF) {
+  const int nd = (D / 8 + 31) / 32, nf = (FF / 8 + 31) / 32;
+#ifndef MLLM_FAST_BUILD
+  if (nd <= 1 && nf <= 2) return decode1_kernel<1, 2>;
+#endif
+  if (nd <= 3 && nf <= 6) return decode1_kernel<3, 6>;
+#ifndef MLLM_FAST_BUILD
+  if (nd <= 3 && nf <= 12) return decode1_kernel<3, 12>;
+  if (nd <= 4 && nf <= 10) return decode1_kernel<4, 10>;
+  if (nd <= 4 && nf <= 16) return decode1_kernel<4, 16>;
+#endif
+  return nullptr;
+}
+
+}  // namespace mllm

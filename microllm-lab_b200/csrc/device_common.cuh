@@ -68,6 +68,12 @@ __device__ __forceinline__ float4 ldcg_f4(const float* p) {
   return v;
 }
 
+// Bulk prefetch of [p, p + bytes) into L2 (no data returned to the SM).  p 16-byte aligned, bytes a
+// multiple of 16.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  if (bytes) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Read-only load with an L2 cache policy (createpolicy); policy 0 means the default path.
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t p;

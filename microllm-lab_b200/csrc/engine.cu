@@ -25,8 +25,10 @@
 
 namespace mllm {
 size_t decode_smem_bytes(const ModelDev& md, int srows, int grid);
+size_t decode1_smem_bytes(const ModelDev& md, int grid);
 typedef void (*DecodeFn)(const RunArgs);
 DecodeFn pick_decode_kernel(int D, int FF, bool multi);
+DecodeFn pick_decode1_kernel(int D, int FF);
 }  // namespace mllm
 
 using namespace mllm;
@@ -71,6 +73,7 @@ struct mllm_engine {
   int prof_forward = -1;
   int poll_sleep_ns = 0;       // MLLM_POLL_SLEEP_NS
   int weight_policy = 0;       // MLLM_WEIGHT_EVICT_LAST
+  int l2_prefetch = 1;         // MLLM_L2_PREFETCH (default on)
 };
 
 namespace {
@@ -208,6 +211,7 @@ int launch(mllm_engine* e, RunArgs& a, int max_forwards, bool multi, bool resume
   a.prof_forward = e->prof_forward;
   a.poll_sleep_ns = e->poll_sleep_ns;
   a.weight_policy = e->weight_policy;
+  a.l2_prefetch = e->l2_prefetch;
   if (!resume) {
     CUDA_TRY(e, cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream));
     CUDA_TRY(e, cudaMemsetAsync(e->d_status, 0, ST_WORDS * sizeof(int32_t), e->stream));
@@ -361,7 +365,7 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   md.max_seq = p.max_seq;
   md.kv_len = kv_len > 0 ? std::min(kv_len, p.max_seq) : p.max_seq;
   e->kernel_multi = pick_decode_kernel(md.D, md.FF, true);
-  e->kernel_single = pick_decode_kernel(md.D, md.FF, false);
+  e->kernel_single = pick_decode1_kernel(md.D, md.FF);
   if (!e->kernel_multi || !e->kernel_single) return bad(MLLM_ERR_UNSUPPORTED, "dModel/dFf beyond the kernel limits (1024 / 4096)");
   mllm_engine* E = e.get();
   auto relay = [&](int rc) {
@@ -431,7 +435,7 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   while (mmax > 1 && decode_smem_bytes(md, mmax, e->grid) > smem_cap) --mmax;
   e->mmax = mmax;
   e->smem_multi = decode_smem_bytes(md, mmax, e->grid);
-  e->smem_single = decode_smem_bytes(md, 1, e->grid);
+  e->smem_single = decode1_smem_bytes(md, e->grid);
   if (e->smem_multi > smem_cap) return bad(MLLM_ERR_UNSUPPORTED, "model does not fit the shared-memory budget");
   for (DecodeFn k : {e->kernel_multi, e->kernel_single}) {
     // The limit is an attribute of the kernel function, shared by every engine that uses the same
@@ -479,6 +483,7 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   if (cudaMallocHost(&e->h_status, (ST_WORDS + 1) * 4) != cudaSuccess) return bad(MLLM_ERR_OOM, "cudaMallocHost failed");
   if (const char* v = getenv("MLLM_POLL_SLEEP_NS")) e->poll_sleep_ns = atoi(v);
   if (const char* v = getenv("MLLM_WEIGHT_EVICT_LAST")) e->weight_policy = atoi(v) ? 1 : 0;
+  if (const char* v = getenv("MLLM_L2_PREFETCH")) e->l2_prefetch = atoi(v) ? 1 : 0;
   if (const char* pf = getenv("MLLM_STAGE_PROFILE")) {
     e->prof_forward = atoi(pf);
     if ((rc = dev_alloc(E, &e->d_prof, (size_t)e->grid * kProfStamps * 8))) return relay(rc);

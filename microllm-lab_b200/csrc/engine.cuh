@@ -93,6 +93,7 @@ struct RunArgs {
   int prefill_only;    // MODE_GENERATE: stop after the first generated id
   int poll_sleep_ns;   // back-off between unsuccessful poll rounds (0 = spin)
   int weight_policy;   // 0: default L2 policy for weights, 1: evict_last
+  int l2_prefetch;     // 1: bulk-prefetch the next layer's weight slices (and the layer's K/V) into L2
 };
 
 }  // namespace mllm
