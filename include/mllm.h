@@ -126,6 +126,18 @@ int mllm_selftest_timeout(mllm_engine* e, int wait_ms);
 int mllm_gemv_q4(const uint8_t* d_packed, const float* d_scales, const float* d_x, float* d_y, int rows, int cols,
                  int n_act, void* stream);
 
+/*
+ * The same product for any number of activation rows on the tensor cores: n_act >= 1 rows of f32
+ * activations x [n_act][cols] -> y [n_act][rows].  Each activation is split into fp16 hi + lo halves
+ * (relative residual <= 2^-22) that multiply the dequantised (q - 8) weights (exact in fp16) with
+ * fp32 accumulation; group scales are applied in fp32.  The fp16 halves live in a per-device
+ * workspace that this call allocates on first use (and grows when a larger call arrives).
+ * Replaces gemmGeneric (engine/infer.js:118-132: a row loop of gemvQ4) for prefill, verify and
+ * multi-sequence decode.
+ */
+int mllm_gemm_q4(const uint8_t* d_packed, const float* d_scales, const float* d_x, float* d_y, int rows, int cols,
+                 int n_act, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

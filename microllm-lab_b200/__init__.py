@@ -2,10 +2,10 @@
 
 Import with ``importlib.import_module("microllm-lab_b200")`` (the directory name holds a hyphen).
 """
-from .engine import CudaPetitGPT, MllmError, SPECIAL, gemv_q4_device, load_library, LIB_PATH, EXPORTS
+from .engine import CudaPetitGPT, MllmError, SPECIAL, gemm_q4_device, gemv_q4_device, load_library, LIB_PATH, EXPORTS
 from .pgw import (CONFIGS, Bundle, copy_span_prompt, dequant_q4, parse_pgw, quant_q4, seeded_prompt, synthetic_pgw,
                   write_pgw)
 
-__all__ = ["CudaPetitGPT", "MllmError", "SPECIAL", "gemv_q4_device", "load_library", "LIB_PATH", "EXPORTS", "CONFIGS",
+__all__ = ["CudaPetitGPT", "MllmError", "SPECIAL", "gemm_q4_device", "gemv_q4_device", "load_library", "LIB_PATH", "EXPORTS", "CONFIGS",
            "Bundle", "copy_span_prompt", "dequant_q4", "parse_pgw", "quant_q4", "seeded_prompt", "synthetic_pgw",
            "write_pgw"]

@@ -1,0 +1,175 @@
+// Tensor-core Q4 group-32 GEMM for token batches: Y[t][r] = sum_g sc[r][g] * sum_k (q[r][k]-8) * X[t][k]
+// (engine/infer.js:88-116 applied to every token row).
+//
+// Weights stay in the PGW layout (packed rows [R][K/2] bytes, scales [R][K/32]); a CTA stages one
+// 32-wide group of 64 rows (16 B per row) and 64 tokens per pipeline step in shared memory with
+// cp.async, dequantises nibbles in registers straight into the A fragments of
+// mma.sync.m16n8k16.f32.f16.f16.f32, and multiplies each group's partial sums by the fp32 scale.
+//
+// Exactness: (q - 8) is exact in fp16.  Activations are split x = hi + lo with hi = fp16(x),
+// lo = fp16(x - hi) (relative residual <= 2^-22), both multiplied on the tensor cores and accumulated
+// in fp32, so the result carries fp32-level error like the CUDA-core kernels.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace mllm {
+
+constexpr int kGemmRows = 64;     // weight rows per CTA (4 warps x 16)
+constexpr int kGemmThreads = 128;
+constexpr int kXPad = 40;         // fp16 per staged token row: 32 + 8 pad (conflict-free B loads)
+constexpr int kStages = 3;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  const int n = pred ? 16 : 0;  // zero-fill when out of range
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool pred) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  const int n = pred ? 4 : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(s), "l"(gmem), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// (lo nibble - 8, hi nibble - 8) of byte j of `w`, as an fp16 pair.  The byte lands in bytes 0 and
+// 2; masking keeps lo (low half) and 16*hi (high half); 0x6400 makes 1024 + lo and 1024 + 16 hi;
+// one fma scales the high half by 1/16 and removes the offsets.  Every step is exact in fp16.
+__device__ __forceinline__ uint32_t nib_pair_f16(uint32_t w, int j) {
+  const uint32_t v = __byte_perm(w, 0, (uint32_t)(j | (4 << 4) | (j << 8) | (4 << 12)));
+  const uint32_t h = (v & 0x00F0000Fu) | 0x64006400u;
+  const __half2 scale = __halves2half2(__float2half_rn(1.f), __float2half_rn(0.0625f));
+  const __half2 off = __halves2half2(__float2half_rn(-1032.f), __float2half_rn(-72.f));
+  const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&h), scale, off);
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+// A fragment (16 rows x 16 k) for lane (gid, t) from the staged group: rows are 16-byte records
+// (32 nibbles), k16 block `kb` is bytes 8kb..8kb+7 of a record.
+__device__ __forceinline__ void load_a_frag(const uint32_t* wrow_gid, const uint32_t* wrow_gid8, int kb, int t,
+                                            uint32_t (&a)[4]) {
+  const uint2 r0 = *reinterpret_cast<const uint2*>(wrow_gid + 2 * kb);   // row gid: bytes 8kb..8kb+7
+  const uint2 r1 = *reinterpret_cast<const uint2*>(wrow_gid8 + 2 * kb);  // row gid+8
+  a[0] = nib_pair_f16(r0.x, t);  // row gid,   k 2t, 2t+1
+  a[1] = nib_pair_f16(r1.x, t);  // row gid+8, k 2t, 2t+1
+  a[2] = nib_pair_f16(r0.y, t);  // row gid,   k 2t+8, 2t+9
+  a[3] = nib_pair_f16(r1.y, t);  // row gid+8, k 2t+8, 2t+9
+}
+
+// x -> (fp16 hi, fp16 lo) with hi + lo = x to ~2^-22 relative.
+__device__ __forceinline__ void split_hi_lo(float x, __half& hi, __half& lo) {
+  hi = __float2half_rn(x);
+  lo = __float2half_rn(x - __half2float(hi));
+}
+
+// GEMM over a token batch.  X_hi/X_lo: fp16 [T][ldx] (k contiguous).  W: PGW packed rows, S: scales.
+// Epilogue `epi(row, token, value)` is called for every (row < R, token < T) of the CTA's tile, from
+// the lane that owns it.  TBW = 8-token blocks per warp (CTA covers 8 * TBW tokens).
+template <int TBW, class Epi>
+__device__ __forceinline__ void q4_gemm_tile(const uint8_t* __restrict__ W, const float* __restrict__ S,
+                                             const __half* __restrict__ Xhi, const __half* __restrict__ Xlo, int ldx,
+                                             int R, int K, int T, int r0, int t0, unsigned char* smem, Epi epi) {
+  constexpr int BT = 8 * TBW;  // tokens per CTA
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gid = lane >> 2, t = lane & 3;
+  const int ng = K >> 5;
+  // stage layout
+  uint8_t* w_s = smem;                                           // [kStages][64][16]
+  float* s_s = reinterpret_cast<float*>(w_s + kStages * kGemmRows * 16);  // [kStages][64]
+  __half* xh_s = reinterpret_cast<__half*>(s_s + kStages * kGemmRows);    // [kStages][BT][kXPad]
+  __half* xl_s = xh_s + kStages * BT * kXPad;
+  auto issue = [&](int g, int st) {
+    // weights: 64 rows x 16 B, scales: 64 floats (16 x 16 B), activations: BT rows x 64 B x 2
+    for (int i = threadIdx.x; i < kGemmRows; i += kGemmThreads) {
+      const int r = r0 + i;
+      cp_async16(w_s + (st * kGemmRows + i) * 16, W + (size_t)min(r, R - 1) * (K >> 1) + g * 16, r < R);
+    }
+    if (threadIdx.x < kGemmRows) {  // scales of a group are one float per row (stride ng)
+      const int r = r0 + threadIdx.x;
+      cp_async4(s_s + st * kGemmRows + threadIdx.x, S + (size_t)min(r, R - 1) * ng + g, r < R);
+    }
+    for (int i = threadIdx.x; i < BT * 4; i += kGemmThreads) {  // 4 x 16 B per token row (32 fp16)
+      const int tk = i >> 2, c = i & 3;
+      const int tok = t0 + tk;
+      const bool ok = tok < T;
+      const size_t off = (size_t)min(tok, T - 1) * ldx + g * 32 + c * 8;
+      cp_async16(xh_s + (st * BT + tk) * kXPad + c * 8, Xhi + off, ok);
+      cp_async16(xl_s + (st * BT + tk) * kXPad + c * 8, Xlo + off, ok);
+    }
+  };
+  float acc[TBW][4];
+#pragma unroll
+  for (int b = 0; b < TBW; ++b)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[b][i] = 0.f;
+  // prologue
+#pragma unroll
+  for (int s = 0; s < kStages - 1; ++s) {
+    if (s < ng) issue(s, s);
+    cp_async_commit();
+  }
+  for (int g = 0; g < ng; ++g) {
+    cp_async_wait<kStages - 2>();
+    __syncthreads();
+    const int st = g % kStages;
+    {
+      const int gn = g + kStages - 1;
+      if (gn < ng) issue(gn, gn % kStages);
+      cp_async_commit();
+    }
+    const uint32_t* wr0 = reinterpret_cast<const uint32_t*>(w_s + (st * kGemmRows + warp * 16 + gid) * 16);
+    const uint32_t* wr1 = reinterpret_cast<const uint32_t*>(w_s + (st * kGemmRows + warp * 16 + gid + 8) * 16);
+    const float sc0 = s_s[st * kGemmRows + warp * 16 + gid];
+    const float sc1 = s_s[st * kGemmRows + warp * 16 + gid + 8];
+    uint32_t a0[4], a1[4];
+    load_a_frag(wr0, wr1, 0, t, a0);
+    load_a_frag(wr0, wr1, 1, t, a1);
+#pragma unroll
+    for (int b = 0; b < TBW; ++b) {
+      const __half* xh = xh_s + (st * BT + b * 8 + gid) * kXPad + 2 * t;
+      const __half* xl = xl_s + (st * BT + b * 8 + gid) * kXPad + 2 * t;
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      mma16816(d, a0, *reinterpret_cast<const uint32_t*>(xh), *reinterpret_cast<const uint32_t*>(xh + 8));
+      mma16816(d, a0, *reinterpret_cast<const uint32_t*>(xl), *reinterpret_cast<const uint32_t*>(xl + 8));
+      mma16816(d, a1, *reinterpret_cast<const uint32_t*>(xh + 16), *reinterpret_cast<const uint32_t*>(xh + 24));
+      mma16816(d, a1, *reinterpret_cast<const uint32_t*>(xl + 16), *reinterpret_cast<const uint32_t*>(xl + 24));
+      acc[b][0] = fmaf(sc0, d[0], acc[b][0]);
+      acc[b][1] = fmaf(sc0, d[1], acc[b][1]);
+      acc[b][2] = fmaf(sc1, d[2], acc[b][2]);
+      acc[b][3] = fmaf(sc1, d[3], acc[b][3]);
+    }
+  }
+  cp_async_wait<0>();
+  // epilogue: lane (gid, t) owns rows gid, gid+8 and tokens 2t, 2t+1 of each 8-token block
+  const int ra = r0 + warp * 16 + gid, rb = ra + 8;
+#pragma unroll
+  for (int b = 0; b < TBW; ++b) {
+    const int ta = t0 + b * 8 + 2 * t, tb = ta + 1;
+    if (ra < R && ta < T) epi(ra, ta, acc[b][0]);
+    if (ra < R && tb < T) epi(ra, tb, acc[b][1]);
+    if (rb < R && ta < T) epi(rb, ta, acc[b][2]);
+    if (rb < R && tb < T) epi(rb, tb, acc[b][3]);
+  }
+}
+
+template <int TBW>
+constexpr size_t q4_gemm_smem_bytes() {
+  return (size_t)kStages * kGemmRows * 16 + (size_t)kStages * kGemmRows * 4 +
+         2 * (size_t)kStages * (8 * TBW) * kXPad * sizeof(__half);
+}
+
+}  // namespace mllm

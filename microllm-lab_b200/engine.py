@@ -27,7 +27,7 @@ STOP_NAMES = {0: "eos", 1: "max_new_tokens", 2: "context_limit"}
 EXPORTS = ["mllm_create", "mllm_destroy", "mllm_last_error", "mllm_config", "mllm_set_stream", "mllm_bytes_allocated",
            "mllm_reset",
            "mllm_cache_len", "mllm_forward", "mllm_generate", "mllm_generate_device", "mllm_selftest_timeout",
-           "mllm_gemv_q4"]
+           "mllm_gemv_q4", "mllm_gemm_q4"]
 
 
 class MllmError(RuntimeError):
@@ -70,6 +70,7 @@ def load_library(path: str = LIB_PATH):
     L.mllm_generate.argtypes = [P, I, P, I, I, ctypes.c_int32, I, I, P, ctypes.POINTER(Stats)]
     L.mllm_generate_device.argtypes = [P, I, P, I, I, ctypes.c_int32, I, I, P, ctypes.POINTER(Stats)]
     L.mllm_gemv_q4.argtypes = [P, P, P, P, I, I, I, P]
+    L.mllm_gemm_q4.argtypes = [P, P, P, P, I, I, I, P]
     L.mllm_selftest_timeout.argtypes = [P, I]
     L.mllm_set_stream.argtypes = [P, P]
     _LIB = L
@@ -86,6 +87,14 @@ def gemv_q4_device(packed_ptr: int, scales_ptr: int, x_ptr: int, y_ptr: int, row
     rc = load_library().mllm_gemv_q4(packed_ptr, scales_ptr, x_ptr, y_ptr, rows, cols, n_act, stream or None)
     if rc:
         raise MllmError(rc, "mllm_gemv_q4 rejected its arguments")
+
+
+def gemm_q4_device(packed_ptr: int, scales_ptr: int, x_ptr: int, y_ptr: int, rows: int, cols: int, n_act: int,
+                   stream: int = 0) -> None:
+    """Tensor-core Q4 GEMM on device pointers (mllm_gemm_q4): y[n_act][rows] = x[n_act][cols] . W^T."""
+    rc = load_library().mllm_gemm_q4(packed_ptr, scales_ptr, x_ptr, y_ptr, rows, cols, n_act, stream or None)
+    if rc:
+        raise MllmError(rc, "mllm_gemm_q4 failed")
 
 
 class CudaPetitGPT:
