@@ -138,6 +138,20 @@ int mllm_gemv_q4(const uint8_t* d_packed, const float* d_scales, const float* d_
 int mllm_gemm_q4(const uint8_t* d_packed, const float* d_scales, const float* d_x, float* d_y, int rows, int cols,
                  int n_act, void* stream);
 
+/*
+ * Allocation-free form of mllm_gemm_q4 (no counterpart in the reference).  For callers that cannot
+ * call cudaMalloc — a host runtime that owns all device memory through its own pool, or a
+ * latency-sensitive thread that cannot take cudaMalloc's implicit synchronisation — the fp16
+ * scratch lives in a fixed 4 MiB array inside the library (held by every device that loads it, until
+ * exit), so no call allocates or frees anything.  Limit: n_act * cols <= 1,048,576 activation values;
+ * larger calls return MLLM_ERR_ARG with a message in mllm_last_error(NULL).  The first call on a
+ * device looks up the array's device address with that device current, so make the first call
+ * before any stream capture.  All calls share the array: calls that overlap on the GPU (different
+ * streams, different host threads) race on it and must be serialised by the caller.
+ */
+int mllm_gemm_q4_noalloc(const uint8_t* d_packed, const float* d_scales, const float* d_x, float* d_y, int rows,
+                         int cols, int n_act, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

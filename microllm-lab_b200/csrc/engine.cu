@@ -29,6 +29,7 @@ size_t decode1_smem_bytes(const ModelDev& md, int grid);
 typedef void (*DecodeFn)(const RunArgs);
 DecodeFn pick_decode_kernel(int D, int FF, bool multi);
 DecodeFn pick_decode1_kernel(int D, int FF);
+void set_global_error(const char* msg);
 }  // namespace mllm
 
 using namespace mllm;
@@ -36,6 +37,13 @@ using namespace mllm;
 namespace {
 
 thread_local std::string g_create_error;
+
+}  // namespace
+
+// Message for mllm_last_error(NULL) from entry points that have no handle.
+void mllm::set_global_error(const char* msg) { g_create_error = msg; }
+
+namespace {
 
 struct Slot {
   float* k = nullptr;

@@ -11,6 +11,10 @@
 #include "q4mma.cuh"
 
 namespace mllm {
+void set_global_error(const char* msg);  // engine.cu: message for mllm_last_error(NULL)
+}
+
+namespace mllm {
 
 // f32 [T][K] -> fp16 hi, lo [T][K]
 __global__ void split_kernel(const float* __restrict__ x, __half* __restrict__ hi, __half* __restrict__ lo, size_t n) {
@@ -95,6 +99,78 @@ extern "C" int mllm_gemm_q4(const uint8_t* d_packed, const float* d_scales, cons
   if (rc) return rc;
   __half* hi = ws;
   __half* lo = ws + ((n + 127) / 128) * 128;
+  if (launch_split(d_x, hi, lo, n, st) != cudaSuccess) return MLLM_ERR_CUDA;
+  if (launch_gemm_store(d_packed, d_scales, hi, lo, d_y, rows, cols, n_act, st) != cudaSuccess) return MLLM_ERR_CUDA;
+  return MLLM_OK;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free variant.  Some callers cannot call cudaMalloc: a host runtime that hands all
+// device memory to its own pool up front (an extra allocation would fail or break its budget), or a
+// latency-sensitive thread that cannot afford cudaMalloc's implicit device synchronisation.  This
+// entry point keeps its scratch — the fp16 hi and lo halves of the activations — in a fixed array
+// compiled into the library, so it allocates nothing at any call.
+// ---------------------------------------------------------------------------------------------
+namespace mllm {
+namespace {
+
+constexpr size_t kNoAllocMaxValues = size_t(1) << 20;  // n_act * cols <= 1,048,576 activation values
+// hi halves in [0, max), lo halves in [max, 2 max): 4 MiB, held by every device that loads the library
+static __device__ __align__(256) __half g_noalloc_scratch[2 * kNoAllocMaxValues];
+
+std::mutex g_noalloc_mu;
+std::vector<__half*> g_noalloc_addr;  // device address of g_noalloc_scratch, per device
+
+// On the first call on a device (that device current) the array's device address is looked up;
+// host code must never pass the symbol itself to a kernel.
+int noalloc_scratch(__half** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    set_global_error("mllm_gemm_q4_noalloc: no current CUDA device");
+    return MLLM_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if ((int)g_noalloc_addr.size() <= dev) g_noalloc_addr.resize(dev + 1, nullptr);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      set_global_error("mllm_gemm_q4_noalloc: cudaGetSymbolAddress failed for the scratch array");
+      return MLLM_ERR_CUDA;
+    }
+    g_noalloc_addr[dev] = (__half*)p;
+  }
+  *out = g_noalloc_addr[dev];
+  return MLLM_OK;
+}
+
+}  // namespace
+}  // namespace mllm
+
+extern "C" int mllm_gemm_q4_noalloc(const uint8_t* d_packed, const float* d_scales, const float* d_x, float* d_y,
+                                    int rows, int cols, int n_act, void* stream) {
+  using namespace mllm;
+  if (!d_packed || !d_scales || !d_x || !d_y || rows <= 0 || cols <= 0 || cols % 32 || n_act <= 0) {
+    set_global_error("mllm_gemm_q4_noalloc: null pointer, non-positive size or cols not a multiple of 32");
+    return MLLM_ERR_ARG;
+  }
+  if (((uintptr_t)d_packed & 15) || ((uintptr_t)d_scales & 3) || ((uintptr_t)d_x & 3)) {
+    set_global_error("mllm_gemm_q4_noalloc: misaligned device pointer");
+    return MLLM_ERR_ARG;
+  }
+  const size_t n = (size_t)n_act * cols;
+  if (n > kNoAllocMaxValues) {
+    set_global_error("mllm_gemm_q4_noalloc: n_act * cols exceeds the fixed scratch of 1,048,576 values");
+    return MLLM_ERR_ARG;
+  }
+  __half* base = nullptr;
+  const int rc = noalloc_scratch(&base);
+  if (rc) return rc;
+  // Every element the GEMM reads is written by the split kernel of the same call, so nothing has
+  // to start at zero; concurrent calls on overlapping streams share the array and race.
+  __half* hi = base;
+  __half* lo = base + kNoAllocMaxValues;
+  cudaStream_t st = (cudaStream_t)stream;
   if (launch_split(d_x, hi, lo, n, st) != cudaSuccess) return MLLM_ERR_CUDA;
   if (launch_gemm_store(d_packed, d_scales, hi, lo, d_y, rows, cols, n_act, st) != cudaSuccess) return MLLM_ERR_CUDA;
   return MLLM_OK;

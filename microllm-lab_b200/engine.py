@@ -27,7 +27,7 @@ STOP_NAMES = {0: "eos", 1: "max_new_tokens", 2: "context_limit"}
 EXPORTS = ["mllm_create", "mllm_destroy", "mllm_last_error", "mllm_config", "mllm_set_stream", "mllm_bytes_allocated",
            "mllm_reset",
            "mllm_cache_len", "mllm_forward", "mllm_generate", "mllm_generate_device", "mllm_selftest_timeout",
-           "mllm_gemv_q4", "mllm_gemm_q4"]
+           "mllm_gemv_q4", "mllm_gemm_q4", "mllm_gemm_q4_noalloc"]
 
 
 class MllmError(RuntimeError):
@@ -71,6 +71,7 @@ def load_library(path: str = LIB_PATH):
     L.mllm_generate_device.argtypes = [P, I, P, I, I, ctypes.c_int32, I, I, P, ctypes.POINTER(Stats)]
     L.mllm_gemv_q4.argtypes = [P, P, P, P, I, I, I, P]
     L.mllm_gemm_q4.argtypes = [P, P, P, P, I, I, I, P]
+    L.mllm_gemm_q4_noalloc.argtypes = [P, P, P, P, I, I, I, P]
     L.mllm_selftest_timeout.argtypes = [P, I]
     L.mllm_set_stream.argtypes = [P, P]
     _LIB = L
