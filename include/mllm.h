@@ -110,6 +110,32 @@ int mllm_generate(mllm_engine* e, int slot, const int32_t* ids, int n, int max_n
 int mllm_generate_device(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max_new, int32_t eos,
                          int spec_k, int ngram, int32_t* d_out, mllm_stats* stats);
 
+/* Result of a batched generate call. */
+typedef struct {
+  int32_t n_seq;            /* sequences run */
+  int32_t total_generated;  /* ids generated over all sequences */
+  int32_t steps;            /* batched decode steps after the prefill */
+  int32_t prefill_forwards; /* token-batch forwards of the prefill */
+  float prefill_ms;         /* device time of the prefill (all prompts, first ids) */
+  float total_ms;           /* device time of the whole call */
+} mllm_batch_stats;
+
+/*
+ * Replicated multi-sequence greedy decode: n_seq independent prompts run as one batch, sequence s on
+ * slot s (n_seq <= max_slots and <= max_tokens_per_forward).  Each sequence follows
+ * engine/infer.js:603-646 exactly as mllm_generate would (its own truncation, first id from its
+ * prefill, EOS / max_new / cache-length stops; GPT-2 files use the penalised argmax of
+ * engine/infer.js:252-287 over that sequence's own generated ids), so the output per sequence is
+ * identical to n_seq separate mllm_generate calls.  The reference runs one sequence per engine
+ * (engine/worker.js:149-159); this is the batched form of that loop (generateBatch in the JS
+ * binding).  Prompts: ids[offsets[s] .. offsets[s+1]) (host, offsets has n_seq + 1 entries).
+ * Output: out_ids [n_seq][max_new] (host), n_out [n_seq] ids generated per sequence, stop
+ * [n_seq] (nullable) mllm_stop per sequence.  Prefill and decode run as token-batch forwards
+ * on the tensor cores; each decode step is one CUDA graph launch.
+ */
+int mllm_generate_batch(mllm_engine* e, int n_seq, const int32_t* ids, const int32_t* offsets, int max_new,
+                        int32_t eos, int32_t* out_ids, int32_t* n_out, int32_t* stop, mllm_batch_stats* stats);
+
 /*
  * Failure-detection self-test (no counterpart in the reference): launches the decode kernel in a
  * mode where every CTA waits for a word that nothing writes, with a `wait_ms` limit.  Expected

@@ -19,8 +19,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr", "-Xptxas", "-v"]
 if os.environ.get("MLLM_FAST_BUILD"):  # development: only the PetitGPT-shape instantiation
     CUFLAGS += ["-DMLLM_FAST_BUILD"]
-SOURCES = ["engine.cu", "decode.cu", "decode1.cu", "gemv.cu", "gemm.cu", "pgw.cpp"]
-HEADERS = ["device_common.cuh", "engine.cuh", "pgw.hpp", "q4mma.cuh"]
+SOURCES = ["engine.cu", "decode.cu", "decode1.cu", "gemv.cu", "gemm.cu", "lwe.cu", "pgw.cpp"]
+HEADERS = ["device_common.cuh", "engine.cuh", "lwe.cuh", "pgw.hpp", "q4mma.cuh"]
 
 
 def _stale(target: str, deps) -> bool:
@@ -33,6 +33,15 @@ def _stale(target: str, deps) -> bool:
 def build(verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     hdrs = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(ROOT, "include", "mllm.h")]
+    # objects built with other flags (e.g. MLLM_FAST_BUILD) are rebuilt
+    stamp = os.path.join(BUILD, "flags.txt")
+    flags = " ".join([NVCC, *ARCH, *CUFLAGS])
+    if not os.path.exists(stamp) or open(stamp).read() != flags:
+        for f in os.listdir(BUILD):
+            if f.endswith(".o"):
+                os.remove(os.path.join(BUILD, f))
+        with open(stamp, "w") as fh:
+            fh.write(flags)
     objs = []
     for src in SOURCES:
         s = os.path.join(CSRC, src)

@@ -21,6 +21,7 @@
 #include "../../include/mllm.h"
 #include "device_common.cuh"
 #include "engine.cuh"
+#include "lwe.cuh"
 #include "pgw.hpp"
 
 namespace mllm {
@@ -49,6 +50,12 @@ struct Slot {
   float* k = nullptr;
   float* v = nullptr;
   int cache_len = 0;
+};
+
+// Device buffer that grows on demand (freed and reallocated; the stream is drained first).
+struct Grow {
+  void* p = nullptr;
+  size_t cap = 0;
 };
 
 }  // namespace
@@ -82,6 +89,15 @@ struct mllm_engine {
   int poll_sleep_ns = 0;       // MLLM_POLL_SLEEP_NS
   int weight_policy = 0;       // MLLM_WEIGHT_EVICT_LAST
   int l2_prefetch = 1;         // MLLM_L2_PREFETCH (default on)
+  // layer-wise engine: token-batch forwards on the tensor cores (prefill, verify, batched decode)
+  int lwe_ok = 0;              // rep = nHeads / nKvHeads fits its attention kernel
+  int lwe_prefill = 1;         // MLLM_LWE_PREFILL=0 keeps prefill and multi-token forwards on decode_kernel
+  int lwe_graph = 1;           // MLLM_LWE_GRAPH=0 launches the batched decode step without a CUDA graph
+  int tmax = 0;                // token rows per forward (MLLM_LWE_TOKENS)
+  LweArgs lw{};
+  LweHost lh;
+  Grow g_bids, g_plan, g_bout, g_state, g_blogits;
+  int32_t* h_active = nullptr; // pinned
 };
 
 namespace {
@@ -112,6 +128,23 @@ int dev_alloc(mllm_engine* e, T** p, size_t bytes) {
   e->allocs.push_back(q);
   e->bytes += bytes;
   *p = (T*)q;
+  return MLLM_OK;
+}
+
+int grow(mllm_engine* e, Grow& g, size_t bytes) {
+  bytes = std::max<size_t>(bytes, 256);
+  if (g.cap >= bytes) return MLLM_OK;
+  if (g.p) {
+    CUDA_TRY(e, cudaStreamSynchronize(e->stream));
+    cudaFree(g.p);
+    e->bytes -= g.cap;
+    g.p = nullptr;
+    g.cap = 0;
+  }
+  cudaError_t st = cudaMalloc(&g.p, bytes);
+  if (st != cudaSuccess) return fail(e, MLLM_ERR_OOM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(st));
+  g.cap = bytes;
+  e->bytes += bytes;
   return MLLM_OK;
 }
 
@@ -267,6 +300,38 @@ int finish(mllm_engine* e) {
 
 uint64_t u64_at(const int32_t* s, int i) { return (uint64_t)(uint32_t)s[i] | ((uint64_t)(uint32_t)s[i + 1] << 32); }
 
+LweArgs lwe_args(const mllm_engine* e) {
+  LweArgs a = e->lw;
+  a.m = e->md;
+  a.err = e->d_err;
+  return a;
+}
+
+// Token-batch forward of n device ids of one slot at positions pos0.. in chunks of tmax tokens
+// (engine/infer.js:553-577 for every token).  The lm_head runs on the last token (argmax -> d_amax[0],
+// logits [V]) or, with lm_each, on every token (d_amax[i], logits [n][V]).  Returns the forward count.
+int lwe_run(mllm_engine* e, int slot, const int32_t* d_ids, int n, int pos0, int lm_each, float* d_logits,
+            int32_t* d_amax, int* forwards) {
+  const Slot& s = e->slots[slot];
+  (void)s;
+  LweArgs a = lwe_args(e);
+  const int V = e->md.vocab;
+  int f = 0;
+  for (int c0 = 0; c0 < n; c0 += e->tmax) {
+    const int Tc = std::min(e->tmax, n - c0);
+    const bool last = c0 + Tc >= n;
+    lwe_fill(a, d_ids + c0, Tc, slot, pos0 + c0, lm_each, e->stream);
+    LweArgs b = a;
+    b.amax = d_amax + (lm_each ? c0 : 0);
+    const int lm_T = lm_each ? Tc : (last ? 1 : 0);
+    float* lg = d_logits && lm_T ? d_logits + (size_t)(lm_each ? c0 : 0) * V : nullptr;
+    CUDA_TRY(e, lwe_forward(b, e->lh, Tc, lm_T, !lm_each, lg, e->stream));
+    ++f;
+  }
+  *forwards = f;
+  return MLLM_OK;
+}
+
 int generate_impl(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max_new, int32_t eos, int spec_k,
                   int ngram, int32_t* d_out, mllm_stats* st) {
   TRY(check_slot(e, slot));
@@ -289,7 +354,20 @@ int generate_impl(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max
   a.ngram = ngram;
   a.out_ids = d_out;
   const int chunks = (n + e->mmax - 1) / e->mmax;
-  if (spec_k > 0) {
+  if (e->lwe_ok && e->lwe_prefill) {
+    // Prefill as token-batch forwards on the tensor cores, first id from its argmax, then the decode
+    // loop (greedy: the single-token kernel; speculative: the general kernel) resumes from out_ids.
+    CUDA_TRY(e, cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream));
+    CUDA_TRY(e, cudaMemsetAsync(e->d_status, 0, ST_WORDS * sizeof(int32_t), e->stream));
+    lwe_mark_time(e->d_status, ST_T0, e->stream);
+    int f = 0;
+    TRY(lwe_run(e, slot, d_ids, n, 0, 0, nullptr, e->lw.amax, &f));
+    lwe_first(lwe_args(e), d_out, e->d_status, eos, f, e->stream);
+    if (max_new > 1) {
+      a.start_gen = 1;
+      TRY(launch(e, a, max_new + 1, spec_k > 0, true));
+    }
+  } else if (spec_k > 0) {
     TRY(launch(e, a, chunks + max_new + 1, true));
   } else {
     // Prefill on the general kernel, then the greedy loop on the single-token kernel; the second
@@ -335,7 +413,10 @@ void mllm_destroy(mllm_engine* e) {
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
   for (void* p : e->allocs) cudaFree(p);
+  for (Grow* g : {&e->g_bids, &e->g_plan, &e->g_bout, &e->g_state, &e->g_blogits})
+    if (g->p) cudaFree(g->p);
   if (e->h_status) cudaFreeHost(e->h_status);
+  if (e->h_active) cudaFreeHost(e->h_active);
   if (e->own_stream) cudaStreamDestroy(e->own_stream);
   delete e;
 }
@@ -489,6 +570,43 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
       (rc = dev_alloc(E, &e->d_argmax, (size_t)(md.kv_len + 16) * 4)))
     return relay(rc);
   if (cudaMallocHost(&e->h_status, (ST_WORDS + 1) * 4) != cudaSuccess) return bad(MLLM_ERR_OOM, "cudaMallocHost failed");
+  if (cudaMallocHost(&e->h_active, 16) != cudaSuccess) return bad(MLLM_ERR_OOM, "cudaMallocHost failed");
+  // ---- layer-wise engine buffers: tmax token rows per forward
+  e->lwe_ok = md.NH / md.NKV <= kLweMaxRep;
+  if (const char* v = getenv("MLLM_LWE_PREFILL")) e->lwe_prefill = atoi(v) ? 1 : 0;
+  if (const char* v = getenv("MLLM_LWE_GRAPH")) e->lwe_graph = atoi(v) ? 1 : 0;
+  e->tmax = 1024;
+  if (const char* v = getenv("MLLM_LWE_TOKENS")) e->tmax = std::max(16, std::min(8192, atoi(v)));
+  e->lh.layers = layers;
+  {
+    LweArgs& w = e->lw;
+    const size_t T = e->tmax;
+    auto r64 = [](int n) { return (n + 63) & ~63; };
+    w.ldx = r64(std::max(D, md.NH * kHeadDim));
+    w.ldx2 = r64(FF);
+    w.lm_cap = e->tmax;
+    const size_t nblk = (md.vocab + 63) / 64;
+    float** kc;
+    float** vc;
+    if ((rc = dev_alloc(E, &w.x, T * D * 4)) || (rc = dev_alloc(E, &w.xh, T * w.ldx * 2)) ||
+        (rc = dev_alloc(E, &w.xl, T * w.ldx * 2)) || (rc = dev_alloc(E, &w.xh2, T * w.ldx2 * 2)) ||
+        (rc = dev_alloc(E, &w.xl2, T * w.ldx2 * 2)) || (rc = dev_alloc(E, &w.qkv, T * md.QKV * 4)) ||
+        (rc = dev_alloc(E, &w.tok, T * 4)) || (rc = dev_alloc(E, &w.slot, T * 4)) || (rc = dev_alloc(E, &w.pos, T * 4)) ||
+        (rc = dev_alloc(E, &w.lm_src, T * 4)) || (rc = dev_alloc(E, &w.amax, T * 4)) ||
+        (rc = dev_alloc(E, &w.pval, nblk * T * 4)) || (rc = dev_alloc(E, &w.pidx, nblk * T * 4)) ||
+        (rc = dev_alloc(E, &kc, e->slots.size() * sizeof(float*))) ||
+        (rc = dev_alloc(E, &vc, e->slots.size() * sizeof(float*))))
+      return relay(rc);
+    std::vector<float*> hk, hv;
+    for (auto& sl : e->slots) {
+      hk.push_back(sl.k);
+      hv.push_back(sl.v);
+    }
+    cudaMemcpy(kc, hk.data(), hk.size() * sizeof(float*), cudaMemcpyHostToDevice);
+    cudaMemcpy(vc, hv.data(), hv.size() * sizeof(float*), cudaMemcpyHostToDevice);
+    w.kc = kc;
+    w.vc = vc;
+  }
   if (const char* v = getenv("MLLM_POLL_SLEEP_NS")) e->poll_sleep_ns = atoi(v);
   if (const char* v = getenv("MLLM_WEIGHT_EVICT_LAST")) e->weight_policy = atoi(v) ? 1 : 0;
   if (const char* v = getenv("MLLM_L2_PREFETCH")) e->l2_prefetch = atoi(v) ? 1 : 0;
@@ -565,7 +683,13 @@ int mllm_forward(mllm_engine* e, int slot, const int32_t* ids, int n, int pos0, 
   a.logits_each = logits_each ? 1 : 0;
   a.logits = logits ? e->d_logits : nullptr;
   a.argmax_out = e->d_argmax;
-  TRY(launch(e, a, (n + e->mmax - 1) / e->mmax, n > 1));
+  if (n > 1 && e->lwe_ok && e->lwe_prefill) {
+    CUDA_TRY(e, cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream));
+    int f = 0;
+    TRY(lwe_run(e, slot, e->d_ids, n, pos0, logits_each, logits ? e->d_logits : nullptr, e->d_argmax, &f));
+  } else {
+    TRY(launch(e, a, (n + e->mmax - 1) / e->mmax, n > 1));
+  }
   TRY(fetch_status(e));
   if (logits) CUDA_TRY(e, cudaMemcpyAsync(logits, e->d_logits, need * 4, cudaMemcpyDeviceToHost, e->stream));
   if (argmax)
@@ -621,6 +745,178 @@ int mllm_generate_device(mllm_engine* e, int slot, const int32_t* d_ids, int n, 
   if (n <= 0 || n > std::max(1, e->md.max_seq - max_new - 1) || n > e->md.kv_len - 1)
     return fail(e, MLLM_ERR_ARG, "prompt length %d does not fit (truncate on the host first)", n);
   return generate_impl(e, slot, d_ids, n, max_new, eos, spec_k, ngram, d_out, st);
+}
+
+
+// Replicated multi-sequence greedy decode (see include/mllm.h).  Host side: truncation and the
+// prefill plan; device side: token-batch prefill forwards, first ids, then one batched decode step
+// per generated position, captured once as a CUDA graph and replayed.
+int mllm_generate_batch(mllm_engine* e, int n_seq, const int32_t* ids, const int32_t* offsets, int max_new,
+                        int32_t eos, int32_t* out_ids, int32_t* n_out, int32_t* stop, mllm_batch_stats* stats) {
+  if (!e) return MLLM_ERR_ARG;
+  cudaSetDevice(e->device);
+  if (!ids || !offsets || !out_ids || !n_out) return fail(e, MLLM_ERR_ARG, "null ids/offsets/out_ids/n_out");
+  if (n_seq <= 0 || n_seq > (int)e->slots.size())
+    return fail(e, MLLM_ERR_ARG, "n_seq %d outside [1, %zu] (max_slots)", n_seq, e->slots.size());
+  if (n_seq > e->tmax) return fail(e, MLLM_ERR_UNSUPPORTED, "n_seq %d exceeds %d rows per forward", n_seq, e->tmax);
+  if (!e->lwe_ok) return fail(e, MLLM_ERR_UNSUPPORTED, "nHeads / nKvHeads above %d", kLweMaxRep);
+  if (max_new <= 0 || max_new > e->md.kv_len + 16) return fail(e, MLLM_ERR_ARG, "max_new outside [1, kv_len + 16]");
+  const ModelDev& md = e->md;
+  const int kv_len = md.kv_len;
+  // engine/infer.js:604-608 per sequence
+  const int max_prompt = std::max(1, md.max_seq - max_new - 1);
+  std::vector<int32_t> lens(n_seq), first(n_seq);
+  for (int q = 0; q < n_seq; ++q) {
+    const int len = offsets[q + 1] - offsets[q];
+    if (offsets[q] < 0 || len <= 0) return fail(e, MLLM_ERR_ARG, "sequence %d has an empty prompt", q);
+    const int tl = std::min(len, max_prompt);
+    if (tl > kv_len - 1) return fail(e, MLLM_ERR_ARG, "prompt of sequence %d does not fit the cache", q);
+    lens[q] = tl;
+    first[q] = offsets[q] + (len - tl);
+  }
+  const int total_ids = offsets[n_seq];
+  for (int i = offsets[0]; i < total_ids; ++i)
+    if (ids[i] < 0 || ids[i] >= md.vocab) return fail(e, MLLM_ERR_ARG, "token id %d out of range", ids[i]);
+  // Plan: every prompt token (slot, position, source index); forward c takes tokens [c*tmax, ..).
+  // Per forward, the lm rows are the tokens that end a prompt.
+  std::vector<int32_t> p_slot, p_pos, p_src, lm_src, lm_slot, lm_off{0};
+  for (int q = 0; q < n_seq; ++q)
+    for (int i = 0; i < lens[q]; ++i) {
+      p_slot.push_back(q);
+      p_pos.push_back(i);
+      p_src.push_back(first[q] + i);
+    }
+  const int P = (int)p_slot.size();
+  const int nchunk = (P + e->tmax - 1) / e->tmax;
+  for (int c = 0; c < nchunk; ++c) {
+    const int c0 = c * e->tmax, c1 = std::min(P, c0 + e->tmax);
+    for (int k = c0; k < c1; ++k)
+      if (p_pos[k] == lens[p_slot[k]] - 1) {
+        lm_src.push_back(k - c0);
+        lm_slot.push_back(p_slot[k]);
+      }
+    lm_off.push_back((int)lm_src.size());
+  }
+  // one device buffer: slot[P] pos[P] src[P] lm_src[n] lm_slot[n]
+  std::vector<int32_t> plan;
+  plan.reserve(3 * P + 2 * n_seq);
+  plan.insert(plan.end(), p_slot.begin(), p_slot.end());
+  plan.insert(plan.end(), p_pos.begin(), p_pos.end());
+  plan.insert(plan.end(), p_src.begin(), p_src.end());
+  plan.insert(plan.end(), lm_src.begin(), lm_src.end());
+  plan.insert(plan.end(), lm_slot.begin(), lm_slot.end());
+  const size_t state_words = 2 * (size_t)n_seq + 16;  // counts[n], lens[n], active
+  TRY(grow(e, e->g_bids, (size_t)total_ids * 4));
+  TRY(grow(e, e->g_plan, plan.size() * 4));
+  TRY(grow(e, e->g_bout, (size_t)n_seq * max_new * 4));
+  TRY(grow(e, e->g_state, state_words * 4));
+  const bool gpt2 = md.arch == 1;
+  if (gpt2) TRY(grow(e, e->g_blogits, (size_t)n_seq * md.vocab * 4));
+  int32_t* d_bids = (int32_t*)e->g_bids.p;
+  int32_t* d_plan = (int32_t*)e->g_plan.p;
+  int32_t* d_bout = (int32_t*)e->g_bout.p;
+  int32_t* d_counts = (int32_t*)e->g_state.p;
+  int32_t* d_lens = d_counts + n_seq;
+  int32_t* d_active = d_lens + n_seq;
+  float* d_blogits = (float*)e->g_blogits.p;
+  cudaStream_t st = e->stream;
+  CUDA_TRY(e, cudaMemcpyAsync(d_bids, ids, (size_t)total_ids * 4, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(e, cudaMemcpyAsync(d_plan, plan.data(), plan.size() * 4, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(e, cudaMemcpyAsync(d_lens, lens.data(), (size_t)n_seq * 4, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(e, cudaMemsetAsync(e->d_err, 0, sizeof(int), st));
+  CUDA_TRY(e, cudaMemsetAsync(e->d_status, 0, ST_WORDS * sizeof(int32_t), st));
+  lwe_mark_time(e->d_status, ST_T0, st);
+  // ---- prefill
+  const int32_t* d_pslot = d_plan;
+  const int32_t* d_ppos = d_plan + P;
+  const int32_t* d_psrc = d_plan + 2 * P;
+  const int32_t* d_lmsrc = d_plan + 3 * P;
+  const int32_t* d_lmslot = d_lmsrc + n_seq;
+  const LweArgs base = lwe_args(e);
+  for (int c = 0; c < nchunk; ++c) {
+    const int c0 = c * e->tmax, Tc = std::min(e->tmax, P - c0);
+    const int nlm = lm_off[c + 1] - lm_off[c];
+    LweArgs a = base;
+    a.slot = const_cast<int32_t*>(d_pslot + c0);
+    a.pos = const_cast<int32_t*>(d_ppos + c0);
+    a.lm_src = const_cast<int32_t*>(d_lmsrc + lm_off[c]);
+    lwe_gather(a.tok, d_bids, d_psrc + c0, Tc, st);
+    CUDA_TRY(e, lwe_forward(a, e->lh, Tc, nlm, true, nullptr, st));
+    if (nlm) lwe_batch_first(a.amax, d_lmslot + lm_off[c], nlm, max_new, eos, kv_len, d_bout, d_counts, d_lens, st);
+  }
+  lwe_mark_time(e->d_status, ST_TFIRST, st);
+  // ---- decode: row t = sequence t
+  int steps_max = 0;
+  for (int q = 0; q < n_seq; ++q) steps_max = std::max(steps_max, std::min(max_new, kv_len - lens[q]) - 1);
+  int steps = 0;
+  if (steps_max > 0) {
+    const LweArgs d = base;  // tok/slot/pos/lm_src: the engine's own rows
+    lwe_batch_decode_setup(d, n_seq, d_bout, d_counts, d_lens, max_new, st);
+    auto step = [&]() -> cudaError_t {
+      cudaError_t r = lwe_forward(d, e->lh, n_seq, n_seq, false, gpt2 ? d_blogits : nullptr, st);
+      if (r != cudaSuccess) return r;
+      if (gpt2) lwe_penalised_argmax(d_blogits, md.vocab, n_seq, d_bout, d_counts, max_new, d.amax, st);
+      lwe_batch_advance(d, n_seq, max_new, eos, d_bout, d_counts, d_lens, st);
+      return cudaGetLastError();
+    };
+    cudaGraphExec_t exec = nullptr;
+    if (e->lwe_graph) {
+      cudaGraph_t graph = nullptr;
+      CUDA_TRY(e, cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+      const cudaError_t r1 = step();
+      const cudaError_t r2 = cudaStreamEndCapture(st, &graph);
+      if (r1 != cudaSuccess || r2 != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        return fail(e, MLLM_ERR_CUDA, "capture of the decode step failed: %s",
+                    cudaGetErrorString(r1 != cudaSuccess ? r1 : r2));
+      }
+      const cudaError_t r3 = cudaGraphInstantiate(&exec, graph, 0);
+      cudaGraphDestroy(graph);
+      if (r3 != cudaSuccess) return fail(e, MLLM_ERR_CUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(r3));
+    }
+    // With an EOS id the batch may finish early: every 16 steps the number of running sequences is
+    // read back (the steps already queued behind it keep the GPU busy meanwhile).
+    cudaError_t rs = cudaSuccess;
+    for (; steps < steps_max && rs == cudaSuccess; ++steps) {
+      rs = exec ? cudaGraphLaunch(exec, st) : step();
+      if (eos >= 0 && rs == cudaSuccess && (steps & 15) == 15 && steps + 1 < steps_max) {
+        lwe_count_active(d_counts, n_seq, d_active, st);
+        rs = cudaMemcpyAsync(e->h_active, d_active, 4, cudaMemcpyDeviceToHost, st);
+        if (rs == cudaSuccess) rs = cudaStreamSynchronize(st);
+        if (rs == cudaSuccess && *e->h_active == 0) {
+          ++steps;
+          break;
+        }
+      }
+    }
+    if (exec) cudaGraphExecDestroy(exec);
+    if (rs != cudaSuccess) return fail(e, MLLM_ERR_CUDA, "batched decode step: %s", cudaGetErrorString(rs));
+  }
+  lwe_mark_time(e->d_status, ST_TEND, st);
+  std::vector<int32_t> counts(n_seq);
+  CUDA_TRY(e, cudaMemcpyAsync(out_ids, d_bout, (size_t)n_seq * max_new * 4, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(e, cudaMemcpyAsync(counts.data(), d_counts, (size_t)n_seq * 4, cudaMemcpyDeviceToHost, st));
+  TRY(fetch_status(e));
+  TRY(finish(e));
+  int total = 0;
+  for (int q = 0; q < n_seq; ++q) {
+    const int c = std::abs(counts[q]);
+    n_out[q] = c;
+    total += c;
+    if (stop) stop[q] = (c > 0 && out_ids[(size_t)q * max_new + c - 1] == eos) ? MLLM_STOP_EOS : MLLM_STOP_MAX_NEW;
+    e->slots[q].cache_len = std::min(lens[q] + c - 1, kv_len);
+  }
+  if (stats) {
+    const int32_t* hs = e->h_status;
+    stats->n_seq = n_seq;
+    stats->total_generated = total;
+    stats->steps = steps;
+    stats->prefill_forwards = nchunk;
+    const uint64_t t0 = u64_at(hs, ST_T0), t1 = u64_at(hs, ST_TFIRST), t2 = u64_at(hs, ST_TEND);
+    stats->prefill_ms = t1 > t0 ? (float)((t1 - t0) * 1e-6) : 0.f;
+    stats->total_ms = t2 > t0 ? (float)((t2 - t0) * 1e-6) : 0.f;
+  }
+  return MLLM_OK;
 }
 
 }  // extern "C"

@@ -1,0 +1,64 @@
+// Arguments of the layer-wise engine kernels (lwe.cu), shared with the host runtime (engine.cu).
+#pragma once
+#include <cuda_fp16.h>
+
+#include <cstdint>
+#include <vector>
+
+#include "engine.cuh"
+
+namespace mllm {
+
+constexpr int kLweMaxRep = 4;  // query heads per kv head handled by one attention CTA
+
+struct LweArgs {
+  ModelDev m;
+  int layer;
+  float* x;               // [tmax][D] residual stream
+  __half* xh;             // [tmax][ldx] fp16 hi of the GEMM input (norm / attention output)
+  __half* xl;
+  int ldx;
+  __half* xh2;            // [tmax][ldx2] fp16 hi of the w2 / mlp.proj input
+  __half* xl2;
+  int ldx2;
+  float* qkv;             // [tmax][QKV]
+  int32_t* tok;           // [tmax] token ids
+  int32_t* slot;          // [tmax] sequence slots
+  int32_t* pos;           // [tmax] positions
+  float* const* kc;       // [max_slots] per-slot K cache bases ([layer][kvHead][kvLen][64])
+  float* const* vc;
+  float* pval;            // [nblk][lm_cap] lm_head argmax partials
+  int32_t* pidx;
+  int lm_cap;
+  int32_t* amax;          // [lm_cap] argmax per lm row
+  int32_t* lm_src;        // [lm_cap] token index of each lm row
+  int* err;               // device error flag: 2 = a token id out of range
+};
+
+// Host-side copies of the per-layer descriptors the launches pass by value.
+struct LweHost {
+  std::vector<LayerDev> layers;
+};
+
+cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_from_src, float* logits,
+                        cudaStream_t st);
+size_t lwe_gemm_smem();
+// One prompt (or forward) chunk of a single slot: ids (device) at positions pos0.., lm rows either
+// every token (lm_each) or the last one.
+void lwe_fill(LweArgs a, const int32_t* ids, int n, int slot, int pos0, int lm_each, cudaStream_t st);
+void lwe_first(LweArgs a, int32_t* out_ids, int32_t* status, int eos, int forwards, cudaStream_t st);
+void lwe_mark_time(int32_t* status, int idx, cudaStream_t st);
+// Replicated multi-sequence decode
+void lwe_gather(int32_t* tok, const int32_t* ids, const int32_t* src, int n, cudaStream_t st);
+void lwe_batch_first(const int32_t* amax, const int32_t* lm_slot, int nlm, int max_new, int eos, int kv_len,
+                     int32_t* out_ids, int32_t* counts, const int32_t* lens, cudaStream_t st);
+void lwe_batch_decode_setup(LweArgs a, int n, const int32_t* out_ids, const int32_t* counts, const int32_t* lens,
+                            int max_new, cudaStream_t st);
+void lwe_batch_advance(LweArgs a, int n, int max_new, int eos, int32_t* out_ids, int32_t* counts,
+                       const int32_t* lens, cudaStream_t st);
+void lwe_count_active(const int32_t* counts, int n, int32_t* active, cudaStream_t st);
+size_t lwe_argmax_pen_smem(int V, int max_new);
+void lwe_penalised_argmax(const float* logits, int V, int T, const int32_t* out_ids, const int32_t* counts, int max_new,
+                          int32_t* amax, cudaStream_t st);
+
+}  // namespace mllm

@@ -79,14 +79,80 @@ __device__ __forceinline__ void split_hi_lo(float x, __half& hi, __half& lo) {
 // GEMM over a token batch.  X_hi/X_lo: fp16 [T][ldx] (k contiguous).  W: PGW packed rows, S: scales.
 // Epilogue `epi(row, token, value)` is called for every (row < R, token < T) of the CTA's tile, from
 // the lane that owns it.  TBW = 8-token blocks per warp (CTA covers 8 * TBW tokens).
+// Row source of the default GEMM: tile row i -> matrix row r0 + i.
+struct RowsLinear {
+  const uint8_t* W;
+  const float* S;
+  int R, r0, half_k, ng;
+  __device__ __forceinline__ bool valid(int i) const { return r0 + i < R; }
+  __device__ __forceinline__ const uint8_t* wrow(int i) const { return W + (size_t)min(r0 + i, R - 1) * half_k; }
+  __device__ __forceinline__ const float* srow(int i) const { return S + (size_t)min(r0 + i, R - 1) * ng; }
+};
+
+// Row source pairing two matrices with the same shape (w1 and w3): in each 16-row warp tile, rows
+// 0..7 come from A and rows 8..15 from B at the same matrix rows, so the lane that owns row gid of A
+// also owns row gid of B (accumulator elements 0/1 and 2/3).
+struct RowsPaired {
+  const uint8_t* WA;
+  const float* SA;
+  const uint8_t* WB;
+  const float* SB;
+  int R, r0, half_k, ng;  // r0: first matrix row of the CTA (32 per CTA)
+  __device__ __forceinline__ int mrow(int i) const { return r0 + (i >> 4) * 8 + (i & 7); }
+  __device__ __forceinline__ bool valid(int i) const { return mrow(i) < R; }
+  __device__ __forceinline__ const uint8_t* wrow(int i) const {
+    return ((i & 8) ? WB : WA) + (size_t)min(mrow(i), R - 1) * half_k;
+  }
+  __device__ __forceinline__ const float* srow(int i) const {
+    return ((i & 8) ? SB : SA) + (size_t)min(mrow(i), R - 1) * ng;
+  }
+};
+
+template <int TBW, class Rows>
+__device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __restrict__ Xhi,
+                                             const __half* __restrict__ Xlo, int ldx, int K, int T, int t0,
+                                             unsigned char* smem, float (&acc)[TBW][4]);
+
+// Element-wise epilogue form: epi(tile_row, token, value) for every valid (row, token) of the tile.
+template <int TBW, class Rows, class Epi>
+__device__ __forceinline__ void q4_gemm_rows(const Rows& rows, const __half* __restrict__ Xhi,
+                                             const __half* __restrict__ Xlo, int ldx, int K, int T, int t0,
+                                             unsigned char* smem, Epi epi) {
+  float acc[TBW][4];
+  q4_gemm_core<TBW>(rows, Xhi, Xlo, ldx, K, T, t0, smem, acc);
+  // lane (gid, t) owns tile rows gid, gid+8 of its warp and tokens 2t, 2t+1 of each 8-token block
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
+  const int ia = warp * 16 + gid, ib = ia + 8;
+  const bool va = rows.valid(ia), vb = rows.valid(ib);
+#pragma unroll
+  for (int b = 0; b < TBW; ++b) {
+    const int ta = t0 + b * 8 + 2 * t, tb = ta + 1;
+    if (va && ta < T) epi(ia, ta, acc[b][0]);
+    if (va && tb < T) epi(ia, tb, acc[b][1]);
+    if (vb && ta < T) epi(ib, ta, acc[b][2]);
+    if (vb && tb < T) epi(ib, tb, acc[b][3]);
+  }
+}
+
 template <int TBW, class Epi>
 __device__ __forceinline__ void q4_gemm_tile(const uint8_t* __restrict__ W, const float* __restrict__ S,
                                              const __half* __restrict__ Xhi, const __half* __restrict__ Xlo, int ldx,
                                              int R, int K, int T, int r0, int t0, unsigned char* smem, Epi epi) {
+  const RowsLinear rows{W, S, R, r0, K >> 1, K >> 5};
+  q4_gemm_rows<TBW>(rows, Xhi, Xlo, ldx, K, T, t0, smem, [&](int i, int t, float v) { epi(r0 + i, t, v); });
+}
+
+// Main loop: `rows` maps tile rows 0..63 to weight rows; acc[b][0..3] of lane (gid, t) hold tile rows
+// (16 warp + gid, same, +8, +8) x tokens (t0 + 8b + 2t, +1, 2t, +1).  Ends with all copies drained.
+template <int TBW, class Rows>
+__device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __restrict__ Xhi,
+                                             const __half* __restrict__ Xlo, int ldx, int K, int T, int t0,
+                                             unsigned char* smem, float (&acc)[TBW][4]) {
   constexpr int BT = 8 * TBW;  // tokens per CTA
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gid = lane >> 2, t = lane & 3;
   const int ng = K >> 5;
+  (void)ng;
   // stage layout
   uint8_t* w_s = smem;                                           // [kStages][64][16]
   float* s_s = reinterpret_cast<float*>(w_s + kStages * kGemmRows * 16);  // [kStages][64]
@@ -94,14 +160,10 @@ __device__ __forceinline__ void q4_gemm_tile(const uint8_t* __restrict__ W, cons
   __half* xl_s = xh_s + kStages * BT * kXPad;
   auto issue = [&](int g, int st) {
     // weights: 64 rows x 16 B, scales: 64 floats (16 x 16 B), activations: BT rows x 64 B x 2
-    for (int i = threadIdx.x; i < kGemmRows; i += kGemmThreads) {
-      const int r = r0 + i;
-      cp_async16(w_s + (st * kGemmRows + i) * 16, W + (size_t)min(r, R - 1) * (K >> 1) + g * 16, r < R);
-    }
-    if (threadIdx.x < kGemmRows) {  // scales of a group are one float per row (stride ng)
-      const int r = r0 + threadIdx.x;
-      cp_async4(s_s + st * kGemmRows + threadIdx.x, S + (size_t)min(r, R - 1) * ng + g, r < R);
-    }
+    for (int i = threadIdx.x; i < kGemmRows; i += kGemmThreads)
+      cp_async16(w_s + (st * kGemmRows + i) * 16, rows.wrow(i) + g * 16, rows.valid(i));
+    if (threadIdx.x < kGemmRows)  // scales of a group are one float per row (stride ng)
+      cp_async4(s_s + st * kGemmRows + threadIdx.x, rows.srow(threadIdx.x) + g, rows.valid(threadIdx.x));
     for (int i = threadIdx.x; i < BT * 4; i += kGemmThreads) {  // 4 x 16 B per token row (32 fp16)
       const int tk = i >> 2, c = i & 3;
       const int tok = t0 + tk;
@@ -111,7 +173,6 @@ __device__ __forceinline__ void q4_gemm_tile(const uint8_t* __restrict__ W, cons
       cp_async16(xl_s + (st * BT + tk) * kXPad + c * 8, Xlo + off, ok);
     }
   };
-  float acc[TBW][4];
 #pragma unroll
   for (int b = 0; b < TBW; ++b)
 #pragma unroll
@@ -154,16 +215,6 @@ __device__ __forceinline__ void q4_gemm_tile(const uint8_t* __restrict__ W, cons
     }
   }
   cp_async_wait<0>();
-  // epilogue: lane (gid, t) owns rows gid, gid+8 and tokens 2t, 2t+1 of each 8-token block
-  const int ra = r0 + warp * 16 + gid, rb = ra + 8;
-#pragma unroll
-  for (int b = 0; b < TBW; ++b) {
-    const int ta = t0 + b * 8 + 2 * t, tb = ta + 1;
-    if (ra < R && ta < T) epi(ra, ta, acc[b][0]);
-    if (ra < R && tb < T) epi(ra, tb, acc[b][1]);
-    if (rb < R && ta < T) epi(rb, ta, acc[b][2]);
-    if (rb < R && tb < T) epi(rb, tb, acc[b][3]);
-  }
 }
 
 template <int TBW>

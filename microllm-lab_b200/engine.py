@@ -26,7 +26,8 @@ STOP_NAMES = {0: "eos", 1: "max_new_tokens", 2: "context_limit"}
 
 EXPORTS = ["mllm_create", "mllm_destroy", "mllm_last_error", "mllm_config", "mllm_set_stream", "mllm_bytes_allocated",
            "mllm_reset",
-           "mllm_cache_len", "mllm_forward", "mllm_generate", "mllm_generate_device", "mllm_selftest_timeout",
+           "mllm_cache_len", "mllm_forward", "mllm_generate", "mllm_generate_device", "mllm_generate_batch",
+           "mllm_selftest_timeout",
            "mllm_gemv_q4", "mllm_gemm_q4", "mllm_gemm_q4_noalloc"]
 
 
@@ -42,6 +43,11 @@ class Stats(ctypes.Structure):
     _fields_ = [("n_generated", ctypes.c_int32), ("stop_reason", ctypes.c_int32), ("spec_hits", ctypes.c_int32),
                 ("spec_tries", ctypes.c_int32), ("forwards", ctypes.c_int32), ("prompt_len", ctypes.c_int32),
                 ("ttft_ms", ctypes.c_float), ("total_ms", ctypes.c_float)]
+
+
+class BatchStats(ctypes.Structure):
+    _fields_ = [("n_seq", ctypes.c_int32), ("total_generated", ctypes.c_int32), ("steps", ctypes.c_int32),
+                ("prefill_forwards", ctypes.c_int32), ("prefill_ms", ctypes.c_float), ("total_ms", ctypes.c_float)]
 
 
 _LIB = None
@@ -69,6 +75,7 @@ def load_library(path: str = LIB_PATH):
     L.mllm_forward.argtypes = [P, I, P, I, I, I, P, P]
     L.mllm_generate.argtypes = [P, I, P, I, I, ctypes.c_int32, I, I, P, ctypes.POINTER(Stats)]
     L.mllm_generate_device.argtypes = [P, I, P, I, I, ctypes.c_int32, I, I, P, ctypes.POINTER(Stats)]
+    L.mllm_generate_batch.argtypes = [P, I, P, P, I, ctypes.c_int32, P, P, P, ctypes.POINTER(BatchStats)]
     L.mllm_gemv_q4.argtypes = [P, P, P, P, I, I, I, P]
     L.mllm_gemm_q4.argtypes = [P, P, P, P, I, I, I, P]
     L.mllm_gemm_q4_noalloc.argtypes = [P, P, P, P, I, I, I, P]
@@ -218,6 +225,32 @@ class CudaPetitGPT:
             for i, t in enumerate(gen):
                 onToken(t, {"phase": "prefill" if i == 0 else "decode"})
         return res
+
+    def generateBatch(self, seqs, maxNewTokens: int = 64, eosId: int = SPECIAL["EOS"]):
+        """Replicated multi-sequence greedy decode (mllm_generate_batch): ``seqs`` is a list of prompts;
+        sequence s runs on slot s.  Returns (results, stats) where results[s] is the dict
+        ``generate`` would return for that prompt alone (generatedIds, stopReason) and stats holds the
+        batch counters and device times."""
+        seqs = [np.ascontiguousarray(q, np.int32) for q in seqs]
+        n = len(seqs)
+        offs = np.zeros(n + 1, np.int32)
+        offs[1:] = np.cumsum([len(q) for q in seqs])
+        flat = np.concatenate(seqs) if n else np.zeros(0, np.int32)
+        flat = np.ascontiguousarray(flat, np.int32)
+        out = np.zeros((n, max(int(maxNewTokens), 1)), np.int32)
+        n_out = np.zeros(n, np.int32)
+        stop = np.zeros(n, np.int32)
+        st = BatchStats()
+        t0 = time.perf_counter()
+        self._check(self._lib.mllm_generate_batch(self._h, n, _ptr(flat), _ptr(offs), int(maxNewTokens), int(eosId),
+                                                  _ptr(out), _ptr(n_out), _ptr(stop), ctypes.byref(st)))
+        wall = (time.perf_counter() - t0) * 1e3
+        res = [{"generatedIds": out[i, :n_out[i]].tolist(), "stopReason": STOP_NAMES.get(int(stop[i]), "max_new_tokens")}
+               for i in range(n)]
+        stats = {"nSeq": int(st.n_seq), "totalGenerated": int(st.total_generated), "steps": int(st.steps),
+                 "prefillForwards": int(st.prefill_forwards), "prefillMs": float(st.prefill_ms),
+                 "deviceMs": float(st.total_ms), "totalMs": wall}
+        return res, stats
 
     def selftest_timeout(self, wait_ms: int = 50) -> int:
         """Run the device wait-limit self-test; returns the mllm_status (MLLM_ERR_TIMEOUT = -6 expected)."""

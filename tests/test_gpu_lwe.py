@@ -1,0 +1,167 @@
+"""Layer-wise (token-batch) engine on the tensor cores, through the C ABI, against the CPU oracle:
+multi-token forwards (prefill, verify rows) and the replicated multi-sequence decode
+(mllm_generate_batch).
+
+Bars: token ids and stop reasons bit-exact per sequence; logits max-abs <= 2e-2."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, pkg
+from oracle import oracle as O
+
+LOGIT_TOL = 2e-2
+
+
+def _data(name):
+    P = pkg()
+    if name == "tiny-llama":
+        return P.synthetic_pgw("tiny-llama", 3)
+    if name == "tiny-gpt2":
+        return P.synthetic_pgw("tiny-gpt2", 4)
+    return open(os.path.join(GOLDEN, name.replace("-", "_") + ".pgw"), "rb").read()
+
+
+def _engine(data, monkeypatch=None, env=None, **kw):
+    """Engine created with extra environment knobs (read by mllm_create only)."""
+    P = pkg()
+    env = env or {}
+    old = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
+    try:
+        return P.CudaPetitGPT(data, **kw)
+    finally:
+        for k, v in old.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+
+
+@pytest.fixture(scope="module")
+def batch_models(cuda_ok):
+    out = {}
+    for name in ["tiny-llama", "tiny-gpt2", "ref-llama", "ref-gpt2"]:
+        data = _data(name)
+        out[name] = (data, _engine(data, max_slots=8), O.OracleModel(data))
+    yield out
+    for _, eng, _ in out.values():
+        eng.destroy()
+
+
+def _prompts(V, lens, seed):
+    P = pkg()
+    return [P.seeded_prompt(n, V, seed + i) for i, n in enumerate(lens)]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["tiny-llama", "tiny-gpt2", "ref-llama", "ref-gpt2"])
+def test_batch_matches_per_sequence_oracle(batch_models, name):
+    """Each sequence of the batch equals engine/infer.js:603-646 run alone (GPT-2: argmaxGpt2 over
+    that sequence's own ids)."""
+    data, eng, om = batch_models[name]
+    V = eng.cfg["vocabSize"]
+    seqs = _prompts(V, [1, 5, 17, 33, 9, 12], 40)
+    res, st = eng.generateBatch(seqs, maxNewTokens=32, eosId=-1)
+    assert st["nSeq"] == len(seqs) and st["totalGenerated"] == 32 * len(seqs)
+    for q, r in zip(seqs, res):
+        ref = om.generate(q, 32, eos=-1)
+        assert r["generatedIds"] == ref["generatedIds"]
+        assert r["stopReason"] == ref["stopReason"]
+
+
+@pytest.mark.gpu
+def test_batch_single_sequence_equals_generate(batch_models):
+    data, eng, om = batch_models["ref-llama"]
+    ids = pkg().seeded_prompt(20, eng.cfg["vocabSize"], 50)
+    res, _ = eng.generateBatch([ids], maxNewTokens=24, eosId=-1)
+    assert res[0]["generatedIds"] == eng.generate(ids, maxNewTokens=24, eosId=-1)["generatedIds"]
+
+
+@pytest.mark.gpu
+def test_batch_stop_rules(batch_models):
+    """EOS per sequence (the others keep going), maxNewTokens = 1, and the cache-length stop."""
+    data, eng, om = batch_models["tiny-llama"]
+    seqs = _prompts(512, [12, 7, 20, 3], 60)
+    full = om.generate(seqs[0], 20, eos=-1)["generatedIds"]
+    eos = full[5]
+    res, _ = eng.generateBatch(seqs, maxNewTokens=20, eosId=eos)
+    for q, r in zip(seqs, res):
+        ref = om.generate(q, 20, eos=eos)
+        assert r["generatedIds"] == ref["generatedIds"] and r["stopReason"] == ref["stopReason"]
+    assert res[0]["stopReason"] == "eos" and len(res[0]["generatedIds"]) == 6
+    res, st = eng.generateBatch(seqs, maxNewTokens=1, eosId=-1)
+    assert [r["generatedIds"] for r in res] == [om.generate(q, 1, eos=-1)["generatedIds"] for q in seqs]
+    assert st["steps"] == 0
+    # maxNewTokens 170 > maxSeqLen 160: prompts cut to 1 id, decode stops at the cache length
+    res, _ = eng.generateBatch(seqs[:3], maxNewTokens=170, eosId=-1)
+    for q, r in zip(seqs[:3], res):
+        ref = om.generate(q, 170, eos=-1)
+        assert r["generatedIds"] == ref["generatedIds"]
+        assert len(r["generatedIds"]) == 159
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("env", [{"MLLM_LWE_TOKENS": "16"}, {"MLLM_LWE_GRAPH": "0"}])
+def test_batch_chunked_prefill_and_plain_launches(cuda_ok, env):
+    """16 token rows per forward (prompts split across forwards and forwards mixing sequences), and
+    the decode step launched without a CUDA graph."""
+    data = _data("tiny-llama")
+    eng = _engine(data, env=env, max_slots=5)
+    om = O.OracleModel(data)
+    seqs = _prompts(512, [40, 3, 16, 17, 9], 70)
+    res, st = eng.generateBatch(seqs, maxNewTokens=16, eosId=-1)
+    if "MLLM_LWE_TOKENS" in env:
+        assert st["prefillForwards"] == (sum(len(q) for q in seqs) + 15) // 16
+    for q, r in zip(seqs, res):
+        assert r["generatedIds"] == om.generate(q, 16, eos=-1)["generatedIds"]
+    eng.destroy()
+
+
+@pytest.mark.gpu
+def test_batch_argument_errors(batch_models):
+    P = pkg()
+    data, eng, om = batch_models["tiny-llama"]
+    with pytest.raises(P.MllmError, match="n_seq"):
+        eng.generateBatch([[1, 2]] * 9, maxNewTokens=4)
+    with pytest.raises(P.MllmError, match="empty prompt"):
+        eng.generateBatch([[1, 2], []], maxNewTokens=4)
+    with pytest.raises(P.MllmError, match="out of range"):
+        eng.generateBatch([[1, 2], [3, 600]], maxNewTokens=4)
+    # the handle keeps working
+    q = pkg().seeded_prompt(6, 512, 80)
+    res, _ = eng.generateBatch([q], maxNewTokens=6, eosId=-1)
+    assert res[0]["generatedIds"] == om.generate(q, 6, eos=-1)["generatedIds"]
+
+
+@pytest.mark.gpu
+def test_chunked_forward_rows(cuda_ok):
+    """Multi-token forwards split over 16-row forwards: prompt logits and verify rows at pos0 > 0."""
+    data = _data("ref-llama")
+    eng = _engine(data, env={"MLLM_LWE_TOKENS": "16"})
+    om = O.OracleModel(data)
+    V = eng.cfg["vocabSize"]
+    ids = pkg().seeded_prompt(60, V, 81)
+    g = eng.forwardPrompt(ids[:37])
+    r = om.forward_prompt(ids[:37])
+    assert np.abs(g - r).max() <= LOGIT_TOL
+    g, am = eng.forward(ids[37:60], 37, logits_each=True)
+    r = om.forward(ids[37:60], 37, logits_each=True)
+    assert np.abs(g - r).max() <= LOGIT_TOL
+    assert am.tolist() == [int(np.argmax(x)) for x in r]
+    eng.destroy()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["tiny-llama", "tiny-gpt2"])
+def test_persistent_prefill_path_still_matches(cuda_ok, name):
+    """MLLM_LWE_PREFILL=0 keeps prefill on the persistent kernel: same streams as the oracle."""
+    data = _data(name)
+    eng = _engine(data, env={"MLLM_LWE_PREFILL": "0"})
+    om = O.OracleModel(data)
+    ids = pkg().seeded_prompt(21, eng.cfg["vocabSize"], 82)
+    assert eng.generate(ids, maxNewTokens=20, eosId=-1)["generatedIds"] == om.generate(ids, 20, eos=-1)["generatedIds"]
+    g = eng.forwardPrompt(ids)
+    assert np.abs(g - om.forward_prompt(ids)).max() <= LOGIT_TOL
+    eng.destroy()
