@@ -6,6 +6,7 @@
 // mllm_forward : forwardPrompt / forwardDecode / the verify forward (engine/infer.js:553-601,
 //                engine/webgpu.js:1248).
 // mllm_generate: engine/infer.js:603-646 and engine/webgpu.js:1164-1282 in one device launch.
+#include <cuda_profiler_api.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -292,6 +293,10 @@ int finish(mllm_engine* e) {
       fclose(f);
     }
   }
+  if (e->h_status[ST_WORDS] != 0) {
+    // a CTA that gave up may have left a completion counter of the token-batch kernels non-zero
+    cudaMemset(e->lh.attn_ctr, 0, e->lh.attn_ctr_n * sizeof(int));
+  }
   if (e->h_status[ST_WORDS] == 2) return fail(e, MLLM_ERR_ARG, "a prompt token id is out of range");
   if (e->h_status[ST_WORDS] != 0)
     return fail(e, MLLM_ERR_TIMEOUT, "a device-side wait exceeded its time limit; the call was abandoned");
@@ -325,7 +330,7 @@ int lwe_run(mllm_engine* e, int slot, const int32_t* d_ids, int n, int pos0, int
     b.amax = d_amax + (lm_each ? c0 : 0);
     const int lm_T = lm_each ? Tc : (last ? 1 : 0);
     float* lg = d_logits && lm_T ? d_logits + (size_t)(lm_each ? c0 : 0) * V : nullptr;
-    CUDA_TRY(e, lwe_forward(b, e->lh, Tc, lm_T, !lm_each, lg, e->stream));
+    CUDA_TRY(e, lwe_forward(b, e->lh, Tc, lm_T, !lm_each, lg, false, e->stream));
     ++f;
   }
   *forwards = f;
@@ -575,9 +580,12 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   e->lwe_ok = md.NH / md.NKV <= kLweMaxRep;
   if (const char* v = getenv("MLLM_LWE_PREFILL")) e->lwe_prefill = atoi(v) ? 1 : 0;
   if (const char* v = getenv("MLLM_LWE_GRAPH")) e->lwe_graph = atoi(v) ? 1 : 0;
+  if (const char* v = getenv("MLLM_LWE_FOLD_NORM")) e->lh.fold_norm = atoi(v) ? 1 : 0;
+  if (const char* v = getenv("MLLM_LWE_ATTN_SPLIT")) e->lh.attn_split = atoi(v) ? 1 : 0;
   e->tmax = 1024;
   if (const char* v = getenv("MLLM_LWE_TOKENS")) e->tmax = std::max(16, std::min(8192, atoi(v)));
   e->lh.layers = layers;
+  if (lwe_setup(md.kv_len) != cudaSuccess) return bad(MLLM_ERR_CUDA, "cudaFuncSetAttribute failed (token-batch kernels)");
   {
     LweArgs& w = e->lw;
     const size_t T = e->tmax;
@@ -588,9 +596,19 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
     const size_t nblk = (md.vocab + 63) / 64;
     float** kc;
     float** vc;
+    int chunk, splits;
+    lwe_attn_split_shape(md.kv_len, &chunk, &splits);
+    const size_t rep = md.NH / md.NKV;
+    if ((rc = dev_alloc(E, &e->lh.attn_part, T * md.NKV * splits * rep * 66 * 4)) ||
+        (rc = dev_alloc(E, &e->lh.attn_ctr, T * md.NKV * sizeof(int))))
+      return relay(rc);
+    e->lh.attn_ctr_n = T * md.NKV;
+    cudaMemset(e->lh.attn_ctr, 0, T * md.NKV * sizeof(int));
     if ((rc = dev_alloc(E, &w.x, T * D * 4)) || (rc = dev_alloc(E, &w.xh, T * w.ldx * 2)) ||
         (rc = dev_alloc(E, &w.xl, T * w.ldx * 2)) || (rc = dev_alloc(E, &w.xh2, T * w.ldx2 * 2)) ||
         (rc = dev_alloc(E, &w.xl2, T * w.ldx2 * 2)) || (rc = dev_alloc(E, &w.qkv, T * md.QKV * 4)) ||
+        (rc = dev_alloc(E, &w.xh3, T * w.ldx * 2)) || (rc = dev_alloc(E, &w.xl3, T * w.ldx * 2)) ||
+        (rc = dev_alloc(E, &w.ss, T * kLweSsStride * 4)) ||
         (rc = dev_alloc(E, &w.tok, T * 4)) || (rc = dev_alloc(E, &w.slot, T * 4)) || (rc = dev_alloc(E, &w.pos, T * 4)) ||
         (rc = dev_alloc(E, &w.lm_src, T * 4)) || (rc = dev_alloc(E, &w.amax, T * 4)) ||
         (rc = dev_alloc(E, &w.pval, nblk * T * 4)) || (rc = dev_alloc(E, &w.pidx, nblk * T * 4)) ||
@@ -841,7 +859,7 @@ int mllm_generate_batch(mllm_engine* e, int n_seq, const int32_t* ids, const int
     a.pos = const_cast<int32_t*>(d_ppos + c0);
     a.lm_src = const_cast<int32_t*>(d_lmsrc + lm_off[c]);
     lwe_gather(a.tok, d_bids, d_psrc + c0, Tc, st);
-    CUDA_TRY(e, lwe_forward(a, e->lh, Tc, nlm, true, nullptr, st));
+    CUDA_TRY(e, lwe_forward(a, e->lh, Tc, nlm, true, nullptr, false, st));
     if (nlm) lwe_batch_first(a.amax, d_lmslot + lm_off[c], nlm, max_new, eos, kv_len, d_bout, d_counts, d_lens, st);
   }
   lwe_mark_time(e->d_status, ST_TFIRST, st);
@@ -853,7 +871,7 @@ int mllm_generate_batch(mllm_engine* e, int n_seq, const int32_t* ids, const int
     const LweArgs d = base;  // tok/slot/pos/lm_src: the engine's own rows
     lwe_batch_decode_setup(d, n_seq, d_bout, d_counts, d_lens, max_new, st);
     auto step = [&]() -> cudaError_t {
-      cudaError_t r = lwe_forward(d, e->lh, n_seq, n_seq, false, gpt2 ? d_blogits : nullptr, st);
+      cudaError_t r = lwe_forward(d, e->lh, n_seq, n_seq, false, gpt2 ? d_blogits : nullptr, true, st);
       if (r != cudaSuccess) return r;
       if (gpt2) lwe_penalised_argmax(d_blogits, md.vocab, n_seq, d_bout, d_counts, max_new, d.amax, st);
       lwe_batch_advance(d, n_seq, max_new, eos, d_bout, d_counts, d_lens, st);
@@ -877,7 +895,16 @@ int mllm_generate_batch(mllm_engine* e, int n_seq, const int32_t* ids, const int
     // With an EOS id the batch may finish early: every 16 steps the number of running sequences is
     // read back (the steps already queued behind it keep the GPU busy meanwhile).
     cudaError_t rs = cudaSuccess;
+    // MLLM_PROFILE_DECODE_STEPS=k brackets the first k decode steps with cudaProfilerStart/Stop (for
+    // a profiler started with profiling off).
+    int prof_steps = 0;
+    if (const char* v = getenv("MLLM_PROFILE_DECODE_STEPS")) prof_steps = atoi(v);
+    if (prof_steps > 0) cudaProfilerStart();
     for (; steps < steps_max && rs == cudaSuccess; ++steps) {
+      if (prof_steps > 0 && steps == prof_steps) {
+        cudaStreamSynchronize(st);
+        cudaProfilerStop();
+      }
       rs = exec ? cudaGraphLaunch(exec, st) : step();
       if (eos >= 0 && rs == cudaSuccess && (steps & 15) == 15 && steps + 1 < steps_max) {
         lwe_count_active(d_counts, n_seq, d_active, st);
@@ -888,6 +915,10 @@ int mllm_generate_batch(mllm_engine* e, int n_seq, const int32_t* ids, const int
           break;
         }
       }
+    }
+    if (prof_steps > 0 && steps <= prof_steps) {
+      cudaStreamSynchronize(st);
+      cudaProfilerStop();
     }
     if (exec) cudaGraphExecDestroy(exec);
     if (rs != cudaSuccess) return fail(e, MLLM_ERR_CUDA, "batched decode step: %s", cudaGetErrorString(rs));

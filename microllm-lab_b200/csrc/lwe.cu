@@ -20,11 +20,96 @@
 
 namespace mllm {
 
-constexpr int kLweTBW = 8;  // 64 tokens per GEMM CTA
-constexpr int kLweBT = 8 * kLweTBW;
+// GEMM tiles: 64 weight rows x 8*TBW tokens per CTA; TBW is picked per launch so that small-R GEMMs
+// still fill the GPU, and the k-pipeline is deeper for the smaller token tiles (all under 48 KB).
+// The k groups may also be split over KS groups of 4 warps inside the CTA (more warps in flight per
+// SM when a GEMM has few CTAs); the pipeline is deeper for the smaller tiles (all under 100 KB).
+template <int TBW, int KSPLIT>
+struct LweTile {
+  static constexpr int BT = 8 * TBW;
+  static constexpr int KS = KSPLIT;
+  static constexpr int NS = KS == 1 ? (TBW == 8 ? 4 : (TBW == 4 ? 6 : 8))
+                                    : (KS == 2 ? (TBW == 8 ? 3 : (TBW == 4 ? 4 : 6)) : (TBW == 8 ? 2 : (TBW == 4 ? 3 : 4)));
+  static constexpr int THREADS = kGemmThreads * KS;
+  static constexpr size_t smem() { return q4_gemm_smem_bytes<TBW, NS, KS>(); }
+};
+
+// 1 / RMS of token t from the per-row-tile partial sums of squares the previous GEMM left in a.ss
+// (engine/infer.js:134-143 with the gain folded into the activations).
+__device__ __forceinline__ float fold_inv(const LweArgs& a, int t) {
+  const float* p = a.ss + (size_t)t * kLweSsStride;
+  const int nt = (a.m.D + kGemmRows - 1) / kGemmRows;
+  float s = 0.f;
+  for (int j = 0; j < nt; ++j) s += p[j];
+  return 1.f / sqrtf(s / a.m.D + 1e-6f);
+}
 
 // ---------------------------------------------------------------------------------------------
-__global__ void lwe_embed(const __grid_constant__ LweArgs a, int T) {
+// RMSNorm (engine/infer.js:134-143) or LayerNorm (engine/infer.js:147-164) of one row by one warp,
+// written as fp16 hi/lo.  The row (D <= 1024) is read once into registers through L2 (rows written by
+// other CTAs of the same launch).
+__device__ __forceinline__ void warp_norm_split(const float* x, int D, bool ln, const float* g, __half* oh,
+                                                __half* ol) {
+  const int lane = threadIdx.x & 31;
+  float4 v[8];
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int k = lane * 4 + i * 128;
+    v[i] = k < D ? ldcg_f4(x + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    s1 += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    s2 = fmaf(v[i].x, v[i].x, fmaf(v[i].y, v[i].y, fmaf(v[i].z, v[i].z, fmaf(v[i].w, v[i].w, s2))));
+  }
+  s1 = warp_sum(s1);
+  float mean = 0.f, inv;
+  if (!ln) {
+    s2 = warp_sum(s2);
+    inv = 1.f / sqrtf(s2 / D + 1e-6f);
+  } else {
+    mean = s1 / D;
+    float var = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int k = lane * 4 + i * 128;
+      if (k < D) {
+        var = fmaf(v[i].x - mean, v[i].x - mean, var);
+        var = fmaf(v[i].y - mean, v[i].y - mean, var);
+        var = fmaf(v[i].z - mean, v[i].z - mean, var);
+        var = fmaf(v[i].w - mean, v[i].w - mean, var);
+      }
+    }
+    var = warp_sum(var);
+    inv = 1.f / sqrtf(var / D + 1e-5f);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int k = lane * 4 + i * 128;
+    if (k >= D) break;
+    const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+    const float4 gg = *reinterpret_cast<const float4*>(g + k);
+    const float ga[4] = {gg.x, gg.y, gg.z, gg.w};
+    __half hh[4], ll[4];
+    if (!ln) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) split_hi_lo(e[j] * inv * ga[j], hh[j], ll[j]);
+    } else {
+      const float4 bb = *reinterpret_cast<const float4*>(g + D + k);
+      const float ba[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) split_hi_lo(fmaf((e[j] - mean) * inv, ga[j], ba[j]), hh[j], ll[j]);
+    }
+    *reinterpret_cast<__half2*>(oh + k) = __halves2half2(hh[0], hh[1]);
+    *reinterpret_cast<__half2*>(oh + k + 2) = __halves2half2(hh[2], hh[3]);
+    *reinterpret_cast<__half2*>(ol + k) = __halves2half2(ll[0], ll[1]);
+    *reinterpret_cast<__half2*>(ol + k + 2) = __halves2half2(ll[2], ll[3]);
+  }
+}
+
+// Embedding of token t (one CTA per token); with g != nullptr also the first layer's norm1 into xh/xl.
+__global__ void lwe_embed(const __grid_constant__ LweArgs a, int T, const float* g) {
   const int t = blockIdx.x;
   if (t >= T) return;
   const ModelDev& md = a.m;
@@ -44,6 +129,27 @@ __global__ void lwe_embed(const __grid_constant__ LweArgs a, int T) {
       v += md.wpe[(size_t)min(pos, md.max_seq - 1) * D + k];
     }
     a.x[(size_t)t * D + k] = v;
+  }
+  if (g) {
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const float* x = a.x + (size_t)t * D;
+      __half* oh = a.xh + (size_t)t * a.ldx;
+      __half* ol = a.xl + (size_t)t * a.ldx;
+      if (a.fold) {  // x * gain as fp16 hi/lo, sum of squares for the consumer's 1/RMS
+        float s2 = 0.f;
+        for (int k = threadIdx.x; k < D; k += 32) {
+          const float v = __ldcg(x + k);
+          s2 = fmaf(v, v, s2);
+          split_hi_lo(v * g[k], oh[k], ol[k]);
+        }
+        s2 = warp_sum(s2);
+        const int nt = (D + kGemmRows - 1) / kGemmRows;
+        if (threadIdx.x < nt) a.ss[(size_t)t * kLweSsStride + threadIdx.x] = threadIdx.x == 0 ? s2 : 0.f;
+      } else {
+        warp_norm_split(x, D, md.arch == 1, g, oh, ol);
+      }
+    }
   }
 }
 
@@ -98,16 +204,25 @@ __global__ void lwe_norm_split(const __grid_constant__ LweArgs a, int T, const f
   }
 }
 
-// QKV GEMM: qkv[t][r] = W_qkv[r] . norm1(x_t) (+ bias)
-__global__ void __launch_bounds__(kGemmThreads) lwe_gemm_qkv(const __grid_constant__ LweArgs a, int T, int l) {
+// QKV GEMM: qkv[t][r] = W_qkv[r] . norm1(x_t) (+ bias).  With a.fold the activations are x * gain and
+// the token's 1/RMS multiplies the result.
+template <int TBW, int KS>
+__global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_qkv(const __grid_constant__ LweArgs a, int T,
+                                                                         int l) {
   extern __shared__ __align__(16) unsigned char smem[];
+  using C = LweTile<TBW, KS>;
+  __shared__ float sinv[C::BT];
   const LayerDev& L = a.m.layers[l];
-  const int R = a.m.QKV, K = a.m.D;
+  const int R = a.m.QKV, K = a.m.D, t0 = blockIdx.y * C::BT;
+  if (threadIdx.x < C::BT) sinv[threadIdx.x] = a.fold && t0 + (int)threadIdx.x < T ? fold_inv(a, t0 + threadIdx.x) : 1.f;
+  __syncthreads();
   const float* bias = L.qkv_b;
   float* out = a.qkv;
-  q4_gemm_tile<kLweTBW>(reinterpret_cast<const uint8_t*>(L.qkv.w), L.qkv.s, a.xh, a.xl, a.ldx, R, K, T,
-                        blockIdx.x * kGemmRows, blockIdx.y * kLweBT, smem,
-                        [&](int r, int t, float v) { out[(size_t)t * R + r] = bias ? v + bias[r] : v; });
+  q4_gemm_tile<TBW, C::NS, C::KS>(reinterpret_cast<const uint8_t*>(L.qkv.w), L.qkv.s, a.xh, a.xl, a.ldx, R, K, T,
+                                  blockIdx.x * kGemmRows, t0, smem, [&](int r, int t, float v) {
+                                    v *= sinv[t - t0];
+                                    out[(size_t)t * R + r] = bias ? v + bias[r] : v;
+                                  });
 }
 
 // RoPE on k (and on the q heads of the group) at each token's position, then the K/V cache write
@@ -141,140 +256,423 @@ __global__ void lwe_rope_kv(const __grid_constant__ LweArgs a, int T) {
   a.vc[slot][kv + d] = v[d];
 }
 
-// Attention of the `rep` query heads of kv head g for token t over positions 0..pos[t] of its slot
-// (engine/infer.js:466-495), online softmax, 4 lanes per position (16 dims each), 4 warps.
-// Output rows are written as fp16 hi/lo into xh/xl for the proj GEMM.
+// Attention of the REP query heads of kv head g for token t over positions 0..pos[t] of its slot
+// (engine/infer.js:466-495).  grid (T, NKV), 128 threads.  Three passes over shared memory:
+// scores (one thread per position, the K row read as 16 float4, q broadcast from shared memory),
+// softmax per head (one warp per head), then P.V (16 threads per row of V, 8 position lanes, 8 rows
+// in flight per thread).  Output rows are written as fp16 hi/lo into xh/xl for the proj GEMM.
+// FUSED (every token of the launch in its own slot, as in a batched decode step): the CTA also applies
+// RoPE to its q heads and k (engine/infer.js:436-458) and writes the token's K/V row into the cache
+// (engine/infer.js:459-464) before reading the cache; otherwise lwe_rope_kv ran first.
+template <int REP, bool FUSED>
 __global__ void __launch_bounds__(128) lwe_attention(const __grid_constant__ LweArgs a, int T) {
+  extern __shared__ __align__(16) float asm_[];
   const int t = blockIdx.x, g = blockIdx.y;
   if (t >= T) return;
   const ModelDev& md = a.m;
-  const int NKV = md.NKV, rep = md.NH / NKV, pos = a.pos[t], npos = pos + 1;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, qd = lane & 3, pg = lane >> 2;
-  __shared__ float part[4][kLweMaxRep][68];
-  const float* qrow = a.qkv + (size_t)t * md.QKV + g * rep * 64;
-  float q[kLweMaxRep][16];
-#pragma unroll
-  for (int h = 0; h < kLweMaxRep; ++h)
-#pragma unroll
-    for (int i = 0; i < 16; ++i) q[h][i] = h < rep ? qrow[h * 64 + qd * 16 + i] : 0.f;
-  const size_t base = ((size_t)a.layer * NKV + g) * md.kv_len;
-  const float* kc = a.kc[a.slot[t]] + base * 64;
-  const float* vc = a.vc[a.slot[t]] + base * 64;
-  float m[kLweMaxRep], lsum[kLweMaxRep], o[kLweMaxRep][16];
-#pragma unroll
-  for (int h = 0; h < kLweMaxRep; ++h) {
-    m[h] = -INFINITY;
-    lsum[h] = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) o[h][i] = 0.f;
-  }
-  for (int p0 = warp * 8; p0 < npos; p0 += 32) {
-    const int p = p0 + pg;
-    const bool valid = p < npos;
-    float4 kk[4], vv[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      kk[j] = valid ? ldcg_f4(kc + (size_t)p * 64 + qd * 16 + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
-      vv[j] = valid ? ldcg_f4(vc + (size_t)p * 64 + qd * 16 + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const int NKV = md.NKV, pos = a.pos[t], npos = pos + 1, kvs = md.kv_len;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* qs = asm_;                  // [REP][64]
+  float* sc = qs + REP * 64;         // [REP][kv_len]
+  float* red = sc + REP * kvs;       // [8][REP][64]
+  __shared__ float inv_sum[REP];
+  __shared__ float ks[64];
+  const float* qrow = a.qkv + (size_t)t * md.QKV + g * REP * 64;
+  const size_t base = ((size_t)a.layer * NKV + g) * md.kv_len * 64;
+  float* kcw = a.kc[a.slot[t]] + base;
+  float* vcw = a.vc[a.slot[t]] + base;
+  for (int i = tid; i < REP * 64; i += 128) qs[i] = qrow[i];
+  if (FUSED) {
+    const float* krow = a.qkv + (size_t)t * md.QKV + md.D + g * 64;
+    const float* vrow = krow + NKV * 64;
+    if (tid < 64) {
+      ks[tid] = krow[tid];
+      vcw[(size_t)pos * 64 + tid] = vrow[tid];
     }
-#pragma unroll
-    for (int h = 0; h < kLweMaxRep; ++h) {
-      if (h >= rep) break;
-      float s = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        s = fmaf(q[h][4 * j], kk[j].x, s);
-        s = fmaf(q[h][4 * j + 1], kk[j].y, s);
-        s = fmaf(q[h][4 * j + 2], kk[j].z, s);
-        s = fmaf(q[h][4 * j + 3], kk[j].w, s);
+    __syncthreads();
+    if (md.arch == 0 && md.rope_dim > 0) {
+      const int half = md.rope_dim / 2;
+      const float* cs = md.rope_cos + (size_t)pos * md.rope_dim;
+      const float* sn = md.rope_sin + (size_t)pos * md.rope_dim;
+      // thread (h, d): h = -1 is the key, else query head h of the group; pair (d, d + half)
+      for (int i = tid; i < (REP + 1) * half; i += 128) {
+        const int h = i / half - 1, d = i % half;
+        float* p = h < 0 ? ks : qs + h * 64;
+        const float a0 = p[d], a1 = p[d + half];
+        p[d] = fmaf(-a1, sn[d], a0 * cs[d]);
+        p[d + half] = fmaf(a0, sn[d + half], a1 * cs[d + half]);
       }
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      const float sc = valid ? s * 0.125f : -INFINITY;  // 1/sqrt(64), exact (engine/infer.js:466)
-      const float newm = fmaxf(m[h], warp_max(sc));
-      const float e = valid ? expf(sc - newm) : 0.f;
-      const float corr = m[h] == -INFINITY ? 0.f : expf(m[h] - newm);
-      lsum[h] = fmaf(lsum[h], corr, warp_sum(qd == 0 ? e : 0.f));
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        o[h][4 * j] = fmaf(e, vv[j].x, o[h][4 * j] * corr);
-        o[h][4 * j + 1] = fmaf(e, vv[j].y, o[h][4 * j + 1] * corr);
-        o[h][4 * j + 2] = fmaf(e, vv[j].z, o[h][4 * j + 2] * corr);
-        o[h][4 * j + 3] = fmaf(e, vv[j].w, o[h][4 * j + 3] * corr);
-      }
-      m[h] = newm;
+      __syncthreads();
     }
+    if (tid < 64) kcw[(size_t)pos * 64 + tid] = ks[tid];
   }
+  const float* kc = kcw;
+  const float* vc = vcw;
+  __syncthreads();
+  // scores (engine/infer.js:470-476: f32(dot * 1/sqrt(64)))
+  for (int p = tid; p < npos; p += 128) {
+    const float4* kr = reinterpret_cast<const float4*>(kc + (size_t)p * 64);
+    float4 kk[16];
 #pragma unroll
-  for (int h = 0; h < kLweMaxRep; ++h) {
-    if (h >= rep) break;
+    for (int j = 0; j < 16; ++j) kk[j] = ldcg_f4(reinterpret_cast<const float*>(kr + j));
+    float s[REP];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      o[h][i] += __shfl_xor_sync(0xffffffffu, o[h][i], 4);
-      o[h][i] += __shfl_xor_sync(0xffffffffu, o[h][i], 8);
-      o[h][i] += __shfl_xor_sync(0xffffffffu, o[h][i], 16);
+    for (int h = 0; h < REP; ++h) {
+      s[h] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float4 q = reinterpret_cast<const float4*>(qs + h * 64)[j];
+        s[h] = fmaf(q.x, kk[j].x, s[h]);
+        s[h] = fmaf(q.y, kk[j].y, s[h]);
+        s[h] = fmaf(q.z, kk[j].z, s[h]);
+        s[h] = fmaf(q.w, kk[j].w, s[h]);
+      }
     }
-    if (lane == 0) {
-      part[warp][h][0] = m[h];
-      part[warp][h][1] = lsum[h];
-    }
-    if (pg == 0)
 #pragma unroll
-      for (int i = 0; i < 16; ++i) part[warp][h][4 + qd * 16 + i] = o[h][i];
+    for (int h = 0; h < REP; ++h) sc[h * kvs + p] = s[h] * 0.125f;
   }
   __syncthreads();
-  // combine the 4 warps: thread (h, d) for h < rep, d < 64 -> 128 threads cover 2 heads per pass
-  for (int hd = threadIdx.x; hd < rep * 64; hd += blockDim.x) {
-    const int h = hd >> 6, d = hd & 63;
-    float M = -INFINITY;
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, part[w][h][0]);
-    float Ls = 0.f, r = 0.f;
-    for (int w = 0; w < 4; ++w) {
-      if (part[w][h][1] > 0.f) {
-        const float f = expf(part[w][h][0] - M);
-        Ls = fmaf(part[w][h][1], f, Ls);
-        r = fmaf(part[w][h][4 + d], f, r);
+  // softmax per head (engine/infer.js:477-486)
+  if (warp < REP) {
+    float* row = sc + warp * kvs;
+    float m = -INFINITY;
+    for (int p = lane; p < npos; p += 32) m = fmaxf(m, row[p]);
+    m = warp_max(m);
+    float sum = 0.f;
+    for (int p = lane; p < npos; p += 32) {
+      const float e = expf(row[p] - m);
+      row[p] = e;
+      sum += e;
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) inv_sum[warp] = 1.f / sum;
+  }
+  __syncthreads();
+  // P.V (engine/infer.js:487-495): thread = (position lane pl, float4 column dq)
+  {
+    const int pl = tid >> 4, dq = tid & 15;
+    float4 acc[REP];
+#pragma unroll
+    for (int h = 0; h < REP; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p0 = pl; p0 < npos; p0 += 64) {
+      float4 vv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int p = min(p0 + 8 * u, pos);
+        vv[u] = ldcg_f4(vc + (size_t)p * 64 + dq * 4);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int p = p0 + 8 * u;
+        if (p < npos) {
+#pragma unroll
+          for (int h = 0; h < REP; ++h) {
+            const float e = sc[h * kvs + p];
+            acc[h].x = fmaf(e, vv[u].x, acc[h].x);
+            acc[h].y = fmaf(e, vv[u].y, acc[h].y);
+            acc[h].z = fmaf(e, vv[u].z, acc[h].z);
+            acc[h].w = fmaf(e, vv[u].w, acc[h].w);
+          }
+        }
       }
     }
-    const size_t off = (size_t)t * a.ldx + (g * rep + h) * 64 + d;
-    split_hi_lo(r / Ls, a.xh[off], a.xl[off]);
+#pragma unroll
+    for (int h = 0; h < REP; ++h) reinterpret_cast<float4*>(red + (pl * REP + h) * 64)[dq] = acc[h];
+  }
+  __syncthreads();
+  for (int hd = tid; hd < REP * 64; hd += 128) {
+    const int h = hd >> 6, d = hd & 63;
+    float r = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) r += red[(q * REP + h) * 64 + d];
+    const size_t off = (size_t)t * a.ldx + (g * REP + h) * 64 + d;
+    split_hi_lo(r * inv_sum[h], a.xh[off], a.xl[off]);
   }
 }
 
-// GEMM with a residual epilogue: x[t][r] += W[r] . in_t (+ bias)  (proj and w2)
-__global__ void __launch_bounds__(kGemmThreads) lwe_gemm_resid(const __grid_constant__ LweArgs a, int T, Q4 w,
-                                                               const float* bias, int K) {
+// Decode-step attention split over positions (flash-decoding): grid (T, NKV, S), 64 threads; split sp
+// covers positions [sp*64, sp*64 + 64) of 0..pos[t].  The split's K and V rows (contiguous in the
+// cache) come into shared memory with two bulk copies while the CTA loads and rotates q.  Every token
+// is in its own slot: the split holding position pos applies RoPE to k (engine/infer.js:436-458),
+// writes the K/V row to the cache (engine/infer.js:459-464) and patches it into its staged copy.
+// Each split leaves (max, sum, P.V) per head in `part`; the last split to finish (counter
+// ctr[t*NKV+g], reset by it) merges them in split order and writes the heads' outputs as fp16 hi/lo
+// into xh/xl.
+constexpr int kAttnChunk = 64;
+template <int REP>
+__global__ void __launch_bounds__(64) lwe_attn_split(const __grid_constant__ LweArgs a, int T, float* part, int* ctr) {
+  extern __shared__ __align__(128) float kvs[];  // K [64][64], V [64][64]
+  const int t = blockIdx.x, g = blockIdx.y, sp = blockIdx.z, S = gridDim.z;
+  const ModelDev& md = a.m;
+  const int NKV = md.NKV, pos = a.pos[t], npos = pos + 1;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int p0 = sp * kAttnChunk, p1 = min(npos, p0 + kAttnChunk), n = p1 - p0;
+  float* kb = kvs;
+  float* vb = kvs + kAttnChunk * 64;
+  __shared__ __align__(16) float qs[REP * 64];
+  __shared__ float ks[64];
+  __shared__ float sc[REP][kAttnChunk];
+  __shared__ __align__(16) float red[4][REP][64];
+  __shared__ float mx[REP], ls[REP];
+  __shared__ int last;
+  __shared__ __align__(8) uint64_t bar;
+  const size_t base = ((size_t)a.layer * NKV + g) * md.kv_len * 64;
+  float* kcw = a.kc[a.slot[t]] + base;
+  float* vcw = a.vc[a.slot[t]] + base;
+  float* mypart = part + (((size_t)t * NKV + g) * S + sp) * REP * 66;
+  if (n > 0) {
+    const bool owner = p1 == npos;
+    if (tid == 0) {
+      mbar_init(&bar, 1);
+      mbar_init_fence();
+    }
+    __syncthreads();
+    if (tid == 0) {
+      mbar_expect_tx(&bar, 2u * n * 256u);
+      bulk_g2s(kb, kcw + (size_t)p0 * 64, n * 256u, &bar);
+      bulk_g2s(vb, vcw + (size_t)p0 * 64, n * 256u, &bar);
+    }
+    const float* qrow = a.qkv + (size_t)t * md.QKV + g * REP * 64;
+    for (int i = tid; i < REP * 64; i += 64) qs[i] = qrow[i];
+    float vnew = 0.f;
+    if (owner) {
+      const float* krow = a.qkv + (size_t)t * md.QKV + md.D + g * 64;
+      ks[tid] = krow[tid];
+      vnew = krow[NKV * 64 + tid];
+      vcw[(size_t)pos * 64 + tid] = vnew;
+    }
+    __syncthreads();
+    if (md.arch == 0 && md.rope_dim > 0) {
+      const int half = md.rope_dim / 2;
+      const float* cs = md.rope_cos + (size_t)pos * md.rope_dim;
+      const float* sn = md.rope_sin + (size_t)pos * md.rope_dim;
+      for (int i = tid; i < (REP + 1) * half; i += 64) {
+        const int h = i / half - 1, d = i % half;
+        if (h < 0 && !owner) continue;
+        float* q = h < 0 ? ks : qs + h * 64;
+        const float a0 = q[d], a1 = q[d + half];
+        q[d] = fmaf(-a1, sn[d], a0 * cs[d]);
+        q[d + half] = fmaf(a0, sn[d + half], a1 * cs[d + half]);
+      }
+      __syncthreads();
+    }
+    if (owner) kcw[(size_t)pos * 64 + tid] = ks[tid];
+    if (!mbar_wait_bounded(&bar, 0, kWaitNs)) {
+      atomicCAS(a.err, 0, 1);
+      mbar_wait_bounded(&bar, 0, kWaitNs);  // the copies must land before the CTA may leave
+    }
+    if (owner) {  // the staged row at pos is the one written above
+      kb[(pos - p0) * 64 + tid] = ks[tid];
+      vb[(pos - p0) * 64 + tid] = vnew;
+    }
+    __syncthreads();
+    // scores (engine/infer.js:470-476): thread = position; float4 chunks visited in a rotated order
+    // so that the 8 threads of a shared-memory wavefront hit different banks
+    if (tid < n) {
+      const float4* kr = reinterpret_cast<const float4*>(kb + tid * 64);
+      float acc[REP];
+#pragma unroll
+      for (int h = 0; h < REP; ++h) acc[h] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int c = (j + tid) & 15;
+        const float4 k4 = kr[c];
+#pragma unroll
+        for (int h = 0; h < REP; ++h) {
+          const float4 q = reinterpret_cast<const float4*>(qs + h * 64)[c];
+          acc[h] = fmaf(q.x, k4.x, acc[h]);
+          acc[h] = fmaf(q.y, k4.y, acc[h]);
+          acc[h] = fmaf(q.z, k4.z, acc[h]);
+          acc[h] = fmaf(q.w, k4.w, acc[h]);
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < REP; ++h) sc[h][tid] = acc[h] * 0.125f;
+    }
+    __syncthreads();
+    // partial softmax per head
+    for (int h = warp; h < REP; h += 2) {
+      float m = -INFINITY;
+      for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[h][i]);
+      m = warp_max(m);
+      float sum = 0.f;
+      for (int i = lane; i < n; i += 32) {
+        const float e = expf(sc[h][i] - m);
+        sc[h][i] = e;
+        sum += e;
+      }
+      sum = warp_sum(sum);
+      if (lane == 0) {
+        mx[h] = m;
+        ls[h] = sum;
+      }
+    }
+    __syncthreads();
+    // P.V over the split: thread = (position lane pl of 4, float4 column dq)
+    {
+      const int pl = tid >> 4, dq = tid & 15;
+      float4 acc[REP];
+#pragma unroll
+      for (int h = 0; h < REP; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int i = pl; i < n; i += 4) {
+        const float4 v = reinterpret_cast<const float4*>(vb + i * 64)[dq];
+#pragma unroll
+        for (int h = 0; h < REP; ++h) {
+          const float e = sc[h][i];
+          acc[h].x = fmaf(e, v.x, acc[h].x);
+          acc[h].y = fmaf(e, v.y, acc[h].y);
+          acc[h].z = fmaf(e, v.z, acc[h].z);
+          acc[h].w = fmaf(e, v.w, acc[h].w);
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < REP; ++h) reinterpret_cast<float4*>(red[pl][h])[dq] = acc[h];
+    }
+    __syncthreads();
+    for (int hd = tid; hd < REP * 64; hd += 64) {
+      const int h = hd >> 6, d = hd & 63;
+      mypart[h * 66 + 2 + d] = (red[0][h][d] + red[1][h][d]) + (red[2][h][d] + red[3][h][d]);
+    }
+    if (tid < REP) {
+      mypart[tid * 66] = mx[tid];
+      mypart[tid * 66 + 1] = ls[tid];
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int c = t * NKV + g;
+    const int done = atomicAdd(&ctr[c], 1) + 1;
+    last = done == S;
+    if (last) ctr[c] = 0;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // merge (engine/infer.js:477-495 over the whole range), splits in order
+  const int nsp = (npos + kAttnChunk - 1) / kAttnChunk;
+  const float* tp = part + ((size_t)t * NKV + g) * S * REP * 66;
+  for (int hd = tid; hd < REP * 64; hd += 64) {
+    const int h = hd >> 6, d = hd & 63;
+    float M = -INFINITY;
+    for (int q = 0; q < nsp; ++q) M = fmaxf(M, __ldcg(tp + (q * REP + h) * 66));
+    float L = 0.f, O = 0.f;
+    for (int q = 0; q < nsp; ++q) {
+      const float* pq = tp + (q * REP + h) * 66;
+      const float f = expf(__ldcg(pq) - M);
+      L = fmaf(__ldcg(pq + 1), f, L);
+      O = fmaf(__ldcg(pq + 2 + d), f, O);
+    }
+    const size_t off = (size_t)t * a.ldx + (g * REP + h) * 64 + d;
+    split_hi_lo(O / L, a.xh[off], a.xl[off]);
+  }
+}
+
+// Positions per split of the decode attention and the split count for a cache of kv_len positions.
+void lwe_attn_split_shape(int kv_len, int* chunk, int* splits) {
+  *chunk = kAttnChunk;
+  *splits = (kv_len + kAttnChunk - 1) / kAttnChunk;
+}
+
+static size_t attention_smem(int rep, int kv_len) { return (size_t)(rep * 64 + rep * kv_len + 8 * rep * 64) * 4; }
+
+// GEMM with a residual epilogue: x[t][r] += W[r] . in_t (+ bias)  (proj and w2).  With gn != nullptr
+// (folded RMSNorm) the epilogue also writes (x * gn) as fp16 hi/lo into nh/nl (stride ldn) and this
+// row tile's sum of squares of the new x per token into a.ss[t][blockIdx.x].
+template <int TBW, int KS>
+__global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_resid(const __grid_constant__ LweArgs a, int T,
+                                                                           Q4 w, const float* bias, int K,
+                                                                           const float* gn, __half* nh, __half* nl,
+                                                                           int ldn) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const int R = a.m.D;
+  using C = LweTile<TBW, KS>;
+  __shared__ float ssw[4][C::BT];
+  const int R = a.m.D, r0 = blockIdx.x * kGemmRows, t0 = blockIdx.y * C::BT;
   float* x = a.x;
-  q4_gemm_tile<kLweTBW>(reinterpret_cast<const uint8_t*>(w.w), w.s, a.xh, a.xl, a.ldx, R, K, T,
-                        blockIdx.x * kGemmRows, blockIdx.y * kLweBT, smem, [&](int r, int t, float v) {
-                          x[(size_t)t * R + r] += bias ? v + bias[r] : v;
-                        });
+  const RowsLinear rows{reinterpret_cast<const uint8_t*>(w.w), w.s, R, r0, K >> 1, K >> 5};
+  float acc[TBW][4];
+  q4_gemm_core<TBW, C::NS, C::KS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  if (threadIdx.x < kGemmThreads) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tq = lane & 3;
+    const int ra = r0 + warp * 16 + gid, rb = ra + 8;
+    const bool va = ra < R, vb = rb < R;
+#pragma unroll
+    for (int b = 0; b < TBW; ++b) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int tl = b * 8 + 2 * tq + e, tok = t0 + tl;
+        float sq = 0.f;
+        if (tok < T) {
+          if (va) {
+            float* px = x + (size_t)tok * R + ra;
+            const float xn = *px + (bias ? acc[b][e] + bias[ra] : acc[b][e]);
+            *px = xn;
+            if (gn) {
+              split_hi_lo(xn * gn[ra], nh[(size_t)tok * ldn + ra], nl[(size_t)tok * ldn + ra]);
+              sq = xn * xn;
+            }
+          }
+          if (vb) {
+            float* px = x + (size_t)tok * R + rb;
+            const float xn = *px + (bias ? acc[b][2 + e] + bias[rb] : acc[b][2 + e]);
+            *px = xn;
+            if (gn) {
+              split_hi_lo(xn * gn[rb], nh[(size_t)tok * ldn + rb], nl[(size_t)tok * ldn + rb]);
+              sq = fmaf(xn, xn, sq);
+            }
+          }
+        }
+        if (gn) {
+          sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+          sq += __shfl_xor_sync(0xffffffffu, sq, 8);
+          sq += __shfl_xor_sync(0xffffffffu, sq, 16);
+          if (gid == 0) ssw[warp][tl] = sq;
+        }
+      }
+    }
+  }
+  if (gn) {
+    __syncthreads();
+    if (threadIdx.x < C::BT && t0 + (int)threadIdx.x < T) {
+      const int i = threadIdx.x;
+      a.ss[(size_t)(t0 + i) * kLweSsStride + blockIdx.x] = (ssw[0][i] + ssw[1][i]) + (ssw[2][i] + ssw[3][i]);
+    }
+  }
 }
 
 // w1/w3 paired GEMM with the SiLU*mul epilogue (engine/infer.js:178-183, 522-524); output written as
 // fp16 hi/lo into the second activation buffer (xh2/xl2).  32 matrix rows per CTA.
-__global__ void __launch_bounds__(kGemmThreads) lwe_gemm_w13(const __grid_constant__ LweArgs a, int T, int l) {
+template <int TBW, int KS>
+__global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_w13(const __grid_constant__ LweArgs a, int T,
+                                                                         int l) {
   extern __shared__ __align__(16) unsigned char smem[];
+  using C = LweTile<TBW, KS>;
+  __shared__ float sinv[C::BT];
   const LayerDev& L = a.m.layers[l];
   const int FF = a.m.FF, K = a.m.D;
+  {
+    const int tt = blockIdx.y * C::BT + threadIdx.x;
+    if (threadIdx.x < C::BT) sinv[threadIdx.x] = a.fold && tt < T ? fold_inv(a, tt) : 1.f;
+    __syncthreads();
+  }
   const RowsPaired rows{reinterpret_cast<const uint8_t*>(L.w1.w), L.w1.s, reinterpret_cast<const uint8_t*>(L.w3.w),
                         L.w3.s, FF, (int)blockIdx.x * 32, K >> 1, K >> 5};
-  float acc[kLweTBW][4];
-  const int t0 = blockIdx.y * kLweBT;
-  q4_gemm_core<kLweTBW>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  float acc[TBW][4];
+  const int t0 = blockIdx.y * C::BT;
+  q4_gemm_core<TBW, C::NS, C::KS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  if (threadIdx.x >= kGemmThreads) return;  // partial sums were added into the first warp group
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
   const int ia = warp * 16 + gid;  // A row (w1); the B row (w3) of the same matrix row is ia + 8
   if (!rows.valid(ia)) return;
   const int r = rows.mrow(ia);
 #pragma unroll
-  for (int b = 0; b < kLweTBW; ++b) {
+  for (int b = 0; b < TBW; ++b) {
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int tok = t0 + b * 8 + 2 * t + e;
       if (tok >= T) continue;
-      const float u = acc[b][e], v = acc[b][2 + e];
+      const float iv = sinv[b * 8 + 2 * t + e];
+      const float u = acc[b][e] * iv, v = acc[b][2 + e] * iv;
       const size_t off = (size_t)tok * a.ldx2 + r;
       split_hi_lo((u / (1.f + expf(-u))) * v, a.xh2[off], a.xl2[off]);
     }
@@ -282,13 +680,16 @@ __global__ void __launch_bounds__(kGemmThreads) lwe_gemm_w13(const __grid_consta
 }
 
 // GPT-2 fc GEMM with bias + GELU (engine/infer.js:512-515, 166-171) -> fp16 hi/lo (xh2/xl2)
-__global__ void __launch_bounds__(kGemmThreads) lwe_gemm_fc(const __grid_constant__ LweArgs a, int T, int l) {
+template <int TBW, int KS>
+__global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_fc(const __grid_constant__ LweArgs a, int T,
+                                                                        int l) {
   extern __shared__ __align__(16) unsigned char smem[];
+  using C = LweTile<TBW, KS>;
   const LayerDev& L = a.m.layers[l];
   const int FF = a.m.FF, K = a.m.D;
   const float* bias = L.fc_b;
-  q4_gemm_tile<kLweTBW>(reinterpret_cast<const uint8_t*>(L.w1.w), L.w1.s, a.xh, a.xl, a.ldx, FF, K, T,
-                        blockIdx.x * kGemmRows, blockIdx.y * kLweBT, smem, [&](int r, int t, float v) {
+  q4_gemm_tile<TBW, C::NS, C::KS>(reinterpret_cast<const uint8_t*>(L.w1.w), L.w1.s, a.xh, a.xl, a.ldx, FF, K, T,
+                           blockIdx.x * kGemmRows, blockIdx.y * C::BT, smem, [&](int r, int t, float v) {
                           if (bias) v += bias[r];
                           const float gl = 0.5f * v * (1.f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
                           split_hi_lo(gl, a.xh2[(size_t)t * a.ldx2 + r], a.xl2[(size_t)t * a.ldx2 + r]);
@@ -298,20 +699,23 @@ __global__ void __launch_bounds__(kGemmThreads) lwe_gemm_fc(const __grid_constan
 // lm_head GEMM over the T rows in xh/xl with a per-CTA argmax epilogue: for each token, the best
 // (value, lowest index) over the CTA's 64 vocab rows goes to pval/pidx[blockIdx.x][t].  Optional
 // logits store [t][V].
+template <int TBW>
 __global__ void __launch_bounds__(kGemmThreads) lwe_gemm_lm(const __grid_constant__ LweArgs a, int T, float* logits) {
   extern __shared__ __align__(16) unsigned char smem[];
+  using C = LweTile<TBW, 1>;
+  constexpr int kLweBT = C::BT;
   const int V = a.m.vocab, K = a.m.D;
   const int r0 = blockIdx.x * kGemmRows, t0 = blockIdx.y * kLweBT;
-  float acc[kLweTBW][4];
+  float acc[TBW][4];
   const RowsLinear rows{reinterpret_cast<const uint8_t*>(a.m.lm.w), a.m.lm.s, V, r0, K >> 1, K >> 5};
-  q4_gemm_core<kLweTBW>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  q4_gemm_core<TBW, C::NS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
   const int ra = r0 + warp * 16 + gid, rb = ra + 8;
   __syncthreads();  // the pipeline buffers are reused below
   float* bv = reinterpret_cast<float*>(smem);            // [4 warps][kLweBT]
   int* bi = reinterpret_cast<int*>(bv + 4 * kLweBT);     // [4 warps][kLweBT]
 #pragma unroll
-  for (int b = 0; b < kLweTBW; ++b) {
+  for (int b = 0; b < TBW; ++b) {
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int tl = b * 8 + 2 * t + e, tok = t0 + tl;
@@ -431,44 +835,175 @@ __global__ void lwe_first_token(const int32_t* amax, int32_t* out_ids, int32_t* 
 // ---------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------
-size_t lwe_gemm_smem() { return q4_gemm_smem_bytes<kLweTBW>(); }
+// Tokens per CTA: the largest tile that still gives two CTAs per SM, else the smallest.
+static int pick_tbw(int row_tiles, int T) {
+  constexpr int kTarget = 2 * 148;
+  if ((long)row_tiles * ((T + 63) / 64) >= kTarget) return 8;
+  if ((long)row_tiles * ((T + 31) / 32) >= kTarget) return 4;
+  return 2;
+}
 
-static inline dim3 gemm_grid(int rows_per_cta, int R, int T) {
-  return dim3((R + rows_per_cta - 1) / rows_per_cta, (T + kLweBT - 1) / kLweBT);
+// Tokens per CTA as above; then the in-CTA k split for GEMMs that still have few CTAs.
+static int pick_ks(int ctas) { return ctas >= 2 * 148 ? 1 : (ctas >= 148 ? 2 : 4); }
+
+#define LWE_LAUNCH_(KER, TB, KSV, TILES, T, ...)                                                      \
+  KER<TB, KSV><<<dim3(TILES, ((T) + 8 * TB - 1) / (8 * TB)), LweTile<TB, KSV>::THREADS, LweTile<TB, KSV>::smem(), \
+                 st>>>(__VA_ARGS__)
+#define LWE_GEMM(KER, ROWS_PER_CTA, R, T, ...)                                                        \
+  do {                                                                                                \
+    const int _tiles = ((R) + (ROWS_PER_CTA)-1) / (ROWS_PER_CTA);                                     \
+    const int _tbw = pick_tbw(_tiles, (T));                                                           \
+    const int _ks = pick_ks(_tiles * (((T) + 8 * _tbw - 1) / (8 * _tbw)));                            \
+    switch (_tbw * 8 + _ks) {                                                                         \
+      case 65: LWE_LAUNCH_(KER, 8, 1, _tiles, T, __VA_ARGS__); break;                                 \
+      case 66: LWE_LAUNCH_(KER, 8, 2, _tiles, T, __VA_ARGS__); break;                                 \
+      case 68: LWE_LAUNCH_(KER, 8, 4, _tiles, T, __VA_ARGS__); break;                                 \
+      case 33: LWE_LAUNCH_(KER, 4, 1, _tiles, T, __VA_ARGS__); break;                                 \
+      case 34: LWE_LAUNCH_(KER, 4, 2, _tiles, T, __VA_ARGS__); break;                                 \
+      case 36: LWE_LAUNCH_(KER, 4, 4, _tiles, T, __VA_ARGS__); break;                                 \
+      case 17: LWE_LAUNCH_(KER, 2, 1, _tiles, T, __VA_ARGS__); break;                                 \
+      case 18: LWE_LAUNCH_(KER, 2, 2, _tiles, T, __VA_ARGS__); break;                                 \
+      default: LWE_LAUNCH_(KER, 2, 4, _tiles, T, __VA_ARGS__); break;                                 \
+    }                                                                                                 \
+  } while (0)
+#define LWE_GEMM_LM(R, T, ...)                                                                        \
+  do {                                                                                                \
+    const int _tiles = ((R) + kGemmRows - 1) / kGemmRows;                                             \
+    switch (pick_tbw(_tiles, (T))) {                                                                  \
+      case 8: lwe_gemm_lm<8><<<dim3(_tiles, ((T) + 63) / 64), kGemmThreads, LweTile<8, 1>::smem(), st>>>(__VA_ARGS__); break; \
+      case 4: lwe_gemm_lm<4><<<dim3(_tiles, ((T) + 31) / 32), kGemmThreads, LweTile<4, 1>::smem(), st>>>(__VA_ARGS__); break; \
+      default: lwe_gemm_lm<2><<<dim3(_tiles, ((T) + 15) / 16), kGemmThreads, LweTile<2, 1>::smem(), st>>>(__VA_ARGS__); \
+    }                                                                                                 \
+  } while (0)
+
+template <class F>
+static cudaError_t smem_attr(F* f, size_t bytes) {
+  return bytes > 48 * 1024 ? cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes)
+                           : cudaSuccess;
+}
+template <int TBW, int KS>
+static cudaError_t gemm_attrs_ks() {
+  const size_t b = LweTile<TBW, KS>::smem();
+  cudaError_t e = smem_attr(lwe_gemm_qkv<TBW, KS>, b);
+  if (e == cudaSuccess) e = smem_attr(lwe_gemm_resid<TBW, KS>, b);
+  if (e == cudaSuccess) e = smem_attr(lwe_gemm_w13<TBW, KS>, b);
+  if (e == cudaSuccess) e = smem_attr(lwe_gemm_fc<TBW, KS>, b);
+  return e;
+}
+template <int TBW>
+static cudaError_t gemm_attrs() {
+  cudaError_t e = gemm_attrs_ks<TBW, 1>();
+  if (e == cudaSuccess) e = gemm_attrs_ks<TBW, 2>();
+  if (e == cudaSuccess) e = gemm_attrs_ks<TBW, 4>();
+  if (e == cudaSuccess) e = smem_attr(lwe_gemm_lm<TBW>, LweTile<TBW, 1>::smem());
+  return e;
+}
+
+static void launch_attention_split(const LweArgs& a, const LweHost& h, int T, cudaStream_t st) {
+  const int rep = a.m.NH / a.m.NKV;
+  int chunk, S;
+  lwe_attn_split_shape(a.m.kv_len, &chunk, &S);
+  const dim3 grid(T, a.m.NKV, S);
+  const size_t sm = (size_t)2 * kAttnChunk * 64 * 4;
+  switch (rep) {
+    case 1: lwe_attn_split<1><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
+    case 2: lwe_attn_split<2><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
+    case 3: lwe_attn_split<3><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
+    default: lwe_attn_split<4><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
+  }
+}
+
+template <bool F>
+static void launch_attention_t(const LweArgs& a, int T, cudaStream_t st) {
+  const int rep = a.m.NH / a.m.NKV;
+  const dim3 grid(T, a.m.NKV);
+  const size_t sm = attention_smem(rep, a.m.kv_len);
+  switch (rep) {
+    case 1: lwe_attention<1, F><<<grid, 128, sm, st>>>(a, T); break;
+    case 2: lwe_attention<2, F><<<grid, 128, sm, st>>>(a, T); break;
+    case 3: lwe_attention<3, F><<<grid, 128, sm, st>>>(a, T); break;
+    default: lwe_attention<4, F><<<grid, 128, sm, st>>>(a, T); break;
+  }
+}
+
+template <bool F>
+static cudaError_t attention_attr(int need) {
+  cudaError_t e = cudaFuncSetAttribute(lwe_attention<1, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, need);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(lwe_attention<2, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, need);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(lwe_attention<3, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, need);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(lwe_attention<4, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, need);
+  return e;
+}
+
+// One-time kernel attributes: the attention's shared memory grows with kv_len.
+cudaError_t lwe_setup(int kv_len) {
+  cudaError_t e = gemm_attrs<2>();
+  if (e == cudaSuccess) e = gemm_attrs<4>();
+  if (e == cudaSuccess) e = gemm_attrs<8>();
+  if (e != cudaSuccess) return e;
+  const int need = (int)attention_smem(kLweMaxRep, kv_len);
+  if (need <= 48 * 1024) return cudaSuccess;
+  e = attention_attr<false>(need);
+  return e == cudaSuccess ? attention_attr<true>(need) : e;
 }
 
 // A forward over T tokens whose ids/slots/positions are already in a.tok/a.slot/a.pos.  When
 // lm_T > 0 the lm_head runs on lm_T rows — the token rows a.lm_src[0..lm_T) when lm_from_src, else
 // rows 0..lm_T — and leaves the argmax per row in a.amax; logits (nullable) receives [lm_T][V].
 cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_from_src, float* logits,
-                        cudaStream_t st) {
+                        bool one_per_slot, cudaStream_t st) {
   const ModelDev& md = a.m;
-  const size_t sm = lwe_gemm_smem();
-  lwe_embed<<<T, 128, 0, st>>>(a, T);
-  for (int l = 0; l < md.n_layers; ++l) {
+  const int nl = md.n_layers;
+  // RMSNorm folded into the GEMMs (llama): the residual GEMMs write x * gain and sums of squares,
+  // the consumers apply 1/RMS.  LayerNorm (GPT-2) keeps separate norm kernels.
+  const bool fold = md.arch == 0 && h.fold_norm;
+  a.fold = fold ? 1 : 0;
+  lwe_embed<<<T, 128, 0, st>>>(a, T, h.layers[0].norm1);  // + norm1 of layer 0
+  for (int l = 0; l < nl; ++l) {
     const LayerDev& L = h.layers[l];
     a.layer = l;
-    lwe_norm_split<<<T, 128, 0, st>>>(a, T, L.norm1, nullptr);
-    lwe_gemm_qkv<<<gemm_grid(kGemmRows, md.QKV, T), kGemmThreads, sm, st>>>(a, T, l);
-    lwe_rope_kv<<<dim3(T, md.NKV), 64, 0, st>>>(a, T);
-    lwe_attention<<<dim3(T, md.NKV), 128, 0, st>>>(a, T);
-    lwe_gemm_resid<<<gemm_grid(kGemmRows, md.D, T), kGemmThreads, sm, st>>>(a, T, L.proj, L.proj_b, md.D);
-    lwe_norm_split<<<T, 128, 0, st>>>(a, T, L.norm2, nullptr);
+    LWE_GEMM(lwe_gemm_qkv, kGemmRows, md.QKV, T, a, T, l);
+    if (one_per_slot) {
+      if (h.attn_split)
+        launch_attention_split(a, h, T, st);
+      else
+        launch_attention_t<true>(a, T, st);
+    } else {
+      lwe_rope_kv<<<dim3(T, md.NKV), 64, 0, st>>>(a, T);
+      launch_attention_t<false>(a, T, st);
+    }
+    // proj + residual; norm2 -> N2 (x3 buffer when folded, else a norm kernel into xh)
+    LweArgs n2 = a;
+    if (fold) {
+      n2.xh = a.xh3;
+      n2.xl = a.xl3;
+      LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, T, a, T, L.proj, L.proj_b, md.D, L.norm2, a.xh3, a.xl3, a.ldx);
+    } else {
+      LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, T, a, T, L.proj, L.proj_b, md.D, nullptr, nullptr, nullptr, 0);
+      lwe_norm_split<<<T, 128, 0, st>>>(a, T, L.norm2, nullptr);
+    }
     if (md.arch == 0)
-      lwe_gemm_w13<<<gemm_grid(32, md.FF, T), kGemmThreads, sm, st>>>(a, T, l);
+      LWE_GEMM(lwe_gemm_w13, 32, md.FF, T, n2, T, l);
     else
-      lwe_gemm_fc<<<gemm_grid(kGemmRows, md.FF, T), kGemmThreads, sm, st>>>(a, T, l);
+      LWE_GEMM(lwe_gemm_fc, kGemmRows, md.FF, T, n2, T, l);
     LweArgs b = a;  // w2 / mlp.proj read the second activation buffer
     b.xh = a.xh2;
     b.xl = a.xl2;
     b.ldx = a.ldx2;
-    lwe_gemm_resid<<<gemm_grid(kGemmRows, md.D, T), kGemmThreads, sm, st>>>(b, T, L.w2, L.mproj_b, md.FF);
+    // w2 + residual; the next layer's norm1 -> xh
+    const float* ng = l + 1 < nl ? h.layers[l + 1].norm1 : nullptr;
+    if (fold) {
+      LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, T, b, T, L.w2, L.mproj_b, md.FF, ng, a.xh, a.xl, a.ldx);
+    } else {
+      LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, T, b, T, L.w2, L.mproj_b, md.FF, nullptr, nullptr, nullptr, 0);
+      if (ng) lwe_norm_split<<<T, 128, 0, st>>>(a, T, ng, nullptr);
+    }
   }
   if (lm_T > 0) {
     lwe_norm_split<<<lm_T, 128, 0, st>>>(a, lm_T, md.norm_f, lm_from_src ? a.lm_src : nullptr);
-    const dim3 g = gemm_grid(kGemmRows, md.vocab, lm_T);
-    lwe_gemm_lm<<<g, kGemmThreads, sm, st>>>(a, lm_T, logits);
-    lwe_argmax_reduce<<<(lm_T + 3) / 4, 128, 0, st>>>(a, lm_T, (int)g.x);
+    const int tiles = (md.vocab + kGemmRows - 1) / kGemmRows;
+    LWE_GEMM_LM(md.vocab, lm_T, a, lm_T, logits);
+    lwe_argmax_reduce<<<(lm_T + 3) / 4, 128, 0, st>>>(a, lm_T, tiles);
   }
   return cudaGetLastError();
 }

@@ -10,6 +10,7 @@
 namespace mllm {
 
 constexpr int kLweMaxRep = 4;  // query heads per kv head handled by one attention CTA
+constexpr int kLweSsStride = 16;  // per-token partial sums of squares: one per 64-row tile of dModel <= 1024
 
 struct LweArgs {
   ModelDev m;
@@ -21,6 +22,10 @@ struct LweArgs {
   __half* xh2;            // [tmax][ldx2] fp16 hi of the w2 / mlp.proj input
   __half* xl2;
   int ldx2;
+  __half* xh3;            // [tmax][ldx] fp16 hi of norm2 output when RMSNorm is folded into the GEMMs
+  __half* xl3;
+  float* ss;              // [tmax][kLweSsStride] partial sums of squares of x per 64-row tile
+  int fold;               // RMSNorm folded into the GEMMs for this forward
   float* qkv;             // [tmax][QKV]
   int32_t* tok;           // [tmax] token ids
   int32_t* slot;          // [tmax] sequence slots
@@ -38,11 +43,21 @@ struct LweArgs {
 // Host-side copies of the per-layer descriptors the launches pass by value.
 struct LweHost {
   std::vector<LayerDev> layers;
+  float* attn_part = nullptr;  // [tmax][NKV][splits][rep][66] decode-attention partials
+  int* attn_ctr = nullptr;     // [tmax * NKV] zeroed split counters
+  size_t attn_ctr_n = 0;
+  int attn_split = 0;  // decode attention split over positions (MLLM_LWE_ATTN_SPLIT=1)
+  int fold_norm = 1;   // llama RMSNorm folded into the GEMM epilogues (MLLM_LWE_FOLD_NORM=0: norm kernels)
 };
 
+// one_per_slot: every token belongs to a different slot (a batched decode step), which lets the
+// attention kernel apply RoPE and write the K/V row itself.
 cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_from_src, float* logits,
-                        cudaStream_t st);
-size_t lwe_gemm_smem();
+                        bool one_per_slot, cudaStream_t st);
+// Positions per split and split count of the decode-step attention for a cache of kv_len positions.
+void lwe_attn_split_shape(int kv_len, int* chunk, int* splits);
+// One-time function attributes (call once per device before the first forward).
+cudaError_t lwe_setup(int kv_len);
 // One prompt (or forward) chunk of a single slot: ids (device) at positions pos0.., lm rows either
 // every token (lm_each) or the last one.
 void lwe_fill(LweArgs a, const int32_t* ids, int n, int slot, int pos0, int lm_each, cudaStream_t st);

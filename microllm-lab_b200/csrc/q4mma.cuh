@@ -20,7 +20,7 @@ namespace mllm {
 constexpr int kGemmRows = 64;     // weight rows per CTA (4 warps x 16)
 constexpr int kGemmThreads = 128;
 constexpr int kXPad = 40;         // fp16 per staged token row: 32 + 8 pad (conflict-free B loads)
-constexpr int kStages = 3;
+constexpr int kStages = 3;         // default pipeline depth (32-wide k groups in flight)
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
   const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
@@ -108,18 +108,19 @@ struct RowsPaired {
   }
 };
 
-template <int TBW, class Rows>
+template <int TBW, int NS = kStages, int KS = 1, class Rows>
 __device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __restrict__ Xhi,
                                              const __half* __restrict__ Xlo, int ldx, int K, int T, int t0,
                                              unsigned char* smem, float (&acc)[TBW][4]);
 
 // Element-wise epilogue form: epi(tile_row, token, value) for every valid (row, token) of the tile.
-template <int TBW, class Rows, class Epi>
+template <int TBW, int NS = kStages, int KS = 1, class Rows, class Epi>
 __device__ __forceinline__ void q4_gemm_rows(const Rows& rows, const __half* __restrict__ Xhi,
                                              const __half* __restrict__ Xlo, int ldx, int K, int T, int t0,
                                              unsigned char* smem, Epi epi) {
   float acc[TBW][4];
-  q4_gemm_core<TBW>(rows, Xhi, Xlo, ldx, K, T, t0, smem, acc);
+  q4_gemm_core<TBW, NS, KS>(rows, Xhi, Xlo, ldx, K, T, t0, smem, acc);
+  if (KS > 1 && threadIdx.x >= kGemmThreads) return;  // the k-split partial sums are in group 0
   // lane (gid, t) owns tile rows gid, gid+8 of its warp and tokens 2t, 2t+1 of each 8-token block
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
   const int ia = warp * 16 + gid, ib = ia + 8;
@@ -134,38 +135,52 @@ __device__ __forceinline__ void q4_gemm_rows(const Rows& rows, const __half* __r
   }
 }
 
-template <int TBW, class Epi>
+template <int TBW, int NS = kStages, int KS = 1, class Epi>
 __device__ __forceinline__ void q4_gemm_tile(const uint8_t* __restrict__ W, const float* __restrict__ S,
                                              const __half* __restrict__ Xhi, const __half* __restrict__ Xlo, int ldx,
                                              int R, int K, int T, int r0, int t0, unsigned char* smem, Epi epi) {
   const RowsLinear rows{W, S, R, r0, K >> 1, K >> 5};
-  q4_gemm_rows<TBW>(rows, Xhi, Xlo, ldx, K, T, t0, smem, [&](int i, int t, float v) { epi(r0 + i, t, v); });
+  q4_gemm_rows<TBW, NS, KS>(rows, Xhi, Xlo, ldx, K, T, t0, smem, [&](int i, int t, float v) { epi(r0 + i, t, v); });
 }
 
 // Main loop: `rows` maps tile rows 0..63 to weight rows; acc[b][0..3] of lane (gid, t) hold tile rows
 // (16 warp + gid, same, +8, +8) x tokens (t0 + 8b + 2t, +1, 2t, +1).  Ends with all copies drained.
-template <int TBW, class Rows>
+// KS > 1 splits the k groups over KS groups of 4 warps (group w takes k groups w, w + KS, ...), each
+// with its own pipeline buffers and a named barrier; the partial sums are added, in group order, into
+// group 0's accumulators (threads 0..127), which then hold the result.
+template <int TBW, int NS, int KS, class Rows>
 __device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __restrict__ Xhi,
                                              const __half* __restrict__ Xlo, int ldx, int K, int T, int t0,
                                              unsigned char* smem, float (&acc)[TBW][4]) {
+  constexpr int kStages = NS;
   constexpr int BT = 8 * TBW;  // tokens per CTA
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr size_t kGroupBytes = (size_t)NS * kGemmRows * 16 + (size_t)NS * kGemmRows * 4 +
+                                 2 * (size_t)NS * BT * kXPad * sizeof(__half);
+  const int wg = KS > 1 ? (int)(threadIdx.x >> 7) : 0;
+  const int lt = KS > 1 ? (int)(threadIdx.x & 127) : (int)threadIdx.x;
+  const int lane = lt & 31, warp = lt >> 5;
   const int gid = lane >> 2, t = lane & 3;
   const int ng = K >> 5;
-  (void)ng;
-  // stage layout
-  uint8_t* w_s = smem;                                           // [kStages][64][16]
+  const int niter = (ng - wg + KS - 1) / KS;  // k groups of this warp group: wg, wg + KS, ...
+  // stage layout (per warp group)
+  uint8_t* w_s = smem + (size_t)wg * kGroupBytes;                        // [kStages][64][16]
   float* s_s = reinterpret_cast<float*>(w_s + kStages * kGemmRows * 16);  // [kStages][64]
   __half* xh_s = reinterpret_cast<__half*>(s_s + kStages * kGemmRows);    // [kStages][BT][kXPad]
   __half* xl_s = xh_s + kStages * BT * kXPad;
-  auto issue = [&](int g, int st) {
+  auto sync = [&]() {
+    if (KS == 1) __syncthreads();
+    else asm volatile("bar.sync %0, %1;" ::"r"(1 + wg), "r"(kGemmThreads) : "memory");
+  };
+  auto issue = [&](int i, int st) {
+    const int g = wg + i * KS;
     // weights: 64 rows x 16 B, scales: 64 floats (16 x 16 B), activations: BT rows x 64 B x 2
-    for (int i = threadIdx.x; i < kGemmRows; i += kGemmThreads)
-      cp_async16(w_s + (st * kGemmRows + i) * 16, rows.wrow(i) + g * 16, rows.valid(i));
-    if (threadIdx.x < kGemmRows)  // scales of a group are one float per row (stride ng)
-      cp_async4(s_s + st * kGemmRows + threadIdx.x, rows.srow(threadIdx.x) + g, rows.valid(threadIdx.x));
-    for (int i = threadIdx.x; i < BT * 4; i += kGemmThreads) {  // 4 x 16 B per token row (32 fp16)
-      const int tk = i >> 2, c = i & 3;
+    if (lt < kGemmRows) {
+      cp_async16(w_s + (st * kGemmRows + lt) * 16, rows.wrow(lt) + g * 16, rows.valid(lt));
+      // scales of a group are one float per row (stride ng)
+      cp_async4(s_s + st * kGemmRows + lt, rows.srow(lt) + g, rows.valid(lt));
+    }
+    for (int j = lt; j < BT * 4; j += kGemmThreads) {  // 4 x 16 B per token row (32 fp16)
+      const int tk = j >> 2, c = j & 3;
       const int tok = t0 + tk;
       const bool ok = tok < T;
       const size_t off = (size_t)min(tok, T - 1) * ldx + g * 32 + c * 8;
@@ -180,16 +195,16 @@ __device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __r
   // prologue
 #pragma unroll
   for (int s = 0; s < kStages - 1; ++s) {
-    if (s < ng) issue(s, s);
+    if (s < niter) issue(s, s);
     cp_async_commit();
   }
-  for (int g = 0; g < ng; ++g) {
+  for (int i = 0; i < niter; ++i) {
     cp_async_wait<kStages - 2>();
-    __syncthreads();
-    const int st = g % kStages;
+    sync();
+    const int st = i % kStages;
     {
-      const int gn = g + kStages - 1;
-      if (gn < ng) issue(gn, gn % kStages);
+      const int in = i + kStages - 1;
+      if (in < niter) issue(in, in % kStages);
       cp_async_commit();
     }
     const uint32_t* wr0 = reinterpret_cast<const uint32_t*>(w_s + (st * kGemmRows + warp * 16 + gid) * 16);
@@ -215,12 +230,30 @@ __device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __r
     }
   }
   cp_async_wait<0>();
+  if (KS > 1) {
+    __syncthreads();  // every group is done with its pipeline buffers
+    float* red = reinterpret_cast<float*>(smem);  // [KS-1][128][TBW*4]
+    if (wg > 0) {
+#pragma unroll
+      for (int b = 0; b < TBW; ++b)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) red[((size_t)(wg - 1) * kGemmThreads + lt) * TBW * 4 + b * 4 + i] = acc[b][i];
+    }
+    __syncthreads();
+    if (wg == 0) {
+      for (int w = 1; w < KS; ++w)
+#pragma unroll
+        for (int b = 0; b < TBW; ++b)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[b][i] += red[((size_t)(w - 1) * kGemmThreads + lt) * TBW * 4 + b * 4 + i];
+    }
+  }
 }
 
-template <int TBW>
+template <int TBW, int NS = kStages, int KS = 1>
 constexpr size_t q4_gemm_smem_bytes() {
-  return (size_t)kStages * kGemmRows * 16 + (size_t)kStages * kGemmRows * 4 +
-         2 * (size_t)kStages * (8 * TBW) * kXPad * sizeof(__half);
+  return (size_t)KS * ((size_t)NS * kGemmRows * 16 + (size_t)NS * kGemmRows * 4 +
+                       2 * (size_t)NS * (8 * TBW) * kXPad * sizeof(__half));
 }
 
 }  // namespace mllm
