@@ -44,6 +44,7 @@ typedef struct {
   int32_t prompt_len;   /* prompt length after truncation (engine/infer.js:604-608) */
   float ttft_ms;        /* device time from launch to the first generated id */
   float total_ms;       /* device time of the whole call */
+  int32_t kernel_launches; /* CUDA kernels the call launched */
 } mllm_stats;
 
 /*
@@ -118,6 +119,7 @@ typedef struct {
   int32_t prefill_forwards; /* token-batch forwards of the prefill */
   float prefill_ms;         /* device time of the prefill (all prompts, first ids) */
   float total_ms;           /* device time of the whole call */
+  int32_t kernel_launches;  /* CUDA kernels the call ran (graph nodes counted per replay) */
 } mllm_batch_stats;
 
 /*

@@ -99,7 +99,13 @@ struct mllm_engine {
   LweHost lh;
   Grow g_bids, g_plan, g_bout, g_state, g_blogits;
   int32_t* h_active = nullptr; // pinned
+  long coop_launches = 0;      // persistent-kernel launches issued by this handle
 };
+
+namespace {
+// Kernel launches issued so far for handle e on this thread (persistent kernels + token-batch kernels).
+long launches_now(const mllm_engine* e) { return e->coop_launches + lwe_launch_count(); }
+}  // namespace
 
 namespace {
 
@@ -262,6 +268,7 @@ int launch(mllm_engine* e, RunArgs& a, int max_forwards, bool multi, bool resume
   const size_t smem = multi ? e->smem_multi : e->smem_single;
   void* args[] = {&a};
   cudaError_t lst = cudaLaunchCooperativeKernel((void*)k, e->grid, kThreads, args, smem, e->stream);
+  ++e->coop_launches;
   if (lst != cudaSuccess) {
     cudaFuncAttributes fa{};
     cudaFuncGetAttributes(&fa, (const void*)k);
@@ -340,6 +347,7 @@ int lwe_run(mllm_engine* e, int slot, const int32_t* d_ids, int n, int pos0, int
 int generate_impl(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max_new, int32_t eos, int spec_k,
                   int ngram, int32_t* d_out, mllm_stats* st) {
   TRY(check_slot(e, slot));
+  const long l0 = launches_now(e);
   if (n <= 0 || max_new <= 0) return fail(e, MLLM_ERR_ARG, "empty prompt or max_new <= 0");
   if (n > e->md.kv_len - 1)
     return fail(e, MLLM_ERR_ARG, "prompt of %d ids does not fit the %d-position cache", n, e->md.kv_len);
@@ -403,6 +411,7 @@ int generate_impl(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max
     const uint64_t t0 = u64_at(hs, ST_T0), t1 = u64_at(hs, ST_TFIRST), t2 = u64_at(hs, ST_TEND);
     st->ttft_ms = t1 > t0 ? (float)((t1 - t0) * 1e-6) : 0.f;
     st->total_ms = t2 > t0 ? (float)((t2 - t0) * 1e-6) : 0.f;
+    st->kernel_launches = (int32_t)(launches_now(e) - l0);
   }
   return MLLM_OK;
 }
@@ -793,6 +802,8 @@ int mllm_generate_batch(mllm_engine* e, int n_seq, const int32_t* ids, const int
     first[q] = offsets[q] + (len - tl);
   }
   const int total_ids = offsets[n_seq];
+  const long l0 = launches_now(e);
+  long graph_kernels = 0;  // kernels per decode step (one graph launch each)
   for (int i = offsets[0]; i < total_ids; ++i)
     if (ids[i] < 0 || ids[i] >= md.vocab) return fail(e, MLLM_ERR_ARG, "token id %d out of range", ids[i]);
   // Plan: every prompt token (slot, position, source index); forward c takes tokens [c*tmax, ..).
@@ -881,7 +892,9 @@ int mllm_generate_batch(mllm_engine* e, int n_seq, const int32_t* ids, const int
     if (e->lwe_graph) {
       cudaGraph_t graph = nullptr;
       CUDA_TRY(e, cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+      const long c0 = launches_now(e);
       const cudaError_t r1 = step();
+      graph_kernels = launches_now(e) - c0;  // captured, not run
       const cudaError_t r2 = cudaStreamEndCapture(st, &graph);
       if (r1 != cudaSuccess || r2 != cudaSuccess) {
         if (graph) cudaGraphDestroy(graph);
@@ -946,6 +959,8 @@ int mllm_generate_batch(mllm_engine* e, int n_seq, const int32_t* ids, const int
     const uint64_t t0 = u64_at(hs, ST_T0), t1 = u64_at(hs, ST_TFIRST), t2 = u64_at(hs, ST_TEND);
     stats->prefill_ms = t1 > t0 ? (float)((t1 - t0) * 1e-6) : 0.f;
     stats->total_ms = t2 > t0 ? (float)((t2 - t0) * 1e-6) : 0.f;
+    // a graph launch runs graph_kernels kernels; the capture itself ran none
+    stats->kernel_launches = (int32_t)(launches_now(e) - l0 - graph_kernels + graph_kernels * (long)steps);
   }
   return MLLM_OK;
 }

@@ -20,6 +20,10 @@
 
 namespace mllm {
 
+// Kernel launches issued by this thread (read by the runtime to report launches per call).
+thread_local long g_lwe_launches = 0;
+long lwe_launch_count() { return g_lwe_launches; }
+
 // GEMM tiles: 64 weight rows x 8*TBW tokens per CTA; TBW is picked per launch so that small-R GEMMs
 // still fill the GPU, and the k-pipeline is deeper for the smaller token tiles (all under 48 KB).
 // The k groups may also be split over KS groups of 4 warps inside the CTA (more warps in flight per
@@ -848,7 +852,8 @@ static int pick_ks(int ctas) { return ctas >= 2 * 148 ? 1 : (ctas >= 148 ? 2 : 4
 
 #define LWE_LAUNCH_(KER, TB, KSV, TILES, T, ...)                                                      \
   KER<TB, KSV><<<dim3(TILES, ((T) + 8 * TB - 1) / (8 * TB)), LweTile<TB, KSV>::THREADS, LweTile<TB, KSV>::smem(), \
-                 st>>>(__VA_ARGS__)
+                 st>>>(__VA_ARGS__);                                                                  \
+  ++g_lwe_launches
 #define LWE_GEMM(KER, ROWS_PER_CTA, R, T, ...)                                                        \
   do {                                                                                                \
     const int _tiles = ((R) + (ROWS_PER_CTA)-1) / (ROWS_PER_CTA);                                     \
@@ -874,6 +879,7 @@ static int pick_ks(int ctas) { return ctas >= 2 * 148 ? 1 : (ctas >= 148 ? 2 : 4
       case 4: lwe_gemm_lm<4><<<dim3(_tiles, ((T) + 31) / 32), kGemmThreads, LweTile<4, 1>::smem(), st>>>(__VA_ARGS__); break; \
       default: lwe_gemm_lm<2><<<dim3(_tiles, ((T) + 15) / 16), kGemmThreads, LweTile<2, 1>::smem(), st>>>(__VA_ARGS__); \
     }                                                                                                 \
+    ++g_lwe_launches;                                                                                 \
   } while (0)
 
 template <class F>
@@ -906,10 +912,10 @@ static void launch_attention_split(const LweArgs& a, const LweHost& h, int T, cu
   const dim3 grid(T, a.m.NKV, S);
   const size_t sm = (size_t)2 * kAttnChunk * 64 * 4;
   switch (rep) {
-    case 1: lwe_attn_split<1><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
-    case 2: lwe_attn_split<2><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
-    case 3: lwe_attn_split<3><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
-    default: lwe_attn_split<4><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
+    case 1: lwe_attn_split<1><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); ++g_lwe_launches; break;
+    case 2: lwe_attn_split<2><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); ++g_lwe_launches; break;
+    case 3: lwe_attn_split<3><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); ++g_lwe_launches; break;
+    default: lwe_attn_split<4><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); ++g_lwe_launches; break;
   }
 }
 
@@ -919,10 +925,10 @@ static void launch_attention_t(const LweArgs& a, int T, cudaStream_t st) {
   const dim3 grid(T, a.m.NKV);
   const size_t sm = attention_smem(rep, a.m.kv_len);
   switch (rep) {
-    case 1: lwe_attention<1, F><<<grid, 128, sm, st>>>(a, T); break;
-    case 2: lwe_attention<2, F><<<grid, 128, sm, st>>>(a, T); break;
-    case 3: lwe_attention<3, F><<<grid, 128, sm, st>>>(a, T); break;
-    default: lwe_attention<4, F><<<grid, 128, sm, st>>>(a, T); break;
+    case 1: lwe_attention<1, F><<<grid, 128, sm, st>>>(a, T); ++g_lwe_launches; break;
+    case 2: lwe_attention<2, F><<<grid, 128, sm, st>>>(a, T); ++g_lwe_launches; break;
+    case 3: lwe_attention<3, F><<<grid, 128, sm, st>>>(a, T); ++g_lwe_launches; break;
+    default: lwe_attention<4, F><<<grid, 128, sm, st>>>(a, T); ++g_lwe_launches; break;
   }
 }
 
@@ -959,6 +965,7 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
   const bool fold = md.arch == 0 && h.fold_norm;
   a.fold = fold ? 1 : 0;
   lwe_embed<<<T, 128, 0, st>>>(a, T, h.layers[0].norm1);  // + norm1 of layer 0
+  ++g_lwe_launches;
   for (int l = 0; l < nl; ++l) {
     const LayerDev& L = h.layers[l];
     a.layer = l;
@@ -970,6 +977,7 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
         launch_attention_t<true>(a, T, st);
     } else {
       lwe_rope_kv<<<dim3(T, md.NKV), 64, 0, st>>>(a, T);
+      ++g_lwe_launches;
       launch_attention_t<false>(a, T, st);
     }
     // proj + residual; norm2 -> N2 (x3 buffer when folded, else a norm kernel into xh)
@@ -981,6 +989,7 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
     } else {
       LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, T, a, T, L.proj, L.proj_b, md.D, nullptr, nullptr, nullptr, 0);
       lwe_norm_split<<<T, 128, 0, st>>>(a, T, L.norm2, nullptr);
+      ++g_lwe_launches;
     }
     if (md.arch == 0)
       LWE_GEMM(lwe_gemm_w13, 32, md.FF, T, n2, T, l);
@@ -996,14 +1005,19 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
       LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, T, b, T, L.w2, L.mproj_b, md.FF, ng, a.xh, a.xl, a.ldx);
     } else {
       LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, T, b, T, L.w2, L.mproj_b, md.FF, nullptr, nullptr, nullptr, 0);
-      if (ng) lwe_norm_split<<<T, 128, 0, st>>>(a, T, ng, nullptr);
+      if (ng) {
+        lwe_norm_split<<<T, 128, 0, st>>>(a, T, ng, nullptr);
+        ++g_lwe_launches;
+      }
     }
   }
   if (lm_T > 0) {
     lwe_norm_split<<<lm_T, 128, 0, st>>>(a, lm_T, md.norm_f, lm_from_src ? a.lm_src : nullptr);
+    ++g_lwe_launches;
     const int tiles = (md.vocab + kGemmRows - 1) / kGemmRows;
     LWE_GEMM_LM(md.vocab, lm_T, a, lm_T, logits);
     lwe_argmax_reduce<<<(lm_T + 3) / 4, 128, 0, st>>>(a, lm_T, tiles);
+    ++g_lwe_launches;
   }
   return cudaGetLastError();
 }
@@ -1020,9 +1034,11 @@ __global__ void k_fill(const __grid_constant__ LweArgs a, const int32_t* ids, in
 }
 void lwe_fill(LweArgs a, const int32_t* ids, int n, int slot, int pos0, int lm_each, cudaStream_t st) {
   k_fill<<<(n + 255) / 256, 256, 0, st>>>(a, ids, n, slot, pos0, lm_each);
+  ++g_lwe_launches;
 }
 void lwe_first(LweArgs a, int32_t* out_ids, int32_t* status, int eos, int forwards, cudaStream_t st) {
   lwe_first_token<<<1, 1, 0, st>>>(a.amax, out_ids, status, eos, forwards);
+  ++g_lwe_launches;
 }
 void lwe_mark_time(int32_t* status, int idx, cudaStream_t st) { lwe_mark<<<1, 1, 0, st>>>(status, idx); }
 
@@ -1034,6 +1050,7 @@ __global__ void k_gather(int32_t* tok, const int32_t* ids, const int32_t* src, i
 }
 void lwe_gather(int32_t* tok, const int32_t* ids, const int32_t* src, int n, cudaStream_t st) {
   k_gather<<<(n + 255) / 256, 256, 0, st>>>(tok, ids, src, n);
+  ++g_lwe_launches;
 }
 // First id of each sequence whose prompt ended in this forward: lm row j belongs to slot lm_slot[j]
 // (engine/infer.js:611-623 per sequence); counts[s] = 1 while running, -1 once stopped.
@@ -1049,6 +1066,7 @@ __global__ void k_batch_first(const int32_t* amax, const int32_t* lm_slot, int n
 void lwe_batch_first(const int32_t* amax, const int32_t* lm_slot, int nlm, int max_new, int eos, int kv_len,
                      int32_t* out_ids, int32_t* counts, const int32_t* lens, cudaStream_t st) {
   k_batch_first<<<(nlm + 127) / 128, 128, 0, st>>>(amax, lm_slot, nlm, max_new, eos, kv_len, out_ids, counts, lens);
+  ++g_lwe_launches;
 }
 // Decode rows: token t = slot t, its last id and position (engine/infer.js:627: the id fed at
 // position prompt_len + generated - 1).
@@ -1065,10 +1083,12 @@ __global__ void k_batch_decode_setup(const __grid_constant__ LweArgs a, int n, c
 void lwe_batch_decode_setup(LweArgs a, int n, const int32_t* out_ids, const int32_t* counts, const int32_t* lens,
                             int max_new, cudaStream_t st) {
   k_batch_decode_setup<<<(n + 127) / 128, 128, 0, st>>>(a, n, out_ids, counts, lens, max_new);
+  ++g_lwe_launches;
 }
 void lwe_batch_advance(LweArgs a, int n, int max_new, int eos, int32_t* out_ids, int32_t* counts, const int32_t* lens,
                        cudaStream_t st) {
   lwe_decode_advance<<<(n + 127) / 128, 128, 0, st>>>(a, n, max_new, eos, out_ids, counts, lens);
+  ++g_lwe_launches;
 }
 
 // Number of sequences still running -> *active.
@@ -1084,6 +1104,7 @@ __global__ void k_count_active(const int32_t* counts, int n, int32_t* active) {
 }
 void lwe_count_active(const int32_t* counts, int n, int32_t* active, cudaStream_t st) {
   k_count_active<<<1, 256, 0, st>>>(counts, n, active);
+  ++g_lwe_launches;
 }
 
 // GPT-2 penalised argmax per decode row (engine/infer.js:252-287) over logits [T][V]; the history of
@@ -1202,6 +1223,7 @@ size_t lwe_argmax_pen_smem(int V, int max_new) { return (size_t)2 * ((V + 31) / 
 void lwe_penalised_argmax(const float* logits, int V, int T, const int32_t* out_ids, const int32_t* counts, int max_new,
                           int32_t* amax, cudaStream_t st) {
   lwe_argmax_pen<<<T, 256, lwe_argmax_pen_smem(V, max_new), st>>>(logits, V, T, out_ids, counts, max_new, amax);
+  ++g_lwe_launches;
 }
 
 }  // namespace mllm

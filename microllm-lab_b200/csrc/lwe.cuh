@@ -63,6 +63,8 @@ cudaError_t lwe_setup(int kv_len);
 void lwe_fill(LweArgs a, const int32_t* ids, int n, int slot, int pos0, int lm_each, cudaStream_t st);
 void lwe_first(LweArgs a, int32_t* out_ids, int32_t* status, int eos, int forwards, cudaStream_t st);
 void lwe_mark_time(int32_t* status, int idx, cudaStream_t st);
+// Kernel launches issued so far by the calling thread through these functions.
+long lwe_launch_count();
 // Replicated multi-sequence decode
 void lwe_gather(int32_t* tok, const int32_t* ids, const int32_t* src, int n, cudaStream_t st);
 void lwe_batch_first(const int32_t* amax, const int32_t* lm_slot, int nlm, int max_new, int eos, int kv_len,

@@ -42,12 +42,13 @@ class MllmError(RuntimeError):
 class Stats(ctypes.Structure):
     _fields_ = [("n_generated", ctypes.c_int32), ("stop_reason", ctypes.c_int32), ("spec_hits", ctypes.c_int32),
                 ("spec_tries", ctypes.c_int32), ("forwards", ctypes.c_int32), ("prompt_len", ctypes.c_int32),
-                ("ttft_ms", ctypes.c_float), ("total_ms", ctypes.c_float)]
+                ("ttft_ms", ctypes.c_float), ("total_ms", ctypes.c_float), ("kernel_launches", ctypes.c_int32)]
 
 
 class BatchStats(ctypes.Structure):
     _fields_ = [("n_seq", ctypes.c_int32), ("total_generated", ctypes.c_int32), ("steps", ctypes.c_int32),
-                ("prefill_forwards", ctypes.c_int32), ("prefill_ms", ctypes.c_float), ("total_ms", ctypes.c_float)]
+                ("prefill_forwards", ctypes.c_int32), ("prefill_ms", ctypes.c_float), ("total_ms", ctypes.c_float),
+                ("kernel_launches", ctypes.c_int32)]
 
 
 _LIB = None
@@ -220,6 +221,7 @@ class CudaPetitGPT:
             "specHits": int(st.spec_hits),
             "specTries": int(st.spec_tries),
             "forwards": int(st.forwards),
+            "kernelLaunches": int(st.kernel_launches),
         }
         if onToken:
             for i, t in enumerate(gen):
@@ -249,7 +251,7 @@ class CudaPetitGPT:
                for i in range(n)]
         stats = {"nSeq": int(st.n_seq), "totalGenerated": int(st.total_generated), "steps": int(st.steps),
                  "prefillForwards": int(st.prefill_forwards), "prefillMs": float(st.prefill_ms),
-                 "deviceMs": float(st.total_ms), "totalMs": wall}
+                 "deviceMs": float(st.total_ms), "totalMs": wall, "kernelLaunches": int(st.kernel_launches)}
         return res, stats
 
     def selftest_timeout(self, wait_ms: int = 50) -> int:
