@@ -59,7 +59,8 @@ __device__ __forceinline__ void stamp(const RunArgs& a, uint32_t tag, int idx) {
 
 // Wait for the n contiguous words src[0..n) (tag == tag) and store their values to dst[0..n).
 // Every thread of the CTA calls it; returns false (everywhere) when the wait gave up.
-__device__ __noinline__ bool poll_vec(const uint64_t* src, float* dst, int n, uint32_t tag, int* err, uint64_t limit) {
+__device__ __noinline__ bool poll_vec(const uint64_t* src, float* dst, int n, uint32_t tag, int* err, uint64_t limit,
+                                      int sleep_ns = 0) {
   bool ok = true;
   const uint64_t t0 = globaltimer();
   for (int base = threadIdx.x; base < n && ok; base += 8 * kThreads) {
@@ -79,6 +80,7 @@ __device__ __noinline__ bool poll_vec(const uint64_t* src, float* dst, int n, ui
           dst[base + k * kThreads] = __uint_as_float((uint32_t)v[k]);
           pending &= ~(1u << k);
         }
+      if (pending && sleep_ns) __nanosleep(sleep_ns);
       if (pending && ((++rounds & 31) == 0)) {
         if (*(volatile int*)err || globaltimer() - t0 > limit) {
           atomicCAS(err, 0, 1);
@@ -89,6 +91,57 @@ __device__ __noinline__ bool poll_vec(const uint64_t* src, float* dst, int n, ui
     }
   }
   return __syncthreads_and(ok);
+}
+
+// Wait for the residual row src[0..D) (D <= 4 * kThreads) and store it to xs; for RMSNorm also
+// store x * gain to act and leave each warp's sum of squares in red[warp], so that 1 / RMS is
+// available to every warp after the call without another pass (engine/infer.js:134-143 with the
+// 1 / RMS factor applied to the dot products).  Returns false (everywhere) when the wait gave up.
+__device__ __noinline__ bool poll_x_rms(const uint64_t* src, float* xs, float* act, float* red, int D, float g0, float g1,
+                                        float g2, float g3, uint32_t tag, int* err, uint64_t limit, int sleep_ns) {
+  const float g[4] = {g0, g1, g2, g3};
+  uint32_t pending = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if ((int)threadIdx.x + kThreads * j < D) pending |= 1u << j;
+  bool ok = true;
+  float s2 = 0.f;
+  const uint64_t t0 = globaltimer();
+  int rounds = 0;
+  while (pending) {
+    uint64_t v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (pending & (1u << j)) v[j] = ll_load(src + threadIdx.x + kThreads * j);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if ((pending & (1u << j)) && (uint32_t)(v[j] >> 32) == tag) {
+        const float x = __uint_as_float((uint32_t)v[j]);
+        const int k = threadIdx.x + kThreads * j;
+        xs[k] = x;
+        act[k] = x * g[j];
+        s2 = fmaf(x, x, s2);
+        pending &= ~(1u << j);
+      }
+    if (pending && sleep_ns) __nanosleep(sleep_ns);
+    if (pending && ((++rounds & 31) == 0)) {
+      if (*(volatile int*)err || globaltimer() - t0 > limit) {
+        atomicCAS(err, 0, 1);
+        ok = false;
+        break;
+      }
+    }
+  }
+  s2 = warp_sum(s2);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s2;
+  return __syncthreads_and(ok);
+}
+
+__device__ __forceinline__ float rms_inv(const float* red, int D) {
+  float s = 0.f;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) s += red[w];
+  return 1.f / sqrtf(s / D + 1e-6f);
 }
 
 // RMSNorm (engine/infer.js:134-143, eps 1e-6) or LayerNorm (engine/infer.js:147-164, eps 1e-5) of
@@ -154,12 +207,36 @@ struct Row {
       s[j] = k < nwords ? ldv_f32(sr + (k >> 2)) : 0.f;
     }
   }
-  __device__ __forceinline__ float dot(const float* x, int nwords, int lane) const {
+  __device__ __forceinline__ float partial(const float* x, int nwords, int lane) const {
     float acc = 0.f;
 #pragma unroll
     for (int j = 0; j < NWJ; ++j) {
       const int k = lane + 32 * j;
       if (k < nwords) acc = fmaf(word_dot(w[j], x + 8 * k), s[j], acc);
+    }
+    return acc;
+  }
+  __device__ __forceinline__ float dot(const float* x, int nwords, int lane) const {
+    return warp_sum(partial(x, nwords, lane));
+  }
+  // Same with this lane's activations already in registers (xr[j] = x[8k..8k+7], k = lane + 32 j).
+  __device__ __forceinline__ float dot_reg(const float (&xr)[NWJ][8], int nwords, int lane) const {
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < NWJ; ++j) {
+      const int k = lane + 32 * j;
+      if (k < nwords) {
+        const uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = (w[j] >> 4) & 0x0F0F0F0Fu;
+        float t = nib_at(lo, 0) * xr[j][0];
+        t = fmaf(nib_at(hi, 0), xr[j][1], t);
+        t = fmaf(nib_at(lo, 1), xr[j][2], t);
+        t = fmaf(nib_at(hi, 1), xr[j][3], t);
+        t = fmaf(nib_at(lo, 2), xr[j][4], t);
+        t = fmaf(nib_at(hi, 2), xr[j][5], t);
+        t = fmaf(nib_at(lo, 3), xr[j][6], t);
+        t = fmaf(nib_at(hi, 3), xr[j][7], t);
+        acc = fmaf(t, s[j], acc);
+      }
     }
     return warp_sum(acc);
   }
@@ -173,6 +250,8 @@ __device__ __forceinline__ void load_gains(const float* g, int D, bool ln, float
     bv[j] = (ln && k < D) ? ldv_f32(g + D + k) : 0.f;
   }
 }
+
+constexpr int kProfLayerA = 15;
 
 // Causal attention of head h for the token at `pos` (engine/infer.js:422-495): RoPE on q and on
 // the new k, cache write by the group's first head, then online softmax over positions 0..pos with
@@ -224,6 +303,7 @@ __device__ __noinline__ bool attention(const RunArgs& a, const Lay& S, int l, in
     }
     if (!__syncthreads_and(ok)) return false;
   }
+  if (l == kProfLayerA) stamp(a, tag, 206);
   if (rope && threadIdx.x < 2 * half) {
     float* v = threadIdx.x < half ? q : kl;
     const int d = threadIdx.x % half;
@@ -243,45 +323,60 @@ __device__ __noinline__ bool attention(const RunArgs& a, const Lay& S, int l, in
   float mrun = -INFINITY, lrun = 0.f, o[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) o[i] = 0.f;
-  for (int base = warp * 8; base < npos; base += kWarps * 8) {
-    const int p = base + pg;
-    const bool valid = p < npos;
-    float4 kk[4];
-    const float* kr = p < pos ? a.kc + (kv_base + p) * 64 + qd * 16 : kl + qd * 16;
-    const float* vr = p < pos ? a.vc + (kv_base + p) * 64 + qd * 16 : vl + qd * 16;
-    if (valid && p < pos) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) kk[j] = ldcg_f4(kr + 4 * j);
-    } else if (valid) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) kk[j] = *reinterpret_cast<const float4*>(kr + 4 * j);
-    }
-    float part = 0.f;
-    if (valid) {
+  // Each round covers two 8-position slots per warp (positions r0 + pg and r0 + 64 + pg); the K and
+  // V rows of both are requested together, then one online-softmax update.  The new position's k/v
+  // come from shared memory.
+  auto fetch = [&](int p, float4 (&kk)[4], float4 (&vv)[4]) {
+    if (p < pos) {
+      const float* kr = a.kc + (kv_base + p) * 64 + qd * 16;
+      const float* vr = a.vc + (kv_base + p) * 64 + qd * 16;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float4 qq = *reinterpret_cast<const float4*>(q + qd * 16 + 4 * j);
-        part = fmaf(qq.x, kk[j].x, part);
-        part = fmaf(qq.y, kk[j].y, part);
-        part = fmaf(qq.z, kk[j].z, part);
-        part = fmaf(qq.w, kk[j].w, part);
+        kk[j] = ldcg_f4(kr + 4 * j);
+        vv[j] = ldcg_f4(vr + 4 * j);
       }
+    } else if (p == pos) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        kk[j] = *reinterpret_cast<const float4*>(kl + qd * 16 + 4 * j);
+        vv[j] = *reinterpret_cast<const float4*>(vl + qd * 16 + 4 * j);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kk[j] = vv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto score = [&](const float4 (&kk)[4], bool valid) {
+    float part = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 qq = *reinterpret_cast<const float4*>(q + qd * 16 + 4 * j);
+      part = fmaf(qq.x, kk[j].x, part);
+      part = fmaf(qq.y, kk[j].y, part);
+      part = fmaf(qq.z, kk[j].z, part);
+      part = fmaf(qq.w, kk[j].w, part);
     }
     part += __shfl_xor_sync(0xffffffffu, part, 1);
     part += __shfl_xor_sync(0xffffffffu, part, 2);
-    const float sc = valid ? part * 0.125f : -INFINITY;  // 1/sqrt(64), exact (engine/infer.js:466)
-    const float newm = fmaxf(mrun, warp_max(sc));
-    const float e = valid ? expf(sc - newm) : 0.f;
+    return valid ? part * 0.125f : -INFINITY;  // 1/sqrt(64), exact (engine/infer.js:466)
+  };
+  for (int r0 = warp * 8; r0 < npos; r0 += 2 * kWarps * 8) {
+    const int pA = r0 + pg, pB = r0 + kWarps * 8 + pg;
+    float4 kA[4], vA[4], kB[4], vB[4];
+    fetch(pA, kA, vA);
+    fetch(pB, kB, vB);
+    const float sA = score(kA, pA < npos), sB = score(kB, pB < npos);
+    const float newm = fmaxf(mrun, warp_max(fmaxf(sA, sB)));
+    const float eA = pA < npos ? expf(sA - newm) : 0.f;
+    const float eB = pB < npos ? expf(sB - newm) : 0.f;
     const float corr = mrun == -INFINITY ? 0.f : expf(mrun - newm);
-    lrun = fmaf(lrun, corr, warp_sum(qd == 0 ? e : 0.f));
+    lrun = fmaf(lrun, corr, warp_sum(qd == 0 ? eA + eB : 0.f));
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float4 vv = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (valid) vv = p < pos ? ldcg_f4(vr + 4 * j) : *reinterpret_cast<const float4*>(vr + 4 * j);
-      o[4 * j] = fmaf(e, vv.x, o[4 * j] * corr);
-      o[4 * j + 1] = fmaf(e, vv.y, o[4 * j + 1] * corr);
-      o[4 * j + 2] = fmaf(e, vv.z, o[4 * j + 2] * corr);
-      o[4 * j + 3] = fmaf(e, vv.w, o[4 * j + 3] * corr);
+      o[4 * j] = fmaf(eB, vB[j].x, fmaf(eA, vA[j].x, o[4 * j] * corr));
+      o[4 * j + 1] = fmaf(eB, vB[j].y, fmaf(eA, vA[j].y, o[4 * j + 1] * corr));
+      o[4 * j + 2] = fmaf(eB, vB[j].z, fmaf(eA, vA[j].z, o[4 * j + 2] * corr));
+      o[4 * j + 3] = fmaf(eB, vB[j].w, fmaf(eA, vA[j].w, o[4 * j + 3] * corr));
     }
     mrun = newm;
   }
@@ -291,6 +386,7 @@ __device__ __noinline__ bool attention(const RunArgs& a, const Lay& S, int l, in
     o[i] += __shfl_xor_sync(0xffffffffu, o[i], 8);
     o[i] += __shfl_xor_sync(0xffffffffu, o[i], 16);
   }
+  if (l == kProfLayerA) stamp(a, tag, 207);
   float* wp = S.wpart + warp * 68;
   if (lane == 0) {
     wp[0] = mrun;
@@ -343,9 +439,10 @@ __device__ __noinline__ int lm_head(const RunArgs& a, const Lay& S, uint32_t tag
   {
     float gv[4], bv[4];
     load_gains(md.norm_f, D, md.arch == 1, gv, bv);
-    if (!poll_vec(x.x2 + (size_t)(md.n_layers - 1) * a.mmax * x.s_d, S.xs, D, tag, a.err, limit)) return -1;
+    if (!poll_vec(x.x2 + (size_t)(md.n_layers - 1) * a.mmax * x.s_d, S.xs, D, tag, a.err, limit, a.poll_sleep_ns)) return -1;
     norm_row(S.xs, S.act, S.red, D, md.arch == 1, gv[0], gv[1], gv[2], gv[3], bv[0], bv[1], bv[2], bv[3]);
   }
+  stamp(a, tag, 210);
   int nban = 0, nrec = 0;
   if (pen) {
     if (threadIdx.x == 0) S.misc[0] = 0;
@@ -364,12 +461,20 @@ __device__ __noinline__ int lm_head(const RunArgs& a, const Lay& S, uint32_t tag
   }
   double best = -INFINITY;
   int bidx = 0x7fffffff;
+  // this lane's activations stay in registers for all of its rows (no shared-memory traffic per row)
+  float xr[NWJ][8];
+#pragma unroll
+  for (int j = 0; j < NWJ; ++j) {
+    const int k = lane + 32 * j;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) xr[j][e] = k < nwords ? S.act[8 * k + e] : 0.f;
+  }
   for (int r0 = gw; r0 < md.vocab; r0 += kG * NW) {
 #pragma unroll
     for (int g = 0; g < kG; ++g) {
       const int r = r0 + g * NW;
       if (r >= md.vocab) break;
-      const float v = rw[g].dot(S.act, nwords, lane);
+      const float v = rw[g].dot_reg(xr, nwords, lane);
       const int rn = r + kG * NW;  // next group's row for this slot
       if (rn < md.vocab) rw[g].load(md.lm, rn, nwords, lane);
       if (logits && lane == 0) logits[r] = v;
@@ -426,6 +531,7 @@ __device__ __noinline__ int lm_head(const RunArgs& a, const Lay& S, uint32_t tag
           dst[i] = (uint32_t)v;
           break;
         }
+        if (a.poll_sleep_ns) __nanosleep(a.poll_sleep_ns);
         if (((++rounds & 31) == 0) && (*(volatile int*)a.err || globaltimer() - t0 > limit)) {
           atomicCAS(a.err, 0, 1);
           ok = false;
@@ -469,6 +575,11 @@ __device__ __forceinline__ float gelu(float v) {
   return 0.5f * v * (1.f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
 }
 
+// Fine-grained stamps inside one layer (opt-in stage profile only).
+constexpr int kProfLayer = 15;
+#define D1_FINE(idx) \
+  if (l == kProfLayer) stamp(a, tag, 200 + (idx))
+
 // One layer of the single-token forward at position `pos`.
 template <int NWJ_D, int NWJ_F>
 __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int pos, uint32_t tag) {
@@ -488,12 +599,21 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
     if (gw < QKV) rw.load(L.qkv, gw, D >> 3, lane);
     float gv[4], bv[4];
     load_gains(L.norm1, D, gpt2, gv, bv);
-    if (l > 0 && !poll_vec(x.x2 + ofs_d - (size_t)a.mmax * x.s_d, S.xs, D, tag, a.err, limit)) return false;
-    norm_row(S.xs, S.act, S.red, D, gpt2, gv[0], gv[1], gv[2], gv[3], bv[0], bv[1], bv[2], bv[3]);
+    float inv = 1.f;
+    if (!gpt2 && l > 0) {
+      if (!poll_x_rms(x.x2 + ofs_d - (size_t)a.mmax * x.s_d, S.xs, S.act, S.red, D, gv[0], gv[1], gv[2], gv[3], tag,
+                      a.err, limit, a.poll_sleep_ns))
+        return false;
+      inv = rms_inv(S.red, D);
+    } else {
+      if (l > 0 && !poll_vec(x.x2 + ofs_d - (size_t)a.mmax * x.s_d, S.xs, D, tag, a.err, limit, a.poll_sleep_ns)) return false;
+      norm_row(S.xs, S.act, S.red, D, gpt2, gv[0], gv[1], gv[2], gv[3], bv[0], bv[1], bv[2], bv[3]);
+    }
+    D1_FINE(1);
     uint64_t* dst = x.qkv + (size_t)l * a.mmax * x.s_qkv;
     for (int r = gw; r < QKV; r += NW) {
       if (r != gw) rw.load(L.qkv, r, D >> 3, lane);
-      float v = rw.dot(S.act, D >> 3, lane);
+      float v = rw.dot(S.act, D >> 3, lane) * inv;
       if (lane == 0) ll_store(dst + r, tag, L.qkv_b ? v + L.qkv_b[r] : v);
     }
     __syncthreads();
@@ -507,7 +627,8 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
   if (rows0 < D) {
     Row<NWJ_D> rw;
     if (gw < D) rw.load(L.proj, gw, D >> 3, lane);
-    if (!poll_vec(x.att + ofs_d, S.act, D, tag, a.err, limit)) return false;
+    if (!poll_vec(x.att + ofs_d, S.act, D, tag, a.err, limit, a.poll_sleep_ns)) return false;
+    D1_FINE(2);
     for (int r = gw; r < D; r += NW) {
       if (r != gw) rw.load(L.proj, r, D >> 3, lane);
       float v = rw.dot(S.act, D >> 3, lane);
@@ -519,41 +640,60 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
     __syncthreads();
   }
   stamp(a, tag, 3 + 6 * l);
-  // ---- w1/w3 rows + SiLU*mul, or fc + bias + GELU (wait: x1, then norm2)
+  // ---- w1/w3 rows + SiLU*mul, or fc + bias + GELU (wait: x1, then norm2).  A warp's first two rows
+  // (pairs) are requested before the wait.
   if (rows0 < FF) {
-    Row<NWJ_D> r1, r3;
+    Row<NWJ_D> r1, r3, r1b, r3b;
+    const int gw2 = gw + NW;
     if (gw < FF) {
       r1.load(L.w1, gw, D >> 3, lane);
       if (!gpt2) r3.load(L.w3, gw, D >> 3, lane);
     }
+    if (gw2 < FF) {
+      r1b.load(L.w1, gw2, D >> 3, lane);
+      if (!gpt2) r3b.load(L.w3, gw2, D >> 3, lane);
+    }
     float gv[4], bv[4];
     load_gains(L.norm2, D, gpt2, gv, bv);
-    if (!poll_vec(x.x1 + ofs_d, S.xs, D, tag, a.err, limit)) return false;
-    norm_row(S.xs, S.act, S.red, D, gpt2, gv[0], gv[1], gv[2], gv[3], bv[0], bv[1], bv[2], bv[3]);
+    float inv = 1.f;
+    if (!gpt2) {
+      if (!poll_x_rms(x.x1 + ofs_d, S.xs, S.act, S.red, D, gv[0], gv[1], gv[2], gv[3], tag, a.err, limit,
+                      a.poll_sleep_ns))
+        return false;
+      inv = rms_inv(S.red, D);
+    } else {
+      if (!poll_vec(x.x1 + ofs_d, S.xs, D, tag, a.err, limit, a.poll_sleep_ns)) return false;
+      norm_row(S.xs, S.act, S.red, D, gpt2, gv[0], gv[1], gv[2], gv[3], bv[0], bv[1], bv[2], bv[3]);
+    }
+    D1_FINE(4);
     uint64_t* dst = x.a + (size_t)l * a.mmax * x.s_ff;
-    for (int r = gw; r < FF; r += NW) {
-      if (r != gw) {
-        r1.load(L.w1, r, D >> 3, lane);
-        if (!gpt2) r3.load(L.w3, r, D >> 3, lane);
-      }
-      const float u = r1.dot(S.act, D >> 3, lane);
+    auto emit = [&](int r, const Row<NWJ_D>& ra, const Row<NWJ_D>& rb) {
+      const float u = ra.dot(S.act, D >> 3, lane) * inv;
       if (!gpt2) {
-        const float v = r3.dot(S.act, D >> 3, lane);
+        const float v = rb.dot(S.act, D >> 3, lane) * inv;
         if (lane == 0) ll_store(dst + r, tag, (u / (1.f + expf(-u))) * v);
       } else if (lane == 0) {
         ll_store(dst + r, tag, gelu(L.fc_b ? u + L.fc_b[r] : u));
       }
+    };
+    if (gw < FF) emit(gw, r1, r3);
+    if (gw2 < FF) emit(gw2, r1b, r3b);
+    for (int r = gw + 2 * NW; r < FF; r += NW) {
+      r1.load(L.w1, r, D >> 3, lane);
+      if (!gpt2) r3.load(L.w3, r, D >> 3, lane);
+      emit(r, r1, r3);
     }
     __syncthreads();
   } else if (rows0 < D) {
-    if (!poll_vec(x.x1 + ofs_d, S.xs, D, tag, a.err, limit)) return false;
+    if (!poll_vec(x.x1 + ofs_d, S.xs, D, tag, a.err, limit, a.poll_sleep_ns)) return false;
   }
   stamp(a, tag, 4 + 6 * l);
   // ---- w2 rows + residual (x2)
   if (rows0 < D) {
     Row<NWJ_F> rw;
     if (gw < D) rw.load(L.w2, gw, FF >> 3, lane);
-    if (!poll_vec(x.a + (size_t)l * a.mmax * x.s_ff, S.act, FF, tag, a.err, limit)) return false;
+    if (!poll_vec(x.a + (size_t)l * a.mmax * x.s_ff, S.act, FF, tag, a.err, limit, a.poll_sleep_ns)) return false;
+    D1_FINE(5);
     for (int r = gw; r < D; r += NW) {
       if (r != gw) rw.load(L.w2, r, FF >> 3, lane);
       float v = rw.dot(S.act, FF >> 3, lane);

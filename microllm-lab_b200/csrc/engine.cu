@@ -87,7 +87,7 @@ struct mllm_engine {
   std::string err;
   uint64_t* d_prof = nullptr;  // stage timestamps when MLLM_STAGE_PROFILE is set
   int prof_forward = -1;
-  int poll_sleep_ns = 0;       // MLLM_POLL_SLEEP_NS
+  int poll_sleep_ns = 200;     // MLLM_POLL_SLEEP_NS: back-off between poll rounds (less L2 contention)
   int weight_policy = 0;       // MLLM_WEIGHT_EVICT_LAST
   int l2_prefetch = 1;         // MLLM_L2_PREFETCH (default on)
   // layer-wise engine: token-batch forwards on the tensor cores (prefill, verify, batched decode)
