@@ -14,7 +14,9 @@ ranks / max-over-ranks time.  torch.distributed is used only for the barrier and
 
 ``--impl reference`` times the CPU restatement of the reference path (oracle/, the JS CPU path of
 engine/infer.js; the reference itself needs a JavaScript runtime, absent here) with all host threads
-on a bounded sample of the same workload.  Other workloads: ``--workload gemv|gpt2|spec``.
+on a bounded sample of the same workload.  Other workloads: ``--workload gpt2`` (config 3),
+``spec4``/``spec8`` (config 4, prompt-lookup speculation), ``gemv`` (config 2).  The default run also
+measures config 5 (replicated multi-sequence decode) as the ``batched`` sub-object.
 """
 from __future__ import annotations
 
@@ -185,6 +187,23 @@ def cpu_baseline_batched(data: bytes, plen: int, nnew: int, nseq: int, threads: 
 
 BATCHED = dict(model="smollm2-135m", seed=4, nseq=256, plen=128, nnew=256)
 
+WORKLOADS = {
+    "decode": dict(model="petitgpt", seed=0, prompt=64, new=128, workload="config1 petitgpt b1 p64 n128",
+                   metric="batch-1 Q4 decode tok/s (PetitGPT shape, 64-token prompt, 128 new tokens)",
+                   model_text="PetitGPT-shaped Q4 (30L d576 9/3 ff1536 V32000)"),
+    "gpt2": dict(model="gpt2", seed=2, prompt=128, new=256, workload="config3 gpt2 b1 p128 n256 argmaxGpt2",
+                 metric="batch-1 Q4 decode tok/s (GPT-2 124M shape, 128-token prompt, 256 new tokens)",
+                 model_text="GPT-2-shaped Q4 (12L d768 12 heads ff3072 V50257, LayerNorm, GELU, wpe)"),
+    "spec4": dict(model="smollm2-360m", seed=3, prompt=512, new=256, spec_k=4, copy_spans=True,
+                  workload="config4 smollm2-360m p512 n256 prompt-lookup k4 n3",
+                  metric="batch-1 Q4 decode tok/s with prompt-lookup speculation (SmolLM2-360M shape, k=4)",
+                  model_text="SmolLM2-360M-shaped Q4 (32L d960 15/5 ff2560 V49152)"),
+    "spec8": dict(model="smollm2-360m", seed=3, prompt=512, new=256, spec_k=8, copy_spans=True,
+                  workload="config4 smollm2-360m p512 n256 prompt-lookup k8 n3",
+                  metric="batch-1 Q4 decode tok/s with prompt-lookup speculation (SmolLM2-360M shape, k=8)",
+                  model_text="SmolLM2-360M-shaped Q4 (32L d960 15/5 ff2560 V49152)"),
+}
+
 
 def run_batched_leg(torch, P, local: int, rank: int, ws: int, dist, steps: int, warmup: int, cpu: bool):
     """BASELINE config 5 on this rank's GPU: 256 independent sequences (this rank's partition of the
@@ -303,6 +322,87 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+GEMV_SHAPES = [(576, 576), (192, 576), (1536, 576), (576, 1536), (960, 960), (2560, 960), (960, 2560), (49152, 576)]
+
+
+def run_gemv(args):
+    """isolated Q4 GEMV / skinny GEMM on the config's shapes and M in {1, 5, 9, 16}.
+    For every point both device paths are timed (CUDA-core GEMV, tensor-core GEMM) over a CUDA graph of
+    back-to-back launches: hot = one weight matrix reused, cold = a rotating set of copies larger than
+    L2.  GB/s counts packed nibbles + scales (out*in/2 + out*in/32*4 bytes) per launch."""
+    import torch
+    ws, rank, local = dist_setup()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    P = pkg()
+    rng = np.random.default_rng(1)
+    hbm, _, peak_kind = peaks()
+    st = torch.cuda.Stream()
+    rows = []
+    launches = 0
+    reps = 50
+    with ClockSampler(local) as clk:
+        for (R, C) in GEMV_SHAPES:
+            w = (rng.standard_normal((R, C), dtype=np.float32) * np.float32(0.02))
+            packed, scales = P.quant_q4(w)
+            bytes_w = packed.nbytes + scales.nbytes
+            ncopy = max(1, -(-2 * L2_BYTES // bytes_w))
+            pk = torch.from_numpy(np.ascontiguousarray(packed).reshape(-1)).cuda()
+            sc = torch.from_numpy(np.ascontiguousarray(scales).reshape(-1)).cuda()
+            pks = pk.repeat(ncopy).view(ncopy, -1)
+            scs = sc.repeat(ncopy).view(ncopy, -1)
+            for M in (1, 5, 9, 16):
+                x = torch.from_numpy(rng.standard_normal((M, C), dtype=np.float32)).cuda()
+                y = torch.empty((M, R), device="cuda")
+                point = {"shape": f"{R}x{C}", "M": M, "weight_bytes": bytes_w}
+                for path, fn in (("cuda_core", P.gemv_q4_device), ("tensor", P.gemm_q4_device)):
+                    for mode in ("hot", "cold"):
+                        n = reps if mode == "hot" else min(ncopy, 4096)
+                        idx = [0] * n if mode == "hot" else list(range(n))
+                        with torch.cuda.stream(st):
+                            for i in range(3):  # warm-up (allocates the GEMM workspace before capture)
+                                fn(pks[0].data_ptr(), scs[0].data_ptr(), x.data_ptr(), y.data_ptr(), R, C, M, st.cuda_stream)
+                        st.synchronize()
+                        g = torch.cuda.CUDAGraph()
+                        with torch.cuda.graph(g, stream=st):
+                            for i in idx:
+                                fn(pks[i].data_ptr(), scs[i].data_ptr(), x.data_ptr(), y.data_ptr(), R, C, M,
+                                   torch.cuda.current_stream().cuda_stream)
+                        g.replay()
+                        torch.cuda.synchronize()
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        e0.record()
+                        for _ in range(args.steps):
+                            g.replay()
+                        e1.record()
+                        e1.synchronize()
+                        us = e0.elapsed_time(e1) * 1e3 / (args.steps * n)
+                        launches += args.steps * n * (1 if path == "cuda_core" else 2)
+                        point[f"{path}_{mode}_us"] = us
+                        point[f"{path}_{mode}_gbs"] = bytes_w / (us * 1e-6) / 1e9
+                        del g
+                best = max(point["cuda_core_cold_gbs"], point["tensor_cold_gbs"])
+                point["best_cold_gbs"] = best
+                point["best_hot_gbs"] = max(point["cuda_core_hot_gbs"], point["tensor_hot_gbs"])
+                rows.append(point)
+            del pks, scs
+    head = next(r for r in rows if r["shape"] == "49152x576" and r["M"] == 1)
+    line = {
+        "metric": "Q4 g32 GEMV weight GB/s (lm_head 49152x576, M=1, cold L2)", "value": head["best_cold_gbs"],
+        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": 3, "ms_per_step": None,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4xf32",
+        "data": "synthetic (W ~ N(0,0.02) Q4 g32 seed 1, x ~ N(0,1))",
+        "config": {"workload": "config2 gemv microbench", "shapes": [f"{r}x{c}" for r, c in GEMV_SHAPES],
+                   "M": [1, 5, 9, 16], "timing": "CUDA graph of back-to-back launches, events around replays",
+                   "cold": "rotating copies, total > 2x L2"},
+        "roofline": {"bound": "hbm", "achieved": head["best_cold_gbs"], "peak": hbm, "unit": "GB/s",
+                     "frac": head["best_cold_gbs"] / hbm, "peak_kind": peak_kind, "traffic": None},
+        "gpu_launches": launches, "points": rows, "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_decode(args):
     import torch
     ws, rank, local = dist_setup()
@@ -314,11 +414,14 @@ def run_decode(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
     P = pkg()
-    name = "petitgpt"
+    W = WORKLOADS[args.workload]
+    name, seed, n_prompt, n_new, spec_k = W["model"], W["seed"], W["prompt"], W["new"], W.get("spec_k", 0)
     cfg = P.CONFIGS[name]
-    data = P.synthetic_pgw(name, 0, cache_dir=CACHE)
-    n_prompt, n_new = 64, 128
-    prompt = P.seeded_prompt(n_prompt, cfg["vocabSize"], rank)
+    data = P.synthetic_pgw(name, seed, cache_dir=CACHE)
+    if W.get("copy_spans"):
+        prompt = P.copy_span_prompt(n_prompt, cfg["vocabSize"], seed + rank)
+    else:
+        prompt = P.seeded_prompt(n_prompt, cfg["vocabSize"], seed + rank)
     eng = P.CudaPetitGPT(data, device=local)
     stream = torch.cuda.Stream()
     eng.set_stream(stream.cuda_stream)
@@ -330,17 +433,20 @@ def run_decode(args):
 
     launches = [0]
 
+    spec_stats = []
+
     def step_device():
-        st = eng.generate_device(d_ids.data_ptr(), n_prompt, d_out.data_ptr(), n_new, -1)
+        st = eng.generate_device(d_ids.data_ptr(), n_prompt, d_out.data_ptr(), n_new, -1, spec_k, 3)
         assert st.n_generated == n_new, st.n_generated
         launches[0] += st.kernel_launches
+        spec_stats.append((st.spec_hits, st.spec_tries, st.forwards))
         return st
 
     def step_e2e():
         import ctypes
         st = P.engine.Stats()
-        eng._check(eng._lib.mllm_generate(eng._h, 0, ctypes.c_void_p(h_prompt.data_ptr()), n_prompt, n_new, -1, 0, 3,
-                                          ctypes.c_void_p(h_out.data_ptr()), ctypes.byref(st)))
+        eng._check(eng._lib.mllm_generate(eng._h, 0, ctypes.c_void_p(h_prompt.data_ptr()), n_prompt, n_new, -1, spec_k,
+                                          3, ctypes.c_void_p(h_out.data_ptr()), ctypes.byref(st)))
         assert st.n_generated == n_new
 
     def timed(fn, k):
@@ -386,11 +492,11 @@ def run_decode(args):
     alg = decode_algorithmic_bytes(cfg, n_prompt, n_new)
     achieved = alg / (ms_step / 1e3) / 1e9
     line = {
-        "metric": "batch-1 Q4 decode tok/s (PetitGPT shape, 64-token prompt, 128 new tokens)",
+        "metric": W["metric"],
         "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4xf32",
         "data": "synthetic (seeded N(0,0.02) Q4 weights, seeded uniform prompt ids; real checkpoints are LFS stubs)",
-        "config": {"workload": "config1 petitgpt b1 p64 n128", "model": "PetitGPT-shaped Q4 (30L d576 9/3 ff1536 V32000)",
+        "config": {"workload": W["workload"], "model": W["model_text"],
                    "global_batch": ws, "seq_len": n_prompt + n_new, "parallelism": f"replicas x{ws}",
                    "l2": "flushed (256 MB write) before every timed step; weights 78 MB fit in L2 within a step",
                    "tokens_per_step": n_new,
@@ -405,14 +511,29 @@ def run_decode(args):
                      "kernel_ms_device_timer": float(np.mean(dev_ms)) if dev_ms else None},
         "clocks": clk.summary(),
     }
+    if spec_k:
+        hits = sum(h for h, _, _ in spec_stats[-args.steps:]) / args.steps
+        tries = sum(t for _, t, _ in spec_stats[-args.steps:]) / args.steps
+        fw = sum(f for _, _, f in spec_stats[-args.steps:]) / args.steps
+        line["speculation"] = {"spec_k": spec_k, "ngram": 3, "spec_hits": hits, "spec_tries": tries,
+                               "acceptance_rate": hits / max(tries * spec_k, 1), "accepted_per_try": hits / max(tries, 1),
+                               "forwards_per_call": fw, "tokens_per_forward": n_new / max(fw, 1)}
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         v, pre, per = cpu_baseline_decode(data, prompt, n_new, 1, 4)
         line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": 1, "kind": "port",
-                                "sample": f"oracle (C restatement of engine/infer.js), 1 thread: 64-token prefill "
-                                          f"({pre:.2f} s) + 4 decode steps ({per*1e3:.0f} ms/token), extrapolated "
-                                          f"to 127 decode steps"}
+                                "sample": f"oracle (C restatement of engine/infer.js), 1 thread: {n_prompt}-token "
+                                          f"prefill ({pre:.2f} s) + 4 decode steps ({per*1e3:.0f} ms/token), "
+                                          f"extrapolated to {n_new - 1} decode steps (greedy, no speculation)"}
+    if spec_k and rank == 0:
+        # the same model and prompt without speculation, for the speed-up
+        greedy = []
+        for _ in range(2):
+            st = eng.generate_device(d_ids.data_ptr(), n_prompt, d_out.data_ptr(), n_new, -1, 0, 3)
+            greedy.append(st.total_ms)
+        line["speculation"]["greedy_tok_s"] = n_new / (min(greedy) / 1e3)
+        line["speculation"]["speedup_vs_greedy"] = value / line["speculation"]["greedy_tok_s"]
     eng.destroy()
-    if not args.no_batched:
+    if not args.no_batched and args.workload == "decode":
         line["batched"] = run_batched_leg(torch, P, local, rank, ws, dist, args.batched_steps, 1,
                                           not args.no_cpu_baseline)
     if rank == 0:
@@ -428,13 +549,15 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gpt2", "spec4", "spec8", "gemv"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the config-5 batched sub-object")
     ap.add_argument("--batched-steps", type=int, default=3)
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "gemv":
+        run_gemv(args)
     else:
         run_decode(args)
 
