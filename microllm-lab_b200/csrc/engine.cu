@@ -97,9 +97,11 @@ struct mllm_engine {
   int tmax = 0;                // token rows per forward (MLLM_LWE_TOKENS)
   LweArgs lw{};
   LweHost lh;
-  Grow g_bids, g_plan, g_bout, g_state, g_blogits;
+  Grow g_bids, g_plan, g_bout, g_state, g_blogits, g_spec;
   int32_t* h_active = nullptr; // pinned
   long coop_launches = 0;      // persistent-kernel launches issued by this handle
+  long spec_graph_kernels = 0; // kernels in one speculation graph replay
+  long spec_replay_kernels = 0;
 };
 
 namespace {
@@ -303,6 +305,7 @@ int finish(mllm_engine* e) {
   if (e->h_status[ST_WORDS] != 0) {
     // a CTA that gave up may have left a completion counter of the token-batch kernels non-zero
     cudaMemset(e->lh.attn_ctr, 0, e->lh.attn_ctr_n * sizeof(int));
+    cudaMemset(e->lw.skctr, 0, kLweSplitKTiles * sizeof(int));
   }
   if (e->h_status[ST_WORDS] == 2) return fail(e, MLLM_ERR_ARG, "a prompt token id is out of range");
   if (e->h_status[ST_WORDS] != 0)
@@ -344,6 +347,62 @@ int lwe_run(mllm_engine* e, int slot, const int32_t* d_ids, int n, int pos0, int
   return MLLM_OK;
 }
 
+// Prompt-lookup speculation after a token-batch prefill (first id already in d_out[0]): iterations of
+// draft lookup -> (k + 1)-row verify forward -> accept, one CUDA graph replay each, state on the
+// device; the host only checks the done word every few replays.
+int spec_loop(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max_new, int32_t eos, int k, int ngram,
+              int32_t* d_out, int prefill_forwards) {
+  cudaStream_t st = e->stream;
+  TRY(grow(e, e->g_spec, (size_t)(kSpecHist + e->md.kv_len + 128) * 4));
+  int32_t* sp = (int32_t*)e->g_spec.p;
+  lwe_spec_init(sp, d_ids, n, d_out, max_new, eos, e->md.kv_len, prefill_forwards, st);
+  const LweArgs a = lwe_args(e);
+  cudaGraphExec_t exec = nullptr;
+  if (e->lwe_graph) {
+    cudaGraph_t graph = nullptr;
+    CUDA_TRY(e, cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    const long c0 = launches_now(e);
+    const cudaError_t r1 = lwe_spec_iteration(a, e->lh, sp, d_out, k, ngram, max_new, eos, slot, st);
+    e->spec_graph_kernels = launches_now(e) - c0;
+    const cudaError_t r2 = cudaStreamEndCapture(st, &graph);
+    if (r1 != cudaSuccess || r2 != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      return fail(e, MLLM_ERR_CUDA, "capture of the speculation step failed: %s",
+                  cudaGetErrorString(r1 != cudaSuccess ? r1 : r2));
+    }
+    const cudaError_t r3 = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (r3 != cudaSuccess) return fail(e, MLLM_ERR_CUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(r3));
+  }
+  cudaError_t rs = cudaSuccess;
+  long replays = 0;
+  // MLLM_PROFILE_SPEC_ITERS=k brackets the first k iterations with cudaProfilerStart/Stop.
+  int prof_iters = 0;
+  if (const char* v = getenv("MLLM_PROFILE_SPEC_ITERS")) prof_iters = atoi(v);
+  if (prof_iters > 0) {
+    cudaProfilerStart();
+    for (int i = 0; i < prof_iters; ++i)
+      rs = exec ? cudaGraphLaunch(exec, st) : lwe_spec_iteration(a, e->lh, sp, d_out, k, ngram, max_new, eos, slot, st);
+    replays += prof_iters;
+    cudaStreamSynchronize(st);
+    cudaProfilerStop();
+  }
+  for (int it = (int)replays; it < max_new + 1 && rs == cudaSuccess;) {
+    for (int b = 0; b < 4 && rs == cudaSuccess; ++b, ++it, ++replays)
+      rs = exec ? cudaGraphLaunch(exec, st) : lwe_spec_iteration(a, e->lh, sp, d_out, k, ngram, max_new, eos, slot, st);
+    if (rs == cudaSuccess) rs = cudaMemcpyAsync(e->h_active, sp + kSpecDoneWord, 4, cudaMemcpyDeviceToHost, st);
+    if (rs == cudaSuccess) rs = cudaStreamSynchronize(st);
+    if (rs == cudaSuccess && *e->h_active) break;
+  }
+  if (exec) {
+    cudaGraphExecDestroy(exec);
+    e->spec_replay_kernels = replays * e->spec_graph_kernels;
+  }
+  if (rs != cudaSuccess) return fail(e, MLLM_ERR_CUDA, "speculation step: %s", cudaGetErrorString(rs));
+  lwe_spec_finish(sp, e->d_status, st);
+  return MLLM_OK;
+}
+
 int generate_impl(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max_new, int32_t eos, int spec_k,
                   int ngram, int32_t* d_out, mllm_stats* st) {
   TRY(check_slot(e, slot));
@@ -376,9 +435,12 @@ int generate_impl(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max
     int f = 0;
     TRY(lwe_run(e, slot, d_ids, n, 0, 0, nullptr, e->lw.amax, &f));
     lwe_first(lwe_args(e), d_out, e->d_status, eos, f, e->stream);
-    if (max_new > 1) {
+    if (spec_k > 0) {
+      e->spec_graph_kernels = e->spec_replay_kernels = 0;
+      TRY(spec_loop(e, slot, d_ids, n, max_new, eos, std::min(spec_k, kSpecMaxK), ngram, d_out, f));
+    } else if (max_new > 1) {
       a.start_gen = 1;
-      TRY(launch(e, a, max_new + 1, spec_k > 0, true));
+      TRY(launch(e, a, max_new + 1, false, true));
     }
   } else if (spec_k > 0) {
     TRY(launch(e, a, chunks + max_new + 1, true));
@@ -411,7 +473,9 @@ int generate_impl(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max
     const uint64_t t0 = u64_at(hs, ST_T0), t1 = u64_at(hs, ST_TFIRST), t2 = u64_at(hs, ST_TEND);
     st->ttft_ms = t1 > t0 ? (float)((t1 - t0) * 1e-6) : 0.f;
     st->total_ms = t2 > t0 ? (float)((t2 - t0) * 1e-6) : 0.f;
-    st->kernel_launches = (int32_t)(launches_now(e) - l0);
+    // graph replays ran spec_graph_kernels kernels each; the capture itself ran none
+    st->kernel_launches =
+        (int32_t)(launches_now(e) - l0 - (spec_k > 0 ? e->spec_graph_kernels - e->spec_replay_kernels : 0));
   }
   return MLLM_OK;
 }
@@ -427,7 +491,7 @@ void mllm_destroy(mllm_engine* e) {
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
   for (void* p : e->allocs) cudaFree(p);
-  for (Grow* g : {&e->g_bids, &e->g_plan, &e->g_bout, &e->g_state, &e->g_blogits})
+  for (Grow* g : {&e->g_bids, &e->g_plan, &e->g_bout, &e->g_state, &e->g_blogits, &e->g_spec})
     if (g->p) cudaFree(g->p);
   if (e->h_status) cudaFreeHost(e->h_status);
   if (e->h_active) cudaFreeHost(e->h_active);
@@ -608,22 +672,26 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
     int chunk, splits;
     lwe_attn_split_shape(md.kv_len, &chunk, &splits);
     const size_t rep = md.NH / md.NKV;
-    if ((rc = dev_alloc(E, &e->lh.attn_part, T * md.NKV * splits * rep * 66 * 4)) ||
-        (rc = dev_alloc(E, &e->lh.attn_ctr, T * md.NKV * sizeof(int))))
+    // the position-split attention runs on decode steps (one row per slot) and short verify forwards
+    const size_t arows = std::min<size_t>(T, std::max<size_t>(e->slots.size(), kLweSplitAttnRows));
+    if ((rc = dev_alloc(E, &e->lh.attn_part, arows * md.NKV * splits * rep * 66 * 4)) ||
+        (rc = dev_alloc(E, &e->lh.attn_ctr, arows * md.NKV * sizeof(int))))
       return relay(rc);
-    e->lh.attn_ctr_n = T * md.NKV;
-    cudaMemset(e->lh.attn_ctr, 0, T * md.NKV * sizeof(int));
+    e->lh.attn_ctr_n = arows * md.NKV;
+    cudaMemset(e->lh.attn_ctr, 0, arows * md.NKV * sizeof(int));
     if ((rc = dev_alloc(E, &w.x, T * D * 4)) || (rc = dev_alloc(E, &w.xh, T * w.ldx * 2)) ||
         (rc = dev_alloc(E, &w.xl, T * w.ldx * 2)) || (rc = dev_alloc(E, &w.xh2, T * w.ldx2 * 2)) ||
         (rc = dev_alloc(E, &w.xl2, T * w.ldx2 * 2)) || (rc = dev_alloc(E, &w.qkv, T * md.QKV * 4)) ||
         (rc = dev_alloc(E, &w.xh3, T * w.ldx * 2)) || (rc = dev_alloc(E, &w.xl3, T * w.ldx * 2)) ||
-        (rc = dev_alloc(E, &w.ss, T * kLweSsStride * 4)) ||
+        (rc = dev_alloc(E, &w.ss, T * kLweSsStride * 4)) || (rc = dev_alloc(E, &w.skws, kLweSplitKBytes)) ||
+        (rc = dev_alloc(E, &w.skctr, kLweSplitKTiles * sizeof(int))) ||
         (rc = dev_alloc(E, &w.tok, T * 4)) || (rc = dev_alloc(E, &w.slot, T * 4)) || (rc = dev_alloc(E, &w.pos, T * 4)) ||
         (rc = dev_alloc(E, &w.lm_src, T * 4)) || (rc = dev_alloc(E, &w.amax, T * 4)) ||
         (rc = dev_alloc(E, &w.pval, nblk * T * 4)) || (rc = dev_alloc(E, &w.pidx, nblk * T * 4)) ||
         (rc = dev_alloc(E, &kc, e->slots.size() * sizeof(float*))) ||
         (rc = dev_alloc(E, &vc, e->slots.size() * sizeof(float*))))
       return relay(rc);
+    cudaMemset(w.skctr, 0, kLweSplitKTiles * sizeof(int));
     std::vector<float*> hk, hv;
     for (auto& sl : e->slots) {
       hk.push_back(sl.k);

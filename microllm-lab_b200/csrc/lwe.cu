@@ -48,6 +48,65 @@ __device__ __forceinline__ float fold_inv(const LweArgs& a, int t) {
   return 1.f / sqrtf(s / a.m.D + 1e-6f);
 }
 
+// Split-K across CTAs (gridDim.z > 1, few-token GEMMs): each CTA leaves its partial tile in
+// a.skws; the last CTA of a tile (counter a.skctr[tile], reset by it) adds the partials in split order
+// and goes on to the epilogue, the others return false.  With gridDim.z == 1 it returns true at once.
+template <int TBW>
+__device__ __forceinline__ bool lwe_splitk(const LweArgs& a, float (&acc)[TBW][4]) {
+  const int nz = gridDim.z;
+  if (nz == 1) return true;
+  const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+  const bool g0 = threadIdx.x < kGemmThreads;
+  float* mine = a.skws + (((size_t)tile * nz + blockIdx.z) * kGemmThreads + (threadIdx.x & (kGemmThreads - 1))) * TBW * 4;
+  if (g0) {
+#pragma unroll
+    for (int b = 0; b < TBW; ++b) reinterpret_cast<float4*>(mine)[b] = make_float4(acc[b][0], acc[b][1], acc[b][2], acc[b][3]);
+  }
+  __shared__ int last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int done = atomicAdd(&a.skctr[tile], 1) + 1;
+    last = done == nz;
+    if (last) a.skctr[tile] = 0;
+  }
+  __syncthreads();
+  if (!last) return false;
+  __threadfence();
+  if (g0) {
+#pragma unroll
+    for (int b = 0; b < TBW; ++b) acc[b][0] = acc[b][1] = acc[b][2] = acc[b][3] = 0.f;
+    for (int z = 0; z < nz; ++z) {
+      const float* pz = a.skws + (((size_t)tile * nz + z) * kGemmThreads + threadIdx.x) * TBW * 4;
+#pragma unroll
+      for (int b = 0; b < TBW; ++b) {
+        const float4 v = ldcg_f4(pz + 4 * b);
+        acc[b][0] += v.x;
+        acc[b][1] += v.y;
+        acc[b][2] += v.z;
+        acc[b][3] += v.w;
+      }
+    }
+  }
+  return true;
+}
+
+// Element-wise epilogue over a 64-row tile (threads of the first warp group): epi(row, token, value).
+template <int TBW, class Epi>
+__device__ __forceinline__ void lwe_tile_epi(const float (&acc)[TBW][4], int r0, int t0, int R, int T, Epi epi) {
+  if (threadIdx.x >= kGemmThreads) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
+  const int ra = r0 + warp * 16 + gid, rb = ra + 8;
+#pragma unroll
+  for (int b = 0; b < TBW; ++b) {
+    const int ta = t0 + b * 8 + 2 * t, tb = ta + 1;
+    if (ra < R && ta < T) epi(ra, ta, acc[b][0]);
+    if (ra < R && tb < T) epi(ra, tb, acc[b][1]);
+    if (rb < R && ta < T) epi(rb, ta, acc[b][2]);
+    if (rb < R && tb < T) epi(rb, tb, acc[b][3]);
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 // RMSNorm (engine/infer.js:134-143) or LayerNorm (engine/infer.js:147-164) of one row by one warp,
 // written as fp16 hi/lo.  The row (D <= 1024) is read once into registers through L2 (rows written by
@@ -114,6 +173,7 @@ __device__ __forceinline__ void warp_norm_split(const float* x, int D, bool ln, 
 
 // Embedding of token t (one CTA per token); with g != nullptr also the first layer's norm1 into xh/xl.
 __global__ void lwe_embed(const __grid_constant__ LweArgs a, int T, const float* g) {
+  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   const int t = blockIdx.x;
   if (t >= T) return;
   const ModelDev& md = a.m;
@@ -159,6 +219,7 @@ __global__ void lwe_embed(const __grid_constant__ LweArgs a, int T, const float*
 
 // RMSNorm / LayerNorm of X[src[i]] (or X[i]) -> fp16 hi/lo rows i of xh/xl.  One CTA per row.
 __global__ void lwe_norm_split(const __grid_constant__ LweArgs a, int T, const float* g, const int* src) {
+  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   const int i = blockIdx.x;
   if (i >= T) return;
   const ModelDev& md = a.m;
@@ -213,6 +274,7 @@ __global__ void lwe_norm_split(const __grid_constant__ LweArgs a, int T, const f
 template <int TBW, int KS>
 __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_qkv(const __grid_constant__ LweArgs a, int T,
                                                                          int l) {
+  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(16) unsigned char smem[];
   using C = LweTile<TBW, KS>;
   __shared__ float sinv[C::BT];
@@ -222,16 +284,21 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_qkv(const 
   __syncthreads();
   const float* bias = L.qkv_b;
   float* out = a.qkv;
-  q4_gemm_tile<TBW, C::NS, C::KS>(reinterpret_cast<const uint8_t*>(L.qkv.w), L.qkv.s, a.xh, a.xl, a.ldx, R, K, T,
-                                  blockIdx.x * kGemmRows, t0, smem, [&](int r, int t, float v) {
-                                    v *= sinv[t - t0];
-                                    out[(size_t)t * R + r] = bias ? v + bias[r] : v;
-                                  });
+  const int r0 = blockIdx.x * kGemmRows;
+  const RowsLinear rows{reinterpret_cast<const uint8_t*>(L.qkv.w), L.qkv.s, R, r0, K >> 1, K >> 5};
+  float acc[TBW][4];
+  q4_gemm_core<TBW, C::NS, C::KS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  if (!lwe_splitk<TBW>(a, acc)) return;
+  lwe_tile_epi<TBW>(acc, r0, t0, R, T, [&](int r, int t, float v) {
+    v *= sinv[t - t0];
+    out[(size_t)t * R + r] = bias ? v + bias[r] : v;
+  });
 }
 
 // RoPE on k (and on the q heads of the group) at each token's position, then the K/V cache write
 // (engine/infer.js:436-464).  grid (T, NKV), 64 threads: thread d < 32 rotates pair (d, d + 32).
 __global__ void lwe_rope_kv(const __grid_constant__ LweArgs a, int T) {
+  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   const int t = blockIdx.x, g = blockIdx.y;
   if (t >= T) return;
   const ModelDev& md = a.m;
@@ -270,6 +337,7 @@ __global__ void lwe_rope_kv(const __grid_constant__ LweArgs a, int T) {
 // (engine/infer.js:459-464) before reading the cache; otherwise lwe_rope_kv ran first.
 template <int REP, bool FUSED>
 __global__ void __launch_bounds__(128) lwe_attention(const __grid_constant__ LweArgs a, int T) {
+  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(16) float asm_[];
   const int t = blockIdx.x, g = blockIdx.y;
   if (t >= T) return;
@@ -403,8 +471,9 @@ __global__ void __launch_bounds__(128) lwe_attention(const __grid_constant__ Lwe
 // ctr[t*NKV+g], reset by it) merges them in split order and writes the heads' outputs as fp16 hi/lo
 // into xh/xl.
 constexpr int kAttnChunk = 64;
-template <int REP>
+template <int REP, bool FUSED>
 __global__ void __launch_bounds__(64) lwe_attn_split(const __grid_constant__ LweArgs a, int T, float* part, int* ctr) {
+  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(128) float kvs[];  // K [64][64], V [64][64]
   const int t = blockIdx.x, g = blockIdx.y, sp = blockIdx.z, S = gridDim.z;
   const ModelDev& md = a.m;
@@ -425,7 +494,7 @@ __global__ void __launch_bounds__(64) lwe_attn_split(const __grid_constant__ Lwe
   float* vcw = a.vc[a.slot[t]] + base;
   float* mypart = part + (((size_t)t * NKV + g) * S + sp) * REP * 66;
   if (n > 0) {
-    const bool owner = p1 == npos;
+    const bool owner = FUSED && p1 == npos;
     if (tid == 0) {
       mbar_init(&bar, 1);
       mbar_init_fence();
@@ -446,7 +515,7 @@ __global__ void __launch_bounds__(64) lwe_attn_split(const __grid_constant__ Lwe
       vcw[(size_t)pos * 64 + tid] = vnew;
     }
     __syncthreads();
-    if (md.arch == 0 && md.rope_dim > 0) {
+    if (FUSED && md.arch == 0 && md.rope_dim > 0) {  // unfused: lwe_rope_kv rotated q and wrote K/V
       const int half = md.rope_dim / 2;
       const float* cs = md.rope_cos + (size_t)pos * md.rope_dim;
       const float* sn = md.rope_sin + (size_t)pos * md.rope_dim;
@@ -588,6 +657,7 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_resid(cons
                                                                            Q4 w, const float* bias, int K,
                                                                            const float* gn, __half* nh, __half* nl,
                                                                            int ldn) {
+  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(16) unsigned char smem[];
   using C = LweTile<TBW, KS>;
   __shared__ float ssw[4][C::BT];
@@ -596,6 +666,7 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_resid(cons
   const RowsLinear rows{reinterpret_cast<const uint8_t*>(w.w), w.s, R, r0, K >> 1, K >> 5};
   float acc[TBW][4];
   q4_gemm_core<TBW, C::NS, C::KS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  if (!lwe_splitk<TBW>(a, acc)) return;
   if (threadIdx.x < kGemmThreads) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tq = lane & 3;
     const int ra = r0 + warp * 16 + gid, rb = ra + 8;
@@ -649,6 +720,7 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_resid(cons
 template <int TBW, int KS>
 __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_w13(const __grid_constant__ LweArgs a, int T,
                                                                          int l) {
+  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(16) unsigned char smem[];
   using C = LweTile<TBW, KS>;
   __shared__ float sinv[C::BT];
@@ -664,6 +736,7 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_w13(const 
   float acc[TBW][4];
   const int t0 = blockIdx.y * C::BT;
   q4_gemm_core<TBW, C::NS, C::KS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  if (!lwe_splitk<TBW>(a, acc)) return;
   if (threadIdx.x >= kGemmThreads) return;  // partial sums were added into the first warp group
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
   const int ia = warp * 16 + gid;  // A row (w1); the B row (w3) of the same matrix row is ia + 8
@@ -687,17 +760,22 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_w13(const 
 template <int TBW, int KS>
 __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_fc(const __grid_constant__ LweArgs a, int T,
                                                                         int l) {
+  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(16) unsigned char smem[];
   using C = LweTile<TBW, KS>;
   const LayerDev& L = a.m.layers[l];
   const int FF = a.m.FF, K = a.m.D;
   const float* bias = L.fc_b;
-  q4_gemm_tile<TBW, C::NS, C::KS>(reinterpret_cast<const uint8_t*>(L.w1.w), L.w1.s, a.xh, a.xl, a.ldx, FF, K, T,
-                           blockIdx.x * kGemmRows, blockIdx.y * C::BT, smem, [&](int r, int t, float v) {
-                          if (bias) v += bias[r];
-                          const float gl = 0.5f * v * (1.f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
-                          split_hi_lo(gl, a.xh2[(size_t)t * a.ldx2 + r], a.xl2[(size_t)t * a.ldx2 + r]);
-                        });
+  const int r0 = blockIdx.x * kGemmRows, t0 = blockIdx.y * C::BT;
+  const RowsLinear rows{reinterpret_cast<const uint8_t*>(L.w1.w), L.w1.s, FF, r0, K >> 1, K >> 5};
+  float acc[TBW][4];
+  q4_gemm_core<TBW, C::NS, C::KS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  if (!lwe_splitk<TBW>(a, acc)) return;
+  lwe_tile_epi<TBW>(acc, r0, t0, FF, T, [&](int r, int t, float v) {
+    if (bias) v += bias[r];
+    const float gl = 0.5f * v * (1.f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
+    split_hi_lo(gl, a.xh2[(size_t)t * a.ldx2 + r], a.xl2[(size_t)t * a.ldx2 + r]);
+  });
 }
 
 // lm_head GEMM over the T rows in xh/xl with a per-CTA argmax epilogue: for each token, the best
@@ -705,6 +783,7 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_fc(const _
 // logits store [t][V].
 template <int TBW>
 __global__ void __launch_bounds__(kGemmThreads) lwe_gemm_lm(const __grid_constant__ LweArgs a, int T, float* logits) {
+  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(16) unsigned char smem[];
   using C = LweTile<TBW, 1>;
   constexpr int kLweBT = C::BT;
@@ -774,6 +853,7 @@ __global__ void __launch_bounds__(kGemmThreads) lwe_gemm_lm(const __grid_constan
 
 // Per token: argmax over the row-block partials -> amax[t]; optional scatter of the result.
 __global__ void lwe_argmax_reduce(const __grid_constant__ LweArgs a, int T, int nblk) {
+  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -842,33 +922,47 @@ __global__ void lwe_first_token(const int32_t* amax, int32_t* out_ids, int32_t* 
 // Tokens per CTA: the largest tile that still gives two CTAs per SM, else the smallest.
 static int pick_tbw(int row_tiles, int T) {
   constexpr int kTarget = 2 * 148;
+  if (T <= 16) return 2;  // one token tile either way: the smallest wastes the least
+  if (T <= 32) return row_tiles >= kTarget ? 4 : 2;
   if ((long)row_tiles * ((T + 63) / 64) >= kTarget) return 8;
   if ((long)row_tiles * ((T + 31) / 32) >= kTarget) return 4;
   return 2;
 }
 
-// Tokens per CTA as above; then the in-CTA k split for GEMMs that still have few CTAs.
+// Tokens per CTA as above; then the in-CTA k split for GEMMs that still have few CTAs, and for very
+// few CTAs (a handful of tokens) a split of the k groups across CTAs as well (at least 8 groups each).
 static int pick_ks(int ctas) { return ctas >= 2 * 148 ? 1 : (ctas >= 148 ? 2 : 4); }
+static int pick_ksplit(int ctas, int K, int TBW) {
+  if (ctas >= 96) return 1;  // enough CTAs with the in-CTA split alone
+  int z = (2 * 148 + ctas - 1) / ctas;
+  z = std::min(z, std::max(1, (K / 32) / 8));
+  z = std::min(z, 16);
+  // the partial tiles must fit the workspace
+  while (z > 1 && (size_t)ctas * z * kGemmThreads * TBW * 4 * 4 > kLweSplitKBytes) --z;
+  return z;
+}
 
-#define LWE_LAUNCH_(KER, TB, KSV, TILES, T, ...)                                                      \
-  KER<TB, KSV><<<dim3(TILES, ((T) + 8 * TB - 1) / (8 * TB)), LweTile<TB, KSV>::THREADS, LweTile<TB, KSV>::smem(), \
-                 st>>>(__VA_ARGS__);                                                                  \
+#define LWE_LAUNCH_(KER, TB, KSV, TILES, T, KZ, ...)                                                  \
+  KER<TB, KSV><<<dim3(TILES, ((T) + 8 * TB - 1) / (8 * TB), KZ), LweTile<TB, KSV>::THREADS,        \
+                 LweTile<TB, KSV>::smem(), st>>>(__VA_ARGS__);                                        \
   ++g_lwe_launches
-#define LWE_GEMM(KER, ROWS_PER_CTA, R, T, ...)                                                        \
+#define LWE_GEMM(KER, ROWS_PER_CTA, R, K, T, ...)                                                     \
   do {                                                                                                \
     const int _tiles = ((R) + (ROWS_PER_CTA)-1) / (ROWS_PER_CTA);                                     \
     const int _tbw = pick_tbw(_tiles, (T));                                                           \
-    const int _ks = pick_ks(_tiles * (((T) + 8 * _tbw - 1) / (8 * _tbw)));                            \
+    const int _ctas = _tiles * (((T) + 8 * _tbw - 1) / (8 * _tbw));                                   \
+    const int _ks = pick_ks(_ctas);                                                                   \
+    const int _kz = pick_ksplit(_ctas, (K), _tbw);                                                    \
     switch (_tbw * 8 + _ks) {                                                                         \
-      case 65: LWE_LAUNCH_(KER, 8, 1, _tiles, T, __VA_ARGS__); break;                                 \
-      case 66: LWE_LAUNCH_(KER, 8, 2, _tiles, T, __VA_ARGS__); break;                                 \
-      case 68: LWE_LAUNCH_(KER, 8, 4, _tiles, T, __VA_ARGS__); break;                                 \
-      case 33: LWE_LAUNCH_(KER, 4, 1, _tiles, T, __VA_ARGS__); break;                                 \
-      case 34: LWE_LAUNCH_(KER, 4, 2, _tiles, T, __VA_ARGS__); break;                                 \
-      case 36: LWE_LAUNCH_(KER, 4, 4, _tiles, T, __VA_ARGS__); break;                                 \
-      case 17: LWE_LAUNCH_(KER, 2, 1, _tiles, T, __VA_ARGS__); break;                                 \
-      case 18: LWE_LAUNCH_(KER, 2, 2, _tiles, T, __VA_ARGS__); break;                                 \
-      default: LWE_LAUNCH_(KER, 2, 4, _tiles, T, __VA_ARGS__); break;                                 \
+      case 65: LWE_LAUNCH_(KER, 8, 1, _tiles, T, _kz, __VA_ARGS__); break;                            \
+      case 66: LWE_LAUNCH_(KER, 8, 2, _tiles, T, _kz, __VA_ARGS__); break;                            \
+      case 68: LWE_LAUNCH_(KER, 8, 4, _tiles, T, _kz, __VA_ARGS__); break;                            \
+      case 33: LWE_LAUNCH_(KER, 4, 1, _tiles, T, _kz, __VA_ARGS__); break;                            \
+      case 34: LWE_LAUNCH_(KER, 4, 2, _tiles, T, _kz, __VA_ARGS__); break;                            \
+      case 36: LWE_LAUNCH_(KER, 4, 4, _tiles, T, _kz, __VA_ARGS__); break;                            \
+      case 17: LWE_LAUNCH_(KER, 2, 1, _tiles, T, _kz, __VA_ARGS__); break;                            \
+      case 18: LWE_LAUNCH_(KER, 2, 2, _tiles, T, _kz, __VA_ARGS__); break;                            \
+      default: LWE_LAUNCH_(KER, 2, 4, _tiles, T, _kz, __VA_ARGS__); break;                            \
     }                                                                                                 \
   } while (0)
 #define LWE_GEMM_LM(R, T, ...)                                                                        \
@@ -905,6 +999,7 @@ static cudaError_t gemm_attrs() {
   return e;
 }
 
+template <bool F>
 static void launch_attention_split(const LweArgs& a, const LweHost& h, int T, cudaStream_t st) {
   const int rep = a.m.NH / a.m.NKV;
   int chunk, S;
@@ -912,11 +1007,12 @@ static void launch_attention_split(const LweArgs& a, const LweHost& h, int T, cu
   const dim3 grid(T, a.m.NKV, S);
   const size_t sm = (size_t)2 * kAttnChunk * 64 * 4;
   switch (rep) {
-    case 1: lwe_attn_split<1><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); ++g_lwe_launches; break;
-    case 2: lwe_attn_split<2><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); ++g_lwe_launches; break;
-    case 3: lwe_attn_split<3><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); ++g_lwe_launches; break;
-    default: lwe_attn_split<4><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); ++g_lwe_launches; break;
+    case 1: lwe_attn_split<1, F><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
+    case 2: lwe_attn_split<2, F><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
+    case 3: lwe_attn_split<3, F><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
+    default: lwe_attn_split<4, F><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
   }
+  ++g_lwe_launches;
 }
 
 template <bool F>
@@ -969,32 +1065,36 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
   for (int l = 0; l < nl; ++l) {
     const LayerDev& L = h.layers[l];
     a.layer = l;
-    LWE_GEMM(lwe_gemm_qkv, kGemmRows, md.QKV, T, a, T, l);
+    LWE_GEMM(lwe_gemm_qkv, kGemmRows, md.QKV, md.D, T, a, T, l);
     if (one_per_slot) {
       if (h.attn_split)
-        launch_attention_split(a, h, T, st);
+        launch_attention_split<true>(a, h, T, st);
       else
         launch_attention_t<true>(a, T, st);
     } else {
       lwe_rope_kv<<<dim3(T, md.NKV), 64, 0, st>>>(a, T);
       ++g_lwe_launches;
-      launch_attention_t<false>(a, T, st);
+      // a few tokens (a verify forward) over a long cache: split the positions across CTAs
+      if (T <= kLweSplitAttnRows)
+        launch_attention_split<false>(a, h, T, st);
+      else
+        launch_attention_t<false>(a, T, st);
     }
     // proj + residual; norm2 -> N2 (x3 buffer when folded, else a norm kernel into xh)
     LweArgs n2 = a;
     if (fold) {
       n2.xh = a.xh3;
       n2.xl = a.xl3;
-      LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, T, a, T, L.proj, L.proj_b, md.D, L.norm2, a.xh3, a.xl3, a.ldx);
+      LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.D, T, a, T, L.proj, L.proj_b, md.D, L.norm2, a.xh3, a.xl3, a.ldx);
     } else {
-      LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, T, a, T, L.proj, L.proj_b, md.D, nullptr, nullptr, nullptr, 0);
+      LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.D, T, a, T, L.proj, L.proj_b, md.D, nullptr, nullptr, nullptr, 0);
       lwe_norm_split<<<T, 128, 0, st>>>(a, T, L.norm2, nullptr);
       ++g_lwe_launches;
     }
     if (md.arch == 0)
-      LWE_GEMM(lwe_gemm_w13, 32, md.FF, T, n2, T, l);
+      LWE_GEMM(lwe_gemm_w13, 32, md.FF, md.D, T, n2, T, l);
     else
-      LWE_GEMM(lwe_gemm_fc, kGemmRows, md.FF, T, n2, T, l);
+      LWE_GEMM(lwe_gemm_fc, kGemmRows, md.FF, md.D, T, n2, T, l);
     LweArgs b = a;  // w2 / mlp.proj read the second activation buffer
     b.xh = a.xh2;
     b.xl = a.xl2;
@@ -1002,9 +1102,9 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
     // w2 + residual; the next layer's norm1 -> xh
     const float* ng = l + 1 < nl ? h.layers[l + 1].norm1 : nullptr;
     if (fold) {
-      LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, T, b, T, L.w2, L.mproj_b, md.FF, ng, a.xh, a.xl, a.ldx);
+      LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.FF, T, b, T, L.w2, L.mproj_b, md.FF, ng, a.xh, a.xl, a.ldx);
     } else {
-      LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, T, b, T, L.w2, L.mproj_b, md.FF, nullptr, nullptr, nullptr, 0);
+      LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.FF, T, b, T, L.w2, L.mproj_b, md.FF, nullptr, nullptr, nullptr, 0);
       if (ng) {
         lwe_norm_split<<<T, 128, 0, st>>>(a, T, ng, nullptr);
         ++g_lwe_launches;
@@ -1223,6 +1323,161 @@ size_t lwe_argmax_pen_smem(int V, int max_new) { return (size_t)2 * ((V + 31) / 
 void lwe_penalised_argmax(const float* logits, int V, int T, const int32_t* out_ids, const int32_t* counts, int max_new,
                           int32_t* amax, cudaStream_t st) {
   lwe_argmax_pen<<<T, 256, lwe_argmax_pen_smem(V, max_new), st>>>(logits, V, T, out_ids, counts, max_new, amax);
+  ++g_lwe_launches;
+}
+
+
+// ---------------------------------------------------------------------------------------------
+// Prompt-lookup speculation on the token-batch engine (engine/webgpu.js:1239-1270 with lookupDraft
+// engine/webgpu.js:846-865): every iteration is one CUDA graph replay of prepare (draft lookup over
+// the device-resident history, verify rows) -> forward over spec_k + 1 rows -> accept.  The loop
+// state lives in device memory (SpecState words); once the loop is finished the replays are no-ops.
+// ---------------------------------------------------------------------------------------------
+enum SpecWord { SP_HLEN = 0, SP_GEN, SP_CACHE, SP_DONE, SP_HITS, SP_TRIES, SP_FWD, SP_TOK, SP_DL, SP_STOP, SP_POS0 };
+
+// State after the prefill: history = prompt + first id (already in out_ids[0]).
+__global__ void k_spec_init(int32_t* sp, const int32_t* ids, int n, const int32_t* out_ids, int max_new, int eos,
+                            int kv_len, int prefill_forwards) {
+  int32_t* hist = sp + kSpecHist;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) hist[i] = ids[i];
+  if (threadIdx.x == 0) {
+    const int tok = out_ids[0];
+    hist[n] = tok;
+    sp[SP_HLEN] = n + 1;
+    sp[SP_GEN] = 1;
+    sp[SP_CACHE] = n < kv_len - 1 ? n : kv_len - 1;
+    sp[SP_TOK] = tok;
+    sp[SP_HITS] = 0;
+    sp[SP_TRIES] = 0;
+    sp[SP_FWD] = prefill_forwards;
+    sp[SP_STOP] = tok == eos ? 0 : 1;
+    sp[SP_DONE] = tok == eos ? 1 : 0;
+    sp[SP_DL] = 0;
+  }
+}
+
+// Draft lookup and the verify rows: row 0 = the last id at position cache, rows 1..dl = the draft;
+// rows dl+1..T-1 repeat row dl (same id, same position: identical K/V writes, logits unused).
+__global__ void k_spec_prepare(const __grid_constant__ LweArgs a, int32_t* sp, int spec_k, int ngram, int max_new,
+                               int T, int slot) {
+  __shared__ int best;
+  __shared__ int sdone;
+  const int32_t* hist = sp + kSpecHist;
+  const int kv_len = a.m.kv_len;
+  const int hlen = sp[SP_HLEN], gen = sp[SP_GEN], cache = sp[SP_CACHE];
+  if (threadIdx.x == 0) {
+    best = -1;
+    int d = sp[SP_DONE];
+    if (!d && (gen >= max_new || cache >= kv_len - 1)) d = 1;  // engine/webgpu.js:1239
+    sdone = d;
+    if (d) sp[SP_DONE] = 1;
+  }
+  __syncthreads();
+  if (sdone) return;
+  // latest earlier occurrence of the last `ngram` ids (engine/webgpu.js:846-865)
+  if (hlen >= ngram + 1) {
+    const int limit = hlen - ngram;
+    int b = -1;
+    for (int i = threadIdx.x; i < limit; i += blockDim.x) {
+      bool ok = true;
+      for (int j = 0; j < ngram; ++j)
+        if (hist[i + j] != hist[hlen - ngram + j]) {
+          ok = false;
+          break;
+        }
+      if (ok) b = i;
+    }
+    if (b >= 0) atomicMax(&best, b);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int i = best;
+    int dl = 0;
+    int32_t* draft = sp + kSpecDraft;
+    if (i >= 0)
+      for (int t = 0; t < spec_k && i + ngram + t < hlen; ++t) draft[dl++] = hist[i + ngram + t];
+    if (cache + dl > kv_len - 1) dl = kv_len - 1 - cache;  // verify rows stay inside the cache
+    sp[SP_DL] = dl;
+    sp[SP_POS0] = cache;
+    sp[SP_TRIES] += 1;
+    for (int r = 0; r < T; ++r) {
+      const int e = r < dl ? r : dl;
+      a.tok[r] = e == 0 ? sp[SP_TOK] : draft[e - 1];
+      a.pos[r] = cache + e;
+      a.slot[r] = slot;
+      a.lm_src[r] = r;
+    }
+  }
+}
+
+// engine/webgpu.js:1249-1268: accept r[0], then r[k+1] while r[k] == draft[k].
+__global__ void k_spec_accept(const int32_t* amax, int32_t* sp, int32_t* out_ids, int max_new, int eos) {
+  if (threadIdx.x != 0 || sp[SP_DONE]) return;
+  int32_t* hist = sp + kSpecHist;
+  const int32_t* draft = sp + kSpecDraft;
+  const int dl = sp[SP_DL], pos0 = sp[SP_POS0];
+  int gen = sp[SP_GEN], hlen = sp[SP_HLEN], hits = sp[SP_HITS];
+  const int r0 = amax[0];
+  out_ids[gen++] = r0;
+  hist[hlen++] = r0;
+  int cache = pos0 + 1, tok = r0;
+  if (r0 != eos && dl > 0) {
+    for (int k = 0; k < dl; ++k) {
+      if (amax[k] != draft[k]) break;
+      if (gen >= max_new) break;
+      const int nxt = amax[k + 1];
+      ++hits;
+      out_ids[gen++] = nxt;
+      hist[hlen++] = nxt;
+      cache = pos0 + 2 + k;
+      tok = nxt;
+      if (nxt == eos) break;
+    }
+  }
+  sp[SP_GEN] = gen;
+  sp[SP_HLEN] = hlen;
+  sp[SP_HITS] = hits;
+  sp[SP_CACHE] = cache;
+  sp[SP_TOK] = tok;
+  sp[SP_FWD] += 1;
+  if (tok == eos) {
+    sp[SP_STOP] = 0;
+    sp[SP_DONE] = 1;
+  }
+}
+
+// Status words of the generate call from the loop state.
+__global__ void k_spec_finish(const int32_t* sp, int32_t* status) {
+  status[ST_NGEN] = sp[SP_GEN];
+  status[ST_STOP] = sp[SP_STOP];
+  status[ST_HITS] = sp[SP_HITS];
+  status[ST_TRIES] = sp[SP_TRIES];
+  status[ST_FORWARDS] = sp[SP_FWD];
+  const uint64_t t = globaltimer();
+  status[ST_TEND] = (int32_t)(uint32_t)t;
+  status[ST_TEND + 1] = (int32_t)(uint32_t)(t >> 32);
+}
+
+void lwe_spec_init(int32_t* sp, const int32_t* ids, int n, const int32_t* out_ids, int max_new, int eos, int kv_len,
+                   int prefill_forwards, cudaStream_t st) {
+  k_spec_init<<<1, 256, 0, st>>>(sp, ids, n, out_ids, max_new, eos, kv_len, prefill_forwards);
+  ++g_lwe_launches;
+}
+cudaError_t lwe_spec_iteration(LweArgs a, const LweHost& h, int32_t* sp, int32_t* out_ids, int spec_k, int ngram,
+                               int max_new, int eos, int slot, cudaStream_t st) {
+  const int T = spec_k + 1;
+  k_spec_prepare<<<1, 256, 0, st>>>(a, sp, spec_k, ngram, max_new, T, slot);
+  ++g_lwe_launches;
+  LweArgs f = a;
+  f.skip = sp + SP_DONE;
+  const cudaError_t e = lwe_forward(f, h, T, T, false, nullptr, false, st);
+  if (e != cudaSuccess) return e;
+  k_spec_accept<<<1, 32, 0, st>>>(a.amax, sp, out_ids, max_new, eos);
+  ++g_lwe_launches;
+  return cudaGetLastError();
+}
+void lwe_spec_finish(const int32_t* sp, int32_t* status, cudaStream_t st) {
+  k_spec_finish<<<1, 1, 0, st>>>(sp, status);
   ++g_lwe_launches;
 }
 

@@ -38,7 +38,13 @@ struct LweArgs {
   int32_t* amax;          // [lm_cap] argmax per lm row
   int32_t* lm_src;        // [lm_cap] token index of each lm row
   int* err;               // device error flag: 2 = a token id out of range
+  const int* skip;        // when set and *skip != 0 every kernel of the forward returns at once
+  float* skws;            // split-K partial tiles [kLweSplitKBytes]
+  int* skctr;             // [kLweSplitKTiles] zeroed split-K tile counters
 };
+constexpr size_t kLweSplitKBytes = size_t(8) << 20;
+constexpr int kLweSplitAttnRows = 16;  // forwards of at most this many tokens use the position-split attention
+constexpr int kLweSplitKTiles = 16384;
 
 // Host-side copies of the per-layer descriptors the launches pass by value.
 struct LweHost {
@@ -63,6 +69,17 @@ cudaError_t lwe_setup(int kv_len);
 void lwe_fill(LweArgs a, const int32_t* ids, int n, int slot, int pos0, int lm_each, cudaStream_t st);
 void lwe_first(LweArgs a, int32_t* out_ids, int32_t* status, int eos, int forwards, cudaStream_t st);
 void lwe_mark_time(int32_t* status, int idx, cudaStream_t st);
+// Prompt-lookup speculation: device loop state (int32 words), draft [kSpecDraft, +16) and history
+// [kSpecHist, +kv_len + 64).  The done word is SpecWord 3.
+constexpr int kSpecDraft = 16;
+constexpr int kSpecHist = 64;
+constexpr int kSpecMaxK = 15;
+constexpr int kSpecDoneWord = 3;
+void lwe_spec_init(int32_t* sp, const int32_t* ids, int n, const int32_t* out_ids, int max_new, int eos, int kv_len,
+                   int prefill_forwards, cudaStream_t st);
+cudaError_t lwe_spec_iteration(LweArgs a, const LweHost& h, int32_t* sp, int32_t* out_ids, int spec_k, int ngram,
+                               int max_new, int eos, int slot, cudaStream_t st);
+void lwe_spec_finish(const int32_t* sp, int32_t* status, cudaStream_t st);
 // Kernel launches issued so far by the calling thread through these functions.
 long lwe_launch_count();
 // Replicated multi-sequence decode

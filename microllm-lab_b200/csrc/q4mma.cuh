@@ -160,8 +160,11 @@ __device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __r
   const int lt = KS > 1 ? (int)(threadIdx.x & 127) : (int)threadIdx.x;
   const int lane = lt & 31, warp = lt >> 5;
   const int gid = lane >> 2, t = lane & 3;
-  const int ng = K >> 5;
-  const int niter = (ng - wg + KS - 1) / KS;  // k groups of this warp group: wg, wg + KS, ...
+  // k groups of this CTA: split blockIdx.z of gridDim.z (split-K across CTAs; 1 split normally)
+  const int ngt = K >> 5;
+  const int gbeg = (int)(((long)ngt * blockIdx.z) / gridDim.z), gend = (int)(((long)ngt * (blockIdx.z + 1)) / gridDim.z);
+  const int ng = gend - gbeg;
+  const int niter = ng > wg ? (ng - wg + KS - 1) / KS : 0;  // k groups of this warp group: wg, wg + KS, ...
   // stage layout (per warp group)
   uint8_t* w_s = smem + (size_t)wg * kGroupBytes;                        // [kStages][64][16]
   float* s_s = reinterpret_cast<float*>(w_s + kStages * kGemmRows * 16);  // [kStages][64]
@@ -172,7 +175,7 @@ __device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __r
     else asm volatile("bar.sync %0, %1;" ::"r"(1 + wg), "r"(kGemmThreads) : "memory");
   };
   auto issue = [&](int i, int st) {
-    const int g = wg + i * KS;
+    const int g = gbeg + wg + i * KS;
     // weights: 64 rows x 16 B, scales: 64 floats (16 x 16 B), activations: BT rows x 64 B x 2
     if (lt < kGemmRows) {
       cp_async16(w_s + (st * kGemmRows + lt) * 16, rows.wrow(lt) + g * 16, rows.valid(lt));

@@ -165,3 +165,26 @@ def test_persistent_prefill_path_still_matches(cuda_ok, name):
     g = eng.forwardPrompt(ids)
     assert np.abs(g - om.forward_prompt(ids)).max() <= LOGIT_TOL
     eng.destroy()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("env", [{}, {"MLLM_LWE_GRAPH": "0"}, {"MLLM_LWE_PREFILL": "0"}])
+def test_speculation_paths(cuda_ok, env):
+    """Prompt-lookup speculation (engine/webgpu.js:1164-1282) on the token-batch engine (graph replays,
+    plain launches) and on the persistent kernel: ids, specHits and specTries equal the oracle's."""
+    data = _data("tiny-llama")
+    eng = _engine(data, env=env)
+    om = O.OracleModel(data)
+    ids = pkg().copy_span_prompt(96, 512, 83)
+    for k in (2, 4):
+        g = eng.generate(ids, maxNewTokens=40, eosId=-1, specK=k, ngram=3)
+        r = om.generate_spec(ids, 40, eos=-1, spec_k=k, ngram=3)
+        assert g["generatedIds"] == r["generatedIds"]
+        assert (g["specHits"], g["specTries"]) == (r["specHits"], r["specTries"])
+    # EOS inside an accepted run stops the stream there
+    full = om.generate(ids, 40, eos=-1)["generatedIds"]
+    eos = full[9]
+    g = eng.generate(ids, maxNewTokens=40, eosId=eos, specK=4, ngram=3)
+    r = om.generate_spec(ids, 40, eos=eos, spec_k=4, ngram=3)
+    assert g["generatedIds"] == r["generatedIds"] and g["stopReason"] == r["stopReason"] == "eos"
+    eng.destroy()
