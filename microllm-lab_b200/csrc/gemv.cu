@@ -292,7 +292,8 @@ __global__ void __launch_bounds__(256, 1) gemv_q4_bulk_kernel(const uint8_t* __r
 #pragma unroll
     for (int p = 0; p < NP; ++p) acc[p][0] = acc[p][1] = 0.f;
     if (tr < nr) {
-      for (int g = 0; g < ng; ++g) {
+#pragma unroll 3
+      for (int g = 0; g < ng; ++g) {  // independent groups: unrolled for overlapping mma chains
         const uint4 qa = *reinterpret_cast<const uint4*>(wa + g * 16);
         const uint4 qb = *reinterpret_cast<const uint4*>(wb + g * 16);
         uint32_t a0[4], a1[4];
