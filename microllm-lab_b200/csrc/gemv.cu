@@ -217,10 +217,14 @@ __global__ void __launch_bounds__(256) gemv_q4_tc_kernel(const uint8_t* __restri
 constexpr int kBulkRows = 128;
 constexpr int kBulkNS = 3;
 
-template <int NP>
-__global__ void __launch_bounds__(256, 1) gemv_q4_bulk_kernel(const uint8_t* __restrict__ W, const float* __restrict__ S,
-                                                              const float* __restrict__ X, float* __restrict__ Y, int R,
-                                                              int K, int M, int* err) {
+// KSL warps share each 16-row tile (k groups interleaved) for more warps in flight per SM.
+template <int NP, int KSL>
+__global__ void __launch_bounds__(256 * KSL, 1) gemv_q4_bulk_kernel(const uint8_t* __restrict__ W,
+                                                                    const float* __restrict__ S,
+                                                                    const float* __restrict__ X,
+                                                                    float* __restrict__ Y, int R, int K, int M,
+                                                                    int* err) {
+  __shared__ float red[8 * KSL][NP][2][32];
   extern __shared__ __align__(128) unsigned char sm[];
   const int nkb = K >> 4, ng = K >> 5, half_k = K >> 1;
   const size_t wbytes = (size_t)kBulkRows * half_k, sbytes = (size_t)kBulkRows * ng * 4;
@@ -263,7 +267,8 @@ __global__ void __launch_bounds__(256, 1) gemv_q4_bulk_kernel(const uint8_t* __r
     const __half2 b0 = __halves2half2(v[0], v[1]), b1 = __halves2half2(v[2], v[3]);
     bfrag[e] = make_uint2(*reinterpret_cast<const uint32_t*>(&b0), *reinterpret_cast<const uint32_t*>(&b1));
   }
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
+  const int warp = wid / KSL, ksl = wid % KSL;  // tile of the stage, share of its k groups
   bool ok = true;
   for (int j = 0; j < my_n; ++j) {
     const int r0 = ((int)blockIdx.x + j * (int)gridDim.x) * kBulkRows;
@@ -293,7 +298,7 @@ __global__ void __launch_bounds__(256, 1) gemv_q4_bulk_kernel(const uint8_t* __r
     for (int p = 0; p < NP; ++p) acc[p][0] = acc[p][1] = 0.f;
     if (tr < nr) {
 #pragma unroll 3
-      for (int g = 0; g < ng; ++g) {  // independent groups: unrolled for overlapping mma chains
+      for (int g = ksl; g < ng; g += KSL) {  // independent groups: unrolled for overlapping mma chains
         const uint4 qa = *reinterpret_cast<const uint4*>(wa + g * 16);
         const uint4 qb = *reinterpret_cast<const uint4*>(wb + g * 16);
         uint32_t a0[4], a1[4];
@@ -317,23 +322,35 @@ __global__ void __launch_bounds__(256, 1) gemv_q4_bulk_kernel(const uint8_t* __r
           acc[p][1] = fmaf(s1, d[2] + d[3], acc[p][1]);
         }
       }
-      if (ok) {
+    }
+    if (KSL > 1) {
 #pragma unroll
-        for (int p = 0; p < NP; ++p) {
-          const int m = 4 * p + t;
-          if (m < M) {
-            if (tr + gid < nr) Y[(size_t)m * R + r0 + tr + gid] = acc[p][0];
-            if (tr + gid + 8 < nr) Y[(size_t)m * R + r0 + tr + gid + 8] = acc[p][1];
-          }
+      for (int p = 0; p < NP; ++p) {
+        red[wid][p][0][lane] = acc[p][0];
+        red[wid][p][1][lane] = acc[p][1];
+      }
+    }
+    __syncthreads();  // every warp is done with this stage's buffer (and its partial sums are out)
+    if (ok && ksl == 0 && tr < nr) {
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        for (int w = 1; w < KSL; ++w) {
+          acc[p][0] += red[wid + w][p][0][lane];
+          acc[p][1] += red[wid + w][p][1][lane];
+        }
+        const int m = 4 * p + t;
+        if (m < M) {
+          if (tr + gid < nr) Y[(size_t)m * R + r0 + tr + gid] = acc[p][0];
+          if (tr + gid + 8 < nr) Y[(size_t)m * R + r0 + tr + gid + 8] = acc[p][1];
         }
       }
     }
-    __syncthreads();  // every warp is done with this stage's buffer
+    if (KSL > 1) __syncthreads();  // red is reused by the next stage
     if (threadIdx.x == 0 && j + kBulkNS < my_n && stage_rows(j + kBulkNS) == kBulkRows) issue(j + kBulkNS);
   }
 }
 
-template <int NP>
+template <int NP, int KSL = 2>
 static cudaError_t run_gemv_bulk(const uint8_t* W, const float* S, const float* X, float* Y, int R, int K, int M,
                                  int* err, cudaStream_t st) {
   int dev = 0, sms = 148;
@@ -342,10 +359,11 @@ static cudaError_t run_gemv_bulk(const uint8_t* W, const float* S, const float* 
   const size_t wbytes = (size_t)kBulkRows * (K / 2), sbytes = (size_t)kBulkRows * (K / 32) * 4;
   const size_t stage_bytes = (wbytes + sbytes + 127) & ~(size_t)127;
   const size_t smem = kBulkNS * stage_bytes + (size_t)NP * (K / 16) * 32 * sizeof(uint2);
-  const cudaError_t e = cudaFuncSetAttribute(gemv_q4_bulk_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const cudaError_t e =
+      cudaFuncSetAttribute(gemv_q4_bulk_kernel<NP, KSL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int nst = (R + kBulkRows - 1) / kBulkRows;
-  gemv_q4_bulk_kernel<NP><<<std::min(nst, sms), 256, smem, st>>>(W, S, X, Y, R, K, M, err);
+  gemv_q4_bulk_kernel<NP, KSL><<<std::min(nst, sms), 256 * KSL, smem, st>>>(W, S, X, Y, R, K, M, err);
   return cudaGetLastError();
 }
 
