@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 
 #include "device_common.cuh"
 #include "engine.cuh"
@@ -32,10 +34,10 @@ template <int TBW, int KSPLIT>
 struct LweTile {
   static constexpr int BT = 8 * TBW;
   static constexpr int KS = KSPLIT;
-  static constexpr int NS = KS == 1 ? (TBW == 8 ? 4 : (TBW == 4 ? 6 : 8))
-                                    : (KS == 2 ? (TBW == 8 ? 3 : (TBW == 4 ? 4 : 6)) : (TBW == 8 ? 2 : (TBW == 4 ? 3 : 4)));
+  static constexpr int GPS = KS == 1 ? 4 : 2;  // k groups per pipeline stage
+  static constexpr int NS = (TBW == 8 && KS != 2) ? 2 : 3;
   static constexpr int THREADS = kGemmThreads * KS;
-  static constexpr size_t smem() { return q4_gemm_smem_bytes<TBW, NS, KS>(); }
+  static constexpr size_t smem() { return q4_gemm_smem_bytes<TBW, NS, KS, GPS>(); }
 };
 
 // 1 / RMS of token t from the per-row-tile partial sums of squares the previous GEMM left in a.ss
@@ -287,7 +289,7 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_qkv(const 
   const int r0 = blockIdx.x * kGemmRows;
   const RowsLinear rows{reinterpret_cast<const uint8_t*>(L.qkv.w), L.qkv.s, R, r0, K >> 1, K >> 5};
   float acc[TBW][4];
-  q4_gemm_core<TBW, C::NS, C::KS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  q4_gemm_core<TBW, C::NS, C::KS, decltype(rows), C::GPS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
   if (!lwe_splitk<TBW>(a, acc)) return;
   lwe_tile_epi<TBW>(acc, r0, t0, R, T, [&](int r, int t, float v) {
     v *= sinv[t - t0];
@@ -665,7 +667,7 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_resid(cons
   float* x = a.x;
   const RowsLinear rows{reinterpret_cast<const uint8_t*>(w.w), w.s, R, r0, K >> 1, K >> 5};
   float acc[TBW][4];
-  q4_gemm_core<TBW, C::NS, C::KS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  q4_gemm_core<TBW, C::NS, C::KS, decltype(rows), C::GPS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
   if (!lwe_splitk<TBW>(a, acc)) return;
   if (threadIdx.x < kGemmThreads) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tq = lane & 3;
@@ -735,7 +737,7 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_w13(const 
                         L.w3.s, FF, (int)blockIdx.x * 32, K >> 1, K >> 5};
   float acc[TBW][4];
   const int t0 = blockIdx.y * C::BT;
-  q4_gemm_core<TBW, C::NS, C::KS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  q4_gemm_core<TBW, C::NS, C::KS, decltype(rows), C::GPS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
   if (!lwe_splitk<TBW>(a, acc)) return;
   if (threadIdx.x >= kGemmThreads) return;  // partial sums were added into the first warp group
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
@@ -769,7 +771,7 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_fc(const _
   const int r0 = blockIdx.x * kGemmRows, t0 = blockIdx.y * C::BT;
   const RowsLinear rows{reinterpret_cast<const uint8_t*>(L.w1.w), L.w1.s, FF, r0, K >> 1, K >> 5};
   float acc[TBW][4];
-  q4_gemm_core<TBW, C::NS, C::KS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  q4_gemm_core<TBW, C::NS, C::KS, decltype(rows), C::GPS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
   if (!lwe_splitk<TBW>(a, acc)) return;
   lwe_tile_epi<TBW>(acc, r0, t0, FF, T, [&](int r, int t, float v) {
     if (bias) v += bias[r];
@@ -791,7 +793,7 @@ __global__ void __launch_bounds__(kGemmThreads) lwe_gemm_lm(const __grid_constan
   const int r0 = blockIdx.x * kGemmRows, t0 = blockIdx.y * kLweBT;
   float acc[TBW][4];
   const RowsLinear rows{reinterpret_cast<const uint8_t*>(a.m.lm.w), a.m.lm.s, V, r0, K >> 1, K >> 5};
-  q4_gemm_core<TBW, C::NS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  q4_gemm_core<TBW, C::NS, 1, decltype(rows), C::GPS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
   const int ra = r0 + warp * 16 + gid, rb = ra + 8;
   __syncthreads();  // the pipeline buffers are reused below
@@ -942,9 +944,19 @@ static int pick_ksplit(int ctas, int K, int TBW) {
   return z;
 }
 
+// MLLM_LWE_DEBUG=1: report the first failing launch on stderr (kernel, tile, k split, grid).
+static void lwe_debug_check(const char* what, int tb, int ks, int tiles, int T, int kz, size_t smem) {
+  static const bool on = getenv("MLLM_LWE_DEBUG") != nullptr;
+  if (!on) return;
+  const cudaError_t e = cudaPeekAtLastError();
+  if (e != cudaSuccess)
+    fprintf(stderr, "lwe launch %s<%d,%d> tiles %d T %d kz %d smem %zu: %s\n", what, tb, ks, tiles, T, kz, smem,
+            cudaGetErrorString(e));
+}
 #define LWE_LAUNCH_(KER, TB, KSV, TILES, T, KZ, ...)                                                  \
   KER<TB, KSV><<<dim3(TILES, ((T) + 8 * TB - 1) / (8 * TB), KZ), LweTile<TB, KSV>::THREADS,        \
                  LweTile<TB, KSV>::smem(), st>>>(__VA_ARGS__);                                        \
+  lwe_debug_check(#KER, TB, KSV, TILES, T, KZ, LweTile<TB, KSV>::smem());                              \
   ++g_lwe_launches
 #define LWE_GEMM(KER, ROWS_PER_CTA, R, K, T, ...)                                                     \
   do {                                                                                                \
@@ -978,8 +990,8 @@ static int pick_ksplit(int ctas, int K, int TBW) {
 
 template <class F>
 static cudaError_t smem_attr(F* f, size_t bytes) {
-  return bytes > 48 * 1024 ? cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes)
-                           : cudaSuccess;
+  // always set: the kernels' static shared memory counts against the 48 KB default as well
+  return cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 template <int TBW, int KS>
 static cudaError_t gemm_attrs_ks() {
@@ -1044,7 +1056,6 @@ cudaError_t lwe_setup(int kv_len) {
   if (e == cudaSuccess) e = gemm_attrs<8>();
   if (e != cudaSuccess) return e;
   const int need = (int)attention_smem(kLweMaxRep, kv_len);
-  if (need <= 48 * 1024) return cudaSuccess;
   e = attention_attr<false>(need);
   return e == cudaSuccess ? attention_attr<true>(need) : e;
 }

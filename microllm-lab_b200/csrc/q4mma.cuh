@@ -108,7 +108,9 @@ struct RowsPaired {
   }
 };
 
-template <int TBW, int NS = kStages, int KS = 1, class Rows>
+template <int TBW, int GPS>
+struct GemmStage;
+template <int TBW, int NS, int KS, class Rows, int GPS = 1>
 __device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __restrict__ Xhi,
                                              const __half* __restrict__ Xlo, int ldx, int K, int T, int t0,
                                              unsigned char* smem, float (&acc)[TBW][4]);
@@ -119,7 +121,7 @@ __device__ __forceinline__ void q4_gemm_rows(const Rows& rows, const __half* __r
                                              const __half* __restrict__ Xlo, int ldx, int K, int T, int t0,
                                              unsigned char* smem, Epi epi) {
   float acc[TBW][4];
-  q4_gemm_core<TBW, NS, KS>(rows, Xhi, Xlo, ldx, K, T, t0, smem, acc);
+  q4_gemm_core<TBW, NS, KS, Rows, 1>(rows, Xhi, Xlo, ldx, K, T, t0, smem, acc);
   if (KS > 1 && threadIdx.x >= kGemmThreads) return;  // the k-split partial sums are in group 0
   // lane (gid, t) owns tile rows gid, gid+8 of its warp and tokens 2t, 2t+1 of each 8-token block
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
@@ -145,17 +147,30 @@ __device__ __forceinline__ void q4_gemm_tile(const uint8_t* __restrict__ W, cons
 
 // Main loop: `rows` maps tile rows 0..63 to weight rows; acc[b][0..3] of lane (gid, t) hold tile rows
 // (16 warp + gid, same, +8, +8) x tokens (t0 + 8b + 2t, +1, 2t, +1).  Ends with all copies drained.
-// KS > 1 splits the k groups over KS groups of 4 warps (group w takes k groups w, w + KS, ...), each
-// with its own pipeline buffers and a named barrier; the partial sums are added, in group order, into
-// group 0's accumulators (threads 0..127), which then hold the result.
-template <int TBW, int NS, int KS, class Rows>
+// A pipeline stage carries GPS consecutive 32-wide k groups (one sync per stage).  KS > 1 splits the
+// stages over KS groups of 4 warps (warp group w takes stages w, w + KS, ...), each with its own
+// pipeline buffers and a named barrier; the partial sums are added, in group order, into group 0's
+// accumulators (threads 0..127), which then hold the result.  Padded groups past the end load zero
+// activations and scales, so they add nothing.
+template <int TBW, int GPS>
+struct GemmStage {
+  static constexpr int BT = 8 * TBW;
+  static constexpr int WROW = GPS * 16 + 16;       // bytes per weight row in smem (padded: conflict-free)
+  static constexpr int XROW = GPS * 32 + 8;        // fp16 per token row in smem (padded)
+  static constexpr size_t W = (size_t)kGemmRows * WROW;
+  static constexpr size_t SC = (size_t)kGemmRows * GPS * 4;
+  static constexpr size_t X = (size_t)BT * XROW * 2;  // bytes of one of hi / lo
+  static constexpr size_t bytes = W + SC + 2 * X;
+};
+
+template <int TBW, int NS, int KS, class Rows, int GPS>
 __device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __restrict__ Xhi,
                                              const __half* __restrict__ Xlo, int ldx, int K, int T, int t0,
                                              unsigned char* smem, float (&acc)[TBW][4]) {
+  using SG = GemmStage<TBW, GPS>;
   constexpr int kStages = NS;
-  constexpr int BT = 8 * TBW;  // tokens per CTA
-  constexpr size_t kGroupBytes = (size_t)NS * kGemmRows * 16 + (size_t)NS * kGemmRows * 4 +
-                                 2 * (size_t)NS * BT * kXPad * sizeof(__half);
+  constexpr int BT = SG::BT;
+  constexpr size_t kGroupBytes = (size_t)NS * SG::bytes;
   const int wg = KS > 1 ? (int)(threadIdx.x >> 7) : 0;
   const int lt = KS > 1 ? (int)(threadIdx.x & 127) : (int)threadIdx.x;
   const int lane = lt & 31, warp = lt >> 5;
@@ -163,32 +178,35 @@ __device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __r
   // k groups of this CTA: split blockIdx.z of gridDim.z (split-K across CTAs; 1 split normally)
   const int ngt = K >> 5;
   const int gbeg = (int)(((long)ngt * blockIdx.z) / gridDim.z), gend = (int)(((long)ngt * (blockIdx.z + 1)) / gridDim.z);
-  const int ng = gend - gbeg;
-  const int niter = ng > wg ? (ng - wg + KS - 1) / KS : 0;  // k groups of this warp group: wg, wg + KS, ...
-  // stage layout (per warp group)
-  uint8_t* w_s = smem + (size_t)wg * kGroupBytes;                        // [kStages][64][16]
-  float* s_s = reinterpret_cast<float*>(w_s + kStages * kGemmRows * 16);  // [kStages][64]
-  __half* xh_s = reinterpret_cast<__half*>(s_s + kStages * kGemmRows);    // [kStages][BT][kXPad]
-  __half* xl_s = xh_s + kStages * BT * kXPad;
+  const int nchunk = (gend - gbeg + GPS - 1) / GPS;                   // stages of GPS groups
+  const int niter = nchunk > wg ? (nchunk - wg + KS - 1) / KS : 0;    // stages of this warp group
+  unsigned char* base = smem + (size_t)wg * kGroupBytes;
+  auto w_s = [&](int st) { return base + (size_t)st * SG::bytes; };
+  auto s_s = [&](int st) { return reinterpret_cast<float*>(base + (size_t)st * SG::bytes + SG::W); };
+  auto xh_s = [&](int st) { return reinterpret_cast<__half*>(base + (size_t)st * SG::bytes + SG::W + SG::SC); };
+  auto xl_s = [&](int st) {
+    return reinterpret_cast<__half*>(base + (size_t)st * SG::bytes + SG::W + SG::SC + SG::X);
+  };
   auto sync = [&]() {
     if (KS == 1) __syncthreads();
     else asm volatile("bar.sync %0, %1;" ::"r"(1 + wg), "r"(kGemmThreads) : "memory");
   };
   auto issue = [&](int i, int st) {
-    const int g = gbeg + wg + i * KS;
-    // weights: 64 rows x 16 B, scales: 64 floats (16 x 16 B), activations: BT rows x 64 B x 2
-    if (lt < kGemmRows) {
-      cp_async16(w_s + (st * kGemmRows + lt) * 16, rows.wrow(lt) + g * 16, rows.valid(lt));
-      // scales of a group are one float per row (stride ng)
-      cp_async4(s_s + st * kGemmRows + lt, rows.srow(lt) + g, rows.valid(lt));
+    const int g0 = gbeg + (wg + i * KS) * GPS;
+    // weights: 64 rows x GPS x 16 B; scales: 64 x GPS floats; activations: BT rows x GPS x 64 B x 2
+    for (int j = lt; j < kGemmRows * GPS; j += kGemmThreads) {
+      const int r = j / GPS, q = j % GPS, g = g0 + q;
+      const bool ok = rows.valid(r) && g < gend;
+      cp_async16(w_s(st) + r * SG::WROW + q * 16, rows.wrow(r) + min(g, gend - 1) * 16, ok);
+      cp_async4(s_s(st) + r * GPS + q, rows.srow(r) + min(g, gend - 1), ok);
     }
-    for (int j = lt; j < BT * 4; j += kGemmThreads) {  // 4 x 16 B per token row (32 fp16)
-      const int tk = j >> 2, c = j & 3;
+    for (int j = lt; j < BT * 4 * GPS; j += kGemmThreads) {  // 4 x 16 B per token row and group
+      const int tk = j / (4 * GPS), c = j % (4 * GPS), g = g0 + (c >> 2);
       const int tok = t0 + tk;
-      const bool ok = tok < T;
-      const size_t off = (size_t)min(tok, T - 1) * ldx + g * 32 + c * 8;
-      cp_async16(xh_s + (st * BT + tk) * kXPad + c * 8, Xhi + off, ok);
-      cp_async16(xl_s + (st * BT + tk) * kXPad + c * 8, Xlo + off, ok);
+      const bool ok = tok < T && g < gend;
+      const size_t off = (size_t)min(tok, T - 1) * ldx + min(g, gend - 1) * 32 + (c & 3) * 8;
+      cp_async16(xh_s(st) + tk * SG::XROW + c * 8, Xhi + off, ok);
+      cp_async16(xl_s(st) + tk * SG::XROW + c * 8, Xlo + off, ok);
     }
   };
 #pragma unroll
@@ -210,26 +228,29 @@ __device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __r
       if (in < niter) issue(in, in % kStages);
       cp_async_commit();
     }
-    const uint32_t* wr0 = reinterpret_cast<const uint32_t*>(w_s + (st * kGemmRows + warp * 16 + gid) * 16);
-    const uint32_t* wr1 = reinterpret_cast<const uint32_t*>(w_s + (st * kGemmRows + warp * 16 + gid + 8) * 16);
-    const float sc0 = s_s[st * kGemmRows + warp * 16 + gid];
-    const float sc1 = s_s[st * kGemmRows + warp * 16 + gid + 8];
-    uint32_t a0[4], a1[4];
-    load_a_frag(wr0, wr1, 0, t, a0);
-    load_a_frag(wr0, wr1, 1, t, a1);
 #pragma unroll
-    for (int b = 0; b < TBW; ++b) {
-      const __half* xh = xh_s + (st * BT + b * 8 + gid) * kXPad + 2 * t;
-      const __half* xl = xl_s + (st * BT + b * 8 + gid) * kXPad + 2 * t;
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      mma16816(d, a0, *reinterpret_cast<const uint32_t*>(xh), *reinterpret_cast<const uint32_t*>(xh + 8));
-      mma16816(d, a0, *reinterpret_cast<const uint32_t*>(xl), *reinterpret_cast<const uint32_t*>(xl + 8));
-      mma16816(d, a1, *reinterpret_cast<const uint32_t*>(xh + 16), *reinterpret_cast<const uint32_t*>(xh + 24));
-      mma16816(d, a1, *reinterpret_cast<const uint32_t*>(xl + 16), *reinterpret_cast<const uint32_t*>(xl + 24));
-      acc[b][0] = fmaf(sc0, d[0], acc[b][0]);
-      acc[b][1] = fmaf(sc0, d[1], acc[b][1]);
-      acc[b][2] = fmaf(sc1, d[2], acc[b][2]);
-      acc[b][3] = fmaf(sc1, d[3], acc[b][3]);
+    for (int q = 0; q < GPS; ++q) {
+      const uint32_t* wr0 = reinterpret_cast<const uint32_t*>(w_s(st) + (warp * 16 + gid) * SG::WROW + q * 16);
+      const uint32_t* wr1 = reinterpret_cast<const uint32_t*>(w_s(st) + (warp * 16 + gid + 8) * SG::WROW + q * 16);
+      const float sc0 = s_s(st)[(warp * 16 + gid) * GPS + q];
+      const float sc1 = s_s(st)[(warp * 16 + gid + 8) * GPS + q];
+      uint32_t a0[4], a1[4];
+      load_a_frag(wr0, wr1, 0, t, a0);
+      load_a_frag(wr0, wr1, 1, t, a1);
+#pragma unroll
+      for (int b = 0; b < TBW; ++b) {
+        const __half* xh = xh_s(st) + (b * 8 + gid) * SG::XROW + q * 32 + 2 * t;
+        const __half* xl = xl_s(st) + (b * 8 + gid) * SG::XROW + q * 32 + 2 * t;
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(d, a0, *reinterpret_cast<const uint32_t*>(xh), *reinterpret_cast<const uint32_t*>(xh + 8));
+        mma16816(d, a0, *reinterpret_cast<const uint32_t*>(xl), *reinterpret_cast<const uint32_t*>(xl + 8));
+        mma16816(d, a1, *reinterpret_cast<const uint32_t*>(xh + 16), *reinterpret_cast<const uint32_t*>(xh + 24));
+        mma16816(d, a1, *reinterpret_cast<const uint32_t*>(xl + 16), *reinterpret_cast<const uint32_t*>(xl + 24));
+        acc[b][0] = fmaf(sc0, d[0], acc[b][0]);
+        acc[b][1] = fmaf(sc0, d[1], acc[b][1]);
+        acc[b][2] = fmaf(sc1, d[2], acc[b][2]);
+        acc[b][3] = fmaf(sc1, d[3], acc[b][3]);
+      }
     }
   }
   cp_async_wait<0>();
@@ -253,10 +274,9 @@ __device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __r
   }
 }
 
-template <int TBW, int NS = kStages, int KS = 1>
+template <int TBW, int NS = kStages, int KS = 1, int GPS = 1>
 constexpr size_t q4_gemm_smem_bytes() {
-  return (size_t)KS * ((size_t)NS * kGemmRows * 16 + (size_t)NS * kGemmRows * 4 +
-                       2 * (size_t)NS * (8 * TBW) * kXPad * sizeof(__half));
+  return (size_t)KS * NS * GemmStage<TBW, GPS>::bytes;
 }
 
 }  // namespace mllm
