@@ -30,12 +30,13 @@ long lwe_launch_count() { return g_lwe_launches; }
 // still fill the GPU, and the k-pipeline is deeper for the smaller token tiles (all under 48 KB).
 // The k groups may also be split over KS groups of 4 warps inside the CTA (more warps in flight per
 // SM when a GEMM has few CTAs); the pipeline is deeper for the smaller tiles (all under 100 KB).
-template <int TBW, int KSPLIT>
+template <int TBW, int KSPLIT, bool LM = false>
 struct LweTile {
   static constexpr int BT = 8 * TBW;
   static constexpr int KS = KSPLIT;
-  static constexpr int GPS = KS == 1 ? 4 : 2;  // k groups per pipeline stage
-  static constexpr int NS = (TBW == 8 && KS != 2) ? 2 : 3;
+  // k groups per pipeline stage; the lm_head GEMM (thousands of CTAs) keeps small stages for occupancy
+  static constexpr int GPS = LM ? 1 : (KS == 1 ? 4 : 2);
+  static constexpr int NS = LM ? 4 : ((TBW == 8 && KS != 2) ? 2 : 3);
   static constexpr int THREADS = kGemmThreads * KS;
   static constexpr size_t smem() { return q4_gemm_smem_bytes<TBW, NS, KS, GPS>(); }
 };
@@ -337,8 +338,10 @@ __global__ void lwe_rope_kv(const __grid_constant__ LweArgs a, int T) {
 // FUSED (every token of the launch in its own slot, as in a batched decode step): the CTA also applies
 // RoPE to its q heads and k (engine/infer.js:436-458) and writes the token's K/V row into the cache
 // (engine/infer.js:459-464) before reading the cache; otherwise lwe_rope_kv ran first.
+constexpr int kAttnThreads = 128;
+constexpr int kAttnLanes = kAttnThreads / 16;  // position lanes of the P.V pass
 template <int REP, bool FUSED>
-__global__ void __launch_bounds__(128) lwe_attention(const __grid_constant__ LweArgs a, int T) {
+__global__ void __launch_bounds__(kAttnThreads) lwe_attention(const __grid_constant__ LweArgs a, int T) {
   if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(16) float asm_[];
   const int t = blockIdx.x, g = blockIdx.y;
@@ -348,14 +351,14 @@ __global__ void __launch_bounds__(128) lwe_attention(const __grid_constant__ Lwe
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float* qs = asm_;                  // [REP][64]
   float* sc = qs + REP * 64;         // [REP][kv_len]
-  float* red = sc + REP * kvs;       // [8][REP][64]
+  float* red = sc + REP * kvs;       // [kAttnLanes][REP][64]
   __shared__ float inv_sum[REP];
   __shared__ float ks[64];
   const float* qrow = a.qkv + (size_t)t * md.QKV + g * REP * 64;
   const size_t base = ((size_t)a.layer * NKV + g) * md.kv_len * 64;
   float* kcw = a.kc[a.slot[t]] + base;
   float* vcw = a.vc[a.slot[t]] + base;
-  for (int i = tid; i < REP * 64; i += 128) qs[i] = qrow[i];
+  for (int i = tid; i < REP * 64; i += kAttnThreads) qs[i] = qrow[i];
   if (FUSED) {
     const float* krow = a.qkv + (size_t)t * md.QKV + md.D + g * 64;
     const float* vrow = krow + NKV * 64;
@@ -369,7 +372,7 @@ __global__ void __launch_bounds__(128) lwe_attention(const __grid_constant__ Lwe
       const float* cs = md.rope_cos + (size_t)pos * md.rope_dim;
       const float* sn = md.rope_sin + (size_t)pos * md.rope_dim;
       // thread (h, d): h = -1 is the key, else query head h of the group; pair (d, d + half)
-      for (int i = tid; i < (REP + 1) * half; i += 128) {
+      for (int i = tid; i < (REP + 1) * half; i += kAttnThreads) {
         const int h = i / half - 1, d = i % half;
         float* p = h < 0 ? ks : qs + h * 64;
         const float a0 = p[d], a1 = p[d + half];
@@ -384,7 +387,7 @@ __global__ void __launch_bounds__(128) lwe_attention(const __grid_constant__ Lwe
   const float* vc = vcw;
   __syncthreads();
   // scores (engine/infer.js:470-476: f32(dot * 1/sqrt(64)))
-  for (int p = tid; p < npos; p += 128) {
+  for (int p = tid; p < npos; p += kAttnThreads) {
     const float4* kr = reinterpret_cast<const float4*>(kc + (size_t)p * 64);
     float4 kk[16];
 #pragma unroll
@@ -428,16 +431,16 @@ __global__ void __launch_bounds__(128) lwe_attention(const __grid_constant__ Lwe
     float4 acc[REP];
 #pragma unroll
     for (int h = 0; h < REP; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int p0 = pl; p0 < npos; p0 += 64) {
+    for (int p0 = pl; p0 < npos; p0 += 8 * kAttnLanes) {
       float4 vv[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const int p = min(p0 + 8 * u, pos);
+        const int p = min(p0 + kAttnLanes * u, pos);
         vv[u] = ldcg_f4(vc + (size_t)p * 64 + dq * 4);
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const int p = p0 + 8 * u;
+        const int p = p0 + kAttnLanes * u;
         if (p < npos) {
 #pragma unroll
           for (int h = 0; h < REP; ++h) {
@@ -454,11 +457,11 @@ __global__ void __launch_bounds__(128) lwe_attention(const __grid_constant__ Lwe
     for (int h = 0; h < REP; ++h) reinterpret_cast<float4*>(red + (pl * REP + h) * 64)[dq] = acc[h];
   }
   __syncthreads();
-  for (int hd = tid; hd < REP * 64; hd += 128) {
+  for (int hd = tid; hd < REP * 64; hd += kAttnThreads) {
     const int h = hd >> 6, d = hd & 63;
     float r = 0.f;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) r += red[(q * REP + h) * 64 + d];
+    for (int q = 0; q < kAttnLanes; ++q) r += red[(q * REP + h) * 64 + d];
     const size_t off = (size_t)t * a.ldx + (g * REP + h) * 64 + d;
     split_hi_lo(r * inv_sum[h], a.xh[off], a.xl[off]);
   }
@@ -649,7 +652,9 @@ void lwe_attn_split_shape(int kv_len, int* chunk, int* splits) {
   *splits = (kv_len + kAttnChunk - 1) / kAttnChunk;
 }
 
-static size_t attention_smem(int rep, int kv_len) { return (size_t)(rep * 64 + rep * kv_len + 8 * rep * 64) * 4; }
+static size_t attention_smem(int rep, int kv_len) {
+  return (size_t)(rep * 64 + rep * kv_len + kAttnLanes * rep * 64) * 4;
+}
 
 // GEMM with a residual epilogue: x[t][r] += W[r] . in_t (+ bias)  (proj and w2).  With gn != nullptr
 // (folded RMSNorm) the epilogue also writes (x * gn) as fp16 hi/lo into nh/nl (stride ldn) and this
@@ -787,7 +792,7 @@ template <int TBW>
 __global__ void __launch_bounds__(kGemmThreads) lwe_gemm_lm(const __grid_constant__ LweArgs a, int T, float* logits) {
   if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(16) unsigned char smem[];
-  using C = LweTile<TBW, 1>;
+  using C = LweTile<TBW, 1, true>;
   constexpr int kLweBT = C::BT;
   const int V = a.m.vocab, K = a.m.D;
   const int r0 = blockIdx.x * kGemmRows, t0 = blockIdx.y * kLweBT;
@@ -981,9 +986,9 @@ static void lwe_debug_check(const char* what, int tb, int ks, int tiles, int T, 
   do {                                                                                                \
     const int _tiles = ((R) + kGemmRows - 1) / kGemmRows;                                             \
     switch (pick_tbw(_tiles, (T))) {                                                                  \
-      case 8: lwe_gemm_lm<8><<<dim3(_tiles, ((T) + 63) / 64), kGemmThreads, LweTile<8, 1>::smem(), st>>>(__VA_ARGS__); break; \
-      case 4: lwe_gemm_lm<4><<<dim3(_tiles, ((T) + 31) / 32), kGemmThreads, LweTile<4, 1>::smem(), st>>>(__VA_ARGS__); break; \
-      default: lwe_gemm_lm<2><<<dim3(_tiles, ((T) + 15) / 16), kGemmThreads, LweTile<2, 1>::smem(), st>>>(__VA_ARGS__); \
+      case 8: lwe_gemm_lm<8><<<dim3(_tiles, ((T) + 63) / 64), kGemmThreads, LweTile<8, 1, true>::smem(), st>>>(__VA_ARGS__); break; \
+      case 4: lwe_gemm_lm<4><<<dim3(_tiles, ((T) + 31) / 32), kGemmThreads, LweTile<4, 1, true>::smem(), st>>>(__VA_ARGS__); break; \
+      default: lwe_gemm_lm<2><<<dim3(_tiles, ((T) + 15) / 16), kGemmThreads, LweTile<2, 1, true>::smem(), st>>>(__VA_ARGS__); \
     }                                                                                                 \
     ++g_lwe_launches;                                                                                 \
   } while (0)
@@ -1007,7 +1012,7 @@ static cudaError_t gemm_attrs() {
   cudaError_t e = gemm_attrs_ks<TBW, 1>();
   if (e == cudaSuccess) e = gemm_attrs_ks<TBW, 2>();
   if (e == cudaSuccess) e = gemm_attrs_ks<TBW, 4>();
-  if (e == cudaSuccess) e = smem_attr(lwe_gemm_lm<TBW>, LweTile<TBW, 1>::smem());
+  if (e == cudaSuccess) e = smem_attr(lwe_gemm_lm<TBW>, LweTile<TBW, 1, true>::smem());
   return e;
 }
 
@@ -1033,10 +1038,10 @@ static void launch_attention_t(const LweArgs& a, int T, cudaStream_t st) {
   const dim3 grid(T, a.m.NKV);
   const size_t sm = attention_smem(rep, a.m.kv_len);
   switch (rep) {
-    case 1: lwe_attention<1, F><<<grid, 128, sm, st>>>(a, T); ++g_lwe_launches; break;
-    case 2: lwe_attention<2, F><<<grid, 128, sm, st>>>(a, T); ++g_lwe_launches; break;
-    case 3: lwe_attention<3, F><<<grid, 128, sm, st>>>(a, T); ++g_lwe_launches; break;
-    default: lwe_attention<4, F><<<grid, 128, sm, st>>>(a, T); ++g_lwe_launches; break;
+    case 1: lwe_attention<1, F><<<grid, kAttnThreads, sm, st>>>(a, T); ++g_lwe_launches; break;
+    case 2: lwe_attention<2, F><<<grid, kAttnThreads, sm, st>>>(a, T); ++g_lwe_launches; break;
+    case 3: lwe_attention<3, F><<<grid, kAttnThreads, sm, st>>>(a, T); ++g_lwe_launches; break;
+    default: lwe_attention<4, F><<<grid, kAttnThreads, sm, st>>>(a, T); ++g_lwe_launches; break;
   }
 }
 
