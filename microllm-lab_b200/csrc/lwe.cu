@@ -927,7 +927,11 @@ __global__ void lwe_first_token(const int32_t* amax, int32_t* out_ids, int32_t* 
 // Host side
 // ---------------------------------------------------------------------------------------------
 // Tokens per CTA: the largest tile that still gives two CTAs per SM, else the smallest.
+// LweHost::force_tbw / force_ks (MLLM_LWE_FORCE_TBW / MLLM_LWE_FORCE_KS: 2/4/8, 1/2/4) override the
+// choices below for tile-size experiments on GEMMs of more than 64 token rows.
+static int g_force_tbw = 0, g_force_ks = 0;  // set from the LweHost of the forward being issued
 static int pick_tbw(int row_tiles, int T) {
+  if (g_force_tbw && T > 64) return g_force_tbw;
   constexpr int kTarget = 2 * 148;
   if (T <= 16) return 2;  // one token tile either way: the smallest wastes the least
   if (T <= 32) return row_tiles >= kTarget ? 4 : 2;
@@ -938,7 +942,10 @@ static int pick_tbw(int row_tiles, int T) {
 
 // Tokens per CTA as above; then the in-CTA k split for GEMMs that still have few CTAs, and for very
 // few CTAs (a handful of tokens) a split of the k groups across CTAs as well (at least 8 groups each).
-static int pick_ks(int ctas) { return ctas >= 2 * 148 ? 1 : (ctas >= 148 ? 2 : 4); }
+static int pick_ks(int ctas) {
+  if (g_force_ks) return g_force_ks;
+  return ctas >= 2 * 148 ? 1 : (ctas >= 148 ? 2 : 4);
+}
 static int pick_ksplit(int ctas, int K, int TBW) {
   if (ctas >= 96) return 1;  // enough CTAs with the in-CTA split alone
   int z = (2 * 148 + ctas - 1) / ctas;
@@ -1072,6 +1079,8 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
                         bool one_per_slot, cudaStream_t st) {
   const ModelDev& md = a.m;
   const int nl = md.n_layers;
+  g_force_tbw = h.force_tbw;
+  g_force_ks = h.force_ks;
   // RMSNorm folded into the GEMMs (llama): the residual GEMMs write x * gain and sums of squares,
   // the consumers apply 1/RMS.  LayerNorm (GPT-2) keeps separate norm kernels.
   const bool fold = md.arch == 0 && h.fold_norm;

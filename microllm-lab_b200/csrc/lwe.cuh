@@ -54,6 +54,8 @@ struct LweHost {
   size_t attn_ctr_n = 0;
   int attn_split = 0;  // decode attention split over positions (MLLM_LWE_ATTN_SPLIT=1)
   int fold_norm = 1;   // llama RMSNorm folded into the GEMM epilogues (MLLM_LWE_FOLD_NORM=0: norm kernels)
+  int force_tbw = 0;   // tile-size experiments (MLLM_LWE_FORCE_TBW / MLLM_LWE_FORCE_KS), 0 = automatic
+  int force_ks = 0;
 };
 
 // one_per_slot: every token belongs to a different slot (a batched decode step), which lets the
