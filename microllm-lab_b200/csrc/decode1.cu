@@ -27,6 +27,8 @@ struct Lay {
   int* misc;     // [32]
   double* cval;  // [kWarps]
   int* cidx;     // [kWarps]
+  uint32_t* lmw; // [lm_rpc][D/8] resident lm_head words (when RunArgs::lm_rpc > 0)
+  float* lms;    // [lm_rpc][D/32] their scales
 };
 
 __device__ __forceinline__ int act_width(const ModelDev& md, int grid) {
@@ -48,7 +50,16 @@ __device__ __forceinline__ Lay layout(const ModelDev& md, float* smem) {
   p = reinterpret_cast<float*>(((uintptr_t)p + 7) & ~(uintptr_t)7);
   L.cval = reinterpret_cast<double*>(p); p += 2 * kWarps;
   L.cidx = reinterpret_cast<int*>(p); p += kWarps;
+  p = reinterpret_cast<float*>(((uintptr_t)p + 15) & ~(uintptr_t)15);
+  L.lmw = reinterpret_cast<uint32_t*>(p);
+  L.lms = nullptr;
   return L;
+}
+
+// lm_head rows resident in shared memory: words then scales, both 16-byte aligned.
+__device__ __forceinline__ void lm_resident_ptrs(const ModelDev& md, int rpc, Lay& L) {
+  const size_t wwords = ((size_t)rpc * (md.D >> 3) + 3) & ~(size_t)3;
+  L.lms = reinterpret_cast<float*>(L.lmw + wwords);
 }
 
 // Opt-in stage timestamps (thread 0 of each CTA, one forward): same layout as the general kernel.
@@ -432,10 +443,13 @@ __device__ __noinline__ int lm_head(const RunArgs& a, const Lay& S, uint32_t tag
   const int nwords = D >> 3;
   const uint64_t limit = a.wait_ns ? a.wait_ns : kWaitNs;
   constexpr int kG = 4;
+  const bool resident = a.lm_rpc > 0;
   Row<NWJ> rw[kG];
+  if (!resident) {
 #pragma unroll
-  for (int g = 0; g < kG; ++g)
-    if (gw + g * NW < md.vocab) rw[g].load(md.lm, gw + g * NW, nwords, lane);
+    for (int g = 0; g < kG; ++g)
+      if (gw + g * NW < md.vocab) rw[g].load(md.lm, gw + g * NW, nwords, lane);
+  }
   {
     float gv[4], bv[4];
     load_gains(md.norm_f, D, md.arch == 1, gv, bv);
@@ -469,28 +483,60 @@ __device__ __noinline__ int lm_head(const RunArgs& a, const Lay& S, uint32_t tag
 #pragma unroll
     for (int e = 0; e < 8; ++e) xr[j][e] = k < nwords ? S.act[8 * k + e] : 0.f;
   }
-  for (int r0 = gw; r0 < md.vocab; r0 += kG * NW) {
+  auto consider = [&](int r, float v) {
+    if (logits && lane == 0) logits[r] = v;
+    double val = v;
+    if (pen) {
+      bool banned = false, recent = false;
+      for (int k = lane; k < nban; k += 32) banned |= S.pen[k] == r;
+      for (int k = lane; k < nrec; k += 32) recent |= S.pen[nban + k] == r;
+      banned = __any_sync(0xffffffffu, banned);
+      recent = __any_sync(0xffffffffu, recent);
+      if (banned) val = -1e9;
+      if (recent && val > -1e8) val = val > 0 ? val / 1.15 : val * 1.15;
+    }
+    if (val > best) {  // rows rise within a warp: strict > keeps the lowest index on ties
+      best = val;
+      bidx = r;
+    }
+  };
+  if (resident) {
+    // rows [blockIdx.x * lm_rpc, +lm_rpc) from shared memory, warp w takes rows w, w + 8, ...
+    const int r0 = blockIdx.x * a.lm_rpc, r1 = min(md.vocab, r0 + a.lm_rpc);
+    const int ng = nwords >> 2;
+    for (int r = r0 + warp; r < r1; r += kWarps) {
+      const uint32_t* wr = S.lmw + (size_t)(r - r0) * nwords;
+      const float* sr = S.lms + (size_t)(r - r0) * ng;
+      float acc = 0.f;
 #pragma unroll
-    for (int g = 0; g < kG; ++g) {
-      const int r = r0 + g * NW;
-      if (r >= md.vocab) break;
-      const float v = rw[g].dot_reg(xr, nwords, lane);
-      const int rn = r + kG * NW;  // next group's row for this slot
-      if (rn < md.vocab) rw[g].load(md.lm, rn, nwords, lane);
-      if (logits && lane == 0) logits[r] = v;
-      double val = v;
-      if (pen) {
-        bool banned = false, recent = false;
-        for (int k = lane; k < nban; k += 32) banned |= S.pen[k] == r;
-        for (int k = lane; k < nrec; k += 32) recent |= S.pen[nban + k] == r;
-        banned = __any_sync(0xffffffffu, banned);
-        recent = __any_sync(0xffffffffu, recent);
-        if (banned) val = -1e9;
-        if (recent && val > -1e8) val = val > 0 ? val / 1.15 : val * 1.15;
+      for (int j = 0; j < NWJ; ++j) {
+        const int k = lane + 32 * j;
+        if (k < nwords) {
+          const uint32_t w = wr[k];
+          const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+          float t = nib_at(lo, 0) * xr[j][0];
+          t = fmaf(nib_at(hi, 0), xr[j][1], t);
+          t = fmaf(nib_at(lo, 1), xr[j][2], t);
+          t = fmaf(nib_at(hi, 1), xr[j][3], t);
+          t = fmaf(nib_at(lo, 2), xr[j][4], t);
+          t = fmaf(nib_at(hi, 2), xr[j][5], t);
+          t = fmaf(nib_at(lo, 3), xr[j][6], t);
+          t = fmaf(nib_at(hi, 3), xr[j][7], t);
+          acc = fmaf(t, sr[k >> 2], acc);
+        }
       }
-      if (val > best) {  // rows rise within a warp: strict > keeps the lowest index on ties
-        best = val;
-        bidx = r;
+      consider(r, warp_sum(acc));
+    }
+  } else {
+    for (int r0 = gw; r0 < md.vocab; r0 += kG * NW) {
+#pragma unroll
+      for (int g = 0; g < kG; ++g) {
+        const int r = r0 + g * NW;
+        if (r >= md.vocab) break;
+        const float v = rw[g].dot_reg(xr, nwords, lane);
+        const int rn = r + kG * NW;  // next group's row for this slot
+        if (rn < md.vocab) rw[g].load(md.lm, rn, nwords, lane);
+        consider(r, v);
       }
     }
   }
@@ -717,7 +763,18 @@ template <int NWJ_D, int NWJ_F>
 __global__ void __launch_bounds__(kThreads, 1) decode1_kernel(const __grid_constant__ RunArgs a) {
   extern __shared__ __align__(16) float smem[];
   const ModelDev& md = a.m;
-  const d1::Lay S = d1::layout(md, smem);
+  d1::Lay S = d1::layout(md, smem);
+  if (a.lm_rpc > 0) {
+    // this CTA's lm_head rows stay in shared memory for every forward of the launch
+    d1::lm_resident_ptrs(md, a.lm_rpc, S);
+    const int r0 = blockIdx.x * a.lm_rpc, nr = max(0, min(md.vocab, r0 + a.lm_rpc) - r0);
+    const int nwords = md.D >> 3, ng = md.D >> 5;
+    const uint4* src = reinterpret_cast<const uint4*>(md.lm.w + (size_t)r0 * nwords);
+    uint4* dst = reinterpret_cast<uint4*>(S.lmw);
+    for (int i = threadIdx.x; i < nr * nwords / 4; i += kThreads) dst[i] = __ldg(src + i);
+    for (int i = threadIdx.x; i < nr * ng; i += kThreads) S.lms[i] = __ldg(md.lm.s + (size_t)r0 * ng + i);
+    __syncthreads();
+  }
   const bool lead = blockIdx.x == 0 && threadIdx.x == 0;
   const int n = a.n_ids, D = md.D;
   const bool gen_mode = a.mode == MODE_GENERATE;
@@ -796,13 +853,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode1_kernel(const __grid_const
   }
 }
 
-size_t decode1_smem_bytes(const ModelDev& md, int grid) {
+size_t decode1_smem_bytes(const ModelDev& md, int grid, int lm_rpc) {
   int actw = std::max(std::max(md.D, md.QKV), md.FF);
   actw = std::max(actw, 3 * grid + 4);
   actw = (actw + 3) & ~3;
   size_t words = (size_t)md.D + actw + kWarps * 68 + 2 * kWarps + (md.kv_len + 64) + (md.kv_len + 128) + 32;
   words = (words + 1) & ~(size_t)1;
   words += 2 * kWarps + kWarps;
+  words = (words + 3) & ~(size_t)3;
+  if (lm_rpc > 0) words += (((size_t)lm_rpc * (md.D >> 3) + 3) & ~(size_t)3) + (size_t)lm_rpc * (md.D >> 5);
   return words * 4;
 }
 

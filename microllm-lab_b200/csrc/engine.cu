@@ -27,7 +27,7 @@
 
 namespace mllm {
 size_t decode_smem_bytes(const ModelDev& md, int srows, int grid);
-size_t decode1_smem_bytes(const ModelDev& md, int grid);
+size_t decode1_smem_bytes(const ModelDev& md, int grid, int lm_rpc);
 typedef void (*DecodeFn)(const RunArgs);
 DecodeFn pick_decode_kernel(int D, int FF, bool multi);
 DecodeFn pick_decode1_kernel(int D, int FF);
@@ -90,6 +90,7 @@ struct mllm_engine {
   int poll_sleep_ns = 200;     // MLLM_POLL_SLEEP_NS: back-off between poll rounds (less L2 contention)
   int weight_policy = 0;       // MLLM_WEIGHT_EVICT_LAST
   int l2_prefetch = 1;         // MLLM_L2_PREFETCH (default on)
+  int lm_rpc = 0;              // lm_head rows per CTA kept in the single-token kernel's shared memory
   // layer-wise engine: token-batch forwards on the tensor cores (prefill, verify, batched decode)
   int lwe_ok = 0;              // rep = nHeads / nKvHeads fits its attention kernel
   int lwe_prefill = 1;         // MLLM_LWE_PREFILL=0 keeps prefill and multi-token forwards on decode_kernel
@@ -262,6 +263,7 @@ int launch(mllm_engine* e, RunArgs& a, int max_forwards, bool multi, bool resume
   a.poll_sleep_ns = e->poll_sleep_ns;
   a.weight_policy = e->weight_policy;
   a.l2_prefetch = e->l2_prefetch;
+  a.lm_rpc = multi ? 0 : e->lm_rpc;
   if (!resume) {
     CUDA_TRY(e, cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream));
     CUDA_TRY(e, cudaMemsetAsync(e->d_status, 0, ST_WORDS * sizeof(int32_t), e->stream));
@@ -602,7 +604,14 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   while (mmax > 1 && decode_smem_bytes(md, mmax, e->grid) > smem_cap) --mmax;
   e->mmax = mmax;
   e->smem_multi = decode_smem_bytes(md, mmax, e->grid);
-  e->smem_single = decode1_smem_bytes(md, e->grid);
+  // lm_head rows resident in the single-token kernel's shared memory when they fit (MLLM_LM_RESIDENT=0: off)
+  {
+    const int rpc = (md.vocab + e->grid - 1) / e->grid;
+    bool want = true;
+    if (const char* v = getenv("MLLM_LM_RESIDENT")) want = atoi(v) != 0;
+    e->lm_rpc = want && decode1_smem_bytes(md, e->grid, rpc) <= smem_cap ? rpc : 0;
+  }
+  e->smem_single = decode1_smem_bytes(md, e->grid, e->lm_rpc);
   if (e->smem_multi > smem_cap) return bad(MLLM_ERR_UNSUPPORTED, "model does not fit the shared-memory budget");
   for (DecodeFn k : {e->kernel_multi, e->kernel_single}) {
     // The limit is an attribute of the kernel function, shared by every engine that uses the same

@@ -94,6 +94,8 @@ struct RunArgs {
   int poll_sleep_ns;   // back-off between unsuccessful poll rounds (0 = spin)
   int weight_policy;   // 0: default L2 policy for weights, 1: evict_last
   int l2_prefetch;     // 1: bulk-prefetch the next layer's weight slices (and the layer's K/V) into L2
+  int lm_rpc;          // single-token kernel: > 0 = each CTA keeps lm_head rows [cta * lm_rpc, +lm_rpc) in
+                       // shared memory for the whole launch (copied once at entry)
 };
 
 }  // namespace mllm
