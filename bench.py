@@ -37,9 +37,12 @@ sys.path.insert(0, ROOT)
 CACHE = os.environ.get("MLLM_PGW_CACHE", "/tmp/mllm_pgw_cache")
 L2_BYTES = 126 * 1024 * 1024
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one decode_kernel launch of the default workload,
-# from the ncu capture summarised in profiles/decode_kernel_petitgpt_b1.md (None until captured).
-DECODE_TRAFFIC_PER_LAUNCH = None
+# dram__bytes_read.sum + dram__bytes_write.sum summed over every kernel of one generate call of the
+# config-1 workload (token-batch prefill + the decode1_kernel launch), from one ncu capture of
+# `microllm-lab_b200/profile_case.py decode --new 128` (decode1_kernel: 417,123,840 B; prefill
+# kernels: 132,081,664 B).
+# ncu flushes the caches before each captured kernel, as the bench flushes L2 before each call.
+DECODE_TRAFFIC_PER_CALL = {"config1 petitgpt b1 p64 n128": 549_205_504}
 
 
 def pkg():
@@ -107,6 +110,11 @@ class ClockSampler:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def decode_weight_bytes(cfg: dict) -> int:
+    """Q4 weights (packed nibbles + fp32 group scales) plus fp32 norm gains of one forward."""
+    return decode_algorithmic_bytes(cfg, 0, 1)
 
 
 def decode_algorithmic_bytes(cfg: dict, n_prompt: int, n_new: int) -> int:
@@ -498,16 +506,24 @@ def run_decode(args):
         "data": "synthetic (seeded N(0,0.02) Q4 weights, seeded uniform prompt ids; real checkpoints are LFS stubs)",
         "config": {"workload": W["workload"], "model": W["model_text"],
                    "global_batch": ws, "seq_len": n_prompt + n_new, "parallelism": f"replicas x{ws}",
-                   "l2": "flushed (256 MB write) before every timed step; weights 78 MB fit in L2 within a step",
+                   "l2": (f"flushed (256 MB write) before every timed step; Q4 weights "
+                          f"{decode_weight_bytes(cfg) / 1e6:.0f} MB "
+                          + ("fit in L2 within a step" if decode_weight_bytes(cfg) < L2_BYTES else
+                             "exceed L2, re-read from HBM every forward")),
                    "tokens_per_step": n_new,
                    "launches_per_step": launches[0] // max(args.steps, 1),
-                   "path": "prefill as token-batch tensor-core forwards, then the 127 decode steps in one "
-                           "persistent single-token kernel launch"},
+                   "path": (f"prefill as token-batch tensor-core forwards, then one CUDA-graph replay per "
+                            f"speculation iteration (k_spec_prepare, {spec_k + 1}-row verify forward, k_spec_accept)"
+                            if spec_k else
+                            f"prefill as token-batch tensor-core forwards, then the {n_new - 1} decode steps in one "
+                            f"persistent single-token kernel launch")},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": n_prompt * 4, "d2h_bytes_per_step": n_new * 4 + 68},
         "gpu_launches": launches[0],
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": peak_kind, "traffic": DECODE_TRAFFIC_PER_LAUNCH,
-                     "kernel": "decode1_kernel<3,6> (whole generate call)", "algorithmic_bytes_per_launch": alg,
+                     "peak_kind": peak_kind, "traffic": DECODE_TRAFFIC_PER_CALL.get(W["workload"]),
+                     "kernel": ("whole generate call (token-batch prefill + graph-replayed speculation iterations)"
+                                if spec_k else "decode1_kernel<3,6> (whole generate call)"),
+                     "algorithmic_bytes_per_launch": alg,
                      "kernel_ms_device_timer": float(np.mean(dev_ms)) if dev_ms else None},
         "clocks": clk.summary(),
     }

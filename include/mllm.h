@@ -8,7 +8,7 @@
  *
  * Each entry point names the reference interface it replaces (paths relative to the reference
  * project root).  The JavaScript engine surface those bind to is PetitGPT (engine/infer.js:289-647)
- * and GpuPetitGPT (engine/webgpu.js:867-1297); INTEGRATION.md shows the Node-API binding.
+ * and GpuPetitGPT (engine/webgpu.js:867-1297); a Node-API addon binds each entry point one to one.
  */
 #ifndef MLLM_H
 #define MLLM_H

@@ -26,6 +26,32 @@ namespace mllm {
 thread_local long g_lwe_launches = 0;
 long lwe_launch_count() { return g_lwe_launches; }
 
+// Programmatic dependent launch.  The forward's kernels are launched with programmatic stream
+// serialisation: a kernel's CTAs start as soon as the previous grid's CTAs have exited, before that
+// grid's memory flush, and wait for it with griddepcontrol.wait before they read or write any buffer
+// that another kernel writes (the skip flag included).  The GEMMs request their first weight stages
+// before that wait.  No kernel triggers its dependents early (an early trigger let the next grid's CTAs
+// take SM slots during this grid's tail and unbalanced the GEMMs), and every kernel waits before it
+// exits, so a grid's completion still implies its predecessors'.  Without the launch attribute the
+// wait returns at once.
+__device__ __forceinline__ void pdl_enter() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+thread_local bool g_lwe_pdl = true;
+template <typename... P, typename... A>
+static inline void lwe_launch(void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = g_lwe_pdl ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, k, std::forward<A>(args)...);
+  ++g_lwe_launches;
+}
+
 // GEMM tiles: 64 weight rows x 8*TBW tokens per CTA; TBW is picked per launch so that small-R GEMMs
 // still fill the GPU, and the k-pipeline is deeper for the smaller token tiles (all under 48 KB).
 // The k groups may also be split over KS groups of 4 warps inside the CTA (more warps in flight per
@@ -176,6 +202,7 @@ __device__ __forceinline__ void warp_norm_split(const float* x, int D, bool ln, 
 
 // Embedding of token t (one CTA per token); with g != nullptr also the first layer's norm1 into xh/xl.
 __global__ void lwe_embed(const __grid_constant__ LweArgs a, int T, const float* g) {
+  pdl_enter();
   if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   const int t = blockIdx.x;
   if (t >= T) return;
@@ -222,6 +249,7 @@ __global__ void lwe_embed(const __grid_constant__ LweArgs a, int T, const float*
 
 // RMSNorm / LayerNorm of X[src[i]] (or X[i]) -> fp16 hi/lo rows i of xh/xl.  One CTA per row.
 __global__ void lwe_norm_split(const __grid_constant__ LweArgs a, int T, const float* g, const int* src) {
+  pdl_enter();
   if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   const int i = blockIdx.x;
   if (i >= T) return;
@@ -277,21 +305,23 @@ __global__ void lwe_norm_split(const __grid_constant__ LweArgs a, int T, const f
 template <int TBW, int KS>
 __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_qkv(const __grid_constant__ LweArgs a, int T,
                                                                          int l) {
-  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(16) unsigned char smem[];
   using C = LweTile<TBW, KS>;
   __shared__ float sinv[C::BT];
   const LayerDev& L = a.m.layers[l];
   const int R = a.m.QKV, K = a.m.D, t0 = blockIdx.y * C::BT;
-  if (threadIdx.x < C::BT) sinv[threadIdx.x] = a.fold && t0 + (int)threadIdx.x < T ? fold_inv(a, t0 + threadIdx.x) : 1.f;
-  __syncthreads();
   const float* bias = L.qkv_b;
   float* out = a.qkv;
   const int r0 = blockIdx.x * kGemmRows;
   const RowsLinear rows{reinterpret_cast<const uint8_t*>(L.qkv.w), L.qkv.s, R, r0, K >> 1, K >> 5};
   float acc[TBW][4];
-  q4_gemm_core<TBW, C::NS, C::KS, decltype(rows), C::GPS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  // waits for the previous kernel inside, after requesting the first weight stages
+  if (!q4_gemm_core<TBW, C::NS, C::KS, decltype(rows), C::GPS, true>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc,
+                                                                     a.skip))
+    return;  // a finished speculative loop replays as no-ops
   if (!lwe_splitk<TBW>(a, acc)) return;
+  if (threadIdx.x < C::BT) sinv[threadIdx.x] = a.fold && t0 + (int)threadIdx.x < T ? fold_inv(a, t0 + threadIdx.x) : 1.f;
+  __syncthreads();
   lwe_tile_epi<TBW>(acc, r0, t0, R, T, [&](int r, int t, float v) {
     v *= sinv[t - t0];
     out[(size_t)t * R + r] = bias ? v + bias[r] : v;
@@ -301,6 +331,7 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_qkv(const 
 // RoPE on k (and on the q heads of the group) at each token's position, then the K/V cache write
 // (engine/infer.js:436-464).  grid (T, NKV), 64 threads: thread d < 32 rotates pair (d, d + 32).
 __global__ void lwe_rope_kv(const __grid_constant__ LweArgs a, int T) {
+  pdl_enter();
   if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   const int t = blockIdx.x, g = blockIdx.y;
   if (t >= T) return;
@@ -342,6 +373,7 @@ constexpr int kAttnThreads = 128;
 constexpr int kAttnLanes = kAttnThreads / 16;  // position lanes of the P.V pass
 template <int REP, bool FUSED>
 __global__ void __launch_bounds__(kAttnThreads) lwe_attention(const __grid_constant__ LweArgs a, int T) {
+  pdl_enter();
   if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(16) float asm_[];
   const int t = blockIdx.x, g = blockIdx.y;
@@ -478,6 +510,7 @@ __global__ void __launch_bounds__(kAttnThreads) lwe_attention(const __grid_const
 constexpr int kAttnChunk = 64;
 template <int REP, bool FUSED>
 __global__ void __launch_bounds__(64) lwe_attn_split(const __grid_constant__ LweArgs a, int T, float* part, int* ctr) {
+  pdl_enter();
   if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(128) float kvs[];  // K [64][64], V [64][64]
   const int t = blockIdx.x, g = blockIdx.y, sp = blockIdx.z, S = gridDim.z;
@@ -664,7 +697,6 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_resid(cons
                                                                            Q4 w, const float* bias, int K,
                                                                            const float* gn, __half* nh, __half* nl,
                                                                            int ldn) {
-  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(16) unsigned char smem[];
   using C = LweTile<TBW, KS>;
   __shared__ float ssw[4][C::BT];
@@ -672,7 +704,10 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_resid(cons
   float* x = a.x;
   const RowsLinear rows{reinterpret_cast<const uint8_t*>(w.w), w.s, R, r0, K >> 1, K >> 5};
   float acc[TBW][4];
-  q4_gemm_core<TBW, C::NS, C::KS, decltype(rows), C::GPS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  // waits for the previous kernel inside, after requesting the first weight stages
+  if (!q4_gemm_core<TBW, C::NS, C::KS, decltype(rows), C::GPS, true>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc,
+                                                                     a.skip))
+    return;  // a finished speculative loop replays as no-ops
   if (!lwe_splitk<TBW>(a, acc)) return;
   if (threadIdx.x < kGemmThreads) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tq = lane & 3;
@@ -727,23 +762,25 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_resid(cons
 template <int TBW, int KS>
 __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_w13(const __grid_constant__ LweArgs a, int T,
                                                                          int l) {
-  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(16) unsigned char smem[];
   using C = LweTile<TBW, KS>;
   __shared__ float sinv[C::BT];
   const LayerDev& L = a.m.layers[l];
   const int FF = a.m.FF, K = a.m.D;
-  {
-    const int tt = blockIdx.y * C::BT + threadIdx.x;
-    if (threadIdx.x < C::BT) sinv[threadIdx.x] = a.fold && tt < T ? fold_inv(a, tt) : 1.f;
-    __syncthreads();
-  }
   const RowsPaired rows{reinterpret_cast<const uint8_t*>(L.w1.w), L.w1.s, reinterpret_cast<const uint8_t*>(L.w3.w),
                         L.w3.s, FF, (int)blockIdx.x * 32, K >> 1, K >> 5};
   float acc[TBW][4];
   const int t0 = blockIdx.y * C::BT;
-  q4_gemm_core<TBW, C::NS, C::KS, decltype(rows), C::GPS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  // waits for the previous kernel inside, after requesting the first weight stages
+  if (!q4_gemm_core<TBW, C::NS, C::KS, decltype(rows), C::GPS, true>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc,
+                                                                     a.skip))
+    return;  // a finished speculative loop replays as no-ops
   if (!lwe_splitk<TBW>(a, acc)) return;
+  {
+    const int tt = t0 + threadIdx.x;
+    if (threadIdx.x < C::BT) sinv[threadIdx.x] = a.fold && tt < T ? fold_inv(a, tt) : 1.f;
+    __syncthreads();
+  }
   if (threadIdx.x >= kGemmThreads) return;  // partial sums were added into the first warp group
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
   const int ia = warp * 16 + gid;  // A row (w1); the B row (w3) of the same matrix row is ia + 8
@@ -767,7 +804,6 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_w13(const 
 template <int TBW, int KS>
 __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_fc(const __grid_constant__ LweArgs a, int T,
                                                                         int l) {
-  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(16) unsigned char smem[];
   using C = LweTile<TBW, KS>;
   const LayerDev& L = a.m.layers[l];
@@ -776,7 +812,10 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_fc(const _
   const int r0 = blockIdx.x * kGemmRows, t0 = blockIdx.y * C::BT;
   const RowsLinear rows{reinterpret_cast<const uint8_t*>(L.w1.w), L.w1.s, FF, r0, K >> 1, K >> 5};
   float acc[TBW][4];
-  q4_gemm_core<TBW, C::NS, C::KS, decltype(rows), C::GPS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  // waits for the previous kernel inside, after requesting the first weight stages
+  if (!q4_gemm_core<TBW, C::NS, C::KS, decltype(rows), C::GPS, true>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc,
+                                                                     a.skip))
+    return;  // a finished speculative loop replays as no-ops
   if (!lwe_splitk<TBW>(a, acc)) return;
   lwe_tile_epi<TBW>(acc, r0, t0, FF, T, [&](int r, int t, float v) {
     if (bias) v += bias[r];
@@ -790,7 +829,6 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_fc(const _
 // logits store [t][V].
 template <int TBW>
 __global__ void __launch_bounds__(kGemmThreads) lwe_gemm_lm(const __grid_constant__ LweArgs a, int T, float* logits) {
-  if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   extern __shared__ __align__(16) unsigned char smem[];
   using C = LweTile<TBW, 1, true>;
   constexpr int kLweBT = C::BT;
@@ -798,7 +836,9 @@ __global__ void __launch_bounds__(kGemmThreads) lwe_gemm_lm(const __grid_constan
   const int r0 = blockIdx.x * kGemmRows, t0 = blockIdx.y * kLweBT;
   float acc[TBW][4];
   const RowsLinear rows{reinterpret_cast<const uint8_t*>(a.m.lm.w), a.m.lm.s, V, r0, K >> 1, K >> 5};
-  q4_gemm_core<TBW, C::NS, 1, decltype(rows), C::GPS>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc);
+  // waits for the previous kernel inside, after requesting the first weight stages
+  if (!q4_gemm_core<TBW, C::NS, 1, decltype(rows), C::GPS, true>(rows, a.xh, a.xl, a.ldx, K, T, t0, smem, acc, a.skip))
+    return;  // a finished speculative loop replays as no-ops
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
   const int ra = r0 + warp * 16 + gid, rb = ra + 8;
   __syncthreads();  // the pipeline buffers are reused below
@@ -860,6 +900,7 @@ __global__ void __launch_bounds__(kGemmThreads) lwe_gemm_lm(const __grid_constan
 
 // Per token: argmax over the row-block partials -> amax[t]; optional scatter of the result.
 __global__ void lwe_argmax_reduce(const __grid_constant__ LweArgs a, int T, int nblk) {
+  pdl_enter();
   if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -890,6 +931,7 @@ __global__ void lwe_argmax_reduce(const __grid_constant__ LweArgs a, int T, int 
 // apply the stop rules of engine/infer.js:617-639 and advance token and position.
 __global__ void lwe_decode_advance(const __grid_constant__ LweArgs a, int T, int max_new, int eos,
                                    int32_t* out_ids, int32_t* counts, const int32_t* prompt_len) {
+  pdl_enter();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   if (counts[t] < 0) return;  // finished (sign flipped)
@@ -966,10 +1008,9 @@ static void lwe_debug_check(const char* what, int tb, int ks, int tiles, int T, 
             cudaGetErrorString(e));
 }
 #define LWE_LAUNCH_(KER, TB, KSV, TILES, T, KZ, ...)                                                  \
-  KER<TB, KSV><<<dim3(TILES, ((T) + 8 * TB - 1) / (8 * TB), KZ), LweTile<TB, KSV>::THREADS,        \
-                 LweTile<TB, KSV>::smem(), st>>>(__VA_ARGS__);                                        \
-  lwe_debug_check(#KER, TB, KSV, TILES, T, KZ, LweTile<TB, KSV>::smem());                              \
-  ++g_lwe_launches
+  lwe_launch(KER<TB, KSV>, dim3(TILES, ((T) + 8 * TB - 1) / (8 * TB), KZ), dim3(LweTile<TB, KSV>::THREADS), \
+             LweTile<TB, KSV>::smem(), st, __VA_ARGS__);                                              \
+  lwe_debug_check(#KER, TB, KSV, TILES, T, KZ, LweTile<TB, KSV>::smem())
 #define LWE_GEMM(KER, ROWS_PER_CTA, R, K, T, ...)                                                     \
   do {                                                                                                \
     const int _tiles = ((R) + (ROWS_PER_CTA)-1) / (ROWS_PER_CTA);                                     \
@@ -993,11 +1034,10 @@ static void lwe_debug_check(const char* what, int tb, int ks, int tiles, int T, 
   do {                                                                                                \
     const int _tiles = ((R) + kGemmRows - 1) / kGemmRows;                                             \
     switch (pick_tbw(_tiles, (T))) {                                                                  \
-      case 8: lwe_gemm_lm<8><<<dim3(_tiles, ((T) + 63) / 64), kGemmThreads, LweTile<8, 1, true>::smem(), st>>>(__VA_ARGS__); break; \
-      case 4: lwe_gemm_lm<4><<<dim3(_tiles, ((T) + 31) / 32), kGemmThreads, LweTile<4, 1, true>::smem(), st>>>(__VA_ARGS__); break; \
-      default: lwe_gemm_lm<2><<<dim3(_tiles, ((T) + 15) / 16), kGemmThreads, LweTile<2, 1, true>::smem(), st>>>(__VA_ARGS__); \
+      case 8: lwe_launch(lwe_gemm_lm<8>, dim3(_tiles, ((T) + 63) / 64), dim3(kGemmThreads), LweTile<8, 1, true>::smem(), st, __VA_ARGS__); break; \
+      case 4: lwe_launch(lwe_gemm_lm<4>, dim3(_tiles, ((T) + 31) / 32), dim3(kGemmThreads), LweTile<4, 1, true>::smem(), st, __VA_ARGS__); break; \
+      default: lwe_launch(lwe_gemm_lm<2>, dim3(_tiles, ((T) + 15) / 16), dim3(kGemmThreads), LweTile<2, 1, true>::smem(), st, __VA_ARGS__); \
     }                                                                                                 \
-    ++g_lwe_launches;                                                                                 \
   } while (0)
 
 template <class F>
@@ -1031,12 +1071,11 @@ static void launch_attention_split(const LweArgs& a, const LweHost& h, int T, cu
   const dim3 grid(T, a.m.NKV, S);
   const size_t sm = (size_t)2 * kAttnChunk * 64 * 4;
   switch (rep) {
-    case 1: lwe_attn_split<1, F><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
-    case 2: lwe_attn_split<2, F><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
-    case 3: lwe_attn_split<3, F><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
-    default: lwe_attn_split<4, F><<<grid, 64, sm, st>>>(a, T, h.attn_part, h.attn_ctr); break;
+    case 1: lwe_launch(lwe_attn_split<1, F>, grid, dim3(64), sm, st, a, T, h.attn_part, h.attn_ctr); break;
+    case 2: lwe_launch(lwe_attn_split<2, F>, grid, dim3(64), sm, st, a, T, h.attn_part, h.attn_ctr); break;
+    case 3: lwe_launch(lwe_attn_split<3, F>, grid, dim3(64), sm, st, a, T, h.attn_part, h.attn_ctr); break;
+    default: lwe_launch(lwe_attn_split<4, F>, grid, dim3(64), sm, st, a, T, h.attn_part, h.attn_ctr); break;
   }
-  ++g_lwe_launches;
 }
 
 template <bool F>
@@ -1045,10 +1084,10 @@ static void launch_attention_t(const LweArgs& a, int T, cudaStream_t st) {
   const dim3 grid(T, a.m.NKV);
   const size_t sm = attention_smem(rep, a.m.kv_len);
   switch (rep) {
-    case 1: lwe_attention<1, F><<<grid, kAttnThreads, sm, st>>>(a, T); ++g_lwe_launches; break;
-    case 2: lwe_attention<2, F><<<grid, kAttnThreads, sm, st>>>(a, T); ++g_lwe_launches; break;
-    case 3: lwe_attention<3, F><<<grid, kAttnThreads, sm, st>>>(a, T); ++g_lwe_launches; break;
-    default: lwe_attention<4, F><<<grid, kAttnThreads, sm, st>>>(a, T); ++g_lwe_launches; break;
+    case 1: lwe_launch(lwe_attention<1, F>, grid, dim3(kAttnThreads), sm, st, a, T); break;
+    case 2: lwe_launch(lwe_attention<2, F>, grid, dim3(kAttnThreads), sm, st, a, T); break;
+    case 3: lwe_launch(lwe_attention<3, F>, grid, dim3(kAttnThreads), sm, st, a, T); break;
+    default: lwe_launch(lwe_attention<4, F>, grid, dim3(kAttnThreads), sm, st, a, T); break;
   }
 }
 
@@ -1085,8 +1124,8 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
   // the consumers apply 1/RMS.  LayerNorm (GPT-2) keeps separate norm kernels.
   const bool fold = md.arch == 0 && h.fold_norm;
   a.fold = fold ? 1 : 0;
-  lwe_embed<<<T, 128, 0, st>>>(a, T, h.layers[0].norm1);  // + norm1 of layer 0
-  ++g_lwe_launches;
+  g_lwe_pdl = h.pdl != 0;
+  lwe_launch(lwe_embed, dim3(T), dim3(128), 0, st, a, T, h.layers[0].norm1);  // + norm1 of layer 0
   for (int l = 0; l < nl; ++l) {
     const LayerDev& L = h.layers[l];
     a.layer = l;
@@ -1097,8 +1136,7 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
       else
         launch_attention_t<true>(a, T, st);
     } else {
-      lwe_rope_kv<<<dim3(T, md.NKV), 64, 0, st>>>(a, T);
-      ++g_lwe_launches;
+      lwe_launch(lwe_rope_kv, dim3(T, md.NKV), dim3(64), 0, st, a, T);
       // a few tokens (a verify forward) over a long cache: split the positions across CTAs
       if (T <= kLweSplitAttnRows)
         launch_attention_split<false>(a, h, T, st);
@@ -1113,8 +1151,7 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
       LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.D, T, a, T, L.proj, L.proj_b, md.D, L.norm2, a.xh3, a.xl3, a.ldx);
     } else {
       LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.D, T, a, T, L.proj, L.proj_b, md.D, nullptr, nullptr, nullptr, 0);
-      lwe_norm_split<<<T, 128, 0, st>>>(a, T, L.norm2, nullptr);
-      ++g_lwe_launches;
+      lwe_launch(lwe_norm_split, dim3(T), dim3(128), 0, st, a, T, L.norm2, (const int*)nullptr);
     }
     if (md.arch == 0)
       LWE_GEMM(lwe_gemm_w13, 32, md.FF, md.D, T, n2, T, l);
@@ -1131,18 +1168,16 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
     } else {
       LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.FF, T, b, T, L.w2, L.mproj_b, md.FF, nullptr, nullptr, nullptr, 0);
       if (ng) {
-        lwe_norm_split<<<T, 128, 0, st>>>(a, T, ng, nullptr);
-        ++g_lwe_launches;
+        lwe_launch(lwe_norm_split, dim3(T), dim3(128), 0, st, a, T, ng, (const int*)nullptr);
       }
     }
   }
   if (lm_T > 0) {
-    lwe_norm_split<<<lm_T, 128, 0, st>>>(a, lm_T, md.norm_f, lm_from_src ? a.lm_src : nullptr);
-    ++g_lwe_launches;
+    lwe_launch(lwe_norm_split, dim3(lm_T), dim3(128), 0, st, a, lm_T, md.norm_f,
+               (const int*)(lm_from_src ? a.lm_src : nullptr));
     const int tiles = (md.vocab + kGemmRows - 1) / kGemmRows;
     LWE_GEMM_LM(md.vocab, lm_T, a, lm_T, logits);
-    lwe_argmax_reduce<<<(lm_T + 3) / 4, 128, 0, st>>>(a, lm_T, tiles);
-    ++g_lwe_launches;
+    lwe_launch(lwe_argmax_reduce, dim3((lm_T + 3) / 4), dim3(128), 0, st, a, lm_T, tiles);
   }
   return cudaGetLastError();
 }
@@ -1212,8 +1247,7 @@ void lwe_batch_decode_setup(LweArgs a, int n, const int32_t* out_ids, const int3
 }
 void lwe_batch_advance(LweArgs a, int n, int max_new, int eos, int32_t* out_ids, int32_t* counts, const int32_t* lens,
                        cudaStream_t st) {
-  lwe_decode_advance<<<(n + 127) / 128, 128, 0, st>>>(a, n, max_new, eos, out_ids, counts, lens);
-  ++g_lwe_launches;
+  lwe_launch(lwe_decode_advance, dim3((n + 127) / 128), dim3(128), 0, st, a, n, max_new, eos, out_ids, counts, lens);
 }
 
 // Number of sequences still running -> *active.
@@ -1385,6 +1419,7 @@ __global__ void k_spec_init(int32_t* sp, const int32_t* ids, int n, const int32_
 // rows dl+1..T-1 repeat row dl (same id, same position: identical K/V writes, logits unused).
 __global__ void k_spec_prepare(const __grid_constant__ LweArgs a, int32_t* sp, int spec_k, int ngram, int max_new,
                                int T, int slot) {
+  pdl_enter();
   __shared__ int best;
   __shared__ int sdone;
   const int32_t* hist = sp + kSpecHist;
@@ -1437,6 +1472,7 @@ __global__ void k_spec_prepare(const __grid_constant__ LweArgs a, int32_t* sp, i
 
 // engine/webgpu.js:1249-1268: accept r[0], then r[k+1] while r[k] == draft[k].
 __global__ void k_spec_accept(const int32_t* amax, int32_t* sp, int32_t* out_ids, int max_new, int eos) {
+  pdl_enter();
   if (threadIdx.x != 0 || sp[SP_DONE]) return;
   int32_t* hist = sp + kSpecHist;
   const int32_t* draft = sp + kSpecDraft;
@@ -1491,14 +1527,13 @@ void lwe_spec_init(int32_t* sp, const int32_t* ids, int n, const int32_t* out_id
 cudaError_t lwe_spec_iteration(LweArgs a, const LweHost& h, int32_t* sp, int32_t* out_ids, int spec_k, int ngram,
                                int max_new, int eos, int slot, cudaStream_t st) {
   const int T = spec_k + 1;
-  k_spec_prepare<<<1, 256, 0, st>>>(a, sp, spec_k, ngram, max_new, T, slot);
-  ++g_lwe_launches;
+  g_lwe_pdl = h.pdl != 0;
+  lwe_launch(k_spec_prepare, dim3(1), dim3(256), 0, st, a, sp, spec_k, ngram, max_new, T, slot);
   LweArgs f = a;
   f.skip = sp + SP_DONE;
   const cudaError_t e = lwe_forward(f, h, T, T, false, nullptr, false, st);
   if (e != cudaSuccess) return e;
-  k_spec_accept<<<1, 32, 0, st>>>(a.amax, sp, out_ids, max_new, eos);
-  ++g_lwe_launches;
+  lwe_launch(k_spec_accept, dim3(1), dim3(32), 0, st, (const int32_t*)a.amax, sp, out_ids, max_new, eos);
   return cudaGetLastError();
 }
 void lwe_spec_finish(const int32_t* sp, int32_t* status, cudaStream_t st) {

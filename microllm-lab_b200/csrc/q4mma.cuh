@@ -110,10 +110,11 @@ struct RowsPaired {
 
 template <int TBW, int GPS>
 struct GemmStage;
-template <int TBW, int NS, int KS, class Rows, int GPS = 1>
-__device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __restrict__ Xhi,
+template <int TBW, int NS, int KS, class Rows, int GPS = 1, bool PDL = false>
+__device__ __forceinline__ bool q4_gemm_core(const Rows& rows, const __half* __restrict__ Xhi,
                                              const __half* __restrict__ Xlo, int ldx, int K, int T, int t0,
-                                             unsigned char* smem, float (&acc)[TBW][4]);
+                                             unsigned char* smem, float (&acc)[TBW][4],
+                                             const int* skip = nullptr);
 
 // Element-wise epilogue form: epi(tile_row, token, value) for every valid (row, token) of the tile.
 template <int TBW, int NS = kStages, int KS = 1, class Rows, class Epi>
@@ -163,10 +164,15 @@ struct GemmStage {
   static constexpr size_t bytes = W + SC + 2 * X;
 };
 
-template <int TBW, int NS, int KS, class Rows, int GPS>
-__device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __restrict__ Xhi,
+//
+// PDL: the kernel was launched as a programmatic dependent of the previous kernel in the stream.  The
+// weights and scales of the prologue stages (which no kernel writes) are requested first; then the
+// CTA waits for the previous grid (griddepcontrol.wait) and, unless *skip is set, requests the
+// activations.  Returns false, with every copy drained, when *skip is set.
+template <int TBW, int NS, int KS, class Rows, int GPS, bool PDL>
+__device__ __forceinline__ bool q4_gemm_core(const Rows& rows, const __half* __restrict__ Xhi,
                                              const __half* __restrict__ Xlo, int ldx, int K, int T, int t0,
-                                             unsigned char* smem, float (&acc)[TBW][4]) {
+                                             unsigned char* smem, float (&acc)[TBW][4], const int* skip) {
   using SG = GemmStage<TBW, GPS>;
   constexpr int kStages = NS;
   constexpr int BT = SG::BT;
@@ -191,15 +197,18 @@ __device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __r
     if (KS == 1) __syncthreads();
     else asm volatile("bar.sync %0, %1;" ::"r"(1 + wg), "r"(kGemmThreads) : "memory");
   };
-  auto issue = [&](int i, int st) {
+  // weights: 64 rows x GPS x 16 B; scales: 64 x GPS floats; activations: BT rows x GPS x 64 B x 2
+  auto issue_w = [&](int i, int st) {
     const int g0 = gbeg + (wg + i * KS) * GPS;
-    // weights: 64 rows x GPS x 16 B; scales: 64 x GPS floats; activations: BT rows x GPS x 64 B x 2
     for (int j = lt; j < kGemmRows * GPS; j += kGemmThreads) {
       const int r = j / GPS, q = j % GPS, g = g0 + q;
       const bool ok = rows.valid(r) && g < gend;
       cp_async16(w_s(st) + r * SG::WROW + q * 16, rows.wrow(r) + min(g, gend - 1) * 16, ok);
       cp_async4(s_s(st) + r * GPS + q, rows.srow(r) + min(g, gend - 1), ok);
     }
+  };
+  auto issue_x = [&](int i, int st) {
+    const int g0 = gbeg + (wg + i * KS) * GPS;
     for (int j = lt; j < BT * 4 * GPS; j += kGemmThreads) {  // 4 x 16 B per token row and group
       const int tk = j / (4 * GPS), c = j % (4 * GPS), g = g0 + (c >> 2);
       const int tok = t0 + tk;
@@ -209,15 +218,36 @@ __device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __r
       cp_async16(xl_s(st) + tk * SG::XROW + c * 8, Xlo + off, ok);
     }
   };
+  auto issue = [&](int i, int st) {
+    issue_w(i, st);
+    issue_x(i, st);
+  };
 #pragma unroll
   for (int b = 0; b < TBW; ++b)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[b][i] = 0.f;
-  // prologue
+  // prologue (commit group s holds stage s's activations; group 0 also every prologue weight copy)
+  if constexpr (PDL) {
 #pragma unroll
-  for (int s = 0; s < kStages - 1; ++s) {
-    if (s < niter) issue(s, s);
-    cp_async_commit();
+    for (int s = 0; s < kStages - 1; ++s)
+      if (s < niter) issue_w(s, s);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (skip && *skip) {
+      cp_async_commit();
+      cp_async_wait<0>();
+      return false;
+    }
+#pragma unroll
+    for (int s = 0; s < kStages - 1; ++s) {
+      if (s < niter) issue_x(s, s);
+      cp_async_commit();
+    }
+  } else {
+#pragma unroll
+    for (int s = 0; s < kStages - 1; ++s) {
+      if (s < niter) issue(s, s);
+      cp_async_commit();
+    }
   }
   for (int i = 0; i < niter; ++i) {
     cp_async_wait<kStages - 2>();
@@ -272,6 +302,7 @@ __device__ __forceinline__ void q4_gemm_core(const Rows& rows, const __half* __r
           for (int i = 0; i < 4; ++i) acc[b][i] += red[((size_t)(w - 1) * kGemmThreads + lt) * TBW * 4 + b * 4 + i];
     }
   }
+  return true;
 }
 
 template <int TBW, int NS = kStages, int KS = 1, int GPS = 1>

@@ -1,9 +1,9 @@
 #!/usr/bin/env python3
 """Regenerate the golden fixtures in this directory from the reference's own Python code.
 
-Run in a container where the reference project is mounted (default /root/reference, or set
-MLLM_REFERENCE_DIR).  It needs torch, transformers and tokenizers; the tests that read the fixtures
-need none of them and never read the reference project.
+Run in a container where the reference project is mounted; MLLM_REFERENCE_DIR names its root
+(the default below is the mount point of the build container).  It needs torch, transformers and
+tokenizers; the tests that read the fixtures need none of them and never read the reference project.
 
 Fixtures:
   q4_pack.npz          float32 matrices (seeded, plus edge cases) and what the reference's
