@@ -43,6 +43,10 @@ L2_BYTES = 126 * 1024 * 1024
 # kernels: 132,081,664 B).
 # ncu flushes the caches before each captured kernel, as the bench flushes L2 before each call.
 DECODE_TRAFFIC_PER_CALL = {"config1 petitgpt b1 p64 n128": 549_205_504}
+# dram__bytes_read.sum + dram__bytes_write.sum of one cold gemv_q4_bulk_kernel launch on the lm_head
+# shape (49152 x 576, M = 1), from an ncu capture of `microllm-lab_b200/profile_case.py gemv`: exactly the
+# 17,694,720 bytes of nibbles and scales plus the activations.
+GEMV_LM_TRAFFIC_PER_LAUNCH = 17_712_384
 
 
 def pkg():
@@ -335,9 +339,11 @@ GEMV_SHAPES = [(576, 576), (192, 576), (1536, 576), (576, 1536), (960, 960), (25
 
 def run_gemv(args):
     """isolated Q4 GEMV / skinny GEMM on the config's shapes and M in {1, 5, 9, 16}.
-    For every point both device paths are timed (CUDA-core GEMV, tensor-core GEMM) over a CUDA graph of
-    back-to-back launches: hot = one weight matrix reused, cold = a rotating set of copies larger than
-    L2.  GB/s counts packed nibbles + scales (out*in/2 + out*in/32*4 bytes) per launch."""
+    For every point both entry points are timed over a CUDA graph of back-to-back launches:
+    `gemv` = mllm_gemv_q4 (CUDA-core, tensor-core or bulk-staged tensor-core kernel, picked per shape) and
+    `gemm` = mllm_gemm_q4 (the token-batch tensor-core GEMM); hot = one weight matrix reused, cold = a
+    rotating set of copies larger than L2.  GB/s counts packed nibbles + scales (out*in/2 + out*in/32*4
+    bytes) per launch."""
     import torch
     ws, rank, local = dist_setup()
     if rank != 0:
@@ -364,7 +370,7 @@ def run_gemv(args):
                 x = torch.from_numpy(rng.standard_normal((M, C), dtype=np.float32)).cuda()
                 y = torch.empty((M, R), device="cuda")
                 point = {"shape": f"{R}x{C}", "M": M, "weight_bytes": bytes_w}
-                for path, fn in (("cuda_core", P.gemv_q4_device), ("tensor", P.gemm_q4_device)):
+                for path, fn in (("gemv", P.gemv_q4_device), ("gemm", P.gemm_q4_device)):
                     for mode in ("hot", "cold"):
                         n = reps if mode == "hot" else min(ncopy, 4096)
                         idx = [0] * n if mode == "hot" else list(range(n))
@@ -386,13 +392,13 @@ def run_gemv(args):
                         e1.record()
                         e1.synchronize()
                         us = e0.elapsed_time(e1) * 1e3 / (args.steps * n)
-                        launches += args.steps * n * (1 if path == "cuda_core" else 2)
+                        launches += args.steps * n * (1 if path == "gemv" else 2)
                         point[f"{path}_{mode}_us"] = us
                         point[f"{path}_{mode}_gbs"] = bytes_w / (us * 1e-6) / 1e9
                         del g
-                best = max(point["cuda_core_cold_gbs"], point["tensor_cold_gbs"])
+                best = max(point["gemv_cold_gbs"], point["gemm_cold_gbs"])
                 point["best_cold_gbs"] = best
-                point["best_hot_gbs"] = max(point["cuda_core_hot_gbs"], point["tensor_hot_gbs"])
+                point["best_hot_gbs"] = max(point["gemv_hot_gbs"], point["gemm_hot_gbs"])
                 rows.append(point)
             del pks, scs
     head = next(r for r in rows if r["shape"] == "49152x576" and r["M"] == 1)
@@ -405,7 +411,9 @@ def run_gemv(args):
                    "M": [1, 5, 9, 16], "timing": "CUDA graph of back-to-back launches, events around replays",
                    "cold": "rotating copies, total > 2x L2"},
         "roofline": {"bound": "hbm", "achieved": head["best_cold_gbs"], "peak": hbm, "unit": "GB/s",
-                     "frac": head["best_cold_gbs"] / hbm, "peak_kind": peak_kind, "traffic": None},
+                     "frac": head["best_cold_gbs"] / hbm, "peak_kind": peak_kind,
+                     "traffic": GEMV_LM_TRAFFIC_PER_LAUNCH,
+                     "kernel": "gemv_q4_bulk_kernel<1,2> (mllm_gemv_q4 on 49152x576, M=1)"},
         "gpu_launches": launches, "points": rows, "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
