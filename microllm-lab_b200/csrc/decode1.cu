@@ -639,6 +639,8 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
   const bool gpt2 = md.arch == 1;
   const uint64_t limit = a.wait_ns ? a.wait_ns : kWaitNs;
   const size_t ofs_d = (size_t)l * a.mmax * x.s_d;
+  // attention heads live on the last NH CTAs, which have the fewest (for the PetitGPT shape, no) QKV rows
+  const int h0 = md.NH <= (int)gridDim.x ? (int)gridDim.x - md.NH : 0;
   // ---- QKV rows (wait: previous layer's x2, then norm1)
   if (rows0 < QKV) {
     Row<NWJ_D> rw;
@@ -666,7 +668,7 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
   }
   stamp(a, tag, 1 + 6 * l);
   // ---- attention (one CTA per head)
-  for (int h = blockIdx.x; h < md.NH; h += gridDim.x)
+  for (int h = (int)blockIdx.x - h0; h >= 0 && h < md.NH; h += gridDim.x)
     if (!attention(a, S, l, h, pos, tag)) return false;
   stamp(a, tag, 2 + 6 * l);
   // ---- proj rows + residual (x1)

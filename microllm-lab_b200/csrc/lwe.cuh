@@ -56,6 +56,7 @@ struct LweHost {
   int fold_norm = 1;   // llama RMSNorm folded into the GEMM epilogues (MLLM_LWE_FOLD_NORM=0: norm kernels)
   int force_tbw = 0;   // tile-size experiments (MLLM_LWE_FORCE_TBW / MLLM_LWE_FORCE_KS), 0 = automatic
   int force_ks = 0;
+  int force_kz = 0;    // split-K across CTAs (MLLM_LWE_FORCE_KZ), 0 = automatic
   int pdl = 1;         // programmatic dependent launch between the forward's kernels (MLLM_LWE_PDL=0: off)
 };
 
