@@ -827,6 +827,198 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_fc(const _
   });
 }
 
+// Wide lm_head GEMM for many rows (a batched decode step) without a logits output.  One CTA per SM:
+// the CTA's 8*TBW token rows of xh/xl stay in shared memory for the whole launch while its run of
+// 64-row vocab tiles streams through an NSW-stage cp.async pipeline, so the activations are read once
+// per CTA instead of once per vocab tile.  Warp (wr, wt) of the 4 x kLmWideWT warps takes tile rows
+// 16 wr .. 16 wr + 15 and token blocks wt, wt + kLmWideWT, ...  Each lane keeps, per token, the best
+// (value, lowest index) over the tiles it has seen; the CTA writes one partial per token to
+// pval/pidx[blockIdx.x].
+constexpr int kLmWideWT = 4;
+template <int TBW, int NSW>
+struct LmWide {
+  static constexpr int BT = 8 * TBW;
+  static constexpr int THREADS = kGemmThreads * kLmWideWT;
+  static constexpr int TBP = (TBW + kLmWideWT - 1) / kLmWideWT;  // token blocks per warp
+  static __host__ __device__ int xrow(int K) { return K + 8; }          // fp16 per staged token row
+  static __host__ __device__ int wrow(int K) { return (K >> 1) + 16; }  // bytes per staged weight row
+  static __host__ __device__ size_t stage(int K) {
+    return ((size_t)kGemmRows * wrow(K) + (size_t)kGemmRows * (K >> 5) * 4 + 15) & ~(size_t)15;
+  }
+  static __host__ __device__ size_t smem(int K) { return (size_t)2 * BT * xrow(K) * 2 + NSW * stage(K); }
+};
+
+template <int TBW, int NSW>
+__global__ void __launch_bounds__(LmWide<TBW, NSW>::THREADS, 1) lwe_gemm_lm_wide(const __grid_constant__ LweArgs a,
+                                                                                 int T, int tiles_per_cta) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  using C = LmWide<TBW, NSW>;
+  constexpr int BT = C::BT, NT = C::THREADS, TBP = C::TBP;
+  __shared__ float bvs[4 * BT];
+  __shared__ int bis[4 * BT];
+  const int V = a.m.vocab, K = a.m.D, ng = K >> 5;
+  const int XR = C::xrow(K), WR = C::wrow(K);
+  const size_t wbytes = (size_t)kGemmRows * WR, stage = C::stage(K);
+  __half* xh = reinterpret_cast<__half*>(smem);
+  __half* xl = xh + (size_t)BT * XR;
+  unsigned char* wst = reinterpret_cast<unsigned char*>(xl + (size_t)BT * XR);
+  const int ntiles = (V + kGemmRows - 1) / kGemmRows;
+  const int rt0 = blockIdx.x * tiles_per_cta, nt = max(0, min(ntiles, rt0 + tiles_per_cta) - rt0);
+  const int t0 = blockIdx.y * BT;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gid = lane >> 2, t = lane & 3;
+  const int wr = warp & 3, wt = warp >> 2;
+  const uint8_t* W = reinterpret_cast<const uint8_t*>(a.m.lm.w);
+  const float* S = a.m.lm.s;
+  auto issue_w = [&](int rt, int st) {
+    unsigned char* dst = wst + (size_t)st * stage;
+    float* sdst = reinterpret_cast<float*>(dst + wbytes);
+    const int r0 = rt * kGemmRows, cpr = K >> 5;  // 16-byte chunks per packed row
+    for (int j = tid; j < kGemmRows * cpr; j += NT) {
+      const int r = j / cpr, c = j % cpr, row = r0 + r;
+      cp_async16(dst + r * WR + c * 16, W + (size_t)min(row, V - 1) * (K >> 1) + c * 16, row < V);
+    }
+    for (int j = tid; j < kGemmRows * ng; j += NT) {
+      const int row = r0 + j / ng;
+      cp_async4(sdst + j, S + (size_t)min(row, V - 1) * ng + j % ng, row < V);
+    }
+  };
+  // weight stages first (no kernel writes them), then wait for the previous kernel, then activations
+#pragma unroll
+  for (int s = 0; s < NSW - 1; ++s) {
+    if (s < nt) issue_w(rt0 + s, s);
+    cp_async_commit();
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (a.skip && *a.skip) {  // a finished speculative loop replays as no-ops
+    cp_async_wait<0>();
+    return;
+  }
+  {
+    const int cpx = K >> 3;  // 16-byte chunks per token row
+    for (int j = tid; j < BT * cpx; j += NT) {
+      const int r = j / cpx, c = j % cpx, tok = t0 + r;
+      const size_t off = (size_t)min(tok, T - 1) * a.ldx + c * 8;
+      cp_async16(xh + r * XR + c * 8, a.xh + off, tok < T);
+      cp_async16(xl + r * XR + c * 8, a.xl + off, tok < T);
+    }
+    cp_async_commit();
+  }
+  // this warp's token blocks: b = wt + kLmWideWT * j, j < TBP (b < TBW)
+  float bv[TBP][2];
+  int bi[TBP][2];
+#pragma unroll
+  for (int j = 0; j < TBP; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      bv[j][e] = -INFINITY;
+      bi[j][e] = 0x7fffffff;
+    }
+  const int ia = wr * 16 + gid, ib = ia + 8;
+  for (int i = 0; i < nt; ++i) {
+    if (i == 0) cp_async_wait<0>();
+    else cp_async_wait<NSW - 2>();
+    __syncthreads();  // tile i has landed everywhere; every warp is done with tile i - 1's stage
+    {
+      const int in = i + NSW - 1;
+      if (in < nt) issue_w(rt0 + in, in % NSW);
+      cp_async_commit();
+    }
+    const unsigned char* ws = wst + (size_t)(i % NSW) * stage;
+    const float* ss = reinterpret_cast<const float*>(ws + wbytes);
+    const uint32_t* wr0 = reinterpret_cast<const uint32_t*>(ws + ia * WR);
+    const uint32_t* wr1 = reinterpret_cast<const uint32_t*>(ws + ib * WR);
+    float acc[TBP][4];
+#pragma unroll
+    for (int j = 0; j < TBP; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    for (int g = 0; g < ng; ++g) {
+      uint32_t a0[4], a1[4];
+      load_a_frag(wr0 + 4 * g, wr1 + 4 * g, 0, t, a0);
+      load_a_frag(wr0 + 4 * g, wr1 + 4 * g, 1, t, a1);
+      const float sc0 = ss[ia * ng + g], sc1 = ss[ib * ng + g];
+#pragma unroll
+      for (int j = 0; j < TBP; ++j) {
+        const int b = wt + kLmWideWT * j;
+        if (b >= TBW) break;
+        const int xo = (b * 8 + (lane & 7)) * XR + g * 32 + (lane >> 3) * 8;
+        uint32_t bh[4], bl[4];
+        ldsm_x4(bh, xh + xo);
+        ldsm_x4(bl, xl + xo);
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(d, a0, bh[0], bh[1]);
+        mma16816(d, a0, bl[0], bl[1]);
+        mma16816(d, a1, bh[2], bh[3]);
+        mma16816(d, a1, bl[2], bl[3]);
+        acc[j][0] = fmaf(sc0, d[0], acc[j][0]);
+        acc[j][1] = fmaf(sc0, d[1], acc[j][1]);
+        acc[j][2] = fmaf(sc1, d[2], acc[j][2]);
+        acc[j][3] = fmaf(sc1, d[3], acc[j][3]);
+      }
+    }
+    // this tile's candidate per (token, lane): row ia, or ib when larger (ia < ib keeps ties)
+    const int ra = (rt0 + i) * kGemmRows + ia, rb = ra + 8;
+#pragma unroll
+    for (int j = 0; j < TBP; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float v = -INFINITY;
+        int idx = 0x7fffffff;
+        if (ra < V) {
+          v = acc[j][e];
+          idx = ra;
+        }
+        if (rb < V && acc[j][2 + e] > v) {
+          v = acc[j][2 + e];
+          idx = rb;
+        }
+        if (v > bv[j][e] || (v == bv[j][e] && idx < bi[j][e])) {
+          bv[j][e] = v;
+          bi[j][e] = idx;
+        }
+      }
+  }
+  cp_async_wait<0>();
+  // reduce over gid (lanes with the same t), then over the 4 row warps of each token block
+#pragma unroll
+  for (int j = 0; j < TBP; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int b = wt + kLmWideWT * j;
+      if (b >= TBW) break;
+      float v = bv[j][e];
+      int idx = bi[j][e];
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > v || (ov == v && oi < idx)) {
+          v = ov;
+          idx = oi;
+        }
+      }
+      if (gid == 0) {
+        bvs[wr * BT + b * 8 + 2 * t + e] = v;
+        bis[wr * BT + b * 8 + 2 * t + e] = idx;
+      }
+    }
+  __syncthreads();
+  for (int tl = tid; tl < BT; tl += NT) {
+    const int tok = t0 + tl;
+    if (tok >= T) continue;
+    float v = bvs[tl];
+    int idx = bis[tl];
+    for (int w = 1; w < 4; ++w) {
+      const float ov = bvs[w * BT + tl];
+      const int oi = bis[w * BT + tl];
+      if (ov > v || (ov == v && oi < idx)) {
+        v = ov;
+        idx = oi;
+      }
+    }
+    a.pval[(size_t)blockIdx.x * a.lm_cap + tok] = v;
+    a.pidx[(size_t)blockIdx.x * a.lm_cap + tok] = idx;
+  }
+}
+
 // lm_head GEMM over the T rows in xh/xl with a per-CTA argmax epilogue: for each token, the best
 // (value, lowest index) over the CTA's 64 vocab rows goes to pval/pidx[blockIdx.x][t].  Optional
 // logits store [t][V].
@@ -1111,8 +1303,46 @@ static cudaError_t attention_attr(int need) {
   return e;
 }
 
+// Wide lm_head GEMM (no logits): the largest token tile / pipeline depth whose shared memory fits.
+static int g_lm_wide_cap = 0;  // dynamic shared memory granted to lwe_gemm_lm_wide (0: not set up)
+template <int TBW, int NSW>
+static bool try_lm_wide(const LweArgs& a, int T, cudaStream_t st, int sms, int* nblk) {
+  using C = LmWide<TBW, NSW>;
+  const size_t sm = C::smem(a.m.D);
+  if (sm > (size_t)g_lm_wide_cap) return false;
+  const int tiles = (a.m.vocab + kGemmRows - 1) / kGemmRows;
+  const int tt = (T + C::BT - 1) / C::BT;
+  int g = std::max(1, sms / tt);
+  const int tpc = (tiles + g - 1) / g;
+  g = (tiles + tpc - 1) / tpc;
+  lwe_launch(lwe_gemm_lm_wide<TBW, NSW>, dim3(g, tt), dim3(C::THREADS), sm, st, a, T, tpc);
+  *nblk = g;
+  return true;
+}
+static bool launch_lm_wide(const LweArgs& a, int T, cudaStream_t st, int* nblk) {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return try_lm_wide<8, 3>(a, T, st, sms, nblk) || try_lm_wide<4, 3>(a, T, st, sms, nblk) ||
+         try_lm_wide<4, 2>(a, T, st, sms, nblk) || try_lm_wide<2, 2>(a, T, st, sms, nblk);
+}
+
 // One-time kernel attributes: the attention's shared memory grows with kv_len.
 cudaError_t lwe_setup(int kv_len) {
+  {
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    const int cap = optin - 4096;  // room for the kernel's static reduction arrays
+    if (smem_attr(lwe_gemm_lm_wide<8, 3>, cap) == cudaSuccess && smem_attr(lwe_gemm_lm_wide<4, 3>, cap) == cudaSuccess &&
+        smem_attr(lwe_gemm_lm_wide<4, 2>, cap) == cudaSuccess && smem_attr(lwe_gemm_lm_wide<2, 2>, cap) == cudaSuccess)
+      g_lm_wide_cap = cap;
+    else
+      (void)cudaGetLastError();
+  }
   cudaError_t e = gemm_attrs<2>();
   if (e == cudaSuccess) e = gemm_attrs<4>();
   if (e == cudaSuccess) e = gemm_attrs<8>();
@@ -1187,9 +1417,11 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
   if (lm_T > 0) {
     lwe_launch(lwe_norm_split, dim3(lm_T), dim3(128), 0, st, a, lm_T, md.norm_f,
                (const int*)(lm_from_src ? a.lm_src : nullptr));
-    const int tiles = (md.vocab + kGemmRows - 1) / kGemmRows;
-    LWE_GEMM_LM(md.vocab, lm_T, a, lm_T, logits);
-    lwe_launch(lwe_argmax_reduce, dim3((lm_T + 3) / 4), dim3(128), 0, st, a, lm_T, tiles);
+    // many rows without logits (a batched decode step): the persistent wide GEMM, one partial per CTA
+    int nblk = (md.vocab + kGemmRows - 1) / kGemmRows;
+    if (!(logits == nullptr && lm_T >= kLmWideRows && h.lm_wide && launch_lm_wide(a, lm_T, st, &nblk)))
+      LWE_GEMM_LM(md.vocab, lm_T, a, lm_T, logits);
+    lwe_launch(lwe_argmax_reduce, dim3((lm_T + 3) / 4), dim3(128), 0, st, a, lm_T, nblk);
   }
   return cudaGetLastError();
 }

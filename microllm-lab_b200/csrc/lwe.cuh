@@ -43,6 +43,7 @@ struct LweArgs {
   int* skctr;             // [kLweSplitKTiles] zeroed split-K tile counters
 };
 constexpr size_t kLweSplitKBytes = size_t(8) << 20;
+constexpr int kLmWideRows = 64;  // lm rows from which the persistent lm_head GEMM is used
 constexpr int kLweSplitAttnRows = 16;  // forwards of at most this many tokens use the position-split attention
 constexpr int kLweSplitKTiles = 16384;
 
@@ -58,6 +59,7 @@ struct LweHost {
   int force_ks = 0;
   int force_kz = 0;    // split-K across CTAs (MLLM_LWE_FORCE_KZ), 0 = automatic
   int pdl = 1;         // programmatic dependent launch between the forward's kernels (MLLM_LWE_PDL=0: off)
+  int lm_wide = 1;     // persistent lm_head GEMM for many rows without logits (MLLM_LWE_LM_WIDE=0: off)
 };
 
 // one_per_slot: every token belongs to a different slot (a batched decode step), which lets the

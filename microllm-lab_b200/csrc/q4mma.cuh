@@ -38,6 +38,16 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Four 8x8 fp16 matrices from shared memory: lane i gives the address of row i % 8 of matrix i / 8; lane
+// (gid, t) receives elements (gid, 2t), (gid, 2t + 1) of each, i.e. for a token-major tile with the
+// matrices at k offsets 0, 8, 16, 24 the B fragments of two k16 steps.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* row) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(row);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -269,13 +279,16 @@ __device__ __forceinline__ bool q4_gemm_core(const Rows& rows, const __half* __r
       load_a_frag(wr0, wr1, 1, t, a1);
 #pragma unroll
       for (int b = 0; b < TBW; ++b) {
-        const __half* xh = xh_s(st) + (b * 8 + gid) * SG::XROW + q * 32 + 2 * t;
-        const __half* xl = xl_s(st) + (b * 8 + gid) * SG::XROW + q * 32 + 2 * t;
+        // B fragments of both k16 steps, hi and lo: two ldmatrix.x4 (rows at lane % 8, k blocks at lane / 8)
+        const int xo = (b * 8 + (lane & 7)) * SG::XROW + q * 32 + (lane >> 3) * 8;
+        uint32_t bh[4], bl[4];
+        ldsm_x4(bh, xh_s(st) + xo);
+        ldsm_x4(bl, xl_s(st) + xo);
         float d[4] = {0.f, 0.f, 0.f, 0.f};
-        mma16816(d, a0, *reinterpret_cast<const uint32_t*>(xh), *reinterpret_cast<const uint32_t*>(xh + 8));
-        mma16816(d, a0, *reinterpret_cast<const uint32_t*>(xl), *reinterpret_cast<const uint32_t*>(xl + 8));
-        mma16816(d, a1, *reinterpret_cast<const uint32_t*>(xh + 16), *reinterpret_cast<const uint32_t*>(xh + 24));
-        mma16816(d, a1, *reinterpret_cast<const uint32_t*>(xl + 16), *reinterpret_cast<const uint32_t*>(xl + 24));
+        mma16816(d, a0, bh[0], bh[1]);
+        mma16816(d, a0, bl[0], bl[1]);
+        mma16816(d, a1, bh[2], bh[3]);
+        mma16816(d, a1, bl[2], bl[3]);
         acc[b][0] = fmaf(sc0, d[0], acc[b][0]);
         acc[b][1] = fmaf(sc0, d[1], acc[b][1]);
         acc[b][2] = fmaf(sc1, d[2], acc[b][2]);

@@ -72,6 +72,31 @@ def test_batch_matches_per_sequence_oracle(batch_models, name):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("name", ["tiny-llama", "ref-llama"])
+def test_batch_wide_lm_head(cuda_ok, name):
+    """96 sequences take the persistent lm_head GEMM (>= 64 rows, no logits): two token tiles, the
+    second partial; ref-llama's 96-id vocab also ends in a partial row tile.  Every sequence equals the
+    oracle, and the engine without the wide GEMM (MLLM_LWE_LM_WIDE=0)."""
+    data = _data(name)
+    om = O.OracleModel(data)
+    eng = _engine(data, max_slots=96)
+    ref_eng = _engine(data, env={"MLLM_LWE_LM_WIDE": "0"}, max_slots=96)
+    try:
+        V = eng.cfg["vocabSize"]
+        seqs = _prompts(V, [1 + (7 * i) % 23 for i in range(96)], 300)
+        res, st = eng.generateBatch(seqs, maxNewTokens=12, eosId=-1)
+        res0, _ = ref_eng.generateBatch(seqs, maxNewTokens=12, eosId=-1)
+        assert st["nSeq"] == 96
+        for i, (q, r, r0) in enumerate(zip(seqs, res, res0)):
+            assert r["generatedIds"] == r0["generatedIds"], i
+            if i % 8 == 0:  # the oracle on every eighth sequence
+                assert r["generatedIds"] == om.generate(q, 12, eos=-1)["generatedIds"], i
+    finally:
+        eng.destroy()
+        ref_eng.destroy()
+
+
+@pytest.mark.gpu
 def test_batch_single_sequence_equals_generate(batch_models):
     data, eng, om = batch_models["ref-llama"]
     ids = pkg().seeded_prompt(20, eng.cfg["vocabSize"], 50)
