@@ -264,10 +264,18 @@ __device__ __forceinline__ void load_gains(const float* g, int D, bool ln, float
 
 constexpr int kProfLayerA = 15;
 
-// Causal attention of head h for the token at `pos` (engine/infer.js:422-495): RoPE on q and on
-// the new k, cache write by the group's first head, then online softmax over positions 0..pos with
-// 4 lanes per position (16 dims each).  Publishes the head's 64 outputs.
-__device__ __noinline__ bool attention(const RunArgs& a, const Lay& S, int l, int h, int pos, uint32_t tag) {
+// Causal attention of head h for the token at `pos` (engine/infer.js:422-495), split over `ns` CTAs
+// by position: split sp covers positions [sp * P, (sp + 1) * P) of 0..pos, P = ceil((pos + 1) / ns).
+// RoPE on q and on the new k, cache write by the last split of the group's first head, then online
+// softmax over the split's positions with 4 lanes per position (16 dims each).  With one split the CTA
+// publishes the head's 64 outputs; otherwise every split but the first publishes its partial
+// (max, sum, 64 unnormalised outputs) to the partials area after the candidate words, and the first split
+// merges them and publishes.
+// SPLIT = false compiles the single-split form only (contexts of at most two rounds of positions).
+template <bool SPLIT>
+__device__ __noinline__ bool attention(const RunArgs& a, const Lay& S, int l, int unit, int pos, uint32_t tag) {
+  const int h = SPLIT ? unit & 0xFF : unit;  // head, split, splits
+  const int sp = SPLIT ? (unit >> 8) & 0xFF : 0, ns = SPLIT ? unit >> 16 : 1;
   const ModelDev& md = a.m;
   const ExchangeDev& x = a.x;
   const int D = md.D, NKV = md.NKV, rep = md.NH / md.NKV, kvh = h / rep;
@@ -324,13 +332,14 @@ __device__ __noinline__ bool attention(const RunArgs& a, const Lay& S, int l, in
   }
   __syncthreads();
   const size_t kv_base = ((size_t)l * NKV + kvh) * md.kv_len;
-  if (h % rep == 0 && threadIdx.x < 128) {  // engine/infer.js:457-464
+  if (h % rep == 0 && sp == ns - 1 && threadIdx.x < 128) {  // engine/infer.js:457-464
     const int d = threadIdx.x & 63;
     if (threadIdx.x < 64) a.kc[(kv_base + pos) * 64 + d] = kl[d];
     else a.vc[(kv_base + pos) * 64 + d] = vl[d];
   }
   const int qd = lane & 3, pg = lane >> 2;
-  const int npos = pos + 1;
+  const int span = (pos + ns) / ns;  // ceil((pos + 1) / ns)
+  const int p_lo = sp * span, p_hi = min(pos + 1, p_lo + span);
   float mrun = -INFINITY, lrun = 0.f, o[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) o[i] = 0.f;
@@ -371,15 +380,15 @@ __device__ __noinline__ bool attention(const RunArgs& a, const Lay& S, int l, in
     part += __shfl_xor_sync(0xffffffffu, part, 2);
     return valid ? part * 0.125f : -INFINITY;  // 1/sqrt(64), exact (engine/infer.js:466)
   };
-  for (int r0 = warp * 8; r0 < npos; r0 += 2 * kWarps * 8) {
+  for (int r0 = p_lo + warp * 8; r0 < p_hi; r0 += 2 * kWarps * 8) {
     const int pA = r0 + pg, pB = r0 + kWarps * 8 + pg;
     float4 kA[4], vA[4], kB[4], vB[4];
     fetch(pA, kA, vA);
     fetch(pB, kB, vB);
-    const float sA = score(kA, pA < npos), sB = score(kB, pB < npos);
+    const float sA = score(kA, pA < p_hi), sB = score(kB, pB < p_hi);
     const float newm = fmaxf(mrun, warp_max(fmaxf(sA, sB)));
-    const float eA = pA < npos ? expf(sA - newm) : 0.f;
-    const float eB = pB < npos ? expf(sB - newm) : 0.f;
+    const float eA = pA < p_hi ? expf(sA - newm) : 0.f;
+    const float eB = pB < p_hi ? expf(sB - newm) : 0.f;
     const float corr = mrun == -INFINITY ? 0.f : expf(mrun - newm);
     lrun = fmaf(lrun, corr, warp_sum(qd == 0 ? eA + eB : 0.f));
 #pragma unroll
@@ -421,10 +430,58 @@ __device__ __noinline__ bool attention(const RunArgs& a, const Lay& S, int l, in
         r1 = fmaf(pw[4 + 2 * lane + 1], f, r1);
       }
     }
-    const float inv = 1.f / Ls;
-    uint64_t* dst = x.att + (size_t)l * a.mmax * x.s_d + h * 64;
-    ll_store(dst + 2 * lane, tag, r0 * inv);
-    ll_store(dst + 2 * lane + 1, tag, r1 * inv);
+    if (ns == 1) {
+      const float inv = 1.f / Ls;
+      uint64_t* dst = x.att + (size_t)l * a.mmax * x.s_d + h * 64;
+      ll_store(dst + 2 * lane, tag, r0 * inv);
+      ll_store(dst + 2 * lane + 1, tag, r1 * inv);
+    } else if (sp > 0) {
+      // partial of this split: words 0 max, 1 sum, 2-3 zero, 4 + d unnormalised output d
+      uint64_t* dst = x.cand + attn_partials_offset(gridDim.x, a.mmax) + (((size_t)l * md.NH + h) * kAttnSplits + sp) * kAttnPartWords;
+      if (lane == 0) {
+        ll_store(dst, tag, M);
+        ll_store(dst + 1, tag, Ls);
+        ll_store(dst + 2, tag, 0.f);
+        ll_store(dst + 3, tag, 0.f);
+      }
+      ll_store(dst + 4 + 2 * lane, tag, r0);
+      ll_store(dst + 5 + 2 * lane, tag, r1);
+    } else {
+      S.wpart[0] = M;  // lane-uniform values; lanes keep r0, r1
+      S.wpart[1] = Ls;
+      S.wpart[4 + 2 * lane] = r0;
+      S.wpart[5 + 2 * lane] = r1;
+    }
+  }
+  if (ns > 1 && sp == 0) {
+    // first split: wait for the other splits' partials, merge, publish the head's outputs
+    __syncthreads();
+    float* part = S.act + 256;
+    const uint64_t* src = x.cand + attn_partials_offset(gridDim.x, a.mmax) +
+                          (((size_t)l * md.NH + h) * kAttnSplits + 1) * kAttnPartWords;
+    if (!poll_vec(src, part, (ns - 1) * kAttnPartWords, tag, a.err, a.wait_ns ? a.wait_ns : kWaitNs,
+                  a.poll_sleep_ns))
+      return false;
+    if (warp == 0) {
+      float M = S.wpart[0];
+      for (int q = 0; q < ns - 1; ++q)
+        if (part[q * kAttnPartWords + 1] > 0.f) M = fmaxf(M, part[q * kAttnPartWords]);
+      const float f0 = expf(S.wpart[0] - M);
+      float Ls = S.wpart[1] * f0, r0 = S.wpart[4 + 2 * lane] * f0, r1 = S.wpart[5 + 2 * lane] * f0;
+      for (int q = 0; q < ns - 1; ++q) {
+        const float* pq = part + q * kAttnPartWords;
+        if (pq[1] > 0.f) {
+          const float f = expf(pq[0] - M);
+          Ls = fmaf(pq[1], f, Ls);
+          r0 = fmaf(pq[4 + 2 * lane], f, r0);
+          r1 = fmaf(pq[5 + 2 * lane], f, r1);
+        }
+      }
+      const float inv = 1.f / Ls;
+      uint64_t* dst = x.att + (size_t)l * a.mmax * x.s_d + h * 64;
+      ll_store(dst + 2 * lane, tag, r0 * inv);
+      ll_store(dst + 2 * lane + 1, tag, r1 * inv);
+    }
   }
   __syncthreads();
   return true;
@@ -627,7 +684,7 @@ constexpr int kProfLayer = 15;
   if (l == kProfLayer) stamp(a, tag, 200 + (idx))
 
 // One layer of the single-token forward at position `pos`.
-template <int NWJ_D, int NWJ_F>
+template <int NWJ_D, int NWJ_F, bool SPLIT>
 __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int pos, uint32_t tag) {
   const ModelDev& md = a.m;
   const ExchangeDev& x = a.x;
@@ -639,8 +696,6 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
   const bool gpt2 = md.arch == 1;
   const uint64_t limit = a.wait_ns ? a.wait_ns : kWaitNs;
   const size_t ofs_d = (size_t)l * a.mmax * x.s_d;
-  // attention heads live on the last NH CTAs, which have the fewest (for the PetitGPT shape, no) QKV rows
-  const int h0 = md.NH <= (int)gridDim.x ? (int)gridDim.x - md.NH : 0;
   // ---- QKV rows (wait: previous layer's x2, then norm1)
   if (rows0 < QKV) {
     Row<NWJ_D> rw;
@@ -667,9 +722,23 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
     __syncthreads();
   }
   stamp(a, tag, 1 + 6 * l);
-  // ---- attention (one CTA per head)
-  for (int h = (int)blockIdx.x - h0; h >= 0 && h < md.NH; h += gridDim.x)
-    if (!attention(a, S, l, h, pos, tag)) return false;
+  // ---- attention
+  {
+    // Attention: NH x ns units (head, position split) on the last CTAs, which have the fewest (for the
+    // PetitGPT shape, no) QKV rows.  Once one CTA would need kAttnMinRounds or more rounds of 128
+    // positions, one split per round (the merge costs an extra exchange, more than one round saves),
+    // capped by the grid, kAttnSplits and the room for the merge's partials in S.act.
+    int ns = 1;
+    if (SPLIT && md.NH <= (int)gridDim.x) {
+      ns = (pos + kAttnRound) / kAttnRound;
+      ns = ns >= kAttnMinRounds ? min(ns, kAttnSplits) : 1;
+      ns = min(ns, min((int)gridDim.x / md.NH, (act_width(md, gridDim.x) - 256) / kAttnPartWords));
+      ns = max(ns, 1);
+    }
+    const int h0 = md.NH <= (int)gridDim.x ? (int)gridDim.x - md.NH * ns : 0;
+    for (int u = (int)blockIdx.x - h0; u >= 0 && u < md.NH * ns; u += gridDim.x)
+      if (!attention<SPLIT>(a, S, l, SPLIT ? (u / ns) | ((u % ns) << 8) | (ns << 16) : u, pos, tag)) return false;
+  }
   stamp(a, tag, 2 + 6 * l);
   // ---- proj rows + residual (x1)
   if (rows0 < D) {
@@ -761,7 +830,7 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
 // The greedy decode loop on the single-token kernel.  Resumes after a prefill launch: the prompt
 // is a.ids[0..n_ids) and out_ids[0..start_gen) already holds the generated ids.  MODE_FORWARD runs
 // one forward of a.ids[0] at a.pos0 (forwardDecode).
-template <int NWJ_D, int NWJ_F>
+template <int NWJ_D, int NWJ_F, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1) decode1_kernel(const __grid_constant__ RunArgs a) {
   extern __shared__ __align__(16) float smem[];
   const ModelDev& md = a.m;
@@ -827,7 +896,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode1_kernel(const __grid_const
       __syncthreads();
     }
     for (int l = 0; l < md.n_layers; ++l)
-      if (!d1::layer<NWJ_D, NWJ_F>(a, S, l, pos, tag)) return;
+      if (!d1::layer<NWJ_D, NWJ_F, SPLIT>(a, S, l, pos, tag)) return;
     const int next = d1::lm_head<NWJ_D>(a, S, tag, f & 1, gen_mode && md.arch == 1, S.hist + n, gen,
                                           gen_mode ? nullptr : a.logits);
     if (next < 0) return;
@@ -869,16 +938,17 @@ size_t decode1_smem_bytes(const ModelDev& md, int grid, int lm_rpc) {
 
 typedef void (*DecodeFn)(const RunArgs);
 
-DecodeFn pick_decode1_kernel(int D, int FF) {
+// split: the variant whose attention splits long contexts over several CTAs per head.
+DecodeFn pick_decode1_kernel(int D, int FF, bool split) {
   const int nd = (D / 8 + 31) / 32, nf = (FF / 8 + 31) / 32;
 #ifndef MLLM_FAST_BUILD
-  if (nd <= 1 && nf <= 2) return decode1_kernel<1, 2>;
+  if (nd <= 1 && nf <= 2) return split ? decode1_kernel<1, 2, true> : decode1_kernel<1, 2, false>;
 #endif
-  if (nd <= 3 && nf <= 6) return decode1_kernel<3, 6>;
+  if (nd <= 3 && nf <= 6) return split ? decode1_kernel<3, 6, true> : decode1_kernel<3, 6, false>;
 #ifndef MLLM_FAST_BUILD
-  if (nd <= 3 && nf <= 12) return decode1_kernel<3, 12>;
-  if (nd <= 4 && nf <= 10) return decode1_kernel<4, 10>;
-  if (nd <= 4 && nf <= 16) return decode1_kernel<4, 16>;
+  if (nd <= 3 && nf <= 12) return split ? decode1_kernel<3, 12, true> : decode1_kernel<3, 12, false>;
+  if (nd <= 4 && nf <= 10) return split ? decode1_kernel<4, 10, true> : decode1_kernel<4, 10, false>;
+  if (nd <= 4 && nf <= 16) return split ? decode1_kernel<4, 16, true> : decode1_kernel<4, 16, false>;
 #endif
   return nullptr;
 }

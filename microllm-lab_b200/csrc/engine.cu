@@ -30,7 +30,7 @@ size_t decode_smem_bytes(const ModelDev& md, int srows, int grid);
 size_t decode1_smem_bytes(const ModelDev& md, int grid, int lm_rpc);
 typedef void (*DecodeFn)(const RunArgs);
 DecodeFn pick_decode_kernel(int D, int FF, bool multi);
-DecodeFn pick_decode1_kernel(int D, int FF);
+DecodeFn pick_decode1_kernel(int D, int FF, bool split);
 void set_global_error(const char* msg);
 }  // namespace mllm
 
@@ -68,6 +68,7 @@ struct mllm_engine {
   ExchangeDev ex{};
   DecodeFn kernel_multi = nullptr;   // prefill chunks, verify forwards, speculation
   DecodeFn kernel_single = nullptr;  // one token per forward: the greedy decode loop
+  DecodeFn kernel_single_split = nullptr;  // the same with position-split attention (long contexts)
   int grid = 0, mmax = 0;
   size_t smem_multi = 0, smem_single = 0;
   cudaStream_t stream = nullptr;     // launches go here
@@ -253,7 +254,7 @@ int launch(mllm_engine* e, RunArgs& a, int max_forwards, bool multi, bool resume
     CUDA_TRY(e, cudaMemset(e->ex.x1, 0, L * M * e->ex.s_d * 8));
     CUDA_TRY(e, cudaMemset(e->ex.a, 0, L * M * e->ex.s_ff * 8));
     CUDA_TRY(e, cudaMemset(e->ex.x2, 0, L * M * e->ex.s_d * 8));
-    CUDA_TRY(e, cudaMemset(e->ex.cand, 0, (size_t)2 * e->grid * M * 4 * 8));
+    CUDA_TRY(e, cudaMemset(e->ex.cand, 0, (attn_partials_offset(e->grid, (int)M) + attn_partials_words(L, e->md.NH)) * 8));
     e->tag = 1;
   }
   a.base_tag = e->tag;
@@ -268,7 +269,11 @@ int launch(mllm_engine* e, RunArgs& a, int max_forwards, bool multi, bool resume
     CUDA_TRY(e, cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream));
     CUDA_TRY(e, cudaMemsetAsync(e->d_status, 0, ST_WORDS * sizeof(int32_t), e->stream));
   }
-  DecodeFn k = multi ? e->kernel_multi : e->kernel_single;
+  // the single-token kernel with position-split attention only when a position of the call can need
+  // kAttnMinRounds rounds of the attention loop
+  const int maxpos = a.mode == MODE_GENERATE ? a.n_ids + a.max_new : a.pos0 + 1;
+  const bool split = maxpos > kAttnRound * (kAttnMinRounds - 1);
+  DecodeFn k = multi ? e->kernel_multi : split ? e->kernel_single_split : e->kernel_single;
   const size_t smem = multi ? e->smem_multi : e->smem_single;
   void* args[] = {&a};
   cudaError_t lst = cudaLaunchCooperativeKernel((void*)k, e->grid, kThreads, args, smem, e->stream);
@@ -534,8 +539,9 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   md.max_seq = p.max_seq;
   md.kv_len = kv_len > 0 ? std::min(kv_len, p.max_seq) : p.max_seq;
   e->kernel_multi = pick_decode_kernel(md.D, md.FF, true);
-  e->kernel_single = pick_decode1_kernel(md.D, md.FF);
-  if (!e->kernel_multi || !e->kernel_single) return bad(MLLM_ERR_UNSUPPORTED, "dModel/dFf beyond the kernel limits (1024 / 4096)");
+  e->kernel_single = pick_decode1_kernel(md.D, md.FF, false);
+  e->kernel_single_split = pick_decode1_kernel(md.D, md.FF, true);
+  if (!e->kernel_multi || !e->kernel_single || !e->kernel_single_split) return bad(MLLM_ERR_UNSUPPORTED, "dModel/dFf beyond the kernel limits (1024 / 4096)");
   mllm_engine* E = e.get();
   auto relay = [&](int rc) {
     if (rc != MLLM_OK) g_create_error = E->err;
@@ -613,7 +619,7 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   }
   e->smem_single = decode1_smem_bytes(md, e->grid, e->lm_rpc);
   if (e->smem_multi > smem_cap) return bad(MLLM_ERR_UNSUPPORTED, "model does not fit the shared-memory budget");
-  for (DecodeFn k : {e->kernel_multi, e->kernel_single}) {
+  for (DecodeFn k : {e->kernel_multi, e->kernel_single, e->kernel_single_split}) {
     // The limit is an attribute of the kernel function, shared by every engine that uses the same
     // instantiation, so it is set to the device maximum rather than to this engine's need.
     if (cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_cap) != cudaSuccess)
@@ -633,14 +639,14 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
     int rc;
     if ((rc = dev_alloc(E, &x.qkv, LM * x.s_qkv * 8)) || (rc = dev_alloc(E, &x.att, LM * x.s_d * 8)) ||
         (rc = dev_alloc(E, &x.x1, LM * x.s_d * 8)) || (rc = dev_alloc(E, &x.a, LM * x.s_ff * 8)) ||
-        (rc = dev_alloc(E, &x.x2, LM * x.s_d * 8)) || (rc = dev_alloc(E, &x.cand, (size_t)2 * e->grid * mmax * 4 * 8)))
+        (rc = dev_alloc(E, &x.x2, LM * x.s_d * 8)) || (rc = dev_alloc(E, &x.cand, (attn_partials_offset(e->grid, mmax) + attn_partials_words(L, md.NH)) * 8)))
       return relay(rc);
     cudaMemset(x.qkv, 0, LM * x.s_qkv * 8);
     cudaMemset(x.att, 0, LM * x.s_d * 8);
     cudaMemset(x.x1, 0, LM * x.s_d * 8);
     cudaMemset(x.a, 0, LM * x.s_ff * 8);
     cudaMemset(x.x2, 0, LM * x.s_d * 8);
-    cudaMemset(x.cand, 0, (size_t)2 * e->grid * mmax * 4 * 8);
+    cudaMemset(x.cand, 0, (attn_partials_offset(e->grid, mmax) + attn_partials_words(L, md.NH)) * 8);
   }
   // ---- per-slot KV caches (engine/infer.js:348-358 layout per layer: [nKv][maxSeq][hd])
   e->slots.resize(max_slots);

@@ -35,13 +35,26 @@ struct ModelDev {
 
 // Exchange buffers (8-byte tagged words).  Each is [n_layers][mmax][stride] with strides padded to
 // 32 words; `cand` is [2][grid][mmax][4].
+// Single-token attention split over positions: at most kAttnSplits CTAs per head, one per kAttnRound
+// positions; a split's partial is kAttnPartWords tagged words (max, sum, 2 zero, 64 outputs).
+constexpr int kAttnSplits = 16;
+constexpr int kAttnRound = 128;
+constexpr int kAttnMinRounds = 3;
+constexpr int kAttnPartWords = 68;
+// Partials of the single-token attention splits: [layers][NH][kAttnSplits][kAttnPartWords] words
+// placed right after the argmax candidate words (2 x grid x mmax x 4) in the same allocation.
+inline __host__ __device__ size_t attn_partials_offset(int grid, int mmax) { return (size_t)2 * grid * mmax * 4; }
+inline __host__ __device__ size_t attn_partials_words(int layers, int nh) {
+  return (size_t)layers * nh * kAttnSplits * kAttnPartWords;
+}
+
 struct ExchangeDev {
   uint64_t* qkv;
   uint64_t* att;
   uint64_t* x1;
   uint64_t* a;
   uint64_t* x2;
-  uint64_t* cand;
+  uint64_t* cand;  // argmax candidates, then the single-token attention partials (attn_partials_offset)
   int s_qkv, s_d, s_ff;  // row strides in words
 };
 

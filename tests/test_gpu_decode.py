@@ -107,6 +107,43 @@ def test_generate_matches_oracle(models, name):
     assert len(set(r["generatedIds"])) > 3  # the test model does not sit in a one-token loop
 
 
+LONG_CFGS = {
+    # GQA 3:1 and 6:2, and GPT-2 (no RoPE): contexts of several 128-position attention splits
+    "llama-3-1": dict(arch="llama", vocabSize=512, nLayers=2, dModel=192, nHeads=3, nKvHeads=1, dFf=320,
+                      maxSeqLen=640, ropeTheta=10000.0),
+    "llama-6-2": dict(arch="llama", vocabSize=384, nLayers=2, dModel=384, nHeads=6, nKvHeads=2, dFf=256,
+                      maxSeqLen=640, ropeTheta=10000.0),
+    "gpt2": dict(arch="gpt2", vocabSize=640, nLayers=2, dModel=128, nHeads=2, nKvHeads=2, dFf=512, maxSeqLen=640),
+}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", list(LONG_CFGS))
+def test_long_context_generate_matches_oracle(cuda_ok, name):
+    """Single-token decode past 128, 256, ... positions, where the attention of each head is split over
+    several CTAs and merged: the greedy stream equals the oracle's (prompt 500, 40 new ids)."""
+    P = pkg()
+    cfg = dict(LONG_CFGS[name])
+    data = P.synthetic_pgw(cfg, 21, cache_dir="/tmp/mllm_pgw_cache")
+    eng = P.CudaPetitGPT(data)
+    try:
+        om = O.OracleModel(data)
+        ids = P.seeded_prompt(500, cfg["vocabSize"], 22)
+        g = eng.generate(ids, maxNewTokens=40, eosId=-1)
+        r = om.generate(ids, 40, eos=-1)
+        assert g["generatedIds"] == r["generatedIds"]
+        # one single-token forward at position 300 (three splits), logits against the oracle
+        eng.resetCache()
+        eng.forwardPrompt(ids[:300])
+        lg = eng.forwardDecode(int(ids[300]))
+        om2 = O.OracleModel(data)
+        om2.forward_prompt(ids[:300])
+        ref = om2.forward_decode(int(ids[300]))
+        assert np.max(np.abs(np.asarray(lg) - ref)) <= 2e-2
+    finally:
+        eng.destroy()
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("k", [2, 4, 8])
 def test_speculative_generate_matches_oracle(models, k):
