@@ -301,10 +301,13 @@ __global__ void lwe_norm_split(const __grid_constant__ LweArgs a, int T, const f
 }
 
 // QKV GEMM: qkv[t][r] = W_qkv[r] . norm1(x_t) (+ bias).  With a.fold the activations are x * gain and
-// the token's 1/RMS multiplies the result.
+// the token's 1/RMS multiplies the result.  With rope != 0 the epilogue also does what lwe_rope_kv does
+// (RoPE on the q and k heads at each token's position, K/V cache rows written): a 64-row tile is one
+// head of the [q heads | k heads | v heads] layout, staged in shared memory so that both halves of each
+// rotated pair are at hand.
 template <int TBW, int KS>
 __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_qkv(const __grid_constant__ LweArgs a, int T,
-                                                                         int l) {
+                                                                         int l, int rope) {
   extern __shared__ __align__(16) unsigned char smem[];
   using C = LweTile<TBW, KS>;
   __shared__ float sinv[C::BT];
@@ -321,11 +324,43 @@ __global__ void __launch_bounds__(LweTile<TBW, KS>::THREADS) lwe_gemm_qkv(const 
     return;  // a finished speculative loop replays as no-ops
   if (!lwe_splitk<TBW>(a, acc)) return;
   if (threadIdx.x < C::BT) sinv[threadIdx.x] = a.fold && t0 + (int)threadIdx.x < T ? fold_inv(a, t0 + threadIdx.x) : 1.f;
-  __syncthreads();
+  __syncthreads();  // also: every warp is done with the pipeline buffers
+  if (!rope) {
+    lwe_tile_epi<TBW>(acc, r0, t0, R, T, [&](int r, int t, float v) {
+      v *= sinv[t - t0];
+      out[(size_t)t * R + r] = bias ? v + bias[r] : v;
+    });
+    return;
+  }
+  constexpr int TS = C::BT + 1;  // padded: conflict-free column reads
+  float* tile = reinterpret_cast<float*>(smem);  // [64][TS]
   lwe_tile_epi<TBW>(acc, r0, t0, R, T, [&](int r, int t, float v) {
     v *= sinv[t - t0];
-    out[(size_t)t * R + r] = bias ? v + bias[r] : v;
+    tile[(r - r0) * TS + (t - t0)] = bias ? v + bias[r] : v;
   });
+  __syncthreads();
+  const ModelDev& md = a.m;
+  const int D = md.D, NKV = md.NKV;
+  const int kind = r0 < D ? 0 : (r0 < D + NKV * 64 ? 1 : 2);  // q, k or v head
+  const int g = kind == 1 ? (r0 - D) >> 6 : (kind == 2 ? (r0 - D - NKV * 64) >> 6 : 0);
+  const int half = kind < 2 && md.arch == 0 ? md.rope_dim / 2 : 0;
+  for (int i = threadIdx.x; i < 64 * C::BT; i += blockDim.x) {
+    const int tl = i >> 6, d = i & 63, t = t0 + tl;
+    if (t >= T) continue;
+    float v = tile[d * TS + tl];
+    const int pos = a.pos[t];
+    if (d < 2 * half) {  // engine/infer.js:436-456, the operation order of lwe_rope_kv
+      const float* cs = md.rope_cos + (size_t)pos * md.rope_dim;
+      const float* sn = md.rope_sin + (size_t)pos * md.rope_dim;
+      if (d < half)
+        v = fmaf(-tile[(d + half) * TS + tl], sn[d], v * cs[d]);
+      else
+        v = fmaf(tile[(d - half) * TS + tl], sn[d], v * cs[d]);
+    }
+    out[(size_t)t * R + r0 + d] = v;
+    if (kind > 0)  // engine/infer.js:457-464
+      (kind == 1 ? a.kc : a.vc)[a.slot[t]][(((size_t)l * NKV + g) * md.kv_len + pos) * 64 + d] = v;
+  }
 }
 
 // RoPE on k (and on the q heads of the group) at each token's position, then the K/V cache write
@@ -1371,14 +1406,18 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
   for (int l = 0; l < nl; ++l) {
     const LayerDev& L = h.layers[l];
     a.layer = l;
-    LWE_GEMM(lwe_gemm_qkv, kGemmRows, md.QKV, md.D, T, a, T, l);
+    // A few rows (a verify forward): RoPE and the K/V cache rows in the QKV epilogue.  Long forwards keep
+    // lwe_rope_kv (the staged epilogue measured 2-3 % slower on 512- and 1,024-token prefill), and the
+    // batched decode step's attention does them itself.
+    const bool rope_epi = !one_per_slot && h.rope_epi && T <= kLweSplitAttnRows;
+    LWE_GEMM(lwe_gemm_qkv, kGemmRows, md.QKV, md.D, T, a, T, l, rope_epi ? 1 : 0);
     if (one_per_slot) {
       if (h.attn_split)
         launch_attention_split<true>(a, h, T, st);
       else
         launch_attention_t<true>(a, T, st);
     } else {
-      lwe_launch(lwe_rope_kv, dim3(T, md.NKV), dim3(64), 0, st, a, T);
+      if (!rope_epi) lwe_launch(lwe_rope_kv, dim3(T, md.NKV), dim3(64), 0, st, a, T);
       // a few tokens (a verify forward) over a long cache: split the positions across CTAs
       if (T <= kLweSplitAttnRows)
         launch_attention_split<false>(a, h, T, st);

@@ -60,6 +60,7 @@ struct LweHost {
   int force_kz = 0;    // split-K across CTAs (MLLM_LWE_FORCE_KZ), 0 = automatic
   int pdl = 1;         // programmatic dependent launch between the forward's kernels (MLLM_LWE_PDL=0: off)
   int lm_wide = 1;     // persistent lm_head GEMM for many rows without logits (MLLM_LWE_LM_WIDE=0: off)
+  int rope_epi = 1;    // RoPE + K/V cache rows in the QKV GEMM epilogue (MLLM_LWE_ROPE_EPI=0: lwe_rope_kv)
 };
 
 // one_per_slot: every token belongs to a different slot (a batched decode step), which lets the
