@@ -676,6 +676,7 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   if (const char* v = getenv("MLLM_LWE_FORCE_KZ")) e->lh.force_kz = atoi(v);
   if (const char* v = getenv("MLLM_LWE_LM_WIDE")) e->lh.lm_wide = atoi(v);
   if (const char* v = getenv("MLLM_LWE_ROPE_EPI")) e->lh.rope_epi = atoi(v);
+  if (const char* v = getenv("MLLM_LWE_W13_WIDE")) e->lh.w13_wide = atoi(v);
   e->tmax = 1024;
   if (const char* v = getenv("MLLM_LWE_TOKENS")) e->tmax = std::max(16, std::min(8192, atoi(v)));
   e->lh.layers = layers;

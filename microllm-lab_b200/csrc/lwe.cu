@@ -1054,6 +1054,131 @@ __global__ void __launch_bounds__(LmWide<TBW, NSW>::THREADS, 1) lwe_gemm_lm_wide
   }
 }
 
+// Wide w1/w3 GEMM for long forwards (prefill chunks): the lm_head layout above applied to
+// lwe_gemm_w13.  Each CTA keeps its 8*TBW token rows of the normalised input in shared memory and
+// streams its run of 32-row tiles of (w1, w3) through an NSW-stage pipeline; staged row i is matrix
+// row 8 (i / 16) + i % 8 of w1 (i % 16 < 8) or w3 (as RowsPaired), so lane (gid, t) of row warp wr holds
+// the w1 and w3 sums of matrix row 8 wr + gid.  Epilogue of lwe_gemm_w13: SiLU(u) * v with the token's
+// 1/RMS, as fp16 hi/lo into xh2/xl2.
+template <int TBW, int NSW>
+__global__ void __launch_bounds__(LmWide<TBW, NSW>::THREADS, 1) lwe_gemm_w13_wide(const __grid_constant__ LweArgs a,
+                                                                                  int T, int l, int tiles_per_cta) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  using C = LmWide<TBW, NSW>;
+  constexpr int BT = C::BT, NT = C::THREADS, TBP = C::TBP;
+  __shared__ float sinv[BT];
+  const LayerDev& L = a.m.layers[l];
+  const int FF = a.m.FF, K = a.m.D, ng = K >> 5;
+  const int XR = C::xrow(K), WR = C::wrow(K);
+  const size_t wbytes = (size_t)kGemmRows * WR, stage = C::stage(K);
+  __half* xh = reinterpret_cast<__half*>(smem);
+  __half* xl = xh + (size_t)BT * XR;
+  unsigned char* wst = reinterpret_cast<unsigned char*>(xl + (size_t)BT * XR);
+  const int ntiles = (FF + 31) / 32;
+  const int rt0 = blockIdx.x * tiles_per_cta, nt = max(0, min(ntiles, rt0 + tiles_per_cta) - rt0);
+  const int t0 = blockIdx.y * BT;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gid = lane >> 2, t = lane & 3;
+  const int wr = warp & 3, wt = warp >> 2;
+  const uint8_t* W1 = reinterpret_cast<const uint8_t*>(L.w1.w);
+  const uint8_t* W3 = reinterpret_cast<const uint8_t*>(L.w3.w);
+  auto issue_w = [&](int rt, int st) {
+    unsigned char* dst = wst + (size_t)st * stage;
+    float* sdst = reinterpret_cast<float*>(dst + wbytes);
+    const int cpr = K >> 5;  // 16-byte chunks per packed row
+    for (int j = tid; j < kGemmRows * cpr; j += NT) {
+      const int r = j / cpr, c = j % cpr, row = rt * 32 + (r >> 4) * 8 + (r & 7);
+      cp_async16(dst + r * WR + c * 16, ((r & 8) ? W3 : W1) + (size_t)min(row, FF - 1) * (K >> 1) + c * 16,
+                 row < FF);
+    }
+    for (int j = tid; j < kGemmRows * ng; j += NT) {
+      const int r = j / ng, row = rt * 32 + (r >> 4) * 8 + (r & 7);
+      cp_async4(sdst + j, ((r & 8) ? L.w3.s : L.w1.s) + (size_t)min(row, FF - 1) * ng + j % ng, row < FF);
+    }
+  };
+#pragma unroll
+  for (int s = 0; s < NSW - 1; ++s) {
+    if (s < nt) issue_w(rt0 + s, s);
+    cp_async_commit();
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (a.skip && *a.skip) {  // a finished speculative loop replays as no-ops
+    cp_async_wait<0>();
+    return;
+  }
+  {
+    const int cpx = K >> 3;  // 16-byte chunks per token row
+    for (int j = tid; j < BT * cpx; j += NT) {
+      const int r = j / cpx, c = j % cpx, tok = t0 + r;
+      const size_t off = (size_t)min(tok, T - 1) * a.ldx + c * 8;
+      cp_async16(xh + r * XR + c * 8, a.xh + off, tok < T);
+      cp_async16(xl + r * XR + c * 8, a.xl + off, tok < T);
+    }
+    cp_async_commit();
+  }
+  for (int i = tid; i < BT; i += NT) sinv[i] = a.fold && t0 + i < T ? fold_inv(a, t0 + i) : 1.f;
+  const int ia = wr * 16 + gid, ib = ia + 8;
+  for (int i = 0; i < nt; ++i) {
+    if (i == 0) cp_async_wait<0>();
+    else cp_async_wait<NSW - 2>();
+    __syncthreads();  // tile i has landed everywhere; every warp is done with tile i - 1's stage
+    {
+      const int in = i + NSW - 1;
+      if (in < nt) issue_w(rt0 + in, in % NSW);
+      cp_async_commit();
+    }
+    const unsigned char* ws = wst + (size_t)(i % NSW) * stage;
+    const float* ss = reinterpret_cast<const float*>(ws + wbytes);
+    const uint32_t* wr0 = reinterpret_cast<const uint32_t*>(ws + ia * WR);
+    const uint32_t* wr1 = reinterpret_cast<const uint32_t*>(ws + ib * WR);
+    float acc[TBP][4];
+#pragma unroll
+    for (int j = 0; j < TBP; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    for (int g = 0; g < ng; ++g) {
+      uint32_t a0[4], a1[4];
+      load_a_frag(wr0 + 4 * g, wr1 + 4 * g, 0, t, a0);
+      load_a_frag(wr0 + 4 * g, wr1 + 4 * g, 1, t, a1);
+      const float sc0 = ss[ia * ng + g], sc1 = ss[ib * ng + g];
+#pragma unroll
+      for (int j = 0; j < TBP; ++j) {
+        const int b = wt + kLmWideWT * j;
+        if (b >= TBW) break;
+        const int xo = (b * 8 + (lane & 7)) * XR + g * 32 + (lane >> 3) * 8;
+        uint32_t bh[4], bl[4];
+        ldsm_x4(bh, xh + xo);
+        ldsm_x4(bl, xl + xo);
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(d, a0, bh[0], bh[1]);
+        mma16816(d, a0, bl[0], bl[1]);
+        mma16816(d, a1, bh[2], bh[3]);
+        mma16816(d, a1, bl[2], bl[3]);
+        acc[j][0] = fmaf(sc0, d[0], acc[j][0]);
+        acc[j][1] = fmaf(sc0, d[1], acc[j][1]);
+        acc[j][2] = fmaf(sc1, d[2], acc[j][2]);
+        acc[j][3] = fmaf(sc1, d[3], acc[j][3]);
+      }
+    }
+    // epilogue (engine/infer.js:178-183, 522-524)
+    const int r = (rt0 + i) * 32 + wr * 8 + gid;
+    if (r < FF) {
+#pragma unroll
+      for (int j = 0; j < TBP; ++j) {
+        const int b = wt + kLmWideWT * j;
+        if (b >= TBW) break;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int tl = b * 8 + 2 * t + e, tok = t0 + tl;
+          if (tok >= T) continue;
+          const float iv = sinv[tl];
+          const float u = acc[j][e] * iv, v = acc[j][2 + e] * iv;
+          const size_t off = (size_t)tok * a.ldx2 + r;
+          split_hi_lo((u / (1.f + expf(-u))) * v, a.xh2[off], a.xl2[off]);
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+}
+
 // lm_head GEMM over the T rows in xh/xl with a per-CTA argmax epilogue: for each token, the best
 // (value, lowest index) over the CTA's 64 vocab rows goes to pval/pidx[blockIdx.x][t].  Optional
 // logits store [t][V].
@@ -1365,6 +1490,25 @@ static bool launch_lm_wide(const LweArgs& a, int T, cudaStream_t st, int* nblk) 
          try_lm_wide<4, 2>(a, T, st, sms, nblk) || try_lm_wide<2, 2>(a, T, st, sms, nblk);
 }
 
+// Wide w1/w3 GEMM for long forwards (K must fit the 64-token tile; else the per-tile GEMM).
+static bool launch_w13_wide(const LweArgs& a, int T, int l, cudaStream_t st) {
+  using C = LmWide<8, 3>;
+  const size_t sm = C::smem(a.m.D);
+  if (sm > (size_t)g_lm_wide_cap) return false;
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const int tiles = (a.m.FF + 31) / 32, tt = (T + C::BT - 1) / C::BT;
+  int g = std::max(1, sms / tt);
+  const int tpc = (tiles + g - 1) / g;
+  g = (tiles + tpc - 1) / tpc;
+  lwe_launch(lwe_gemm_w13_wide<8, 3>, dim3(g, tt), dim3(C::THREADS), sm, st, a, T, l, tpc);
+  return true;
+}
+
 // One-time kernel attributes: the attention's shared memory grows with kv_len.
 cudaError_t lwe_setup(int kv_len) {
   {
@@ -1373,7 +1517,8 @@ cudaError_t lwe_setup(int kv_len) {
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     const int cap = optin - 4096;  // room for the kernel's static reduction arrays
     if (smem_attr(lwe_gemm_lm_wide<8, 3>, cap) == cudaSuccess && smem_attr(lwe_gemm_lm_wide<4, 3>, cap) == cudaSuccess &&
-        smem_attr(lwe_gemm_lm_wide<4, 2>, cap) == cudaSuccess && smem_attr(lwe_gemm_lm_wide<2, 2>, cap) == cudaSuccess)
+        smem_attr(lwe_gemm_lm_wide<4, 2>, cap) == cudaSuccess && smem_attr(lwe_gemm_lm_wide<2, 2>, cap) == cudaSuccess &&
+        smem_attr(lwe_gemm_w13_wide<8, 3>, cap) == cudaSuccess)
       g_lm_wide_cap = cap;
     else
       (void)cudaGetLastError();
@@ -1434,9 +1579,11 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
       LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.D, T, a, T, L.proj, L.proj_b, md.D, nullptr, nullptr, nullptr, 0);
       lwe_launch(lwe_norm_split, dim3(T), dim3(128), 0, st, a, T, L.norm2, (const int*)nullptr);
     }
-    if (md.arch == 0)
-      LWE_GEMM(lwe_gemm_w13, 32, md.FF, md.D, T, n2, T, l);
-    else
+    if (md.arch == 0) {
+      // long forwards (prefill chunks): the persistent wide GEMM, activations read once per CTA
+      if (!(T >= kW13WideRows && h.w13_wide && launch_w13_wide(n2, T, l, st)))
+        LWE_GEMM(lwe_gemm_w13, 32, md.FF, md.D, T, n2, T, l);
+    } else
       LWE_GEMM(lwe_gemm_fc, kGemmRows, md.FF, md.D, T, n2, T, l);
     LweArgs b = a;  // w2 / mlp.proj read the second activation buffer
     b.xh = a.xh2;

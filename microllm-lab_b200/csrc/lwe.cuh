@@ -44,6 +44,7 @@ struct LweArgs {
 };
 constexpr size_t kLweSplitKBytes = size_t(8) << 20;
 constexpr int kLmWideRows = 64;  // lm rows from which the persistent lm_head GEMM is used
+constexpr int kW13WideRows = 512;  // token rows from which the persistent w1/w3 GEMM is used
 constexpr int kLweSplitAttnRows = 16;  // forwards of at most this many tokens use the position-split attention
 constexpr int kLweSplitKTiles = 16384;
 
@@ -60,6 +61,7 @@ struct LweHost {
   int force_kz = 0;    // split-K across CTAs (MLLM_LWE_FORCE_KZ), 0 = automatic
   int pdl = 1;         // programmatic dependent launch between the forward's kernels (MLLM_LWE_PDL=0: off)
   int lm_wide = 1;     // persistent lm_head GEMM for many rows without logits (MLLM_LWE_LM_WIDE=0: off)
+  int w13_wide = 1;    // persistent w1/w3 GEMM for long forwards (MLLM_LWE_W13_WIDE=0: off)
   int rope_epi = 1;    // RoPE + K/V cache rows in the QKV GEMM epilogue (MLLM_LWE_ROPE_EPI=0: lwe_rope_kv)
 };
 

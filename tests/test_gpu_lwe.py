@@ -97,6 +97,28 @@ def test_batch_wide_lm_head(cuda_ok, name):
 
 
 @pytest.mark.gpu
+def test_batch_wide_w13_prefill(cuda_ok):
+    """A 640-row prefill chunk (8 prompts of 80 ids) takes the persistent w1/w3 GEMM: every sequence
+    equals the oracle, and the engine without it (MLLM_LWE_W13_WIDE=0)."""
+    data = _data("tiny-llama")
+    om = O.OracleModel(data)
+    eng = _engine(data, max_slots=8)
+    ref_eng = _engine(data, env={"MLLM_LWE_W13_WIDE": "0"}, max_slots=8)
+    try:
+        V = eng.cfg["vocabSize"]
+        seqs = _prompts(V, [80] * 8, 500)
+        res, st = eng.generateBatch(seqs, maxNewTokens=10, eosId=-1)
+        res0, _ = ref_eng.generateBatch(seqs, maxNewTokens=10, eosId=-1)
+        assert st["prefillForwards"] == 1
+        for i, (q, r, r0) in enumerate(zip(seqs, res, res0)):
+            assert r["generatedIds"] == r0["generatedIds"], i
+            assert r["generatedIds"] == om.generate(q, 10, eos=-1)["generatedIds"], i
+    finally:
+        eng.destroy()
+        ref_eng.destroy()
+
+
+@pytest.mark.gpu
 def test_batch_single_sequence_equals_generate(batch_models):
     data, eng, om = batch_models["ref-llama"]
     ids = pkg().seeded_prompt(20, eng.cfg["vocabSize"], 50)
