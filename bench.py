@@ -413,7 +413,7 @@ def run_gemv(args):
         "roofline": {"bound": "hbm", "achieved": head["best_cold_gbs"], "peak": hbm, "unit": "GB/s",
                      "frac": head["best_cold_gbs"] / hbm, "peak_kind": peak_kind,
                      "traffic": GEMV_LM_TRAFFIC_PER_LAUNCH,
-                     "kernel": "gemv_q4_bulk_kernel<1,2> (mllm_gemv_q4 on 49152x576, M=1)"},
+                     "kernel": "gemv_q4_bulk_kernel<1,2,2,2> (mllm_gemv_q4 on 49152x576, M=1; two CTAs per SM)"},
         "gpu_launches": launches, "points": rows, "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)

@@ -218,8 +218,8 @@ constexpr int kBulkRows = 128;
 constexpr int kBulkNS = 3;
 
 // KSL warps share each 16-row tile (k groups interleaved) for more warps in flight per SM.
-template <int NP, int KSL>
-__global__ void __launch_bounds__(256 * KSL, 1) gemv_q4_bulk_kernel(const uint8_t* __restrict__ W,
+template <int NP, int KSL, int NSB = kBulkNS, int MINB = 1>
+__global__ void __launch_bounds__(256 * KSL, MINB) gemv_q4_bulk_kernel(const uint8_t* __restrict__ W,
                                                                     const float* __restrict__ S,
                                                                     const float* __restrict__ X,
                                                                     float* __restrict__ Y, int R, int K, int M,
@@ -229,27 +229,27 @@ __global__ void __launch_bounds__(256 * KSL, 1) gemv_q4_bulk_kernel(const uint8_
   const int nkb = K >> 4, ng = K >> 5, half_k = K >> 1;
   const size_t wbytes = (size_t)kBulkRows * half_k, sbytes = (size_t)kBulkRows * ng * 4;
   const size_t stage_bytes = (wbytes + sbytes + 127) & ~(size_t)127;
-  uint2* bfrag = reinterpret_cast<uint2*>(sm + kBulkNS * stage_bytes);  // [NP][nkb][32]
-  __shared__ __align__(8) uint64_t full[kBulkNS];
+  uint2* bfrag = reinterpret_cast<uint2*>(sm + NSB * stage_bytes);  // [NP][nkb][32]
+  __shared__ __align__(8) uint64_t full[NSB];
   const int nstage_total = (R + kBulkRows - 1) / kBulkRows;
   // this CTA's stages: blockIdx.x, blockIdx.x + gridDim.x, ...
   const int my_n = nstage_total > (int)blockIdx.x ? (nstage_total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   auto stage_rows = [&](int j) { return min(kBulkRows, R - ((int)blockIdx.x + j * (int)gridDim.x) * kBulkRows); };
   auto issue = [&](int j) {  // thread 0: bulk copies of stage j (full stages only)
     const int r0 = ((int)blockIdx.x + j * (int)gridDim.x) * kBulkRows;
-    unsigned char* dst = sm + (j % kBulkNS) * stage_bytes;
-    uint64_t* bar = &full[j % kBulkNS];
+    unsigned char* dst = sm + (j % NSB) * stage_bytes;
+    uint64_t* bar = &full[j % NSB];
     mbar_expect_tx(bar, (uint32_t)(wbytes + sbytes));
     bulk_g2s(dst, W + (size_t)r0 * half_k, (uint32_t)wbytes, bar);
     bulk_g2s(dst + wbytes, S + (size_t)r0 * ng, (uint32_t)sbytes, bar);
   };
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kBulkNS; ++i) mbar_init(&full[i], 1);
+    for (int i = 0; i < NSB; ++i) mbar_init(&full[i], 1);
     mbar_init_fence();
   }
   __syncthreads();
   if (threadIdx.x == 0)
-    for (int j = 0; j < kBulkNS && j < my_n; ++j)
+    for (int j = 0; j < NSB && j < my_n; ++j)
       if (stage_rows(j) == kBulkRows) issue(j);
   // B fragments (as in the register-prefetch kernel) while the first stages are in flight
   for (int e = threadIdx.x; e < NP * nkb * 32; e += blockDim.x) {
@@ -273,11 +273,11 @@ __global__ void __launch_bounds__(256 * KSL, 1) gemv_q4_bulk_kernel(const uint8_
   for (int j = 0; j < my_n; ++j) {
     const int r0 = ((int)blockIdx.x + j * (int)gridDim.x) * kBulkRows;
     const int nr = stage_rows(j);
-    unsigned char* st = sm + (j % kBulkNS) * stage_bytes;
+    unsigned char* st = sm + (j % NSB) * stage_bytes;
     if (nr == kBulkRows) {
-      if (!mbar_wait_bounded(&full[j % kBulkNS], (uint32_t)((j / kBulkNS) & 1), kWaitNs)) {
+      if (!mbar_wait_bounded(&full[j % NSB], (uint32_t)((j / NSB) & 1), kWaitNs)) {
         if (threadIdx.x == 0) atomicExch(err, 1);
-        mbar_wait_bounded(&full[j % kBulkNS], (uint32_t)((j / kBulkNS) & 1), kWaitNs);
+        mbar_wait_bounded(&full[j % NSB], (uint32_t)((j / NSB) & 1), kWaitNs);
         ok = false;
       }
     } else {  // partial last stage: plain loads
@@ -346,11 +346,11 @@ __global__ void __launch_bounds__(256 * KSL, 1) gemv_q4_bulk_kernel(const uint8_
       }
     }
     if (KSL > 1) __syncthreads();  // red is reused by the next stage
-    if (threadIdx.x == 0 && j + kBulkNS < my_n && stage_rows(j + kBulkNS) == kBulkRows) issue(j + kBulkNS);
+    if (threadIdx.x == 0 && j + NSB < my_n && stage_rows(j + NSB) == kBulkRows) issue(j + NSB);
   }
 }
 
-template <int NP, int KSL = 2>
+template <int NP, int KSL = 2, int NSB = kBulkNS, int MINB = 1>
 static cudaError_t run_gemv_bulk(const uint8_t* W, const float* S, const float* X, float* Y, int R, int K, int M,
                                  int* err, cudaStream_t st) {
   int dev = 0, sms = 148;
@@ -358,18 +358,19 @@ static cudaError_t run_gemv_bulk(const uint8_t* W, const float* S, const float* 
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const size_t wbytes = (size_t)kBulkRows * (K / 2), sbytes = (size_t)kBulkRows * (K / 32) * 4;
   const size_t stage_bytes = (wbytes + sbytes + 127) & ~(size_t)127;
-  const size_t smem = kBulkNS * stage_bytes + (size_t)NP * (K / 16) * 32 * sizeof(uint2);
-  const cudaError_t e =
-      cudaFuncSetAttribute(gemv_q4_bulk_kernel<NP, KSL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const size_t smem = NSB * stage_bytes + (size_t)NP * (K / 16) * 32 * sizeof(uint2);
+  const cudaError_t e = cudaFuncSetAttribute(gemv_q4_bulk_kernel<NP, KSL, NSB, MINB>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int nst = (R + kBulkRows - 1) / kBulkRows;
-  gemv_q4_bulk_kernel<NP, KSL><<<std::min(nst, sms), 256 * KSL, smem, st>>>(W, S, X, Y, R, K, M, err);
+  gemv_q4_bulk_kernel<NP, KSL, NSB, MINB><<<std::min(nst, MINB * sms), 256 * KSL, smem, st>>>(W, S, X, Y, R, K, M, err);
   return cudaGetLastError();
 }
 
-static size_t gemv_bulk_smem(int K, int np) {
+constexpr size_t kBulk2Smem = 108 * 1024;  // dynamic shared memory of a CTA when two share an SM
+static size_t gemv_bulk_smem(int K, int np, int ns = kBulkNS) {
   const size_t wbytes = (size_t)kBulkRows * (K / 2), sbytes = (size_t)kBulkRows * (K / 32) * 4;
-  return kBulkNS * ((wbytes + sbytes + 127) & ~(size_t)127) + (size_t)np * (K / 16) * 32 * 8;
+  return ns * ((wbytes + sbytes + 127) & ~(size_t)127) + (size_t)np * (K / 16) * 32 * 8;
 }
 
 template <int NP, int KSL>
@@ -454,7 +455,11 @@ extern "C" int mllm_gemv_q4(const uint8_t* d_packed, const float* d_scales, cons
       gemv_bulk_smem(cols, np) <= 200 * 1024) {
     int* err = gemv_err_flag();
     if (!err) return MLLM_ERR_CUDA;
-    if (np == 1) e = run_gemv_bulk<1>(d_packed, d_scales, d_x, d_y, rows, cols, n_act, err, st);
+    // one pass of tokens with a small K: two CTAs per SM with two stages each (2.6 % faster on the
+    // 49152 x 576 lm_head shape than one CTA with three stages; the other shapes measured no better)
+    if (np == 1 && gemv_bulk_smem(cols, 1, 2) <= kBulk2Smem)
+      e = run_gemv_bulk<1, 2, 2, 2>(d_packed, d_scales, d_x, d_y, rows, cols, n_act, err, st);
+    else if (np == 1) e = run_gemv_bulk<1>(d_packed, d_scales, d_x, d_y, rows, cols, n_act, err, st);
     else if (np == 2) e = run_gemv_bulk<2>(d_packed, d_scales, d_x, d_y, rows, cols, n_act, err, st);
     else if (np == 3) e = run_gemv_bulk<3>(d_packed, d_scales, d_x, d_y, rows, cols, n_act, err, st);
     else e = run_gemv_bulk<4>(d_packed, d_scales, d_x, d_y, rows, cols, n_act, err, st);
