@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
 """Regenerate the golden fixtures in this directory from the reference's own Python code.
 
-Run in a container where the reference project is mounted; MLLM_REFERENCE_DIR names its root
-(the default below is the mount point of the build container).  It needs torch, transformers and
+Run in a container where the reference project is mounted, with MLLM_REFERENCE_DIR set to its root
+(the script stops with an error when it is unset).  It needs torch, transformers and
 tokenizers; the tests that read the fixtures need none of them and never read the reference project.
 
 Fixtures:
@@ -32,7 +32,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("MLLM_REFERENCE_DIR", "/root/reference")
+REF = os.environ.get("MLLM_REFERENCE_DIR", "")
 sys.path.insert(0, ROOT)
 pgw = importlib.import_module("microllm-lab_b200.pgw")
 
@@ -43,6 +43,8 @@ REF_GPT2 = dict(vocab=259, n_embd=128, n_head=2, n_layer=1, n_positions=128)
 
 
 def load_ref(rel):
+    if not REF or not os.path.isdir(REF):
+        raise SystemExit("set MLLM_REFERENCE_DIR to the reference project's root directory")
     spec = importlib.util.spec_from_file_location("ref_" + os.path.basename(rel)[:-3], os.path.join(REF, rel))
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
