@@ -225,7 +225,7 @@ def run_batched_leg(torch, P, local: int, rank: int, ws: int, dist, steps: int, 
     cfg = P.CONFIGS[B["model"]]
     data = P.synthetic_pgw(B["model"], B["seed"], cache_dir=CACHE)
     nseq, plen, nnew = B["nseq"], B["plen"], B["nnew"]
-    seqs = [P.seeded_prompt(plen, cfg["vocabSize"], 4000 + rank * nseq + i) for i in range(nseq)]
+    seqs = [P.seeded_prompt(plen, cfg["vocabSize"], sd) for sd in batched_sequence_seeds(rank, nseq)]
     eng = P.CudaPetitGPT(data, device=local, max_slots=nseq, kv_len=plen + nnew)
     stream = torch.cuda.Stream()
     eng.set_stream(stream.cuda_stream)
@@ -251,11 +251,7 @@ def run_batched_leg(torch, P, local: int, rank: int, ws: int, dist, steps: int, 
             launches += st["kernelLaunches"]
             chunks = st["prefillForwards"]
             assert st["totalGenerated"] == nseq * nnew
-    if dist:
-        t = torch.tensor([ev_ms, wall_ms], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ev_ms, wall_ms = float(t[0]), float(t[1])
-    tokens = nseq * nnew * steps * ws
+    ev_ms, wall_ms = max_over_ranks(dist, [ev_ms, wall_ms], f"cuda:{local}")
     hbm, _, peak_kind = peaks()
     alg = batched_algorithmic_bytes(cfg, nseq, plen, nnew, chunks)
     ms = ev_ms / steps
@@ -263,14 +259,15 @@ def run_batched_leg(torch, P, local: int, rank: int, ws: int, dist, steps: int, 
     out = {
         "metric": "replicated multi-sequence decode aggregate tok/s (SmolLM2-135M shape, 256 seqs/GPU, "
                   "128-token prompts, 256 new tokens)",
-        "value": tokens / (ev_ms / 1e3), "unit": "tok/s", "n_gpus": ws, "steps": steps, "warmup": warmup,
+        "value": aggregate_rate(nseq * nnew, steps, ws, ev_ms), "unit": "tok/s", "n_gpus": ws, "steps": steps,
+        "warmup": warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "config": {"workload": "config5 smollm2-135m 256 seqs/GPU p128 n256", "sequences_per_gpu": nseq,
                    "partition": "sequence ids rank*256 .. rank*256+255", "inputs": "larger than L2 (4.5 GB KV)",
                    "timing": "CUDA events around one mllm_generate_batch call (its 128 KB prompt upload and "
                              "256 KB id download included)"},
         "prefill_ms": float(np.mean(pre_ms)), "decode_tok_s_per_gpu": nseq * (nnew - 1) / ((np.mean(dev_ms) - np.mean(pre_ms)) / 1e3),
-        "e2e": {"value": tokens / (wall_ms / 1e3), "unit": "tok/s",
+        "e2e": {"value": aggregate_rate(nseq * nnew, steps, ws, wall_ms), "unit": "tok/s",
                 "h2d_bytes_per_step": nseq * plen * 4 + (3 * nseq * plen + 2 * nseq) * 4 + nseq * 4,
                 "d2h_bytes_per_step": nseq * nnew * 4 + nseq * 4 + 17 * 4},
         "gpu_launches": launches,
@@ -295,6 +292,32 @@ def dist_setup():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return ws, rank, local
+
+
+def replica_prompt_seed(seed: int, rank: int) -> int:
+    """Prompt seed of one batch-1 replica: every rank decodes its own sequence."""
+    return seed + rank
+
+
+def batched_sequence_seeds(rank: int, nseq: int) -> list:
+    """Prompt seeds of this rank's partition of the config-5 sequence set (ids rank*nseq .. +nseq-1)."""
+    return [4000 + rank * nseq + i for i in range(nseq)]
+
+
+def max_over_ranks(dist, values, device) -> list:
+    """Element-wise max of this rank's timings (ms) over all ranks; every rank receives the result.
+    One all-reduce, the same on every rank. Without a process group the values come back unchanged."""
+    if not dist:
+        return [float(v) for v in values]
+    import torch
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.cpu()]
+
+
+def aggregate_rate(units_per_rank_step: int, steps: int, ws: int, max_ms: float) -> float:
+    """Whole-job rate: the units all ranks processed over the max-over-ranks time, per second."""
+    return units_per_rank_step * steps * ws / (max_ms / 1e3)
 
 
 def run_reference(args):
@@ -435,9 +458,9 @@ def run_decode(args):
     cfg = P.CONFIGS[name]
     data = P.synthetic_pgw(name, seed, cache_dir=CACHE)
     if W.get("copy_spans"):
-        prompt = P.copy_span_prompt(n_prompt, cfg["vocabSize"], seed + rank)
+        prompt = P.copy_span_prompt(n_prompt, cfg["vocabSize"], replica_prompt_seed(seed, rank))
     else:
-        prompt = P.seeded_prompt(n_prompt, cfg["vocabSize"], seed + rank)
+        prompt = P.seeded_prompt(n_prompt, cfg["vocabSize"], replica_prompt_seed(seed, rank))
     eng = P.CudaPetitGPT(data, device=local)
     stream = torch.cuda.Stream()
     eng.set_stream(stream.cuda_stream)
@@ -495,14 +518,11 @@ def run_decode(args):
         torch.cuda.synchronize()
         t_e2e, _ = timed(step_e2e, args.steps)
     torch.cuda.synchronize()
+    t_dev, t_e2e = max_over_ranks(dist, [t_dev, t_e2e], f"cuda:{local}")
     if dist:
-        t = torch.tensor([t_dev, t_e2e], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_dev, t_e2e = float(t[0]), float(t[1])
         dist.barrier()
-    tokens = n_new * args.steps * ws
-    value = tokens / (t_dev / 1e3)
-    e2e = tokens / (t_e2e / 1e3)
+    value = aggregate_rate(n_new, args.steps, ws, t_dev)
+    e2e = aggregate_rate(n_new, args.steps, ws, t_e2e)
     ms_step = t_dev / args.steps
     hbm, _, peak_kind = peaks()
     alg = decode_algorithmic_bytes(cfg, n_prompt, n_new)
