@@ -202,7 +202,8 @@ class CudaPetitGPT:
                  ngram: int = 3):
         """Greedy generation in one device launch.  ``specK > 0`` turns on prompt-lookup speculation
         (n-gram size ``ngram``), which runs on the device.  ``onToken(id, meta)`` is called for each
-        id after the launch returns, with the reference's phases ("prefill", "decode", "spec")."""
+        id after the launch returns, with phase "prefill" for the first id and "decode" for the rest (the
+        launch does not report which ids were accepted drafts, the reference's "spec" phase)."""
         ids = np.ascontiguousarray(ids, np.int32)
         out = np.zeros(max(int(maxNewTokens), 1), np.int32)
         st = Stats()
