@@ -56,7 +56,9 @@ class DecodeWorker:
             if cmd == "load":
                 self._load(m)
             elif cmd == "generate":
-                self._generate(m.get("prompt"), m.get("maxNewTokens") or 64, m.get("opts") or {}, m.get("promptIds"))
+                # `maxNewTokens || 64`, then numeric as the reference's arithmetic makes it
+                self._generate(m.get("prompt"), int(m.get("maxNewTokens") or 64), m.get("opts") or {},
+                               m.get("promptIds"))
             elif cmd == "unload":
                 self._drop_engine()
                 self.post({"type": "unloaded"})

@@ -136,6 +136,9 @@ def test_prompt_truncation_keeps_bos():
     # without a leading BOS: the last 4 ids
     w.handle({"cmd": "generate", "promptIds": ids[1:], "maxNewTokens": 8})
     assert engines[0].calls[-1]["ids"] == [116, 117, 118, 119]
+    # a numeric string counts as its number
+    w.handle({"cmd": "generate", "promptIds": ids, "maxNewTokens": "8"})
+    assert engines[0].calls[-1]["ids"] == [BOS, 117, 118, 119] and engines[0].calls[-1]["maxNewTokens"] == 8
     # maxPrompt floors at 1: BOS alone survives
     w.handle({"cmd": "generate", "promptIds": ids, "maxNewTokens": 30})
     assert engines[0].calls[-1]["ids"] == [BOS]
