@@ -14,10 +14,17 @@ The fixture holds:
     the cases exactly as the full one does.
 
 The tests then need neither the 2.2 MB file nor `tokenizers`.
+
+Before writing, the script checks the product tokenizer (microllm-lab_b200/tokenizer.py) against HF on
+the full file, over 3,000 seeded random strings. The strings mix scripts, emoji, digits, punctuation,
+contractions, whitespace runs and special-token text. The script stops on the first difference.
 """
+import importlib
 import json
 import os
+import random
 import re
+import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF = os.environ.get("MLLM_REFERENCE_DIR", "")
@@ -46,6 +53,38 @@ CASES = [
 ]
 
 
+def stress_check(path, hf, n=3000, seed=7):
+    """Product tokenizer vs HF on seeded random strings over the full tokenizer.json."""
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    T = importlib.import_module("microllm-lab_b200.tokenizer")
+    tok = T.Tokenizer.from_file(path)
+    rng = random.Random(seed)
+    alph = (list("abcdefghijklmnopqrstuvwxyzABCDEFGHIJKLMNOPQRSTUVWXYZ0123456789 .,;:!?'\"-_()[]{}<>|/\\@#$%^&*+=~`\t\n")
+            + list("éèüößçñØåÆœ€£¥—–…“”‘’") + list("日本語中文한국어テキストабвгдеёжзиαβγδεζ")
+            + ["🎉", "🚀", "👍🏽", "\u00a0", "\u2003", "\u200b"])
+    specials = ["<|user|>", "<|assistant|>", "<|system|>", "[BOS]", "[EOS]", "[PAD]", "[UNK]"]
+    for _ in range(n):
+        parts = []
+        for _ in range(rng.randint(0, 60)):
+            r = rng.random()
+            if r < 0.03:
+                parts.append(rng.choice(specials))
+            elif r < 0.08:
+                parts.append("'" + rng.choice(["s", "t", "re", "ve", "m", "ll", "d"]))
+            elif r < 0.15:
+                parts.append(" " * rng.randint(1, 4))
+            else:
+                parts.append(rng.choice(alph))
+        text = "".join(parts)
+        want = hf.encode(text, add_special_tokens=False).ids
+        got = tok.encode(text)
+        if got != want:
+            raise SystemExit(f"tokenizer differs from HF on {text!r}: {got[:12]} vs {want[:12]}")
+        if tok.decode(got) != hf.decode(want, skip_special_tokens=False):
+            raise SystemExit(f"decode differs from HF on {text!r}")
+    print(f"product tokenizer = HF on {n} random strings")
+
+
 def main():
     if not REF or not os.path.isdir(REF):
         raise SystemExit("set MLLM_REFERENCE_DIR to the reference project's root directory")
@@ -54,6 +93,7 @@ def main():
     with open(path, encoding="utf-8") as f:
         spec = json.load(f)
     hf = Tokenizer.from_file(path)
+    stress_check(path, hf)
     specials = [t["content"] for t in spec.get("added_tokens", []) if t.get("special")]
     split = re.compile("|".join(re.escape(s) for s in sorted(specials, key=len, reverse=True)))
     pieces = set()
