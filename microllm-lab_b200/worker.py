@@ -17,9 +17,11 @@ Kept from the reference:
 Differences, by design of this backend:
   - The engine is always the CUDA one (``backend: "cuda"``): there is no CPU or WASM path to fall back
     to, so ``preferGpu`` has no effect and a missing device is an ``error`` reply.
-  - Tokenisation is not part of the decode path: ``tokenizer`` is any object with
-    ``encode_messages(messages, card) -> ids`` and ``decode(ids, skip_special=False) -> str``.  Without one,
-    ``generate`` takes ``promptIds`` (ids as they are, still truncated) and the text fields are None.
+  - The tokenizer comes from ``load``'s ``tokenizerSpec`` (a tokenizer.json object, as in the reference),
+    or from any object with ``encode_messages(messages, card) -> ids`` and
+    ``decode(ids, skip_special=False) -> str`` given to the constructor or as ``load``'s ``tokenizer``.
+    There is no fetch of a default tokenizer.json. Without a tokenizer, ``generate`` takes ``promptIds``
+    (ids as they are, still truncated), and the text fields are None.
   - All tokens come from one device launch, so the ``token`` replies are posted when the launch returns,
     in generation order.
   - ``opts.specK`` / ``opts.ngram`` turn on the on-device prompt-lookup speculation.
@@ -86,6 +88,9 @@ class DecodeWorker:
         self.model_id = model_id
         if msg.get("tokenizer") is not None:
             self.tokenizer = msg["tokenizer"]
+        elif msg.get("tokenizerSpec") is not None:  # a tokenizer.json object, as engine/worker.js:40-41 takes
+            from .tokenizer import Tokenizer
+            self.tokenizer = Tokenizer(msg["tokenizerSpec"])
         self._drop_engine()
         buffer = msg.get("buffer")
         if buffer is None:

@@ -117,3 +117,24 @@ def test_worker_encodes_text_prompts_with_the_tokenizer(tok):
     assert eng.calls[-1] == [S["BOS"], S["USER"], *tok.encode("The quick brown"), S["ASSISTANT"]]
     assert posted[-1]["type"] == "done" and posted[-1]["text"] == " fox"
     assert "".join(m["piece"] for m in posted if m["type"] == "token") == " fox"
+
+
+def test_worker_load_takes_a_tokenizer_spec(golden):
+    class Eng:
+        cfg = {"maxSeqLen": 256}
+        bytesAllocated = 0
+
+        def generate(self, ids, maxNewTokens, eosId, onToken, specK, ngram):
+            self.ids = list(ids)
+            return {"generatedIds": [], "stopReason": "max_new_tokens", "ttftMs": 0.0}
+
+        def destroy(self):
+            pass
+
+    posted, eng = [], Eng()
+    w = P.DecodeWorker(posted.append, engine_factory=lambda buf: eng)
+    w.handle({"cmd": "load", "buffer": b"x", "tokenizerSpec": golden["spec"]})
+    w.handle({"cmd": "generate", "prompt": "Hello, world!", "maxNewTokens": 4})
+    hello = next(c["ids"] for c in golden["cases"] if c["text"] == "Hello, world!")
+    assert eng.ids == [S["BOS"], S["USER"], *hello, S["ASSISTANT"]]
+    assert posted[-1]["type"] == "done" and posted[-1]["text"] == ""
