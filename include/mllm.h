@@ -159,7 +159,10 @@ int mllm_gemv_q4(const uint8_t* d_packed, const float* d_scales, const float* d_
  * activations x [n_act][cols] -> y [n_act][rows].  Each activation is split into fp16 hi + lo halves
  * (relative residual <= 2^-22) that multiply the dequantised (q - 8) weights (exact in fp16) with
  * fp32 accumulation; group scales are applied in fp32.  The fp16 halves live in a per-device
- * workspace that this call allocates on first use (and grows when a larger call arrives).
+ * workspace that this call allocates on first use (and grows when a larger call arrives; a replaced
+ * workspace is kept until exit, since kernels enqueued earlier may still read it).  All calls on one
+ * device share that workspace: calls whose kernels overlap on the GPU (different streams or host
+ * threads) race on it and must be serialised by the caller.
  * Replaces gemmGeneric (engine/infer.js:118-132: a row loop of gemvQ4) for prefill, verify and
  * multi-sequence decode.
  */

@@ -54,31 +54,32 @@ cudaError_t launch_split(const float* x, __half* hi, __half* lo, size_t n, cudaS
 }
 
 namespace {
-// Per-device workspace for the fp16 halves of the activations (grown on demand, kept until exit).
+// Per-device workspace for the fp16 halves of the activations.  It grows on demand; a superseded
+// buffer is kept (not freed) until exit, because work already enqueued by an earlier call on some
+// stream may still read it.  Growth is geometric, so few buffers are ever retired.
 struct Workspace {
   std::mutex mu;
   std::vector<void*> ptr;
   std::vector<size_t> cap;
+  std::vector<void*> retired;
 };
 Workspace g_ws;
 
-int workspace(size_t bytes, __half** out) {
+// Called with g_ws.mu held.
+int workspace_locked(size_t bytes, __half** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MLLM_ERR_CUDA;
-  std::lock_guard<std::mutex> lk(g_ws.mu);
   if ((int)g_ws.ptr.size() <= dev) {
     g_ws.ptr.resize(dev + 1, nullptr);
     g_ws.cap.resize(dev + 1, 0);
   }
   if (g_ws.cap[dev] < bytes) {
-    if (g_ws.ptr[dev]) {
-      cudaDeviceSynchronize();
-      cudaFree(g_ws.ptr[dev]);
-    }
-    g_ws.ptr[dev] = nullptr;
-    g_ws.cap[dev] = 0;
-    if (cudaMalloc(&g_ws.ptr[dev], bytes) != cudaSuccess) return MLLM_ERR_OOM;
-    g_ws.cap[dev] = bytes;
+    const size_t want = std::max(bytes, 2 * g_ws.cap[dev]);
+    void* p = nullptr;
+    if (cudaMalloc(&p, want) != cudaSuccess) return MLLM_ERR_OOM;
+    if (g_ws.ptr[dev]) g_ws.retired.push_back(g_ws.ptr[dev]);
+    g_ws.ptr[dev] = p;
+    g_ws.cap[dev] = want;
   }
   *out = (__half*)g_ws.ptr[dev];
   return MLLM_OK;
@@ -94,8 +95,12 @@ extern "C" int mllm_gemm_q4(const uint8_t* d_packed, const float* d_scales, cons
   if (((uintptr_t)d_packed & 15) || ((uintptr_t)d_scales & 3) || ((uintptr_t)d_x & 3)) return MLLM_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   const size_t n = (size_t)n_act * cols;
+  // The lock is held until both kernels are enqueued, so no other call can replace the workspace in
+  // between.  Calls whose kernels overlap on the GPU (different streams or threads) still share the
+  // workspace and must be serialised by the caller.
+  std::lock_guard<std::mutex> lk(g_ws.mu);
   __half* ws = nullptr;
-  int rc = workspace(2 * n * sizeof(__half) + 256, &ws);
+  int rc = workspace_locked(2 * n * sizeof(__half) + 256, &ws);
   if (rc) return rc;
   __half* hi = ws;
   __half* lo = ws + ((n + 127) / 128) * 128;

@@ -26,7 +26,9 @@ def test_noalloc_gemm_matches_allocating_entry_on_two_calls(cuda_ok):
     P = pkg()
     L = P.load_library()
     rng = np.random.default_rng(31)
-    for rows, cols, m in ((960, 576, 9), (576, 1536, 64)):  # two calls in a row, different sizes
+    # two calls in a row with different sizes, then one that fills the scratch exactly
+    # (1024 x 1024 = 1,048,576 values: the last bytes of the lo half are written and read)
+    for rows, cols, m in ((960, 576, 9), (576, 1536, 64), (64, 1024, 1024)):
         packed, sc, x = _case(rng, rows, cols, m)
         dp, ds, dx = (torch.from_numpy(a).cuda() for a in (packed, sc, x))
         y_ref = torch.empty((m, rows), dtype=torch.float32, device="cuda")
