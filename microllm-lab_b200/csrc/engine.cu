@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "../../include/mllm.h"
+#include "cdec.cuh"
 #include "device_common.cuh"
 #include "engine.cuh"
 #include "lwe.cuh"
@@ -101,6 +102,12 @@ struct mllm_engine {
   LweHost lh;
   Grow g_bids, g_plan, g_bout, g_state, g_blogits, g_spec;
   int32_t* h_active = nullptr; // pinned
+  // cluster decode (cdec.cu): the single-token loop on one 16-CTA cluster, for the models it supports
+  int cd_ok = 0;
+  size_t cd_smem = 0;
+  uint4* d_cdw = nullptr;      // repacked weight streams
+  uint32_t* d_cdoff = nullptr; // [16 x 16] first record of each warp's stream
+  uint32_t* d_cdcnt = nullptr; // [16 x 16] records per token
   long coop_launches = 0;      // persistent-kernel launches issued by this handle
   long spec_graph_kernels = 0; // kernels in one speculation graph replay
   long spec_replay_kernels = 0;
@@ -273,6 +280,17 @@ int launch(mllm_engine* e, RunArgs& a, int max_forwards, bool multi, bool resume
   // kAttnMinRounds rounds of the attention loop
   const int maxpos = a.mode == MODE_GENERATE ? a.n_ids + a.max_new : a.pos0 + 1;
   const bool split = maxpos > kAttnRound * (kAttnMinRounds - 1);
+  if (!multi && e->cd_ok) {
+    CdArgs ca;
+    ca.r = a;
+    ca.wst = e->d_cdw;
+    ca.woff = e->d_cdoff;
+    ca.wcnt = e->d_cdcnt;
+    const cudaError_t lst = cd_launch(ca, e->cd_smem, e->stream);
+    ++e->coop_launches;
+    if (lst != cudaSuccess) return fail(e, MLLM_ERR_CUDA, "cluster decode launch failed: %s", cudaGetErrorString(lst));
+    return MLLM_OK;
+  }
   DecodeFn k = multi ? e->kernel_multi : split ? e->kernel_single_split : e->kernel_single;
   const size_t smem = multi ? e->smem_multi : e->smem_single;
   void* args[] = {&a};
@@ -627,6 +645,39 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
     int per_sm = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, k == e->kernel_multi ? e->smem_multi : e->smem_single);
     if (per_sm < 1) return bad(MLLM_ERR_CUDA, "decode kernel cannot be resident with its shared memory");
+  }
+  // ---- cluster decode: weights repacked into per-(CTA, warp) streams (MLLM_CLUSTER_DECODE=0: off)
+  {
+    bool want = true;
+    if (const char* v = getenv("MLLM_CLUSTER_DECODE")) want = atoi(v) != 0;
+    if (want && cd_supported(md, smem_cap) && cd_setup(smem_cap) == cudaSuccess &&
+        cd_max_clusters(cd_smem_bytes(md)) >= 1) {
+      auto host_q4 = [&](const std::string& name, int rows, int cols) {
+        const PgwTensor* t = tensor(p, name);
+        return HostQ4{buf + p.payload_off + t->offset, buf + p.payload_off + t->scale_offset, rows, cols};
+      };
+      std::vector<HostQ4> mats;
+      for (int l = 0; l < L; ++l) {
+        const std::string b = "blocks." + std::to_string(l) + ".";
+        mats.push_back(host_q4(b + "attn.qkv", md.QKV, D));
+        mats.push_back(host_q4(b + "attn.proj", D, D));
+        mats.push_back(host_q4(b + "mlp.w1", FF, D));
+        mats.push_back(host_q4(b + "mlp.w3", FF, D));
+        mats.push_back(host_q4(b + "mlp.w2", D, FF));
+      }
+      std::vector<uint8_t> packed;
+      std::vector<uint32_t> off, cnt;
+      cd_pack(md, mats, host_q4("lm_head", md.vocab, D), &packed, &off, &cnt);
+      int rc;
+      if ((rc = dev_alloc(E, &e->d_cdw, packed.size())) || (rc = dev_alloc(E, &e->d_cdoff, off.size() * 4)) ||
+          (rc = dev_alloc(E, &e->d_cdcnt, cnt.size() * 4)))
+        return relay(rc);
+      cudaMemcpy(e->d_cdw, packed.data(), packed.size(), cudaMemcpyHostToDevice);
+      cudaMemcpy(e->d_cdoff, off.data(), off.size() * 4, cudaMemcpyHostToDevice);
+      cudaMemcpy(e->d_cdcnt, cnt.data(), cnt.size() * 4, cudaMemcpyHostToDevice);
+      e->cd_smem = cd_smem_bytes(md);
+      e->cd_ok = 1;
+    }
   }
   // ---- exchange buffers
   {
