@@ -164,14 +164,15 @@ def cpu_baseline_decode(data: bytes, prompt, n_new_full: int, threads: int, samp
 def batched_algorithmic_bytes(cfg: dict, nseq: int, plen: int, nnew: int, chunks: int) -> int:
     """Minimum bytes of one mllm_generate_batch call: every forward (prefill chunk of tmax tokens, or
     decode step over all sequences) reads the Q4 weights and norms once; every token's K/V row is
-    written once; attention reads the K/V rows of positions 0..pos of its own sequence.  `chunks` =
-    prefill forwards of the call."""
+    written once; a decode step's attention reads the K/V rows of positions 0..pos of its own sequence;
+    a prefill chunk reads each of its sequences' K/V rows once (as a flash-style kernel would: the
+    re-reads of a causal prompt are not counted).  `chunks` = prefill forwards of the call."""
     d, ff, V, L = cfg["dModel"], cfg["dFf"], cfg["vocabSize"], cfg["nLayers"]
     kvd = cfg["nKvHeads"] * 64
     q4 = lambda r, c: r * c // 2 + r * (c // 32) * 4
     w = q4(V, d) + L * (q4(d + 2 * kvd, d) + q4(d, d) + 2 * q4(ff, d) + q4(d, ff)) + (2 * L + 1) * d * 4
     kv_row = 2 * L * kvd * 4
-    total = chunks * w + nseq * plen * kv_row + nseq * kv_row * plen * (plen + 1) // 2
+    total = chunks * w + 2 * nseq * plen * kv_row
     for i in range(1, nnew):
         pos = plen + i - 1
         total += w + nseq * (kv_row * (pos + 1) + kv_row)
@@ -272,8 +273,9 @@ def run_batched_leg(torch, P, local: int, rank: int, ws: int, dist, steps: int, 
                 "d2h_bytes_per_step": nseq * nnew * 4 + nseq * 4 + 17 * 4},
         "gpu_launches": launches,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": peak_kind, "traffic": None, "kernel": "whole call (token-batch kernels; attention "
-                     "over the fp32 KV cache dominates)", "algorithmic_bytes_per_step": alg},
+                     "peak_kind": peak_kind, "traffic": None, "kernel": "whole call: token-batch GEMMs (lwe_gemm_resid, _w13, _qkv, "
+                     "_lm_wide: about 65 % of a decode step) and attention over the fp32 KV cache (lwe_attention, "
+                     "about 34 %)", "algorithmic_bytes_per_step": alg},
         "clocks": clk.summary(),
     }
     if cpu and rank == 0 and ws == 1:
@@ -320,38 +322,47 @@ def aggregate_rate(units_per_rank_step: int, steps: int, ws: int, max_ms: float)
     return units_per_rank_step * steps * ws / (max_ms / 1e3)
 
 
+def config_of(W: dict, ws: int) -> dict:
+    """The workload's `config` dict, identical in both arms (descriptive notes live outside it)."""
+    return {"workload": W["workload"], "model": W["model_text"], "global_batch": ws,
+            "seq_len": W["prompt"] + W["new"], "parallelism": "replicas"}
+
+
 def run_reference(args):
-    """--impl reference: the CPU restatement of the reference path, all host threads, rank 0 only."""
+    """--impl reference: the CPU restatement of the reference path (oracle/: engine/infer.js), all host
+    threads, rank 0 only, on the default workload (config 1).  Every step is the whole workload: the
+    64-token prefill and all 127 decode steps, greedy, as engine/infer.js:603-646 runs them."""
     ws, rank, _ = dist_setup()
     if rank != 0:
         return
     P = pkg()
-    cfg = P.CONFIGS["petitgpt"]
-    data = P.synthetic_pgw("petitgpt", 0, cache_dir=CACHE)
-    prompt = P.seeded_prompt(64, cfg["vocabSize"], 0)
+    W = WORKLOADS["decode"]
+    cfg = P.CONFIGS[W["model"]]
+    data = P.synthetic_pgw(W["model"], W["seed"], cache_dir=CACHE)
+    prompt = P.seeded_prompt(W["prompt"], cfg["vocabSize"], replica_prompt_seed(W["seed"], 0))
     threads = os.cpu_count() or 1
-    sample = 4
+    from oracle.oracle import OracleModel
+    om = OracleModel(data, threads=threads)
     for _ in range(args.warmup):
-        cpu_baseline_decode(data, prompt, 128, threads, sample)
-    vals, pre, per = [], [], []
-    t0 = time.perf_counter()
+        om.generate(prompt, W["new"], eos=-1)
+    times = []
     for _ in range(args.steps):
-        v, a, b = cpu_baseline_decode(data, prompt, 128, threads, sample)
-        vals.append(v)
-        pre.append(a)
-        per.append(b)
-    wall = time.perf_counter() - t0
-    v = float(np.mean(vals))
+        t0 = time.perf_counter()
+        r = om.generate(prompt, W["new"], eos=-1)
+        times.append(time.perf_counter() - t0)
+        assert len(r["generatedIds"]) == W["new"]
+    wall = sum(times)
+    v = W["new"] * args.steps / wall
     line = {
-        "impl": "reference", "metric": "batch-1 Q4 decode tok/s (PetitGPT shape, 64-token prompt, 128 new tokens)",
+        "impl": "reference", "metric": W["metric"],
         "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": wall / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f64-accumulate/f32-store", "data": "synthetic (seeded N(0,0.02) Q4 weights, seeded prompt)",
-        "config": {"workload": "config1 petitgpt b1 p64 n128", "model": "PetitGPT-shaped Q4 (30L d576 9/3 ff1536 V32000)",
-                   "global_batch": 1, "seq_len": 192, "parallelism": "replicas"},
+        "dtype": "f64-accumulate/f32-store", "data": DATA_TEXT,
+        "config": config_of(W, 1),
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": f"per step: 64-token prefill + {sample} decode steps, extrapolated to 127 "
-                                   f"decode steps (prefill {np.mean(pre):.2f} s, {np.mean(per)*1e3:.1f} ms/token)"},
+                         "sample": f"every step the whole workload: {W['prompt']}-token prefill + {W['new'] - 1} "
+                                   f"greedy decode steps (oracle/, the C restatement of engine/infer.js; "
+                                   f"{threads} threads inside each forward)"},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -360,100 +371,171 @@ def run_reference(args):
 GEMV_SHAPES = [(576, 576), (192, 576), (1536, 576), (576, 1536), (960, 960), (2560, 960), (960, 2560), (49152, 576)]
 
 
+def gemv_points(torch, P, steps: int, shapes=GEMV_SHAPES, ms=(1, 5, 9, 16), modes=("hot", "cold")):
+    """BASELINE config 2 points: isolated Q4 GEMV / skinny GEMM.  For every point both entry points are
+    timed over a CUDA graph of back-to-back launches: `gemv` = mllm_gemv_q4 (CUDA-core, tensor-core or
+    bulk-staged tensor-core kernel, picked per shape) and `gemm` = mllm_gemm_q4 (the token-batch
+    tensor-core GEMM); hot = one weight matrix reused, cold = a rotating set of copies larger than L2.
+    GB/s counts packed nibbles + scales (out*in/2 + out*in/32*4 bytes) per launch.  Returns (points,
+    kernel launches)."""
+    rng = np.random.default_rng(1)
+    st = torch.cuda.Stream()
+    rows, launches, reps = [], 0, 50
+    for (R, C) in shapes:
+        w = (rng.standard_normal((R, C), dtype=np.float32) * np.float32(0.02))
+        packed, scales = P.quant_q4(w)
+        bytes_w = packed.nbytes + scales.nbytes
+        ncopy = max(1, -(-2 * L2_BYTES // bytes_w))
+        pk = torch.from_numpy(np.ascontiguousarray(packed).reshape(-1)).cuda()
+        sc = torch.from_numpy(np.ascontiguousarray(scales).reshape(-1)).cuda()
+        pks = pk.repeat(ncopy).view(ncopy, -1)
+        scs = sc.repeat(ncopy).view(ncopy, -1)
+        for M in ms:
+            x = torch.from_numpy(rng.standard_normal((M, C), dtype=np.float32)).cuda()
+            y = torch.empty((M, R), device="cuda")
+            point = {"shape": f"{R}x{C}", "M": M, "weight_bytes": bytes_w}
+            for path, fn in (("gemv", P.gemv_q4_device), ("gemm", P.gemm_q4_device)):
+                for mode in modes:
+                    n = reps if mode == "hot" else min(ncopy, 4096)
+                    idx = [0] * n if mode == "hot" else list(range(n))
+                    with torch.cuda.stream(st):
+                        for i in range(3):  # warm-up (allocates the GEMM workspace before capture)
+                            fn(pks[0].data_ptr(), scs[0].data_ptr(), x.data_ptr(), y.data_ptr(), R, C, M, st.cuda_stream)
+                    st.synchronize()
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=st):
+                        for i in idx:
+                            fn(pks[i].data_ptr(), scs[i].data_ptr(), x.data_ptr(), y.data_ptr(), R, C, M,
+                               torch.cuda.current_stream().cuda_stream)
+                    g.replay()
+                    torch.cuda.synchronize()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    for _ in range(steps):
+                        g.replay()
+                    e1.record()
+                    e1.synchronize()
+                    us = e0.elapsed_time(e1) * 1e3 / (steps * n)
+                    launches += steps * n * (1 if path == "gemv" else 2)
+                    point[f"{path}_{mode}_us"] = us
+                    point[f"{path}_{mode}_gbs"] = bytes_w / (us * 1e-6) / 1e9
+                    del g
+            if "cold" in modes:
+                point["best_cold_gbs"] = max(point["gemv_cold_gbs"], point["gemm_cold_gbs"])
+            if "hot" in modes:
+                point["best_hot_gbs"] = max(point["gemv_hot_gbs"], point["gemm_hot_gbs"])
+            rows.append(point)
+        del pks, scs
+    return rows, launches
+
+
+def gemv_e2e(torch, P, steps: int):
+    """The headline GEMV point (lm_head 49152x576, M = 1) through the C ABI with host buffers: every
+    step copies x from pinned host memory, runs mllm_gemv_q4 and reads y back; events around it."""
+    R, C = 49152, 576
+    rng = np.random.default_rng(1)
+    packed, scales = P.quant_q4(rng.standard_normal((R, C), dtype=np.float32) * np.float32(0.02))
+    pk = torch.from_numpy(np.ascontiguousarray(packed).reshape(-1)).cuda()
+    sc = torch.from_numpy(np.ascontiguousarray(scales).reshape(-1)).cuda()
+    hx = torch.from_numpy(rng.standard_normal((1, C), dtype=np.float32)).pin_memory()
+    hy = torch.empty((1, R), dtype=torch.float32).pin_memory()
+    x = torch.empty((1, C), device="cuda")
+    y = torch.empty((1, R), device="cuda")
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+    st = torch.cuda.Stream()
+    total = 0.0
+    for i in range(steps + 3):
+        with torch.cuda.stream(st):
+            flush.fill_(1.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            x.copy_(hx, non_blocking=True)
+            P.gemv_q4_device(pk.data_ptr(), sc.data_ptr(), x.data_ptr(), y.data_ptr(), R, C, 1, st.cuda_stream)
+            hy.copy_(y, non_blocking=True)
+            e1.record(st)
+        e1.synchronize()
+        if i >= 3:
+            total += e0.elapsed_time(e1)
+    us = total * 1e3 / steps
+    return (packed.nbytes + scales.nbytes) / (us * 1e-6) / 1e9, C * 4, R * 4
+
+
+def cpu_baseline_gemv(P, threads: int):
+    """Oracle gemvQ4 (engine/infer.js:88-116, f64 sums) on the headline shape, all host threads."""
+    from oracle.oracle import gemv_q4
+    R, C = 49152, 576
+    rng = np.random.default_rng(1)
+    packed, scales = P.quant_q4(rng.standard_normal((R, C), dtype=np.float32) * np.float32(0.02))
+    x = rng.standard_normal(C, dtype=np.float32)
+    gemv_q4(packed, scales, x, threads=threads)
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < 1.0:
+        gemv_q4(packed, scales, x, threads=threads)
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return (packed.nbytes + scales.nbytes) / dt / 1e9, n
+
+
+def gemv_line(torch, P, steps: int, full: bool, cpu: bool) -> dict:
+    """Config 2 as a JSON object: the headline point (lm_head shape, M = 1, cold L2) with its roofline,
+    e2e and CPU baseline, plus every shape x M point (cold; hot too when `full`)."""
+    hbm, _, peak_kind = peaks()
+    rows, launches = gemv_points(torch, P, steps, modes=("hot", "cold") if full else ("cold",))
+    head = next(r for r in rows if r["shape"] == "49152x576" and r["M"] == 1)
+    e2e, h2d, d2h = gemv_e2e(torch, P, max(steps, 3))
+    out = {
+        "metric": "Q4 g32 GEMV weight GB/s (lm_head 49152x576, M=1, cold L2)", "value": head["best_cold_gbs"],
+        "unit": "GB/s", "n_gpus": 1, "steps": steps, "warmup": 3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4xf32", "data": "synthetic (W ~ N(0,0.02) Q4 g32 seed 1, x ~ N(0,1))",
+        "config": {"workload": "config2 gemv microbench", "shapes": [f"{r}x{c}" for r, c in GEMV_SHAPES],
+                   "M": [1, 5, 9, 16], "timing": "CUDA graph of back-to-back launches, events around replays",
+                   "cold": "rotating copies, total > 2x L2"},
+        "e2e": {"value": e2e, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "hbm", "achieved": head["best_cold_gbs"], "peak": hbm, "unit": "GB/s",
+                     "frac": head["best_cold_gbs"] / hbm, "peak_kind": peak_kind,
+                     "traffic": GEMV_LM_TRAFFIC_PER_LAUNCH,
+                     "kernel": "gemv_q4_bulk_kernel<1,2,2,2> (mllm_gemv_q4 on 49152x576, M=1; two CTAs per SM)"},
+        "gpu_launches": launches, "points": rows,
+    }
+    if cpu:
+        threads = os.cpu_count() or 1
+        v, n = cpu_baseline_gemv(P, threads)
+        out["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
+                               "sample": f"oracle gemvQ4 (f64 sums) on 49152x576, M=1, {n} calls in 1 s"}
+    return out
+
+
 def run_gemv(args):
-    """isolated Q4 GEMV / skinny GEMM on the config's shapes and M in {1, 5, 9, 16}.
-    For every point both entry points are timed over a CUDA graph of back-to-back launches:
-    `gemv` = mllm_gemv_q4 (CUDA-core, tensor-core or bulk-staged tensor-core kernel, picked per shape) and
-    `gemm` = mllm_gemm_q4 (the token-batch tensor-core GEMM); hot = one weight matrix reused, cold = a
-    rotating set of copies larger than L2.  GB/s counts packed nibbles + scales (out*in/2 + out*in/32*4
-    bytes) per launch."""
+    """--workload gemv: config 2 alone (hot and cold), one JSON line."""
     import torch
     ws, rank, local = dist_setup()
     if rank != 0:
         return
     torch.cuda.set_device(local)
     P = pkg()
-    rng = np.random.default_rng(1)
-    hbm, _, peak_kind = peaks()
-    st = torch.cuda.Stream()
-    rows = []
-    launches = 0
-    reps = 50
     with ClockSampler(local) as clk:
-        for (R, C) in GEMV_SHAPES:
-            w = (rng.standard_normal((R, C), dtype=np.float32) * np.float32(0.02))
-            packed, scales = P.quant_q4(w)
-            bytes_w = packed.nbytes + scales.nbytes
-            ncopy = max(1, -(-2 * L2_BYTES // bytes_w))
-            pk = torch.from_numpy(np.ascontiguousarray(packed).reshape(-1)).cuda()
-            sc = torch.from_numpy(np.ascontiguousarray(scales).reshape(-1)).cuda()
-            pks = pk.repeat(ncopy).view(ncopy, -1)
-            scs = sc.repeat(ncopy).view(ncopy, -1)
-            for M in (1, 5, 9, 16):
-                x = torch.from_numpy(rng.standard_normal((M, C), dtype=np.float32)).cuda()
-                y = torch.empty((M, R), device="cuda")
-                point = {"shape": f"{R}x{C}", "M": M, "weight_bytes": bytes_w}
-                for path, fn in (("gemv", P.gemv_q4_device), ("gemm", P.gemm_q4_device)):
-                    for mode in ("hot", "cold"):
-                        n = reps if mode == "hot" else min(ncopy, 4096)
-                        idx = [0] * n if mode == "hot" else list(range(n))
-                        with torch.cuda.stream(st):
-                            for i in range(3):  # warm-up (allocates the GEMM workspace before capture)
-                                fn(pks[0].data_ptr(), scs[0].data_ptr(), x.data_ptr(), y.data_ptr(), R, C, M, st.cuda_stream)
-                        st.synchronize()
-                        g = torch.cuda.CUDAGraph()
-                        with torch.cuda.graph(g, stream=st):
-                            for i in idx:
-                                fn(pks[i].data_ptr(), scs[i].data_ptr(), x.data_ptr(), y.data_ptr(), R, C, M,
-                                   torch.cuda.current_stream().cuda_stream)
-                        g.replay()
-                        torch.cuda.synchronize()
-                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                        e0.record()
-                        for _ in range(args.steps):
-                            g.replay()
-                        e1.record()
-                        e1.synchronize()
-                        us = e0.elapsed_time(e1) * 1e3 / (args.steps * n)
-                        launches += args.steps * n * (1 if path == "gemv" else 2)
-                        point[f"{path}_{mode}_us"] = us
-                        point[f"{path}_{mode}_gbs"] = bytes_w / (us * 1e-6) / 1e9
-                        del g
-                best = max(point["gemv_cold_gbs"], point["gemm_cold_gbs"])
-                point["best_cold_gbs"] = best
-                point["best_hot_gbs"] = max(point["gemv_hot_gbs"], point["gemm_hot_gbs"])
-                rows.append(point)
-            del pks, scs
-    head = next(r for r in rows if r["shape"] == "49152x576" and r["M"] == 1)
-    line = {
-        "metric": "Q4 g32 GEMV weight GB/s (lm_head 49152x576, M=1, cold L2)", "value": head["best_cold_gbs"],
-        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": 3, "ms_per_step": None,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4xf32",
-        "data": "synthetic (W ~ N(0,0.02) Q4 g32 seed 1, x ~ N(0,1))",
-        "config": {"workload": "config2 gemv microbench", "shapes": [f"{r}x{c}" for r, c in GEMV_SHAPES],
-                   "M": [1, 5, 9, 16], "timing": "CUDA graph of back-to-back launches, events around replays",
-                   "cold": "rotating copies, total > 2x L2"},
-        "roofline": {"bound": "hbm", "achieved": head["best_cold_gbs"], "peak": hbm, "unit": "GB/s",
-                     "frac": head["best_cold_gbs"] / hbm, "peak_kind": peak_kind,
-                     "traffic": GEMV_LM_TRAFFIC_PER_LAUNCH,
-                     "kernel": "gemv_q4_bulk_kernel<1,2,2,2> (mllm_gemv_q4 on 49152x576, M=1; two CTAs per SM)"},
-        "gpu_launches": launches, "points": rows, "clocks": clk.summary(),
-    }
+        line = gemv_line(torch, P, args.steps, True, not args.no_cpu_baseline)
+    line["warmup"] = args.warmup
+    line["ms_per_step"] = None
+    line["clocks"] = clk.summary()
     print(json.dumps(line), flush=True)
 
 
-def run_decode(args):
-    import torch
-    ws, rank, local = dist_setup()
-    dist = None
-    if ws > 1:
-        import datetime
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    torch.cuda.set_device(local)
-    P = pkg()
-    W = WORKLOADS[args.workload]
+DATA_TEXT = "synthetic (seeded N(0,0.02) Q4 weights, seeded prompt ids; real checkpoints are LFS stubs)"
+DECODE_KERNEL = {
+    "decode": "cdec_kernel (one 16-CTA cluster, whole generate call)",
+    "gpt2": "decode1_kernel (148 CTAs, whole generate call)",
+}
+
+
+def measure_generate(torch, P, key: str, local: int, rank: int, ws: int, dist, steps: int, warmup: int,
+                     cpu_threads: int) -> dict:
+    """One generate workload (configs 1, 3, 4) on this rank's GPU: `steps` timed generate calls after
+    `warmup`, device path (prompt and ids resident in HBM) and e2e path (host buffers through
+    mllm_generate), L2 flushed before each; max over ranks.  cpu_threads > 0 adds the oracle baseline on
+    rank 0 at N = 1."""
+    W = WORKLOADS[key]
     name, seed, n_prompt, n_new, spec_k = W["model"], W["seed"], W["prompt"], W["new"], W.get("spec_k", 0)
     cfg = P.CONFIGS[name]
     data = P.synthetic_pgw(name, seed, cache_dir=CACHE)
@@ -469,13 +551,11 @@ def run_decode(args):
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=f"cuda:{local}")
     h_prompt = torch.from_numpy(prompt).pin_memory()
     h_out = torch.zeros(n_new + 16, dtype=torch.int32).pin_memory()
-
     launches = [0]
-
     spec_stats = []
 
-    def step_device():
-        st = eng.generate_device(d_ids.data_ptr(), n_prompt, d_out.data_ptr(), n_new, -1, spec_k, 3)
+    def step_device(k=spec_k):
+        st = eng.generate_device(d_ids.data_ptr(), n_prompt, d_out.data_ptr(), n_new, -1, k, 3)
         assert st.n_generated == n_new, st.n_generated
         launches[0] += st.kernel_launches
         spec_stats.append((st.spec_hits, st.spec_tries, st.forwards))
@@ -505,7 +585,7 @@ def run_decode(args):
                 dev_ms.append(st.total_ms)
         return total, dev_ms
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step_device()
         step_e2e()
     torch.cuda.synchronize()
@@ -513,73 +593,109 @@ def run_decode(args):
         dist.barrier()
     torch.cuda.synchronize()
     launches[0] = 0
+    spec_stats.clear()
     with ClockSampler(local) as clk:
-        t_dev, dev_ms = timed(step_device, args.steps)
+        t_dev, dev_ms = timed(step_device, steps)
         torch.cuda.synchronize()
-        t_e2e, _ = timed(step_e2e, args.steps)
+        t_e2e, _ = timed(step_e2e, steps)
     torch.cuda.synchronize()
+    gpu_launches = launches[0]
     t_dev, t_e2e = max_over_ranks(dist, [t_dev, t_e2e], f"cuda:{local}")
-    if dist:
-        dist.barrier()
-    value = aggregate_rate(n_new, args.steps, ws, t_dev)
-    e2e = aggregate_rate(n_new, args.steps, ws, t_e2e)
-    ms_step = t_dev / args.steps
+    value = aggregate_rate(n_new, steps, ws, t_dev)
+    e2e = aggregate_rate(n_new, steps, ws, t_e2e)
+    ms_step = t_dev / steps
     hbm, _, peak_kind = peaks()
     alg = decode_algorithmic_bytes(cfg, n_prompt, n_new)
     achieved = alg / (ms_step / 1e3) / 1e9
+    traffic = DECODE_TRAFFIC_PER_CALL.get(W["workload"])
+    w_bytes = decode_weight_bytes(cfg)
     line = {
         "metric": W["metric"],
-        "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "value": value, "unit": "tok/s", "n_gpus": ws, "steps": steps, "warmup": warmup,
         "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4xf32",
-        "data": "synthetic (seeded N(0,0.02) Q4 weights, seeded uniform prompt ids; real checkpoints are LFS stubs)",
-        "config": {"workload": W["workload"], "model": W["model_text"],
-                   "global_batch": ws, "seq_len": n_prompt + n_new, "parallelism": f"replicas x{ws}",
-                   "l2": (f"flushed (256 MB write) before every timed step; Q4 weights "
-                          f"{decode_weight_bytes(cfg) / 1e6:.0f} MB "
-                          + ("fit in L2 within a step" if decode_weight_bytes(cfg) < L2_BYTES else
-                             "exceed L2, re-read from HBM every forward")),
-                   "tokens_per_step": n_new,
-                   "launches_per_step": launches[0] // max(args.steps, 1),
-                   "path": (f"prefill as token-batch tensor-core forwards, then one CUDA-graph replay per "
-                            f"speculation iteration (k_spec_prepare, {spec_k + 1}-row verify forward, k_spec_accept)"
-                            if spec_k else
-                            f"prefill as token-batch tensor-core forwards, then the {n_new - 1} decode steps in one "
-                            f"persistent single-token kernel launch")},
+        "data": DATA_TEXT,
+        "config": config_of(W, ws),
+        "notes": {"l2": (f"flushed (256 MB write) before every timed step; Q4 weights {w_bytes / 1e6:.0f} MB "
+                         + ("fit in L2 within a step" if w_bytes < L2_BYTES else
+                            "exceed L2, re-read from HBM every forward")),
+                  "tokens_per_step": n_new, "launches_per_step": gpu_launches // max(steps, 1),
+                  "path": (f"prefill as token-batch tensor-core forwards, then one CUDA-graph replay per "
+                           f"speculation iteration (k_spec_prepare, {spec_k + 1}-row verify forward, k_spec_accept)"
+                           if spec_k else
+                           f"prefill as token-batch tensor-core forwards, then the {n_new - 1} decode steps in one "
+                           f"persistent single-token kernel launch ({DECODE_KERNEL.get(key, 'cdec_kernel')})")},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": n_prompt * 4, "d2h_bytes_per_step": n_new * 4 + 68},
-        "gpu_launches": launches[0],
+        "gpu_launches": gpu_launches,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": peak_kind, "traffic": DECODE_TRAFFIC_PER_CALL.get(W["workload"]),
+                     "peak_kind": peak_kind, "traffic": traffic,
+                     "limiter": ("latency: the weights stay L2-resident between tokens (DRAM traffic "
+                                 f"{traffic / alg:.1%} of the algorithmic bytes), so the per-layer chain of "
+                                 "stage exchanges sets the time" if traffic else
+                                 "latency of the per-token chain of stages (see the profiles)"),
                      "kernel": ("whole generate call (token-batch prefill + graph-replayed speculation iterations)"
-                                if spec_k else "decode1_kernel<3,6> (whole generate call)"),
+                                if spec_k else DECODE_KERNEL.get(key, "cdec_kernel") ),
                      "algorithmic_bytes_per_launch": alg,
                      "kernel_ms_device_timer": float(np.mean(dev_ms)) if dev_ms else None},
         "clocks": clk.summary(),
     }
     if spec_k:
-        hits = sum(h for h, _, _ in spec_stats[-args.steps:]) / args.steps
-        tries = sum(t for _, t, _ in spec_stats[-args.steps:]) / args.steps
-        fw = sum(f for _, _, f in spec_stats[-args.steps:]) / args.steps
+        hits = sum(h for h, _, _ in spec_stats[:steps]) / steps
+        tries = sum(t for _, t, _ in spec_stats[:steps]) / steps
+        fw = sum(f for _, _, f in spec_stats[:steps]) / steps
         line["speculation"] = {"spec_k": spec_k, "ngram": 3, "spec_hits": hits, "spec_tries": tries,
                                "acceptance_rate": hits / max(tries * spec_k, 1), "accepted_per_try": hits / max(tries, 1),
                                "forwards_per_call": fw, "tokens_per_forward": n_new / max(fw, 1)}
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        v, pre, per = cpu_baseline_decode(data, prompt, n_new, 1, 4)
-        line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": 1, "kind": "port",
-                                "sample": f"oracle (C restatement of engine/infer.js), 1 thread: {n_prompt}-token "
-                                          f"prefill ({pre:.2f} s) + 4 decode steps ({per*1e3:.0f} ms/token), "
-                                          f"extrapolated to {n_new - 1} decode steps (greedy, no speculation)"}
-    if spec_k and rank == 0:
-        # the same model and prompt without speculation, for the speed-up
-        greedy = []
-        for _ in range(2):
-            st = eng.generate_device(d_ids.data_ptr(), n_prompt, d_out.data_ptr(), n_new, -1, 0, 3)
-            greedy.append(st.total_ms)
-        line["speculation"]["greedy_tok_s"] = n_new / (min(greedy) / 1e3)
-        line["speculation"]["speedup_vs_greedy"] = value / line["speculation"]["greedy_tok_s"]
+        # the same model and prompt without speculation, for the speed-up (same timing, same flush)
+        t_g, _ = timed(lambda: step_device(0), max(2, min(steps, 3)))
+        t_g = max_over_ranks(dist, [t_g], f"cuda:{local}")[0]
+        greedy = n_new * max(2, min(steps, 3)) / (t_g / 1e3)
+        line["speculation"]["greedy_tok_s"] = greedy
+        line["speculation"]["speedup_vs_greedy"] = (value / ws) / greedy
+    if rank == 0 and ws == 1 and cpu_threads > 0:
+        sample = 4
+        v, pre, per = cpu_baseline_decode(data, prompt, n_new, cpu_threads, sample)
+        line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cpu_threads, "kind": "port",
+                                "sample": f"oracle (C restatement of engine/infer.js), {cpu_threads} thread(s): "
+                                          f"{n_prompt}-token prefill ({pre:.2f} s) + {sample} greedy decode steps "
+                                          f"({per*1e3:.0f} ms/token), extrapolated to {n_new - 1} decode steps"}
     eng.destroy()
-    if not args.no_batched and args.workload == "decode":
-        line["batched"] = run_batched_leg(torch, P, local, rank, ws, dist, args.batched_steps, 1,
-                                          not args.no_cpu_baseline)
+    return line
+
+
+def run_decode(args):
+    import torch
+    ws, rank, local = dist_setup()
+    dist = None
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    P = pkg()
+    cpu = not args.no_cpu_baseline
+    line = measure_generate(torch, P, args.workload, local, rank, ws, dist, args.steps, args.warmup, 1 if cpu else 0)
+    if args.workload == "decode" and not args.no_batched:
+        line["batched"] = run_batched_leg(torch, P, local, rank, ws, dist, args.batched_steps, 1, cpu)
+    if args.workload == "decode" and not args.no_extra:
+        threads = os.cpu_count() or 1
+        ls, lw = args.leg_steps, 2
+        line["gpt2"] = measure_generate(torch, P, "gpt2", local, rank, ws, dist, ls, lw, threads if cpu else 0)
+        line["spec4"] = measure_generate(torch, P, "spec4", local, rank, ws, dist, ls, lw, 0)
+        line["spec8"] = measure_generate(torch, P, "spec8", local, rank, ws, dist, ls, lw, 0)
+        if cpu and rank == 0 and ws == 1:
+            W = WORKLOADS["spec4"]
+            data = P.synthetic_pgw(W["model"], W["seed"], cache_dir=CACHE)
+            prompt = P.copy_span_prompt(W["prompt"], P.CONFIGS[W["model"]]["vocabSize"], W["seed"])
+            v, pre, per = cpu_baseline_decode(data, prompt, W["new"], threads, 2)
+            cb = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
+                  "sample": f"oracle greedy (no speculation), {threads} threads: {W['prompt']}-token prefill "
+                            f"({pre:.2f} s) + 2 decode steps ({per*1e3:.0f} ms/token), extrapolated to "
+                            f"{W['new'] - 1} decode steps"}
+            line["spec4"]["cpu_baseline"] = cb
+            line["spec8"]["cpu_baseline"] = cb
+        if rank == 0:
+            line["gemv"] = gemv_line(torch, P, 3, False, cpu)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist:
@@ -597,6 +713,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the config-5 batched sub-object")
     ap.add_argument("--batched-steps", type=int, default=3)
+    ap.add_argument("--leg-steps", type=int, default=3, help="timed steps of the config 3 and 4 sub-objects")
+    ap.add_argument("--no-extra", action="store_true", help="only config 1 (and config 5 unless --no-batched)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -6,27 +6,32 @@
 // every CTA pushes its slice of the stage output into the same buffer of all 16 CTAs with st.async,
 // and each receiving buffer has an mbarrier that completes when all of the stage's bytes have landed.
 //
-//   x (+ sum of squares)  -> QKV rows (x 1/RMS)                   -> qkv        (all CTAs)
+//   x (+ sums of squares)  -> QKV rows (x 1/RMS)                    -> qkv        (all CTAs)
 //   qkv -> RoPE, causal attention of unit (kv head, position split) -> partials  (all CTAs)
-//   partials -> merge -> proj rows + residual                      -> x1 (+ ss) (all CTAs)
-//   x1 -> w1/w3 rows (x 1/RMS) -> SiLU(u) * v                      -> h         (all CTAs)
-//   h -> w2 rows + residual                                         -> x2 (+ ss) (all CTAs)
+//   partials -> merge -> proj rows + residual                       -> x1 (+ ss) (all CTAs)
+//   x1 -> w1/w3 rows (x 1/RMS) -> SiLU(u) * v                       -> h         (all CTAs)
+//   h -> w2 rows + residual                                          -> x2 (+ ss) (all CTAs)
 // then the final RMSNorm, the lm_head rows of each CTA with a local argmax, and an exchange of the 16
 // candidates (engine/infer.js:240-250: the lowest index wins a tie).
 //
-// Row dot products run on the tensor cores (mma.sync m16n8k16, fp32 accumulation): a 16-row x 32-wide
-// weight group is one record of a warp's private stream; nibbles become exact fp16 (q - 8) with four
-// LOP3 and four half2 fix-ups per 8 values; the activation is split into fp16 hi + lo halves that fill
-// B columns 0 and 1 (relative residual <= 2^-22); each group's sum is scaled by its fp32 scale.  The
-// weights are repacked at load time into one stream per (CTA, warp) in the order the warp consumes
-// them, and every warp keeps a ring of kCdRing records filled ahead of use with 16-byte cp.async, so
-// weight fetch from L2 overlaps the exchanges.  On one 16-SM cluster a 16-byte load stream reaches
-// about 1.25 TB/s and an all-to-all exchange costs about 0.4 us (measured on B200).
+// Row dot products run on the CUDA cores in fp32 (engine/infer.js:88-116 with f32 instead of f64
+// sums).  A 16-row x 32-wide weight group is one 320-byte record of a warp's private stream: lane
+// (gid, t) holds word t (8 nibbles) of rows gid and gid + 8, and its four lanes t = 0..3 add their
+// partial sums at the end of a tile.  A nibble becomes an exact fp32 (q - 8) 16^e with one LOP3
+// (2^23 + q 16^e from the mantissa bits, e = 0..4) and one packed subtraction; the activation is
+// stored pre-scaled by 16^-e, so every product (q - 8) x is formed exactly and rounded once, as a
+// plain fp32 multiply would.  Packed f32x2 adds and FMAs halve the floating-point instructions.
+// (Measured on B200: legacy mma.sync tiles were bound by the tensor pipe, about 21 pipe cycles per
+// m16n8k16 per SM, 4x slower than this.)
+//
+// The weights are repacked at load time into one stream per (CTA, warp) in the order the warp
+// consumes them; every warp keeps a ring of kCdRing records filled ahead of use with 16-byte
+// cp.async, so weight fetch overlaps the exchanges.  Per-layer vectors (norm gains, the RoPE row of
+// the position) are fetched into registers a layer or a token ahead.
 //
 // Every wait is bounded (RunArgs::wait_ns, default 0.5 s).  A CTA whose wait runs out raises the
 // device error flag; the others see it in their next wait; all CTAs then meet at the final cluster
 // barrier (so no CTA leaves while another may still write into its shared memory) and return.
-#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -34,7 +39,6 @@
 
 #include "cdec.cuh"
 #include "device_common.cuh"
-#include "q4mma.cuh"
 
 namespace mllm {
 namespace cd {
@@ -52,10 +56,15 @@ __device__ __forceinline__ uint32_t mapa(uint32_t a, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(o) : "r"(a), "r"(rank));
   return o;
 }
-// 16-byte store into CTA `rank`'s shared memory; completes bytes on that CTA's mbarrier.
+// Stores into CTA `rank`'s shared memory that complete their bytes on that CTA's mbarrier.
 __device__ __forceinline__ void st_async4(uint32_t raddr, float4 v, uint32_t rbar) {
   asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(raddr),
                "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(rbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async1(uint32_t raddr, float v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr),
+               "r"(__float_as_uint(v)), "r"(rbar)
                : "memory");
 }
 __device__ __forceinline__ void bar_init(uint32_t bar, int count) {
@@ -94,6 +103,62 @@ __device__ __forceinline__ float2 ldcg_f2(const float* p) {
   return v;
 }
 
+// Packed fp32 pairs (f32x2 adds and FMAs on sm_100).
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 up2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// Nibble i of a word (bits 4i, element k = i of the lane's 8) is taken at the scale 16^e(i) that leaves
+// it inside a float mantissa without a shift: e = 0..4 for i = 0..4 and, after one shift by 12 bits,
+// e = 2..4 for i = 5..7.
+__host__ __device__ constexpr int cd_nib_exp(int i) { return i < 5 ? i : i - 3; }
+
+// sum_i (q_i - 8) x_i for the 8 nibbles of w against the pre-scaled activations a[i] = x_i 16^-e(i).
+__device__ __forceinline__ float dot8(uint32_t w, const float4& a0, const float4& a1) {
+  const uint32_t w12 = w >> 12;
+  const float f0 = __uint_as_float((w & 0x0000Fu) | 0x4B000000u);
+  const float f1 = __uint_as_float((w & 0x000F0u) | 0x4B000000u);
+  const float f2 = __uint_as_float((w & 0x00F00u) | 0x4B000000u);
+  const float f3 = __uint_as_float((w & 0x0F000u) | 0x4B000000u);
+  const float f4 = __uint_as_float((w & 0xF0000u) | 0x4B000000u);
+  const float f5 = __uint_as_float((w12 & 0x00F00u) | 0x4B000000u);
+  const float f6 = __uint_as_float((w12 & 0x0F000u) | 0x4B000000u);
+  const float f7 = __uint_as_float((w12 & 0xF0000u) | 0x4B000000u);
+  // 2^23 + 8 * 16^e: subtracting it leaves (q - 8) 16^e exactly
+  const uint64_t d01 = add2(pk2(f0, f1), pk2(-8388616.f, -8388736.f));
+  const uint64_t d23 = add2(pk2(f2, f3), pk2(-8390656.f, -8421376.f));
+  const uint64_t d45 = add2(pk2(f4, f5), pk2(-8912896.f, -8390656.f));
+  const uint64_t d67 = add2(pk2(f6, f7), pk2(-8421376.f, -8912896.f));
+  uint64_t p = mul2(d01, pk2(a0.x, a0.y));
+  p = fma2(d23, pk2(a0.z, a0.w), p);
+  p = fma2(d45, pk2(a1.x, a1.y), p);
+  p = fma2(d67, pk2(a1.z, a1.w), p);
+  const float2 r = up2(p);
+  return r.x + r.y;
+}
+
 enum { B_X2 = 0, B_QKV = 1, B_ATT = 2, B_X1 = 3, B_H = 4, B_CAND = 5, B_COUNT = 6 };
 
 // A warp's weight stream: records [0, n) per token, repeated every token; `iss` records have been
@@ -129,86 +194,33 @@ __device__ __forceinline__ void ring_ready(Ring& R, int lane) {
   }
 }
 
-// (q - 8) of the 8 nibbles of one word as 4 fp16 pairs: (k0,k4), (k1,k5), (k2,k6), (k3,k7), where
-// byte j of the word holds k 2j (low nibble) and 2j + 1 (high).  Every step is exact in fp16.
-__device__ __forceinline__ void dq8(uint32_t w, uint32_t (&o)[4]) {
-  const uint32_t w8 = w >> 8;
-  uint32_t q0 = (w & 0x000F000Fu) | 0x64006400u;
-  uint32_t q1 = (w & 0x00F000F0u) | 0x64006400u;
-  uint32_t q2 = (w8 & 0x000F000Fu) | 0x64006400u;
-  uint32_t q3 = (w8 & 0x00F000F0u) | 0x64006400u;
-  const __half2 off = __halves2half2(__float2half_rn(-1032.f), __float2half_rn(-1032.f));
-  const __half2 s16 = __halves2half2(__float2half_rn(0.0625f), __float2half_rn(0.0625f));
-  const __half2 off16 = __halves2half2(__float2half_rn(-72.f), __float2half_rn(-72.f));
-  __half2 r0 = __hadd2(*reinterpret_cast<__half2*>(&q0), off);
-  __half2 r1 = __hfma2(*reinterpret_cast<__half2*>(&q1), s16, off16);
-  __half2 r2 = __hadd2(*reinterpret_cast<__half2*>(&q2), off);
-  __half2 r3 = __hfma2(*reinterpret_cast<__half2*>(&q3), s16, off16);
-  o[0] = *reinterpret_cast<uint32_t*>(&r0);
-  o[1] = *reinterpret_cast<uint32_t*>(&r1);
-  o[2] = *reinterpret_cast<uint32_t*>(&r2);
-  o[3] = *reinterpret_cast<uint32_t*>(&r3);
-}
-
-// One record: rows gid / gid + 8 of the tile, this lane's k values 8t..8t+7 of the group.  A step-0
-// fragment takes k (8t, 8t+4) and (8t+1, 8t+5), step 1 (8t+2, 8t+6) and (8t+3, 8t+7); the B fragments
-// in `bf` follow the same order (build_bfrag).  Lanes with t == 0 accumulate rows gid and gid + 8.
-__device__ __forceinline__ void unit_mma(const uint8_t* rec, const uint4* bf_g, int lane, float& acc0, float& acc1) {
-  const int gid = lane >> 2, t = lane & 3;
-  const uint2 wv = *reinterpret_cast<const uint2*>(rec + 8 * lane);
-  const float2 sc = *reinterpret_cast<const float2*>(rec + 256 + 8 * gid);
-  uint4 b = make_uint4(0u, 0u, 0u, 0u);
-  if (gid < 2) b = bf_g[gid * 4 + t];
-  uint32_t p[4], q[4];
-  dq8(wv.x, p);
-  dq8(wv.y, q);
-  float c[4] = {0.f, 0.f, 0.f, 0.f};
-  const uint32_t a0[4] = {p[0], q[0], p[1], q[1]};
-  const uint32_t a1[4] = {p[2], q[2], p[3], q[3]};
-  mma16816(c, a0, b.x, b.y);
-  mma16816(c, a1, b.z, b.w);
-  acc0 = fmaf(c[0] + c[1], sc.x, acc0);
-  acc1 = fmaf(c[2] + c[3], sc.y, acc1);
-}
-
-// B fragments of a K-long activation (times `gain` when given): bf[g][half][t] = 4 registers of fp16
-// pairs (x[8t], x[8t+4]), (x[8t+1], x[8t+5]), (x[8t+2], x[8t+6]), (x[8t+3], x[8t+7]) of group g,
-// half 0 = hi, 1 = lo.
-__device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
-  return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
-}
-__device__ void build_bfrag(const float* x, const float* gain, int K, uint4* bf) {
-  const int G = K >> 5;
-  for (int q = threadIdx.x; q < G * 4; q += kCdThreads) {
-    const int g = q >> 2, t = q & 3, k0 = 32 * g + 8 * t;
-    __half hi[8], lo[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float v = gain ? x[k0 + j] * __ldg(gain + k0 + j) : x[k0 + j];
-      split_hi_lo(v, hi[j], lo[j]);
-    }
-    bf[(g * 2) * 4 + t] = make_uint4(pack_h2(hi[0], hi[4]), pack_h2(hi[1], hi[5]), pack_h2(hi[2], hi[6]),
-                                     pack_h2(hi[3], hi[7]));
-    bf[(g * 2 + 1) * 4 + t] = make_uint4(pack_h2(lo[0], lo[4]), pack_h2(lo[1], lo[5]), pack_h2(lo[2], lo[6]),
-                                         pack_h2(lo[3], lo[7]));
-  }
-}
-
-// This warp's share of one stage: partial row sums per (unit tile, k slice) into red.
-__device__ __forceinline__ void run_units(Ring& R, const CdGeom& g, const uint4* bf, float* red, int warp, int lane) {
+// This warp's share of one stage (see CdGeom): per unit tile, the rows' partial sums over the warp's
+// k slice, scaled per group, reduced over the lane quad, into red[(tile * KW + slice) * 16 + row].
+__device__ __forceinline__ void run_units(Ring& R, const CdGeom& g, const float* actp, float* red, int warp, int lane) {
   const int ks = warp % g.KW, ts = warp / g.KW;
   const int g0 = ks * g.G / g.KW, g1 = (ks + 1) * g.G / g.KW;
+  const int gid = lane >> 2, t = lane & 3;
   for (int tl = ts; tl < g.Tu; tl += g.TW) {
-    float a0 = 0.f, a1 = 0.f;
+    float acc0 = 0.f, acc1 = 0.f;
     for (int gg = g0; gg < g1; ++gg) {
       ring_ready(R, lane);
-      unit_mma(R.buf + (R.con % kCdRing) * kCdRecBytes, bf + gg * 8, lane, a0, a1);
+      const uint8_t* rec = R.buf + (R.con % kCdRing) * kCdRecBytes;
+      const uint2 wv = *reinterpret_cast<const uint2*>(rec + 8 * lane);
+      const float2 sc = *reinterpret_cast<const float2*>(rec + 256 + 8 * gid);
+      const float4* ap = reinterpret_cast<const float4*>(actp + 32 * gg + 8 * t);
+      const float4 a0 = ap[0], a1 = ap[1];
+      acc0 = fmaf(dot8(wv.x, a0, a1), sc.x, acc0);
+      acc1 = fmaf(dot8(wv.y, a0, a1), sc.y, acc1);
       ++R.con;
     }
-    if ((lane & 3) == 0) {
-      float* r = red + (tl * g.KW + ks) * 16 + (lane >> 2);
-      r[0] = a0;
-      r[8] = a1;
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+    if (t == 0) {
+      float* r = red + (tl * g.KW + ks) * 16 + gid;
+      r[0] = acc0;
+      r[8] = acc1;
     }
   }
 }
@@ -221,15 +233,10 @@ __device__ __forceinline__ float row_sum(const float* red, const CdGeom& g, int 
   return s;
 }
 
-// Send n floats (n % 4 == 0) from this CTA's src to shared address `dst` (the same buffer in every
-// CTA), completing on barrier `bar` of each CTA.
-__device__ __forceinline__ void push_all(const float* src, uint32_t dst, int n, uint32_t bar) {
-  const int n4 = n >> 2;
-  for (int i = threadIdx.x; i < kCdCtas * n4; i += kCdThreads) {
-    const int d = i / n4, q = i - d * n4;
-    const float4 v = reinterpret_cast<const float4*>(src)[q];
-    st_async4(mapa(dst + 16 * q, d), v, mapa(bar, d));
-  }
+// Pre-scaled stage activation for element k: x * 16^-e(k % 8) (exact).
+__device__ __forceinline__ float pre_scale(float x, int k) {
+  const int e = cd_nib_exp(k & 7);
+  return x * __uint_as_float((uint32_t)(127 - 4 * e) << 23);
 }
 
 // Bounded wait of the whole CTA for `parity` of a local barrier; false everywhere when it gave up.
@@ -249,24 +256,31 @@ __device__ __forceinline__ bool xwait(uint32_t bar, uint32_t parity, int* err, u
   return __syncthreads_and(ok);
 }
 
-// Sum of squares of this CTA's n values v (held by threads 0..n-1), in a fixed order; result in misc[16].
-__device__ __forceinline__ void block_ss(float v, float* misc) {
-  float s = warp_sum(v * v);
-  if ((threadIdx.x & 31) == 0) misc[threadIdx.x >> 5] = s;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.f;
-    for (int w = 0; w < kCdWarps; ++w) t += misc[w];
-    misc[16] = t;
-  }
-  __syncthreads();
+// 1 / RMS (eps 1e-6, engine/infer.js:134-143) of a residual buffer whose D / 4 quad partial sums of
+// squares follow its D values; every warp forms the same sum in the same order.
+__device__ __forceinline__ float inv_rms(const float* xb, int D) {
+  const int lane = threadIdx.x & 31;
+  float s = 0.f;
+  for (int q = lane; q < D / 4; q += 32) s += xb[D + q];
+  s = warp_sum(s);
+  return 1.f / sqrtf(s / D + 1e-6f);
 }
 
-__device__ __forceinline__ float inv_rms(const float* xb, int D) {
-  float s = 0.f;
-#pragma unroll
-  for (int c = 0; c < kCdCtas; ++c) s += xb[D + 4 * c];
-  return 1.f / sqrtf(s / D + 1e-6f);
+// Epilogue + exchange of a row stage: thread i takes row quad q = i / 16 of the CTA's rows and sends
+// it to CTA i % 16.  `val(i)` gives the value of local row i (0 .. nrows).  With ss, the quad's sum of
+// squares also goes to slot (first quad + q) after the destination's D values.
+template <class F>
+__device__ __forceinline__ void push_rows(int nrows, uint32_t dst, uint32_t bar, int ss_slot0, uint32_t ss_dst, F val) {
+  for (int i = threadIdx.x; i < nrows * 4; i += kCdThreads) {
+    const int q = i >> 4, d = i & 15;
+    const float4 v = make_float4(val(4 * q), val(4 * q + 1), val(4 * q + 2), val(4 * q + 3));
+    const uint32_t rb = mapa(bar, d);
+    st_async4(mapa(dst + 16 * q, d), v, rb);
+    if (ss_slot0 >= 0) {
+      const float s = fmaf(v.w, v.w, fmaf(v.z, v.z, fmaf(v.y, v.y, v.x * v.x)));
+      st_async1(mapa(ss_dst + 4 * (ss_slot0 + q), d), s, rb);
+    }
+  }
 }
 
 }  // namespace cd
@@ -282,7 +296,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int D = md.D, QKV = md.QKV, FF = md.FF, NKV = md.NKV, rep = md.NH / md.NKV;
   const int S = cd_splits(md), U = NKV * S;
-  uint4* bfrag = reinterpret_cast<uint4*>(smem + Ls.bfrag);
+  float* actp = reinterpret_cast<float*>(smem + Ls.actp);
   float* red = reinterpret_cast<float*>(smem + Ls.red);
   float* xb2 = reinterpret_cast<float*>(smem + Ls.xb2);
   float* xb1 = reinterpret_cast<float*>(smem + Ls.xb1);
@@ -290,14 +304,15 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   float* hb = reinterpret_cast<float*>(smem + Ls.hb);
   float* attb = reinterpret_cast<float*>(smem + Ls.attb);
   float* cand = reinterpret_cast<float*>(smem + Ls.cand);
-  float* att = reinterpret_cast<float*>(smem + Ls.att);
   float* outv = reinterpret_cast<float*>(smem + Ls.outv);
   float* wpart = reinterpret_cast<float*>(smem + Ls.wpart);
   float* qk = reinterpret_cast<float*>(smem + Ls.qk);
+  float* mw = reinterpret_cast<float*>(smem + Ls.mw);
+  const float** norms = reinterpret_cast<const float**>(smem + Ls.norms);
   float* misc = reinterpret_cast<float*>(smem + Ls.misc);
   int* imisc = reinterpret_cast<int*>(misc);
   const uint32_t sbar = smem_u32(smem + Ls.bars);
-  const uint32_t bytes_x = (uint32_t)(D * 4 + kCdCtas * 16);
+  const uint32_t bytes_x = (uint32_t)(D * 4 + D);  // D values + D / 4 quad sums of squares
   const uint32_t bar_bytes[B_COUNT] = {bytes_x, (uint32_t)QKV * 4, (uint32_t)(U * rep * kCdPartWords * 4), bytes_x,
                                        (uint32_t)FF * 4, (uint32_t)(kCdCtas * 16)};
   const uint64_t limit = a.wait_ns ? a.wait_ns : kWaitNs;
@@ -307,6 +322,10 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     for (int b = 0; b < B_COUNT; ++b) bar_arm(sbar + 8 * b, bar_bytes[b]);
   }
+  // norm gain pointers of every layer, then norm_f
+  for (int i = tid; i < 2 * md.n_layers; i += kCdThreads)
+    norms[i] = (i & 1) ? md.layers[i >> 1].norm2 : md.layers[i >> 1].norm1;
+  if (tid == 0) norms[2 * md.n_layers] = md.norm_f;
   __syncthreads();
   cluster_sync_all();  // every barrier is armed before any CTA sends
 
@@ -342,6 +361,16 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
     cd_stage_shape(md, CD_LM, &rows, &K, &pr);
     glm = cd_geom(rows, K, pr, c);
   }
+  // gains of this thread's elements k = tid, tid + 512 (D <= 1024): current layer and the next one
+  float g1[2], g2[2], n1[2], n2[2];
+  auto load_gains = [&](int l, float (&o1)[2], float (&o2)[2]) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int k = tid + kCdThreads * j;
+      o1[j] = k < D ? ldv_f32(norms[2 * l] + k) : 0.f;
+      o2[j] = (k < D && l < md.n_layers) ? ldv_f32(norms[2 * l + 1] + k) : 0.f;
+    }
+  };
   if (a.mode == MODE_SELFTEST_WAIT) {
     // Failure-detection self-test: phase 0 of the candidate barrier needs bytes nobody sends; the
     // wait runs out its limit and raises the error flag.
@@ -356,6 +385,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
     if (tok == a.eos) stop = 0;
   }
   if (R.n) ring_issue(R, lane);
+  load_gains(0, n1, n2);
 
   for (;;) {
     int pos;
@@ -367,34 +397,54 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       tok = a.ids[0];
       pos = a.pos0;
     }
+    // RoPE row of this position for the q / k element this thread rotates (threads < (rep + 1) * 64)
+    float rc = 1.f, rs = 0.f;
+    {
+      const int d = tid & 63;
+      if (tid < (rep + 1) * 64 && d < md.rope_dim) {
+        rc = ldv_f32(md.rope_cos + (size_t)pos * md.rope_dim + d);
+        rs = ldv_f32(md.rope_sin + (size_t)pos * md.rope_dim + d);
+      }
+    }
     // ---- embed (engine/infer.js:360-420): the dequantised tied lm_head row, in every CTA
     {
       const uint8_t* row = reinterpret_cast<const uint8_t*>(md.lm.w) + (size_t)tok * (D / 2);
       const float* sc = md.lm.s + (size_t)tok * (D / 32);
-      float ss = 0.f;
-      for (int k = tid; k < D; k += kCdThreads) {
-        const int b = row[k >> 1];
-        const float v = (float)(((k & 1) ? (b >> 4) : (b & 15)) - 8) * sc[k >> 5];
-        xb2[k] = v;
-        ss = fmaf(v, v, ss);
-      }
-      ss = warp_sum(ss);
-      if (lane == 0) misc[warp] = ss;
-      __syncthreads();
-      if (tid < 4 * kCdCtas) {
-        float t = 0.f;
-        if (tid == 0)
-          for (int w = 0; w < kCdWarps; ++w) t += misc[w];
-        xb2[D + tid] = t;  // slot 0 holds the whole sum, slots 1..15 zero
+      for (int q = tid; q < D / 4; q += kCdThreads) {
+        const uint16_t b2 = *reinterpret_cast<const uint16_t*>(row + 2 * q);
+        const float s0 = sc[q >> 3];
+        float v[4];
+        v[0] = (float)((int)(b2 & 15) - 8) * s0;
+        v[1] = (float)((int)((b2 >> 4) & 15) - 8) * s0;
+        v[2] = (float)((int)((b2 >> 8) & 15) - 8) * s0;
+        v[3] = (float)((int)((b2 >> 12) & 15) - 8) * s0;
+        *reinterpret_cast<float4*>(xb2 + 4 * q) = make_float4(v[0], v[1], v[2], v[3]);
+        xb2[D + q] = fmaf(v[3], v[3], fmaf(v[2], v[2], fmaf(v[1], v[1], v[0] * v[0])));
       }
       __syncthreads();
     }
     for (int l = 0; l < md.n_layers; ++l) {
-      const LayerDev& Ly = md.layers[l];
       if (l > 0 && !(ok = wait_bar(B_X2))) goto done;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        g1[j] = n1[j];
+        g2[j] = n2[j];
+      }
+      load_gains(l + 1 < md.n_layers ? l + 1 : l, n1, n2);
+      if (l + 1 == md.n_layers) {  // the final norm's gain rides in n1
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int k = tid + kCdThreads * j;
+          n1[j] = k < D ? ldv_f32(norms[2 * md.n_layers] + k) : 0.f;
+        }
+      }
       const float inv1 = inv_rms(xb2, D);
-      build_bfrag(xb2, Ly.norm1, D, bfrag);
-      // attention unit of this CTA and the K/V rows its warp walks first (issued before the stage)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int k = tid + kCdThreads * j;
+        if (k < D) actp[k] = pre_scale(xb2[k] * g1[j], k);
+      }
+      // attention unit of this CTA and the K/V rows its warp walks first (requested before the stage)
       const bool has_unit = c < U;
       const int kvh = c / S, sp = c % S;
       const int span = (pos + S) / S;
@@ -413,27 +463,25 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       }
       __syncthreads();
       // ---- QKV rows
-      run_units(R, gq, bfrag, red, warp, lane);
+      run_units(R, gq, actp, red, warp, lane);
       __syncthreads();
-      for (int i = tid; i < gq.T * 16; i += kCdThreads) outv[i] = inv1 * row_sum(red, gq, i);
-      __syncthreads();
-      push_all(outv, smem_u32(qkvb + 16 * gq.t0), gq.T * 16, sbar + 8 * B_QKV);
+      push_rows(gq.T * 16, smem_u32(qkvb + 16 * gq.t0), sbar + 8 * B_QKV, -1, 0,
+                [&](int i) { return inv1 * row_sum(red, gq, i); });
       if (!(ok = wait_bar(B_QKV))) goto done;
-      // ---- attention of unit (kvh, sp): RoPE'd q heads, new k and v into qk (engine/infer.js:442-495)
+      // ---- attention of unit (kvh, sp) (engine/infer.js:442-495)
       if (has_unit) {
-        const float* cs = md.rope_cos + (size_t)pos * md.rope_dim;
-        const float* sn = md.rope_sin + (size_t)pos * md.rope_dim;
-        const int rd = md.rope_dim, half = rd / 2;
-        for (int i = tid; i < (rep + 2) * 64; i += kCdThreads) {
-          const int vec = i >> 6, d = i & 63;
+        // RoPE'd q heads of the group, the new k (rotated) and v (engine/infer.js:185-225)
+        if (tid < (rep + 2) * 64) {
+          const int vec = tid >> 6, d = tid & 63;
           const float* src = vec < rep ? qkvb + (kvh * rep + vec) * 64
                                        : vec == rep ? qkvb + D + kvh * 64 : qkvb + D + NKV * 64 + kvh * 64;
           float v = src[d];
-          if (vec <= rep && d < rd) {
-            if (d < half) v = fmaf(-src[d + half], sn[d], src[d] * cs[d]);
-            else v = fmaf(src[d - half], sn[d], src[d] * cs[d]);
+          const int half = md.rope_dim / 2;
+          if (vec <= rep && d < md.rope_dim) {
+            if (d < half) v = fmaf(-src[d + half], rs, v * rc);
+            else v = fmaf(src[d - half], rs, v * rc);
           }
-          qk[i] = v;
+          qk[tid] = v;
         }
         __syncthreads();
         if (pos >= p_lo && pos < p_hi && tid < 128) {  // the cache row of this position (engine/infer.js:457-464)
@@ -465,9 +513,8 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
             kk = ldcg_f2(a.kc + (kv_base + p) * 64 + 2 * lane);
             vv = ldcg_f2(a.vc + (kv_base + p) * 64 + 2 * lane);
           }
-          // rotate the prefetched registers so that kpre[0] always belongs to the next position
 #pragma unroll
-          for (int q = 0; q + 1 < kCdKvPre; ++q) {
+          for (int q = 0; q + 1 < kCdKvPre; ++q) {  // kpre[0] always belongs to the next position
             kpre[q] = kpre[q + 1];
             vpre[q] = vpre[q + 1];
           }
@@ -496,111 +543,109 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
           wp[5 + 2 * lane] = o[h][1];
         }
         __syncthreads();
-        // the CTA's partial per head: max, sum, 2 zero words, 64 unnormalised outputs
-        for (int i = tid; i < rep * 64; i += kCdThreads) {
-          const int h = i >> 6, d = i & 63;
-          float M = -INFINITY;
-          for (int w = 0; w < kCdWarps; ++w) {
-            const float* wp = wpart + (w * rep + h) * kCdPartWords;
-            if (wp[1] > 0.f) M = fmaxf(M, wp[0]);
-          }
-          float Lsum = 0.f, O = 0.f;
-          for (int w = 0; w < kCdWarps; ++w) {
-            const float* wp = wpart + (w * rep + h) * kCdPartWords;
-            if (wp[1] > 0.f) {
-              const float fct = expf(wp[0] - M);
-              Lsum = fmaf(wp[1], fct, Lsum);
-              O = fmaf(wp[4 + d], fct, O);
-            }
-          }
-          float* op = outv + h * kCdPartWords;
-          op[4 + d] = O;
-          if (d == 0) {
-            op[0] = M;
-            op[1] = Lsum;
-            op[2] = 0.f;
-            op[3] = 0.f;
+        // per head: max over the warps, then each warp's weight exp(m_w - M); the CTA's partial is
+        // (M, sum of weighted sums, 64 weighted outputs)
+        if (tid < rep * 32) {
+          const int h = tid >> 5, w = tid & 31;
+          const float* wp = wpart + (w * rep + h) * kCdPartWords;
+          const bool live = w < kCdWarps && wp[1] > 0.f;
+          const float M = warp_max(live ? wp[0] : -INFINITY);
+          const float wt = live ? expf(wp[0] - M) : 0.f;
+          if (w < kCdWarps) mw[h * kCdWarps + w] = wt;
+          const float Ls2 = warp_sum(live ? wp[1] * wt : 0.f);
+          if (w == 0) {
+            outv[h * kCdPartWords] = M;
+            outv[h * kCdPartWords + 1] = Ls2;
+            outv[h * kCdPartWords + 2] = 0.f;
+            outv[h * kCdPartWords + 3] = 0.f;
           }
         }
         __syncthreads();
-        push_all(outv, smem_u32(attb + c * rep * kCdPartWords), rep * kCdPartWords, sbar + 8 * B_ATT);
+        if (tid < rep * 64) {
+          const int h = tid >> 6, d = tid & 63;
+          float O = 0.f;
+          for (int w = 0; w < kCdWarps; ++w) O = fmaf(wpart[(w * rep + h) * kCdPartWords + 4 + d], mw[h * kCdWarps + w], O);
+          outv[h * kCdPartWords + 4 + d] = O;
+        }
+        __syncthreads();
+        const int n4 = rep * kCdPartWords / 4;
+        const uint32_t dst = smem_u32(attb + c * rep * kCdPartWords);
+        for (int i = tid; i < kCdCtas * n4; i += kCdThreads) {
+          const int d = i / n4, q = i - d * n4;
+          st_async4(mapa(dst + 16 * q, d), reinterpret_cast<const float4*>(outv)[q], mapa(sbar + 8 * B_ATT, d));
+        }
       }
       if (!(ok = wait_bar(B_ATT))) goto done;
-      // ---- merge the splits of every head, then proj rows + residual (x1)
-      for (int i = tid; i < D; i += kCdThreads) {
-        const int h = i >> 6, d = i & 63, kv = h / rep, j = h % rep;
+      // ---- merge the splits of every head: weights exp(M_s - M) / L per (head, split), then the
+      // attention output straight into the proj activation
+      if (tid < md.NH) {
+        const int h = tid, kv = h / rep, j = h % rep;
         float M = -INFINITY;
         for (int s = 0; s < S; ++s) {
           const float* pp = attb + ((kv * S + s) * rep + j) * kCdPartWords;
           if (pp[1] > 0.f) M = fmaxf(M, pp[0]);
         }
-        float Lsum = 0.f, O = 0.f;
+        float Lsum = 0.f;
         for (int s = 0; s < S; ++s) {
           const float* pp = attb + ((kv * S + s) * rep + j) * kCdPartWords;
-          if (pp[1] > 0.f) {
-            const float fct = expf(pp[0] - M);
-            Lsum = fmaf(pp[1], fct, Lsum);
-            O = fmaf(pp[4 + d], fct, O);
-          }
+          const float wt = pp[1] > 0.f ? expf(pp[0] - M) : 0.f;
+          mw[h * kCdCtas + s] = wt;
+          Lsum = fmaf(pp[1], wt, Lsum);
         }
-        att[i] = O / Lsum;
+        const float inv = 1.f / Lsum;
+        for (int s = 0; s < S; ++s) mw[h * kCdCtas + s] *= inv;
       }
       __syncthreads();
-      build_bfrag(att, nullptr, D, bfrag);
-      __syncthreads();
-      run_units(R, gp, bfrag, red, warp, lane);
-      __syncthreads();
-      {
-        float v = 0.f;
-        if (tid < gp.T * 16) {
-          v = xb2[16 * gp.t0 + tid] + row_sum(red, gp, tid);
-          outv[tid] = v;
-        }
-        block_ss(v, misc);  // needs gp.T * 16 <= kCdThreads
+      for (int i = tid; i < D; i += kCdThreads) {
+        const int h = i >> 6, d = i & 63, kv = h / rep, j = h % rep;
+        float O = 0.f;
+        for (int s = 0; s < S; ++s) O = fmaf(attb[((kv * S + s) * rep + j) * kCdPartWords + 4 + d], mw[h * kCdCtas + s], O);
+        actp[i] = pre_scale(O, i);
       }
-      push_all(outv, smem_u32(xb1 + 16 * gp.t0), gp.T * 16, sbar + 8 * B_X1);
-      if (tid < kCdCtas)
-        st_async4(mapa(smem_u32(xb1 + D + 4 * c), tid), make_float4(misc[16], 0.f, 0.f, 0.f), mapa(sbar + 8 * B_X1, tid));
+      __syncthreads();
+      // ---- proj rows + residual (x1)
+      run_units(R, gp, actp, red, warp, lane);
+      __syncthreads();
+      push_rows(gp.T * 16, smem_u32(xb1 + 16 * gp.t0), sbar + 8 * B_X1, 4 * gp.t0, smem_u32(xb1 + D),
+                [&](int i) { return xb2[16 * gp.t0 + i] + row_sum(red, gp, i); });
       if (!(ok = wait_bar(B_X1))) goto done;
       // ---- w1 / w3 rows, SiLU(u) * v (engine/infer.js:506-527)
       const float inv2 = inv_rms(xb1, D);
-      build_bfrag(xb1, Ly.norm2, D, bfrag);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int k = tid + kCdThreads * j;
+        if (k < D) actp[k] = pre_scale(xb1[k] * g2[j], k);
+      }
       __syncthreads();
-      run_units(R, gw13, bfrag, red, warp, lane);
+      run_units(R, gw13, actp, red, warp, lane);
       __syncthreads();
-      for (int i = tid; i < gw13.T * 16; i += kCdThreads) {
+      push_rows(gw13.T * 16, smem_u32(hb + 16 * gw13.t0), sbar + 8 * B_H, -1, 0, [&](int i) {
         const int tl = i >> 4, r = i & 15;
         const float u = inv2 * row_sum(red, gw13, (2 * tl) * 16 + r);
         const float v = inv2 * row_sum(red, gw13, (2 * tl + 1) * 16 + r);
-        outv[i] = (u / (1.f + expf(-u))) * v;
-      }
-      __syncthreads();
-      push_all(outv, smem_u32(hb + 16 * gw13.t0), gw13.T * 16, sbar + 8 * B_H);
+        return (u / (1.f + expf(-u))) * v;
+      });
       if (!(ok = wait_bar(B_H))) goto done;
       // ---- w2 rows + residual (x2)
-      build_bfrag(hb, nullptr, FF, bfrag);
+      for (int k = tid; k < FF; k += kCdThreads) actp[k] = pre_scale(hb[k], k);
       __syncthreads();
-      run_units(R, gw2, bfrag, red, warp, lane);
+      run_units(R, gw2, actp, red, warp, lane);
       __syncthreads();
-      {
-        float v = 0.f;
-        if (tid < gw2.T * 16) {
-          v = xb1[16 * gw2.t0 + tid] + row_sum(red, gw2, tid);
-          outv[tid] = v;
-        }
-        block_ss(v, misc);
-      }
-      push_all(outv, smem_u32(xb2 + 16 * gw2.t0), gw2.T * 16, sbar + 8 * B_X2);
-      if (tid < kCdCtas)
-        st_async4(mapa(smem_u32(xb2 + D + 4 * c), tid), make_float4(misc[16], 0.f, 0.f, 0.f), mapa(sbar + 8 * B_X2, tid));
+      push_rows(gw2.T * 16, smem_u32(xb2 + 16 * gw2.t0), sbar + 8 * B_X2, 4 * gw2.t0, smem_u32(xb2 + D),
+                [&](int i) { return xb1[16 * gw2.t0 + i] + row_sum(red, gw2, i); });
     }
     // ---- final RMSNorm, lm_head rows of this CTA, argmax candidates (engine/infer.js:240-250)
     if (!(ok = wait_bar(B_X2))) goto done;
     {
       const float invf = inv_rms(xb2, D);
-      build_bfrag(xb2, md.norm_f, D, bfrag);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int k = tid + kCdThreads * j;
+        if (k < D) actp[k] = pre_scale(xb2[k] * n1[j], k);
+      }
+      load_gains(0, n1, n2);  // the next token's first layer
       __syncthreads();
-      run_units(R, glm, bfrag, red, warp, lane);
+      run_units(R, glm, actp, red, warp, lane);
       __syncthreads();
       float best = -INFINITY;
       int bidx = 0x7fffffff;
@@ -691,11 +736,8 @@ done:
 bool cd_supported(const ModelDev& m, size_t smem_cap) {
   if (m.arch != 0 || m.D != m.NH * 64 || m.NH % m.NKV || m.NH / m.NKV > 4) return false;
   if (m.D % 16 || m.QKV % 16 || m.FF % 16 || m.D % 32 || m.FF % 32) return false;
-  if (m.NKV > kCdCtas || m.rope_dim > 64 || m.rope_dim % 2) return false;
-  for (int c = 0; c < kCdCtas; ++c) {
-    if (cd_geom(m.D, m.D, false, c).T * 16 > kCdThreads) return false;
-    if (cd_geom(m.D, m.FF, false, c).T * 16 > kCdThreads) return false;
-  }
+  if (m.NKV > kCdCtas || m.rope_dim > 64 || m.rope_dim % 2 || m.D > 2 * kCdThreads) return false;
+  if ((m.NH / m.NKV + 2) * 64 > kCdThreads || m.NH > kCdThreads) return false;
   return (size_t)cd_smem(m).total <= smem_cap;
 }
 

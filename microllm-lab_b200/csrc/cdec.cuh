@@ -73,8 +73,8 @@ __host__ __device__ inline int cd_splits(const ModelDev& m) { return m.NKV >= kC
 
 // Shared-memory plan of the kernel (byte offsets; every region 16-byte aligned).
 struct CdSmem {
-  int ring, bfrag, red, xb2, xb1, qkv, hb, attb, cand, att, outv, wpart, qk, hist, misc, bars, total;
-  int red_floats, outv_floats;
+  int ring, actp, red, xb2, xb1, qkv, hb, attb, cand, outv, wpart, qk, mw, norms, misc, bars, total;
+  int red_floats;
 };
 
 __host__ __device__ inline int cd_align16(int b) { return (b + 15) & ~15; }
@@ -82,7 +82,7 @@ __host__ __device__ inline int cd_align16(int b) { return (b + 15) & ~15; }
 __host__ __device__ inline CdSmem cd_smem(const ModelDev& m) {
   CdSmem s;
   const int rep = m.NH / m.NKV;
-  int redf = 16, outf = 16;
+  int redf = 16;
   for (int st = 0; st <= CD_LM; ++st) {
     int rows, K;
     bool paired;
@@ -90,11 +90,8 @@ __host__ __device__ inline CdSmem cd_smem(const ModelDev& m) {
     for (int c = 0; c < kCdCtas; ++c) {
       const CdGeom g = cd_geom(rows, K, paired, c);
       redf = redf > g.Tu * g.KW * 16 ? redf : g.Tu * g.KW * 16;
-      if (st != CD_LM) outf = outf > g.Tu * 16 ? outf : g.Tu * 16;
     }
   }
-  if (outf < rep * kCdPartWords) outf = rep * kCdPartWords;  // outv also stages the attention partial
-  const int gmax = (m.FF > m.D ? m.FF : m.D) / 32;
   int o = 0;
   auto take = [&](int bytes) {
     const int at = o;
@@ -102,24 +99,23 @@ __host__ __device__ inline CdSmem cd_smem(const ModelDev& m) {
     return at;
   };
   s.ring = take(kCdWarps * kCdRing * kCdRecBytes);
-  s.bfrag = take(gmax * 8 * 16);
+  s.actp = take((m.FF > m.D ? m.FF : m.D) * 4);
   s.red = take(redf * 4);
-  s.xb2 = take((m.D + 64) * 4);
-  s.xb1 = take((m.D + 64) * 4);
+  s.xb2 = take((m.D + m.D / 4) * 4);
+  s.xb1 = take((m.D + m.D / 4) * 4);
   s.qkv = take(m.QKV * 4);
   s.hb = take(m.FF * 4);
   s.attb = take(kCdCtas * rep * kCdPartWords * 4);
   s.cand = take(kCdCtas * 16);
-  s.att = take(m.D * 4);
-  s.outv = take(outf * 4);
+  s.outv = take(rep * kCdPartWords * 4);
   s.wpart = take(kCdWarps * rep * kCdPartWords * 4);
   s.qk = take((rep + 2) * 64 * 4);
-  s.hist = take((m.kv_len + 64) * 4);
+  s.mw = take((m.NH + 4) * kCdCtas * 4);  // merge weights [head][split], attention warp weights [head][warp]
+  s.norms = take((2 * m.n_layers + 1) * 8);
   s.misc = take(64 * 4);
   s.bars = take(8 * 8);
   s.total = o;
   s.red_floats = redf;
-  s.outv_floats = outf;
   return s;
 }
 

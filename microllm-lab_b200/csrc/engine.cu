@@ -646,9 +646,9 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, k == e->kernel_multi ? e->smem_multi : e->smem_single);
     if (per_sm < 1) return bad(MLLM_ERR_CUDA, "decode kernel cannot be resident with its shared memory");
   }
-  // ---- cluster decode: weights repacked into per-(CTA, warp) streams (MLLM_CLUSTER_DECODE=0: off)
+  // ---- cluster decode: weights repacked into per-(CTA, warp) streams (MLLM_CLUSTER_DECODE=1: on)
   {
-    bool want = true;
+    bool want = false;
     if (const char* v = getenv("MLLM_CLUSTER_DECODE")) want = atoi(v) != 0;
     if (want && cd_supported(md, smem_cap) && cd_setup(smem_cap) == cudaSuccess &&
         cd_max_clusters(cd_smem_bytes(md)) >= 1) {
