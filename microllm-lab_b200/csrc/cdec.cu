@@ -24,16 +24,20 @@
 // (Measured on B200: legacy mma.sync tiles were bound by the tensor pipe, about 21 pipe cycles per
 // m16n8k16 per SM, 4x slower than this.)
 //
-// The weights are repacked at load time into one stream per (CTA, warp) in the order the warp
-// consumes them; every warp keeps a ring of kCdRing records filled ahead of use with 16-byte
-// cp.async, so weight fetch overlaps the exchanges.  Per-layer vectors (norm gains, the RoPE row of
-// the position) are fetched into registers a layer or a token ahead.
+// The weights are repacked at load time into one stream per CTA, in the order its warps consume
+// them, cut into 40 KB chunks (8 records per warp); a ring of up to 4 chunk slots is filled by one
+// bulk copy per chunk (cp.async.bulk, completing on the slot's mbarrier), so weight fetch runs a
+// layer ahead of the exchanges.  (Measured on B200 from one 16-SM cluster: bulk copies of 40-64 KB
+// stream 60-70 GB/s per SM; per-warp 16-byte cp.async rings reached about 36 GB/s.)  Per-layer
+// vectors (norm gains, the RoPE row of the position) are fetched into registers a layer or a token
+// ahead.
 //
 // Every wait is bounded (RunArgs::wait_ns, default 0.5 s).  A CTA whose wait runs out raises the
 // device error flag; the others see it in their next wait; all CTAs then meet at the final cluster
 // barrier (so no CTA leaves while another may still write into its shared memory) and return.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -82,20 +86,6 @@ __device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
       : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
-}
-__device__ __forceinline__ void cp_async16_cg(void* smem, const void* gmem) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_wait_upto(uint32_t pending) {
-  switch (pending) {
-    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
-    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
-    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
-    case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
-    case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
-    default: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
-  }
 }
 __device__ __forceinline__ float2 ldcg_f2(const float* p) {
   float2 v;
@@ -161,75 +151,139 @@ __device__ __forceinline__ float dot8(uint32_t w, const float4& a0, const float4
 
 enum { B_X2 = 0, B_QKV = 1, B_ATT = 2, B_X1 = 3, B_H = 4, B_CAND = 5, B_COUNT = 6 };
 
-// A warp's weight stream: records [0, n) per token, repeated every token; `iss` records have been
-// requested (in groups of kCdBatch), `con` consumed.  Record r lives in ring slot r % kCdRing.
-struct Ring {
-  const uint4* src;
-  uint8_t* buf;
-  uint32_t n, iss, con;
+// The CTA's weight ring: nslot chunk slots, each filled by one bulk copy that completes on the slot's
+// full barrier.  Every warp waits for a chunk before its first record in it and releases the chunk
+// after its last; the warp whose release completes the count of 16 issues the chunk nslot further on
+// into the same slot, so no thread ever blocks on the producer side.  Chunk k of the kernel is chunk
+// k % cpt of the CTA's per-token stream (the stream repeats every token).  A warp walks its records
+// with an incremental pointer; chunk indices, slots and barrier phases advance once per chunk.
+struct Feed {
+  const uint8_t* src;   // this CTA's cpt chunks
+  uint8_t* ring;        // nslot slots
+  int* cnt;             // [nslot] releases of the slot's current chunk; [kCdMaxSlots + s] last chunk issued
+  uint32_t full;        // shared address of the slot 0 full barrier (8 bytes per slot)
+  uint32_t cpt, nslot;
+  // this warp
+  const uint8_t* cur;   // its next record
+  uint32_t kc;          // global index of the chunk holding it
+  uint32_t slot, phase; // kc % nslot and the parity of kc / nslot
+  uint32_t ri;          // records of this warp already taken from chunk kc
+  uint32_t tok_end;     // first chunk of the next token
 };
 
-// Request batches while the ring has room for one.
-__device__ __forceinline__ void ring_issue(Ring& R, int lane) {
-  while (R.iss - R.con + kCdBatch <= kCdRing) {
-#pragma unroll
-    for (int b = 0; b < kCdBatch; ++b) {
-      const uint32_t rec = R.iss + b;
-      if (lane < kCdRecBytes / 16)
-        cp_async16_cg(R.buf + (rec % kCdRing) * kCdRecBytes + lane * 16, R.src + (size_t)(rec % R.n) * 20 + lane);
+__device__ __forceinline__ void feed_issue(Feed& F, uint32_t k) {
+  const uint32_t s = k % F.nslot;
+  F.cnt[kCdMaxSlots + s] = (int)k;
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier reads of the slot come first
+  bar_arm(F.full + 8 * s, kCdChunk);
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(F.ring + (size_t)s * kCdChunk)),
+               "l"(F.src + (size_t)(k % F.cpt) * kCdChunk), "r"((uint32_t)kCdChunk), "r"(F.full + 8 * s)
+               : "memory");
+}
+
+__device__ __forceinline__ bool bar_try_cta(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait of one warp for the bytes of its current chunk.
+__device__ __forceinline__ bool feed_wait(const Feed& F, int* err, uint64_t limit) {
+  const uint32_t bar = F.full + 8 * F.slot;
+  if (bar_try_cta(bar, F.phase)) return true;
+  const uint64_t t0 = globaltimer();
+  for (int n = 0;; ++n) {
+    if (bar_try_cta(bar, F.phase)) return true;
+    if ((n & 15) == 15 && (*(volatile int*)err || globaltimer() - t0 > limit)) {
+      atomicCAS(err, 0, 1);
+      return false;
     }
-    cp_commit();
-    R.iss += kCdBatch;
   }
 }
 
-// Make record R.con readable by the whole warp (at the start of each batch: refill first, then wait
-// for the batch's group).
-__device__ __forceinline__ void ring_ready(Ring& R, int lane) {
-  if (R.con % kCdBatch == 0) {
-    __syncwarp();
-    ring_issue(R, lane);
-    cp_wait_upto(R.iss / kCdBatch - R.con / kCdBatch - 1);
-    __syncwarp();
+// Release chunk kc (this warp is done with it) and move to the next one.
+__device__ __forceinline__ void feed_next_chunk(Feed& F, int warp, int lane) {
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence_block();
+    if (atomicAdd(&F.cnt[F.slot], 1) == kCdWarps - 1) {
+      F.cnt[F.slot] = 0;
+      feed_issue(F, F.kc + F.nslot);
+    }
   }
+  __syncwarp();
+  ++F.kc;
+  F.ri = 0;
+  if (++F.slot == F.nslot) {
+    F.slot = 0;
+    F.phase ^= 1u;
+  }
+  F.cur = F.ring + (size_t)F.slot * kCdChunk + (size_t)warp * kCdRpc * kCdRecBytes;
 }
 
-// This warp's share of one stage (see CdGeom): per unit tile, the rows' partial sums over the warp's
-// k slice, scaled per group, reduced over the lane quad, into red[(tile * KW + slice) * 16 + row].
-__device__ __forceinline__ void run_units(Ring& R, const CdGeom& g, const float* actp, float* red, int warp, int lane) {
-  const int ks = warp % g.KW, ts = warp / g.KW;
-  const int g0 = ks * g.G / g.KW, g1 = (ks + 1) * g.G / g.KW;
+// End of a token: release the chunk this warp left part-way and every later chunk of the token.
+__device__ __forceinline__ bool feed_token_end(Feed& F, int warp, int lane, int* err, uint64_t limit) {
+  if (F.ri) feed_next_chunk(F, warp, lane);
+  while (F.kc < F.tok_end) {
+    if (!feed_wait(F, err, limit)) return false;
+    feed_next_chunk(F, warp, lane);
+  }
+  F.tok_end += F.cpt;
+  return true;
+}
+
+// This warp's share of one stage (see CdGeom): its contiguous range of units; per tile the rows'
+// partial sums over the range's groups, scaled per group, reduced over the lane quad, into
+// red[(tile * maxc + slot) * 16 + row] (slot = this warp's order among the tile's warps).  False when a
+// wait for weights gave up.
+__device__ __forceinline__ bool run_units(Feed& F, const CdGeom& g, int off, const float* actp, float* red, int warp,
+                                          int lane, int* err, uint64_t limit) {
+  const int v = (warp - off) & (kCdWarps - 1);
+  const int u1 = cd_ustart(g, v + 1);
   const int gid = lane >> 2, t = lane & 3;
-  for (int tl = ts; tl < g.Tu; tl += g.TW) {
+  int u = cd_ustart(g, v);
+  while (u < u1) {
+    const int tl = u / g.G;
+    const int ue = min(u1, (tl + 1) * g.G);
+    const int slot = v - cd_vwarp(g, tl * g.G);
+    const float* ap = actp + 32 * (u - tl * g.G) + 8 * t;
     float acc0 = 0.f, acc1 = 0.f;
-    for (int gg = g0; gg < g1; ++gg) {
-      ring_ready(R, lane);
-      const uint8_t* rec = R.buf + (R.con % kCdRing) * kCdRecBytes;
-      const uint2 wv = *reinterpret_cast<const uint2*>(rec + 8 * lane);
-      const float2 sc = *reinterpret_cast<const float2*>(rec + 256 + 8 * gid);
-      const float4* ap = reinterpret_cast<const float4*>(actp + 32 * gg + 8 * t);
-      const float4 a0 = ap[0], a1 = ap[1];
+    for (; u < ue; ++u, ap += 32) {
+      if (F.ri == 0 && !feed_wait(F, err, limit)) return false;
+      const uint2 wv = *reinterpret_cast<const uint2*>(F.cur + 8 * lane);
+      const float2 sc = *reinterpret_cast<const float2*>(F.cur + 256 + 8 * gid);
+      const float4 a0 = reinterpret_cast<const float4*>(ap)[0];
+      const float4 a1 = reinterpret_cast<const float4*>(ap)[1];
       acc0 = fmaf(dot8(wv.x, a0, a1), sc.x, acc0);
       acc1 = fmaf(dot8(wv.y, a0, a1), sc.y, acc1);
-      ++R.con;
+      F.cur += kCdRecBytes;
+      if (++F.ri == kCdRpc) feed_next_chunk(F, warp, lane);
     }
     acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
     acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
     acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
     acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
     if (t == 0) {
-      float* r = red + (tl * g.KW + ks) * 16 + gid;
+      float* r = red + (tl * g.maxc + slot) * 16 + gid;
       r[0] = acc0;
       r[8] = acc1;
     }
   }
+  return true;
 }
 
-// Row i (0 .. 16 Tu) of the CTA's unit tiles: the k-slice partials summed in slice order.
+// Row i (0 .. 16 Tu) of the CTA's unit tiles: the partials of the tile's warps, in warp order.
 __device__ __forceinline__ float row_sum(const float* red, const CdGeom& g, int i) {
-  const float* r = red + (i >> 4) * g.KW * 16 + (i & 15);
+  const int tl = i >> 4;
+  const int nc = cd_vwarp(g, tl * g.G + g.G - 1) - cd_vwarp(g, tl * g.G) + 1;
+  const float* r = red + tl * g.maxc * 16 + (i & 15);
   float s = 0.f;
-  for (int k = 0; k < g.KW; ++k) s += r[k * 16];
+  for (int k = 0; k < nc; ++k) s += r[k * 16];
   return s;
 }
 
@@ -266,14 +320,17 @@ __device__ __forceinline__ float inv_rms(const float* xb, int D) {
   return 1.f / sqrtf(s / D + 1e-6f);
 }
 
-// Epilogue + exchange of a row stage: thread i takes row quad q = i / 16 of the CTA's rows and sends
-// it to CTA i % 16.  `val(i)` gives the value of local row i (0 .. nrows).  With ss, the quad's sum of
-// squares also goes to slot (first quad + q) after the destination's D values.
+// Epilogue + exchange of a row stage: `val(i)` gives the value of local row i (0 .. nrows); thread i
+// computes row i into stage, then thread i sends row quad i / 16 to CTA i % 16.  With ss, the quad's
+// sum of squares also goes to slot (first quad + quad) after the destination's D values.
 template <class F>
-__device__ __forceinline__ void push_rows(int nrows, uint32_t dst, uint32_t bar, int ss_slot0, uint32_t ss_dst, F val) {
+__device__ __forceinline__ void push_rows(int nrows, float* stage, uint32_t dst, uint32_t bar, int ss_slot0,
+                                          uint32_t ss_dst, F val) {
+  for (int i = threadIdx.x; i < nrows; i += kCdThreads) stage[i] = val(i);
+  __syncthreads();
   for (int i = threadIdx.x; i < nrows * 4; i += kCdThreads) {
     const int q = i >> 4, d = i & 15;
-    const float4 v = make_float4(val(4 * q), val(4 * q + 1), val(4 * q + 2), val(4 * q + 3));
+    const float4 v = reinterpret_cast<const float4*>(stage)[q];
     const uint32_t rb = mapa(bar, d);
     st_async4(mapa(dst + 16 * q, d), v, rb);
     if (ss_slot0 >= 0) {
@@ -291,7 +348,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   extern __shared__ __align__(16) uint8_t smem[];
   const RunArgs& a = A.r;
   const ModelDev& md = a.m;
-  const CdSmem Ls = cd_smem(md);
+  const CdSmem Ls = cd_smem(md, A.smem_cap);
   const int c = (int)cta_rank();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int D = md.D, QKV = md.QKV, FF = md.FF, NKV = md.NKV, rep = md.NH / md.NKV;
@@ -319,9 +376,11 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   uint32_t par[B_COUNT] = {0, 0, 0, 0, 0, 0};
   if (tid == 0) {
     for (int b = 0; b < B_COUNT; ++b) bar_init(sbar + 8 * b, 1);
+    for (int sl = 0; sl < Ls.nslot; ++sl) bar_init(sbar + 8 * (8 + sl), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     for (int b = 0; b < B_COUNT; ++b) bar_arm(sbar + 8 * b, bar_bytes[b]);
   }
+  if (tid < 2 * kCdMaxSlots) reinterpret_cast<int*>(smem + Ls.feed)[tid] = tid < kCdMaxSlots ? 0 : -1;
   // norm gain pointers of every layer, then norm_f
   for (int i = tid; i < 2 * md.n_layers; i += kCdThreads)
     norms[i] = (i & 1) ? md.layers[i >> 1].norm2 : md.layers[i >> 1].norm1;
@@ -337,11 +396,16 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
     return true;
   };
 
-  Ring R;
-  R.src = A.wst + (size_t)A.woff[c * kCdWarps + warp] * (kCdRecBytes / 16);
-  R.buf = smem + Ls.ring + warp * kCdRing * kCdRecBytes;
-  R.n = A.wcnt[c * kCdWarps + warp];
-  R.iss = R.con = 0;
+  Feed F;
+  F.src = A.wst + (size_t)A.woff[c] * kCdChunk;
+  F.ring = smem + Ls.ring;
+  F.cnt = reinterpret_cast<int*>(smem + Ls.feed);
+  F.full = sbar + 8 * 8;
+  F.cpt = A.wcpt[c];
+  F.nslot = (uint32_t)Ls.nslot;
+  F.cur = F.ring + (size_t)warp * kCdRpc * kCdRecBytes;
+  F.kc = F.slot = F.phase = F.ri = 0;
+  F.tok_end = F.cpt;
 
   const bool gen_mode = a.mode == MODE_GENERATE;
   int gen = 0, tok = 0, stop = 1, f = 0;
@@ -361,6 +425,10 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
     cd_stage_shape(md, CD_LM, &rows, &K, &pr);
     glm = cd_geom(rows, K, pr, c);
   }
+  const int off_lm = cd_stage_off(md, c, 0, CD_LM);
+  const int rl = (cd_stage_off(md, c, 1, CD_QKV) - cd_stage_off(md, c, 0, CD_QKV)) & (kCdWarps - 1);  // per layer
+  const int off_p = cd_stage_off(md, c, 0, CD_PROJ), off_13 = cd_stage_off(md, c, 0, CD_W13),
+            off_2 = cd_stage_off(md, c, 0, CD_W2);
   // gains of this thread's elements k = tid, tid + 512 (D <= 1024): current layer and the next one
   float g1[2], g2[2], n1[2], n2[2];
   auto load_gains = [&](int l, float (&o1)[2], float (&o2)[2]) {
@@ -384,7 +452,8 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
     tok = a.out_ids[gen - 1];
     if (tok == a.eos) stop = 0;
   }
-  if (R.n) ring_issue(R, lane);
+  if (tid == 0)
+    for (uint32_t k = 0; k < F.nslot; ++k) feed_issue(F, k);
   load_gains(0, n1, n2);
 
   for (;;) {
@@ -463,9 +532,11 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       }
       __syncthreads();
       // ---- QKV rows
-      run_units(R, gq, actp, red, warp, lane);
-      __syncthreads();
-      push_rows(gq.T * 16, smem_u32(qkvb + 16 * gq.t0), sbar + 8 * B_QKV, -1, 0,
+      if (!__syncthreads_and(run_units(F, gq, (l * rl) & (kCdWarps - 1), actp, red, warp, lane, a.err, limit))) {
+        ok = false;
+        goto done;
+      }
+      push_rows(gq.T * 16, outv, smem_u32(qkvb + 16 * gq.t0), sbar + 8 * B_QKV, -1, 0,
                 [&](int i) { return inv1 * row_sum(red, gq, i); });
       if (!(ok = wait_bar(B_QKV))) goto done;
       // ---- attention of unit (kvh, sp) (engine/infer.js:442-495)
@@ -604,9 +675,11 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       }
       __syncthreads();
       // ---- proj rows + residual (x1)
-      run_units(R, gp, actp, red, warp, lane);
-      __syncthreads();
-      push_rows(gp.T * 16, smem_u32(xb1 + 16 * gp.t0), sbar + 8 * B_X1, 4 * gp.t0, smem_u32(xb1 + D),
+      if (!__syncthreads_and(run_units(F, gp, (l * rl + off_p) & (kCdWarps - 1), actp, red, warp, lane, a.err, limit))) {
+        ok = false;
+        goto done;
+      }
+      push_rows(gp.T * 16, outv, smem_u32(xb1 + 16 * gp.t0), sbar + 8 * B_X1, 4 * gp.t0, smem_u32(xb1 + D),
                 [&](int i) { return xb2[16 * gp.t0 + i] + row_sum(red, gp, i); });
       if (!(ok = wait_bar(B_X1))) goto done;
       // ---- w1 / w3 rows, SiLU(u) * v (engine/infer.js:506-527)
@@ -617,9 +690,11 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         if (k < D) actp[k] = pre_scale(xb1[k] * g2[j], k);
       }
       __syncthreads();
-      run_units(R, gw13, actp, red, warp, lane);
-      __syncthreads();
-      push_rows(gw13.T * 16, smem_u32(hb + 16 * gw13.t0), sbar + 8 * B_H, -1, 0, [&](int i) {
+      if (!__syncthreads_and(run_units(F, gw13, (l * rl + off_13) & (kCdWarps - 1), actp, red, warp, lane, a.err, limit))) {
+        ok = false;
+        goto done;
+      }
+      push_rows(gw13.T * 16, outv, smem_u32(hb + 16 * gw13.t0), sbar + 8 * B_H, -1, 0, [&](int i) {
         const int tl = i >> 4, r = i & 15;
         const float u = inv2 * row_sum(red, gw13, (2 * tl) * 16 + r);
         const float v = inv2 * row_sum(red, gw13, (2 * tl + 1) * 16 + r);
@@ -629,9 +704,11 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       // ---- w2 rows + residual (x2)
       for (int k = tid; k < FF; k += kCdThreads) actp[k] = pre_scale(hb[k], k);
       __syncthreads();
-      run_units(R, gw2, actp, red, warp, lane);
-      __syncthreads();
-      push_rows(gw2.T * 16, smem_u32(xb2 + 16 * gw2.t0), sbar + 8 * B_X2, 4 * gw2.t0, smem_u32(xb2 + D),
+      if (!__syncthreads_and(run_units(F, gw2, (l * rl + off_2) & (kCdWarps - 1), actp, red, warp, lane, a.err, limit))) {
+        ok = false;
+        goto done;
+      }
+      push_rows(gw2.T * 16, outv, smem_u32(xb2 + 16 * gw2.t0), sbar + 8 * B_X2, 4 * gw2.t0, smem_u32(xb2 + D),
                 [&](int i) { return xb1[16 * gw2.t0 + i] + row_sum(red, gw2, i); });
     }
     // ---- final RMSNorm, lm_head rows of this CTA, argmax candidates (engine/infer.js:240-250)
@@ -645,8 +722,14 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       }
       load_gains(0, n1, n2);  // the next token's first layer
       __syncthreads();
-      run_units(R, glm, actp, red, warp, lane);
-      __syncthreads();
+      if (!__syncthreads_and(run_units(F, glm, off_lm, actp, red, warp, lane, a.err, limit))) {
+        ok = false;
+        goto done;
+      }
+      if (!__syncthreads_and(feed_token_end(F, warp, lane, a.err, limit))) {
+        ok = false;
+        goto done;
+      }
       float best = -INFINITY;
       int bidx = 0x7fffffff;
       const int r0 = 16 * glm.t0;
@@ -711,7 +794,26 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
     if (tok == a.eos) stop = 0;
   }
 done:
-  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  if (tid == 0) {
+    // the bulk copies still in flight land before the CTA leaves (bounded)
+    const int* last = reinterpret_cast<const int*>(smem + Ls.feed) + kCdMaxSlots;
+    for (int sl = 0; sl < Ls.nslot; ++sl)
+      if (last[sl] >= 0) {
+        const uint32_t k = (uint32_t)last[sl];
+        const uint32_t bar = sbar + 8 * (8 + sl), parity = (k / F.nslot) & 1;
+        const uint64_t t0 = globaltimer();
+        for (;;) {
+          uint32_t done_ok;
+          asm volatile(
+              "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+              : "=r"(done_ok)
+              : "r"(bar), "r"(parity)
+              : "memory");
+          if (done_ok || globaltimer() - t0 > limit) break;
+        }
+      }
+  }
   if (c == 0 && tid == 0 && a.mode != MODE_SELFTEST_WAIT && ok) {
     if (gen_mode) {
       a.status[ST_NGEN] = gen;
@@ -738,43 +840,47 @@ bool cd_supported(const ModelDev& m, size_t smem_cap) {
   if (m.D % 16 || m.QKV % 16 || m.FF % 16 || m.D % 32 || m.FF % 32) return false;
   if (m.NKV > kCdCtas || m.rope_dim > 64 || m.rope_dim % 2 || m.D > 2 * kCdThreads) return false;
   if ((m.NH / m.NKV + 2) * 64 > kCdThreads || m.NH > kCdThreads) return false;
-  return (size_t)cd_smem(m).total <= smem_cap;
+  const CdSmem p = cd_smem(m, (int)smem_cap);
+  return p.nslot >= 3 && (size_t)p.total <= smem_cap;
 }
 
-size_t cd_smem_bytes(const ModelDev& m) { return (size_t)cd_smem(m).total; }
+size_t cd_smem_bytes(const ModelDev& m, size_t smem_cap) { return (size_t)cd_smem(m, (int)smem_cap).total; }
 
 // Records of every (CTA, warp) stream, in consumption order: per layer QKV, PROJ, W13 (w1 / w3 tiles
 // interleaved), W2, then the lm_head.  A record holds, for lane = 4 gid + t, the words t of group g of
 // rows gid and gid + 8 (8 bytes at 8 lane), then the scales of rows (gid, gid + 8) as a float pair at
 // 256 + 8 gid.  Rows past the end hold q = 8 nibbles and zero scales.
 void cd_pack(const ModelDev& m, const std::vector<HostQ4>& mats /* per layer: qkv, proj, w1, w3, w2 */,
-             const HostQ4& lm, std::vector<uint8_t>* out, std::vector<uint32_t>* off, std::vector<uint32_t>* cnt) {
-  off->assign(kCdCtas * kCdWarps, 0);
+             const HostQ4& lm, std::vector<uint8_t>* out, std::vector<uint32_t>* off, std::vector<uint32_t>* cpt,
+             std::vector<uint32_t>* cnt) {
+  off->assign(kCdCtas, 0);
+  cpt->assign(kCdCtas, 0);
   cnt->assign(kCdCtas * kCdWarps, 0);
-  size_t total = 0;
-  // count
-  auto stage_units = [&](int st, int c, int w) {
+  auto stage_units = [&](int st, int c, int w, int off) {
     int rows, K;
     bool paired;
     cd_stage_shape(m, st, &rows, &K, &paired);
     const CdGeom g = cd_geom(rows, K, paired, c);
-    const int ks = w % g.KW, ts = w / g.KW;
-    const int ng = (ks + 1) * g.G / g.KW - ks * g.G / g.KW;
-    const int nt = ts < g.Tu ? (g.Tu - ts + g.TW - 1) / g.TW : 0;
-    return (size_t)nt * ng;
+    const int v = (w - off) & (kCdWarps - 1);
+    return (size_t)(cd_ustart(g, v + 1) - cd_ustart(g, v));
   };
-  for (int c = 0; c < kCdCtas; ++c)
+  size_t chunks = 0;
+  for (int c = 0; c < kCdCtas; ++c) {
+    size_t mx = 0;
     for (int w = 0; w < kCdWarps; ++w) {
       size_t n = 0;
-      for (int st = CD_QKV; st <= CD_W2; ++st) n += stage_units(st, c, w) * m.n_layers;
-      n += stage_units(CD_LM, c, w);
-      (*off)[c * kCdWarps + w] = (uint32_t)total;
+      for (int l = 0; l < m.n_layers; ++l)
+        for (int st = CD_QKV; st <= CD_W2; ++st) n += stage_units(st, c, w, cd_stage_off(m, c, l, st));
+      n += stage_units(CD_LM, c, w, cd_stage_off(m, c, 0, CD_LM));
       (*cnt)[c * kCdWarps + w] = (uint32_t)n;
-      total += n;
+      mx = std::max(mx, n);
     }
-  out->assign(total * kCdRecBytes, 0);
-  uint8_t* dst = out->data();
-  auto emit = [&](const HostQ4& q, int r0, int g) {
+    (*off)[c] = (uint32_t)chunks;
+    (*cpt)[c] = (uint32_t)((mx + kCdRpc - 1) / kCdRpc);
+    chunks += (*cpt)[c];
+  }
+  out->assign(chunks * kCdChunk, 0);
+  auto emit = [&](uint8_t* dst, const HostQ4& q, int r0, int g) {
     const int hb = q.K / 2, ng = q.K / 32;
     for (int lane = 0; lane < 32; ++lane) {
       const int gid = lane >> 2, t = lane & 3;
@@ -792,31 +898,38 @@ void cd_pack(const ModelDev& m, const std::vector<HostQ4>& mats /* per layer: qk
         if (r < q.rows) memcpy(&s, q.s + ((size_t)r * ng + g) * 4, 4);
         memcpy(dst + 256 + 8 * gid + 4 * h, &s, 4);
       }
-    dst += kCdRecBytes;
-  };
-  auto emit_stage = [&](int st, int c, int w, const HostQ4* a, const HostQ4* b) {
-    int rows, K;
-    bool paired;
-    cd_stage_shape(m, st, &rows, &K, &paired);
-    const CdGeom g = cd_geom(rows, K, paired, c);
-    const int ks = w % g.KW, ts = w / g.KW;
-    const int g0 = ks * g.G / g.KW, g1 = (ks + 1) * g.G / g.KW;
-    for (int tl = ts; tl < g.Tu; tl += g.TW) {
-      const HostQ4& q = paired ? ((tl & 1) ? *b : *a) : *a;
-      const int tile = g.t0 + (paired ? tl / 2 : tl);
-      for (int gg = g0; gg < g1; ++gg) emit(q, 16 * tile, gg);
-    }
   };
   for (int c = 0; c < kCdCtas; ++c)
     for (int w = 0; w < kCdWarps; ++w) {
+      // record j of warp w goes to chunk j / kCdRpc, position w * kCdRpc + j % kCdRpc
+      size_t j = 0;
+      auto put = [&](const HostQ4& q, int r0, int g) {
+        uint8_t* dst = out->data() + ((size_t)(*off)[c] + j / kCdRpc) * kCdChunk +
+                       (size_t)(w * kCdRpc + j % kCdRpc) * kCdRecBytes;
+        emit(dst, q, r0, g);
+        ++j;
+      };
+      auto emit_stage = [&](int st, int off, const HostQ4* a, const HostQ4* b) {
+        int rows, K;
+        bool paired;
+        cd_stage_shape(m, st, &rows, &K, &paired);
+        const CdGeom g = cd_geom(rows, K, paired, c);
+        const int v = (w - off) & (kCdWarps - 1);
+        for (int u = cd_ustart(g, v); u < cd_ustart(g, v + 1); ++u) {
+          const int tl = u / g.G, gg = u % g.G;
+          const HostQ4& q = paired ? ((tl & 1) ? *b : *a) : *a;
+          const int tile = g.t0 + (paired ? tl / 2 : tl);
+          put(q, 16 * tile, gg);
+        }
+      };
       for (int l = 0; l < m.n_layers; ++l) {
         const HostQ4* L = &mats[(size_t)l * 5];
-        emit_stage(CD_QKV, c, w, &L[0], nullptr);
-        emit_stage(CD_PROJ, c, w, &L[1], nullptr);
-        emit_stage(CD_W13, c, w, &L[2], &L[3]);
-        emit_stage(CD_W2, c, w, &L[4], nullptr);
+        emit_stage(CD_QKV, cd_stage_off(m, c, l, CD_QKV), &L[0], nullptr);
+        emit_stage(CD_PROJ, cd_stage_off(m, c, l, CD_PROJ), &L[1], nullptr);
+        emit_stage(CD_W13, cd_stage_off(m, c, l, CD_W13), &L[2], &L[3]);
+        emit_stage(CD_W2, cd_stage_off(m, c, l, CD_W2), &L[4], nullptr);
       }
-      emit_stage(CD_LM, c, w, &lm, nullptr);
+      emit_stage(CD_LM, cd_stage_off(m, c, 0, CD_LM), &lm, nullptr);
     }
 }
 

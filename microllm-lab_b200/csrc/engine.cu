@@ -105,9 +105,11 @@ struct mllm_engine {
   // cluster decode (cdec.cu): the single-token loop on one 16-CTA cluster, for the models it supports
   int cd_ok = 0;
   size_t cd_smem = 0;
-  uint4* d_cdw = nullptr;      // repacked weight streams
-  uint32_t* d_cdoff = nullptr; // [16 x 16] first record of each warp's stream
-  uint32_t* d_cdcnt = nullptr; // [16 x 16] records per token
+  uint8_t* d_cdw = nullptr;    // repacked weight chunks
+  uint32_t* d_cdoff = nullptr; // [16] first chunk of each CTA's stream
+  uint32_t* d_cdcpt = nullptr; // [16] chunks per token of each CTA
+  uint32_t* d_cdcnt = nullptr; // [16 x 16] records per token of each warp
+  int cd_cap = 0;              // shared-memory limit the kernel's plan uses
   long coop_launches = 0;      // persistent-kernel launches issued by this handle
   long spec_graph_kernels = 0; // kernels in one speculation graph replay
   long spec_replay_kernels = 0;
@@ -285,7 +287,9 @@ int launch(mllm_engine* e, RunArgs& a, int max_forwards, bool multi, bool resume
     ca.r = a;
     ca.wst = e->d_cdw;
     ca.woff = e->d_cdoff;
+    ca.wcpt = e->d_cdcpt;
     ca.wcnt = e->d_cdcnt;
+    ca.smem_cap = e->cd_cap;
     const cudaError_t lst = cd_launch(ca, e->cd_smem, e->stream);
     ++e->coop_launches;
     if (lst != cudaSuccess) return fail(e, MLLM_ERR_CUDA, "cluster decode launch failed: %s", cudaGetErrorString(lst));
@@ -651,7 +655,7 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
     bool want = false;
     if (const char* v = getenv("MLLM_CLUSTER_DECODE")) want = atoi(v) != 0;
     if (want && cd_supported(md, smem_cap) && cd_setup(smem_cap) == cudaSuccess &&
-        cd_max_clusters(cd_smem_bytes(md)) >= 1) {
+        cd_max_clusters(cd_smem_bytes(md, smem_cap)) >= 1) {
       auto host_q4 = [&](const std::string& name, int rows, int cols) {
         const PgwTensor* t = tensor(p, name);
         return HostQ4{buf + p.payload_off + t->offset, buf + p.payload_off + t->scale_offset, rows, cols};
@@ -666,16 +670,18 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
         mats.push_back(host_q4(b + "mlp.w2", D, FF));
       }
       std::vector<uint8_t> packed;
-      std::vector<uint32_t> off, cnt;
-      cd_pack(md, mats, host_q4("lm_head", md.vocab, D), &packed, &off, &cnt);
+      std::vector<uint32_t> off, cpt, cnt;
+      cd_pack(md, mats, host_q4("lm_head", md.vocab, D), &packed, &off, &cpt, &cnt);
       int rc;
       if ((rc = dev_alloc(E, &e->d_cdw, packed.size())) || (rc = dev_alloc(E, &e->d_cdoff, off.size() * 4)) ||
-          (rc = dev_alloc(E, &e->d_cdcnt, cnt.size() * 4)))
+          (rc = dev_alloc(E, &e->d_cdcpt, cpt.size() * 4)) || (rc = dev_alloc(E, &e->d_cdcnt, cnt.size() * 4)))
         return relay(rc);
       cudaMemcpy(e->d_cdw, packed.data(), packed.size(), cudaMemcpyHostToDevice);
       cudaMemcpy(e->d_cdoff, off.data(), off.size() * 4, cudaMemcpyHostToDevice);
+      cudaMemcpy(e->d_cdcpt, cpt.data(), cpt.size() * 4, cudaMemcpyHostToDevice);
       cudaMemcpy(e->d_cdcnt, cnt.data(), cnt.size() * 4, cudaMemcpyHostToDevice);
-      e->cd_smem = cd_smem_bytes(md);
+      e->cd_cap = (int)smem_cap;
+      e->cd_smem = cd_smem_bytes(md, smem_cap);
       e->cd_ok = 1;
     }
   }
