@@ -39,7 +39,7 @@ typedef struct {
   int32_t n_generated;  /* ids written to out_ids */
   int32_t stop_reason;  /* mllm_stop */
   int32_t spec_hits;    /* accepted draft tokens (specHits) */
-  int32_t spec_tries;   /* verify forwards that carried a draft (specTries) */
+  int32_t spec_tries;   /* speculation iterations, each one verify forward, drafted or not (specTries) */
   int32_t forwards;     /* forward passes run on the device, prefill chunks included */
   int32_t prompt_len;   /* prompt length after truncation (engine/infer.js:604-608) */
   float ttft_ms;        /* device time from launch to the first generated id */

@@ -137,11 +137,6 @@ __device__ __forceinline__ void prefetch_rows(const Q4& q, int R, int n, int r0,
   }
 }
 
-// Opt-in stage timestamps: thread 0 of every CTA records globaltimer at stage ends of one forward.
-__device__ __forceinline__ void stamp(const Ctx& c, uint32_t tag, int idx) {
-  if (c.a.prof && threadIdx.x == 0 && tag == c.a.base_tag + (uint32_t)c.a.prof_forward && idx < kProfStamps)
-    c.a.prof[(size_t)blockIdx.x * kProfStamps + idx] = globaltimer();
-}
 
 // RMSNorm (engine/infer.js:134-143) or LayerNorm (engine/infer.js:147-164) of rows xs[rows_from + i]
 // into act[i], i < count.  All 256 threads share every row (element k = thread + 256 j); the gains
@@ -508,7 +503,6 @@ __device__ __forceinline__ bool forward(Ctx& c, int M_, int pos0, int lm, uint32
   const int M = MULTI ? M_ : 1;
   Smem& sm = c.sm;
 
-  stamp(c, tag, 0);
   // ---- embed (engine/infer.js:360-420): dequantised tied lm_head row, GPT-2 /scale_factors + wpe
   for (int t = threadIdx.x; t < M * D; t += kThreads) {
     const int i = t / D, k = t % D;
@@ -568,12 +562,10 @@ __device__ __forceinline__ bool forward(Ctx& c, int M_, int pos0, int lm, uint32
     } else if (x2_prev && cta_has_rows(D)) {
       if (!poll_rowsof(x2_prev, x.s_d, sm.xs, D, D)) return false;
     }
-    stamp(c, tag, 1 + 6 * l);
     // ---------------- ATT
     for (int u = blockIdx.x; u < md.NH * M; u += c.G) {
       if (!attention_unit<MULTI>(c, l, u % md.NH, u / md.NH, pos0, tag)) return false;
     }
-    stamp(c, tag, 2 + 6 * l);
     // ---------------- PROJ + residual
     if (cta_has_rows(D)) {
       const uint64_t* src = x.att + (size_t)l * mmax * x.s_d;
@@ -588,7 +580,6 @@ __device__ __forceinline__ bool forward(Ctx& c, int M_, int pos0, int lm, uint32
           }))
         return false;
     }
-    stamp(c, tag, 3 + 6 * l);
     // ---------------- F1: w1/w3 + SiLU*mul, or fc + bias + GELU (waits for x1)
     const uint64_t* x1_l = x.x1 + (size_t)l * mmax * x.s_d;
     if (cta_has_rows(FF)) {
@@ -615,7 +606,6 @@ __device__ __forceinline__ bool forward(Ctx& c, int M_, int pos0, int lm, uint32
     } else if (cta_has_rows(D)) {
       if (!poll_rowsof(x1_l, x.s_d, sm.xs, D, D)) return false;
     }
-    stamp(c, tag, 4 + 6 * l);
     // ---------------- F2: w2 + residual
     if (cta_has_rows(D)) {
       const uint64_t* src = x.a + (size_t)l * mmax * x.s_ff;
@@ -632,7 +622,6 @@ __device__ __forceinline__ bool forward(Ctx& c, int M_, int pos0, int lm, uint32
     }
   }
   const uint64_t* x2_last = x.x2 + (size_t)(md.n_layers - 1) * mmax * x.s_d;
-  stamp(c, tag, 5 + 6 * (md.n_layers - 1));
 
   // ---------------- final norm + lm_head + argmax candidates
   const int nlm = (MULTI && lm == LM_EACH) ? M : 1;
@@ -756,7 +745,6 @@ __device__ __forceinline__ bool forward(Ctx& c, int M_, int pos0, int lm, uint32
       ll_store_u32(slot + 2, tag, 0);
     }
   }
-  stamp(c, tag, kProfStamps - 3);
   // ---------------- all-CTA exchange of candidates: closes the forward
   {
     const uint64_t* base = x.cand + (size_t)parity * c.G * mmax * 4;
@@ -790,7 +778,6 @@ __device__ __forceinline__ bool forward(Ctx& c, int M_, int pos0, int lm, uint32
     }
     __syncthreads();
   }
-  stamp(c, tag, kProfStamps - 2);
   return true;
 }
 

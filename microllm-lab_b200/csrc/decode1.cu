@@ -62,11 +62,6 @@ __device__ __forceinline__ void lm_resident_ptrs(const ModelDev& md, int rpc, La
   L.lms = reinterpret_cast<float*>(L.lmw + wwords);
 }
 
-// Opt-in stage timestamps (thread 0 of each CTA, one forward): same layout as the general kernel.
-__device__ __forceinline__ void stamp(const RunArgs& a, uint32_t tag, int idx) {
-  if (a.prof && threadIdx.x == 0 && tag == a.base_tag + (uint32_t)a.prof_forward && idx < kProfStamps)
-    a.prof[(size_t)blockIdx.x * kProfStamps + idx] = globaltimer();
-}
 
 // Wait for the n contiguous words src[0..n) (tag == tag) and store their values to dst[0..n).
 // Every thread of the CTA calls it; returns false (everywhere) when the wait gave up.
@@ -262,7 +257,6 @@ __device__ __forceinline__ void load_gains(const float* g, int D, bool ln, float
   }
 }
 
-constexpr int kProfLayerA = 15;
 
 // Causal attention of head h for the token at `pos` (engine/infer.js:422-495), split over `ns` CTAs
 // by position: split sp covers positions [sp * P, (sp + 1) * P) of 0..pos, P = ceil((pos + 1) / ns).
@@ -322,7 +316,6 @@ __device__ __noinline__ bool attention(const RunArgs& a, const Lay& S, int l, in
     }
     if (!__syncthreads_and(ok)) return false;
   }
-  if (l == kProfLayerA) stamp(a, tag, 206);
   if (rope && threadIdx.x < 2 * half) {
     float* v = threadIdx.x < half ? q : kl;
     const int d = threadIdx.x % half;
@@ -406,7 +399,6 @@ __device__ __noinline__ bool attention(const RunArgs& a, const Lay& S, int l, in
     o[i] += __shfl_xor_sync(0xffffffffu, o[i], 8);
     o[i] += __shfl_xor_sync(0xffffffffu, o[i], 16);
   }
-  if (l == kProfLayerA) stamp(a, tag, 207);
   float* wp = S.wpart + warp * 68;
   if (lane == 0) {
     wp[0] = mrun;
@@ -513,7 +505,6 @@ __device__ __noinline__ int lm_head(const RunArgs& a, const Lay& S, uint32_t tag
     if (!poll_vec(x.x2 + (size_t)(md.n_layers - 1) * a.mmax * x.s_d, S.xs, D, tag, a.err, limit, a.poll_sleep_ns)) return -1;
     norm_row(S.xs, S.act, S.red, D, md.arch == 1, gv[0], gv[1], gv[2], gv[3], bv[0], bv[1], bv[2], bv[3]);
   }
-  stamp(a, tag, 210);
   int nban = 0, nrec = 0;
   if (pen) {
     if (threadIdx.x == 0) S.misc[0] = 0;
@@ -617,7 +608,6 @@ __device__ __noinline__ int lm_head(const RunArgs& a, const Lay& S, uint32_t tag
     S.cval[warp] = best;
     S.cidx[warp] = bidx;
   }
-  stamp(a, tag, kProfStamps - 3);
   __threadfence();  // cache rows written in this forward become visible before the candidate
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -685,7 +675,6 @@ __device__ __noinline__ int lm_head(const RunArgs& a, const Lay& S, uint32_t tag
     if (lane == 0) S.misc[2] = bi;
   }
   __syncthreads();
-  stamp(a, tag, kProfStamps - 2);
   return S.misc[2];
 }
 
@@ -694,10 +683,6 @@ __device__ __forceinline__ float gelu(float v) {
   return 0.5f * v * (1.f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
 }
 
-// Fine-grained stamps inside one layer (opt-in stage profile only).
-constexpr int kProfLayer = 15;
-#define D1_FINE(idx) \
-  if (l == kProfLayer) stamp(a, tag, 200 + (idx))
 
 // One layer of the single-token forward at position `pos`.
 template <int NWJ_D, int NWJ_F, bool SPLIT>
@@ -728,7 +713,6 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
       if (l > 0 && !poll_vec(x.x2 + ofs_d - (size_t)a.mmax * x.s_d, S.xs, D, tag, a.err, limit, a.poll_sleep_ns)) return false;
       norm_row(S.xs, S.act, S.red, D, gpt2, gv[0], gv[1], gv[2], gv[3], bv[0], bv[1], bv[2], bv[3]);
     }
-    D1_FINE(1);
     uint64_t* dst = x.qkv + (size_t)l * a.mmax * x.s_qkv;
     for (int r = gw; r < QKV; r += NW) {
       if (r != gw) rw.load(L.qkv, r, D >> 3, lane);
@@ -737,7 +721,6 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
     }
     __syncthreads();
   }
-  stamp(a, tag, 1 + 6 * l);
   // ---- attention
   {
     // Attention: NH x ns units (head, position split) on the last CTAs, which have the fewest (for the
@@ -755,13 +738,11 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
     for (int u = (int)blockIdx.x - h0; u >= 0 && u < md.NH * ns; u += gridDim.x)
       if (!attention<SPLIT>(a, S, l, SPLIT ? (u / ns) | ((u % ns) << 8) | (ns << 16) : u, pos, tag)) return false;
   }
-  stamp(a, tag, 2 + 6 * l);
   // ---- proj rows + residual (x1)
   if (rows0 < D) {
     Row<NWJ_D> rw;
     if (gw < D) rw.load(L.proj, gw, D >> 3, lane);
     if (!poll_vec(x.att + ofs_d, S.act, D, tag, a.err, limit, a.poll_sleep_ns)) return false;
-    D1_FINE(2);
     for (int r = gw; r < D; r += NW) {
       if (r != gw) rw.load(L.proj, r, D >> 3, lane);
       float v = rw.dot(S.act, D >> 3, lane);
@@ -772,7 +753,6 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
     }
     __syncthreads();
   }
-  stamp(a, tag, 3 + 6 * l);
   // ---- w1/w3 rows + SiLU*mul, or fc + bias + GELU (wait: x1, then norm2).  A warp's first two rows
   // (pairs) are requested before the wait.
   if (rows0 < FF) {
@@ -798,7 +778,6 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
       if (!poll_vec(x.x1 + ofs_d, S.xs, D, tag, a.err, limit, a.poll_sleep_ns)) return false;
       norm_row(S.xs, S.act, S.red, D, gpt2, gv[0], gv[1], gv[2], gv[3], bv[0], bv[1], bv[2], bv[3]);
     }
-    D1_FINE(4);
     uint64_t* dst = x.a + (size_t)l * a.mmax * x.s_ff;
     auto emit = [&](int r, const Row<NWJ_D>& ra, const Row<NWJ_D>& rb) {
       const float u = ra.dot(S.act, D >> 3, lane) * inv;
@@ -820,13 +799,11 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
   } else if (rows0 < D) {
     if (!poll_vec(x.x1 + ofs_d, S.xs, D, tag, a.err, limit, a.poll_sleep_ns)) return false;
   }
-  stamp(a, tag, 4 + 6 * l);
   // ---- w2 rows + residual (x2)
   if (rows0 < D) {
     Row<NWJ_F> rw;
     if (gw < D) rw.load(L.w2, gw, FF >> 3, lane);
     if (!poll_vec(x.a + (size_t)l * a.mmax * x.s_ff, S.act, FF, tag, a.err, limit, a.poll_sleep_ns)) return false;
-    D1_FINE(5);
     for (int r = gw; r < D; r += NW) {
       if (r != gw) rw.load(L.w2, r, FF >> 3, lane);
       float v = rw.dot(S.act, FF >> 3, lane);
@@ -837,7 +814,6 @@ __device__ __noinline__ bool layer(const RunArgs& a, const Lay& S, int l, int po
     }
     __syncthreads();
   }
-  stamp(a, tag, 5 + 6 * l);
   return true;
 }
 
@@ -895,7 +871,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode1_kernel(const __grid_const
       pos = a.pos0;
     }
     const uint32_t tag = a.base_tag + f;
-    d1::stamp(a, tag, 0);
     // embed (engine/infer.js:360-420): dequantised tied lm_head row, GPT-2 /scale_factors + wpe
     {
       const uint8_t* row = reinterpret_cast<const uint8_t*>(md.lm.w) + (size_t)tok * (D / 2);

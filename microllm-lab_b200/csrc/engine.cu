@@ -6,7 +6,6 @@
 // mllm_forward : forwardPrompt / forwardDecode / the verify forward (engine/infer.js:553-601,
 //                engine/webgpu.js:1248).
 // mllm_generate: engine/infer.js:603-646 and engine/webgpu.js:1164-1282 in one device launch.
-#include <cuda_profiler_api.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -87,8 +86,6 @@ struct mllm_engine {
   int32_t* h_status = nullptr;  // pinned [ST_WORDS + 1]
   uint32_t tag = 1;
   std::string err;
-  uint64_t* d_prof = nullptr;  // stage timestamps when MLLM_STAGE_PROFILE is set
-  int prof_forward = -1;
   int poll_sleep_ns = 200;     // MLLM_POLL_SLEEP_NS: back-off between poll rounds (less L2 contention)
   int weight_policy = 0;       // MLLM_WEIGHT_EVICT_LAST
   int l2_prefetch = 1;         // MLLM_L2_PREFETCH (default on)
@@ -268,8 +265,6 @@ int launch(mllm_engine* e, RunArgs& a, int max_forwards, bool multi, bool resume
   }
   a.base_tag = e->tag;
   e->tag += (uint32_t)max_forwards + 2;
-  a.prof = e->d_prof;
-  a.prof_forward = e->prof_forward;
   a.poll_sleep_ns = e->poll_sleep_ns;
   a.weight_policy = e->weight_policy;
   a.l2_prefetch = e->l2_prefetch;
@@ -322,14 +317,6 @@ int fetch_status(mllm_engine* e) {
 
 int finish(mllm_engine* e) {
   CUDA_TRY(e, cudaStreamSynchronize(e->stream));
-  if (e->d_prof) {  // MLLM_STAGE_PROFILE=<forward index>, MLLM_STAGE_PROFILE_OUT=<file>: raw u64 dump
-    std::vector<uint64_t> h((size_t)e->grid * kProfStamps);
-    cudaMemcpy(h.data(), e->d_prof, h.size() * 8, cudaMemcpyDeviceToHost);
-    const char* path = getenv("MLLM_STAGE_PROFILE_OUT");
-    if (FILE* f = fopen(path ? path : "mllm_stage_profile.bin", "wb")) {
-      fwrite(h.data(), 8, h.size(), f);
-      fclose(f);
-    }
   }
   if (e->h_status[ST_WORDS] != 0) {
     // a CTA that gave up may have left a completion counter of the token-batch kernels non-zero
@@ -405,17 +392,6 @@ int spec_loop(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max_new
   }
   cudaError_t rs = cudaSuccess;
   long replays = 0;
-  // MLLM_PROFILE_SPEC_ITERS=k brackets the first k iterations with cudaProfilerStart/Stop.
-  int prof_iters = 0;
-  if (const char* v = getenv("MLLM_PROFILE_SPEC_ITERS")) prof_iters = atoi(v);
-  if (prof_iters > 0) {
-    cudaProfilerStart();
-    for (int i = 0; i < prof_iters; ++i)
-      rs = exec ? cudaGraphLaunch(exec, st) : lwe_spec_iteration(a, e->lh, sp, d_out, k, ngram, max_new, eos, slot, st);
-    replays += prof_iters;
-    cudaStreamSynchronize(st);
-    cudaProfilerStop();
-  }
   for (int it = (int)replays; it < max_new + 1 && rs == cudaSuccess;) {
     for (int b = 0; b < 4 && rs == cudaSuccess; ++b, ++it, ++replays)
       rs = exec ? cudaGraphLaunch(exec, st) : lwe_spec_iteration(a, e->lh, sp, d_out, k, ngram, max_new, eos, slot, st);
@@ -727,10 +703,7 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   if (const char* v = getenv("MLLM_LWE_GRAPH")) e->lwe_graph = atoi(v) ? 1 : 0;
   if (const char* v = getenv("MLLM_LWE_FOLD_NORM")) e->lh.fold_norm = atoi(v) ? 1 : 0;
   if (const char* v = getenv("MLLM_LWE_ATTN_SPLIT")) e->lh.attn_split = atoi(v) ? 1 : 0;
-  if (const char* v = getenv("MLLM_LWE_FORCE_TBW")) e->lh.force_tbw = atoi(v);
-  if (const char* v = getenv("MLLM_LWE_FORCE_KS")) e->lh.force_ks = atoi(v);
   if (const char* v = getenv("MLLM_LWE_PDL")) e->lh.pdl = atoi(v);
-  if (const char* v = getenv("MLLM_LWE_FORCE_KZ")) e->lh.force_kz = atoi(v);
   if (const char* v = getenv("MLLM_LWE_LM_WIDE")) e->lh.lm_wide = atoi(v);
   if (const char* v = getenv("MLLM_LWE_ROPE_EPI")) e->lh.rope_epi = atoi(v);
   if (const char* v = getenv("MLLM_LWE_W13_WIDE")) e->lh.w13_wide = atoi(v);
@@ -784,11 +757,6 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   if (const char* v = getenv("MLLM_POLL_SLEEP_NS")) e->poll_sleep_ns = atoi(v);
   if (const char* v = getenv("MLLM_WEIGHT_EVICT_LAST")) e->weight_policy = atoi(v) ? 1 : 0;
   if (const char* v = getenv("MLLM_L2_PREFETCH")) e->l2_prefetch = atoi(v) ? 1 : 0;
-  if (const char* pf = getenv("MLLM_STAGE_PROFILE")) {
-    e->prof_forward = atoi(pf);
-    if ((rc = dev_alloc(E, &e->d_prof, (size_t)e->grid * kProfStamps * 8))) return relay(rc);
-    cudaMemset(e->d_prof, 0, (size_t)e->grid * kProfStamps * 8);
-  }
   if (cudaStreamCreateWithFlags(&e->own_stream, cudaStreamNonBlocking) != cudaSuccess) return bad(MLLM_ERR_CUDA, "stream creation failed");
   e->stream = e->own_stream;
   if (cudaDeviceSynchronize() != cudaSuccess) return bad(MLLM_ERR_CUDA, "device error during upload");
@@ -1055,16 +1023,7 @@ int mllm_generate_batch(mllm_engine* e, int n_seq, const int32_t* ids, const int
     // With an EOS id the batch may finish early: every 16 steps the number of running sequences is
     // read back (the steps already queued behind it keep the GPU busy meanwhile).
     cudaError_t rs = cudaSuccess;
-    // MLLM_PROFILE_DECODE_STEPS=k brackets the first k decode steps with cudaProfilerStart/Stop (for
-    // a profiler started with profiling off).
-    int prof_steps = 0;
-    if (const char* v = getenv("MLLM_PROFILE_DECODE_STEPS")) prof_steps = atoi(v);
-    if (prof_steps > 0) cudaProfilerStart();
     for (; steps < steps_max && rs == cudaSuccess; ++steps) {
-      if (prof_steps > 0 && steps == prof_steps) {
-        cudaStreamSynchronize(st);
-        cudaProfilerStop();
-      }
       rs = exec ? cudaGraphLaunch(exec, st) : step();
       if (eos >= 0 && rs == cudaSuccess && (steps & 15) == 15 && steps + 1 < steps_max) {
         lwe_count_active(d_counts, n_seq, d_active, st);
@@ -1075,10 +1034,6 @@ int mllm_generate_batch(mllm_engine* e, int n_seq, const int32_t* ids, const int
           break;
         }
       }
-    }
-    if (prof_steps > 0 && steps <= prof_steps) {
-      cudaStreamSynchronize(st);
-      cudaProfilerStop();
     }
     if (exec) cudaGraphExecDestroy(exec);
     if (rs != cudaSuccess) return fail(e, MLLM_ERR_CUDA, "batched decode step: %s", cudaGetErrorString(rs));

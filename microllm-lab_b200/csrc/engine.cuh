@@ -58,8 +58,6 @@ struct ExchangeDev {
   int s_qkv, s_d, s_ff;  // row strides in words
 };
 
-constexpr int kProfStamps = 256;  // stage timestamps per CTA (opt-in profiling)
-
 enum RunMode { MODE_FORWARD = 0, MODE_GENERATE = 1, MODE_SELFTEST_WAIT = 2 };
 
 // Status words written by CTA 0 (int32 view): see the layout in engine.cu.
@@ -100,8 +98,6 @@ struct RunArgs {
   uint32_t base_tag;
   int* err;
   uint64_t wait_ns;    // per-wait limit (0 = kWaitNs)
-  uint64_t* prof;      // nullable: [grid][kProfStamps] stage timestamps of forward `prof_forward`
-  int prof_forward;
   int start_gen;       // MODE_GENERATE: ids already generated (in out_ids) by an earlier launch; 0 = prefill first
   int prefill_only;    // MODE_GENERATE: stop after the first generated id
   int poll_sleep_ns;   // back-off between unsuccessful poll rounds (0 = spin)

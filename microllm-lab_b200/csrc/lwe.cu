@@ -1324,11 +1324,8 @@ __global__ void lwe_first_token(const int32_t* amax, int32_t* out_ids, int32_t* 
 // Host side
 // ---------------------------------------------------------------------------------------------
 // Tokens per CTA: for T < 512, the largest tile that still gives two CTAs per SM, else the smallest.
-// LweHost::force_tbw / force_ks (MLLM_LWE_FORCE_TBW / MLLM_LWE_FORCE_KS: 2/4/8, 1/2/4) override the
-// choices below for tile-size experiments on GEMMs of more than 64 token rows.
-static int g_force_tbw = 0, g_force_ks = 0, g_force_kz = 0;  // set from the LweHost of the forward being issued
+// (A 27-point sweep of forced tiles and k splits on the 256-row decode step found none better.)
 static int pick_tbw(int row_tiles, int T) {
-  if (g_force_tbw && T > 64) return g_force_tbw;
   // Long prefill chunks: the smallest tile everywhere (thousands of CTAs) measured 10 % faster than
   // the larger tiles on 1,024-token chunks; a 256-row decode step keeps the rule below.
   if (T >= 512) return 2;
@@ -1343,18 +1340,12 @@ static int pick_tbw(int row_tiles, int T) {
 // Tokens per CTA as above; then the in-CTA k split for GEMMs that still have few CTAs, and for very
 // few CTAs (a handful of tokens) a split of the k groups across CTAs as well (at least 8 groups each).
 static int pick_ks(int ctas) {
-  if (g_force_ks) return g_force_ks;
   return ctas >= 2 * 148 ? 1 : (ctas >= 148 ? 2 : 4);
 }
 static int pick_ksplit(int ctas, int K, int TBW) {
-  int z;
-  if (g_force_kz) {
-    z = g_force_kz;
-  } else {
-    if (ctas >= 96) return 1;  // enough CTAs with the in-CTA split alone
-    z = (2 * 148 + ctas - 1) / ctas;
-  }
-  z = std::min(z, std::max(1, (K / 32) / (g_force_kz ? 2 : 8)));
+  if (ctas >= 96) return 1;  // enough CTAs with the in-CTA split alone
+  int z = (2 * 148 + ctas - 1) / ctas;
+  z = std::min(z, std::max(1, (K / 32) / 8));
   z = std::min(z, 16);
   // the partial tiles must fit the workspace
   while (z > 1 && (size_t)ctas * z * kGemmThreads * TBW * 4 * 4 > kLweSplitKBytes) --z;
@@ -1539,9 +1530,6 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
                         bool one_per_slot, cudaStream_t st) {
   const ModelDev& md = a.m;
   const int nl = md.n_layers;
-  g_force_tbw = h.force_tbw;
-  g_force_ks = h.force_ks;
-  g_force_kz = h.force_kz;
   // RMSNorm folded into the GEMMs (llama): the residual GEMMs write x * gain and sums of squares,
   // the consumers apply 1/RMS.  LayerNorm (GPT-2) keeps separate norm kernels.
   const bool fold = md.arch == 0 && h.fold_norm;

@@ -56,9 +56,6 @@ struct LweHost {
   size_t attn_ctr_n = 0;
   int attn_split = 0;  // decode attention split over positions (MLLM_LWE_ATTN_SPLIT=1)
   int fold_norm = 1;   // llama RMSNorm folded into the GEMM epilogues (MLLM_LWE_FOLD_NORM=0: norm kernels)
-  int force_tbw = 0;   // tile-size experiments (MLLM_LWE_FORCE_TBW / MLLM_LWE_FORCE_KS), 0 = automatic
-  int force_ks = 0;
-  int force_kz = 0;    // split-K across CTAs (MLLM_LWE_FORCE_KZ), 0 = automatic
   int pdl = 1;         // programmatic dependent launch between the forward's kernels (MLLM_LWE_PDL=0: off)
   int lm_wide = 1;     // persistent lm_head GEMM for many rows without logits (MLLM_LWE_LM_WIDE=0: off)
   int w13_wide = 1;    // persistent w1/w3 GEMM for long forwards (MLLM_LWE_W13_WIDE=0: off)

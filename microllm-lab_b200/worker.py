@@ -28,6 +28,7 @@ Differences, by design of this backend:
 """
 from __future__ import annotations
 
+import math
 import time
 import traceback
 
@@ -37,6 +38,35 @@ from .engine import SPECIAL
 def _nullish(v, default):
     """JavaScript's ``v ?? default``: the default only for a missing (None) value."""
     return default if v is None else v
+
+
+def _js_truthy(v) -> bool:
+    """JavaScript truthiness: undefined/null, false, 0, NaN and "" are false; every object is true."""
+    if v is None or v is False:
+        return False
+    if isinstance(v, (int, float)):
+        return v == v and v != 0
+    if isinstance(v, str):
+        return v != ""
+    return True
+
+
+def _js_number(v) -> float:
+    """JavaScript's numeric coercion of a message field (``maxNew - 4`` and ``i < maxNew`` coerce it)."""
+    if isinstance(v, bool):
+        return float(v)
+    try:
+        return float(v)
+    except (TypeError, ValueError):
+        return float("nan")
+
+
+def _new_token_count(max_new: float) -> int:
+    """Ids engine/infer.js:603-646 yields for a (possibly fractional) maxNewTokens: the prefill's id, then
+    one per i = 1, 2, ... while i < maxNewTokens."""
+    if max_new != max_new or max_new <= 1:
+        return 1
+    return int(math.ceil(max_new))
 
 
 class DecodeWorker:
@@ -59,7 +89,8 @@ class DecodeWorker:
                 self._load(m)
             elif cmd == "generate":
                 # `maxNewTokens || 64`, then numeric as the reference's arithmetic makes it
-                self._generate(m.get("prompt"), int(m.get("maxNewTokens") or 64), m.get("opts") or {},
+                mx = m.get("maxNewTokens")
+                self._generate(m.get("prompt"), _js_number(mx if _js_truthy(mx) else 64), m.get("opts") or {},
                                m.get("promptIds"))
             elif cmd == "unload":
                 self._drop_engine()
@@ -88,7 +119,7 @@ class DecodeWorker:
         self.model_id = model_id
         if msg.get("tokenizer") is not None:
             self.tokenizer = msg["tokenizer"]
-        elif msg.get("tokenizerSpec") is not None:  # a tokenizer.json object, as engine/worker.js:40-41 takes
+        elif _js_truthy(msg.get("tokenizerSpec")):  # a tokenizer.json object, as engine/worker.js:40-41 takes
             from .tokenizer import Tokenizer
             self.tokenizer = Tokenizer(msg["tokenizerSpec"])
         self._drop_engine()
@@ -128,12 +159,13 @@ class DecodeWorker:
             raise RuntimeError("no model loaded")
         ids = self._prompt_ids(prompt, prompt_ids)
         max_seq = self.card.get("maxSeqLen") or self.engine.cfg.get("maxSeqLen") or 2048
-        max_prompt = max(1, max_seq - max_new - 4)
-        if len(ids) > max_prompt:
+        max_prompt = max(1, max_seq - max_new - 4) if max_new == max_new else float("nan")
+        if len(ids) > max_prompt:  # false for NaN, as in JavaScript
             bos = _nullish(self.card.get("bosId"), SPECIAL["BOS"])
             has_bos = ids[0] == bos
             keep = max_prompt - (1 if has_bos else 0)
-            tail = ids[len(ids) - keep:] if keep > 0 else []
+            start = int(len(ids) - keep)  # Array.prototype.slice truncates a fractional start
+            tail = ids[start:] if start < len(ids) else []
             ids = [ids[0]] + tail if has_bos else tail
         eos_id = -1 if opts.get("ignoreEos") else _nullish(self.card.get("eosId"), SPECIAL["EOS"])
         t0 = time.perf_counter()
@@ -141,7 +173,7 @@ class DecodeWorker:
         def on_token(tok, meta):
             self.post({"type": "token", "id": int(tok), "piece": self._decode([int(tok)], True), **meta})
 
-        result = self.engine.generate(ids, maxNewTokens=max_new, eosId=eos_id, onToken=on_token,
+        result = self.engine.generate(ids, maxNewTokens=_new_token_count(max_new), eosId=eos_id, onToken=on_token,
                                       specK=int(opts.get("specK") or 0), ngram=int(opts.get("ngram") or 3))
         gen = list(result["generatedIds"])
         text = self._decode(gen[:-1] if gen and gen[-1] == eos_id else gen, True)

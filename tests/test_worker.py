@@ -155,6 +155,29 @@ def test_prompt_truncation_keeps_bos():
     assert posted[-1]["type"] == "error" and "promptIds" in posted[-1]["message"]
 
 
+def test_fractional_max_new_and_js_truthiness():
+    """engine/infer.js:625 loops `for (i = 1; i < maxNewTokens; i++)`: a fractional 3.5 (or "3.5") yields
+    ceil(3.5) = 4 ids; maxPrompt = max(1, 16 - 3.5 - 4) = 8.5 keeps BOS + the ids from slice(trunc(21 -
+    7.5)) = slice(13).  An empty tokenizerSpec object is truthy in JavaScript (it reaches the tokenizer
+    loader, which rejects it); an empty string is not (the loaded tokenizer stays)."""
+    w, posted, engines = make(max_seq=16)
+    w.handle({"cmd": "load", "buffer": b"x"})
+    ids = [BOS] + list(range(100, 120))
+    for mx in (3.5, "3.5"):
+        w.handle({"cmd": "generate", "promptIds": ids, "maxNewTokens": mx})
+        call = engines[0].calls[-1]
+        assert call["maxNewTokens"] == 4, mx
+        assert call["ids"] == [BOS] + ids[13:], mx
+    w.handle({"cmd": "generate", "promptIds": ids, "maxNewTokens": 8.7})
+    assert engines[0].calls[-1]["maxNewTokens"] == 9
+    tok = FakeTokenizer()
+    w.handle({"cmd": "load", "buffer": b"x", "tokenizer": tok})
+    w.handle({"cmd": "load", "buffer": b"x", "tokenizerSpec": ""})
+    assert posted[-1]["type"] == "loaded" and w.tokenizer is tok
+    w.handle({"cmd": "load", "buffer": b"x", "tokenizerSpec": {}})
+    assert posted[-1]["type"] == "error"
+
+
 @pytest.mark.skipif(importlib.util.find_spec("torch") is None, reason="torch absent")
 def test_default_engine_without_a_device_is_an_error_reply():
     import torch
