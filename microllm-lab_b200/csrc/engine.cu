@@ -317,7 +317,6 @@ int fetch_status(mllm_engine* e) {
 
 int finish(mllm_engine* e) {
   CUDA_TRY(e, cudaStreamSynchronize(e->stream));
-  }
   if (e->h_status[ST_WORDS] != 0) {
     // a CTA that gave up may have left a completion counter of the token-batch kernels non-zero
     cudaMemset(e->lh.attn_ctr, 0, e->lh.attn_ctr_n * sizeof(int));
