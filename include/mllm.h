@@ -106,6 +106,20 @@ int mllm_forward(mllm_engine* e, int slot, const int32_t* ids, int n, int pos0, 
 int mllm_generate(mllm_engine* e, int slot, const int32_t* ids, int n, int max_new, int32_t eos, int spec_k,
                   int ngram, int32_t* out_ids, mllm_stats* stats);
 
+/*
+ * Streaming form of mllm_generate: the same call, with each generated id handed to
+ * on_token(id, index, phase, user) on the calling thread while the device is still generating
+ * (engine/infer.js:615,630 and engine/webgpu.js:1202-1237, 1253, 1265 call onToken per id; phase 0 =
+ * "prefill" (the first id), 1 = "decode", 2 = "spec" (an accepted draft id)).  The kernels publish
+ * every id into mapped pinned host memory with a system-scope release as soon as it is chosen; the
+ * call polls those words while it waits for the device, so no per-token synchronisation is added.
+ * Ids arrive in generation order, each exactly once; out_ids and stats are filled as by
+ * mllm_generate.  on_token must not call back into this handle.  NULL on_token = mllm_generate.
+ */
+typedef void (*mllm_token_fn)(int32_t id, int32_t index, int32_t phase, void* user);
+int mllm_generate_stream(mllm_engine* e, int slot, const int32_t* ids, int n, int max_new, int32_t eos, int spec_k,
+                         int ngram, int32_t* out_ids, mllm_stats* stats, mllm_token_fn on_token, void* user);
+
 /* mllm_generate with the prompt and the output already in device memory (d_ids: int32 [n],
  * d_out: int32 [max_new]); stats stay host-side.  Used to time the device path without copies. */
 int mllm_generate_device(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max_new, int32_t eos,

@@ -789,7 +789,10 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       if (c == 0 && tid == 0 && a.argmax_out) a.argmax_out[0] = tok;
       continue;
     }
-    if (c == 0 && tid == 0) a.out_ids[gen] = tok;
+    if (c == 0 && tid == 0) {
+      a.out_ids[gen] = tok;
+      stream_publish(a.stream_ids, gen, tok, 1);
+    }
     ++gen;
     if (tok == a.eos) stop = 0;
   }

@@ -897,7 +897,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode1_kernel(const __grid_const
       continue;
     }
     tok = next;
-    if (lead) a.out_ids[gen] = tok;
+    if (lead) {
+      a.out_ids[gen] = tok;
+      stream_publish(a.stream_ids, gen, tok, 1);
+    }
     if (threadIdx.x == 0) S.hist[n + gen] = tok;
     ++gen;
     __syncthreads();

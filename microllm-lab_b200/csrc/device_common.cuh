@@ -145,6 +145,19 @@ __device__ __forceinline__ float word_dot(uint32_t u, const float* x) {
   return s;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Token streaming into mapped host memory: word 0 counts the ids published, ids follow from word
+// kStreamHead (bits 30-31 carry the phase: 0 prefill, 1 decode, 2 accepted draft).  The id is stored
+// first and the count with a system-scope release, so a host thread that reads the count sees every
+// id below it.
+// ---------------------------------------------------------------------------------------------
+constexpr int kStreamHead = 16;
+__device__ __forceinline__ void stream_publish(int32_t* s, int i, int id, int phase) {
+  if (!s) return;
+  asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(s + kStreamHead + i), "r"(id | (phase << 30)) : "memory");
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(s), "r"(i + 1) : "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -16,6 +17,7 @@
 #include <cstring>
 #include <memory>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/mllm.h"
@@ -107,8 +109,19 @@ struct mllm_engine {
   uint32_t* d_cdcpt = nullptr; // [16] chunks per token of each CTA
   uint32_t* d_cdcnt = nullptr; // [16 x 16] records per token of each warp
   int cd_cap = 0;              // shared-memory limit the kernel's plan uses
+  // token streaming (mllm_generate_stream): ids published by the kernels into mapped pinned memory
+  int32_t* h_stream = nullptr; // host view: [0] count, [kStreamHead + i] id i | phase << 30
+  int32_t* d_stream = nullptr; // the same words, device view
+  mllm_token_fn on_token = nullptr;
+  void* on_token_user = nullptr;
+  int delivered = 0;           // ids handed to on_token so far in this call
   long coop_launches = 0;      // persistent-kernel launches issued by this handle
   long spec_graph_kernels = 0; // kernels in one speculation graph replay
+  long spec_captured = 0;      // kernels counted while capturing in this call (captured, not run)
+  // the instantiated speculation step of the last call, kept while its arguments repeat
+  cudaGraphExec_t spec_exec = nullptr;
+  const void* spec_key_ptr[3] = {nullptr, nullptr, nullptr};  // sp, d_out, stream words
+  int spec_key[5] = {0, 0, 0, 0, -1};                         // k, ngram, max_new, eos, slot
   long spec_replay_kernels = 0;
 };
 
@@ -315,8 +328,34 @@ int fetch_status(mllm_engine* e) {
   return MLLM_OK;
 }
 
+// Hand the ids published since the last call to the caller's on_token (streaming calls only).
+void deliver(mllm_engine* e) {
+  if (!e->on_token) return;
+  const int n = *reinterpret_cast<volatile int32_t*>(e->h_stream);
+  std::atomic_thread_fence(std::memory_order_acquire);
+  for (; e->delivered < n; ++e->delivered) {
+    const uint32_t v = (uint32_t) reinterpret_cast<volatile int32_t*>(e->h_stream)[kStreamHead + e->delivered];
+    e->on_token((int32_t)(v & 0x3FFFFFFFu), e->delivered, (int32_t)(v >> 30), e->on_token_user);
+  }
+}
+
+// Wait for the handle's stream; while it runs, ids published by the kernels go to on_token as they
+// land (streaming calls) instead of after the launch.
+cudaError_t wait_stream(mllm_engine* e) {
+  if (!e->on_token) return cudaStreamSynchronize(e->stream);
+  for (;;) {
+    deliver(e);
+    const cudaError_t q = cudaStreamQuery(e->stream);
+    if (q != cudaErrorNotReady) {
+      deliver(e);
+      return q;
+    }
+    std::this_thread::yield();
+  }
+}
+
 int finish(mllm_engine* e) {
-  CUDA_TRY(e, cudaStreamSynchronize(e->stream));
+  CUDA_TRY(e, wait_stream(e));
   if (e->h_status[ST_WORDS] != 0) {
     // a CTA that gave up may have left a completion counter of the token-batch kernels non-zero
     cudaMemset(e->lh.attn_ctr, 0, e->lh.attn_ctr_n * sizeof(int));
@@ -372,36 +411,48 @@ int spec_loop(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max_new
   int32_t* sp = (int32_t*)e->g_spec.p;
   lwe_spec_init(sp, d_ids, n, d_out, max_new, eos, e->md.kv_len, prefill_forwards, st);
   const LweArgs a = lwe_args(e);
+  int32_t* sid = e->on_token ? e->d_stream : nullptr;
   cudaGraphExec_t exec = nullptr;
   if (e->lwe_graph) {
-    cudaGraph_t graph = nullptr;
-    CUDA_TRY(e, cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    const long c0 = launches_now(e);
-    const cudaError_t r1 = lwe_spec_iteration(a, e->lh, sp, d_out, k, ngram, max_new, eos, slot, st);
-    e->spec_graph_kernels = launches_now(e) - c0;
-    const cudaError_t r2 = cudaStreamEndCapture(st, &graph);
-    if (r1 != cudaSuccess || r2 != cudaSuccess) {
-      if (graph) cudaGraphDestroy(graph);
-      return fail(e, MLLM_ERR_CUDA, "capture of the speculation step failed: %s",
-                  cudaGetErrorString(r1 != cudaSuccess ? r1 : r2));
+    // The step's kernels and their arguments depend only on these values (the engine's buffers are
+    // fixed), so a repeated call replays the graph instantiated by the previous one.
+    const void* kp[3] = {sp, d_out, sid};
+    const int kv[5] = {k, ngram, max_new, eos, slot};
+    if (!e->spec_exec || memcmp(kp, e->spec_key_ptr, sizeof kp) || memcmp(kv, e->spec_key, sizeof kv)) {
+      if (e->spec_exec) cudaGraphExecDestroy(e->spec_exec);
+      e->spec_exec = nullptr;
+      cudaGraph_t graph = nullptr;
+      CUDA_TRY(e, cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+      const long c0 = launches_now(e);
+      const cudaError_t r1 = lwe_spec_iteration(a, e->lh, sp, d_out, k, ngram, max_new, eos, slot, sid, st);
+      e->spec_graph_kernels = e->spec_captured = launches_now(e) - c0;
+      const cudaError_t r2 = cudaStreamEndCapture(st, &graph);
+      if (r1 != cudaSuccess || r2 != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        return fail(e, MLLM_ERR_CUDA, "capture of the speculation step failed: %s",
+                    cudaGetErrorString(r1 != cudaSuccess ? r1 : r2));
+      }
+      const cudaError_t r3 = cudaGraphInstantiate(&e->spec_exec, graph, 0);
+      cudaGraphDestroy(graph);
+      if (r3 != cudaSuccess) {
+        e->spec_exec = nullptr;
+        return fail(e, MLLM_ERR_CUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(r3));
+      }
+      memcpy(e->spec_key_ptr, kp, sizeof kp);
+      memcpy(e->spec_key, kv, sizeof kv);
     }
-    const cudaError_t r3 = cudaGraphInstantiate(&exec, graph, 0);
-    cudaGraphDestroy(graph);
-    if (r3 != cudaSuccess) return fail(e, MLLM_ERR_CUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(r3));
+    exec = e->spec_exec;
   }
   cudaError_t rs = cudaSuccess;
   long replays = 0;
   for (int it = (int)replays; it < max_new + 1 && rs == cudaSuccess;) {
     for (int b = 0; b < 4 && rs == cudaSuccess; ++b, ++it, ++replays)
-      rs = exec ? cudaGraphLaunch(exec, st) : lwe_spec_iteration(a, e->lh, sp, d_out, k, ngram, max_new, eos, slot, st);
+      rs = exec ? cudaGraphLaunch(exec, st) : lwe_spec_iteration(a, e->lh, sp, d_out, k, ngram, max_new, eos, slot, sid, st);
     if (rs == cudaSuccess) rs = cudaMemcpyAsync(e->h_active, sp + kSpecDoneWord, 4, cudaMemcpyDeviceToHost, st);
-    if (rs == cudaSuccess) rs = cudaStreamSynchronize(st);
+    if (rs == cudaSuccess) rs = wait_stream(e);
     if (rs == cudaSuccess && *e->h_active) break;
   }
-  if (exec) {
-    cudaGraphExecDestroy(exec);
-    e->spec_replay_kernels = replays * e->spec_graph_kernels;
-  }
+  if (exec) e->spec_replay_kernels = replays * e->spec_graph_kernels;
   if (rs != cudaSuccess) return fail(e, MLLM_ERR_CUDA, "speculation step: %s", cudaGetErrorString(rs));
   lwe_spec_finish(sp, e->d_status, st);
   return MLLM_OK;
@@ -429,6 +480,7 @@ int generate_impl(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max
   a.spec_k = spec_k;
   a.ngram = ngram;
   a.out_ids = d_out;
+  a.stream_ids = e->on_token ? e->d_stream : nullptr;
   const int chunks = (n + e->mmax - 1) / e->mmax;
   if (e->lwe_ok && e->lwe_prefill) {
     // Prefill as token-batch forwards on the tensor cores, first id from its argmax, then the decode
@@ -438,9 +490,9 @@ int generate_impl(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max
     lwe_mark_time(e->d_status, ST_T0, e->stream);
     int f = 0;
     TRY(lwe_run(e, slot, d_ids, n, 0, 0, nullptr, e->lw.amax, &f));
-    lwe_first(lwe_args(e), d_out, e->d_status, eos, f, e->stream);
+    lwe_first(lwe_args(e), d_out, e->d_status, eos, f, a.stream_ids, e->stream);
     if (spec_k > 0) {
-      e->spec_graph_kernels = e->spec_replay_kernels = 0;
+      e->spec_captured = e->spec_replay_kernels = 0;
       TRY(spec_loop(e, slot, d_ids, n, max_new, eos, std::min(spec_k, kSpecMaxK), ngram, d_out, f));
     } else if (max_new > 1) {
       a.start_gen = 1;
@@ -479,7 +531,7 @@ int generate_impl(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max
     st->total_ms = t2 > t0 ? (float)((t2 - t0) * 1e-6) : 0.f;
     // graph replays ran spec_graph_kernels kernels each; the capture itself ran none
     st->kernel_launches =
-        (int32_t)(launches_now(e) - l0 - (spec_k > 0 ? e->spec_graph_kernels - e->spec_replay_kernels : 0));
+        (int32_t)(launches_now(e) - l0 - (spec_k > 0 ? e->spec_captured - e->spec_replay_kernels : 0));
   }
   return MLLM_OK;
 }
@@ -499,6 +551,8 @@ void mllm_destroy(mllm_engine* e) {
     if (g->p) cudaFree(g->p);
   if (e->h_status) cudaFreeHost(e->h_status);
   if (e->h_active) cudaFreeHost(e->h_active);
+  if (e->h_stream) cudaFreeHost(e->h_stream);
+  if (e->spec_exec) cudaGraphExecDestroy(e->spec_exec);
   if (e->own_stream) cudaStreamDestroy(e->own_stream);
   delete e;
 }
@@ -696,6 +750,9 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
     return relay(rc);
   if (cudaMallocHost(&e->h_status, (ST_WORDS + 1) * 4) != cudaSuccess) return bad(MLLM_ERR_OOM, "cudaMallocHost failed");
   if (cudaMallocHost(&e->h_active, 16) != cudaSuccess) return bad(MLLM_ERR_OOM, "cudaMallocHost failed");
+  if (cudaHostAlloc(&e->h_stream, (size_t)(kStreamHead + md.kv_len + 32) * 4, cudaHostAllocMapped) != cudaSuccess ||
+      cudaHostGetDevicePointer(&e->d_stream, e->h_stream, 0) != cudaSuccess)
+    return bad(MLLM_ERR_OOM, "mapped host buffer for token streaming failed");
   // ---- layer-wise engine buffers: tmax token rows per forward
   e->lwe_ok = md.NH / md.NKV <= kLweMaxRep;
   if (const char* v = getenv("MLLM_LWE_PREFILL")) e->lwe_prefill = atoi(v) ? 1 : 0;
@@ -863,6 +920,24 @@ int mllm_generate(mllm_engine* e, int slot, const int32_t* ids, int n, int max_n
   CUDA_TRY(e, cudaMemcpyAsync(out_ids, e->d_out, std::max(gen, 0) * 4, cudaMemcpyDeviceToHost, e->stream));
   CUDA_TRY(e, cudaStreamSynchronize(e->stream));
   return MLLM_OK;
+}
+
+int mllm_generate_stream(mllm_engine* e, int slot, const int32_t* ids, int n, int max_new, int32_t eos, int spec_k,
+                         int ngram, int32_t* out_ids, mllm_stats* st, mllm_token_fn on_token, void* user) {
+  if (!e) return MLLM_ERR_ARG;
+  if (!on_token) return mllm_generate(e, slot, ids, n, max_new, eos, spec_k, ngram, out_ids, st);
+  cudaSetDevice(e->device);
+  *reinterpret_cast<volatile int32_t*>(e->h_stream) = 0;  // no kernel of this handle is running
+  e->on_token = on_token;
+  e->on_token_user = user;
+  e->delivered = 0;
+  const int rc = mllm_generate(e, slot, ids, n, max_new, eos, spec_k, ngram, out_ids, st);
+  // ids of a path that does not publish (the persistent multi-token kernel) go out after the launch
+  if (rc == MLLM_OK)
+    for (int i = e->delivered; i < e->h_status[ST_NGEN]; ++i) on_token(out_ids[i], i, i == 0 ? 0 : 1, user);
+  e->on_token = nullptr;
+  e->on_token_user = nullptr;
+  return rc;
 }
 
 int mllm_selftest_timeout(mllm_engine* e, int wait_ms) {

@@ -94,6 +94,7 @@ struct RunArgs {
   int spec_k;
   int ngram;
   int32_t* out_ids;    // MODE_GENERATE: [max_new]
+  int32_t* stream_ids; // MODE_GENERATE, nullable: mapped host words the ids are also published to
   int32_t* status;     // [ST_WORDS]
   uint32_t base_tag;
   int* err;

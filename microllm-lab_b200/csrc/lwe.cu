@@ -1307,9 +1307,11 @@ __global__ void lwe_mark(int32_t* status, int idx) {
 }
 
 // First id of a generate from the prefill's argmax (engine/infer.js:611-623).
-__global__ void lwe_first_token(const int32_t* amax, int32_t* out_ids, int32_t* status, int eos, int forwards) {
+__global__ void lwe_first_token(const int32_t* amax, int32_t* out_ids, int32_t* status, int eos, int forwards,
+                                int32_t* stream) {
   const int id = amax[0];
   out_ids[0] = id;
+  stream_publish(stream, 0, id, 0);
   status[ST_NGEN] = 1;
   status[ST_STOP] = id == eos ? 0 : 1;
   status[ST_FORWARDS] = forwards;
@@ -1614,8 +1616,8 @@ void lwe_fill(LweArgs a, const int32_t* ids, int n, int slot, int pos0, int lm_e
   k_fill<<<(n + 255) / 256, 256, 0, st>>>(a, ids, n, slot, pos0, lm_each);
   ++g_lwe_launches;
 }
-void lwe_first(LweArgs a, int32_t* out_ids, int32_t* status, int eos, int forwards, cudaStream_t st) {
-  lwe_first_token<<<1, 1, 0, st>>>(a.amax, out_ids, status, eos, forwards);
+void lwe_first(LweArgs a, int32_t* out_ids, int32_t* status, int eos, int forwards, int32_t* stream, cudaStream_t st) {
+  lwe_first_token<<<1, 1, 0, st>>>(a.amax, out_ids, status, eos, forwards, stream);
   ++g_lwe_launches;
 }
 void lwe_mark_time(int32_t* status, int idx, cudaStream_t st) { lwe_mark<<<1, 1, 0, st>>>(status, idx); }
@@ -1889,7 +1891,8 @@ __global__ void k_spec_prepare(const __grid_constant__ LweArgs a, int32_t* sp, i
 }
 
 // engine/webgpu.js:1249-1268: accept r[0], then r[k+1] while r[k] == draft[k].
-__global__ void k_spec_accept(const int32_t* amax, int32_t* sp, int32_t* out_ids, int max_new, int eos) {
+__global__ void k_spec_accept(const int32_t* amax, int32_t* sp, int32_t* out_ids, int max_new, int eos,
+                              int32_t* stream) {
   pdl_enter();
   if (threadIdx.x != 0 || sp[SP_DONE]) return;
   int32_t* hist = sp + kSpecHist;
@@ -1897,6 +1900,7 @@ __global__ void k_spec_accept(const int32_t* amax, int32_t* sp, int32_t* out_ids
   const int dl = sp[SP_DL], pos0 = sp[SP_POS0];
   int gen = sp[SP_GEN], hlen = sp[SP_HLEN], hits = sp[SP_HITS];
   const int r0 = amax[0];
+  stream_publish(stream, gen, r0, 1);
   out_ids[gen++] = r0;
   hist[hlen++] = r0;
   int cache = pos0 + 1, tok = r0;
@@ -1906,6 +1910,7 @@ __global__ void k_spec_accept(const int32_t* amax, int32_t* sp, int32_t* out_ids
       if (gen >= max_new) break;
       const int nxt = amax[k + 1];
       ++hits;
+      stream_publish(stream, gen, nxt, 2);
       out_ids[gen++] = nxt;
       hist[hlen++] = nxt;
       cache = pos0 + 2 + k;
@@ -1943,7 +1948,7 @@ void lwe_spec_init(int32_t* sp, const int32_t* ids, int n, const int32_t* out_id
   ++g_lwe_launches;
 }
 cudaError_t lwe_spec_iteration(LweArgs a, const LweHost& h, int32_t* sp, int32_t* out_ids, int spec_k, int ngram,
-                               int max_new, int eos, int slot, cudaStream_t st) {
+                               int max_new, int eos, int slot, int32_t* stream, cudaStream_t st) {
   const int T = spec_k + 1;
   g_lwe_pdl = h.pdl != 0;
   lwe_launch(k_spec_prepare, dim3(1), dim3(256), 0, st, a, sp, spec_k, ngram, max_new, T, slot);
@@ -1951,7 +1956,7 @@ cudaError_t lwe_spec_iteration(LweArgs a, const LweHost& h, int32_t* sp, int32_t
   f.skip = sp + SP_DONE;
   const cudaError_t e = lwe_forward(f, h, T, T, false, nullptr, false, st);
   if (e != cudaSuccess) return e;
-  lwe_launch(k_spec_accept, dim3(1), dim3(32), 0, st, (const int32_t*)a.amax, sp, out_ids, max_new, eos);
+  lwe_launch(k_spec_accept, dim3(1), dim3(32), 0, st, (const int32_t*)a.amax, sp, out_ids, max_new, eos, stream);
   return cudaGetLastError();
 }
 void lwe_spec_finish(const int32_t* sp, int32_t* status, cudaStream_t st) {

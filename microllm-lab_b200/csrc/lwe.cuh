@@ -73,7 +73,7 @@ cudaError_t lwe_setup(int kv_len);
 // One prompt (or forward) chunk of a single slot: ids (device) at positions pos0.., lm rows either
 // every token (lm_each) or the last one.
 void lwe_fill(LweArgs a, const int32_t* ids, int n, int slot, int pos0, int lm_each, cudaStream_t st);
-void lwe_first(LweArgs a, int32_t* out_ids, int32_t* status, int eos, int forwards, cudaStream_t st);
+void lwe_first(LweArgs a, int32_t* out_ids, int32_t* status, int eos, int forwards, int32_t* stream, cudaStream_t st);
 void lwe_mark_time(int32_t* status, int idx, cudaStream_t st);
 // Prompt-lookup speculation: device loop state (int32 words), draft [kSpecDraft, +16) and history
 // [kSpecHist, +kv_len + 64).  The done word is SpecWord 3.
@@ -84,7 +84,7 @@ constexpr int kSpecDoneWord = 3;
 void lwe_spec_init(int32_t* sp, const int32_t* ids, int n, const int32_t* out_ids, int max_new, int eos, int kv_len,
                    int prefill_forwards, cudaStream_t st);
 cudaError_t lwe_spec_iteration(LweArgs a, const LweHost& h, int32_t* sp, int32_t* out_ids, int spec_k, int ngram,
-                               int max_new, int eos, int slot, cudaStream_t st);
+                               int max_new, int eos, int slot, int32_t* stream, cudaStream_t st);
 void lwe_spec_finish(const int32_t* sp, int32_t* status, cudaStream_t st);
 // Kernel launches issued so far by the calling thread through these functions.
 long lwe_launch_count();

@@ -23,10 +23,13 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmllm_cuda.so")
 SPECIAL = {"PAD": 0, "UNK": 1, "BOS": 2, "EOS": 3, "SYSTEM": 4, "USER": 5, "ASSISTANT": 6}  # engine/tokenizer.js:188-196
 STOP_NAMES = {0: "eos", 1: "max_new_tokens", 2: "context_limit"}
+PHASE_NAMES = {0: "prefill", 1: "decode", 2: "spec"}  # onToken phases (engine/infer.js:615,630; webgpu.js:1253,1265)
+TOKEN_FN = ctypes.CFUNCTYPE(None, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p)
 
 EXPORTS = ["mllm_create", "mllm_destroy", "mllm_last_error", "mllm_config", "mllm_set_stream", "mllm_bytes_allocated",
            "mllm_reset",
-           "mllm_cache_len", "mllm_forward", "mllm_generate", "mllm_generate_device", "mllm_generate_batch",
+           "mllm_cache_len", "mllm_forward", "mllm_generate", "mllm_generate_stream", "mllm_generate_device",
+           "mllm_generate_batch",
            "mllm_selftest_timeout",
            "mllm_gemv_q4", "mllm_gemm_q4", "mllm_gemm_q4_noalloc"]
 
@@ -76,6 +79,7 @@ def load_library(path: str = LIB_PATH):
     L.mllm_forward.argtypes = [P, I, P, I, I, I, P, P]
     L.mllm_generate.argtypes = [P, I, P, I, I, ctypes.c_int32, I, I, P, ctypes.POINTER(Stats)]
     L.mllm_generate_device.argtypes = [P, I, P, I, I, ctypes.c_int32, I, I, P, ctypes.POINTER(Stats)]
+    L.mllm_generate_stream.argtypes = [P, I, P, I, I, ctypes.c_int32, I, I, P, ctypes.POINTER(Stats), TOKEN_FN, P]
     L.mllm_generate_batch.argtypes = [P, I, P, P, I, ctypes.c_int32, P, P, P, ctypes.POINTER(BatchStats)]
     L.mllm_gemv_q4.argtypes = [P, P, P, P, I, I, I, P]
     L.mllm_gemm_q4.argtypes = [P, P, P, P, I, I, I, P]
@@ -201,18 +205,41 @@ class CudaPetitGPT:
     def generate(self, ids, maxNewTokens: int = 64, eosId: int = SPECIAL["EOS"], onToken=None, specK: int = 0,
                  ngram: int = 3):
         """Greedy generation in one device launch.  ``specK > 0`` turns on prompt-lookup speculation
-        (n-gram size ``ngram``), which runs on the device.  ``onToken(id, meta)`` is called for each
-        id after the launch returns, with phase "prefill" for the first id and "decode" for the rest (the
-        launch does not report which ids were accepted drafts, the reference's "spec" phase)."""
+        (n-gram size ``ngram``), which runs on the device.  ``onToken(id, meta)`` is called for each id
+        while the device is still generating (mllm_generate_stream: the kernels publish every id into
+        mapped host memory as it is chosen), with phase "prefill" (and ``ms``, the host time since the
+        call began) for the first id, "decode" for the others, and "spec" for accepted draft ids, as
+        engine/infer.js:615,630 and engine/webgpu.js:1253,1265 report them."""
         ids = np.ascontiguousarray(ids, np.int32)
         out = np.zeros(max(int(maxNewTokens), 1), np.int32)
         st = Stats()
         t0 = time.perf_counter()
-        self._check(self._lib.mllm_generate(self._h, self.slot, _ptr(ids), len(ids), int(maxNewTokens), int(eosId),
-                                            int(specK), int(ngram), _ptr(out), ctypes.byref(st)))
+        if onToken is None:
+            self._check(self._lib.mllm_generate(self._h, self.slot, _ptr(ids), len(ids), int(maxNewTokens),
+                                                int(eosId), int(specK), int(ngram), _ptr(out), ctypes.byref(st)))
+        else:
+            errors = []
+
+            def cb(tok, index, phase, _user):
+                if errors:
+                    return
+                meta = {"phase": PHASE_NAMES.get(int(phase), "decode")}
+                if index == 0:
+                    meta["ms"] = (time.perf_counter() - t0) * 1e3
+                try:
+                    onToken(int(tok), meta)
+                except BaseException as ex:  # raised again once the call returns
+                    errors.append(ex)
+
+            fn = TOKEN_FN(cb)
+            self._check(self._lib.mllm_generate_stream(self._h, self.slot, _ptr(ids), len(ids), int(maxNewTokens),
+                                                       int(eosId), int(specK), int(ngram), _ptr(out), ctypes.byref(st),
+                                                       fn, None))
+            if errors:
+                raise errors[0]
         wall = (time.perf_counter() - t0) * 1e3
         gen = out[:st.n_generated].tolist()
-        res = {
+        return {
             "generatedIds": gen,
             "stopReason": STOP_NAMES.get(st.stop_reason, "max_new_tokens"),
             "ttftMs": float(st.ttft_ms),
@@ -224,10 +251,6 @@ class CudaPetitGPT:
             "forwards": int(st.forwards),
             "kernelLaunches": int(st.kernel_launches),
         }
-        if onToken:
-            for i, t in enumerate(gen):
-                onToken(t, {"phase": "prefill" if i == 0 else "decode"})
-        return res
 
     def generateBatch(self, seqs, maxNewTokens: int = 64, eosId: int = SPECIAL["EOS"]):
         """Replicated multi-sequence greedy decode (mllm_generate_batch): ``seqs`` is a list of prompts;

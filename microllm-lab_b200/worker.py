@@ -22,8 +22,8 @@ Differences, by design of this backend:
     ``decode(ids, skip_special=False) -> str`` given to the constructor or as ``load``'s ``tokenizer``.
     There is no fetch of a default tokenizer.json. Without a tokenizer, ``generate`` takes ``promptIds``
     (ids as they are, still truncated), and the text fields are None.
-  - All tokens come from one device launch, so the ``token`` replies are posted when the launch returns,
-    in generation order.
+  - The ``token`` replies are posted while the device generates: the kernels publish every id into
+    mapped host memory as it is chosen (mllm_generate_stream), in generation order.
   - ``opts.specK`` / ``opts.ngram`` turn on the on-device prompt-lookup speculation.
 """
 from __future__ import annotations
