@@ -78,6 +78,13 @@ int mllm_set_stream(mllm_engine* e, void* stream);
 /* Device bytes held by the handle (GpuPetitGPT.bytesAllocated, engine/webgpu.js:1047-1065). */
 size_t mllm_bytes_allocated(const mllm_engine* e);
 
+/*
+ * The kernel that runs single-token decode on this handle ("decode1: grid of G CTAs" or
+ * "cdec_kernel: N cluster(s) of 16 CTAs").  No reference counterpart: the reference has one WebGPU
+ * pipeline per stage (engine/webgpu.js:892-1106); this names the launch that replaces them.
+ */
+const char* mllm_decode_kernel(const mllm_engine* e);
+
 /* engine/infer.js:348-358 (resetCache) for one slot. */
 int mllm_reset(mllm_engine* e, int slot);
 

@@ -1,18 +1,27 @@
 // Cluster decode kernel: the greedy single-token decode loop of engine/infer.js:625-639 (each token is
-// forwardDecode, engine/infer.js:579-601) for llama-arch files, as ONE thread-block cluster of 16 CTAs
-// (one per SM) that stays resident for every token of the call.
+// forwardDecode, engine/infer.js:579-601) for llama-arch files, as one thread-block cluster of 16 CTAs
+// (one per SM) per kv head, resident for every token of the call.
 //
-// Per layer, five stages; each ends with an all-to-all exchange through distributed shared memory:
-// every CTA pushes its slice of the stage output into the same buffer of all 16 CTAs with st.async,
-// and each receiving buffer has an mbarrier that completes when all of the stage's bytes have landed.
+// The layer is split the way tensor parallelism splits it, so that only two exchanges per layer cross
+// clusters.  Cluster g owns kv head g and its rep query heads:
 //
-//   x (+ sums of squares)  -> QKV rows (x 1/RMS)                    -> qkv        (all CTAs)
-//   qkv -> RoPE, causal attention of unit (kv head, position split) -> partials  (all CTAs)
-//   partials -> merge -> proj rows + residual                       -> x1 (+ ss) (all CTAs)
-//   x1 -> w1/w3 rows (x 1/RMS) -> SiLU(u) * v                       -> h         (all CTAs)
-//   h -> w2 rows + residual                                          -> x2 (+ ss) (all CTAs)
-// then the final RMSNorm, the lm_head rows of each CTA with a local argmax, and an exchange of the 16
+//   x -> RMSNorm -> the group's q/k/v rows (its 16 CTAs split them)   -> qkv       (DSMEM, cluster)
+//   qkv -> RoPE, causal attention of the group, positions split 16 ways -> partials (DSMEM, cluster)
+//   partials -> merge -> proj columns of the group's heads -> partial of all D rows
+//                                                 -> x1 = x + sum of the clusters' partials   (global)
+//   x1 -> RMSNorm -> w1/w3 rows of this CTA's 32-row FF slice -> SiLU(u) v (stays in the CTA)
+//      -> w2 columns of the slice -> partial of all D rows -> reduce over the cluster (DSMEM)
+//                                                 -> x2 = x1 + sum of the clusters' partials  (global)
+// then the final RMSNorm, the lm_head rows of each CTA with a local argmax, and an exchange of the
 // candidates (engine/infer.js:240-250: the lowest index wins a tie).
+//
+// Inside a cluster every exchange is an all-to-all through distributed shared memory: each CTA
+// pushes its slice into the same buffer of all 16 CTAs with st.async, and each receiving buffer has
+// an mbarrier that completes when all of the stage's bytes have landed.  Between clusters a slice is
+// published as tagged 8-byte words in global memory ({tag, value}, single-copy atomic); each CTA
+// polls 1/16 of the other clusters' words and forwards them by st.async to its 15 peers, so the
+// words cross the L2 once per cluster.  Sums over clusters and over the CTAs of a cluster run in a
+// fixed order, so the result does not depend on timing.
 //
 // Row dot products run on the CUDA cores in fp32 (engine/infer.js:88-116 with f32 instead of f64
 // sums).  A 16-row x 32-wide weight group is one 320-byte record of a warp's private stream: lane
@@ -26,11 +35,9 @@
 //
 // The weights are repacked at load time into one stream per CTA, in the order its warps consume
 // them, cut into 40 KB chunks (8 records per warp); a ring of up to 4 chunk slots is filled by one
-// bulk copy per chunk (cp.async.bulk, completing on the slot's mbarrier), so weight fetch runs a
-// layer ahead of the exchanges.  (Measured on B200 from one 16-SM cluster: bulk copies of 40-64 KB
-// stream 60-70 GB/s per SM; per-warp 16-byte cp.async rings reached about 36 GB/s.)  Per-layer
-// vectors (norm gains, the RoPE row of the position) are fetched into registers a layer or a token
-// ahead.
+// bulk copy per chunk (cp.async.bulk of this GPU's memory, completing on the slot's mbarrier), so
+// weight fetch runs layers ahead of the exchanges.  Per-layer vectors (norm gains, the RoPE row of
+// the position) are fetched into registers a layer or a token ahead.
 //
 // Every wait is bounded (RunArgs::wait_ns, default 0.5 s).  A CTA whose wait runs out raises the
 // device error flag; the others see it in their next wait; all CTAs then meet at the final cluster
@@ -50,6 +57,11 @@ namespace cd {
 __device__ __forceinline__ uint32_t cta_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
   return r;
 }
 __device__ __forceinline__ void cluster_sync_all() {
@@ -149,7 +161,9 @@ __device__ __forceinline__ float dot8(uint32_t w, const float4& a0, const float4
   return r.x + r.y;
 }
 
-enum { B_X2 = 0, B_QKV = 1, B_ATT = 2, B_X1 = 3, B_H = 4, B_CAND = 5, B_COUNT = 6 };
+// Exchange barriers: x2 partials (pp2), the group's q/k/v, attention partials, x1 partials (pp1), the
+// w2 reduce-scatter (rs), argmax candidates.
+enum { B_X2 = 0, B_QKV = 1, B_ATT = 2, B_X1 = 3, B_RS = 4, B_CAND = 5, B_COUNT = 6 };
 
 // The CTA's weight ring: nslot chunk slots, each filled by one bulk copy that completes on the slot's
 // full barrier.  Every warp waits for a chunk before its first record in it and releases the chunk
@@ -320,23 +334,69 @@ __device__ __forceinline__ float inv_rms(const float* xb, int D) {
   return 1.f / sqrtf(s / D + 1e-6f);
 }
 
-// Epilogue + exchange of a row stage: `val(i)` gives the value of local row i (0 .. nrows); thread i
-// computes row i into stage, then thread i sends row quad i / 16 to CTA i % 16.  With ss, the quad's
-// sum of squares also goes to slot (first quad + quad) after the destination's D values.
-template <class F>
-__device__ __forceinline__ void push_rows(int nrows, float* stage, uint32_t dst, uint32_t bar, int ss_slot0,
-                                          uint32_t ss_dst, F val) {
-  for (int i = threadIdx.x; i < nrows; i += kCdThreads) stage[i] = val(i);
-  __syncthreads();
-  for (int i = threadIdx.x; i < nrows * 4; i += kCdThreads) {
+
+// Publish rows [r0, r0 + n) (n a multiple of 4) of cluster cid's D-long partial vector, staged in
+// `vals`: into the global words gx (several clusters), then into `part` (float index cid D + r0) of
+// every CTA of the cluster; then forward this CTA's 1/16 share of the other clusters' vectors, as
+// their tags arrive, to every CTA of the cluster.  All bytes complete on `bar` of the receiving CTA.
+// False when a wait for remote words gave up (the error flag is then raised).
+__device__ __forceinline__ bool publish(const float* vals, int n, int r0, int D, int cid, int nc, uint32_t part,
+                                        uint32_t bar, uint64_t* gx, uint32_t tag, int rank, int* err,
+                                        uint64_t limit) {
+  if (gx)
+    for (int i = threadIdx.x; i < n; i += kCdThreads) ll_store(gx + (size_t)cid * D + r0 + i, tag, vals[i]);
+  for (int i = threadIdx.x; i < n * 4; i += kCdThreads) {  // n / 4 quads x 16 CTAs
     const int q = i >> 4, d = i & 15;
-    const float4 v = reinterpret_cast<const float4*>(stage)[q];
-    const uint32_t rb = mapa(bar, d);
-    st_async4(mapa(dst + 16 * q, d), v, rb);
-    if (ss_slot0 >= 0) {
-      const float s = fmaf(v.w, v.w, fmaf(v.z, v.z, fmaf(v.y, v.y, v.x * v.x)));
-      st_async1(mapa(ss_dst + 4 * (ss_slot0 + q), d), s, rb);
+    st_async4(mapa(part + 4 * (cid * D + r0 + 4 * q), d), reinterpret_cast<const float4*>(vals)[q], mapa(bar, d));
+  }
+  if (!gx) return true;
+  const int QD = D / 4, QR = (nc - 1) * QD;
+  const int j1 = (rank + 1) * QR / kCdCtas;
+  bool ok = true;
+  for (int j = rank * QR / kCdCtas + threadIdx.x; j < j1 && ok; j += kCdThreads) {
+    const int gi = j / QD, q = j - gi * QD;
+    const int g = gi < cid ? gi : gi + 1;
+    const uint64_t* src = gx + (size_t)g * D + 4 * q;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t pending = 15;
+    const uint64_t t0 = globaltimer();
+    for (int it = 0; pending; ++it) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (pending & (1u << e)) {
+          const uint64_t w = ll_load(src + e);
+          if ((uint32_t)(w >> 32) == tag) {
+            v[e] = __uint_as_float((uint32_t)w);
+            pending &= ~(1u << e);
+          }
+        }
+      if (pending && (it & 15) == 15 && (*(volatile int*)err || globaltimer() - t0 > limit)) {
+        atomicCAS(err, 0, 1);
+        ok = false;
+        break;
+      }
     }
+    if (!ok) break;
+    for (int d = 0; d < kCdCtas; ++d)
+      st_async4(mapa(part + 4 * (g * D + 4 * q), d), make_float4(v[0], v[1], v[2], v[3]), mapa(bar, d));
+  }
+  return ok;
+}
+
+// Residual sum out = x + sum_g part[g] (cluster order) over all D values, with the D / 4 quad sums of
+// squares after them.
+__device__ __forceinline__ void residual_sum(float* out, const float* x, const float* part, int D, int nc) {
+  for (int q = threadIdx.x; q < D / 4; q += kCdThreads) {
+    float4 v = reinterpret_cast<const float4*>(x)[q];
+    for (int g = 0; g < nc; ++g) {
+      const float4 p = reinterpret_cast<const float4*>(part + (size_t)g * D)[q];
+      v.x += p.x;
+      v.y += p.y;
+      v.z += p.z;
+      v.w += p.w;
+    }
+    reinterpret_cast<float4*>(out)[q] = v;
+    out[D + q] = fmaf(v.w, v.w, fmaf(v.z, v.z, fmaf(v.y, v.y, v.x * v.x)));
   }
 }
 
@@ -344,21 +404,28 @@ __device__ __forceinline__ void push_rows(int nrows, float* stage, uint32_t dst,
 
 using namespace cd;
 
+static_assert(5 * sizeof(CdGeom) + 6 * sizeof(int) <= 256, "stage table region");
+
 __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_constant__ CdArgs A) {
   extern __shared__ __align__(16) uint8_t smem[];
   const RunArgs& a = A.r;
   const ModelDev& md = a.m;
-  const CdSmem Ls = cd_smem(md, A.smem_cap);
-  const int c = (int)cta_rank();
+  const CdSmem& Ls = A.L;
+  const int nc = A.nc, nct = nc * kCdCtas;
+  const int c = (int)cta_rank();     // rank in the cluster
+  const int cid = (int)cluster_id(); // the cluster's kv head
+  const int gc = cid * kCdCtas + c;  // CTA of the launch
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int D = md.D, QKV = md.QKV, FF = md.FF, NKV = md.NKV, rep = md.NH / md.NKV;
-  const int S = cd_splits(md), U = NKV * S;
+  const int D = md.D, NKV = md.NKV, rep = md.NH / md.NKV;
+  const int RO = D / kCdCtas;        // rows this CTA reduces in the w2 reduce-scatter
   float* actp = reinterpret_cast<float*>(smem + Ls.actp);
   float* red = reinterpret_cast<float*>(smem + Ls.red);
   float* xb2 = reinterpret_cast<float*>(smem + Ls.xb2);
   float* xb1 = reinterpret_cast<float*>(smem + Ls.xb1);
+  float* pp1 = reinterpret_cast<float*>(smem + Ls.pp1);
+  float* pp2 = reinterpret_cast<float*>(smem + Ls.pp2);
+  float* rs = reinterpret_cast<float*>(smem + Ls.rs);
   float* qkvb = reinterpret_cast<float*>(smem + Ls.qkv);
-  float* hb = reinterpret_cast<float*>(smem + Ls.hb);
   float* attb = reinterpret_cast<float*>(smem + Ls.attb);
   float* cand = reinterpret_cast<float*>(smem + Ls.cand);
   float* outv = reinterpret_cast<float*>(smem + Ls.outv);
@@ -369,9 +436,9 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   float* misc = reinterpret_cast<float*>(smem + Ls.misc);
   int* imisc = reinterpret_cast<int*>(misc);
   const uint32_t sbar = smem_u32(smem + Ls.bars);
-  const uint32_t bytes_x = (uint32_t)(D * 4 + D);  // D values + D / 4 quad sums of squares
-  const uint32_t bar_bytes[B_COUNT] = {bytes_x, (uint32_t)QKV * 4, (uint32_t)(U * rep * kCdPartWords * 4), bytes_x,
-                                       (uint32_t)FF * 4, (uint32_t)(kCdCtas * 16)};
+  const uint32_t bar_bytes[B_COUNT] = {(uint32_t)(nc * D * 4), (uint32_t)((rep + 2) * 64 * 4),
+                                       (uint32_t)(kCdCtas * rep * kCdPartWords * 4), (uint32_t)(nc * D * 4),
+                                       (uint32_t)(D * 4), (uint32_t)(nct * 16)};
   const uint64_t limit = a.wait_ns ? a.wait_ns : kWaitNs;
   uint32_t par[B_COUNT] = {0, 0, 0, 0, 0, 0};
   if (tid == 0) {
@@ -385,8 +452,24 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   for (int i = tid; i < 2 * md.n_layers; i += kCdThreads)
     norms[i] = (i & 1) ? md.layers[i >> 1].norm2 : md.layers[i >> 1].norm1;
   if (tid == 0) norms[2 * md.n_layers] = md.norm_f;
+  // per stage: this CTA's geometry and the rotation offset of layer 0; then the offset's step per layer
+  CdGeom* geo = reinterpret_cast<CdGeom*>(smem + Ls.geo);  // [5]
+  int* offs = reinterpret_cast<int*>(geo + 5);              // [6]
+  if (tid < 5) {
+    geo[tid] = cd_stage_geom(md, tid, cid, c, nc);
+    offs[tid] = cd_stage_off(md, cid, c, nc, 0, tid);
+    if (tid == 0) offs[5] = (cd_stage_off(md, cid, c, nc, 1, CD_QKV) - cd_stage_off(md, cid, c, nc, 0, CD_QKV)) &
+                            (kCdWarps - 1);
+  }
   __syncthreads();
   cluster_sync_all();  // every barrier is armed before any CTA sends
+  const CdGeom& gq = geo[CD_QKV];
+  const CdGeom& gp = geo[CD_PROJ];
+  const CdGeom& gw13 = geo[CD_W13];
+  const CdGeom& gw2 = geo[CD_W2];
+  const CdGeom& glm = geo[CD_LM];
+  const int rl = offs[5];
+  const int off_p = offs[CD_PROJ], off_13 = offs[CD_W13], off_2 = offs[CD_W2], off_lm = offs[CD_LM];
 
   // bounded wait + re-arm for the next use of the same buffer
   auto wait_bar = [&](int b) -> bool {
@@ -395,13 +478,20 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
     if (tid == 0) bar_arm(sbar + 8 * b, bar_bytes[b]);
     return true;
   };
+  // global exchange words of a buffer for its current use (null with one cluster), and the use's tag
+  auto gxb = [&](int gb, int b) -> uint64_t* {
+    if (nc == 1) return nullptr;
+    const size_t words = (cd_gx_words(md, nc, gb + 1) - cd_gx_words(md, nc, gb)) / 2;
+    return A.gx + cd_gx_words(md, nc, gb) + (par[b] & 1) * words;
+  };
+  auto tagb = [&](int b) { return A.tag0 + 1u + par[b]; };
 
   Feed F;
-  F.src = A.wst + (size_t)A.woff[c] * kCdChunk;
+  F.src = A.wst + (size_t)A.woff[gc] * kCdChunk;
   F.ring = smem + Ls.ring;
   F.cnt = reinterpret_cast<int*>(smem + Ls.feed);
   F.full = sbar + 8 * 8;
-  F.cpt = A.wcpt[c];
+  F.cpt = A.wcpt[gc];
   F.nslot = (uint32_t)Ls.nslot;
   F.cur = F.ring + (size_t)warp * kCdRpc * kCdRecBytes;
   F.kc = F.slot = F.phase = F.ri = 0;
@@ -410,25 +500,6 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   const bool gen_mode = a.mode == MODE_GENERATE;
   int gen = 0, tok = 0, stop = 1, f = 0;
   bool ok = true;
-  CdGeom gq, gp, gw13, gw2, glm;
-  {
-    int rows, K;
-    bool pr;
-    cd_stage_shape(md, CD_QKV, &rows, &K, &pr);
-    gq = cd_geom(rows, K, pr, c);
-    cd_stage_shape(md, CD_PROJ, &rows, &K, &pr);
-    gp = cd_geom(rows, K, pr, c);
-    cd_stage_shape(md, CD_W13, &rows, &K, &pr);
-    gw13 = cd_geom(rows, K, pr, c);
-    cd_stage_shape(md, CD_W2, &rows, &K, &pr);
-    gw2 = cd_geom(rows, K, pr, c);
-    cd_stage_shape(md, CD_LM, &rows, &K, &pr);
-    glm = cd_geom(rows, K, pr, c);
-  }
-  const int off_lm = cd_stage_off(md, c, 0, CD_LM);
-  const int rl = (cd_stage_off(md, c, 1, CD_QKV) - cd_stage_off(md, c, 0, CD_QKV)) & (kCdWarps - 1);  // per layer
-  const int off_p = cd_stage_off(md, c, 0, CD_PROJ), off_13 = cd_stage_off(md, c, 0, CD_W13),
-            off_2 = cd_stage_off(md, c, 0, CD_W2);
   // gains of this thread's elements k = tid, tid + 512 (D <= 1024): current layer and the next one
   float g1[2], g2[2], n1[2], n2[2];
   auto load_gains = [&](int l, float (&o1)[2], float (&o2)[2]) {
@@ -467,12 +538,12 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       pos = a.pos0;
     }
     // RoPE row of this position for the q / k element this thread rotates (threads < (rep + 1) * 64)
-    float rc = 1.f, rs = 0.f;
+    float rc = 1.f, rs_ = 0.f;
     {
       const int d = tid & 63;
       if (tid < (rep + 1) * 64 && d < md.rope_dim) {
         rc = ldv_f32(md.rope_cos + (size_t)pos * md.rope_dim + d);
-        rs = ldv_f32(md.rope_sin + (size_t)pos * md.rope_dim + d);
+        rs_ = ldv_f32(md.rope_sin + (size_t)pos * md.rope_dim + d);
       }
     }
     // ---- embed (engine/infer.js:360-420): the dequantised tied lm_head row, in every CTA
@@ -493,7 +564,11 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       __syncthreads();
     }
     for (int l = 0; l < md.n_layers; ++l) {
-      if (l > 0 && !(ok = wait_bar(B_X2))) goto done;
+      if (l > 0) {  // x2 of the previous layer
+        if (!(ok = wait_bar(B_X2))) goto done;
+        residual_sum(xb2, xb1, pp2, D, nc);
+        __syncthreads();
+      }
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         g1[j] = n1[j];
@@ -513,17 +588,16 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         const int k = tid + kCdThreads * j;
         if (k < D) actp[k] = pre_scale(xb2[k] * g1[j], k);
       }
-      // attention unit of this CTA and the K/V rows its warp walks first (requested before the stage)
-      const bool has_unit = c < U;
-      const int kvh = c / S, sp = c % S;
-      const int span = (pos + S) / S;
-      const int p_lo = sp * span, p_hi = min(pos + 1, p_lo + span);
-      const size_t kv_base = ((size_t)l * NKV + kvh) * md.kv_len;
+      // this CTA's split of the positions and the K/V rows its warp walks first (requested before the
+      // stage)
+      const int span = (pos + kCdCtas) / kCdCtas;
+      const int p_lo = c * span, p_hi = min(pos + 1, p_lo + span);
+      const size_t kv_base = ((size_t)l * NKV + cid) * md.kv_len;
       float2 kpre[kCdKvPre], vpre[kCdKvPre];
 #pragma unroll
       for (int j = 0; j < kCdKvPre; ++j) {
         const int p = p_lo + warp + kCdWarps * j;
-        if (has_unit && p < p_hi && p < pos) {
+        if (p < p_hi && p < pos) {
           kpre[j] = ldcg_f2(a.kc + (kv_base + p) * 64 + 2 * lane);
           vpre[j] = ldcg_f2(a.vc + (kv_base + p) * 64 + 2 * lane);
         } else {
@@ -531,31 +605,35 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         }
       }
       __syncthreads();
-      // ---- QKV rows
+      // ---- the group's q/k/v rows (engine/infer.js:431-440)
       if (!__syncthreads_and(run_units(F, gq, (l * rl) & (kCdWarps - 1), actp, red, warp, lane, a.err, limit))) {
         ok = false;
         goto done;
       }
-      push_rows(gq.T * 16, outv, smem_u32(qkvb + 16 * gq.t0), sbar + 8 * B_QKV, -1, 0,
-                [&](int i) { return inv1 * row_sum(red, gq, i); });
+      for (int i = tid; i < gq.T * 16; i += kCdThreads) outv[i] = inv1 * row_sum(red, gq, i);
+      __syncthreads();
+      for (int i = tid; i < gq.T * 16 * 4; i += kCdThreads) {  // quads x 16 CTAs
+        const int q = i >> 4, d = i & 15;
+        st_async4(mapa(smem_u32(qkvb + 16 * gq.t0 + 4 * q), d), reinterpret_cast<const float4*>(outv)[q],
+                  mapa(sbar + 8 * B_QKV, d));
+      }
       if (!(ok = wait_bar(B_QKV))) goto done;
-      // ---- attention of unit (kvh, sp) (engine/infer.js:442-495)
-      if (has_unit) {
+      // ---- attention of the group over this CTA's positions (engine/infer.js:442-495)
+      {
         // RoPE'd q heads of the group, the new k (rotated) and v (engine/infer.js:185-225)
         if (tid < (rep + 2) * 64) {
           const int vec = tid >> 6, d = tid & 63;
-          const float* src = vec < rep ? qkvb + (kvh * rep + vec) * 64
-                                       : vec == rep ? qkvb + D + kvh * 64 : qkvb + D + NKV * 64 + kvh * 64;
+          const float* src = qkvb + vec * 64;
           float v = src[d];
           const int half = md.rope_dim / 2;
           if (vec <= rep && d < md.rope_dim) {
-            if (d < half) v = fmaf(-src[d + half], rs, v * rc);
-            else v = fmaf(src[d - half], rs, v * rc);
+            if (d < half) v = fmaf(-src[d + half], rs_, v * rc);
+            else v = fmaf(src[d - half], rs_, v * rc);
           }
           qk[tid] = v;
         }
         __syncthreads();
-        if (pos >= p_lo && pos < p_hi && tid < 128) {  // the cache row of this position (engine/infer.js:457-464)
+        if (pos >= p_lo && pos < p_hi && tid < 128) {  // the cache row (engine/infer.js:457-464)
           const int d = tid & 63;
           if (tid < 64) a.kc[(kv_base + pos) * 64 + d] = qk[rep * 64 + d];
           else a.vc[(kv_base + pos) * 64 + d] = qk[(rep + 1) * 64 + d];
@@ -647,42 +725,47 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         }
       }
       if (!(ok = wait_bar(B_ATT))) goto done;
-      // ---- merge the splits of every head: weights exp(M_s - M) / L per (head, split), then the
-      // attention output straight into the proj activation
-      if (tid < md.NH) {
-        const int h = tid, kv = h / rep, j = h % rep;
+      // ---- merge the 16 splits of each head: weights exp(M_s - M) / L, then the group's attention
+      // output straight into the proj activation
+      if (tid < rep) {
+        const int h = tid;
         float M = -INFINITY;
-        for (int s = 0; s < S; ++s) {
-          const float* pp = attb + ((kv * S + s) * rep + j) * kCdPartWords;
+        for (int s = 0; s < kCdCtas; ++s) {
+          const float* pp = attb + (s * rep + h) * kCdPartWords;
           if (pp[1] > 0.f) M = fmaxf(M, pp[0]);
         }
         float Lsum = 0.f;
-        for (int s = 0; s < S; ++s) {
-          const float* pp = attb + ((kv * S + s) * rep + j) * kCdPartWords;
+        for (int s = 0; s < kCdCtas; ++s) {
+          const float* pp = attb + (s * rep + h) * kCdPartWords;
           const float wt = pp[1] > 0.f ? expf(pp[0] - M) : 0.f;
           mw[h * kCdCtas + s] = wt;
           Lsum = fmaf(pp[1], wt, Lsum);
         }
         const float inv = 1.f / Lsum;
-        for (int s = 0; s < S; ++s) mw[h * kCdCtas + s] *= inv;
+        for (int s = 0; s < kCdCtas; ++s) mw[h * kCdCtas + s] *= inv;
       }
       __syncthreads();
-      for (int i = tid; i < D; i += kCdThreads) {
-        const int h = i >> 6, d = i & 63, kv = h / rep, j = h % rep;
+      for (int i = tid; i < rep * 64; i += kCdThreads) {
+        const int h = i >> 6, d = i & 63;
         float O = 0.f;
-        for (int s = 0; s < S; ++s) O = fmaf(attb[((kv * S + s) * rep + j) * kCdPartWords + 4 + d], mw[h * kCdCtas + s], O);
+        for (int s = 0; s < kCdCtas; ++s) O = fmaf(attb[(s * rep + h) * kCdPartWords + 4 + d], mw[h * kCdCtas + s], O);
         actp[i] = pre_scale(O, i);
       }
       __syncthreads();
-      // ---- proj rows + residual (x1)
+      // ---- proj columns of the group -> partial rows -> x1 (engine/infer.js:497-504)
       if (!__syncthreads_and(run_units(F, gp, (l * rl + off_p) & (kCdWarps - 1), actp, red, warp, lane, a.err, limit))) {
         ok = false;
         goto done;
       }
-      push_rows(gp.T * 16, outv, smem_u32(xb1 + 16 * gp.t0), sbar + 8 * B_X1, 4 * gp.t0, smem_u32(xb1 + D),
-                [&](int i) { return xb2[16 * gp.t0 + i] + row_sum(red, gp, i); });
+      for (int i = tid; i < gp.T * 16; i += kCdThreads) outv[i] = row_sum(red, gp, i);
+      __syncthreads();
+      // a remote wait that gives up raises the error flag; the wait that follows then fails everywhere
+      (void)publish(outv, gp.T * 16, 16 * gp.t0, D, cid, nc, smem_u32(pp1), sbar + 8 * B_X1, gxb(CD_GX_PP1, B_X1),
+                    tagb(B_X1), c, a.err, limit);
       if (!(ok = wait_bar(B_X1))) goto done;
-      // ---- w1 / w3 rows, SiLU(u) * v (engine/infer.js:506-527)
+      residual_sum(xb1, xb2, pp1, D, nc);
+      __syncthreads();
+      // ---- w1 / w3 rows of this CTA's FF slice, SiLU(u) * v (engine/infer.js:506-527)
       const float inv2 = inv_rms(xb1, D);
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
@@ -694,25 +777,39 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         ok = false;
         goto done;
       }
-      push_rows(gw13.T * 16, outv, smem_u32(hb + 16 * gw13.t0), sbar + 8 * B_H, -1, 0, [&](int i) {
+      for (int i = tid; i < gw13.T * 16; i += kCdThreads) {
         const int tl = i >> 4, r = i & 15;
         const float u = inv2 * row_sum(red, gw13, (2 * tl) * 16 + r);
         const float v = inv2 * row_sum(red, gw13, (2 * tl + 1) * 16 + r);
-        return (u / (1.f + expf(-u))) * v;
-      });
-      if (!(ok = wait_bar(B_H))) goto done;
-      // ---- w2 rows + residual (x2)
-      for (int k = tid; k < FF; k += kCdThreads) actp[k] = pre_scale(hb[k], k);
+        actp[i] = pre_scale((u / (1.f + expf(-u))) * v, i);
+      }
       __syncthreads();
+      // ---- w2 columns of the slice -> partial of all D rows -> reduce over the cluster -> x2
       if (!__syncthreads_and(run_units(F, gw2, (l * rl + off_2) & (kCdWarps - 1), actp, red, warp, lane, a.err, limit))) {
         ok = false;
         goto done;
       }
-      push_rows(gw2.T * 16, outv, smem_u32(xb2 + 16 * gw2.t0), sbar + 8 * B_X2, 4 * gw2.t0, smem_u32(xb2 + D),
-                [&](int i) { return xb1[16 * gw2.t0 + i] + row_sum(red, gw2, i); });
+      for (int i = tid; i < D; i += kCdThreads) outv[i] = gw2.G > 0 ? row_sum(red, gw2, i) : 0.f;
+      __syncthreads();
+      for (int i = tid; i < D / 4; i += kCdThreads) {  // quad i goes to the CTA that reduces its rows
+        const int d = (4 * i) / RO, k = 4 * i - d * RO;
+        st_async4(mapa(smem_u32(rs + c * RO + k), d), reinterpret_cast<const float4*>(outv)[i],
+                  mapa(sbar + 8 * B_RS, d));
+      }
+      if (!(ok = wait_bar(B_RS))) goto done;
+      for (int i = tid; i < RO; i += kCdThreads) {
+        float s = 0.f;
+        for (int k = 0; k < kCdCtas; ++k) s += rs[k * RO + i];
+        outv[i] = s;
+      }
+      __syncthreads();
+      (void)publish(outv, RO, c * RO, D, cid, nc, smem_u32(pp2), sbar + 8 * B_X2, gxb(CD_GX_PP2, B_X2), tagb(B_X2), c,
+                    a.err, limit);
     }
     // ---- final RMSNorm, lm_head rows of this CTA, argmax candidates (engine/infer.js:240-250)
     if (!(ok = wait_bar(B_X2))) goto done;
+    residual_sum(xb2, xb1, pp2, D, nc);
+    __syncthreads();
     {
       const float invf = inv_rms(xb2, D);
 #pragma unroll
@@ -757,6 +854,9 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         imisc[48 + warp] = bidx;
       }
       __syncthreads();
+      // this CTA's candidate: to every CTA of the cluster directly, and (several clusters) to gx,
+      // from where each CTA forwards its 1/16 share of the other clusters' candidates
+      uint64_t* gcand = gxb(CD_GX_CAND, B_CAND);
       if (tid < kCdCtas) {
         float bv = -INFINITY;
         int bi = 0x7fffffff;
@@ -768,13 +868,42 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
             bi = id;
           }
         }
-        st_async4(mapa(smem_u32(cand + 4 * c), tid), make_float4(bv, __int_as_float(bi), 0.f, 0.f),
+        if (gcand && tid == 0) {
+          ll_store(gcand + 2 * gc, tagb(B_CAND), bv);
+          ll_store_u32(gcand + 2 * gc + 1, tagb(B_CAND), (uint32_t)bi);
+        }
+        st_async4(mapa(smem_u32(cand + 4 * gc), tid), make_float4(bv, __int_as_float(bi), 0.f, 0.f),
                   mapa(sbar + 8 * B_CAND, tid));
+      }
+      if (gcand) {
+        // other clusters' CTAs: [0, 16 cid) and [16 cid + 16, nct); this CTA takes 1/16 of them
+        const int nr = nct - kCdCtas;
+        bool cok = true;
+        for (int j = c * nr / kCdCtas + tid; j < (c + 1) * nr / kCdCtas && cok; j += kCdThreads) {
+          const int g = j < cid * kCdCtas ? j : j + kCdCtas;
+          uint64_t w0 = 0, w1 = 0;
+          const uint64_t t0 = globaltimer();
+          for (int n = 0;; ++n) {
+            w0 = ll_load(gcand + 2 * g);
+            w1 = ll_load(gcand + 2 * g + 1);
+            if ((uint32_t)(w0 >> 32) == tagb(B_CAND) && (uint32_t)(w1 >> 32) == tagb(B_CAND)) break;
+            if ((n & 15) == 15 && (*(volatile int*)a.err || globaltimer() - t0 > limit)) {
+              atomicCAS(a.err, 0, 1);
+              cok = false;
+              break;
+            }
+          }
+          if (!cok) break;
+          for (int d = 0; d < kCdCtas; ++d)
+            st_async4(mapa(smem_u32(cand + 4 * g), d),
+                      make_float4(__uint_as_float((uint32_t)w0), __uint_as_float((uint32_t)w1), 0.f, 0.f),
+                      mapa(sbar + 8 * B_CAND, d));
+        }
       }
       if (!(ok = wait_bar(B_CAND))) goto done;
       float bv = -INFINITY;
       int bi = 0x7fffffff;
-      for (int cc = 0; cc < kCdCtas; ++cc) {
+      for (int cc = 0; cc < nct; ++cc) {
         const float v = cand[4 * cc];
         const int id = __float_as_int(cand[4 * cc + 1]);
         if (v > bv || (v == bv && id < bi)) {
@@ -786,10 +915,10 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
     }
     ++f;
     if (!gen_mode) {
-      if (c == 0 && tid == 0 && a.argmax_out) a.argmax_out[0] = tok;
+      if (gc == 0 && tid == 0 && a.argmax_out) a.argmax_out[0] = tok;
       continue;
     }
-    if (c == 0 && tid == 0) {
+    if (gc == 0 && tid == 0) {
       a.out_ids[gen] = tok;
       stream_publish(a.stream_ids, gen, tok, 1);
     }
@@ -817,7 +946,7 @@ done:
         }
       }
   }
-  if (c == 0 && tid == 0 && a.mode != MODE_SELFTEST_WAIT && ok) {
+  if (gc == 0 && tid == 0 && a.mode != MODE_SELFTEST_WAIT && ok) {
     if (gen_mode) {
       a.status[ST_NGEN] = gen;
       a.status[ST_STOP] = stop;
@@ -836,18 +965,19 @@ done:
 // ---------------------------------------------------------------------------------------------
 
 // Whether the cluster kernel runs this model: llama arch, head_dim 64, at most 4 query heads per kv
-// head, every exchanged vector a whole number of 16-row tiles, per-CTA stage rows within the thread
-// count (the residual stages keep one row per thread), and the shared-memory plan within `smem_cap`.
+// head, at most kCdMaxClusters kv heads (one cluster each), FF a whole number of 32-row slices, an
+// lm_head tile for every CTA, and the shared-memory plan within `smem_cap` with at least two ring
+// slots.
 bool cd_supported(const ModelDev& m, size_t smem_cap) {
   if (m.arch != 0 || m.D != m.NH * 64 || m.NH % m.NKV || m.NH / m.NKV > 4) return false;
-  if (m.D % 16 || m.QKV % 16 || m.FF % 16 || m.D % 32 || m.FF % 32) return false;
-  if (m.NKV > kCdCtas || m.rope_dim > 64 || m.rope_dim % 2 || m.D > 2 * kCdThreads) return false;
-  if ((m.NH / m.NKV + 2) * 64 > kCdThreads || m.NH > kCdThreads) return false;
-  const CdSmem p = cd_smem(m, (int)smem_cap);
-  return p.nslot >= 3 && (size_t)p.total <= smem_cap;
+  if (m.NKV < 1 || m.NKV > kCdMaxClusters || m.FF % 32 || m.D > 2 * kCdThreads) return false;
+  if (m.rope_dim > 64 || m.rope_dim % 2) return false;
+  if ((m.vocab + 15) / 16 < m.NKV * kCdCtas) return false;
+  const CdSmem p = cd_smem(m, (int)smem_cap, m.NKV);
+  return p.nslot >= 2 && (size_t)p.total <= smem_cap;
 }
 
-size_t cd_smem_bytes(const ModelDev& m, size_t smem_cap) { return (size_t)cd_smem(m, (int)smem_cap).total; }
+size_t cd_smem_bytes(const ModelDev& m, size_t smem_cap) { return (size_t)cd_smem(m, (int)smem_cap, m.NKV).total; }
 
 // Records of every (CTA, warp) stream, in consumption order: per layer QKV, PROJ, W13 (w1 / w3 tiles
 // interleaved), W2, then the lm_head.  A record holds, for lane = 4 gid + t, the words t of group g of
@@ -856,31 +986,30 @@ size_t cd_smem_bytes(const ModelDev& m, size_t smem_cap) { return (size_t)cd_sme
 void cd_pack(const ModelDev& m, const std::vector<HostQ4>& mats /* per layer: qkv, proj, w1, w3, w2 */,
              const HostQ4& lm, std::vector<uint8_t>* out, std::vector<uint32_t>* off, std::vector<uint32_t>* cpt,
              std::vector<uint32_t>* cnt) {
-  off->assign(kCdCtas, 0);
-  cpt->assign(kCdCtas, 0);
-  cnt->assign(kCdCtas * kCdWarps, 0);
-  auto stage_units = [&](int st, int c, int w, int off) {
-    int rows, K;
-    bool paired;
-    cd_stage_shape(m, st, &rows, &K, &paired);
-    const CdGeom g = cd_geom(rows, K, paired, c);
-    const int v = (w - off) & (kCdWarps - 1);
+  const int nc = m.NKV, nct = nc * kCdCtas;
+  off->assign(nct, 0);
+  cpt->assign(nct, 0);
+  cnt->assign((size_t)nct * kCdWarps, 0);
+  auto stage_units = [&](int st, int cid, int c, int w, int o) {
+    const CdGeom g = cd_stage_geom(m, st, cid, c, nc);
+    const int v = (w - o) & (kCdWarps - 1);
     return (size_t)(cd_ustart(g, v + 1) - cd_ustart(g, v));
   };
   size_t chunks = 0;
-  for (int c = 0; c < kCdCtas; ++c) {
+  for (int gc = 0; gc < nct; ++gc) {
+    const int cid = gc / kCdCtas, c = gc % kCdCtas;
     size_t mx = 0;
     for (int w = 0; w < kCdWarps; ++w) {
       size_t n = 0;
       for (int l = 0; l < m.n_layers; ++l)
-        for (int st = CD_QKV; st <= CD_W2; ++st) n += stage_units(st, c, w, cd_stage_off(m, c, l, st));
-      n += stage_units(CD_LM, c, w, cd_stage_off(m, c, 0, CD_LM));
-      (*cnt)[c * kCdWarps + w] = (uint32_t)n;
+        for (int st = CD_QKV; st <= CD_W2; ++st) n += stage_units(st, cid, c, w, cd_stage_off(m, cid, c, nc, l, st));
+      n += stage_units(CD_LM, cid, c, w, cd_stage_off(m, cid, c, nc, 0, CD_LM));
+      (*cnt)[gc * kCdWarps + w] = (uint32_t)n;
       mx = std::max(mx, n);
     }
-    (*off)[c] = (uint32_t)chunks;
-    (*cpt)[c] = (uint32_t)((mx + kCdRpc - 1) / kCdRpc);
-    chunks += (*cpt)[c];
+    (*off)[gc] = (uint32_t)chunks;
+    (*cpt)[gc] = (uint32_t)((mx + kCdRpc - 1) / kCdRpc);
+    chunks += (*cpt)[gc];
   }
   out->assign(chunks * kCdChunk, 0);
   auto emit = [&](uint8_t* dst, const HostQ4& q, int r0, int g) {
@@ -902,38 +1031,37 @@ void cd_pack(const ModelDev& m, const std::vector<HostQ4>& mats /* per layer: qk
         memcpy(dst + 256 + 8 * gid + 4 * h, &s, 4);
       }
   };
-  for (int c = 0; c < kCdCtas; ++c)
+  for (int gc = 0; gc < nct; ++gc) {
+    const int cid = gc / kCdCtas, c = gc % kCdCtas;
     for (int w = 0; w < kCdWarps; ++w) {
       // record j of warp w goes to chunk j / kCdRpc, position w * kCdRpc + j % kCdRpc
       size_t j = 0;
       auto put = [&](const HostQ4& q, int r0, int g) {
-        uint8_t* dst = out->data() + ((size_t)(*off)[c] + j / kCdRpc) * kCdChunk +
+        uint8_t* dst = out->data() + ((size_t)(*off)[gc] + j / kCdRpc) * kCdChunk +
                        (size_t)(w * kCdRpc + j % kCdRpc) * kCdRecBytes;
         emit(dst, q, r0, g);
         ++j;
       };
-      auto emit_stage = [&](int st, int off, const HostQ4* a, const HostQ4* b) {
-        int rows, K;
-        bool paired;
-        cd_stage_shape(m, st, &rows, &K, &paired);
-        const CdGeom g = cd_geom(rows, K, paired, c);
-        const int v = (w - off) & (kCdWarps - 1);
+      auto emit_stage = [&](int st, int l, const HostQ4* a, const HostQ4* b) {
+        const CdGeom g = cd_stage_geom(m, st, cid, c, nc);
+        const int v = (w - cd_stage_off(m, cid, c, nc, l, st)) & (kCdWarps - 1);
         for (int u = cd_ustart(g, v); u < cd_ustart(g, v + 1); ++u) {
-          const int tl = u / g.G, gg = u % g.G;
-          const HostQ4& q = paired ? ((tl & 1) ? *b : *a) : *a;
-          const int tile = g.t0 + (paired ? tl / 2 : tl);
-          put(q, 16 * tile, gg);
+          const int tl = u / g.G, gg = g.k0 + u % g.G;
+          if (st == CD_QKV) put(*a, cd_qkv_row(m, cid, g.t0 + tl), gg);
+          else if (st == CD_W13) put((tl & 1) ? *b : *a, 16 * (g.t0 + tl / 2), gg);
+          else put(*a, 16 * (g.t0 + tl), gg);
         }
       };
       for (int l = 0; l < m.n_layers; ++l) {
         const HostQ4* L = &mats[(size_t)l * 5];
-        emit_stage(CD_QKV, cd_stage_off(m, c, l, CD_QKV), &L[0], nullptr);
-        emit_stage(CD_PROJ, cd_stage_off(m, c, l, CD_PROJ), &L[1], nullptr);
-        emit_stage(CD_W13, cd_stage_off(m, c, l, CD_W13), &L[2], &L[3]);
-        emit_stage(CD_W2, cd_stage_off(m, c, l, CD_W2), &L[4], nullptr);
+        emit_stage(CD_QKV, l, &L[0], nullptr);
+        emit_stage(CD_PROJ, l, &L[1], nullptr);
+        emit_stage(CD_W13, l, &L[2], &L[3]);
+        emit_stage(CD_W2, l, &L[4], nullptr);
       }
-      emit_stage(CD_LM, cd_stage_off(m, c, 0, CD_LM), &lm, nullptr);
+      emit_stage(CD_LM, 0, &lm, nullptr);
     }
+  }
 }
 
 // Kernel attributes (once per process): the cluster of 16 is a non-portable size.
@@ -961,19 +1089,23 @@ int cd_max_clusters(size_t smem) {
   return n;
 }
 
+// One launch of args.nc clusters; with several clusters the launch is cooperative, so that either all
+// of them are resident together or the launch fails (a cluster waits on the others' words).
 cudaError_t cd_launch(const CdArgs& args, size_t smem, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kCdCtas);
+  cfg.gridDim = dim3(kCdCtas * args.nc);
   cfg.blockDim = dim3(kCdThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = kCdCtas;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeCooperative;
+  at[1].val.cooperative = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = args.nc > 1 ? 2 : 1;
   void* params[] = {const_cast<CdArgs*>(&args)};
   return cudaLaunchKernelExC(&cfg, (const void*)cdec_kernel, params);
 }

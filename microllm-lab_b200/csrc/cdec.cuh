@@ -1,6 +1,7 @@
 // Cluster decode: the single-token greedy decode loop (engine/infer.js:579-601 per token,
-// engine/infer.js:625-639 for the loop) as ONE thread-block cluster of 16 CTAs that exchange every
-// stage output through distributed shared memory.
+// engine/infer.js:625-639 for the loop) as one 16-CTA thread-block cluster per kv head; the clusters
+// exchange stage outputs through distributed shared memory inside a cluster and through tagged global
+// words between clusters.
 //
 // Shared by the host runtime (weight repacking, shared-memory sizing) and the kernel (cdec.cu).
 #pragma once
@@ -13,7 +14,8 @@
 
 namespace mllm {
 
-constexpr int kCdCtas = 16;                 // CTAs of the cluster (one per SM)
+constexpr int kCdCtas = 16;                 // CTAs of a cluster (one per SM)
+constexpr int kCdMaxClusters = 8;           // clusters of one launch (one per kv head)
 constexpr int kCdWarps = 16;                // warps per CTA
 constexpr int kCdThreads = kCdWarps * 32;   // 512
 constexpr int kCdRecBytes = 320;            // one weight record: 16 rows x 32-wide group (256 B) + 16 scales
@@ -23,16 +25,17 @@ constexpr int kCdMaxSlots = 4;              // chunks in flight per CTA (ring sl
 constexpr int kCdKvPre = 4;                 // K/V positions per warp held in registers ahead of attention
 constexpr int kCdPartWords = 68;            // attention partial of one head: max, sum, 2 pad, 64 outputs
 
-// Row split of one matrix-vector stage for one CTA, and its warp split.  The stage's rows form
-// NT = ceil(rows / 16) tiles; CTA c takes tiles [t0, t0 + T).  A paired stage (w1 with w3) interleaves
-// the two matrices' tiles: unit tile 2i is w1 tile t0 + i, 2i + 1 is w3 tile t0 + i.  The CTA's
-// N = Tu x G units (unit tile, group of 32), tile-major, are dealt to the warps as contiguous ranges:
-// virtual warp v takes [v q + min(v, rem), (v + 1) q + min(v + 1, rem)) with q = N / 16, rem = N % 16.
-// Warp w plays virtual warp (w - off) mod 16, where off rotates by each stage's rem, so the extra units
-// go round-robin and no warp's stream position drifts more than one record from another's.  A tile
-// spanned by several warps gets one partial per warp, summed in warp order (maxc = the most per tile).
+// Work of one CTA in one matrix-vector stage, and its warp split.  The CTA takes the unit tiles
+// [t0, t0 + T) of the stage's tile list (16 rows each) over G groups of 32 columns starting at group
+// k0.  A paired stage (w1 with w3) interleaves the two matrices' tiles: unit tile 2i is w1 tile t0 + i,
+// 2i + 1 is w3 tile t0 + i.  The N = Tu x G units (unit tile, group), tile-major, are dealt to the
+// warps as contiguous ranges: virtual warp v takes [v q + min(v, rem), (v + 1) q + min(v + 1, rem))
+// with q = N / 16, rem = N % 16.  Warp w plays virtual warp (w - off) mod 16, where off rotates by each
+// stage's rem, so the extra units go round-robin and no warp's stream position drifts more than one
+// record from another's.  A tile spanned by several warps gets one partial per warp, summed in warp
+// order (maxc = the most per tile).
 struct CdGeom {
-  int t0, T, Tu, G, N, q, rem, maxc;
+  int t0, T, Tu, G, k0, N, q, rem, maxc;
 };
 
 __host__ __device__ inline int cd_ustart(const CdGeom& g, int v) { return v * g.q + (v < g.rem ? v : g.rem); }
@@ -41,18 +44,18 @@ __host__ __device__ inline int cd_vwarp(const CdGeom& g, int u) {  // virtual wa
   return u < big ? u / (g.q + 1) : g.rem + (u - big) / (g.q > 0 ? g.q : 1);
 }
 
-__host__ __device__ inline CdGeom cd_geom(int rows, int K, bool paired, int c) {
-  const int NT = (rows + 15) / 16;
+__host__ __device__ inline CdGeom cd_geom(int t0, int T, int G, int k0, bool paired) {
   CdGeom g;
-  g.t0 = (c * NT) / kCdCtas;
-  g.T = ((c + 1) * NT) / kCdCtas - g.t0;
-  g.Tu = paired ? 2 * g.T : g.T;
-  g.G = K / 32;
+  g.t0 = t0;
+  g.T = T;
+  g.Tu = paired ? 2 * T : T;
+  g.G = G;
+  g.k0 = k0;
   g.N = g.Tu * g.G;
   g.q = g.N / kCdWarps;
   g.rem = g.N % kCdWarps;
   g.maxc = 1;
-  for (int t = 0; t < g.Tu; ++t) {
+  for (int t = 0; t < g.Tu && g.G > 0; ++t) {
     const int n = cd_vwarp(g, t * g.G + g.G - 1) - cd_vwarp(g, t * g.G) + 1;
     g.maxc = g.maxc > n ? g.maxc : n;
   }
@@ -60,34 +63,54 @@ __host__ __device__ inline CdGeom cd_geom(int rows, int K, bool paired, int c) {
 }
 
 // Stage kinds in stream order within a layer, then the lm_head.
+//   CD_QKV:  cluster g (kv head g) computes the rows of its group: q heads g rep .. g rep + rep - 1, then
+//            k head g, then v head g ((rep + 2) x 64 rows, group-local tiles split over its 16 CTAs).
+//   CD_PROJ: cluster g multiplies its heads' attention output (columns g rep 64 .. + rep 64 of proj)
+//            into a partial of all D rows; the D / 16 row tiles are split over its 16 CTAs.
+//   CD_W13:  the FF rows, in slices of 32, split over all 16 nc CTAs (w1 and w3 tiles paired).
+//   CD_W2:   every CTA multiplies its own h slice (the columns of its w13 rows) into a partial of all
+//            D rows.
+//   CD_LM:   the vocab rows split over all CTAs.
 enum CdStage { CD_QKV = 0, CD_PROJ = 1, CD_W13 = 2, CD_W2 = 3, CD_LM = 4 };
 
-__host__ __device__ inline void cd_stage_shape(const ModelDev& m, int s, int* rows, int* K, bool* paired) {
-  *paired = s == CD_W13;
-  switch (s) {
-    case CD_QKV: *rows = m.QKV; *K = m.D; break;
-    case CD_PROJ: *rows = m.D; *K = m.D; break;
-    case CD_W13: *rows = m.FF; *K = m.D; break;
-    case CD_W2: *rows = m.D; *K = m.FF; break;
-    default: *rows = m.vocab; *K = m.D; break;
+__host__ __device__ inline CdGeom cd_stage_geom(const ModelDev& m, int st, int cid, int c, int nc) {
+  const int rep = m.NH / m.NKV, nct = nc * kCdCtas, gc = cid * kCdCtas + c;
+  const int NS = m.FF / 32, s0 = gc * NS / nct, s1 = (gc + 1) * NS / nct;
+  switch (st) {
+    case CD_QKV: {
+      const int NT = (rep + 2) * 4;
+      const int t0 = c * NT / kCdCtas;
+      return cd_geom(t0, (c + 1) * NT / kCdCtas - t0, m.D / 32, 0, false);
+    }
+    case CD_PROJ: {
+      const int NT = m.D / 16;
+      const int t0 = c * NT / kCdCtas;
+      return cd_geom(t0, (c + 1) * NT / kCdCtas - t0, 2 * rep, cid * 2 * rep, false);
+    }
+    case CD_W13: return cd_geom(2 * s0, 2 * (s1 - s0), m.D / 32, 0, true);
+    case CD_W2: return cd_geom(0, m.D / 16, s1 - s0, s0, false);
+    default: {
+      const int NT = (m.vocab + 15) / 16;
+      const int t0 = gc * NT / nct;
+      return cd_geom(t0, (gc + 1) * NT / nct - t0, m.D / 32, 0, false);
+    }
   }
 }
 
-// Rotation offset of stage `st` (CD_QKV .. CD_W2 of layer l, or CD_LM) of CTA c: the sum of the
-// rems of the stages before it in the token's stream, mod 16.
-__host__ __device__ inline int cd_stage_off(const ModelDev& m, int c, int l, int st);
+// Row of the QKV matrix at the start of group-local tile j of kv group g.
+__host__ __device__ inline int cd_qkv_row(const ModelDev& m, int g, int j) {
+  const int rep = m.NH / m.NKV;
+  if (j < rep * 4) return g * rep * 64 + 16 * j;
+  if (j < rep * 4 + 4) return m.D + g * 64 + 16 * (j - rep * 4);
+  return m.D + m.NKV * 64 + g * 64 + 16 * (j - rep * 4 - 4);
+}
 
-// Attention work: NKV x S units (kv head, split of positions), S = max(1, 16 / NKV); unit u runs on
-// CTA u.
-__host__ __device__ inline int cd_splits(const ModelDev& m) { return m.NKV >= kCdCtas ? 1 : kCdCtas / m.NKV; }
-
-__host__ __device__ inline int cd_stage_off(const ModelDev& m, int c, int l, int st) {
+// Rotation offset of stage `st` (CD_QKV .. CD_W2 of layer l, or CD_LM) of CTA (cid, c): the sum of
+// the rems of the stages before it in the token's stream, mod 16.
+__host__ __device__ inline int cd_stage_off(const ModelDev& m, int cid, int c, int nc, int l, int st) {
   int rl = 0, pre = 0;
   for (int s = CD_QKV; s <= CD_W2; ++s) {
-    int rows, K;
-    bool paired;
-    cd_stage_shape(m, s, &rows, &K, &paired);
-    const int r = cd_geom(rows, K, paired, c).rem;
+    const int r = cd_stage_geom(m, s, cid, c, nc).rem;
     rl += r;
     if (s < st) pre += r;
   }
@@ -97,49 +120,51 @@ __host__ __device__ inline int cd_stage_off(const ModelDev& m, int c, int l, int
 
 // Shared-memory plan of the kernel (byte offsets; every region 16-byte aligned).
 struct CdSmem {
-  int ring, actp, red, xb2, xb1, qkv, hb, attb, cand, outv, wpart, qk, mw, norms, misc, bars, feed, total;
+  int ring, actp, red, xb2, xb1, pp1, pp2, rs, qkv, attb, cand, outv, wpart, qk, mw, norms, misc, bars, feed, geo,
+      total;
   int red_floats, nslot;
 };
 
 __host__ __device__ inline int cd_align16(int b) { return (b + 15) & ~15; }
 
 // `cap`: the shared-memory limit; the ring takes as many chunk slots (up to kCdMaxSlots) as fit.
-__host__ __device__ inline CdSmem cd_smem(const ModelDev& m, int cap) {
+__host__ __device__ inline CdSmem cd_smem(const ModelDev& m, int cap, int nc) {
   CdSmem s;
   const int rep = m.NH / m.NKV;
-  int redf = 16, outf = rep * kCdPartWords;
-  for (int st = 0; st <= CD_LM; ++st) {
-    int rows, K;
-    bool paired;
-    cd_stage_shape(m, st, &rows, &K, &paired);
-    for (int c = 0; c < kCdCtas; ++c) {
-      const CdGeom g = cd_geom(rows, K, paired, c);
-      redf = redf > g.Tu * g.maxc * 16 ? redf : g.Tu * g.maxc * 16;
-      if (st != CD_LM) outf = outf > g.T * 16 ? outf : g.T * 16;
-    }
-  }
+  int redf = 16, outf = m.D > rep * kCdPartWords ? m.D : rep * kCdPartWords, actf = m.D;
+  for (int st = 0; st <= CD_LM; ++st)
+    for (int cid = 0; cid < nc; ++cid)
+      for (int c = 0; c < kCdCtas; ++c) {
+        const CdGeom g = cd_stage_geom(m, st, cid, c, nc);
+        redf = redf > g.Tu * g.maxc * 16 ? redf : g.Tu * g.maxc * 16;
+        if (st != CD_LM) outf = outf > g.T * 16 ? outf : g.T * 16;
+        if (st == CD_W2) actf = actf > 32 * g.G ? actf : 32 * g.G;
+      }
   int o = 0;
   auto take = [&](int bytes) {
     const int at = o;
     o += cd_align16(bytes);
     return at;
   };
-  s.actp = take((m.FF > m.D ? m.FF : m.D) * 4);
+  s.actp = take(actf * 4);
   s.red = take(redf * 4);
   s.xb2 = take((m.D + m.D / 4) * 4);
   s.xb1 = take((m.D + m.D / 4) * 4);
-  s.qkv = take(m.QKV * 4);
-  s.hb = take(m.FF * 4);
+  s.pp1 = take(nc * m.D * 4);             // proj partials of every cluster
+  s.pp2 = take(nc * m.D * 4);             // w2 partials of every cluster
+  s.rs = take(m.D * 4);                   // w2 partials of this CTA's D / 16 rows from the 16 CTAs
+  s.qkv = take((rep + 2) * 64 * 4);
   s.attb = take(kCdCtas * rep * kCdPartWords * 4);
-  s.cand = take(kCdCtas * 16);
-  s.outv = take(outf * 4);  // a stage's output rows before the push, or the attention partial
+  s.cand = take(nc * kCdCtas * 16);
+  s.outv = take(outf * 4);                // a stage's output rows before the push, or the attention partial
   s.wpart = take(kCdWarps * rep * kCdPartWords * 4);
   s.qk = take((rep + 2) * 64 * 4);
-  s.mw = take((m.NH + 4) * kCdCtas * 4);  // merge weights [head][split], attention warp weights [head][warp]
+  s.mw = take((rep + 4) * kCdCtas * 4);   // merge weights [head][split], attention warp weights [head][warp]
   s.norms = take((2 * m.n_layers + 1) * 8);
   s.misc = take(64 * 4);
   s.bars = take(16 * 8);                  // exchange barriers, then one full barrier per ring slot
   s.feed = take(4 * kCdMaxSlots * 4);     // per slot: release count, last chunk issued
+  s.geo = take(256);                      // per stage: CdGeom and rotation offset
   o = (o + 127) & ~127;
   s.nslot = (cap - o) / kCdChunk;
   if (s.nslot > kCdMaxSlots) s.nslot = kCdMaxSlots;
@@ -150,15 +175,31 @@ __host__ __device__ inline CdSmem cd_smem(const ModelDev& m, int cap) {
   return s;
 }
 
+// Global exchange words between clusters, 8-byte {tag, value}, each buffer [2 parities][words]:
+// proj partials [nc][D], w2 partials [nc][D], argmax candidates [16 nc][2].
+enum { CD_GX_PP1 = 0, CD_GX_PP2 = 1, CD_GX_CAND = 2 };
+__host__ __device__ inline size_t cd_gx_words(const ModelDev& m, int nc, int b /* -1: total */) {
+  const size_t w[3] = {(size_t)nc * m.D, (size_t)nc * m.D, (size_t)2 * nc * kCdCtas};
+  size_t off = 0;
+  for (int i = 0; i < 3; ++i) {
+    if (i == b) return off;
+    off += 2 * w[i];
+  }
+  return off;
+}
+
 // A CTA's weight stream is cpt[c] chunks per token; chunk j holds, for every warp w, its records
 // [j kCdRpc, (j + 1) kCdRpc) (zero records past the warp's count).  One bulk copy moves a chunk.
 struct CdArgs {
   RunArgs r;
   const uint8_t* wst;    // packed chunks of every CTA
-  const uint32_t* woff;  // [kCdCtas] first chunk of each CTA's stream
-  const uint32_t* wcpt;  // [kCdCtas] chunks per token of each CTA
-  const uint32_t* wcnt;  // [kCdCtas * kCdWarps] records per token of each warp
-  int smem_cap;          // the shared-memory limit the plan (cd_smem) was made for
+  const uint32_t* woff;  // [16 nc] first chunk of each CTA's stream
+  const uint32_t* wcpt;  // [16 nc] chunks per token of each CTA
+  const uint32_t* wcnt;  // [16 nc x kCdWarps] records per token of each warp
+  CdSmem L;              // shared-memory plan (cd_smem)
+  int nc;                // clusters of the launch (= nKvHeads)
+  uint64_t* gx;          // global exchange words (cd_gx_words), zeroed before the first launch; null if nc = 1
+  uint32_t tag0;         // tags of this launch are tag0 + 1 + use index (uses < 2^22 per launch)
 };
 
 // ---- host side (cdec.cu)

@@ -101,14 +101,20 @@ struct mllm_engine {
   LweHost lh;
   Grow g_bids, g_plan, g_bout, g_state, g_blogits, g_spec;
   int32_t* h_active = nullptr; // pinned
-  // cluster decode (cdec.cu): the single-token loop on one 16-CTA cluster, for the models it supports
+  // cluster decode (cdec.cu): the single-token loop on one 16-CTA cluster per kv head, for the models
+  // it supports
   int cd_ok = 0;
+  int cd_nc = 1;               // clusters per launch (nKvHeads)
+  CdSmem cd_plan{};            // the kernel's shared-memory plan
   size_t cd_smem = 0;
   uint8_t* d_cdw = nullptr;    // repacked weight chunks
-  uint32_t* d_cdoff = nullptr; // [16] first chunk of each CTA's stream
-  uint32_t* d_cdcpt = nullptr; // [16] chunks per token of each CTA
-  uint32_t* d_cdcnt = nullptr; // [16 x 16] records per token of each warp
-  int cd_cap = 0;              // shared-memory limit the kernel's plan uses
+  uint32_t* d_cdoff = nullptr; // [16 nc] first chunk of each CTA's stream
+  uint32_t* d_cdcpt = nullptr; // [16 nc] chunks per token of each CTA
+  uint32_t* d_cdcnt = nullptr; // [16 nc x 16] records per token of each warp
+  uint64_t* d_cdgx = nullptr;  // exchange words between the clusters (nc > 1)
+  size_t cd_gx_bytes = 0;
+  uint32_t cd_launches = 0;    // launches since the exchange words were last zeroed
+  mutable char kernel_desc[64] = {};
   // token streaming (mllm_generate_stream): ids published by the kernels into mapped pinned memory
   int32_t* h_stream = nullptr; // host view: [0] count, [kStreamHead + i] id i | phase << 30
   int32_t* d_stream = nullptr; // the same words, device view
@@ -297,7 +303,15 @@ int launch(mllm_engine* e, RunArgs& a, int max_forwards, bool multi, bool resume
     ca.woff = e->d_cdoff;
     ca.wcpt = e->d_cdcpt;
     ca.wcnt = e->d_cdcnt;
-    ca.smem_cap = e->cd_cap;
+    ca.L = e->cd_plan;
+    ca.nc = e->cd_nc;
+    ca.gx = e->d_cdgx;
+    // each launch owns 2^22 tags of the exchange words; after 2^10 launches the words are zeroed
+    // and the tags start over
+    if (e->d_cdgx && e->cd_launches % 1024u == 0)
+      CUDA_TRY(e, cudaMemsetAsync(e->d_cdgx, 0, e->cd_gx_bytes, e->stream));
+    ca.tag0 = (e->cd_launches % 1024u) << 22;
+    ++e->cd_launches;
     const cudaError_t lst = cd_launch(ca, e->cd_smem, e->stream);
     ++e->coop_launches;
     if (lst != cudaSuccess) return fail(e, MLLM_ERR_CUDA, "cluster decode launch failed: %s", cudaGetErrorString(lst));
@@ -683,8 +697,9 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   {
     bool want = false;
     if (const char* v = getenv("MLLM_CLUSTER_DECODE")) want = atoi(v) != 0;
+    const int nc = md.NKV;
     if (want && cd_supported(md, smem_cap) && cd_setup(smem_cap) == cudaSuccess &&
-        cd_max_clusters(cd_smem_bytes(md, smem_cap)) >= 1) {
+        cd_max_clusters(cd_smem_bytes(md, smem_cap)) >= nc) {
       auto host_q4 = [&](const std::string& name, int rows, int cols) {
         const PgwTensor* t = tensor(p, name);
         return HostQ4{buf + p.payload_off + t->offset, buf + p.payload_off + t->scale_offset, rows, cols};
@@ -705,12 +720,17 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
       if ((rc = dev_alloc(E, &e->d_cdw, packed.size())) || (rc = dev_alloc(E, &e->d_cdoff, off.size() * 4)) ||
           (rc = dev_alloc(E, &e->d_cdcpt, cpt.size() * 4)) || (rc = dev_alloc(E, &e->d_cdcnt, cnt.size() * 4)))
         return relay(rc);
+      if (nc > 1) {
+        e->cd_gx_bytes = cd_gx_words(md, nc, -1) * 8;
+        if ((rc = dev_alloc(E, &e->d_cdgx, e->cd_gx_bytes))) return relay(rc);
+      }
       cudaMemcpy(e->d_cdw, packed.data(), packed.size(), cudaMemcpyHostToDevice);
       cudaMemcpy(e->d_cdoff, off.data(), off.size() * 4, cudaMemcpyHostToDevice);
       cudaMemcpy(e->d_cdcpt, cpt.data(), cpt.size() * 4, cudaMemcpyHostToDevice);
       cudaMemcpy(e->d_cdcnt, cnt.data(), cnt.size() * 4, cudaMemcpyHostToDevice);
-      e->cd_cap = (int)smem_cap;
       e->cd_smem = cd_smem_bytes(md, smem_cap);
+      e->cd_plan = cd_smem(md, (int)smem_cap, nc);
+      e->cd_nc = nc;
       e->cd_ok = 1;
     }
   }
@@ -829,6 +849,15 @@ int mllm_config(const mllm_engine* e, int32_t* c) {
 }
 
 size_t mllm_bytes_allocated(const mllm_engine* e) { return e ? e->bytes : 0; }
+
+const char* mllm_decode_kernel(const mllm_engine* e) {
+  if (!e) return "";
+  if (e->cd_ok)
+    snprintf(e->kernel_desc, sizeof(e->kernel_desc), "cdec_kernel: %d cluster(s) of %d CTAs", e->cd_nc, kCdCtas);
+  else
+    snprintf(e->kernel_desc, sizeof(e->kernel_desc), "decode1: grid of %d CTAs", e->grid);
+  return e->kernel_desc;
+}
 
 int mllm_set_stream(mllm_engine* e, void* stream) {
   if (!e) return MLLM_ERR_ARG;

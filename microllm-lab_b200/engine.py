@@ -27,7 +27,7 @@ PHASE_NAMES = {0: "prefill", 1: "decode", 2: "spec"}  # onToken phases (engine/i
 TOKEN_FN = ctypes.CFUNCTYPE(None, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p)
 
 EXPORTS = ["mllm_create", "mllm_destroy", "mllm_last_error", "mllm_config", "mllm_set_stream", "mllm_bytes_allocated",
-           "mllm_reset",
+           "mllm_decode_kernel", "mllm_reset",
            "mllm_cache_len", "mllm_forward", "mllm_generate", "mllm_generate_stream", "mllm_generate_device",
            "mllm_generate_batch",
            "mllm_selftest_timeout",
@@ -74,6 +74,8 @@ def load_library(path: str = LIB_PATH):
     L.mllm_config.argtypes = [P, P]
     L.mllm_bytes_allocated.argtypes = [P]
     L.mllm_bytes_allocated.restype = Z
+    L.mllm_decode_kernel.argtypes = [P]
+    L.mllm_decode_kernel.restype = ctypes.c_char_p
     L.mllm_reset.argtypes = [P, I]
     L.mllm_cache_len.argtypes = [P, I]
     L.mllm_forward.argtypes = [P, I, P, I, I, I, P, P]
@@ -163,6 +165,11 @@ class CudaPetitGPT:
     @property
     def bytesAllocated(self) -> int:
         return int(self._lib.mllm_bytes_allocated(self._h))
+
+    @property
+    def decodeKernel(self) -> str:
+        """The kernel that runs single-token decode on this handle."""
+        return self._lib.mllm_decode_kernel(self._h).decode()
 
     def _check(self, rc: int):
         if rc:
