@@ -703,6 +703,54 @@ def run_decode(args):
         dist.destroy_process_group()
 
 
+def run_case(args):
+    """One small, untimed run of a path, sized for a profiler capture (``--case``; prints one summary line).
+
+    decode:  a BASELINE config-1 generate call (PetitGPT shape, seed 0, 64-token prompt) with --new ids;
+    batched: config 5 (SmolLM2-135M shape) with --seqs sequences of 128-token prompts and --new ids;
+    spec:    config 4 (SmolLM2-360M shape, 512-token copy-span prompt) with --new ids at k = --k;
+    gemv:    one cold mllm_gemv_q4 on the lm_head shape (49152 x 576, M = 1)."""
+    import torch
+    P = pkg()
+    if args.case == "gemv":
+        rows, cols = 49152, 576
+        rng = np.random.default_rng(1)
+        packed, scales = P.quant_q4(rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02))
+        pk = torch.from_numpy(np.ascontiguousarray(packed).reshape(-1)).cuda()
+        sc = torch.from_numpy(np.ascontiguousarray(scales).reshape(-1)).cuda()
+        x = torch.from_numpy(rng.standard_normal((1, cols), dtype=np.float32)).cuda()
+        y = torch.empty((1, rows), device="cuda")
+        P.gemv_q4_device(pk.data_ptr(), sc.data_ptr(), x.data_ptr(), y.data_ptr(), rows, cols, 1)
+        torch.cuda.synchronize()
+        print(json.dumps({"case": "gemv", "rows": rows, "cols": cols, "checksum": float(y.double().sum())}))
+        return
+    if args.case == "batched":
+        B = BATCHED
+        cfg = P.CONFIGS[B["model"]]
+        data = P.synthetic_pgw(B["model"], B["seed"], cache_dir=CACHE)
+        nnew = args.new or 3
+        seqs = [P.seeded_prompt(B["plen"], cfg["vocabSize"], sd) for sd in batched_sequence_seeds(0, args.seqs)]
+        eng = P.CudaPetitGPT(data, max_slots=args.seqs, kv_len=B["plen"] + nnew)
+        _, stats = eng.generateBatch(seqs, maxNewTokens=nnew, eosId=-1)
+        print(json.dumps({"case": "batched", "seqs": args.seqs, "new": nnew, "stats": stats}))
+        eng.destroy()
+        return
+    key = "spec4" if args.case == "spec" else "decode"
+    W = WORKLOADS[key]
+    cfg = P.CONFIGS[W["model"]]
+    data = P.synthetic_pgw(W["model"], W["seed"], cache_dir=CACHE)
+    if W.get("copy_spans"):
+        prompt = P.copy_span_prompt(W["prompt"], cfg["vocabSize"], W["seed"])
+    else:
+        prompt = P.seeded_prompt(W["prompt"], cfg["vocabSize"], W["seed"])
+    eng = P.CudaPetitGPT(data)
+    nnew = args.new or 24
+    g = eng.generate(prompt, maxNewTokens=nnew, eosId=-1, specK=args.k if args.case == "spec" else 0)
+    print(json.dumps({"case": args.case, "kernel": eng.decodeKernel, "new": nnew, "deviceMs": g["deviceMs"],
+                      "ids": g["generatedIds"][:8]}))
+    eng.destroy()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -715,8 +763,15 @@ def main():
     ap.add_argument("--batched-steps", type=int, default=3)
     ap.add_argument("--leg-steps", type=int, default=3, help="timed steps of the config 3 and 4 sub-objects")
     ap.add_argument("--no-extra", action="store_true", help="only config 1 (and config 5 unless --no-batched)")
+    ap.add_argument("--case", choices=["decode", "batched", "spec", "gemv"],
+                    help="one small untimed run for a profiler capture (see run_case)")
+    ap.add_argument("--new", type=int, default=0, help="--case: ids to generate")
+    ap.add_argument("--seqs", type=int, default=128, help="--case batched: sequences")
+    ap.add_argument("--k", type=int, default=4, help="--case spec: draft length")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     elif args.workload == "gemv":
         run_gemv(args)

@@ -253,9 +253,10 @@ __device__ __forceinline__ bool feed_token_end(Feed& F, int warp, int lane, int*
 
 // This warp's share of one stage (see CdGeom): its contiguous range of units; per tile the rows'
 // partial sums over the range's groups, scaled per group, reduced over the lane quad, into
-// red[(tile * maxc + slot) * 16 + row] (slot = this warp's order among the tile's warps).  False when a
-// wait for weights gave up.
-__device__ __forceinline__ bool run_units(Feed& F, const CdGeom& g, int off, const float* actp, float* red, int warp,
+// red[(tile * maxc + slot) * 16 + row] (slot = this warp's order among the tile's warps); the warp
+// that ends a tile zeroes the tile's slots after its own, so every tile holds maxc partials.  False
+// when a wait for weights gave up.
+__device__ __forceinline__ bool run_units(Feed& F, const CdGeom g, int off, const float* actp, float* red, int warp,
                                           int lane, int* err, uint64_t limit) {
   const int v = (warp - off) & (kCdWarps - 1);
   const int u1 = cd_ustart(g, v + 1);
@@ -286,19 +287,36 @@ __device__ __forceinline__ bool run_units(Feed& F, const CdGeom& g, int off, con
       float* r = red + (tl * g.maxc + slot) * 16 + gid;
       r[0] = acc0;
       r[8] = acc1;
+      if (ue == (tl + 1) * g.G)
+        for (int k = slot + 1; k < g.maxc; ++k) r[16 * (k - slot)] = r[16 * (k - slot) + 8] = 0.f;
     }
   }
   return true;
 }
 
-// Row i (0 .. 16 Tu) of the CTA's unit tiles: the partials of the tile's warps, in warp order.
-__device__ __forceinline__ float row_sum(const float* red, const CdGeom& g, int i) {
-  const int tl = i >> 4;
-  const int nc = cd_vwarp(g, tl * g.G + g.G - 1) - cd_vwarp(g, tl * g.G) + 1;
-  const float* r = red + tl * g.maxc * 16 + (i & 15);
-  float s = 0.f;
-  for (int k = 0; k < nc; ++k) s += r[k * 16];
-  return s;
+// Sum of each unit row's maxc partials into its slot 0, as a fixed tree over P = 2^ceil(log2 maxc)
+// lanes per row (the same order on every call).  Called by the whole CTA after run_units; ends with a
+// CTA barrier when there was anything to add.
+__device__ __forceinline__ void reduce_tiles(float* red, const CdGeom g) {
+  if (g.maxc <= 1) return;
+  int lp = 1;
+  while ((1 << lp) < g.maxc) ++lp;
+  const int P = 1 << lp, total = g.Tu * 16 * P;
+  for (int base = 0; base < total; base += kCdThreads) {
+    const int t = base + (int)threadIdx.x;
+    const int row = t >> lp, k = t & (P - 1);
+    float* r = red + ((row >> 4) * g.maxc) * 16 + (row & 15);
+    float v = (t < total && k < g.maxc) ? r[16 * k] : 0.f;
+    for (int o = P >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncwarp();
+    if (t < total && k == 0) r[0] = v;
+  }
+  __syncthreads();
+}
+
+// Row i (0 .. 16 Tu) of the CTA's unit tiles after reduce_tiles.
+__device__ __forceinline__ float row_val(const float* red, const CdGeom& g, int i) {
+  return red[((i >> 4) * g.maxc) * 16 + (i & 15)];
 }
 
 // Pre-scaled stage activation for element k: x * 16^-e(k % 8) (exact).
@@ -412,6 +430,18 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   const ModelDev& md = a.m;
   const CdSmem& Ls = A.L;
   const int nc = A.nc, nct = nc * kCdCtas;
+  {
+    // The launch must have the shape the weight streams were packed for: nc clusters of 16 CTAs.  A
+    // launch of another shape (for example one re-issued without its cluster attribute) returns
+    // before touching any stream table or peer memory, with the shape error on the flag.
+    uint32_t ncta, nclu;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(ncta));
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(nclu));
+    if (ncta != (uint32_t)kCdCtas || nclu != (uint32_t)nc || gridDim.x != (uint32_t)nct) {
+      if (threadIdx.x == 0) atomicCAS(A.r.err, 0, kCdShapeError);
+      return;
+    }
+  }
   const int c = (int)cta_rank();     // rank in the cluster
   const int cid = (int)cluster_id(); // the cluster's kv head
   const int gc = cid * kCdCtas + c;  // CTA of the launch
@@ -610,7 +640,8 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         ok = false;
         goto done;
       }
-      for (int i = tid; i < gq.T * 16; i += kCdThreads) outv[i] = inv1 * row_sum(red, gq, i);
+      reduce_tiles(red, gq);
+      for (int i = tid; i < gq.T * 16; i += kCdThreads) outv[i] = inv1 * row_val(red, gq, i);
       __syncthreads();
       for (int i = tid; i < gq.T * 16 * 4; i += kCdThreads) {  // quads x 16 CTAs
         const int q = i >> 4, d = i & 15;
@@ -710,10 +741,10 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
           }
         }
         __syncthreads();
-        if (tid < rep * 64) {
-          const int h = tid >> 6, d = tid & 63;
+        if (tid < rep * 64) {  // warp w walked positions only if p_lo + w < p_hi
+          const int h = tid >> 6, d = tid & 63, nw = max(0, min(kCdWarps, p_hi - p_lo));
           float O = 0.f;
-          for (int w = 0; w < kCdWarps; ++w) O = fmaf(wpart[(w * rep + h) * kCdPartWords + 4 + d], mw[h * kCdWarps + w], O);
+          for (int w = 0; w < nw; ++w) O = fmaf(wpart[(w * rep + h) * kCdPartWords + 4 + d], mw[h * kCdWarps + w], O);
           outv[h * kCdPartWords + 4 + d] = O;
         }
         __syncthreads();
@@ -727,29 +758,24 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       if (!(ok = wait_bar(B_ATT))) goto done;
       // ---- merge the 16 splits of each head: weights exp(M_s - M) / L, then the group's attention
       // output straight into the proj activation
-      if (tid < rep) {
-        const int h = tid;
-        float M = -INFINITY;
-        for (int s = 0; s < kCdCtas; ++s) {
-          const float* pp = attb + (s * rep + h) * kCdPartWords;
-          if (pp[1] > 0.f) M = fmaxf(M, pp[0]);
-        }
-        float Lsum = 0.f;
-        for (int s = 0; s < kCdCtas; ++s) {
-          const float* pp = attb + (s * rep + h) * kCdPartWords;
-          const float wt = pp[1] > 0.f ? expf(pp[0] - M) : 0.f;
-          mw[h * kCdCtas + s] = wt;
-          Lsum = fmaf(pp[1], wt, Lsum);
-        }
-        const float inv = 1.f / Lsum;
-        for (int s = 0; s < kCdCtas; ++s) mw[h * kCdCtas + s] *= inv;
+      // splits that hold positions: CTA s covers [s span, (s + 1) span)
+      const int nsp = min(kCdCtas, pos / span + 1);
+      if (warp < rep) {  // warp h: the weights of head h's splits (lane s)
+        const int h = warp, s = lane;
+        const float* pp = attb + (s * rep + h) * kCdPartWords;
+        const bool live = s < nsp && pp[1] > 0.f;
+        const float M = warp_max(live ? pp[0] : -INFINITY);
+        const float wt = live ? expf(pp[0] - M) : 0.f;
+        const float inv = 1.f / warp_sum(live ? pp[1] * wt : 0.f);
+        if (s < kCdCtas) mw[h * kCdCtas + s] = wt * inv;
       }
       __syncthreads();
-      for (int i = tid; i < rep * 64; i += kCdThreads) {
-        const int h = i >> 6, d = i & 63;
+      if (tid < 2 * rep * 64) {  // output i = tid / 2: even splits on one lane, odd on the next
+        const int i = tid >> 1, h = i >> 6, d = i & 63;
         float O = 0.f;
-        for (int s = 0; s < kCdCtas; ++s) O = fmaf(attb[(s * rep + h) * kCdPartWords + 4 + d], mw[h * kCdCtas + s], O);
-        actp[i] = pre_scale(O, i);
+        for (int s = tid & 1; s < nsp; s += 2) O = fmaf(attb[(s * rep + h) * kCdPartWords + 4 + d], mw[h * kCdCtas + s], O);
+        O += __shfl_xor_sync(0xffffffffu, O, 1);
+        if ((tid & 1) == 0) actp[i] = pre_scale(O, i);
       }
       __syncthreads();
       // ---- proj columns of the group -> partial rows -> x1 (engine/infer.js:497-504)
@@ -757,7 +783,8 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         ok = false;
         goto done;
       }
-      for (int i = tid; i < gp.T * 16; i += kCdThreads) outv[i] = row_sum(red, gp, i);
+      reduce_tiles(red, gp);
+      for (int i = tid; i < gp.T * 16; i += kCdThreads) outv[i] = row_val(red, gp, i);
       __syncthreads();
       // a remote wait that gives up raises the error flag; the wait that follows then fails everywhere
       (void)publish(outv, gp.T * 16, 16 * gp.t0, D, cid, nc, smem_u32(pp1), sbar + 8 * B_X1, gxb(CD_GX_PP1, B_X1),
@@ -777,10 +804,11 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         ok = false;
         goto done;
       }
+      reduce_tiles(red, gw13);
       for (int i = tid; i < gw13.T * 16; i += kCdThreads) {
         const int tl = i >> 4, r = i & 15;
-        const float u = inv2 * row_sum(red, gw13, (2 * tl) * 16 + r);
-        const float v = inv2 * row_sum(red, gw13, (2 * tl + 1) * 16 + r);
+        const float u = inv2 * row_val(red, gw13, (2 * tl) * 16 + r);
+        const float v = inv2 * row_val(red, gw13, (2 * tl + 1) * 16 + r);
         actp[i] = pre_scale((u / (1.f + expf(-u))) * v, i);
       }
       __syncthreads();
@@ -789,7 +817,8 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         ok = false;
         goto done;
       }
-      for (int i = tid; i < D; i += kCdThreads) outv[i] = gw2.G > 0 ? row_sum(red, gw2, i) : 0.f;
+      reduce_tiles(red, gw2);
+      for (int i = tid; i < D; i += kCdThreads) outv[i] = gw2.G > 0 ? row_val(red, gw2, i) : 0.f;
       __syncthreads();
       for (int i = tid; i < D / 4; i += kCdThreads) {  // quad i goes to the CTA that reduces its rows
         const int d = (4 * i) / RO, k = 4 * i - d * RO;
@@ -797,10 +826,13 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
                   mapa(sbar + 8 * B_RS, d));
       }
       if (!(ok = wait_bar(B_RS))) goto done;
-      for (int i = tid; i < RO; i += kCdThreads) {
-        float s = 0.f;
-        for (int k = 0; k < kCdCtas; ++k) s += rs[k * RO + i];
-        outv[i] = s;
+      if (tid < 8 * RO) {  // row tid / 8: lane k adds the partials of CTAs k and k + 8, then a tree over the 8 lanes
+        const int i = tid >> 3, k = tid & 7;
+        float s = rs[k * RO + i] + rs[(k + 8) * RO + i];
+        s += __shfl_xor_sync(0xffffffffu, s, 4);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        if (k == 0) outv[i] = s;
       }
       __syncthreads();
       (void)publish(outv, RO, c * RO, D, cid, nc, smem_u32(pp2), sbar + 8 * B_X2, gxb(CD_GX_PP2, B_X2), tagb(B_X2), c,
@@ -827,13 +859,14 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         ok = false;
         goto done;
       }
+      reduce_tiles(red, glm);
       float best = -INFINITY;
       int bidx = 0x7fffffff;
       const int r0 = 16 * glm.t0;
       for (int i = tid; i < glm.T * 16; i += kCdThreads) {
         const int r = r0 + i;
         if (r >= md.vocab) break;
-        const float v = invf * row_sum(red, glm, i);
+        const float v = invf * row_val(red, glm, i);
         if (!gen_mode && a.logits) a.logits[r] = v;
         if (v > best) {  // rows rise per thread: strict > keeps the lowest index on ties
           best = v;

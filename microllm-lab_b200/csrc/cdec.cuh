@@ -24,6 +24,7 @@ constexpr int kCdChunk = kCdWarps * kCdRpc * kCdRecBytes;  // 40,960 bytes: one 
 constexpr int kCdMaxSlots = 4;              // chunks in flight per CTA (ring slots)
 constexpr int kCdKvPre = 4;                 // K/V positions per warp held in registers ahead of attention
 constexpr int kCdPartWords = 68;            // attention partial of one head: max, sum, 2 pad, 64 outputs
+constexpr int kCdShapeError = 3;            // error flag value: the launch's cluster shape is not the packed one
 
 // Work of one CTA in one matrix-vector stage, and its warp split.  The CTA takes the unit tiles
 // [t0, t0 + T) of the stage's tile list (16 rows each) over G groups of 32 columns starting at group

@@ -376,6 +376,8 @@ int finish(mllm_engine* e) {
     cudaMemset(e->lw.skctr, 0, kLweSplitKTiles * sizeof(int));
   }
   if (e->h_status[ST_WORDS] == 2) return fail(e, MLLM_ERR_ARG, "a prompt token id is out of range");
+  if (e->h_status[ST_WORDS] == kCdShapeError)
+    return fail(e, MLLM_ERR_CUDA, "cluster decode ran with a launch shape other than its clusters of %d CTAs", kCdCtas);
   if (e->h_status[ST_WORDS] != 0)
     return fail(e, MLLM_ERR_TIMEOUT, "a device-side wait exceeded its time limit; the call was abandoned");
   return MLLM_OK;
