@@ -256,41 +256,65 @@ __device__ __forceinline__ bool feed_token_end(Feed& F, int warp, int lane, int*
 // red[(tile * maxc + slot) * 16 + row] (slot = this warp's order among the tile's warps); the warp
 // that ends a tile zeroes the tile's slots after its own, so every tile holds maxc partials.  False
 // when a wait for weights gave up.
-__device__ __forceinline__ bool run_units(Feed& F, const CdGeom g, int off, const float* actp, float* red, int warp,
-                                          int lane, int* err, uint64_t limit) {
-  const int v = (warp - off) & (kCdWarps - 1);
-  const int u1 = cd_ustart(g, v + 1);
+// This virtual warp's units of one stage, precomputed once per launch: [u0, u1), the tile of u0 and the
+// warp's slot in it (a warp that goes on into the next tile is that tile's first warp: slot 0).
+struct CdRange {
+  int u0, u1, tl0, slot0;
+};
+
+__device__ __forceinline__ bool run_units(Feed& F, const CdRange R, int G, int maxc, const float* actp, float* red,
+                                          int warp, int lane, int* err, uint64_t limit) {
   const int gid = lane >> 2, t = lane & 3;
-  int u = cd_ustart(g, v);
-  while (u < u1) {
-    const int tl = u / g.G;
-    const int ue = min(u1, (tl + 1) * g.G);
-    const int slot = v - cd_vwarp(g, tl * g.G);
-    const float* ap = actp + 32 * (u - tl * g.G) + 8 * t;
-    float acc0 = 0.f, acc1 = 0.f;
-    for (; u < ue; ++u, ap += 32) {
-      if (F.ri == 0 && !feed_wait(F, err, limit)) return false;
-      const uint2 wv = *reinterpret_cast<const uint2*>(F.cur + 8 * lane);
-      const float2 sc = *reinterpret_cast<const float2*>(F.cur + 256 + 8 * gid);
-      const float4 a0 = reinterpret_cast<const float4*>(ap)[0];
-      const float4 a1 = reinterpret_cast<const float4*>(ap)[1];
-      acc0 = fmaf(dot8(wv.x, a0, a1), sc.x, acc0);
-      acc1 = fmaf(dot8(wv.y, a0, a1), sc.y, acc1);
-      F.cur += kCdRecBytes;
-      if (++F.ri == kCdRpc) feed_next_chunk(F, warp, lane);
-    }
+  int u = R.u0, tl = R.tl0, slot = R.slot0;
+  int k = u - tl * G;  // group of the current unit within its tile
+  const float* ap = actp + 32 * k + 8 * t;
+  float acc0 = 0.f, acc1 = 0.f;
+  // the tile's partial into its slot; the warp that ends a tile zeroes the slots after its own
+  auto flush = [&](bool ends_tile) {
     acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
     acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
     acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
     acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
     if (t == 0) {
-      float* r = red + (tl * g.maxc + slot) * 16 + gid;
+      float* r = red + (tl * maxc + slot) * 16 + gid;
       r[0] = acc0;
       r[8] = acc1;
-      if (ue == (tl + 1) * g.G)
-        for (int k = slot + 1; k < g.maxc; ++k) r[16 * (k - slot)] = r[16 * (k - slot) + 8] = 0.f;
+      if (ends_tile)
+        for (int q = slot + 1; q < maxc; ++q) r[16 * (q - slot)] = r[16 * (q - slot) + 8] = 0.f;
+    }
+  };
+  while (u < R.u1) {
+    if (F.ri == 0 && !feed_wait(F, err, limit)) return false;
+    // the records of this chunk that belong to the current tile: no wait or fence between them, so
+    // their loads overlap the previous records' arithmetic
+    const int n = min(min(R.u1 - u, G - k), kCdRpc - (int)F.ri);
+    const uint8_t* cur = F.cur;
+#pragma unroll 4
+    for (int j = 0; j < n; ++j) {
+      const uint2 wv = *reinterpret_cast<const uint2*>(cur + 8 * lane);
+      const float2 sc = *reinterpret_cast<const float2*>(cur + 256 + 8 * gid);
+      const float4 a0 = reinterpret_cast<const float4*>(ap)[0];
+      const float4 a1 = reinterpret_cast<const float4*>(ap)[1];
+      acc0 = fmaf(dot8(wv.x, a0, a1), sc.x, acc0);
+      acc1 = fmaf(dot8(wv.y, a0, a1), sc.y, acc1);
+      cur += kCdRecBytes;
+      ap += 32;
+    }
+    F.cur = cur;
+    F.ri += n;
+    u += n;
+    k += n;
+    if (F.ri == kCdRpc) feed_next_chunk(F, warp, lane);
+    if (k == G) {
+      flush(true);
+      ++tl;
+      k = 0;
+      slot = 0;
+      acc0 = acc1 = 0.f;
+      ap = actp + 8 * t;
     }
   }
+  if (k > 0) flush(false);
   return true;
 }
 
@@ -375,26 +399,24 @@ __device__ __forceinline__ bool publish(const float* vals, int n, int r0, int D,
     const int gi = j / QD, q = j - gi * QD;
     const int g = gi < cid ? gi : gi + 1;
     const uint64_t* src = gx + (size_t)g * D + 4 * q;
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    uint32_t pending = 15;
+    // the quad's four words in two 16-byte loads per round, both in flight together
+    uint64_t w0, w1, w2, w3;
     const uint64_t t0 = globaltimer();
-    for (int it = 0; pending; ++it) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        if (pending & (1u << e)) {
-          const uint64_t w = ll_load(src + e);
-          if ((uint32_t)(w >> 32) == tag) {
-            v[e] = __uint_as_float((uint32_t)w);
-            pending &= ~(1u << e);
-          }
-        }
-      if (pending && (it & 15) == 15 && (*(volatile int*)err || globaltimer() - t0 > limit)) {
+    for (int it = 0;; ++it) {
+      ll_load2(src, w0, w1);
+      ll_load2(src + 2, w2, w3);
+      if ((uint32_t)(w0 >> 32) == tag && (uint32_t)(w1 >> 32) == tag && (uint32_t)(w2 >> 32) == tag &&
+          (uint32_t)(w3 >> 32) == tag)
+        break;
+      if ((it & 15) == 15 && (*(volatile int*)err || globaltimer() - t0 > limit)) {
         atomicCAS(err, 0, 1);
         ok = false;
         break;
       }
     }
     if (!ok) break;
+    const float v[4] = {__uint_as_float((uint32_t)w0), __uint_as_float((uint32_t)w1), __uint_as_float((uint32_t)w2),
+                        __uint_as_float((uint32_t)w3)};
     for (int d = 0; d < kCdCtas; ++d)
       st_async4(mapa(part + 4 * (g * D + 4 * q), d), make_float4(v[0], v[1], v[2], v[3]), mapa(bar, d));
   }
@@ -422,7 +444,7 @@ __device__ __forceinline__ void residual_sum(float* out, const float* x, const f
 
 using namespace cd;
 
-static_assert(5 * sizeof(CdGeom) + 6 * sizeof(int) <= 256, "stage table region");
+static_assert(5 * sizeof(CdGeom) + 6 * sizeof(int) + 5 * kCdWarps * sizeof(CdRange) <= 2048, "stage table region");
 
 __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_constant__ CdArgs A) {
   extern __shared__ __align__(16) uint8_t smem[];
@@ -462,10 +484,15 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   float* wpart = reinterpret_cast<float*>(smem + Ls.wpart);
   float* qk = reinterpret_cast<float*>(smem + Ls.qk);
   float* mw = reinterpret_cast<float*>(smem + Ls.mw);
+  float* kst = reinterpret_cast<float*>(smem + Ls.kvst);  // [kCdKvStage][64]
+  float* vst = kst + kCdKvStage * 64;
   const float** norms = reinterpret_cast<const float**>(smem + Ls.norms);
   float* misc = reinterpret_cast<float*>(smem + Ls.misc);
   int* imisc = reinterpret_cast<int*>(misc);
   const uint32_t sbar = smem_u32(smem + Ls.bars);
+  const uint32_t kvbar = sbar + 8 * 6;
+  uint32_t kvph = 0;       // phases of the K/V staging barrier completed
+  bool kv_pending = false; // a staging copy is in flight
   const uint32_t bar_bytes[B_COUNT] = {(uint32_t)(nc * D * 4), (uint32_t)((rep + 2) * 64 * 4),
                                        (uint32_t)(kCdCtas * rep * kCdPartWords * 4), (uint32_t)(nc * D * 4),
                                        (uint32_t)(D * 4), (uint32_t)(nct * 16)};
@@ -473,6 +500,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   uint32_t par[B_COUNT] = {0, 0, 0, 0, 0, 0};
   if (tid == 0) {
     for (int b = 0; b < B_COUNT; ++b) bar_init(sbar + 8 * b, 1);
+    bar_init(kvbar, 1);
     for (int sl = 0; sl < Ls.nslot; ++sl) bar_init(sbar + 8 * (8 + sl), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     for (int b = 0; b < B_COUNT; ++b) bar_arm(sbar + 8 * b, bar_bytes[b]);
@@ -485,6 +513,17 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   // per stage: this CTA's geometry and the rotation offset of layer 0; then the offset's step per layer
   CdGeom* geo = reinterpret_cast<CdGeom*>(smem + Ls.geo);  // [5]
   int* offs = reinterpret_cast<int*>(geo + 5);              // [6]
+  CdRange* wr = reinterpret_cast<CdRange*>(offs + 6);       // [5][16]: per stage and virtual warp
+  if (tid < 5 * kCdWarps) {
+    const int st = tid / kCdWarps, v = tid % kCdWarps;
+    const CdGeom g = cd_stage_geom(md, st, cid, c, nc);
+    CdRange r;
+    r.u0 = cd_ustart(g, v);
+    r.u1 = cd_ustart(g, v + 1);
+    r.tl0 = g.G > 0 ? r.u0 / g.G : 0;
+    r.slot0 = r.u0 < r.u1 ? v - cd_vwarp(g, r.tl0 * g.G) : 0;
+    wr[tid] = r;
+  }
   if (tid < 5) {
     geo[tid] = cd_stage_geom(md, tid, cid, c, nc);
     offs[tid] = cd_stage_off(md, cid, c, nc, 0, tid);
@@ -526,6 +565,26 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   F.cur = F.ring + (size_t)warp * kCdRpc * kCdRecBytes;
   F.kc = F.slot = F.phase = F.ri = 0;
   F.tok_end = F.cpt;
+  // Copy the first nst cache rows (K and V) of this CTA's positions [p0, ..) of `layer` into shared
+  // memory (one thread issues; every thread records the pending phase).  The issuing thread's proxy
+  // fence orders the cache rows other CTAs of the cluster stored (seen through the cluster's
+  // release/acquire exchanges) and this CTA's earlier reads of the buffers before the copies.
+  auto stage_kv = [&](int layer, int p0, int nst, bool issuer) {
+    if (nst <= 0) return;
+    if (issuer) {
+      const size_t base = ((size_t)layer * md.NKV + cid) * md.kv_len + p0;
+      asm volatile("fence.proxy.async;" ::: "memory");
+      bar_arm(kvbar, 2u * nst * 256u);
+      bulk_g2s(kst, a.kc + base * 64, nst * 256u, reinterpret_cast<uint64_t*>(smem + Ls.bars) + 6);
+      bulk_g2s(vst, a.vc + base * 64, nst * 256u, reinterpret_cast<uint64_t*>(smem + Ls.bars) + 6);
+    }
+    kv_pending = true;
+  };
+  // this warp's share of stage st when the stage's rotation offset is off
+  auto units = [&](int st, int off) {
+    return run_units(F, wr[st * kCdWarps + ((warp - off) & (kCdWarps - 1))], geo[st].G, geo[st].maxc, actp, red, warp,
+                     lane, a.err, limit);
+  };
 
   const bool gen_mode = a.mode == MODE_GENERATE;
   int gen = 0, tok = 0, stop = 1, f = 0;
@@ -618,25 +677,17 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         const int k = tid + kCdThreads * j;
         if (k < D) actp[k] = pre_scale(xb2[k] * g1[j], k);
       }
-      // this CTA's split of the positions and the K/V rows its warp walks first (requested before the
-      // stage)
+      // this CTA's split of the positions [p_lo, p_hi); its first kCdKvStage cache rows are copied into
+      // shared memory now, so that they have landed when attention starts
       const int span = (pos + kCdCtas) / kCdCtas;
       const int p_lo = c * span, p_hi = min(pos + 1, p_lo + span);
+      const int npos = max(0, p_hi - p_lo);
+      const int nst = max(0, min(min(p_hi, pos) - p_lo, kCdKvStage));
       const size_t kv_base = ((size_t)l * NKV + cid) * md.kv_len;
-      float2 kpre[kCdKvPre], vpre[kCdKvPre];
-#pragma unroll
-      for (int j = 0; j < kCdKvPre; ++j) {
-        const int p = p_lo + warp + kCdWarps * j;
-        if (p < p_hi && p < pos) {
-          kpre[j] = ldcg_f2(a.kc + (kv_base + p) * 64 + 2 * lane);
-          vpre[j] = ldcg_f2(a.vc + (kv_base + p) * 64 + 2 * lane);
-        } else {
-          kpre[j] = vpre[j] = make_float2(0.f, 0.f);
-        }
-      }
+      if (l == 0) stage_kv(0, p_lo, nst, tid == 0);
       __syncthreads();
       // ---- the group's q/k/v rows (engine/infer.js:431-440)
-      if (!__syncthreads_and(run_units(F, gq, (l * rl) & (kCdWarps - 1), actp, red, warp, lane, a.err, limit))) {
+      if (!__syncthreads_and(units(CD_QKV, l * rl))) {
         ok = false;
         goto done;
       }
@@ -664,90 +715,159 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
           qk[tid] = v;
         }
         __syncthreads();
+        // every position of the CTA in the staged rows: the new row is copied in beside them
+        const bool fast = npos <= kCdKvStage;
         if (pos >= p_lo && pos < p_hi && tid < 128) {  // the cache row (engine/infer.js:457-464)
           const int d = tid & 63;
-          if (tid < 64) a.kc[(kv_base + pos) * 64 + d] = qk[rep * 64 + d];
-          else a.vc[(kv_base + pos) * 64 + d] = qk[(rep + 1) * 64 + d];
-          __threadfence();
-        }
-        float qr[4][2], m[4], lsum[4], o[4][2];
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          qr[h][0] = h < rep ? qk[h * 64 + 2 * lane] : 0.f;
-          qr[h][1] = h < rep ? qk[h * 64 + 2 * lane + 1] : 0.f;
-          m[h] = -INFINITY;
-          lsum[h] = 0.f;
-          o[h][0] = o[h][1] = 0.f;
-        }
-        for (int j = 0;; ++j) {
-          const int p = p_lo + warp + kCdWarps * j;
-          if (p >= p_hi) break;
-          float2 kk, vv;
-          if (p == pos) {
-            kk = make_float2(qk[rep * 64 + 2 * lane], qk[rep * 64 + 2 * lane + 1]);
-            vv = make_float2(qk[(rep + 1) * 64 + 2 * lane], qk[(rep + 1) * 64 + 2 * lane + 1]);
-          } else if (j < kCdKvPre) {
-            kk = kpre[0];
-            vv = vpre[0];
+          if (tid < 64) {
+            const float v = qk[rep * 64 + d];
+            a.kc[(kv_base + pos) * 64 + d] = v;
+            if (fast) kst[(pos - p_lo) * 64 + d] = v;
           } else {
-            kk = ldcg_f2(a.kc + (kv_base + p) * 64 + 2 * lane);
-            vv = ldcg_f2(a.vc + (kv_base + p) * 64 + 2 * lane);
-          }
-#pragma unroll
-          for (int q = 0; q + 1 < kCdKvPre; ++q) {  // kpre[0] always belongs to the next position
-            kpre[q] = kpre[q + 1];
-            vpre[q] = vpre[q + 1];
-          }
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            if (h >= rep) break;
-            const float sdot = warp_sum(fmaf(qr[h][1], kk.y, qr[h][0] * kk.x)) * 0.125f;  // 1/sqrt(64)
-            const float nm = fmaxf(m[h], sdot);
-            const float corr = m[h] == -INFINITY ? 0.f : expf(m[h] - nm);
-            const float e = expf(sdot - nm);
-            lsum[h] = fmaf(lsum[h], corr, e);
-            o[h][0] = fmaf(e, vv.x, o[h][0] * corr);
-            o[h][1] = fmaf(e, vv.y, o[h][1] * corr);
-            m[h] = nm;
+            const float v = qk[(rep + 1) * 64 + d];
+            a.vc[(kv_base + pos) * 64 + d] = v;
+            if (fast) vst[(pos - p_lo) * 64 + d] = v;
           }
         }
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          if (h >= rep) break;
-          float* wp = wpart + (warp * rep + h) * kCdPartWords;
-          if (lane == 0) {
-            wp[0] = m[h];
-            wp[1] = lsum[h];
-          }
-          wp[4 + 2 * lane] = o[h][0];
-          wp[5 + 2 * lane] = o[h][1];
+        if (nst > 0) {
+          if (!mbar_wait_bounded(reinterpret_cast<uint64_t*>(smem + Ls.bars) + 6, kvph & 1, limit)) atomicCAS(a.err, 0, 1);
+          ++kvph;
+          kv_pending = false;
         }
         __syncthreads();
-        // per head: max over the warps, then each warp's weight exp(m_w - M); the CTA's partial is
-        // (M, sum of weighted sums, 64 weighted outputs)
-        if (tid < rep * 32) {
-          const int h = tid >> 5, w = tid & 31;
-          const float* wp = wpart + (w * rep + h) * kCdPartWords;
-          const bool live = w < kCdWarps && wp[1] > 0.f;
-          const float M = warp_max(live ? wp[0] : -INFINITY);
-          const float wt = live ? expf(wp[0] - M) : 0.f;
-          if (w < kCdWarps) mw[h * kCdWarps + w] = wt;
-          const float Ls2 = warp_sum(live ? wp[1] * wt : 0.f);
-          if (w == 0) {
-            outv[h * kCdPartWords] = M;
-            outv[h * kCdPartWords + 1] = Ls2;
-            outv[h * kCdPartWords + 2] = 0.f;
-            outv[h * kCdPartWords + 3] = 0.f;
+        if (fast) {
+          // warp h scores head h: lane j takes position p_lo + j (q . k over the 64 dims, read in a rotated
+          // order so that the lanes' rows fall in different banks); then the softmax weights scale the v
+          // rows, each lane owning two of the 64 outputs
+          if (warp < rep) {
+            const float* qh = qk + warp * 64;
+            float s = -INFINITY;
+            if (lane < npos) {
+              float acc[4] = {0.f, 0.f, 0.f, 0.f};
+              const float* kr = kst + lane * 64;
+#pragma unroll 4
+              for (int d4 = 0; d4 < 16; ++d4) {
+                const int d = ((d4 + lane) & 15) * 4;
+                const float4 k4 = *reinterpret_cast<const float4*>(kr + d);
+                const float4 q4 = *reinterpret_cast<const float4*>(qh + d);
+                acc[d4 & 3] = fmaf(q4.w, k4.w, fmaf(q4.z, k4.z, fmaf(q4.y, k4.y, fmaf(q4.x, k4.x, acc[d4 & 3]))));
+              }
+              s = ((acc[0] + acc[1]) + (acc[2] + acc[3])) * 0.125f;  // 1/sqrt(64)
+            }
+            const float mx = warp_max(s);
+            const float e = lane < npos ? expf(s - mx) : 0.f;
+            const float lsum = warp_sum(e);
+            float o0 = 0.f, o1 = 0.f;
+#pragma unroll 4
+            for (int jj = 0; jj < npos; ++jj) {
+              const float w = __shfl_sync(0xffffffffu, e, jj);
+              const float2 v2 = *reinterpret_cast<const float2*>(vst + jj * 64 + 2 * lane);
+              o0 = fmaf(w, v2.x, o0);
+              o1 = fmaf(w, v2.y, o1);
+            }
+            float* op = outv + warp * kCdPartWords;
+            if (lane == 0) {
+              op[0] = mx;
+              op[1] = lsum;
+              op[2] = op[3] = 0.f;
+            }
+            op[4 + 2 * lane] = o0;
+            op[5 + 2 * lane] = o1;
+          }
+        } else {
+        // Warp w takes head h = w % rep and every nwh-th chunk of 32 positions from chunk w / rep; lane j
+        // of a chunk scores position p_lo + chunk start + j (q . k over the 64 dims, read in a rotated
+        // order so that the lanes' rows fall in different banks), then the chunk's softmax weights scale
+        // the v rows, each lane owning two of the 64 outputs (online softmax across chunks).
+        const int nwh = kCdWarps / rep, h = warp % rep, sub = warp / rep;
+        float m = -INFINITY, lsum = 0.f, o0 = 0.f, o1 = 0.f;
+        if (sub < nwh) {
+          const float* qh = qk + h * 64;
+          for (int c0 = 32 * sub; c0 < npos; c0 += 32 * nwh) {
+            const int j = c0 + lane, p = p_lo + j;
+            float s = -INFINITY;
+            if (j < npos) {
+              float acc[4] = {0.f, 0.f, 0.f, 0.f};
+              if (p == pos || j < nst) {
+                const float* kr = p == pos ? qk + rep * 64 : kst + j * 64;
+#pragma unroll 4
+                for (int d4 = 0; d4 < 16; ++d4) {
+                  const int d = ((d4 + lane) & 15) * 4;
+                  const float4 k4 = *reinterpret_cast<const float4*>(kr + d);
+                  const float4 q4 = *reinterpret_cast<const float4*>(qh + d);
+                  acc[d4 & 3] = fmaf(q4.w, k4.w, fmaf(q4.z, k4.z, fmaf(q4.y, k4.y, fmaf(q4.x, k4.x, acc[d4 & 3]))));
+                }
+              } else {
+                const float* kr = a.kc + (kv_base + p) * 64;
+#pragma unroll 4
+                for (int d4 = 0; d4 < 16; ++d4) {
+                  const float4 k4 = ldcg_f4(kr + 4 * d4);
+                  const float4 q4 = *reinterpret_cast<const float4*>(qh + 4 * d4);
+                  acc[d4 & 3] = fmaf(q4.w, k4.w, fmaf(q4.z, k4.z, fmaf(q4.y, k4.y, fmaf(q4.x, k4.x, acc[d4 & 3]))));
+                }
+              }
+              s = ((acc[0] + acc[1]) + (acc[2] + acc[3])) * 0.125f;  // 1/sqrt(64)
+            }
+            const float nm = fmaxf(m, warp_max(s));
+            const float corr = m == -INFINITY ? 0.f : expf(m - nm);
+            const float e = j < npos ? expf(s - nm) : 0.f;
+            lsum = fmaf(lsum, corr, warp_sum(e));
+            o0 *= corr;
+            o1 *= corr;
+            const int cnt = min(32, npos - c0);
+            for (int jj = 0; jj < cnt; ++jj) {
+              const float w = __shfl_sync(0xffffffffu, e, jj);
+              const int q = c0 + jj, pq = p_lo + q;
+              float2 v2;
+              if (pq == pos) v2 = *reinterpret_cast<const float2*>(qk + (rep + 1) * 64 + 2 * lane);
+              else if (q < nst) v2 = *reinterpret_cast<const float2*>(vst + q * 64 + 2 * lane);
+              else v2 = ldcg_f2(a.vc + (kv_base + pq) * 64 + 2 * lane);
+              o0 = fmaf(w, v2.x, o0);
+              o1 = fmaf(w, v2.y, o1);
+            }
+            m = nm;
           }
         }
-        __syncthreads();
-        if (tid < rep * 64) {  // warp w walked positions only if p_lo + w < p_hi
-          const int h = tid >> 6, d = tid & 63, nw = max(0, min(kCdWarps, p_hi - p_lo));
-          float O = 0.f;
-          for (int w = 0; w < nw; ++w) O = fmaf(wpart[(w * rep + h) * kCdPartWords + 4 + d], mw[h * kCdWarps + w], O);
-          outv[h * kCdPartWords + 4 + d] = O;
+        // the CTA's partial per head (max, sum, 64 weighted outputs), combined over the head's warps
+        {
+          const int nsub = min(nwh, (npos + 31) / 32);
+          if (sub < nwh) {
+            float* wp = wpart + (sub * rep + h) * kCdPartWords;
+            if (lane == 0) {
+              wp[0] = m;
+              wp[1] = lsum;
+            }
+            wp[4 + 2 * lane] = o0;
+            wp[5 + 2 * lane] = o1;
+          }
+          __syncthreads();
+          if (tid < rep * 32) {
+            const int hh = tid >> 5, w = tid & 31;
+            const float* wp = wpart + (w * rep + hh) * kCdPartWords;
+            const bool live = w < nsub && wp[1] > 0.f;
+            const float M = warp_max(live ? wp[0] : -INFINITY);
+            const float wt = live ? expf(wp[0] - M) : 0.f;
+            if (w < kCdWarps) mw[hh * kCdWarps + w] = wt;
+            const float Ls2 = warp_sum(live ? wp[1] * wt : 0.f);
+            if (w == 0) {
+              outv[hh * kCdPartWords] = M;
+              outv[hh * kCdPartWords + 1] = Ls2;
+              outv[hh * kCdPartWords + 2] = 0.f;
+              outv[hh * kCdPartWords + 3] = 0.f;
+            }
+          }
+          __syncthreads();
+          if (tid < rep * 64) {
+            const int hh = tid >> 6, d = tid & 63;
+            float O = 0.f;
+            for (int w = 0; w < nsub; ++w) O = fmaf(wpart[(w * rep + hh) * kCdPartWords + 4 + d], mw[hh * kCdWarps + w], O);
+            outv[hh * kCdPartWords + 4 + d] = O;
+          }
+        }
         }
         __syncthreads();
+        // the staged rows are read: the next layer's rows go in now, from a thread of the last warp
+        if (l + 1 < md.n_layers) stage_kv(l + 1, p_lo, nst, tid == kCdThreads - 1);
         const int n4 = rep * kCdPartWords / 4;
         const uint32_t dst = smem_u32(attb + c * rep * kCdPartWords);
         for (int i = tid; i < kCdCtas * n4; i += kCdThreads) {
@@ -779,7 +899,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       }
       __syncthreads();
       // ---- proj columns of the group -> partial rows -> x1 (engine/infer.js:497-504)
-      if (!__syncthreads_and(run_units(F, gp, (l * rl + off_p) & (kCdWarps - 1), actp, red, warp, lane, a.err, limit))) {
+      if (!__syncthreads_and(units(CD_PROJ, l * rl + off_p))) {
         ok = false;
         goto done;
       }
@@ -800,7 +920,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         if (k < D) actp[k] = pre_scale(xb1[k] * g2[j], k);
       }
       __syncthreads();
-      if (!__syncthreads_and(run_units(F, gw13, (l * rl + off_13) & (kCdWarps - 1), actp, red, warp, lane, a.err, limit))) {
+      if (!__syncthreads_and(units(CD_W13, l * rl + off_13))) {
         ok = false;
         goto done;
       }
@@ -813,7 +933,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       }
       __syncthreads();
       // ---- w2 columns of the slice -> partial of all D rows -> reduce over the cluster -> x2
-      if (!__syncthreads_and(run_units(F, gw2, (l * rl + off_2) & (kCdWarps - 1), actp, red, warp, lane, a.err, limit))) {
+      if (!__syncthreads_and(units(CD_W2, l * rl + off_2))) {
         ok = false;
         goto done;
       }
@@ -851,7 +971,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       }
       load_gains(0, n1, n2);  // the next token's first layer
       __syncthreads();
-      if (!__syncthreads_and(run_units(F, glm, off_lm, actp, red, warp, lane, a.err, limit))) {
+      if (!__syncthreads_and(units(CD_LM, off_lm))) {
         ok = false;
         goto done;
       }
@@ -917,8 +1037,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
           uint64_t w0 = 0, w1 = 0;
           const uint64_t t0 = globaltimer();
           for (int n = 0;; ++n) {
-            w0 = ll_load(gcand + 2 * g);
-            w1 = ll_load(gcand + 2 * g + 1);
+            ll_load2(gcand + 2 * g, w0, w1);
             if ((uint32_t)(w0 >> 32) == tagb(B_CAND) && (uint32_t)(w1 >> 32) == tagb(B_CAND)) break;
             if ((n & 15) == 15 && (*(volatile int*)a.err || globaltimer() - t0 > limit)) {
               atomicCAS(a.err, 0, 1);
@@ -962,6 +1081,7 @@ done:
   __syncthreads();
   if (tid == 0) {
     // the bulk copies still in flight land before the CTA leaves (bounded)
+    if (kv_pending) (void)mbar_wait_bounded(reinterpret_cast<uint64_t*>(smem + Ls.bars) + 6, kvph & 1, limit);
     const int* last = reinterpret_cast<const int*>(smem + Ls.feed) + kCdMaxSlots;
     for (int sl = 0; sl < Ls.nslot; ++sl)
       if (last[sl] >= 0) {

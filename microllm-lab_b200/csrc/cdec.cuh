@@ -22,7 +22,7 @@ constexpr int kCdRecBytes = 320;            // one weight record: 16 rows x 32-w
 constexpr int kCdRpc = 8;                   // records per warp in one chunk of a CTA's weight stream
 constexpr int kCdChunk = kCdWarps * kCdRpc * kCdRecBytes;  // 40,960 bytes: one bulk copy
 constexpr int kCdMaxSlots = 4;              // chunks in flight per CTA (ring slots)
-constexpr int kCdKvPre = 4;                 // K/V positions per warp held in registers ahead of attention
+constexpr int kCdKvStage = 32;              // cache rows (K and V each) of a CTA's positions staged in shared memory
 constexpr int kCdPartWords = 68;            // attention partial of one head: max, sum, 2 pad, 64 outputs
 constexpr int kCdShapeError = 3;            // error flag value: the launch's cluster shape is not the packed one
 
@@ -121,8 +121,8 @@ __host__ __device__ inline int cd_stage_off(const ModelDev& m, int cid, int c, i
 
 // Shared-memory plan of the kernel (byte offsets; every region 16-byte aligned).
 struct CdSmem {
-  int ring, actp, red, xb2, xb1, pp1, pp2, rs, qkv, attb, cand, outv, wpart, qk, mw, norms, misc, bars, feed, geo,
-      total;
+  int ring, actp, red, xb2, xb1, pp1, pp2, rs, qkv, attb, cand, outv, wpart, qk, mw, kvst, norms, misc, bars, feed,
+      geo, total;
   int red_floats, nslot;
 };
 
@@ -161,11 +161,12 @@ __host__ __device__ inline CdSmem cd_smem(const ModelDev& m, int cap, int nc) {
   s.wpart = take(kCdWarps * rep * kCdPartWords * 4);
   s.qk = take((rep + 2) * 64 * 4);
   s.mw = take((rep + 4) * kCdCtas * 4);   // merge weights [head][split], attention warp weights [head][warp]
+  s.kvst = take(2 * kCdKvStage * 64 * 4); // staged K rows, then V rows
   s.norms = take((2 * m.n_layers + 1) * 8);
   s.misc = take(64 * 4);
-  s.bars = take(16 * 8);                  // exchange barriers, then one full barrier per ring slot
+  s.bars = take(16 * 8);                  // exchange barriers, the K/V staging barrier (6), one per ring slot (8 + s)
   s.feed = take(4 * kCdMaxSlots * 4);     // per slot: release count, last chunk issued
-  s.geo = take(256);                      // per stage: CdGeom and rotation offset
+  s.geo = take(2048);                     // per stage: CdGeom, rotation offset, warp unit ranges
   o = (o + 127) & ~127;
   s.nslot = (cap - o) / kCdChunk;
   if (s.nslot > kCdMaxSlots) s.nslot = kCdMaxSlots;
