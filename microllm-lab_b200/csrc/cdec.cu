@@ -262,12 +262,40 @@ struct CdRange {
   int u0, u1, tl0, slot0;
 };
 
-__device__ __forceinline__ bool run_units(Feed& F, const CdRange R, int G, int maxc, const float* actp, float* red,
-                                          int warp, int lane, int* err, uint64_t limit) {
+__device__ __forceinline__ bool run_units(Feed& F, const CdRange R, int G, int maxc, int t0, int kh, const float* actp,
+                                          float* red, int warp, int lane, int* err, uint64_t limit) {
   const int gid = lane >> 2, t = lane & 3;
+  if (G == 1) {
+    // one group per tile: every record is its own tile, and the four lanes of a row store their
+    // partials in slots t (summed by reduce_tiles), so no shuffle separates one record from the next
+    const float4 a0 = reinterpret_cast<const float4*>(actp + 8 * t)[0];
+    const float4 a1 = reinterpret_cast<const float4*>(actp + 8 * t)[1];
+    int u = R.u0;
+    while (u < R.u1) {
+      if (F.ri == 0 && !feed_wait(F, err, limit)) return false;
+      const int n = min(R.u1 - u, kCdRpc - (int)F.ri);
+      const uint8_t* cur = F.cur;
+      float* r = red + (u * 4 + t) * 16 + gid;
+#pragma unroll 4
+      for (int j = 0; j < n; ++j) {
+        const uint2 wv = *reinterpret_cast<const uint2*>(cur + 8 * lane);
+        const float2 sc = *reinterpret_cast<const float2*>(cur + 256 + 8 * gid);
+        r[0] = dot8(wv.x, a0, a1) * sc.x;
+        r[8] = dot8(wv.y, a0, a1) * sc.y;
+        cur += kCdRecBytes;
+        r += 64;
+      }
+      F.cur = cur;
+      F.ri += n;
+      u += n;
+      if (F.ri == kCdRpc) feed_next_chunk(F, warp, lane);
+    }
+    return true;
+  }
   int u = R.u0, tl = R.tl0, slot = R.slot0;
   int k = u - tl * G;  // group of the current unit within its tile
-  const float* ap = actp + 32 * k + 8 * t;
+  // K halves: odd tiles start G groups into the activation
+  const float* ap = actp + 32 * (k + (kh ? ((t0 + tl) & 1) * G : 0)) + 8 * t;
   float acc0 = 0.f, acc1 = 0.f;
   // the tile's partial into its slot; the warp that ends a tile zeroes the slots after its own
   auto flush = [&](bool ends_tile) {
@@ -311,7 +339,7 @@ __device__ __forceinline__ bool run_units(Feed& F, const CdRange R, int G, int m
       k = 0;
       slot = 0;
       acc0 = acc1 = 0.f;
-      ap = actp + 8 * t;
+      ap = actp + 32 * (kh ? ((t0 + tl) & 1) * G : 0) + 8 * t;
     }
   }
   if (k > 0) flush(false);
@@ -322,7 +350,7 @@ __device__ __forceinline__ bool run_units(Feed& F, const CdRange R, int G, int m
 // lanes per row (the same order on every call).  Called by the whole CTA after run_units; ends with a
 // CTA barrier when there was anything to add.
 __device__ __forceinline__ void reduce_tiles(float* red, const CdGeom g) {
-  if (g.maxc <= 1) return;
+  if (g.maxc <= 1 || g.G == 1) return;  // one-group tiles: row_val adds the four lane partials
   int lp = 1;
   while ((1 << lp) < g.maxc) ++lp;
   const int P = 1 << lp, total = g.Tu * 16 * P;
@@ -338,9 +366,12 @@ __device__ __forceinline__ void reduce_tiles(float* red, const CdGeom g) {
   __syncthreads();
 }
 
-// Row i (0 .. 16 Tu) of the CTA's unit tiles after reduce_tiles.
+// Row i (0 .. 16 Tu) of the CTA's unit tiles after reduce_tiles (one-group tiles: the sum of the four
+// lane partials, as a fixed tree).
 __device__ __forceinline__ float row_val(const float* red, const CdGeom& g, int i) {
-  return red[((i >> 4) * g.maxc) * 16 + (i & 15)];
+  const float* r = red + ((i >> 4) * g.maxc) * 16 + (i & 15);
+  if (g.G == 1) return (r[0] + r[16]) + (r[32] + r[48]);
+  return r[0];
 }
 
 // Pre-scaled stage activation for element k: x * 16^-e(k % 8) (exact).
@@ -366,13 +397,34 @@ __device__ __forceinline__ bool xwait(uint32_t bar, uint32_t parity, int* err, u
   return __syncthreads_and(ok);
 }
 
-// 1 / RMS (eps 1e-6, engine/infer.js:134-143) of a residual buffer whose D / 4 quad partial sums of
-// squares follow its D values; every warp forms the same sum in the same order.
-__device__ __forceinline__ float inv_rms(const float* xb, int D) {
+// Residual sum of this thread's elements k = tid, tid + 512 (D <= 1024): out[k] = x[k] + sum_g
+// part[g D + k] (cluster order; part null: out[k] as it stands), the next stage's activation
+// act[k] = pre-scaled out[k] * gain, and the warp's sum of squares into ssw[warp].  1 / RMS then
+// follows from ssw after a CTA barrier (inv_rms_of).
+__device__ __forceinline__ void residual_act(float* out, const float* x, const float* part, int D, int nc,
+                                             const float (&gain)[2], float* act, float* ssw) {
+  float s2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int k = (int)threadIdx.x + kCdThreads * j;
+    if (k < D) {
+      float v = part ? x[k] : out[k];
+      if (part)
+        for (int g = 0; g < nc; ++g) v += part[(size_t)g * D + k];
+      out[k] = v;
+      act[k] = pre_scale(v * gain[j], k);
+      s2 = fmaf(v, v, s2);
+    }
+  }
+  s2 = warp_sum(s2);
+  if ((threadIdx.x & 31) == 0) ssw[threadIdx.x >> 5] = s2;
+}
+
+// 1 / RMS (eps 1e-6, engine/infer.js:134-143) from the 16 warp sums of squares; every warp forms the
+// same sum in the same order.
+__device__ __forceinline__ float inv_rms_of(const float* ssw, int D) {
   const int lane = threadIdx.x & 31;
-  float s = 0.f;
-  for (int q = lane; q < D / 4; q += 32) s += xb[D + q];
-  s = warp_sum(s);
+  const float s = warp_sum(lane < kCdWarps ? ssw[lane] : 0.f);
   return 1.f / sqrtf(s / D + 1e-6f);
 }
 
@@ -421,23 +473,6 @@ __device__ __forceinline__ bool publish(const float* vals, int n, int r0, int D,
       st_async4(mapa(part + 4 * (g * D + 4 * q), d), make_float4(v[0], v[1], v[2], v[3]), mapa(bar, d));
   }
   return ok;
-}
-
-// Residual sum out = x + sum_g part[g] (cluster order) over all D values, with the D / 4 quad sums of
-// squares after them.
-__device__ __forceinline__ void residual_sum(float* out, const float* x, const float* part, int D, int nc) {
-  for (int q = threadIdx.x; q < D / 4; q += kCdThreads) {
-    float4 v = reinterpret_cast<const float4*>(x)[q];
-    for (int g = 0; g < nc; ++g) {
-      const float4 p = reinterpret_cast<const float4*>(part + (size_t)g * D)[q];
-      v.x += p.x;
-      v.y += p.y;
-      v.z += p.z;
-      v.w += p.w;
-    }
-    reinterpret_cast<float4*>(out)[q] = v;
-    out[D + q] = fmaf(v.w, v.w, fmaf(v.z, v.z, fmaf(v.y, v.y, v.x * v.x)));
-  }
 }
 
 }  // namespace cd
@@ -493,7 +528,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   const uint32_t kvbar = sbar + 8 * 6;
   uint32_t kvph = 0;       // phases of the K/V staging barrier completed
   bool kv_pending = false; // a staging copy is in flight
-  const uint32_t bar_bytes[B_COUNT] = {(uint32_t)(nc * D * 4), (uint32_t)((rep + 2) * 64 * 4),
+  const uint32_t bar_bytes[B_COUNT] = {(uint32_t)(nc * D * 4), (uint32_t)(2 * (rep + 2) * 64 * 4),
                                        (uint32_t)(kCdCtas * rep * kCdPartWords * 4), (uint32_t)(nc * D * 4),
                                        (uint32_t)(D * 4), (uint32_t)(nct * 16)};
   const uint64_t limit = a.wait_ns ? a.wait_ns : kWaitNs;
@@ -582,8 +617,8 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   };
   // this warp's share of stage st when the stage's rotation offset is off
   auto units = [&](int st, int off) {
-    return run_units(F, wr[st * kCdWarps + ((warp - off) & (kCdWarps - 1))], geo[st].G, geo[st].maxc, actp, red, warp,
-                     lane, a.err, limit);
+    return run_units(F, wr[st * kCdWarps + ((warp - off) & (kCdWarps - 1))], geo[st].G, geo[st].maxc, geo[st].t0,
+                     geo[st].kh, actp, red, warp, lane, a.err, limit);
   };
 
   const bool gen_mode = a.mode == MODE_GENERATE;
@@ -635,33 +670,30 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         rs_ = ldv_f32(md.rope_sin + (size_t)pos * md.rope_dim + d);
       }
     }
-    // ---- embed (engine/infer.js:360-420): the dequantised tied lm_head row, in every CTA
+    // ---- embed (engine/infer.js:360-420): the dequantised tied lm_head row, this thread's elements
     {
       const uint8_t* row = reinterpret_cast<const uint8_t*>(md.lm.w) + (size_t)tok * (D / 2);
       const float* sc = md.lm.s + (size_t)tok * (D / 32);
-      for (int q = tid; q < D / 4; q += kCdThreads) {
-        const uint16_t b2 = *reinterpret_cast<const uint16_t*>(row + 2 * q);
-        const float s0 = sc[q >> 3];
-        float v[4];
-        v[0] = (float)((int)(b2 & 15) - 8) * s0;
-        v[1] = (float)((int)((b2 >> 4) & 15) - 8) * s0;
-        v[2] = (float)((int)((b2 >> 8) & 15) - 8) * s0;
-        v[3] = (float)((int)((b2 >> 12) & 15) - 8) * s0;
-        *reinterpret_cast<float4*>(xb2 + 4 * q) = make_float4(v[0], v[1], v[2], v[3]);
-        xb2[D + q] = fmaf(v[3], v[3], fmaf(v[2], v[2], fmaf(v[1], v[1], v[0] * v[0])));
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int k = tid + kCdThreads * j;
+        if (k < D) {
+          const int b = row[k >> 1];  // element 2i in the low nibble of byte i, 2i + 1 in the high one
+          xb2[k] = (float)(((k & 1) ? (b >> 4) : (b & 15)) - 8) * sc[k >> 5];
+        }
       }
-      __syncthreads();
     }
     for (int l = 0; l < md.n_layers; ++l) {
-      if (l > 0) {  // x2 of the previous layer
-        if (!(ok = wait_bar(B_X2))) goto done;
-        residual_sum(xb2, xb1, pp2, D, nc);
-        __syncthreads();
-      }
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         g1[j] = n1[j];
         g2[j] = n2[j];
+      }
+      if (l > 0) {  // x2 of the previous layer
+        if (!(ok = wait_bar(B_X2))) goto done;
+        residual_act(xb2, xb1, pp2, D, nc, g1, actp, misc);
+      } else {
+        residual_act(xb2, nullptr, nullptr, D, nc, g1, actp, misc);
       }
       load_gains(l + 1 < md.n_layers ? l + 1 : l, n1, n2);
       if (l + 1 == md.n_layers) {  // the final norm's gain rides in n1
@@ -670,12 +702,6 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
           const int k = tid + kCdThreads * j;
           n1[j] = k < D ? ldv_f32(norms[2 * md.n_layers] + k) : 0.f;
         }
-      }
-      const float inv1 = inv_rms(xb2, D);
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int k = tid + kCdThreads * j;
-        if (k < D) actp[k] = pre_scale(xb2[k] * g1[j], k);
       }
       // this CTA's split of the positions [p_lo, p_hi); its first kCdKvStage cache rows are copied into
       // shared memory now, so that they have landed when attention starts
@@ -686,6 +712,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       const size_t kv_base = ((size_t)l * NKV + cid) * md.kv_len;
       if (l == 0) stage_kv(0, p_lo, nst, tid == 0);
       __syncthreads();
+      const float inv1 = inv_rms_of(misc, D);
       // ---- the group's q/k/v rows (engine/infer.js:431-440)
       if (!__syncthreads_and(units(CD_QKV, l * rl))) {
         ok = false;
@@ -696,8 +723,9 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       __syncthreads();
       for (int i = tid; i < gq.T * 16 * 4; i += kCdThreads) {  // quads x 16 CTAs
         const int q = i >> 4, d = i & 15;
-        st_async4(mapa(smem_u32(qkvb + 16 * gq.t0 + 4 * q), d), reinterpret_cast<const float4*>(outv)[q],
-                  mapa(sbar + 8 * B_QKV, d));
+        const int j = gq.t0 + (q >> 2);  // K half j % 2 of group-local tile j / 2
+        st_async4(mapa(smem_u32(qkvb + (j & 1) * (rep + 2) * 64 + 16 * (j >> 1) + 4 * (q & 3)), d),
+                  reinterpret_cast<const float4*>(outv)[q], mapa(sbar + 8 * B_QKV, d));
       }
       if (!(ok = wait_bar(B_QKV))) goto done;
       // ---- attention of the group over this CTA's positions (engine/infer.js:442-495)
@@ -706,11 +734,12 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         if (tid < (rep + 2) * 64) {
           const int vec = tid >> 6, d = tid & 63;
           const float* src = qkvb + vec * 64;
-          float v = src[d];
+          const float* src2 = src + (rep + 2) * 64;  // the second K half
+          float v = src[d] + src2[d];
           const int half = md.rope_dim / 2;
           if (vec <= rep && d < md.rope_dim) {
-            if (d < half) v = fmaf(-src[d + half], rs_, v * rc);
-            else v = fmaf(src[d - half], rs_, v * rc);
+            if (d < half) v = fmaf(-(src[d + half] + src2[d + half]), rs_, v * rc);
+            else v = fmaf(src[d - half] + src2[d - half], rs_, v * rc);
           }
           qk[tid] = v;
         }
@@ -910,16 +939,10 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       (void)publish(outv, gp.T * 16, 16 * gp.t0, D, cid, nc, smem_u32(pp1), sbar + 8 * B_X1, gxb(CD_GX_PP1, B_X1),
                     tagb(B_X1), c, a.err, limit);
       if (!(ok = wait_bar(B_X1))) goto done;
-      residual_sum(xb1, xb2, pp1, D, nc);
+      residual_act(xb1, xb2, pp1, D, nc, g2, actp, misc);
       __syncthreads();
       // ---- w1 / w3 rows of this CTA's FF slice, SiLU(u) * v (engine/infer.js:506-527)
-      const float inv2 = inv_rms(xb1, D);
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int k = tid + kCdThreads * j;
-        if (k < D) actp[k] = pre_scale(xb1[k] * g2[j], k);
-      }
-      __syncthreads();
+      const float inv2 = inv_rms_of(misc, D);
       if (!__syncthreads_and(units(CD_W13, l * rl + off_13))) {
         ok = false;
         goto done;
@@ -960,17 +983,11 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
     }
     // ---- final RMSNorm, lm_head rows of this CTA, argmax candidates (engine/infer.js:240-250)
     if (!(ok = wait_bar(B_X2))) goto done;
-    residual_sum(xb2, xb1, pp2, D, nc);
+    residual_act(xb2, xb1, pp2, D, nc, n1, actp, misc);
+    load_gains(0, n1, n2);  // the next token's first layer
     __syncthreads();
     {
-      const float invf = inv_rms(xb2, D);
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int k = tid + kCdThreads * j;
-        if (k < D) actp[k] = pre_scale(xb2[k] * n1[j], k);
-      }
-      load_gains(0, n1, n2);  // the next token's first layer
-      __syncthreads();
+      const float invf = inv_rms_of(misc, D);
       if (!__syncthreads_and(units(CD_LM, off_lm))) {
         ok = false;
         goto done;
@@ -1200,7 +1217,7 @@ void cd_pack(const ModelDev& m, const std::vector<HostQ4>& mats /* per layer: qk
         const int v = (w - cd_stage_off(m, cid, c, nc, l, st)) & (kCdWarps - 1);
         for (int u = cd_ustart(g, v); u < cd_ustart(g, v + 1); ++u) {
           const int tl = u / g.G, gg = g.k0 + u % g.G;
-          if (st == CD_QKV) put(*a, cd_qkv_row(m, cid, g.t0 + tl), gg);
+          if (st == CD_QKV) put(*a, cd_qkv_row(m, cid, (g.t0 + tl) >> 1), gg + ((g.t0 + tl) & 1) * g.G);
           else if (st == CD_W13) put((tl & 1) ? *b : *a, 16 * (g.t0 + tl / 2), gg);
           else put(*a, 16 * (g.t0 + tl), gg);
         }

@@ -34,9 +34,11 @@ constexpr int kCdShapeError = 3;            // error flag value: the launch's cl
 // with q = N / 16, rem = N % 16.  Warp w plays virtual warp (w - off) mod 16, where off rotates by each
 // stage's rem, so the extra units go round-robin and no warp's stream position drifts more than one
 // record from another's.  A tile spanned by several warps gets one partial per warp, summed in warp
-// order (maxc = the most per tile).
+// order (maxc = the most per tile); a stage of one group per tile instead keeps the partials of the
+// four lanes that share a row (maxc = 4).
 struct CdGeom {
   int t0, T, Tu, G, k0, N, q, rem, maxc;
+  int kh;  // 1: tile t0 + t covers groups [(t0 + t) % 2 G, + G) of the rows of tile (t0 + t) / 2 (K halves)
 };
 
 __host__ __device__ inline int cd_ustart(const CdGeom& g, int v) { return v * g.q + (v < g.rem ? v : g.rem); }
@@ -48,6 +50,7 @@ __host__ __device__ inline int cd_vwarp(const CdGeom& g, int u) {  // virtual wa
 __host__ __device__ inline CdGeom cd_geom(int t0, int T, int G, int k0, bool paired) {
   CdGeom g;
   g.t0 = t0;
+  g.kh = 0;
   g.T = T;
   g.Tu = paired ? 2 * T : T;
   g.G = G;
@@ -60,12 +63,14 @@ __host__ __device__ inline CdGeom cd_geom(int t0, int T, int G, int k0, bool pai
     const int n = cd_vwarp(g, t * g.G + g.G - 1) - cd_vwarp(g, t * g.G) + 1;
     g.maxc = g.maxc > n ? g.maxc : n;
   }
+  if (g.G == 1) g.maxc = 4;  // one-group tiles keep the four lane-quad partials of each row (see run_units)
   return g;
 }
 
 // Stage kinds in stream order within a layer, then the lm_head.
 //   CD_QKV:  cluster g (kv head g) computes the rows of its group: q heads g rep .. g rep + rep - 1, then
-//            k head g, then v head g ((rep + 2) x 64 rows, group-local tiles split over its 16 CTAs).
+//            k head g, then v head g ((rep + 2) x 64 rows); each group-local tile is cut into its two K
+//            halves and the 2 (rep + 2) 4 halves are split over the 16 CTAs (two partial vectors).
 //   CD_PROJ: cluster g multiplies its heads' attention output (columns g rep 64 .. + rep 64 of proj)
 //            into a partial of all D rows; the D / 16 row tiles are split over its 16 CTAs.
 //   CD_W13:  the FF rows, in slices of 32, split over all 16 nc CTAs (w1 and w3 tiles paired).
@@ -78,10 +83,12 @@ __host__ __device__ inline CdGeom cd_stage_geom(const ModelDev& m, int st, int c
   const int rep = m.NH / m.NKV, nct = nc * kCdCtas, gc = cid * kCdCtas + c;
   const int NS = m.FF / 32, s0 = gc * NS / nct, s1 = (gc + 1) * NS / nct;
   switch (st) {
-    case CD_QKV: {
-      const int NT = (rep + 2) * 4;
+    case CD_QKV: {  // K halves of the group's (rep + 2) 4 tiles, so that 16 CTAs share them evenly
+      const int NT = 2 * (rep + 2) * 4;
       const int t0 = c * NT / kCdCtas;
-      return cd_geom(t0, (c + 1) * NT / kCdCtas - t0, m.D / 32, 0, false);
+      CdGeom g = cd_geom(t0, (c + 1) * NT / kCdCtas - t0, m.D / 64, 0, false);
+      g.kh = 1;
+      return g;
     }
     case CD_PROJ: {
       const int NT = m.D / 16;
@@ -154,7 +161,7 @@ __host__ __device__ inline CdSmem cd_smem(const ModelDev& m, int cap, int nc) {
   s.pp1 = take(nc * m.D * 4);             // proj partials of every cluster
   s.pp2 = take(nc * m.D * 4);             // w2 partials of every cluster
   s.rs = take(m.D * 4);                   // w2 partials of this CTA's D / 16 rows from the 16 CTAs
-  s.qkv = take((rep + 2) * 64 * 4);
+  s.qkv = take(2 * (rep + 2) * 64 * 4);  // the two K-half partials of the group's q/k/v
   s.attb = take(kCdCtas * rep * kCdPartWords * 4);
   s.cand = take(nc * kCdCtas * 16);
   s.outv = take(outf * 4);                // a stage's output rows before the push, or the attention partial
