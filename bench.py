@@ -37,12 +37,19 @@ sys.path.insert(0, ROOT)
 CACHE = os.environ.get("MLLM_PGW_CACHE", "/tmp/mllm_pgw_cache")
 L2_BYTES = 126 * 1024 * 1024
 
-# dram__bytes_read.sum + dram__bytes_write.sum summed over every kernel of one generate call of the
-# config-1 workload (token-batch prefill + the decode1_kernel launch), from one ncu capture of
-# `microllm-lab_b200/profile_case.py decode --new 128` (decode1_kernel: 417,123,840 B; prefill
-# kernels: 132,081,664 B).
-# ncu flushes the caches before each captured kernel, as the bench flushes L2 before each call.
-DECODE_TRAFFIC_PER_CALL = {"config1 petitgpt b1 p64 n128": 549_205_504}
+# dram__bytes_read.sum + dram__bytes_write.sum of ONE decode1_kernel launch of the config-1 workload
+# (127 decode forwards), from two single-kernel ncu captures of the same call with fewer ids:
+# `bench.py --case decode --new 24` (23 forwards) 102,231,552 B and `--new 48` (47 forwards)
+# 121,998,592 B.  The first forward reads the weights from DRAM (ncu flushes the caches before the
+# kernel, as the bench flushes L2 before each call); every later one adds (121,998,592 - 102,231,552)
+# / 24 = 823,627 B.  127 forwards: 102,231,552 + 104 x 823,627 = 187,888,760 B.
+DECODE_TRAFFIC_PER_LAUNCH = {("config1 petitgpt b1 p64 n128", "decode1"): 187_888_760}
+# sm__pipe_tensor_cycles_active (% of peak, active cycles) of the decode-step GEMMs of config 5, one
+# single-kernel ncu --set full capture each on `bench.py --case batched --seqs 128 --prompt 8 --new 3`
+# (the first decode step's launch; mma.sync.m16n8k16 tiles): the share of the tensor pipe they keep busy.
+BATCHED_TENSOR_PIPE = {"source": "ncu single-kernel captures, 128-row decode step", "unit": "% of peak",
+                       "lwe_gemm_qkv<2,4>": 11.9, "lwe_gemm_w13<2,1>": 20.9, "lwe_gemm_resid<2,4>": 5.0,
+                       "lwe_gemm_lm_wide<8,3>": 43.0, "lwe_attention<3,1>": 0.0}
 # dram__bytes_read.sum + dram__bytes_write.sum of one cold gemv_q4_bulk_kernel launch on the lm_head
 # shape (49152 x 576, M = 1), from an ncu capture of `microllm-lab_b200/profile_case.py gemv`: exactly the
 # 17,694,720 bytes of nibbles and scales plus the activations.
@@ -276,6 +283,7 @@ def run_batched_leg(torch, P, local: int, rank: int, ws: int, dist, steps: int, 
                      "peak_kind": peak_kind, "traffic": None, "kernel": "whole call: token-batch GEMMs (lwe_gemm_resid, _w13, _qkv, "
                      "_lm_wide: about 65 % of a decode step) and attention over the fp32 KV cache (lwe_attention, "
                      "about 34 %)", "algorithmic_bytes_per_step": alg},
+        "tensor_pipe": BATCHED_TENSOR_PIPE,
         "clocks": clk.summary(),
     }
     if cpu and rank == 0 and ws == 1:
@@ -523,14 +531,10 @@ def run_gemv(args):
 
 
 DATA_TEXT = "synthetic (seeded N(0,0.02) Q4 weights, seeded prompt ids; real checkpoints are LFS stubs)"
-DECODE_KERNEL = {
-    "decode": "cdec_kernel (one 16-CTA cluster, whole generate call)",
-    "gpt2": "decode1_kernel (148 CTAs, whole generate call)",
-}
 
 
 def measure_generate(torch, P, key: str, local: int, rank: int, ws: int, dist, steps: int, warmup: int,
-                     cpu_threads: int) -> dict:
+                     cpu_threads: int, env: dict = None) -> dict:
     """One generate workload (configs 1, 3, 4) on this rank's GPU: `steps` timed generate calls after
     `warmup`, device path (prompt and ids resident in HBM) and e2e path (host buffers through
     mllm_generate), L2 flushed before each; max over ranks.  cpu_threads > 0 adds the oracle baseline on
@@ -543,7 +547,16 @@ def measure_generate(torch, P, key: str, local: int, rank: int, ws: int, dist, s
         prompt = P.copy_span_prompt(n_prompt, cfg["vocabSize"], replica_prompt_seed(seed, rank))
     else:
         prompt = P.seeded_prompt(n_prompt, cfg["vocabSize"], replica_prompt_seed(seed, rank))
-    eng = P.CudaPetitGPT(data, device=local)
+    old_env = {k: os.environ.get(k) for k in (env or {})}
+    os.environ.update(env or {})  # read by mllm_create only
+    try:
+        eng = P.CudaPetitGPT(data, device=local)
+    finally:
+        for k, v in old_env.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
     stream = torch.cuda.Stream()
     eng.set_stream(stream.cuda_stream)
     d_ids = torch.from_numpy(prompt).to(f"cuda:{local}")
@@ -571,7 +584,8 @@ def measure_generate(torch, P, key: str, local: int, rank: int, ws: int, dist, s
     def timed(fn, k):
         """k steps, each bracketed by events on the launch stream, L2 flushed before each step."""
         total = 0.0
-        dev_ms = []
+        dev_ms.clear()
+        first_ms.clear()
         for _ in range(k):
             with torch.cuda.stream(stream):
                 flush.fill_(1.0)
@@ -583,8 +597,10 @@ def measure_generate(torch, P, key: str, local: int, rank: int, ws: int, dist, s
             total += e0.elapsed_time(e1)
             if st is not None:
                 dev_ms.append(st.total_ms)
-        return total, dev_ms
+                first_ms.append(st.ttft_ms)
+        return total, list(dev_ms)
 
+    dev_ms, first_ms = [], []
     for _ in range(warmup):
         step_device()
         step_e2e()
@@ -606,9 +622,17 @@ def measure_generate(torch, P, key: str, local: int, rank: int, ws: int, dist, s
     ms_step = t_dev / steps
     hbm, _, peak_kind = peaks()
     alg = decode_algorithmic_bytes(cfg, n_prompt, n_new)
-    achieved = alg / (ms_step / 1e3) / 1e9
-    traffic = DECODE_TRAFFIC_PER_CALL.get(W["workload"])
     w_bytes = decode_weight_bytes(cfg)
+    kname = eng.decodeKernel
+    if spec_k:  # the whole call is the unit: graph-replayed speculation iterations
+        alg_launch, launch_ms = alg, ms_step
+        traffic = None
+    else:  # the persistent single-token launch: the decode forwards after the first id
+        prefill = w_bytes + n_prompt * 2 * cfg["nLayers"] * cfg["nKvHeads"] * 64 * 4
+        alg_launch = alg - prefill
+        launch_ms = float(np.mean([t - f for t, f in zip(dev_ms, first_ms)])) if dev_ms else ms_step
+        traffic = DECODE_TRAFFIC_PER_LAUNCH.get((W["workload"], kname.split(":")[0]))
+    achieved = alg_launch / (launch_ms / 1e3) / 1e9
     line = {
         "metric": W["metric"],
         "value": value, "unit": "tok/s", "n_gpus": ws, "steps": steps, "warmup": warmup,
@@ -623,19 +647,21 @@ def measure_generate(torch, P, key: str, local: int, rank: int, ws: int, dist, s
                            f"speculation iteration (k_spec_prepare, {spec_k + 1}-row verify forward, k_spec_accept)"
                            if spec_k else
                            f"prefill as token-batch tensor-core forwards, then the {n_new - 1} decode steps in one "
-                           f"persistent single-token kernel launch ({DECODE_KERNEL.get(key, 'cdec_kernel')})")},
+                           f"persistent single-token kernel launch ({kname})")},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": n_prompt * 4, "d2h_bytes_per_step": n_new * 4 + 68},
         "gpu_launches": gpu_launches,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": peak_kind, "traffic": traffic,
                      "limiter": ("latency: the weights stay L2-resident between tokens (DRAM traffic "
-                                 f"{traffic / alg:.1%} of the algorithmic bytes), so the per-layer chain of "
+                                 f"{traffic / alg_launch:.1%} of the algorithmic bytes), so the per-layer chain of "
                                  "stage exchanges sets the time" if traffic else
                                  "latency of the per-token chain of stages (see the profiles)"),
                      "kernel": ("whole generate call (token-batch prefill + graph-replayed speculation iterations)"
-                                if spec_k else DECODE_KERNEL.get(key, "cdec_kernel") ),
-                     "algorithmic_bytes_per_launch": alg,
-                     "kernel_ms_device_timer": float(np.mean(dev_ms)) if dev_ms else None},
+                                if spec_k else f"{kname}: the {n_new - 1} decode forwards after the first id"),
+                     "algorithmic_bytes_per_launch": alg_launch,
+                     "launch_ms_device_timer": launch_ms,
+                     "traffic_source": ("two single-kernel ncu captures (23 and 47 forwards) scaled to "
+                                        f"{n_new - 1} forwards" if traffic else None)},
         "clocks": clk.summary(),
     }
     if spec_k:
@@ -680,6 +706,9 @@ def run_decode(args):
     if args.workload == "decode" and not args.no_extra:
         threads = os.cpu_count() or 1
         ls, lw = args.leg_steps, 2
+        # config 1 on the cluster decode kernel (one 16-CTA cluster per kv head; opt-in in the engine)
+        line["decode_cluster"] = measure_generate(torch, P, "decode", local, rank, ws, dist, ls, lw, 0,
+                                                  env={"MLLM_CLUSTER_DECODE": "1"})
         line["gpt2"] = measure_generate(torch, P, "gpt2", local, rank, ws, dist, ls, lw, threads if cpu else 0)
         line["spec4"] = measure_generate(torch, P, "spec4", local, rank, ws, dist, ls, lw, 0)
         line["spec8"] = measure_generate(torch, P, "spec8", local, rank, ws, dist, ls, lw, 0)
@@ -703,14 +732,76 @@ def run_decode(args):
         dist.destroy_process_group()
 
 
+TIMELINE_STAGES = ["x2 wait + residual + act", "1/RMS", "q/k/v rows (units + epilogue)", "q/k/v push",
+                   "q/k/v wait", "RoPE + q/k", "K/V staging wait + cache row", "attention (scores, softmax, v)",
+                   "partial push", "partials wait", "merge -> proj activation", "proj columns (units + epilogue)",
+                   "x1 publish (global + forward)", "x1 wait", "x1 residual + act + 1/RMS",
+                   "w1/w3 rows (units)", "SiLU(u) v", "w2 columns (units + epilogue)", "reduce-scatter push",
+                   "reduce-scatter wait", "x2 publish (sum + global + forward)"]
+
+
+def run_timeline(args):
+    """Stage timeline of the cluster decode kernel (see run_case); the stamps are globaltimer values of
+    thread 0 of every CTA, each stage the difference of max-over-CTA stamps."""
+    import ctypes
+    P = pkg()
+    lib = os.path.join(ROOT, "microllm-lab_b200", "libmllm_cuda_timeline.so")
+    L = P.engine.load_library(lib)
+    if not os.path.samefile(L._name, lib):
+        raise RuntimeError("the timeline library must be the first libmllm loaded in the process")
+    os.environ["MLLM_CLUSTER_DECODE"] = "1"
+    W = WORKLOADS["decode"]
+    cfg = P.CONFIGS[W["model"]]
+    data = P.synthetic_pgw(W["model"], W["seed"], cache_dir=CACHE)
+    prompt = P.seeded_prompt(W["prompt"], cfg["vocabSize"], W["seed"])
+    eng = P.CudaPetitGPT(data)
+    if "cdec" not in eng.decodeKernel:
+        raise RuntimeError(f"cluster decode is not available for this model: {eng.decodeKernel}")
+    nc = int(eng.decodeKernel.split(":")[1].split()[0])
+    L.mllm_timeline_config.argtypes = [ctypes.c_int]
+    L.mllm_timeline_dump.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    if L.mllm_timeline_config(args.forward):
+        raise RuntimeError("mllm_timeline_config failed")
+    nnew = max(args.new or 24, args.forward + 2)
+    g = eng.generate(prompt, maxNewTokens=nnew, eosId=-1)
+    st = np.zeros((16 * nc, 1024), np.uint64)
+    if L.mllm_timeline_dump(st.ctypes.data, 16 * nc):
+        raise RuntimeError("mllm_timeline_dump failed")
+    eng.destroy()
+    mx = st.astype(np.int64).max(axis=0)
+    nl, per = cfg["nLayers"], 24
+    rows = []
+    for k in range(1, len(TIMELINE_STAGES) + 1):
+        d = [(mx[l * per + k] - mx[l * per + k - 1]) / 1e3 for l in range(nl)]
+        rows.append({"stage": TIMELINE_STAGES[k - 1], "us_mean": round(float(np.mean(d)), 3),
+                     "us_layer15": round(float(d[min(15, nl - 1)]), 3)})
+    layer_us = [(mx[(l + 1) * per] - mx[l * per]) / 1e3 for l in range(nl - 1)]
+    tail = {"x2 wait + final norm": (mx[1001] - mx[1000]) / 1e3, "lm_head rows": (mx[1002] - mx[1001]) / 1e3,
+            "stream end + argmax": (mx[1003] - mx[1002]) / 1e3, "candidate exchange": (mx[1004] - mx[1003]) / 1e3}
+    print(json.dumps({"case": "timeline", "kernel": f"cdec_kernel, {nc} clusters of 16 CTAs",
+                      "forward": args.forward, "position": W["prompt"] + args.forward,
+                      "layer_us_mean": round(float(np.mean(layer_us)), 3),
+                      "token_us": round((mx[1004] - mx[0]) / 1e3, 2), "stages": rows,
+                      "tail_us": {k: round(float(v), 3) for k, v in tail.items()},
+                      "deviceMs": g["deviceMs"], "new": nnew}, indent=1))
+
+
 def run_case(args):
     """One small, untimed run of a path, sized for a profiler capture (``--case``; prints one summary line).
 
     decode:  a BASELINE config-1 generate call (PetitGPT shape, seed 0, 64-token prompt) with --new ids;
-    batched: config 5 (SmolLM2-135M shape) with --seqs sequences of 128-token prompts and --new ids;
+    timeline: the same call on the cluster decode kernel from libmllm_cuda_timeline.so (built by
+             ``build.py --timeline``), printing the per-stage times of forward --forward: per layer and
+             stage the max over CTAs of the stage's closing stamp minus the previous one, averaged over
+             the layers, and the lm_head tail;
+    batched: config 5 (SmolLM2-135M shape) with --seqs sequences of --prompt-token prompts (default 128)
+             and --new ids;
     spec:    config 4 (SmolLM2-360M shape, 512-token copy-span prompt) with --new ids at k = --k;
     gemv:    one cold mllm_gemv_q4 on the lm_head shape (49152 x 576, M = 1)."""
     import torch
+    if args.case == "timeline":
+        run_timeline(args)
+        return
     P = pkg()
     if args.case == "gemv":
         rows, cols = 49152, 576
@@ -728,11 +819,11 @@ def run_case(args):
         B = BATCHED
         cfg = P.CONFIGS[B["model"]]
         data = P.synthetic_pgw(B["model"], B["seed"], cache_dir=CACHE)
-        nnew = args.new or 3
-        seqs = [P.seeded_prompt(B["plen"], cfg["vocabSize"], sd) for sd in batched_sequence_seeds(0, args.seqs)]
-        eng = P.CudaPetitGPT(data, max_slots=args.seqs, kv_len=B["plen"] + nnew)
+        nnew, plen = args.new or 3, args.prompt or B["plen"]
+        seqs = [P.seeded_prompt(plen, cfg["vocabSize"], sd) for sd in batched_sequence_seeds(0, args.seqs)]
+        eng = P.CudaPetitGPT(data, max_slots=args.seqs, kv_len=plen + nnew)
         _, stats = eng.generateBatch(seqs, maxNewTokens=nnew, eosId=-1)
-        print(json.dumps({"case": "batched", "seqs": args.seqs, "new": nnew, "stats": stats}))
+        print(json.dumps({"case": "batched", "seqs": args.seqs, "prompt": plen, "new": nnew, "stats": stats}))
         eng.destroy()
         return
     key = "spec4" if args.case == "spec" else "decode"
@@ -763,11 +854,13 @@ def main():
     ap.add_argument("--batched-steps", type=int, default=3)
     ap.add_argument("--leg-steps", type=int, default=3, help="timed steps of the config 3 and 4 sub-objects")
     ap.add_argument("--no-extra", action="store_true", help="only config 1 (and config 5 unless --no-batched)")
-    ap.add_argument("--case", choices=["decode", "batched", "spec", "gemv"],
+    ap.add_argument("--case", choices=["decode", "timeline", "batched", "spec", "gemv"],
                     help="one small untimed run for a profiler capture (see run_case)")
     ap.add_argument("--new", type=int, default=0, help="--case: ids to generate")
     ap.add_argument("--seqs", type=int, default=128, help="--case batched: sequences")
+    ap.add_argument("--prompt", type=int, default=0, help="--case batched: prompt tokens (0 = config 5's 128)")
     ap.add_argument("--k", type=int, default=4, help="--case spec: draft length")
+    ap.add_argument("--forward", type=int, default=20, help="--case timeline: the stamped forward of the launch")
     args = ap.parse_args()
     if args.case:
         run_case(args)

@@ -479,6 +479,25 @@ __device__ __forceinline__ bool publish(const float* vals, int n, int r0, int D,
 
 using namespace cd;
 
+// Stage timeline (build with -DMLLM_CDEC_TIMELINE, the separate libmllm_cuda_timeline.so): thread 0 of
+// every CTA stores the globaltimer at each stage boundary of one forward (mllm_timeline_config): layer
+// l, stage k at word l * kCdTlLayer + k; the token's tail (final norm, lm_head, candidates) at
+// kCdTlTail + k.  The stamps cost nothing in the normal build.
+#ifdef MLLM_CDEC_TIMELINE
+constexpr int kCdTlLayer = 24, kCdTlTail = 1000, kCdTlWords = 1024;
+__device__ unsigned long long g_cd_tl[kCdMaxClusters * kCdCtas][kCdTlWords];
+__device__ int g_cd_tl_forward = 3;
+#define CD_TL(idx)                                                                                   \
+  do {                                                                                               \
+    if (tid == 0 && f == g_cd_tl_forward && (idx) < kCdTlWords) g_cd_tl[gc][(idx)] = globaltimer(); \
+  } while (0)
+#else
+constexpr int kCdTlLayer = 0, kCdTlTail = 0;
+#define CD_TL(idx) \
+  do {             \
+  } while (0)
+#endif
+
 static_assert(5 * sizeof(CdGeom) + 6 * sizeof(int) + 5 * kCdWarps * sizeof(CdRange) <= 2048, "stage table region");
 
 __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_constant__ CdArgs A) {
@@ -689,11 +708,14 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         g1[j] = n1[j];
         g2[j] = n2[j];
       }
+      CD_TL(l * kCdTlLayer + 0);
       if (l > 0) {  // x2 of the previous layer
         if (!(ok = wait_bar(B_X2))) goto done;
         residual_act(xb2, xb1, pp2, D, nc, g1, actp, misc);
+        CD_TL(l * kCdTlLayer + 1);
       } else {
         residual_act(xb2, nullptr, nullptr, D, nc, g1, actp, misc);
+        CD_TL(l * kCdTlLayer + 1);
       }
       load_gains(l + 1 < md.n_layers ? l + 1 : l, n1, n2);
       if (l + 1 == md.n_layers) {  // the final norm's gain rides in n1
@@ -713,6 +735,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       if (l == 0) stage_kv(0, p_lo, nst, tid == 0);
       __syncthreads();
       const float inv1 = inv_rms_of(misc, D);
+      CD_TL(l * kCdTlLayer + 2);
       // ---- the group's q/k/v rows (engine/infer.js:431-440)
       if (!__syncthreads_and(units(CD_QKV, l * rl))) {
         ok = false;
@@ -720,6 +743,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       }
       reduce_tiles(red, gq);
       for (int i = tid; i < gq.T * 16; i += kCdThreads) outv[i] = inv1 * row_val(red, gq, i);
+      CD_TL(l * kCdTlLayer + 3);
       __syncthreads();
       for (int i = tid; i < gq.T * 16 * 4; i += kCdThreads) {  // quads x 16 CTAs
         const int q = i >> 4, d = i & 15;
@@ -727,7 +751,9 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         st_async4(mapa(smem_u32(qkvb + (j & 1) * (rep + 2) * 64 + 16 * (j >> 1) + 4 * (q & 3)), d),
                   reinterpret_cast<const float4*>(outv)[q], mapa(sbar + 8 * B_QKV, d));
       }
+      CD_TL(l * kCdTlLayer + 4);
       if (!(ok = wait_bar(B_QKV))) goto done;
+      CD_TL(l * kCdTlLayer + 5);
       // ---- attention of the group over this CTA's positions (engine/infer.js:442-495)
       {
         // RoPE'd q heads of the group, the new k (rotated) and v (engine/infer.js:185-225)
@@ -744,6 +770,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
           qk[tid] = v;
         }
         __syncthreads();
+        CD_TL(l * kCdTlLayer + 6);
         // every position of the CTA in the staged rows: the new row is copied in beside them
         const bool fast = npos <= kCdKvStage;
         if (pos >= p_lo && pos < p_hi && tid < 128) {  // the cache row (engine/infer.js:457-464)
@@ -764,6 +791,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
           kv_pending = false;
         }
         __syncthreads();
+        CD_TL(l * kCdTlLayer + 7);
         if (fast) {
           // warp h scores head h: lane j takes position p_lo + j (q . k over the 64 dims, read in a rotated
           // order so that the lanes' rows fall in different banks); then the softmax weights scale the v
@@ -895,6 +923,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
         }
         }
         __syncthreads();
+        CD_TL(l * kCdTlLayer + 8);
         // the staged rows are read: the next layer's rows go in now, from a thread of the last warp
         if (l + 1 < md.n_layers) stage_kv(l + 1, p_lo, nst, tid == kCdThreads - 1);
         const int n4 = rep * kCdPartWords / 4;
@@ -904,7 +933,9 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
           st_async4(mapa(dst + 16 * q, d), reinterpret_cast<const float4*>(outv)[q], mapa(sbar + 8 * B_ATT, d));
         }
       }
+      CD_TL(l * kCdTlLayer + 9);
       if (!(ok = wait_bar(B_ATT))) goto done;
+      CD_TL(l * kCdTlLayer + 10);
       // ---- merge the 16 splits of each head: weights exp(M_s - M) / L, then the group's attention
       // output straight into the proj activation
       // splits that hold positions: CTA s covers [s span, (s + 1) span)
@@ -928,25 +959,31 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       }
       __syncthreads();
       // ---- proj columns of the group -> partial rows -> x1 (engine/infer.js:497-504)
+      CD_TL(l * kCdTlLayer + 11);
       if (!__syncthreads_and(units(CD_PROJ, l * rl + off_p))) {
         ok = false;
         goto done;
       }
       reduce_tiles(red, gp);
       for (int i = tid; i < gp.T * 16; i += kCdThreads) outv[i] = row_val(red, gp, i);
+      CD_TL(l * kCdTlLayer + 12);
       __syncthreads();
       // a remote wait that gives up raises the error flag; the wait that follows then fails everywhere
       (void)publish(outv, gp.T * 16, 16 * gp.t0, D, cid, nc, smem_u32(pp1), sbar + 8 * B_X1, gxb(CD_GX_PP1, B_X1),
                     tagb(B_X1), c, a.err, limit);
+      CD_TL(l * kCdTlLayer + 13);
       if (!(ok = wait_bar(B_X1))) goto done;
+      CD_TL(l * kCdTlLayer + 14);
       residual_act(xb1, xb2, pp1, D, nc, g2, actp, misc);
       __syncthreads();
       // ---- w1 / w3 rows of this CTA's FF slice, SiLU(u) * v (engine/infer.js:506-527)
       const float inv2 = inv_rms_of(misc, D);
+      CD_TL(l * kCdTlLayer + 15);
       if (!__syncthreads_and(units(CD_W13, l * rl + off_13))) {
         ok = false;
         goto done;
       }
+      CD_TL(l * kCdTlLayer + 16);
       reduce_tiles(red, gw13);
       for (int i = tid; i < gw13.T * 16; i += kCdThreads) {
         const int tl = i >> 4, r = i & 15;
@@ -956,19 +993,23 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       }
       __syncthreads();
       // ---- w2 columns of the slice -> partial of all D rows -> reduce over the cluster -> x2
+      CD_TL(l * kCdTlLayer + 17);
       if (!__syncthreads_and(units(CD_W2, l * rl + off_2))) {
         ok = false;
         goto done;
       }
       reduce_tiles(red, gw2);
       for (int i = tid; i < D; i += kCdThreads) outv[i] = gw2.G > 0 ? row_val(red, gw2, i) : 0.f;
+      CD_TL(l * kCdTlLayer + 18);
       __syncthreads();
       for (int i = tid; i < D / 4; i += kCdThreads) {  // quad i goes to the CTA that reduces its rows
         const int d = (4 * i) / RO, k = 4 * i - d * RO;
         st_async4(mapa(smem_u32(rs + c * RO + k), d), reinterpret_cast<const float4*>(outv)[i],
                   mapa(sbar + 8 * B_RS, d));
       }
+      CD_TL(l * kCdTlLayer + 19);
       if (!(ok = wait_bar(B_RS))) goto done;
+      CD_TL(l * kCdTlLayer + 20);
       if (tid < 8 * RO) {  // row tid / 8: lane k adds the partials of CTAs k and k + 8, then a tree over the 8 lanes
         const int i = tid >> 3, k = tid & 7;
         float s = rs[k * RO + i] + rs[(k + 8) * RO + i];
@@ -980,18 +1021,22 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       __syncthreads();
       (void)publish(outv, RO, c * RO, D, cid, nc, smem_u32(pp2), sbar + 8 * B_X2, gxb(CD_GX_PP2, B_X2), tagb(B_X2), c,
                     a.err, limit);
+      CD_TL(l * kCdTlLayer + 21);
     }
     // ---- final RMSNorm, lm_head rows of this CTA, argmax candidates (engine/infer.js:240-250)
+    CD_TL(kCdTlTail + 0);
     if (!(ok = wait_bar(B_X2))) goto done;
     residual_act(xb2, xb1, pp2, D, nc, n1, actp, misc);
     load_gains(0, n1, n2);  // the next token's first layer
     __syncthreads();
     {
       const float invf = inv_rms_of(misc, D);
+      CD_TL(kCdTlTail + 1);
       if (!__syncthreads_and(units(CD_LM, off_lm))) {
         ok = false;
         goto done;
       }
+      CD_TL(kCdTlTail + 2);
       if (!__syncthreads_and(feed_token_end(F, warp, lane, a.err, limit))) {
         ok = false;
         goto done;
@@ -1069,7 +1114,9 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
                       mapa(sbar + 8 * B_CAND, d));
         }
       }
+      CD_TL(kCdTlTail + 3);
       if (!(ok = wait_bar(B_CAND))) goto done;
+      CD_TL(kCdTlTail + 4);
       float bv = -INFINITY;
       int bi = 0x7fffffff;
       for (int cc = 0; cc < nct; ++cc) {
@@ -1233,6 +1280,17 @@ void cd_pack(const ModelDev& m, const std::vector<HostQ4>& mats /* per layer: qk
     }
   }
 }
+
+#ifdef MLLM_CDEC_TIMELINE
+// Timeline build only: which forward of a launch is stamped, and the stamps of the first `ctas` CTAs.
+extern "C" int mllm_timeline_config(int forward) {
+  return (int)cudaMemcpyToSymbol(g_cd_tl_forward, &forward, sizeof(int));
+}
+extern "C" int mllm_timeline_dump(unsigned long long* host, int ctas) {
+  if (ctas < 1 || ctas > kCdMaxClusters * kCdCtas) return -1;
+  return (int)cudaMemcpyFromSymbol(host, g_cd_tl, (size_t)ctas * kCdTlWords * sizeof(unsigned long long));
+}
+#endif
 
 // Kernel attributes (once per process): the cluster of 16 is a non-portable size.
 cudaError_t cd_setup(size_t smem_cap) {

@@ -418,7 +418,7 @@ __global__ void __launch_bounds__(kAttnThreads) lwe_attention(const __grid_const
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float* qs = asm_;                  // [REP][64]
   float* sc = qs + REP * 64;         // [REP][kv_len]
-  float* red = sc + REP * kvs;       // [kAttnLanes][REP][64]
+  float* red = sc + ((REP * kvs + 3) & ~3);  // [kAttnLanes][REP][64], 16-byte aligned (float4 stores)
   __shared__ float inv_sum[REP];
   __shared__ float ks[64];
   const float* qrow = a.qkv + (size_t)t * md.QKV + g * REP * 64;
@@ -724,7 +724,7 @@ void lwe_attn_split_shape(int kv_len, int* chunk, int* splits) {
 }
 
 static size_t attention_smem(int rep, int kv_len) {
-  return (size_t)(rep * 64 + rep * kv_len + kAttnLanes * rep * 64) * 4;
+  return (size_t)(rep * 64 + ((rep * kv_len + 3) & ~3) + kAttnLanes * rep * 64) * 4;
 }
 
 // GEMM with a residual epilogue: x[t][r] += W[r] . in_t (+ bias)  (proj and w2).  With gn != nullptr

@@ -235,3 +235,23 @@ def test_speculation_paths(cuda_ok, env):
     r = om.generate_spec(ids, 40, eos=eos, spec_k=4, ngram=3)
     assert g["generatedIds"] == r["generatedIds"] and g["stopReason"] == r["stopReason"] == "eos"
     eng.destroy()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kv_len", [11, 13, 14, 15])
+def test_batch_with_cache_lengths_off_the_vector_width(cuda_ok, kv_len):
+    """Cache lengths where rep x kv_len is not a multiple of 4 (tiny-llama: 3 query heads per kv head):
+    the attention kernel's per-head score rows then end off a 16-byte boundary, and the reduction buffer
+    after them must still take float4 stores.  8-token prompts with 3 new ids, against the oracle."""
+    data = _data("tiny-llama")
+    om = O.OracleModel(data)
+    eng = _engine(data, max_slots=16, kv_len=kv_len)
+    try:
+        V = eng.cfg["vocabSize"]
+        seqs = _prompts(V, [8] * 16, 70)
+        nnew = min(3, kv_len - 8)
+        res, st = eng.generateBatch(seqs, maxNewTokens=nnew, eosId=-1)
+        for q, r in zip(seqs, res):
+            assert r["generatedIds"] == om.generate(q, nnew, eos=-1)["generatedIds"]
+    finally:
+        eng.destroy()
