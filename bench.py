@@ -598,7 +598,7 @@ def measure_generate(torch, P, key: str, local: int, rank: int, ws: int, dist, s
             if st is not None:
                 dev_ms.append(st.total_ms)
                 first_ms.append(st.ttft_ms)
-        return total, list(dev_ms)
+        return total, list(dev_ms), list(first_ms)
 
     dev_ms, first_ms = [], []
     for _ in range(warmup):
@@ -611,9 +611,9 @@ def measure_generate(torch, P, key: str, local: int, rank: int, ws: int, dist, s
     launches[0] = 0
     spec_stats.clear()
     with ClockSampler(local) as clk:
-        t_dev, dev_ms = timed(step_device, steps)
+        t_dev, dev_v, first_v = timed(step_device, steps)
         torch.cuda.synchronize()
-        t_e2e, _ = timed(step_e2e, steps)
+        t_e2e, _, _ = timed(step_e2e, steps)
     torch.cuda.synchronize()
     gpu_launches = launches[0]
     t_dev, t_e2e = max_over_ranks(dist, [t_dev, t_e2e], f"cuda:{local}")
@@ -630,7 +630,7 @@ def measure_generate(torch, P, key: str, local: int, rank: int, ws: int, dist, s
     else:  # the persistent single-token launch: the decode forwards after the first id
         prefill = w_bytes + n_prompt * 2 * cfg["nLayers"] * cfg["nKvHeads"] * 64 * 4
         alg_launch = alg - prefill
-        launch_ms = float(np.mean([t - f for t, f in zip(dev_ms, first_ms)])) if dev_ms else ms_step
+        launch_ms = float(np.mean([t - f for t, f in zip(dev_v, first_v)])) if dev_v else ms_step
         traffic = DECODE_TRAFFIC_PER_LAUNCH.get((W["workload"], kname.split(":")[0]))
     achieved = alg_launch / (launch_ms / 1e3) / 1e9
     line = {
@@ -672,7 +672,7 @@ def measure_generate(torch, P, key: str, local: int, rank: int, ws: int, dist, s
                                "acceptance_rate": hits / max(tries * spec_k, 1), "accepted_per_try": hits / max(tries, 1),
                                "forwards_per_call": fw, "tokens_per_forward": n_new / max(fw, 1)}
         # the same model and prompt without speculation, for the speed-up (same timing, same flush)
-        t_g, _ = timed(lambda: step_device(0), max(2, min(steps, 3)))
+        t_g, _, _ = timed(lambda: step_device(0), max(2, min(steps, 3)))
         t_g = max_over_ranks(dist, [t_g], f"cuda:{local}")[0]
         greedy = n_new * max(2, min(steps, 3)) / (t_g / 1e3)
         line["speculation"]["greedy_tok_s"] = greedy
