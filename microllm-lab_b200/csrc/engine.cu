@@ -93,8 +93,8 @@ struct mllm_engine {
   int l2_prefetch = 1;         // MLLM_L2_PREFETCH (default on)
   int lm_rpc = 0;              // lm_head rows per CTA kept in the single-token kernel's shared memory
   // layer-wise engine: token-batch forwards on the tensor cores (prefill, verify, batched decode)
-  int lwe_ok = 0;              // rep = nHeads / nKvHeads fits its attention kernel
-  int lwe_prefill = 1;         // MLLM_LWE_PREFILL=0 keeps prefill and multi-token forwards on decode_kernel
+  int lwe_ok = 0;              // rep = nHeads / nKvHeads fits its attention kernel (else multi-token forwards
+                               // run on the persistent decode_kernel)
   int lwe_graph = 1;           // MLLM_LWE_GRAPH=0 launches the batched decode step without a CUDA graph
   int tmax = 0;                // token rows per forward (MLLM_LWE_TOKENS)
   LweArgs lw{};
@@ -498,7 +498,7 @@ int generate_impl(mllm_engine* e, int slot, const int32_t* d_ids, int n, int max
   a.out_ids = d_out;
   a.stream_ids = e->on_token ? e->d_stream : nullptr;
   const int chunks = (n + e->mmax - 1) / e->mmax;
-  if (e->lwe_ok && e->lwe_prefill) {
+  if (e->lwe_ok) {
     // Prefill as token-batch forwards on the tensor cores, first id from its argmax, then the decode
     // loop (greedy: the single-token kernel; speculative: the general kernel) resumes from out_ids.
     CUDA_TRY(e, cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream));
@@ -777,7 +777,6 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
     return bad(MLLM_ERR_OOM, "mapped host buffer for token streaming failed");
   // ---- layer-wise engine buffers: tmax token rows per forward
   e->lwe_ok = md.NH / md.NKV <= kLweMaxRep;
-  if (const char* v = getenv("MLLM_LWE_PREFILL")) e->lwe_prefill = atoi(v) ? 1 : 0;
   if (const char* v = getenv("MLLM_LWE_GRAPH")) e->lwe_graph = atoi(v) ? 1 : 0;
   if (const char* v = getenv("MLLM_LWE_FOLD_NORM")) e->lh.fold_norm = atoi(v) ? 1 : 0;
   if (const char* v = getenv("MLLM_LWE_ATTN_SPLIT")) e->lh.attn_split = atoi(v) ? 1 : 0;
@@ -912,7 +911,7 @@ int mllm_forward(mllm_engine* e, int slot, const int32_t* ids, int n, int pos0, 
   a.logits_each = logits_each ? 1 : 0;
   a.logits = logits ? e->d_logits : nullptr;
   a.argmax_out = e->d_argmax;
-  if (n > 1 && e->lwe_ok && e->lwe_prefill) {
+  if (n > 1 && e->lwe_ok) {
     CUDA_TRY(e, cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream));
     int f = 0;
     TRY(lwe_run(e, slot, e->d_ids, n, pos0, logits_each, logits ? e->d_logits : nullptr, e->d_argmax, &f));

@@ -217,6 +217,10 @@ CONFIGS = {
     # makes a token-stream comparison weak.  BASELINE workloads keep 0.02.
     "tiny-llama": dict(arch="llama", vocabSize=512, nLayers=2, dModel=192, nHeads=3, nKvHeads=1, dFf=320,
                        maxSeqLen=160, ropeTheta=10000.0, std=0.1),
+    # More query heads per kv head (6) than the token-batch engine takes (4): prefill, verify and
+    # multi-token forwards run on the persistent decode_kernel for such files.
+    "tiny-llama-r6": dict(arch="llama", vocabSize=512, nLayers=2, dModel=384, nHeads=6, nKvHeads=1, dFf=512,
+                          maxSeqLen=160, ropeTheta=10000.0, std=0.1),
     "tiny-gpt2": dict(arch="gpt2", vocabSize=640, nLayers=2, dModel=128, nHeads=2, nKvHeads=2, dFf=512,
                       maxSeqLen=128, std=0.1),
 }

@@ -201,25 +201,36 @@ def test_chunked_forward_rows(cuda_ok):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("name", ["tiny-llama", "tiny-gpt2"])
-def test_persistent_prefill_path_still_matches(cuda_ok, name):
-    """MLLM_LWE_PREFILL=0 keeps prefill on the persistent kernel: same streams as the oracle."""
-    data = _data(name)
-    eng = _engine(data, env={"MLLM_LWE_PREFILL": "0"})
+def test_more_query_heads_than_the_token_batch_engine_takes(cuda_ok):
+    """6 query heads per kv head (above the token-batch engine's 4): prefill and multi-token forwards run
+    on the persistent decode_kernel, greedy decode on decode1_kernel; streams and logits as the oracle's,
+    and generateBatch is refused as unsupported."""
+    P = pkg()
+    data = P.synthetic_pgw("tiny-llama-r6", 5)
+    eng = _engine(data)
     om = O.OracleModel(data)
-    ids = pkg().seeded_prompt(21, eng.cfg["vocabSize"], 82)
-    assert eng.generate(ids, maxNewTokens=20, eosId=-1)["generatedIds"] == om.generate(ids, 20, eos=-1)["generatedIds"]
-    g = eng.forwardPrompt(ids)
-    assert np.abs(g - om.forward_prompt(ids)).max() <= LOGIT_TOL
-    eng.destroy()
+    try:
+        ids = P.seeded_prompt(21, eng.cfg["vocabSize"], 82)
+        assert eng.generate(ids, maxNewTokens=20, eosId=-1)["generatedIds"] == om.generate(ids, 20, eos=-1)["generatedIds"]
+        g = eng.forwardPrompt(ids)
+        assert np.abs(g - om.forward_prompt(ids)).max() <= LOGIT_TOL
+        g, am = eng.forward(ids[5:17], 5, logits_each=True)
+        r = om.forward(ids[5:17], 5, logits_each=True)
+        assert np.abs(g - r).max() <= LOGIT_TOL
+        with pytest.raises(P.MllmError):
+            eng.generateBatch([ids, ids], maxNewTokens=4, eosId=-1)
+    finally:
+        eng.destroy()
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("env", [{}, {"MLLM_LWE_GRAPH": "0"}, {"MLLM_LWE_PREFILL": "0"}])
-def test_speculation_paths(cuda_ok, env):
+@pytest.mark.parametrize("case", ["graph", "plain", "persistent"])
+def test_speculation_paths(cuda_ok, case):
     """Prompt-lookup speculation (engine/webgpu.js:1164-1282) on the token-batch engine (graph replays,
-    plain launches) and on the persistent kernel: ids, specHits and specTries equal the oracle's."""
-    data = _data("tiny-llama")
+    plain launches) and on the persistent kernel (a file with 6 query heads per kv head): ids, specHits
+    and specTries equal the oracle's."""
+    env = {"MLLM_LWE_GRAPH": "0"} if case == "plain" else {}
+    data = pkg().synthetic_pgw("tiny-llama-r6", 5) if case == "persistent" else _data("tiny-llama")
     eng = _engine(data, env=env)
     om = O.OracleModel(data)
     ids = pkg().copy_span_prompt(96, 512, 83)
