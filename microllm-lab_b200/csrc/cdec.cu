@@ -429,27 +429,30 @@ __device__ __forceinline__ float inv_rms_of(const float* ssw, int D) {
 }
 
 
-// Publish rows [r0, r0 + n) (n a multiple of 4) of cluster cid's D-long partial vector, staged in
-// `vals`: into the global words gx (several clusters), then into `part` (float index cid D + r0) of
-// every CTA of the cluster; then forward this CTA's 1/16 share of the other clusters' vectors, as
-// their tags arrive, to every CTA of the cluster.  All bytes complete on `bar` of the receiving CTA.
-// False when a wait for remote words gave up (the error flag is then raised).
-__device__ __forceinline__ bool publish(const float* vals, int n, int r0, int D, int cid, int nc, uint32_t part,
+// Publish rows [r0, r0 + n) (n a multiple of 4) of this cluster's D-long partial vector (source slot
+// `own` of nsrc; own < 0: this cluster has no partial), staged in `vals`: into the global words gx
+// (several clusters), then into `part` (float index own D + r0) of every CTA of the cluster; then
+// forward this CTA's 1/16 share of the other sources' vectors, as their tags arrive, to every CTA of the
+// cluster.  All bytes complete on `bar` of the receiving CTA.  False when a wait for remote words gave up
+// (the error flag is then raised).
+__device__ __forceinline__ bool publish(const float* vals, int n, int r0, int D, int own, int nsrc, uint32_t part,
                                         uint32_t bar, uint64_t* gx, uint32_t tag, int rank, int* err,
                                         uint64_t limit) {
-  if (gx)
-    for (int i = threadIdx.x; i < n; i += kCdThreads) ll_store(gx + (size_t)cid * D + r0 + i, tag, vals[i]);
-  for (int i = threadIdx.x; i < n * 4; i += kCdThreads) {  // n / 4 quads x 16 CTAs
-    const int q = i >> 4, d = i & 15;
-    st_async4(mapa(part + 4 * (cid * D + r0 + 4 * q), d), reinterpret_cast<const float4*>(vals)[q], mapa(bar, d));
+  if (own >= 0) {
+    if (gx)
+      for (int i = threadIdx.x; i < n; i += kCdThreads) ll_store(gx + (size_t)own * D + r0 + i, tag, vals[i]);
+    for (int i = threadIdx.x; i < n * 4; i += kCdThreads) {  // n / 4 quads x 16 CTAs
+      const int q = i >> 4, d = i & 15;
+      st_async4(mapa(part + 4 * (own * D + r0 + 4 * q), d), reinterpret_cast<const float4*>(vals)[q], mapa(bar, d));
+    }
   }
   if (!gx) return true;
-  const int QD = D / 4, QR = (nc - 1) * QD;
+  const int QD = D / 4, QR = (own >= 0 ? nsrc - 1 : nsrc) * QD;
   const int j1 = (rank + 1) * QR / kCdCtas;
   bool ok = true;
   for (int j = rank * QR / kCdCtas + threadIdx.x; j < j1 && ok; j += kCdThreads) {
     const int gi = j / QD, q = j - gi * QD;
-    const int g = gi < cid ? gi : gi + 1;
+    const int g = (own < 0 || gi < own) ? gi : gi + 1;
     const uint64_t* src = gx + (size_t)g * D + 4 * q;
     // the quad's four words in two 16-byte loads per round, both in flight together
     uint64_t w0, w1, w2, w3;
@@ -492,7 +495,7 @@ __device__ int g_cd_tl_forward = 3;
     if (tid == 0 && f == g_cd_tl_forward && (idx) < kCdTlWords) g_cd_tl[gc][(idx)] = globaltimer(); \
   } while (0)
 #else
-constexpr int kCdTlLayer = 0, kCdTlTail = 0;
+[[maybe_unused]] constexpr int kCdTlLayer = 0, kCdTlTail = 0;
 #define CD_TL(idx) \
   do {             \
   } while (0)
@@ -505,7 +508,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   const RunArgs& a = A.r;
   const ModelDev& md = a.m;
   const CdSmem& Ls = A.L;
-  const int nc = A.nc, nct = nc * kCdCtas;
+  const int nc = A.nc, nct = nc * kCdCtas, na = A.r.m.NKV;  // clusters, CTAs, attention clusters
   {
     // The launch must have the shape the weight streams were packed for: nc clusters of 16 CTAs.  A
     // launch of another shape (for example one re-issued without its cluster attribute) returns
@@ -519,7 +522,8 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
     }
   }
   const int c = (int)cta_rank();     // rank in the cluster
-  const int cid = (int)cluster_id(); // the cluster's kv head
+  const int cid = (int)cluster_id(); // the cluster's kv head (cid < na), else a helper cluster
+  const bool is_attn = cid < na;
   const int gc = cid * kCdCtas + c;  // CTA of the launch
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int D = md.D, NKV = md.NKV, rep = md.NH / md.NKV;
@@ -548,7 +552,7 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
   uint32_t kvph = 0;       // phases of the K/V staging barrier completed
   bool kv_pending = false; // a staging copy is in flight
   const uint32_t bar_bytes[B_COUNT] = {(uint32_t)(nc * D * 4), (uint32_t)(2 * (rep + 2) * 64 * 4),
-                                       (uint32_t)(kCdCtas * rep * kCdPartWords * 4), (uint32_t)(nc * D * 4),
+                                       (uint32_t)(kCdCtas * rep * kCdPartWords * 4), (uint32_t)(na * D * 4),
                                        (uint32_t)(D * 4), (uint32_t)(nct * 16)};
   const uint64_t limit = a.wait_ns ? a.wait_ns : kWaitNs;
   uint32_t par[B_COUNT] = {0, 0, 0, 0, 0, 0};
@@ -732,10 +736,11 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       const int npos = max(0, p_hi - p_lo);
       const int nst = max(0, min(min(p_hi, pos) - p_lo, kCdKvStage));
       const size_t kv_base = ((size_t)l * NKV + cid) * md.kv_len;
-      if (l == 0) stage_kv(0, p_lo, nst, tid == 0);
+      if (l == 0 && is_attn) stage_kv(0, p_lo, nst, tid == 0);
       __syncthreads();
       const float inv1 = inv_rms_of(misc, D);
       CD_TL(l * kCdTlLayer + 2);
+      if (is_attn) {  // ---- attention clusters: q/k/v, attention and the proj columns of the group
       // ---- the group's q/k/v rows (engine/infer.js:431-440)
       if (!__syncthreads_and(units(CD_QKV, l * rl))) {
         ok = false;
@@ -968,13 +973,15 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       for (int i = tid; i < gp.T * 16; i += kCdThreads) outv[i] = row_val(red, gp, i);
       CD_TL(l * kCdTlLayer + 12);
       __syncthreads();
+      }
       // a remote wait that gives up raises the error flag; the wait that follows then fails everywhere
-      (void)publish(outv, gp.T * 16, 16 * gp.t0, D, cid, nc, smem_u32(pp1), sbar + 8 * B_X1, gxb(CD_GX_PP1, B_X1),
-                    tagb(B_X1), c, a.err, limit);
+      // (helper clusters only forward the attention clusters' partials)
+      (void)publish(outv, gp.T * 16, 16 * gp.t0, D, is_attn ? cid : -1, na, smem_u32(pp1), sbar + 8 * B_X1,
+                    gxb(CD_GX_PP1, B_X1), tagb(B_X1), c, a.err, limit);
       CD_TL(l * kCdTlLayer + 13);
       if (!(ok = wait_bar(B_X1))) goto done;
       CD_TL(l * kCdTlLayer + 14);
-      residual_act(xb1, xb2, pp1, D, nc, g2, actp, misc);
+      residual_act(xb1, xb2, pp1, D, na, g2, actp, misc);
       __syncthreads();
       // ---- w1 / w3 rows of this CTA's FF slice, SiLU(u) * v (engine/infer.js:506-527)
       const float inv2 = inv_rms_of(misc, D);
@@ -985,11 +992,18 @@ __global__ void __launch_bounds__(kCdThreads, 1) cdec_kernel(const __grid_consta
       }
       CD_TL(l * kCdTlLayer + 16);
       reduce_tiles(red, gw13);
-      for (int i = tid; i < gw13.T * 16; i += kCdThreads) {
-        const int tl = i >> 4, r = i & 15;
-        const float u = inv2 * row_val(red, gw13, (2 * tl) * 16 + r);
-        const float v = inv2 * row_val(red, gw13, (2 * tl + 1) * 16 + r);
-        actp[i] = pre_scale((u / (1.f + expf(-u))) * v, i);
+      // the w2 activation: this CTA's h values at their place in its 32-column groups (k0 = s0 / 2), zero
+      // in the half group that belongs to the neighbouring CTA
+      for (int i = tid; i < 32 * gw2.G; i += kCdThreads) {
+        const int k = i - 16 * (gw13.t0 & 1);  // h row of this CTA's slices
+        float hv = 0.f;
+        if (k >= 0 && k < 16 * gw13.T) {
+          const int tl = k >> 4, r = k & 15;
+          const float u = inv2 * row_val(red, gw13, (2 * tl) * 16 + r);
+          const float v = inv2 * row_val(red, gw13, (2 * tl + 1) * 16 + r);
+          hv = (u / (1.f + expf(-u))) * v;
+        }
+        actp[i] = pre_scale(hv, i);
       }
       __syncthreads();
       // ---- w2 columns of the slice -> partial of all D rows -> reduce over the cluster -> x2
@@ -1185,25 +1199,27 @@ done:
 // head, at most kCdMaxClusters kv heads (one cluster each), FF a whole number of 32-row slices, an
 // lm_head tile for every CTA, and the shared-memory plan within `smem_cap` with at least two ring
 // slots.
-bool cd_supported(const ModelDev& m, size_t smem_cap) {
+bool cd_supported(const ModelDev& m, size_t smem_cap, int nc) {
   if (m.arch != 0 || m.D != m.NH * 64 || m.NH % m.NKV || m.NH / m.NKV > 4) return false;
   if (m.NKV < 1 || m.NKV > kCdMaxClusters || m.FF % 32 || m.D > 2 * kCdThreads) return false;
   if (m.rope_dim > 64 || m.rope_dim % 2) return false;
-  if ((m.vocab + 15) / 16 < m.NKV * kCdCtas) return false;
-  const CdSmem p = cd_smem(m, (int)smem_cap, m.NKV);
+  if (nc < m.NKV || nc > kCdMaxClusters || (m.vocab + 15) / 16 < nc * kCdCtas) return false;
+  const CdSmem p = cd_smem(m, (int)smem_cap, nc);
   return p.nslot >= 2 && (size_t)p.total <= smem_cap;
 }
 
-size_t cd_smem_bytes(const ModelDev& m, size_t smem_cap) { return (size_t)cd_smem(m, (int)smem_cap, m.NKV).total; }
+size_t cd_smem_bytes(const ModelDev& m, size_t smem_cap, int nc) {
+  return (size_t)cd_smem(m, (int)smem_cap, nc).total;
+}
 
 // Records of every (CTA, warp) stream, in consumption order: per layer QKV, PROJ, W13 (w1 / w3 tiles
 // interleaved), W2, then the lm_head.  A record holds, for lane = 4 gid + t, the words t of group g of
 // rows gid and gid + 8 (8 bytes at 8 lane), then the scales of rows (gid, gid + 8) as a float pair at
 // 256 + 8 gid.  Rows past the end hold q = 8 nibbles and zero scales.
-void cd_pack(const ModelDev& m, const std::vector<HostQ4>& mats /* per layer: qkv, proj, w1, w3, w2 */,
+void cd_pack(const ModelDev& m, int nc, const std::vector<HostQ4>& mats /* per layer: qkv, proj, w1, w3, w2 */,
              const HostQ4& lm, std::vector<uint8_t>* out, std::vector<uint32_t>* off, std::vector<uint32_t>* cpt,
              std::vector<uint32_t>* cnt) {
-  const int nc = m.NKV, nct = nc * kCdCtas;
+  const int nct = nc * kCdCtas;
   off->assign(nct, 0);
   cpt->assign(nct, 0);
   cnt->assign((size_t)nct * kCdWarps, 0);
@@ -1229,14 +1245,15 @@ void cd_pack(const ModelDev& m, const std::vector<HostQ4>& mats /* per layer: qk
     chunks += (*cpt)[gc];
   }
   out->assign(chunks * kCdChunk, 0);
-  auto emit = [&](uint8_t* dst, const HostQ4& q, int r0, int g) {
+  // wmask: bit t keeps word t (columns 8t .. 8t + 7 of the group); masked words hold weight 0
+  auto emit = [&](uint8_t* dst, const HostQ4& q, int r0, int g, unsigned wmask) {
     const int hb = q.K / 2, ng = q.K / 32;
     for (int lane = 0; lane < 32; ++lane) {
       const int gid = lane >> 2, t = lane & 3;
       for (int h = 0; h < 2; ++h) {
         const int r = r0 + gid + 8 * h;
         uint32_t word = 0x88888888u;
-        if (r < q.rows) memcpy(&word, q.w + (size_t)r * hb + 16 * g + 4 * t, 4);
+        if (r < q.rows && ((wmask >> t) & 1)) memcpy(&word, q.w + (size_t)r * hb + 16 * g + 4 * t, 4);
         memcpy(dst + 8 * lane + 4 * h, &word, 4);
       }
     }
@@ -1253,10 +1270,10 @@ void cd_pack(const ModelDev& m, const std::vector<HostQ4>& mats /* per layer: qk
     for (int w = 0; w < kCdWarps; ++w) {
       // record j of warp w goes to chunk j / kCdRpc, position w * kCdRpc + j % kCdRpc
       size_t j = 0;
-      auto put = [&](const HostQ4& q, int r0, int g) {
+      auto put = [&](const HostQ4& q, int r0, int g, unsigned wmask = 15u) {
         uint8_t* dst = out->data() + ((size_t)(*off)[gc] + j / kCdRpc) * kCdChunk +
                        (size_t)(w * kCdRpc + j % kCdRpc) * kCdRecBytes;
-        emit(dst, q, r0, g);
+        emit(dst, q, r0, g, wmask);
         ++j;
       };
       auto emit_stage = [&](int st, int l, const HostQ4* a, const HostQ4* b) {
@@ -1264,9 +1281,22 @@ void cd_pack(const ModelDev& m, const std::vector<HostQ4>& mats /* per layer: qk
         const int v = (w - cd_stage_off(m, cid, c, nc, l, st)) & (kCdWarps - 1);
         for (int u = cd_ustart(g, v); u < cd_ustart(g, v + 1); ++u) {
           const int tl = u / g.G, gg = g.k0 + u % g.G;
-          if (st == CD_QKV) put(*a, cd_qkv_row(m, cid, (g.t0 + tl) >> 1), gg + ((g.t0 + tl) & 1) * g.G);
-          else if (st == CD_W13) put((tl & 1) ? *b : *a, 16 * (g.t0 + tl / 2), gg);
-          else put(*a, 16 * (g.t0 + tl), gg);
+          if (st == CD_QKV) {
+            put(*a, cd_qkv_row(m, cid, (g.t0 + tl) >> 1), gg + ((g.t0 + tl) & 1) * g.G);
+          } else if (st == CD_W13) {
+            put((tl & 1) ? *b : *a, 16 * (g.t0 + tl / 2), gg);
+          } else if (st == CD_W2) {  // only this CTA's h columns [16 s0, 16 s1) of group gg
+            int s0, s1;
+            cd_ff_slices(m, gc, nct, &s0, &s1);
+            unsigned wmask = 0;
+            for (int t = 0; t < 4; ++t) {
+              const int k = 32 * gg + 8 * t;
+              if (k >= 16 * s0 && k < 16 * s1) wmask |= 1u << t;
+            }
+            put(*a, 16 * (g.t0 + tl), gg, wmask);
+          } else {
+            put(*a, 16 * (g.t0 + tl), gg);
+          }
         }
       };
       for (int l = 0; l < m.n_layers; ++l) {

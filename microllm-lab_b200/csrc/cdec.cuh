@@ -1,7 +1,8 @@
 // Cluster decode: the single-token greedy decode loop (engine/infer.js:579-601 per token,
-// engine/infer.js:625-639 for the loop) as one 16-CTA thread-block cluster per kv head; the clusters
-// exchange stage outputs through distributed shared memory inside a cluster and through tagged global
-// words between clusters.
+// engine/infer.js:625-639 for the loop) as one 16-CTA thread-block cluster per kv head (the attention
+// clusters) plus helper clusters that share the MLP and lm_head rows; the clusters exchange stage
+// outputs through distributed shared memory inside a cluster and through tagged global words between
+// clusters.
 //
 // Shared by the host runtime (weight repacking, shared-memory sizing) and the kernel (cdec.cu).
 #pragma once
@@ -15,7 +16,7 @@
 namespace mllm {
 
 constexpr int kCdCtas = 16;                 // CTAs of a cluster (one per SM)
-constexpr int kCdMaxClusters = 8;           // clusters of one launch (one per kv head)
+constexpr int kCdMaxClusters = 8;           // clusters of one launch (kv heads + helpers)
 constexpr int kCdWarps = 16;                // warps per CTA
 constexpr int kCdThreads = kCdWarps * 32;   // 512
 constexpr int kCdRecBytes = 320;            // one weight record: 16 rows x 32-wide group (256 B) + 16 scales
@@ -68,20 +69,31 @@ __host__ __device__ inline CdGeom cd_geom(int t0, int T, int G, int k0, bool pai
 }
 
 // Stage kinds in stream order within a layer, then the lm_head.
-//   CD_QKV:  cluster g (kv head g) computes the rows of its group: q heads g rep .. g rep + rep - 1, then
-//            k head g, then v head g ((rep + 2) x 64 rows); each group-local tile is cut into its two K
-//            halves and the 2 (rep + 2) 4 halves are split over the 16 CTAs (two partial vectors).
-//   CD_PROJ: cluster g multiplies its heads' attention output (columns g rep 64 .. + rep 64 of proj)
-//            into a partial of all D rows; the D / 16 row tiles are split over its 16 CTAs.
-//   CD_W13:  the FF rows, in slices of 32, split over all 16 nc CTAs (w1 and w3 tiles paired).
+//   CD_QKV:  attention cluster g (kv head g, g < nKvHeads) computes the rows of its group: q heads
+//            g rep .. g rep + rep - 1, then k head g, then v head g ((rep + 2) x 64 rows); each group-local
+//            tile is cut into its two K halves and the 2 (rep + 2) 4 halves are split over the 16 CTAs
+//            (two partial vectors).  Helper clusters have none.
+//   CD_PROJ: attention cluster g multiplies its heads' attention output (columns g rep 64 .. + rep 64
+//            of proj) into a partial of all D rows; the D / 16 row tiles are split over its 16 CTAs.
+//   CD_W13:  the FF rows, in slices of 16 (one w1 and one w3 tile), split over all 16 nc CTAs.
 //   CD_W2:   every CTA multiplies its own h slice (the columns of its w13 rows) into a partial of all
-//            D rows.
+//            D rows; a slice that covers half of a 32-column group leaves the other half of its records
+//            at weight 0 (nibble 8).
 //   CD_LM:   the vocab rows split over all CTAs.
 enum CdStage { CD_QKV = 0, CD_PROJ = 1, CD_W13 = 2, CD_W2 = 3, CD_LM = 4 };
 
+// FF slices (16 rows each) [s0, s1) of CTA gc of nct: its w1/w3 tiles and the h columns of its w2 records.
+__host__ __device__ inline void cd_ff_slices(const ModelDev& m, int gc, int nct, int* s0, int* s1) {
+  const int NS = m.FF / 16;
+  *s0 = gc * NS / nct;
+  *s1 = (gc + 1) * NS / nct;
+}
+
 __host__ __device__ inline CdGeom cd_stage_geom(const ModelDev& m, int st, int cid, int c, int nc) {
   const int rep = m.NH / m.NKV, nct = nc * kCdCtas, gc = cid * kCdCtas + c;
-  const int NS = m.FF / 32, s0 = gc * NS / nct, s1 = (gc + 1) * NS / nct;
+  int s0, s1;
+  cd_ff_slices(m, gc, nct, &s0, &s1);
+  if ((st == CD_QKV || st == CD_PROJ) && cid >= m.NKV) return cd_geom(0, 0, 2, 0, false);  // helper cluster
   switch (st) {
     case CD_QKV: {  // K halves of the group's (rep + 2) 4 tiles, so that 16 CTAs share them evenly
       const int NT = 2 * (rep + 2) * 4;
@@ -95,8 +107,9 @@ __host__ __device__ inline CdGeom cd_stage_geom(const ModelDev& m, int st, int c
       const int t0 = c * NT / kCdCtas;
       return cd_geom(t0, (c + 1) * NT / kCdCtas - t0, 2 * rep, cid * 2 * rep, false);
     }
-    case CD_W13: return cd_geom(2 * s0, 2 * (s1 - s0), m.D / 32, 0, true);
-    case CD_W2: return cd_geom(0, m.D / 16, s1 - s0, s0, false);
+    case CD_W13: return cd_geom(s0, s1 - s0, m.D / 32, 0, true);
+    case CD_W2: return s1 > s0 ? cd_geom(0, m.D / 16, (s1 + 1) / 2 - s0 / 2, s0 / 2, false)
+                               : cd_geom(0, m.D / 16, 0, 0, false);
     default: {
       const int NT = (m.vocab + 15) / 16;
       const int t0 = gc * NT / nct;
@@ -158,7 +171,7 @@ __host__ __device__ inline CdSmem cd_smem(const ModelDev& m, int cap, int nc) {
   s.red = take(redf * 4);
   s.xb2 = take((m.D + m.D / 4) * 4);
   s.xb1 = take((m.D + m.D / 4) * 4);
-  s.pp1 = take(nc * m.D * 4);             // proj partials of every cluster
+  s.pp1 = take(m.NKV * m.D * 4);          // proj partials of the attention clusters
   s.pp2 = take(nc * m.D * 4);             // w2 partials of every cluster
   s.rs = take(m.D * 4);                   // w2 partials of this CTA's D / 16 rows from the 16 CTAs
   s.qkv = take(2 * (rep + 2) * 64 * 4);  // the two K-half partials of the group's q/k/v
@@ -185,10 +198,10 @@ __host__ __device__ inline CdSmem cd_smem(const ModelDev& m, int cap, int nc) {
 }
 
 // Global exchange words between clusters, 8-byte {tag, value}, each buffer [2 parities][words]:
-// proj partials [nc][D], w2 partials [nc][D], argmax candidates [16 nc][2].
+// proj partials [nKvHeads][D], w2 partials [nc][D], argmax candidates [16 nc][2].
 enum { CD_GX_PP1 = 0, CD_GX_PP2 = 1, CD_GX_CAND = 2 };
 __host__ __device__ inline size_t cd_gx_words(const ModelDev& m, int nc, int b /* -1: total */) {
-  const size_t w[3] = {(size_t)nc * m.D, (size_t)nc * m.D, (size_t)2 * nc * kCdCtas};
+  const size_t w[3] = {(size_t)m.NKV * m.D, (size_t)nc * m.D, (size_t)2 * nc * kCdCtas};
   size_t off = 0;
   for (int i = 0; i < 3; ++i) {
     if (i == b) return off;
@@ -206,7 +219,7 @@ struct CdArgs {
   const uint32_t* wcpt;  // [16 nc] chunks per token of each CTA
   const uint32_t* wcnt;  // [16 nc x kCdWarps] records per token of each warp
   CdSmem L;              // shared-memory plan (cd_smem)
-  int nc;                // clusters of the launch (= nKvHeads)
+  int nc;                // clusters of the launch: nKvHeads attention clusters, then helpers
   uint64_t* gx;          // global exchange words (cd_gx_words), zeroed before the first launch; null if nc = 1
   uint32_t tag0;         // tags of this launch are tag0 + 1 + use index (uses < 2^22 per launch)
 };
@@ -220,9 +233,9 @@ struct HostQ4 {
   int rows, K;
 };
 
-bool cd_supported(const ModelDev& m, size_t smem_cap);
-size_t cd_smem_bytes(const ModelDev& m, size_t smem_cap);
-void cd_pack(const ModelDev& m, const std::vector<HostQ4>& mats, const HostQ4& lm, std::vector<uint8_t>* out,
+bool cd_supported(const ModelDev& m, size_t smem_cap, int nc);
+size_t cd_smem_bytes(const ModelDev& m, size_t smem_cap, int nc);
+void cd_pack(const ModelDev& m, int nc, const std::vector<HostQ4>& mats, const HostQ4& lm, std::vector<uint8_t>* out,
              std::vector<uint32_t>* off, std::vector<uint32_t>* cpt, std::vector<uint32_t>* cnt);
 cudaError_t cd_setup(size_t smem_cap);
 int cd_max_clusters(size_t smem);

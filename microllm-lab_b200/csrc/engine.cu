@@ -695,13 +695,18 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, k == e->kernel_multi ? e->smem_multi : e->smem_single);
     if (per_sm < 1) return bad(MLLM_ERR_CUDA, "decode kernel cannot be resident with its shared memory");
   }
-  // ---- cluster decode: weights repacked into per-(CTA, warp) streams (MLLM_CLUSTER_DECODE=1: on)
+  // ---- cluster decode: weights repacked into per-(CTA, warp) streams (MLLM_CLUSTER_DECODE=1: on, with
+  // as many clusters as the device holds at once; =N with N > 1: at most max(N, nKvHeads) clusters)
   {
-    bool want = false;
-    if (const char* v = getenv("MLLM_CLUSTER_DECODE")) want = atoi(v) != 0;
-    const int nc = md.NKV;
-    if (want && cd_supported(md, smem_cap) && cd_setup(smem_cap) == cudaSuccess &&
-        cd_max_clusters(cd_smem_bytes(md, smem_cap)) >= nc) {
+    int cap = 0;
+    if (const char* v = getenv("MLLM_CLUSTER_DECODE")) cap = atoi(v);
+    const bool want = cap != 0;
+    cap = cap > 1 ? std::max(cap, md.NKV) : kCdMaxClusters;
+    int nc = 0;
+    if (want && cd_setup(smem_cap) == cudaSuccess)
+      for (nc = std::min(cap, kCdMaxClusters); nc >= md.NKV && nc >= 1; --nc)
+        if (cd_supported(md, smem_cap, nc) && cd_max_clusters(cd_smem_bytes(md, smem_cap, nc)) >= nc) break;
+    if (want && nc >= md.NKV && nc >= 1) {
       auto host_q4 = [&](const std::string& name, int rows, int cols) {
         const PgwTensor* t = tensor(p, name);
         return HostQ4{buf + p.payload_off + t->offset, buf + p.payload_off + t->scale_offset, rows, cols};
@@ -717,7 +722,7 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
       }
       std::vector<uint8_t> packed;
       std::vector<uint32_t> off, cpt, cnt;
-      cd_pack(md, mats, host_q4("lm_head", md.vocab, D), &packed, &off, &cpt, &cnt);
+      cd_pack(md, nc, mats, host_q4("lm_head", md.vocab, D), &packed, &off, &cpt, &cnt);
       int rc;
       if ((rc = dev_alloc(E, &e->d_cdw, packed.size())) || (rc = dev_alloc(E, &e->d_cdoff, off.size() * 4)) ||
           (rc = dev_alloc(E, &e->d_cdcpt, cpt.size() * 4)) || (rc = dev_alloc(E, &e->d_cdcnt, cnt.size() * 4)))
@@ -730,7 +735,7 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
       cudaMemcpy(e->d_cdoff, off.data(), off.size() * 4, cudaMemcpyHostToDevice);
       cudaMemcpy(e->d_cdcpt, cpt.data(), cpt.size() * 4, cudaMemcpyHostToDevice);
       cudaMemcpy(e->d_cdcnt, cnt.data(), cnt.size() * 4, cudaMemcpyHostToDevice);
-      e->cd_smem = cd_smem_bytes(md, smem_cap);
+      e->cd_smem = cd_smem_bytes(md, smem_cap, nc);
       e->cd_plan = cd_smem(md, (int)smem_cap, nc);
       e->cd_nc = nc;
       e->cd_ok = 1;
