@@ -797,12 +797,26 @@ def run_case(args):
     batched: config 5 (SmolLM2-135M shape) with --seqs sequences of --prompt-token prompts (default 128)
              and --new ids;
     spec:    config 4 (SmolLM2-360M shape, 512-token copy-span prompt) with --new ids at k = --k;
-    gemv:    one cold mllm_gemv_q4 on the lm_head shape (49152 x 576, M = 1)."""
+    gemv:    one cold mllm_gemv_q4 on the lm_head shape (49152 x 576, M = 1);
+    gemm:    two mllm_gemm_q4 calls (tcgen05 tiles) on --rows x --cols with --seqs activation rows."""
     import torch
     if args.case == "timeline":
         run_timeline(args)
         return
     P = pkg()
+    if args.case == "gemm":  # one mllm_gemm_q4 (tcgen05 tiles) on --rows x --cols with --seqs activation rows
+        rows, cols, m = args.rows, args.cols, args.seqs
+        rng = np.random.default_rng(1)
+        packed, scales = P.quant_q4(rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02))
+        pk = torch.from_numpy(np.ascontiguousarray(packed).reshape(-1)).cuda()
+        sc = torch.from_numpy(np.ascontiguousarray(scales).reshape(-1)).cuda()
+        x = torch.from_numpy(rng.standard_normal((m, cols), dtype=np.float32)).cuda()
+        y = torch.empty((m, rows), device="cuda")
+        for _ in range(2):
+            P.gemm_q4_device(pk.data_ptr(), sc.data_ptr(), x.data_ptr(), y.data_ptr(), rows, cols, m)
+        torch.cuda.synchronize()
+        print(json.dumps({"case": "gemm", "rows": rows, "cols": cols, "m": m, "checksum": float(y.double().sum())}))
+        return
     if args.case == "gemv":
         rows, cols = 49152, 576
         rng = np.random.default_rng(1)
@@ -854,13 +868,15 @@ def main():
     ap.add_argument("--batched-steps", type=int, default=3)
     ap.add_argument("--leg-steps", type=int, default=3, help="timed steps of the config 3 and 4 sub-objects")
     ap.add_argument("--no-extra", action="store_true", help="only config 1 (and config 5 unless --no-batched)")
-    ap.add_argument("--case", choices=["decode", "timeline", "batched", "spec", "gemv"],
+    ap.add_argument("--case", choices=["decode", "timeline", "batched", "spec", "gemv", "gemm"],
                     help="one small untimed run for a profiler capture (see run_case)")
     ap.add_argument("--new", type=int, default=0, help="--case: ids to generate")
     ap.add_argument("--seqs", type=int, default=128, help="--case batched: sequences")
     ap.add_argument("--prompt", type=int, default=0, help="--case batched: prompt tokens (0 = config 5's 128)")
     ap.add_argument("--k", type=int, default=4, help="--case spec: draft length")
     ap.add_argument("--forward", type=int, default=20, help="--case timeline: the stamped forward of the launch")
+    ap.add_argument("--rows", type=int, default=1536, help="--case gemm: weight rows")
+    ap.add_argument("--cols", type=int, default=576, help="--case gemm: columns (K)")
     args = ap.parse_args()
     if args.case:
         run_case(args)

@@ -47,6 +47,9 @@ cudaError_t launch_gemm_store(const uint8_t* W, const float* S, const __half* xh
   return cudaGetLastError();
 }
 
+cudaError_t launch_gemm_tc5(const uint8_t* W, const float* S, const __half* xh, const __half* xl, float* Y, int R,
+                            int K, int T, cudaStream_t st);  // gemm_tc5.cu
+
 cudaError_t launch_split(const float* x, __half* hi, __half* lo, size_t n, cudaStream_t st) {
   const int blocks = (int)std::min<size_t>((n + 255) / 256, 148 * 8);
   split_kernel<<<blocks, 256, 0, st>>>(x, hi, lo, n);
@@ -105,7 +108,7 @@ extern "C" int mllm_gemm_q4(const uint8_t* d_packed, const float* d_scales, cons
   __half* hi = ws;
   __half* lo = ws + ((n + 127) / 128) * 128;
   if (launch_split(d_x, hi, lo, n, st) != cudaSuccess) return MLLM_ERR_CUDA;
-  if (launch_gemm_store(d_packed, d_scales, hi, lo, d_y, rows, cols, n_act, st) != cudaSuccess) return MLLM_ERR_CUDA;
+  if (launch_gemm_tc5(d_packed, d_scales, hi, lo, d_y, rows, cols, n_act, st) != cudaSuccess) return MLLM_ERR_CUDA;
   return MLLM_OK;
 }
 
@@ -177,6 +180,6 @@ extern "C" int mllm_gemm_q4_noalloc(const uint8_t* d_packed, const float* d_scal
   __half* lo = base + kNoAllocMaxValues;
   cudaStream_t st = (cudaStream_t)stream;
   if (launch_split(d_x, hi, lo, n, st) != cudaSuccess) return MLLM_ERR_CUDA;
-  if (launch_gemm_store(d_packed, d_scales, hi, lo, d_y, rows, cols, n_act, st) != cudaSuccess) return MLLM_ERR_CUDA;
+  if (launch_gemm_tc5(d_packed, d_scales, hi, lo, d_y, rows, cols, n_act, st) != cudaSuccess) return MLLM_ERR_CUDA;
   return MLLM_OK;
 }
