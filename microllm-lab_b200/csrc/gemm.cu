@@ -47,8 +47,15 @@ cudaError_t launch_gemm_store(const uint8_t* W, const float* S, const __half* xh
   return cudaGetLastError();
 }
 
+// gemm_tc5.cu: the tcgen05 GEMM and the tiled activation halves it reads
 cudaError_t launch_gemm_tc5(const uint8_t* W, const float* S, const __half* xh, const __half* xl, float* Y, int R,
-                            int K, int T, cudaStream_t st);  // gemm_tc5.cu
+                            int K, int T, cudaStream_t st);
+cudaError_t launch_split_tiled(const float* x, __half* hi, __half* lo, int T, int K, cudaStream_t st);
+size_t tc5_tiled_halves(int T, int K);
+
+// Up to 16 activation rows the mma.sync tile (one 16-token pass, no tensor-memory set-up) is the faster
+// of the two; from 17 rows on the tcgen05 GEMM is.
+bool use_tc5(int n_act) { return n_act > 16; }
 
 cudaError_t launch_split(const float* x, __half* hi, __half* lo, size_t n, cudaStream_t st) {
   const int blocks = (int)std::min<size_t>((n + 255) / 256, 148 * 8);
@@ -97,7 +104,8 @@ extern "C" int mllm_gemm_q4(const uint8_t* d_packed, const float* d_scales, cons
   if (!d_packed || !d_scales || !d_x || !d_y || rows <= 0 || cols <= 0 || cols % 32 || n_act <= 0) return MLLM_ERR_ARG;
   if (((uintptr_t)d_packed & 15) || ((uintptr_t)d_scales & 3) || ((uintptr_t)d_x & 3)) return MLLM_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
-  const size_t n = (size_t)n_act * cols;
+  const bool tc5 = use_tc5(n_act);
+  const size_t n = tc5 ? tc5_tiled_halves(n_act, cols) : (size_t)n_act * cols;
   // The lock is held until both kernels are enqueued, so no other call can replace the workspace in
   // between.  Calls whose kernels overlap on the GPU (different streams or threads) still share the
   // workspace and must be serialised by the caller.
@@ -107,8 +115,13 @@ extern "C" int mllm_gemm_q4(const uint8_t* d_packed, const float* d_scales, cons
   if (rc) return rc;
   __half* hi = ws;
   __half* lo = ws + ((n + 127) / 128) * 128;
-  if (launch_split(d_x, hi, lo, n, st) != cudaSuccess) return MLLM_ERR_CUDA;
-  if (launch_gemm_tc5(d_packed, d_scales, hi, lo, d_y, rows, cols, n_act, st) != cudaSuccess) return MLLM_ERR_CUDA;
+  if (tc5) {
+    if (launch_split_tiled(d_x, hi, lo, n_act, cols, st) != cudaSuccess) return MLLM_ERR_CUDA;
+    if (launch_gemm_tc5(d_packed, d_scales, hi, lo, d_y, rows, cols, n_act, st) != cudaSuccess) return MLLM_ERR_CUDA;
+  } else {
+    if (launch_split(d_x, hi, lo, n, st) != cudaSuccess) return MLLM_ERR_CUDA;
+    if (launch_gemm_store(d_packed, d_scales, hi, lo, d_y, rows, cols, n_act, st) != cudaSuccess) return MLLM_ERR_CUDA;
+  }
   return MLLM_OK;
 }
 
@@ -179,7 +192,13 @@ extern "C" int mllm_gemm_q4_noalloc(const uint8_t* d_packed, const float* d_scal
   __half* hi = base;
   __half* lo = base + kNoAllocMaxValues;
   cudaStream_t st = (cudaStream_t)stream;
+  if (use_tc5(n_act) && tc5_tiled_halves(n_act, cols) <= kNoAllocMaxValues) {
+    if (launch_split_tiled(d_x, hi, lo, n_act, cols, st) != cudaSuccess) return MLLM_ERR_CUDA;
+    if (launch_gemm_tc5(d_packed, d_scales, hi, lo, d_y, rows, cols, n_act, st) != cudaSuccess) return MLLM_ERR_CUDA;
+    return MLLM_OK;
+  }
+  // the tiled halves pad n_act to a multiple of 8 and would not fit: row-major halves instead
   if (launch_split(d_x, hi, lo, n, st) != cudaSuccess) return MLLM_ERR_CUDA;
-  if (launch_gemm_tc5(d_packed, d_scales, hi, lo, d_y, rows, cols, n_act, st) != cudaSuccess) return MLLM_ERR_CUDA;
+  if (launch_gemm_store(d_packed, d_scales, hi, lo, d_y, rows, cols, n_act, st) != cudaSuccess) return MLLM_ERR_CUDA;
   return MLLM_OK;
 }

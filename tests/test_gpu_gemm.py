@@ -22,7 +22,10 @@ def test_gemm_q4_matches_reference(rows, cols, cuda_ok):
     packed, sc = P.quant_q4(w)
     wd = P.dequant_q4(packed, sc).astype(np.float64)
     dp, ds = torch.from_numpy(packed).cuda(), torch.from_numpy(sc).cuda()
-    for m in (1, 5, 9, 16, 67, 256):
+    # up to 16 rows: the mma.sync tile; 24, 40, 67, 256: tcgen05 token tiles of 32, 64 and 128; 1,024 rows
+    # of the (2560, 960) shape: 256-token tiles (the 128-token grid would exceed one wave of 148 CTAs)
+    ms = (1, 5, 9, 16, 24, 40, 67, 256) + ((1024,) if (rows, cols) == (2560, 960) else ())
+    for m in ms:
         if rows * m > 49152 * 16 and m > 16:
             continue
         x = rng.standard_normal((m, cols), dtype=np.float32)
