@@ -787,6 +787,7 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   if (const char* v = getenv("MLLM_LWE_ATTN_SPLIT")) e->lh.attn_split = atoi(v) ? 1 : 0;
   if (const char* v = getenv("MLLM_LWE_PDL")) e->lh.pdl = atoi(v);
   if (const char* v = getenv("MLLM_LWE_LM_WIDE")) e->lh.lm_wide = atoi(v);
+  if (const char* v = getenv("MLLM_LWE_LM_TC5")) e->lh.lm_tc5 = atoi(v);
   if (const char* v = getenv("MLLM_LWE_ROPE_EPI")) e->lh.rope_epi = atoi(v);
   if (const char* v = getenv("MLLM_LWE_W13_WIDE")) e->lh.w13_wide = atoi(v);
   e->tmax = 1024;

@@ -19,6 +19,7 @@
 #include "engine.cuh"
 #include "lwe.cuh"
 #include "q4mma.cuh"
+#include "tc5.cuh"
 
 namespace mllm {
 
@@ -247,7 +248,10 @@ __global__ void lwe_embed(const __grid_constant__ LweArgs a, int T, const float*
   }
 }
 
-// RMSNorm / LayerNorm of X[src[i]] (or X[i]) -> fp16 hi/lo rows i of xh/xl.  One CTA per row.
+// RMSNorm / LayerNorm of X[src[i]] (or X[i]) -> fp16 hi/lo rows i of xh/xl.  One CTA per row.  TILED
+// writes xh3/xl3 instead, in the 8-token-block layout the tcgen05 tile reads (tc5.cuh): element (i, k)
+// at ((k / 32) T8 + i / 8) 256 + ((k % 32) / 8) 64 + (i % 8) 8 + k % 8, T8 = ceil(T / 8).
+template <bool TILED>
 __global__ void lwe_norm_split(const __grid_constant__ LweArgs a, int T, const float* g, const int* src) {
   pdl_enter();
   if (a.skip && *a.skip) return;  // a finished speculative loop replays as no-ops
@@ -277,11 +281,15 @@ __global__ void lwe_norm_split(const __grid_constant__ LweArgs a, int T, const f
     s1 += red[0][w];
     s2 += red[1][w];
   }
-  __half* oh = a.xh + (size_t)i * a.ldx;
-  __half* ol = a.xl + (size_t)i * a.ldx;
+  __half* oh = TILED ? a.xh3 : a.xh + (size_t)i * a.ldx;
+  __half* ol = TILED ? a.xl3 : a.xl + (size_t)i * a.ldx;
+  const int T8 = (T + 7) / 8;
+  auto at = [&](int k) -> size_t {
+    return TILED ? (((size_t)(k >> 5) * T8 + (i >> 3)) * 256 + ((k >> 3) & 3) * 64 + (i & 7) * 8 + (k & 7)) : (size_t)k;
+  };
   if (md.arch == 0) {
     const float inv = 1.f / sqrtf(s2 / D + 1e-6f);  // engine/infer.js:134-143
-    for (int k = threadIdx.x; k < D; k += blockDim.x) split_hi_lo(x[k] * inv * g[k], oh[k], ol[k]);
+    for (int k = threadIdx.x; k < D; k += blockDim.x) split_hi_lo(x[k] * inv * g[k], oh[at(k)], ol[at(k)]);
   } else {
     const float mean = s1 / D;  // engine/infer.js:147-164 (second pass for the variance)
     float v = 0.f;
@@ -296,7 +304,8 @@ __global__ void lwe_norm_split(const __grid_constant__ LweArgs a, int T, const f
     v = 0.f;
     for (int w = 0; w < nw; ++w) v += red[0][w];
     const float inv = 1.f / sqrtf(v / D + 1e-5f);
-    for (int k = threadIdx.x; k < D; k += blockDim.x) split_hi_lo(fmaf((x[k] - mean) * inv, g[k], g[D + k]), oh[k], ol[k]);
+    for (int k = threadIdx.x; k < D; k += blockDim.x)
+      split_hi_lo(fmaf((x[k] - mean) * inv, g[k], g[D + k]), oh[at(k)], ol[at(k)]);
   }
 }
 
@@ -1282,6 +1291,91 @@ __global__ void lwe_argmax_reduce(const __grid_constant__ LweArgs a, int T, int 
   if (lane == 0) a.amax[t] = idx;
 }
 
+// lm_head + argmax partials on the tcgen05 tile (tc5.cuh) for many rows without logits (a batched decode
+// step): CTA (b, y) holds vocab rows 128 b .. + 127 against lm rows N y .. + N - 1 of the tiled final-norm
+// output (xh3 / xl3, lwe_norm_split<true>) and writes, per lm row, the best (value, index) over its 128
+// vocab rows to pval / pidx[b] (ties keep the lower index, as lwe_gemm_lm).  In each warp, a butterfly
+// of xor-shuffles folds 32 rows x 16 tokens down to one token per lane pair (16 shuffles for 16
+// tokens); the four warps of a column half then merge through shared memory.
+__device__ __forceinline__ bool lm_better(float ov, int oi, float v, int i) { return ov > v || (ov == v && oi < i); }
+template <int NV>
+__device__ __forceinline__ void lm_fold(float (&v)[16], int (&ix)[16], int o, int lane) {
+  const bool up = (lane & o) != 0;  // this lane keeps entries NV .. 2NV - 1, its partner 0 .. NV - 1
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float kv = up ? v[NV + i] : v[i], sv = up ? v[i] : v[NV + i];
+    const int ki = up ? ix[NV + i] : ix[i], si = up ? ix[i] : ix[NV + i];
+    const float ov = __shfl_xor_sync(0xffffffffu, sv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, si, o);
+    const bool take = lm_better(ov, oi, kv, ki);
+    v[i] = take ? ov : kv;
+    ix[i] = take ? oi : ki;
+  }
+}
+
+template <int N, int S>
+__global__ void __launch_bounds__(tc5::kTc5Threads + 64, 1) lwe_lm_tc5(const __grid_constant__ LweArgs a, int T) {
+  using namespace tc5;
+  static_assert(N >= 32, "two column halves of 16-token chunks");
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int V = a.m.vocab, K = a.m.D;
+  const int r0 = blockIdx.x * kTc5Rows, t0 = blockIdx.y * N;
+  // the copy thread waits for the final norm (griddepcontrol.wait) before its first activation copy
+  const Tc5Acc acc = tc5_tile<N, S>(reinterpret_cast<const uint8_t*>(a.m.lm.w), a.m.lm.s, a.xh3, a.xl3, V, K,
+                                    (T + 7) / 8, r0, t0, smem, true, a.err);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* bv = reinterpret_cast<float*>(smem);  // [4 row quarters][N] (the stages are idle now)
+  int* bi = reinterpret_cast<int*>(bv + 4 * N);
+  if (acc.ok && warp < kTc5Threads / 32) {
+    const int cbeg = (warp >> 2) * (N / 2), q = warp & 3;
+    const int row = r0 + q * 32 + lane;
+    // the token of the 16-chunk this lane holds after the folds
+    const int tk = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+    for (int c0 = cbeg; c0 < cbeg + N / 2; c0 += 16) {
+      float v[16];
+      int ix[16];
+      tc5_cols16<N>(acc, warp, c0, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        ix[i] = row < V ? row : 0x7fffffff;
+        if (row >= V) v[i] = -INFINITY;
+      }
+      lm_fold<8>(v, ix, 16, lane);
+      lm_fold<4>(v, ix, 8, lane);
+      lm_fold<2>(v, ix, 4, lane);
+      lm_fold<1>(v, ix, 2, lane);
+      const float ov = __shfl_xor_sync(0xffffffffu, v[0], 1);
+      const int oi = __shfl_xor_sync(0xffffffffu, ix[0], 1);
+      if (lm_better(ov, oi, v[0], ix[0])) {
+        v[0] = ov;
+        ix[0] = oi;
+      }
+      if ((lane & 1) == 0) {
+        bv[q * N + c0 + tk] = v[0];
+        bi[q * N + c0 + tk] = ix[0];
+      }
+    }
+  }
+  __syncthreads();
+  if (acc.ok) {
+    for (int c = threadIdx.x; c < N; c += blockDim.x) {
+      const int t = t0 + c;
+      if (t >= T) continue;
+      float v = bv[c];
+      int ix = bi[c];
+#pragma unroll
+      for (int q = 1; q < 4; ++q)
+        if (lm_better(bv[q * N + c], bi[q * N + c], v, ix)) {
+          v = bv[q * N + c];
+          ix = bi[q * N + c];
+        }
+      a.pval[(size_t)blockIdx.x * a.lm_cap + t] = v;
+      a.pidx[(size_t)blockIdx.x * a.lm_cap + t] = ix;
+    }
+  }
+  tc5_release<N>(acc);
+}
+
 // One greedy step of the replicated multi-sequence decode for every active slot: record the new id,
 // apply the stop rules of engine/infer.js:617-639 and advance token and position.
 __global__ void lwe_decode_advance(const __grid_constant__ LweArgs a, int T, int max_new, int eos,
@@ -1483,6 +1577,22 @@ static bool launch_lm_wide(const LweArgs& a, int T, cudaStream_t st, int* nblk) 
          try_lm_wide<4, 2>(a, T, st, sms, nblk) || try_lm_wide<2, 2>(a, T, st, sms, nblk);
 }
 
+// lm_head on the tcgen05 tile: the final norm writes the tiled halves, then one CTA per 128 vocab rows
+// and N lm rows; the partials are one per vocab tile.
+static bool g_lm_tc5_ok = false;  // shared-memory attributes granted (lwe_setup)
+static void launch_lm_tc5(const LweArgs& a, int T, const float* norm_f, const int* src, cudaStream_t st, int* nblk) {
+  lwe_launch(lwe_norm_split<true>, dim3(T), dim3(128), 0, st, a, T, norm_f, src);
+  const int tiles = (a.m.vocab + tc5::kTc5Rows - 1) / tc5::kTc5Rows;
+  constexpr int kThreads = tc5::kTc5Threads + 64;
+  if (T > 128)
+    lwe_launch(lwe_lm_tc5<256, 4>, dim3(tiles, (T + 255) / 256), dim3(kThreads), tc5::tc5_smem_bytes<256, 4>(), st, a,
+               T);
+  else
+    lwe_launch(lwe_lm_tc5<128, 6>, dim3(tiles, (T + 127) / 128), dim3(kThreads), tc5::tc5_smem_bytes<128, 6>(), st,
+               a, T);
+  *nblk = tiles;
+}
+
 // Wide w1/w3 GEMM for long forwards (K must fit the 64-token tile; else the per-tile GEMM).
 static bool launch_w13_wide(const LweArgs& a, int T, int l, cudaStream_t st) {
   using C = LmWide<8, 3>;
@@ -1516,6 +1626,9 @@ cudaError_t lwe_setup(int kv_len) {
     else
       (void)cudaGetLastError();
   }
+  g_lm_tc5_ok = smem_attr(lwe_lm_tc5<256, 4>, (int)tc5::tc5_smem_bytes<256, 4>()) == cudaSuccess &&
+                smem_attr(lwe_lm_tc5<128, 6>, (int)tc5::tc5_smem_bytes<128, 6>()) == cudaSuccess;
+  if (!g_lm_tc5_ok) (void)cudaGetLastError();
   cudaError_t e = gemm_attrs<2>();
   if (e == cudaSuccess) e = gemm_attrs<4>();
   if (e == cudaSuccess) e = gemm_attrs<8>();
@@ -1567,7 +1680,7 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
       LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.D, T, a, T, L.proj, L.proj_b, md.D, L.norm2, a.xh3, a.xl3, a.ldx);
     } else {
       LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.D, T, a, T, L.proj, L.proj_b, md.D, nullptr, nullptr, nullptr, 0);
-      lwe_launch(lwe_norm_split, dim3(T), dim3(128), 0, st, a, T, L.norm2, (const int*)nullptr);
+      lwe_launch(lwe_norm_split<false>, dim3(T), dim3(128), 0, st, a, T, L.norm2, (const int*)nullptr);
     }
     if (md.arch == 0) {
       // long forwards (prefill chunks): the persistent wide GEMM, activations read once per CTA
@@ -1586,17 +1699,22 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
     } else {
       LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.FF, T, b, T, L.w2, L.mproj_b, md.FF, nullptr, nullptr, nullptr, 0);
       if (ng) {
-        lwe_launch(lwe_norm_split, dim3(T), dim3(128), 0, st, a, T, ng, (const int*)nullptr);
+        lwe_launch(lwe_norm_split<false>, dim3(T), dim3(128), 0, st, a, T, ng, (const int*)nullptr);
       }
     }
   }
   if (lm_T > 0) {
-    lwe_launch(lwe_norm_split, dim3(lm_T), dim3(128), 0, st, a, lm_T, md.norm_f,
-               (const int*)(lm_from_src ? a.lm_src : nullptr));
-    // many rows without logits (a batched decode step): the persistent wide GEMM, one partial per CTA
+    const int* src = lm_from_src ? a.lm_src : nullptr;
     int nblk = (md.vocab + kGemmRows - 1) / kGemmRows;
-    if (!(logits == nullptr && lm_T >= kLmWideRows && h.lm_wide && launch_lm_wide(a, lm_T, st, &nblk)))
-      LWE_GEMM_LM(md.vocab, lm_T, a, lm_T, logits);
+    if (logits == nullptr && lm_T >= kLmWideRows && h.lm_tc5 && g_lm_tc5_ok && !a.skip) {
+      // many rows without logits (a batched decode step): the tcgen05 tile, one partial per vocab tile
+      launch_lm_tc5(a, lm_T, md.norm_f, src, st, &nblk);
+    } else {
+      lwe_launch(lwe_norm_split<false>, dim3(lm_T), dim3(128), 0, st, a, lm_T, md.norm_f, src);
+      // the same without tcgen05: the persistent wide GEMM, one partial per CTA
+      if (!(logits == nullptr && lm_T >= kLmWideRows && h.lm_wide && launch_lm_wide(a, lm_T, st, &nblk)))
+        LWE_GEMM_LM(md.vocab, lm_T, a, lm_T, logits);
+    }
     lwe_launch(lwe_argmax_reduce, dim3((lm_T + 3) / 4), dim3(128), 0, st, a, lm_T, nblk);
   }
   return cudaGetLastError();

@@ -58,6 +58,7 @@ struct LweHost {
   int fold_norm = 1;   // llama RMSNorm folded into the GEMM epilogues (MLLM_LWE_FOLD_NORM=0: norm kernels)
   int pdl = 1;         // programmatic dependent launch between the forward's kernels (MLLM_LWE_PDL=0: off)
   int lm_wide = 1;     // persistent lm_head GEMM for many rows without logits (MLLM_LWE_LM_WIDE=0: off)
+  int lm_tc5 = 1;      // the same on the tcgen05 tile, ahead of lm_wide (MLLM_LWE_LM_TC5=0: off)
   int w13_wide = 1;    // persistent w1/w3 GEMM for long forwards (MLLM_LWE_W13_WIDE=0: off)
   int rope_epi = 1;    // RoPE + K/V cache rows in the QKV GEMM epilogue (MLLM_LWE_ROPE_EPI=0: lwe_rope_kv)
 };

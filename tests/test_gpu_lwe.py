@@ -74,26 +74,28 @@ def test_batch_matches_per_sequence_oracle(batch_models, name):
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", ["tiny-llama", "ref-llama"])
 def test_batch_wide_lm_head(cuda_ok, name):
-    """96 sequences take the persistent lm_head GEMM (>= 64 rows, no logits): two token tiles, the
-    second partial; ref-llama's 96-id vocab also ends in a partial row tile.  Every sequence equals the
-    oracle, and the engine without the wide GEMM (MLLM_LWE_LM_WIDE=0)."""
+    """96 sequences (>= 64 lm rows, no logits) take the lm_head on the tcgen05 tile: one 128-token tile
+    holding 96 rows (12 blocks of 8); ref-llama's 96-id vocab also ends in a partial row tile.  Every
+    sequence equals the oracle, the persistent mma.sync GEMM (MLLM_LWE_LM_TC5=0; two token tiles, the
+    second partial) and the per-tile GEMM (both off)."""
     data = _data(name)
     om = O.OracleModel(data)
-    eng = _engine(data, max_slots=96)
-    ref_eng = _engine(data, env={"MLLM_LWE_LM_WIDE": "0"}, max_slots=96)
+    engs = [_engine(data, max_slots=96),
+            _engine(data, env={"MLLM_LWE_LM_TC5": "0"}, max_slots=96),
+            _engine(data, env={"MLLM_LWE_LM_TC5": "0", "MLLM_LWE_LM_WIDE": "0"}, max_slots=96)]
     try:
-        V = eng.cfg["vocabSize"]
+        V = engs[0].cfg["vocabSize"]
         seqs = _prompts(V, [1 + (7 * i) % 23 for i in range(96)], 300)
-        res, st = eng.generateBatch(seqs, maxNewTokens=12, eosId=-1)
-        res0, _ = ref_eng.generateBatch(seqs, maxNewTokens=12, eosId=-1)
-        assert st["nSeq"] == 96
-        for i, (q, r, r0) in enumerate(zip(seqs, res, res0)):
-            assert r["generatedIds"] == r0["generatedIds"], i
+        runs = [e.generateBatch(seqs, maxNewTokens=12, eosId=-1) for e in engs]
+        assert runs[0][1]["nSeq"] == 96
+        for i, q in enumerate(seqs):
+            ids = [r[0][i]["generatedIds"] for r in runs]
+            assert ids[0] == ids[1] == ids[2], i
             if i % 8 == 0:  # the oracle on every eighth sequence
-                assert r["generatedIds"] == om.generate(q, 12, eos=-1)["generatedIds"], i
+                assert ids[0] == om.generate(q, 12, eos=-1)["generatedIds"], i
     finally:
-        eng.destroy()
-        ref_eng.destroy()
+        for e in engs:
+            e.destroy()
 
 
 @pytest.mark.gpu
