@@ -26,7 +26,7 @@ CUFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-rela
 if os.environ.get("MLLM_FAST_BUILD"):  # development: only the PetitGPT-shape instantiation
     CUFLAGS += ["-DMLLM_FAST_BUILD"]
 SOURCES = ["engine.cu", "decode.cu", "decode1.cu", "cdec.cu", "gemv.cu", "gemm.cu", "gemm_tc5.cu", "lwe.cu", "pgw.cpp"]
-HEADERS = ["cdec.cuh", "device_common.cuh", "engine.cuh", "lwe.cuh", "pgw.hpp", "q4mma.cuh"]
+HEADERS = ["cdec.cuh", "device_common.cuh", "engine.cuh", "lwe.cuh", "pgw.hpp", "q4mma.cuh", "tc5.cuh"]
 
 
 def _stale(target: str, deps) -> bool:

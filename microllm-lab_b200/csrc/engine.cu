@@ -796,7 +796,7 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   if (lwe_setup(md.kv_len) != cudaSuccess) return bad(MLLM_ERR_CUDA, "cudaFuncSetAttribute failed (token-batch kernels)");
   {
     LweArgs& w = e->lw;
-    const size_t T = e->tmax;
+    const size_t T = (e->tmax + 7) & ~7;  // whole 8-token blocks: the tiled halves of the tcgen05 lm_head
     auto r64 = [](int n) { return (n + 63) & ~63; };
     w.ldx = r64(std::max(D, md.NH * kHeadDim));
     w.ldx2 = r64(FF);
