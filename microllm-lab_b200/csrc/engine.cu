@@ -788,6 +788,7 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
   if (const char* v = getenv("MLLM_LWE_PDL")) e->lh.pdl = atoi(v);
   if (const char* v = getenv("MLLM_LWE_LM_WIDE")) e->lh.lm_wide = atoi(v);
   if (const char* v = getenv("MLLM_LWE_LM_TC5")) e->lh.lm_tc5 = atoi(v);
+  if (const char* v = getenv("MLLM_LWE_GEMM_TC5")) e->lh.gemm_tc5 = atoi(v);
   if (const char* v = getenv("MLLM_LWE_ROPE_EPI")) e->lh.rope_epi = atoi(v);
   if (const char* v = getenv("MLLM_LWE_W13_WIDE")) e->lh.w13_wide = atoi(v);
   e->tmax = 1024;
@@ -818,7 +819,7 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
         (rc = dev_alloc(E, &w.xl, T * w.ldx * 2)) || (rc = dev_alloc(E, &w.xh2, T * w.ldx2 * 2)) ||
         (rc = dev_alloc(E, &w.xl2, T * w.ldx2 * 2)) || (rc = dev_alloc(E, &w.qkv, T * md.QKV * 4)) ||
         (rc = dev_alloc(E, &w.xh3, T * w.ldx * 2)) || (rc = dev_alloc(E, &w.xl3, T * w.ldx * 2)) ||
-        (rc = dev_alloc(E, &w.ss, T * kLweSsStride * 4)) || (rc = dev_alloc(E, &w.skws, kLweSplitKBytes)) ||
+        (rc = dev_alloc(E, &w.ss, T * kLweSsStride * 4)) || (rc = dev_alloc(E, &w.skws, kLweSkwsBytes)) ||
         (rc = dev_alloc(E, &w.skctr, kLweSplitKTiles * sizeof(int))) ||
         (rc = dev_alloc(E, &w.tok, T * 4)) || (rc = dev_alloc(E, &w.slot, T * 4)) || (rc = dev_alloc(E, &w.pos, T * 4)) ||
         (rc = dev_alloc(E, &w.lm_src, T * 4)) || (rc = dev_alloc(E, &w.amax, T * 4)) ||

@@ -47,8 +47,8 @@ __global__ void __launch_bounds__(kTc5Threads + 64, 1) gemm_tc5_kernel(const uin
   tc5_release<N>(acc);
 }
 
-// f32 [T][K] -> the tiled fp16 hi / lo halves gemm_tc5_kernel reads: 16-byte chunk i (8 halves) holds
-// token 8 t8 + n8, columns 32 g + 8 c .. + 7 with i = ((g T8 + t8) 4 + c) 8 + n8.  Tokens past T are 0.
+// f32 [T][K] -> the tiled fp16 hi / lo halves gemm_tc5_kernel reads (tiled_at): thread i converts token
+// 8 t8 + n8, columns 32 g + 8 c .. + 7 with i = ((g T8 + t8) 4 + c) 8 + n8.  Tokens past T are 0.
 __global__ void split_tiled_kernel(const float* __restrict__ x, __half* __restrict__ hi, __half* __restrict__ lo,
                                    int T, int K, int T8, bool vec) {
   const size_t n = (size_t)T8 * 8 * (K / 8);
@@ -78,8 +78,9 @@ __global__ void split_tiled_kernel(const float* __restrict__ x, __half* __restri
       const float2 hf = __half22float2(h[j]);
       l[j] = __floats2half2_rn(v[2 * j] - hf.x, v[2 * j + 1] - hf.y);
     }
-    *reinterpret_cast<uint4*>(hi + 8 * i) = *reinterpret_cast<const uint4*>(h);
-    *reinterpret_cast<uint4*>(lo + 8 * i) = *reinterpret_cast<const uint4*>(l);
+    const size_t o = tiled_at(t, 32 * g + 8 * c, T8);  // the chunk's place in its swizzled block
+    *reinterpret_cast<uint4*>(hi + o) = *reinterpret_cast<const uint4*>(h);
+    *reinterpret_cast<uint4*>(lo + o) = *reinterpret_cast<const uint4*>(l);
   }
 }
 

@@ -121,6 +121,12 @@ __device__ __forceinline__ bool lwe_splitk(const LweArgs& a, float (&acc)[TBW][4
   return true;
 }
 
+// Offset of activation element (t, k) in a GEMM-input buffer: row-major [T][ld], or the tiled layout of
+// the tcgen05 tile (tc5::tiled_at) when the forward runs its GEMMs there (a.tiled).
+__device__ __forceinline__ size_t act_off(const LweArgs& a, int T, int t, int k, int ld) {
+  return a.tiled ? tc5::tiled_at(t, k, (T + 7) >> 3) : (size_t)t * ld + k;
+}
+
 // Element-wise epilogue over a 64-row tile (threads of the first warp group): epi(row, token, value).
 template <int TBW, class Epi>
 __device__ __forceinline__ void lwe_tile_epi(const float (&acc)[TBW][4], int r0, int t0, int R, int T, Epi epi) {
@@ -236,7 +242,8 @@ __global__ void lwe_embed(const __grid_constant__ LweArgs a, int T, const float*
         for (int k = threadIdx.x; k < D; k += 32) {
           const float v = __ldcg(x + k);
           s2 = fmaf(v, v, s2);
-          split_hi_lo(v * g[k], oh[k], ol[k]);
+          const size_t o = act_off(a, T, t, k, a.ldx);
+          split_hi_lo(v * g[k], a.xh[o], a.xl[o]);
         }
         s2 = warp_sum(s2);
         const int nt = (D + kGemmRows - 1) / kGemmRows;
@@ -249,8 +256,7 @@ __global__ void lwe_embed(const __grid_constant__ LweArgs a, int T, const float*
 }
 
 // RMSNorm / LayerNorm of X[src[i]] (or X[i]) -> fp16 hi/lo rows i of xh/xl.  One CTA per row.  TILED
-// writes xh3/xl3 instead, in the 8-token-block layout the tcgen05 tile reads (tc5.cuh): element (i, k)
-// at ((k / 32) T8 + i / 8) 256 + ((k % 32) / 8) 64 + (i % 8) 8 + k % 8, T8 = ceil(T / 8).
+// writes xh3/xl3 instead, in the 8-token-block layout the tcgen05 tile reads (tc5::tiled_at).
 template <bool TILED>
 __global__ void lwe_norm_split(const __grid_constant__ LweArgs a, int T, const float* g, const int* src) {
   pdl_enter();
@@ -284,9 +290,7 @@ __global__ void lwe_norm_split(const __grid_constant__ LweArgs a, int T, const f
   __half* oh = TILED ? a.xh3 : a.xh + (size_t)i * a.ldx;
   __half* ol = TILED ? a.xl3 : a.xl + (size_t)i * a.ldx;
   const int T8 = (T + 7) / 8;
-  auto at = [&](int k) -> size_t {
-    return TILED ? (((size_t)(k >> 5) * T8 + (i >> 3)) * 256 + ((k >> 3) & 3) * 64 + (i & 7) * 8 + (k & 7)) : (size_t)k;
-  };
+  auto at = [&](int k) -> size_t { return TILED ? tc5::tiled_at(i, k, T8) : (size_t)k; };
   if (md.arch == 0) {
     const float inv = 1.f / sqrtf(s2 / D + 1e-6f);  // engine/infer.js:134-143
     for (int k = threadIdx.x; k < D; k += blockDim.x) split_hi_lo(x[k] * inv * g[k], oh[at(k)], ol[at(k)]);
@@ -541,7 +545,7 @@ __global__ void __launch_bounds__(kAttnThreads) lwe_attention(const __grid_const
     float r = 0.f;
 #pragma unroll
     for (int q = 0; q < kAttnLanes; ++q) r += red[(q * REP + h) * 64 + d];
-    const size_t off = (size_t)t * a.ldx + (g * REP + h) * 64 + d;
+    const size_t off = act_off(a, T, t, (g * REP + h) * 64 + d, a.ldx);
     split_hi_lo(r * inv_sum[h], a.xh[off], a.xl[off]);
   }
 }
@@ -721,7 +725,7 @@ __global__ void __launch_bounds__(64) lwe_attn_split(const __grid_constant__ Lwe
       L = fmaf(__ldcg(pq + 1), f, L);
       O = fmaf(__ldcg(pq + 2 + d), f, O);
     }
-    const size_t off = (size_t)t * a.ldx + (g * REP + h) * 64 + d;
+    const size_t off = act_off(a, T, t, (g * REP + h) * 64 + d, a.ldx);
     split_hi_lo(O / L, a.xh[off], a.xl[off]);
   }
 }
@@ -1376,6 +1380,175 @@ __global__ void __launch_bounds__(tc5::kTc5Threads + 64, 1) lwe_lm_tc5(const __g
   tc5_release<N>(acc);
 }
 
+// ---------------------------------------------------------------------------------------------
+// Layer GEMMs of a llama forward on the tcgen05 tile (tc5.cuh, resident form).
+// grid (row tiles, ceil(T / N), kz): CTA (b, y, z) multiplies 128 tile rows by tokens N y .. N y + N - 1
+// over its share of the K groups (split-K when kz > 1: each CTA leaves its fp32 partial tile in
+// a.skws, the last one of a tile (counter a.skctr) adds them in split order and runs the epilogue).
+//   kTc5Qkv:   qkv[t][r] = acc / RMS_t + bias[r]                                (lwe_gemm_qkv, no RoPE)
+//   kTc5Resid: x[t][r] += acc + bias[r]; with gn the next norm's x * gn as tiled fp16 hi/lo in nh/nl and
+//              the 64-row halves' sums of squares of x in a.ss                   (lwe_gemm_resid)
+//   kTc5W13:   w1/w3 pairs (Tc5Paired), xh2/xl2 tiled = SiLU(u / RMS) (v / RMS)  (lwe_gemm_w13)
+// Every thread waits for the previous kernel (griddepcontrol.wait) before the epilogue touches a buffer
+// another kernel writes; the producers only read weights before it.
+enum Tc5Epi { kTc5Qkv = 0, kTc5Resid = 1, kTc5W13 = 2 };
+
+// The 16 values of a lane (one tile row, 16 tokens) summed over the warp's 32 rows by a butterfly of
+// xor-shuffles, in a fixed order: afterwards lanes 2i and 2i + 1 hold the sum of value
+// tc5_fold_token(2i).
+__device__ __forceinline__ float tc5_fold_sum(float (&v)[16], int lane) {
+#pragma unroll
+  for (int o = 16, nv = 8; o >= 2; o >>= 1, nv >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i >= nv) break;
+      const float keep = up ? v[nv + i] : v[i], send = up ? v[i] : v[nv + i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+__device__ __forceinline__ int tc5_fold_token(int lane) {
+  return ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+}
+
+template <int N, int S, int EPI>
+__global__ void __launch_bounds__(tc5::kTc5Threads + 64, 1)
+    lwe_tc5_gemm(const __grid_constant__ LweArgs a, int T, Q4 w, Q4 w3, const float* bias, int R, int K,
+                 const __half* xh, const __half* xl, const float* gn, __half* nh, __half* nl) {
+  using namespace tc5;
+  static_assert(N >= 32 && N % 32 == 0, "two column halves of 16-token chunks");
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ float sinv[N];
+  __shared__ float ssq[4][N];
+  __shared__ int last;
+  const int NG = K / 32, kz = gridDim.z, z = blockIdx.z;
+  const int ngz = (NG + kz - 1) / kz, g0 = z * ngz, ng = min(ngz, NG - g0);
+  const int t0 = blockIdx.y * N, T8 = (T + 7) / 8;
+  // the tokens' 1/RMS (from the previous kernel's sums of squares), staged by the copy warp's spare
+  // lanes while the K loop runs
+  auto side = [&](int lane) {
+    if (EPI != kTc5Resid)
+      for (int i = lane - 1; i < N; i += 31) sinv[i] = t0 + i < T ? fold_inv(a, t0 + i) : 1.f;
+  };
+  Tc5Acc acc;
+  if constexpr (EPI == kTc5W13) {
+    const Tc5Paired rows{reinterpret_cast<const uint8_t*>(w.w), w.s, reinterpret_cast<const uint8_t*>(w3.w), w3.s,
+                         R, K, (int)blockIdx.x * 64};
+    acc = tc5_tile_rows<N, S, true>(rows, xh, xl, T8, t0, g0, ng, smem, true, a.err, side);
+  } else {
+    const Tc5Linear rows{reinterpret_cast<const uint8_t*>(w.w), w.s, R, K, (int)blockIdx.x * kTc5Rows};
+    acc = tc5_tile_rows<N, S, true>(rows, xh, xl, T8, t0, g0, ng, smem, true, a.err, side);
+  }
+  pdl_enter();  // the previous kernel's x, ss and activation buffers are complete
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool epi_warp = warp < kTc5Threads / 32;
+  const int q = warp & 3, cbeg = (warp >> 2) * (N / 2);
+  const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+  // split-K: this CTA's partial tile [N columns][128 rows] in the workspace, then the last CTA sums them
+  bool run = acc.ok;
+  if (kz > 1) {
+    float* mine = a.skws + ((size_t)tile * kz + z) * kTc5Rows * N;
+    if (acc.ok && epi_warp)
+      for (int c0 = cbeg; c0 < cbeg + N / 2; c0 += 16) {
+        float v[16];
+        tc5_cols16<N>(acc, warp, c0, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) __stcg(mine + (size_t)(c0 + i) * kTc5Rows + q * 32 + lane, v[i]);
+      }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const int done = atomicAdd(&a.skctr[tile], 1) + 1;
+      last = done == kz;
+      if (last) a.skctr[tile] = 0;
+    }
+    __syncthreads();
+    run = run && last;
+    if (run) __threadfence();
+  }
+  if (run && epi_warp) {
+    for (int c0 = cbeg; c0 < cbeg + N / 2; c0 += 16) {
+      float v[16];
+      if (kz > 1) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = 0.f;
+        for (int zz = 0; zz < kz; ++zz) {
+          const float* p = a.skws + ((size_t)tile * kz + zz) * kTc5Rows * N + q * 32 + lane;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] += __ldcg(p + (size_t)(c0 + i) * kTc5Rows);
+        }
+      } else {
+        tc5_cols16<N>(acc, warp, c0, v);
+      }
+      if constexpr (EPI == kTc5Qkv) {
+        const int r = blockIdx.x * kTc5Rows + q * 32 + lane;
+        if (r < R) {
+          const float b = bias ? bias[r] : 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int t = t0 + c0 + i;
+            if (t < T) {
+              const float y = v[i] * sinv[c0 + i];
+              a.qkv[(size_t)t * R + r] = bias ? y + b : y;
+            }
+          }
+        }
+      } else if constexpr (EPI == kTc5Resid) {
+        const int r = blockIdx.x * kTc5Rows + q * 32 + lane;
+        const float b = bias && r < R ? bias[r] : 0.f, gr = gn && r < R ? gn[r] : 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int t = t0 + c0 + i;
+          float sq = 0.f;
+          if (t < T && r < R) {
+            float* px = a.x + (size_t)t * R + r;
+            const float xn = *px + (bias ? v[i] + b : v[i]);
+            *px = xn;
+            if (gn) {
+              const size_t o = tiled_at(t, r, T8);
+              split_hi_lo(xn * gr, nh[o], nl[o]);
+              sq = xn * xn;
+            }
+          }
+          v[i] = sq;
+        }
+        if (gn) {
+          const float s2 = tc5_fold_sum(v, lane);
+          if ((lane & 1) == 0) ssq[q][c0 + tc5_fold_token(lane)] = s2;
+        }
+      } else {  // kTc5W13: lane j < 16 holds u of FF row f, lane j + 16 holds v of the same row
+        const bool up = lane >= 16;
+        const int f = blockIdx.x * 64 + 16 * q + (lane & 15);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float other = __shfl_xor_sync(0xffffffffu, up ? v[i] : v[8 + i], 16);
+          const int c = c0 + (up ? 8 + i : i), t = t0 + c;
+          const float iv = sinv[c];
+          const float u = (up ? other : v[i]) * iv, g = (up ? v[8 + i] : other) * iv;
+          if (t < T && f < R) {
+            const size_t o = tiled_at(t, f, T8);
+            split_hi_lo((u / (1.f + expf(-u))) * g, a.xh2[o], a.xl2[o]);
+          }
+        }
+      }
+    }
+  }
+  if (EPI == kTc5Resid && gn) {
+    __syncthreads();
+    if (run)
+      for (int i = tid; i < N; i += blockDim.x) {
+        const int t = t0 + i;
+        if (t >= T) continue;
+        float* ps = a.ss + (size_t)t * kLweSsStride + 2 * blockIdx.x;
+        ps[0] = ssq[0][i] + ssq[1][i];  // rows 0 .. 63 of the tile
+        if (2 * blockIdx.x + 1 < kLweSsStride) ps[1] = ssq[2][i] + ssq[3][i];
+      }
+  }
+  tc5_release<N>(acc);
+}
+
 // One greedy step of the replicated multi-sequence decode for every active slot: record the new id,
 // apply the stop rules of engine/infer.js:617-639 and advance token and position.
 __global__ void lwe_decode_advance(const __grid_constant__ LweArgs a, int T, int max_new, int eos,
@@ -1593,6 +1766,74 @@ static void launch_lm_tc5(const LweArgs& a, int T, const float* norm_f, const in
   *nblk = tiles;
 }
 
+// Layer GEMMs on the tcgen05 tile (lwe_tc5_gemm).  Tokens per CTA: 32 while that grid fits one wave of
+// the SMs or the 64-token tile's resident activations would not fit, else 64.  The K groups are split
+// over several CTAs as far as the resident activations need to fit, and further (up to 4) while the
+// grid stays within one wave and each CTA keeps >= 12 groups.
+constexpr int kTc5GemmStages = 3;
+static int g_tc5_gemm_cap = 0;  // dynamic shared memory granted to lwe_tc5_gemm (0: not set up)
+static int g_sms = 0;
+template <int N, int EPI>
+static void tc5_gemm_attr() {
+  if (smem_attr(lwe_tc5_gemm<N, kTc5GemmStages, EPI>, g_tc5_gemm_cap) != cudaSuccess) {
+    (void)cudaGetLastError();
+    g_tc5_gemm_cap = 0;
+  }
+}
+struct Tc5Shape {
+  int N, tt, kz, ngz;
+  size_t smem;
+};
+static bool tc5_gemm_shape(int T, int rtiles, int K, Tc5Shape* sh) {
+  using namespace tc5;
+  if (g_tc5_gemm_cap <= 0 || K % 32) return false;
+  const int NG = K / 32, sms = g_sms > 0 ? g_sms : 148;
+  // resident bytes (tc5_smem_resident): the stages, the per-row pads and the alignment slack, then per
+  // group N x 128 of activations, 16 x 128 of raw nibbles and 4 x 128 of scales
+  const int fixed = kTc5GemmStages * kTc5StageGroups * 2 * kTc5ABytes + kTc5Rows * 20 + 1024;
+  auto max_groups = [&](int n) {
+    return std::min(kTc5MaxGroups, (g_tc5_gemm_cap - fixed) / (n * 128 + kTc5Rows * 20));
+  };
+  // 64-token tiles only where the 32-token grid would take more than one wave and no K split is needed
+  const int N = (long)rtiles * ((T + 31) / 32) <= sms || NG > max_groups(64) ? 32 : 64;
+  const int tt = (T + N - 1) / N, tiles = rtiles * tt;
+  const int maxg = max_groups(N);
+  if (maxg < 1) return false;
+  int kz = (NG + maxg - 1) / maxg;
+  while (kz < 4 && (long)tiles * (kz + 1) <= sms && NG / (kz + 1) >= 12) ++kz;
+  const int ngz = (NG + kz - 1) / kz;
+  kz = (NG + ngz - 1) / ngz;  // every split keeps at least one group
+  if (kz > 1 && (tiles > kLweSplitKTiles || (size_t)tiles * kz * kTc5Rows * N * 4 > kLweSkwsBytes)) return false;
+  const size_t sm = tc5_smem_resident(N, kTc5GemmStages, ngz);
+  if (sm > (size_t)g_tc5_gemm_cap) return false;
+  *sh = Tc5Shape{N, tt, kz, ngz, sm};
+  return true;
+}
+// Whether every layer GEMM of a T-row llama forward has a tcgen05 shape (all of them must: the forward's
+// GEMM inputs are then tiled).
+static bool tc5_gemms_fit(const ModelDev& md, int T) {
+  Tc5Shape sh;
+  const int dt = (md.D + tc5::kTc5Rows - 1) / tc5::kTc5Rows;
+  return tc5_gemm_shape(T, (md.QKV + tc5::kTc5Rows - 1) / tc5::kTc5Rows, md.D, &sh) &&
+         tc5_gemm_shape(T, dt, md.D, &sh) && tc5_gemm_shape(T, (md.FF + 63) / 64, md.D, &sh) &&
+         tc5_gemm_shape(T, dt, md.FF, &sh);
+}
+template <int EPI>
+static void launch_tc5_gemm(const LweArgs& a, int T, int rtiles, int R, int K, Q4 w, Q4 w3, const float* bias,
+                            const __half* xh, const __half* xl, const float* gn, __half* nh, __half* nl,
+                            cudaStream_t st) {
+  Tc5Shape sh;
+  (void)tc5_gemm_shape(T, rtiles, K, &sh);  // tc5_gemms_fit checked it for the forward
+  const dim3 grid(rtiles, sh.tt, sh.kz), block(tc5::kTc5Threads + 64);
+  if (sh.N == 32)
+    lwe_launch(lwe_tc5_gemm<32, kTc5GemmStages, EPI>, grid, block, sh.smem, st, a, T, w, w3, bias, R, K, xh, xl, gn, nh,
+               nl);
+  else
+    lwe_launch(lwe_tc5_gemm<64, kTc5GemmStages, EPI>, grid, block, sh.smem, st, a, T, w, w3, bias, R, K, xh, xl, gn, nh,
+               nl);
+  lwe_debug_check("lwe_tc5_gemm", sh.N, EPI, rtiles, T, sh.kz, sh.smem);
+}
+
 // Wide w1/w3 GEMM for long forwards (K must fit the 64-token tile; else the per-tile GEMM).
 static bool launch_w13_wide(const LweArgs& a, int T, int l, cudaStream_t st) {
   using C = LmWide<8, 3>;
@@ -1626,6 +1867,19 @@ cudaError_t lwe_setup(int kv_len) {
     else
       (void)cudaGetLastError();
   }
+  {
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+    g_tc5_gemm_cap = optin - 4096;  // room for the kernel's static arrays
+    tc5_gemm_attr<32, kTc5Qkv>();
+    tc5_gemm_attr<32, kTc5Resid>();
+    tc5_gemm_attr<32, kTc5W13>();
+    tc5_gemm_attr<64, kTc5Qkv>();
+    tc5_gemm_attr<64, kTc5Resid>();
+    tc5_gemm_attr<64, kTc5W13>();
+  }
   g_lm_tc5_ok = smem_attr(lwe_lm_tc5<256, 4>, (int)tc5::tc5_smem_bytes<256, 4>()) == cudaSuccess &&
                 smem_attr(lwe_lm_tc5<128, 6>, (int)tc5::tc5_smem_bytes<128, 6>()) == cudaSuccess;
   if (!g_lm_tc5_ok) (void)cudaGetLastError();
@@ -1649,6 +1903,9 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
   // the consumers apply 1/RMS.  LayerNorm (GPT-2) keeps separate norm kernels.
   const bool fold = md.arch == 0 && h.fold_norm;
   a.fold = fold ? 1 : 0;
+  // llama forwards of many rows: every layer GEMM on the tcgen05 tile, GEMM inputs in the tiled layout
+  const bool tc = fold && h.gemm_tc5 && T >= kTc5GemmRows && !a.skip && tc5_gemms_fit(md, T);
+  a.tiled = tc ? 1 : 0;
   g_lwe_pdl = h.pdl != 0;
   lwe_launch(lwe_embed, dim3(T), dim3(128), 0, st, a, T, h.layers[0].norm1);  // + norm1 of layer 0
   for (int l = 0; l < nl; ++l) {
@@ -1658,7 +1915,13 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
     // lwe_rope_kv (the staged epilogue measured 2-3 % slower on 512- and 1,024-token prefill), and the
     // batched decode step's attention does them itself.
     const bool rope_epi = !one_per_slot && h.rope_epi && T <= kLweSplitAttnRows;
-    LWE_GEMM(lwe_gemm_qkv, kGemmRows, md.QKV, md.D, T, a, T, l, rope_epi ? 1 : 0);
+    const Q4 none{nullptr, nullptr};
+    const int dt = (md.D + tc5::kTc5Rows - 1) / tc5::kTc5Rows;
+    if (tc)
+      launch_tc5_gemm<kTc5Qkv>(a, T, (md.QKV + tc5::kTc5Rows - 1) / tc5::kTc5Rows, md.QKV, md.D, L.qkv, none, L.qkv_b,
+                               a.xh, a.xl, nullptr, nullptr, nullptr, st);
+    else
+      LWE_GEMM(lwe_gemm_qkv, kGemmRows, md.QKV, md.D, T, a, T, l, rope_epi ? 1 : 0);
     if (one_per_slot) {
       if (h.attn_split)
         launch_attention_split<true>(a, h, T, st);
@@ -1677,14 +1940,20 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
     if (fold) {
       n2.xh = a.xh3;
       n2.xl = a.xl3;
-      LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.D, T, a, T, L.proj, L.proj_b, md.D, L.norm2, a.xh3, a.xl3, a.ldx);
+      if (tc)
+        launch_tc5_gemm<kTc5Resid>(a, T, dt, md.D, md.D, L.proj, none, L.proj_b, a.xh, a.xl, L.norm2, a.xh3, a.xl3, st);
+      else
+        LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.D, T, a, T, L.proj, L.proj_b, md.D, L.norm2, a.xh3, a.xl3, a.ldx);
     } else {
       LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.D, T, a, T, L.proj, L.proj_b, md.D, nullptr, nullptr, nullptr, 0);
       lwe_launch(lwe_norm_split<false>, dim3(T), dim3(128), 0, st, a, T, L.norm2, (const int*)nullptr);
     }
     if (md.arch == 0) {
       // long forwards (prefill chunks): the persistent wide GEMM, activations read once per CTA
-      if (!(T >= kW13WideRows && h.w13_wide && launch_w13_wide(n2, T, l, st)))
+      if (tc)
+        launch_tc5_gemm<kTc5W13>(a, T, (md.FF + 63) / 64, md.FF, md.D, L.w1, L.w3, nullptr, a.xh3, a.xl3, nullptr,
+                                 nullptr, nullptr, st);
+      else if (!(T >= kW13WideRows && h.w13_wide && launch_w13_wide(n2, T, l, st)))
         LWE_GEMM(lwe_gemm_w13, 32, md.FF, md.D, T, n2, T, l);
     } else
       LWE_GEMM(lwe_gemm_fc, kGemmRows, md.FF, md.D, T, n2, T, l);
@@ -1695,7 +1964,10 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
     // w2 + residual; the next layer's norm1 -> xh
     const float* ng = l + 1 < nl ? h.layers[l + 1].norm1 : nullptr;
     if (fold) {
-      LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.FF, T, b, T, L.w2, L.mproj_b, md.FF, ng, a.xh, a.xl, a.ldx);
+      if (tc)
+        launch_tc5_gemm<kTc5Resid>(a, T, dt, md.D, md.FF, L.w2, none, L.mproj_b, a.xh2, a.xl2, ng, a.xh, a.xl, st);
+      else
+        LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.FF, T, b, T, L.w2, L.mproj_b, md.FF, ng, a.xh, a.xl, a.ldx);
     } else {
       LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.FF, T, b, T, L.w2, L.mproj_b, md.FF, nullptr, nullptr, nullptr, 0);
       if (ng) {

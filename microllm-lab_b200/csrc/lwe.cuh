@@ -26,6 +26,8 @@ struct LweArgs {
   __half* xl3;
   float* ss;              // [tmax][kLweSsStride] partial sums of squares of x per 64-row tile
   int fold;               // RMSNorm folded into the GEMMs for this forward
+  int tiled;              // the forward's GEMMs run on the tcgen05 tile: xh/xl, xh2/xl2 and xh3/xl3 hold
+                          // the tiled layout (tc5::tiled_at) instead of [tmax][ld] rows
   float* qkv;             // [tmax][QKV]
   int32_t* tok;           // [tmax] token ids
   int32_t* slot;          // [tmax] sequence slots
@@ -39,14 +41,16 @@ struct LweArgs {
   int32_t* lm_src;        // [lm_cap] token index of each lm row
   int* err;               // device error flag: 2 = a token id out of range
   const int* skip;        // when set and *skip != 0 every kernel of the forward returns at once
-  float* skws;            // split-K partial tiles [kLweSplitKBytes]
+  float* skws;            // split-K partial tiles [kLweSkwsBytes]
   int* skctr;             // [kLweSplitKTiles] zeroed split-K tile counters
 };
-constexpr size_t kLweSplitKBytes = size_t(8) << 20;
+constexpr size_t kLweSplitKBytes = size_t(8) << 20;   // split-K partials of the mma.sync GEMMs
+constexpr size_t kLweSkwsBytes = size_t(32) << 20;    // the workspace (the tcgen05 GEMMs use all of it)
 constexpr int kLmWideRows = 64;  // lm rows from which the persistent lm_head GEMM is used
 constexpr int kW13WideRows = 512;  // token rows from which the persistent w1/w3 GEMM is used
 constexpr int kLweSplitAttnRows = 16;  // forwards of at most this many tokens use the position-split attention
 constexpr int kLweSplitKTiles = 16384;
+constexpr int kTc5GemmRows = 32;  // token rows from which the layer GEMMs run on the tcgen05 tile
 
 // Host-side copies of the per-layer descriptors the launches pass by value.
 struct LweHost {
@@ -59,6 +63,9 @@ struct LweHost {
   int pdl = 1;         // programmatic dependent launch between the forward's kernels (MLLM_LWE_PDL=0: off)
   int lm_wide = 1;     // persistent lm_head GEMM for many rows without logits (MLLM_LWE_LM_WIDE=0: off)
   int lm_tc5 = 1;      // the same on the tcgen05 tile, ahead of lm_wide (MLLM_LWE_LM_TC5=0: off)
+  int gemm_tc5 = 0;    // llama forwards of >= kTc5GemmRows rows: every layer GEMM on the tcgen05 tile
+                       // (MLLM_LWE_GEMM_TC5=1; off by default: measured slower than the mma.sync tiles
+                       // at these shapes)
   int w13_wide = 1;    // persistent w1/w3 GEMM for long forwards (MLLM_LWE_W13_WIDE=0: off)
   int rope_epi = 1;    // RoPE + K/V cache rows in the QKV GEMM epilogue (MLLM_LWE_ROPE_EPI=0: lwe_rope_kv)
 };

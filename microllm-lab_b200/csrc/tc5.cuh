@@ -1,16 +1,18 @@
 #pragma once
 // Q4 GEMM tile on the 5th-generation tensor cores (tcgen05.mma, accumulator in tensor memory):
 // acc[r][t] = W[r0 + r] . X[t0 + t] with W the PGW Q4 rows (engine/infer.js:88-116 per activation row),
-// shared by mllm_gemm_q4 (gemm_tc5.cu) and the batched lm_head + argmax (lwe.cu).
+// shared by mllm_gemm_q4 (gemm_tc5.cu), the batched lm_head + argmax and the layer GEMMs of long
+// token-batch forwards (lwe.cu).
 //
 // One CTA computes a 128-row x N-token tile with three roles and no CTA-wide barrier inside the K loop.
 //   - Eight producer warps walk the Q4 groups (32 columns).  Two threads dequantise each weight row's
-//     group into the stage's shared memory, then each arrives on the stage's full mbarrier.
-//   - One copy thread brings the stage's activation halves (N tokens x 32 columns, hi and lo) by two
-//     bulk copies counted on the same barrier (arrive.expect_tx).
+//     group into a stage of shared memory; each warp then arrives once on the stage's full mbarrier.
+//   - One copy thread brings the activation halves (N tokens x 32 columns, hi and lo) by bulk copies:
+//     per stage into a ring (counted on the stage's barrier), or (the resident form) every group at
+//     the start, counted on one barrier.
 //   - One MMA thread waits for a full stage, issues its MMAs and releases the stage with
-//     tcgen05.commit onto its empty mbarrier, which the producers and the copy thread wait for before
-//     they refill it S groups later.
+//     tcgen05.commit onto its empty mbarrier, which the producers (and in the ring form the copy thread)
+//     wait for before they refill it.
 //
 // Precision.  The group scale is folded into the weights, w = (q - 8) s 2^E.  The per-CTA 2^E puts the
 // tile's largest |w| near 2^14, so that the fp16 parts below stay normal.  The scale is split as
@@ -20,10 +22,10 @@
 // takes w_hi x_hi + w_hi x_lo + w_lo x_hi in fp32; the dropped w_lo x_lo term is below 2^-18 of each
 // product.  The epilogue scales by 2^-E (exact).
 //
-// Operand layout in shared memory (K-major, no swizzle, the UMMA canonical interleaved form): an 8-row x
-// 16-byte core matrix is 128 contiguous bytes; core matrices along K are kTc5Lbo bytes apart, along
-// M / N kTc5Sbo bytes apart, so element (row, k) of a 32-column stage sits at
-// (row / 8) kTc5Sbo + (k / 8) kTc5Lbo + (row % 8) 16 + (k % 8) 2.
+// Operand layout in shared memory (K-major, 64-byte swizzle): a row of a 32-column group is 64 bytes,
+// 8 rows form a 512-byte atom (kTc5Sbo apart along M / N), and the 16-byte chunk j of row r sits at
+// chunk position j ^ ((r / 2) % 4), so that the 8 rows of a core matrix fall into different banks.
+// Atoms start on 1024-byte boundaries of the shared window (the swizzle reads address bits 4-8).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -37,19 +39,30 @@ namespace tc5 {
 
 constexpr int kTc5Rows = 128;    // M: weight rows per CTA
 constexpr int kTc5Threads = 256;  // two threads per weight row in the dequantisation
-constexpr int kTc5Lbo = 128;     // bytes between core matrices along K
-constexpr int kTc5Sbo = 512;     // bytes between core matrices along M / N (4 along K per stage)
+constexpr int kTc5Sbo = 512;     // bytes between 8-row atoms along M / N (8 rows x 64 bytes)
 constexpr int kTc5ABytes = kTc5Rows * 32 * 2;  // one fp16 half of a stage's weights: 8 KB
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-// Shared-memory matrix descriptor (K-major, no swizzle, version 1).
+// Shared-memory matrix descriptor (K-major, 64-byte swizzle, version 1; the leading offset is unused for
+// a K extent of one swizzle width and set to 16 bytes).
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
   uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)((kTc5Lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)1 << 16;
   d |= (uint64_t)((kTc5Sbo >> 4) & 0x3FFF) << 32;
   d |= (uint64_t)1 << 46;
+  d |= (uint64_t)4 << 61;  // SWIZZLE_64B
   return d;
+}
+// Byte offset of 16-byte chunk j (columns 8 j .. 8 j + 7 of the group) of row r in a swizzled group.
+__host__ __device__ __forceinline__ int sw64_at(int r, int j) {
+  return (r >> 3) * kTc5Sbo + (r & 7) * 64 + ((j ^ ((r >> 1) & 3)) << 4);
+}
+// Tiled activation layout the tile reads (in halves): element (t, k) of a T-token x K-column array,
+// T8 = ceil(T / 8).  Group k / 32 holds T8 blocks of 8 tokens; a block is one swizzled 512-byte atom, so
+// that a bulk copy of whole blocks lands in shared memory in the operand layout.
+__host__ __device__ __forceinline__ size_t tiled_at(int t, int k, int T8) {
+  return ((size_t)(k >> 5) * T8 + (t >> 3)) * 256 + (sw64_at(t & 7, (k >> 3) & 3) >> 1) + (k & 7);
 }
 
 // Instruction descriptor of kind::f16: fp16 A and B (K-major), fp32 accumulator, M = 128, N.
@@ -110,11 +123,52 @@ __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, uint64_t
 }
 
 
-// Shared-memory bytes of the S-stage ring of tc5_tile<N, S>.
+// Shared-memory bytes of the S-stage ring of tc5_tile<N, S> (+ 1 KB to align the atoms).
 template <int N, int S>
 constexpr size_t tc5_smem_bytes() {
-  return (size_t)S * (2 * kTc5ABytes + 2 * N * 64);
+  return (size_t)S * (2 * kTc5ABytes + 2 * N * 64) + 1024;
 }
+
+// The resident form of the tile (tc5_tile_rows<N, S, true>): stages of kTc5StageGroups groups, and per
+// group the activation halves, the raw nibbles (16 bytes a row, one 16-byte pad per row) and the scales
+// of the tile's 128 rows, all in shared memory for the whole K loop.
+constexpr int kTc5StageGroups = 2;
+constexpr int kTc5MaxGroups = 64;  // K columns per CTA <= 2,048 in the resident form
+__host__ __device__ constexpr size_t tc5_smem_resident(int N, int S, int ng) {
+  return (size_t)S * kTc5StageGroups * 2 * kTc5ABytes + (size_t)ng * 2 * N * 64 + (size_t)kTc5Rows * 16 * (ng + 1) +
+         (size_t)kTc5Rows * 4 * (ng + 1) + 1024;
+}
+
+// Row sources of a tile: tile row lr (0 .. 127) -> its packed Q4 row and scales, false past the matrix.
+struct Tc5Linear {  // rows r0 .. r0 + 127 of an R x K matrix
+  const uint8_t* W;
+  const float* S;
+  int R, K, r0;
+  __device__ __forceinline__ bool row(int lr, const uint8_t*& w, const float*& s) const {
+    const int r = r0 + lr;
+    if (r >= R) return false;
+    w = W + (size_t)r * (K / 2);
+    s = S + (size_t)r * (K / 32);
+    return true;
+  }
+};
+// w1 / w3 pairs of 64 FF rows f0 .. f0 + 63: tile row 32 q + j is w1 row f0 + 16 q + j for j < 16 and
+// w3 row f0 + 16 q + j - 16 for j >= 16, so that lanes j and j + 16 of the warp that drains quarter q
+// hold the two products of one FF row.
+struct Tc5Paired {
+  const uint8_t* W1;
+  const float* S1;
+  const uint8_t* W3;
+  const float* S3;
+  int F, K, f0;
+  __device__ __forceinline__ bool row(int lr, const uint8_t*& w, const float*& s) const {
+    const int j = lr & 31, f = f0 + 16 * (lr >> 5) + (j & 15);
+    if (f >= F) return false;
+    w = (j < 16 ? W1 : W3) + (size_t)f * (K / 2);
+    s = (j < 16 ? S1 : S3) + (size_t)f * (K / 32);
+    return true;
+  }
+};
 
 // What the epilogue of a tile needs: the accumulator's tensor-memory address, the 2^-E scale, and
 // whether every wait of the tile finished in time (the same on every thread).
@@ -123,36 +177,54 @@ struct Tc5Acc {
   float down;
   bool ok;
 };
+struct Tc5NoSide {
+  __device__ __forceinline__ void operator()(int) const {}
+};
 
-// One 128-row x N-token tile, run by kTc5Threads + 64 threads (see the top of this file):
-// rows r0 .. r0 + 127 of the R x K Q4 matrix (W, Sc) against tokens t0 .. t0 + N - 1 of the tiled
-// activation halves xh / xl (T8 8-token blocks; see split_tiled_kernel).  smem holds
-// tc5_smem_bytes<N, S>() bytes.  With pdl the copy thread waits for the previous kernel
-// (griddepcontrol.wait) before its first activation copy; the weights need no wait.  A wait that runs
-// out its limit sets *err and turns ok false.  Every thread must then call tc5_release.
-template <int N, int S>
-__device__ __forceinline__ Tc5Acc tc5_tile(const uint8_t* __restrict__ W, const float* __restrict__ Sc,
-                                           const __half* __restrict__ xh, const __half* __restrict__ xl, int R, int K,
-                                           int T8, int r0, int t0, uint8_t* smem, bool pdl, int* err) {
-  constexpr int kB = N * 64;  // one fp16 half of a stage's activations
-  constexpr int kStage = 2 * kTc5ABytes + 2 * kB;
-  __shared__ __align__(8) uint64_t full[S], empty[S], done;
+// One 128-row x N-token tile over the Q4 groups g0 .. g0 + ng - 1, run by kTc5Threads + 64 threads
+// (see the top of this file): the tile rows of `rows` against tokens t0 .. t0 + N - 1 of the tiled
+// activation halves xh / xl (T8 8-token blocks, tiled_at).
+//   - Ring form (XRES false, tc5_smem_bytes<N, S>()): S one-group stages of weights and activations;
+//     each producer thread fetches its nibbles and scales kPD groups ahead into registers.
+//   - Resident form (XRES, tc5_smem_resident(N, S, ng), ng <= kTc5MaxGroups): every group's activation
+//     halves come in at the start on one barrier, the tile's raw Q4 rows by one bulk copy per row and
+//     its scales by one pass of loads; the producers dequantise kTc5StageGroups groups per stage from
+//     shared memory, so that a stage costs one wait and one arrival per warp for two groups.
+// With pdl the copy warp waits for the previous kernel (griddepcontrol.wait) before its activation
+// copies; the weights need no wait.  Lanes 1 .. 31 of the copy warp then run side(lane) during the K
+// loop: epilogue inputs that the previous kernel wrote can be staged there.  A wait that runs out its
+// limit sets *err and turns ok false.  Every thread must then call tc5_release.
+template <int N, int S, bool XRES, class Rows, class Side = Tc5NoSide>
+__device__ __forceinline__ Tc5Acc tc5_tile_rows(const Rows& rows, const __half* __restrict__ xh,
+                                                const __half* __restrict__ xl, int T8, int t0, int g0, int ng,
+                                                uint8_t* smem, bool pdl, int* err, const Side& side = Tc5NoSide{}) {
+  constexpr int kB = N * 64;                    // one fp16 half of a group's activations
+  constexpr int kPD = 8;                        // ring form: groups each producer thread requests ahead
+  constexpr int G = XRES ? kTc5StageGroups : 1;  // groups per stage
+  constexpr int kStageA = G * 2 * kTc5ABytes;   // a stage's weights: per group [w_hi 8 KB][w_lo 8 KB]
+  __shared__ __align__(8) uint64_t full[S], empty[S], done, xfull, wfull;
   __shared__ uint32_t tmem_base;
   __shared__ float smax[kTc5Threads / 32];
+  smem += (1024u - (su32(smem) & 1023u)) & 1023u;  // swizzle atoms on 1024-byte boundaries
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool producer = tid < kTc5Threads;
-  const int NG = K / 32;
   const int lr = (tid >> 1) & (kTc5Rows - 1), half = tid & 1;  // weight row of the tile, and which 16 columns
-  const int row = r0 + lr;
-  const bool row_ok = producer && row < R;
+  const uint8_t* wrow = nullptr;
+  const float* srow = nullptr;
+  const bool row_ok = producer && rows.row(lr, wrow, srow);
   const uint64_t limit = kWaitNs;
   // N <= 128: x_hi and x_lo (adjacent in shared memory, the same 512-byte stride) form one 2N-token B
   // operand, so w_hi (x_hi | x_lo) is one MMA and the epilogue adds column j + N to column j
   constexpr bool kMerge = N <= 128;
   constexpr int kAcc = kMerge ? 2 * N : N;
   constexpr uint32_t kCols = kAcc < 32 ? 32 : kAcc;  // tensor-memory columns (a power of 2 >= 32)
-  // activation bytes per stage: the 8-token blocks of this tile that exist (the last may be padding)
+  // activation bytes per group: the 8-token blocks of this tile that exist (the last may be padding)
   const uint32_t xbytes = (uint32_t)min(N / 8, T8 - t0 / 8) * 512u;
+  const int nst = (ng + G - 1) / G;  // stages of the K loop
+  uint8_t* const xs = smem + (size_t)S * kStageA;  // activations: S ring stages, or every group
+  const int rs = 16 * (ng + 1);                    // resident raw rows [128][rs] and scales [128][ng + 1]
+  uint8_t* const wraw = xs + (size_t)(XRES ? ng : S) * 2 * kB;
+  float* const sraw = reinterpret_cast<float*>(wraw + (size_t)kTc5Rows * rs);
 
   // ---- tensor memory for the accumulator (warp 0), barriers, the tile's power-of-two weight scale
   if (warp == 0) {
@@ -163,17 +235,64 @@ __device__ __forceinline__ Tc5Acc tc5_tile(const uint8_t* __restrict__ W, const 
   }
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      // every producer thread, plus the copy thread's arrival with the copies' byte count
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&full[s])), "r"(kTc5Threads + 1) : "memory");
+      // one arrival per producer warp, plus (ring form) the copy thread's arrival with the copies' bytes
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&full[s])),
+                   "r"(kTc5Threads / 32 + (XRES ? 0 : 1))
+                   : "memory");
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&empty[s])) : "memory");
     }
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&done)) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&xfull)) : "memory");
+    // one arrival per tile row (with the byte count of its copy when the row exists)
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&wfull)), "r"(kTc5Rows) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // ring form: this thread's nibbles and scales of the first kPD groups, requested before the scale
+  // pass so that both round trips overlap (volatile loads: issued where written)
+  uint2 q[kPD];
+  float sc[kPD];
+  auto fetch = [&](int c, uint2& qq, float& ss) {
+    qq = make_uint2(0x88888888u, 0x88888888u);
+    ss = 0.f;
+    if (row_ok && c < ng) {
+      const uint8_t* p = wrow + 16 * (g0 + c) + 8 * half;
+      asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(qq.x), "=r"(qq.y) : "l"(p));
+      ss = ldv_f32(srow + g0 + c);
+    }
+  };
   float m = 0.f;
-  if (row_ok) {
+  if constexpr (XRES) {
+    __syncthreads();  // the barriers are initialised
+    if (producer && half == 0) {  // the row's nibbles of groups g0 .. g0 + ng - 1: one bulk copy
+      const uint32_t wb = su32(&wfull);
+      if (row_ok) {
+        const uint32_t bytes = 16u * (uint32_t)ng;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(wb), "r"(bytes) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         su32(wraw + (size_t)lr * rs)),
+                     "l"(wrow + 16 * g0), "r"(bytes), "r"(wb)
+                     : "memory");
+      } else {
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(wb) : "memory");
+      }
+    }
+    if (producer) {
 #pragma unroll 8
-    for (int g = half; g < NG; g += 2) m = fmaxf(m, fabsf(__ldg(Sc + (size_t)row * NG + g)));
+      for (int g = half; g < ng; g += 2) {
+        const float v = row_ok ? __ldg(srow + g0 + g) : 0.f;
+        sraw[lr * (ng + 1) + g] = v;
+        m = fmaxf(m, fabsf(v));
+      }
+    }
+  } else {
+    if (producer) {
+#pragma unroll
+      for (int i = 0; i < kPD; ++i) fetch(i, q[i], sc[i]);
+    }
+    if (row_ok) {
+#pragma unroll 8
+      for (int g = half; g < ng; g += 2) m = fmaxf(m, fabsf(__ldg(srow + g0 + g)));
+    }
   }
   m = warp_max(m);
   if (lane == 0 && producer) smax[warp] = m;
@@ -190,113 +309,153 @@ __device__ __forceinline__ Tc5Acc tc5_tile(const uint8_t* __restrict__ W, const 
   bool ok = true;
 
   if (producer) {
-    const uint8_t* wrow = W + (size_t)row * (K / 2);
-    const float* srow = Sc + (size_t)row * NG;
-    // this thread's nibbles and scale of the next four groups, requested ahead so that the global-load
-    // latency overlaps the groups in between (rows past R hold weight 0)
-    uint2 q0, q1, q2, q3;
-    float s0, s1, s2, s3;
-    auto fetch = [&](int g, uint2& q, float& sc) {
-      q = make_uint2(0x88888888u, 0x88888888u);
-      sc = 0.f;
-      if (row_ok && g < NG) {
-        q = __ldg(reinterpret_cast<const uint2*>(wrow + 16 * g + 8 * half));
-        sc = __ldg(srow + g);
-      }
-    };
-    fetch(0, q0, s0);
-    fetch(1, q1, s1);
-    fetch(2, q2, s2);
-    fetch(3, q3, s3);
-    const int rb = (lr >> 3) * kTc5Sbo + (lr & 7) * 16 + 2 * half * kTc5Lbo;
-    for (int g = 0; g < NG; ++g) {
-      const int s = g % S;
-      // the MMAs that read this stage S groups ago are done
-      if (ok && g >= S && !bar_wait(su32(&empty[s]), ((g / S) - 1) & 1, limit)) {
-        atomicExch(err, 1);
-        ok = false;
-      }
-      uint8_t* st = smem + (size_t)s * kStage;
-      // weights: this thread's half (16 columns) of its row's group g.  The scale is split into
-      // sh (its top 8 significant bits) + sl; (q - 8) has at most 3 significant bits, so
-      // (q - 8) sh is exact in fp16 (the high half) and (q - 8) fl16(sl) carries the rest.
-      const uint2 q = q0;
-      const float sc = s0 * up;
-      q0 = q1;
-      s0 = s1;
-      q1 = q2;
-      s1 = s2;
-      q2 = q3;
-      s2 = s3;
-      fetch(g + 4, q3, s3);
-      const float sh = __uint_as_float(__float_as_uint(sc) & 0xFFFF0000u);
-      const float sl = sc - sh;
+    const int rb0 = sw64_at(lr, 2 * half), rb1 = sw64_at(lr, 2 * half + 1);  // this thread's two chunks
+    // weights: this thread's half (16 columns) of its row's group.  The scale is split into
+    // sh (its top 8 significant bits) + sl; (q - 8) has at most 3 significant bits, so
+    // (q - 8) sh is exact in fp16 (the high half) and (q - 8) fl16(sl) carries the rest.
+    auto dequant = [&](uint8_t* st, uint2 qc, float scale) {
+      const float sh = __uint_as_float(__float_as_uint(scale) & 0xFFFF0000u);
+      const float sl = scale - sh;
       const __half2 mh = __floats2half2_rn(sh, sh * 0.0625f), ml = __floats2half2_rn(sl, sl * 0.0625f);
-      const uint32_t qw[2] = {q.x, q.y};
+      const uint32_t qw[2] = {qc.x, qc.y};
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int cc = 0; cc < 2; ++cc) {
         __half2 hi[4], lo[4];
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-          const __half2 v = nib_pair(qw[c], (uint32_t)(p | (4 << 4) | (p << 8) | (4 << 12)));
+          const __half2 v = nib_pair(qw[cc], (uint32_t)(p | (4 << 4) | (p << 8) | (4 << 12)));
           hi[p] = __hmul2(v, mh);
           lo[p] = __hmul2(v, ml);
         }
-        *reinterpret_cast<uint4*>(st + rb + c * kTc5Lbo) = *reinterpret_cast<const uint4*>(hi);
-        *reinterpret_cast<uint4*>(st + kTc5ABytes + rb + c * kTc5Lbo) = *reinterpret_cast<const uint4*>(lo);
+        const int rb = cc ? rb1 : rb0;
+        *reinterpret_cast<uint4*>(st + rb) = *reinterpret_cast<const uint4*>(hi);
+        *reinterpret_cast<uint4*>(st + kTc5ABytes + rb) = *reinterpret_cast<const uint4*>(lo);
       }
-      // make this thread's weight writes visible to the tensor cores and mark them done
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&full[s])) : "memory");
-    }
-  } else if (warp == kTc5Threads / 32 + 1) {
-    // ---- the copy warp: per group, once the stage is free, the activation halves by two bulk copies
-    if (lane == 0) {
-      if (pdl) asm volatile("griddepcontrol.wait;" ::: "memory");  // the activations come from the previous kernel
-      for (int g = 0; g < NG; ++g) {
-        const int s = g % S;
-        if (ok && g >= S && !bar_wait(su32(&empty[s]), ((g / S) - 1) & 1, limit)) {
+    };
+    // the MMAs that read stage s one round ago are done (one lane waits for the warp)
+    auto stage_free = [&](int k, int s) {
+      if (k >= S) {
+        if (lane == 0 && ok && !bar_wait(su32(&empty[s]), ((k / S) - 1) & 1, limit)) {
           atomicExch(err, 1);
           ok = false;
         }
-        const uint32_t full_s = su32(&full[s]), st = su32(smem + (size_t)s * kStage);
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full_s), "r"(2u * xbytes)
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+      }
+    };
+    // make the warp's weight writes visible to the tensor cores, then one arrival for the warp
+    auto stage_full = [&](int s) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&full[s])) : "memory");
+    };
+    if constexpr (XRES) {
+      if (!bar_wait(su32(&wfull), 0, limit)) {  // the raw rows have landed (every thread observes it)
+        atomicExch(err, 1);
+        ok = false;
+      }
+      for (int k = 0; k < nst; ++k) {
+        const int s = k % S;
+        stage_free(k, s);
+        uint8_t* st = smem + (size_t)s * kStageA;
+#pragma unroll
+        for (int u = 0; u < G; ++u) {
+          const int c = G * k + u;
+          if (c >= ng) break;
+          dequant(st + u * 2 * kTc5ABytes, *reinterpret_cast<const uint2*>(wraw + (size_t)lr * rs + 16 * c + 8 * half),
+                  sraw[lr * (ng + 1) + c] * up);
+        }
+        stage_full(s);
+      }
+    } else {
+      // the nibbles and scales of group c + kPD are requested while group c is dequantised, so that the
+      // global-load latency overlaps the groups in between (rows past the matrix hold weight 0)
+      for (int cb = 0; cb < ng; cb += kPD) {
+#pragma unroll
+        for (int i = 0; i < kPD; ++i) {
+          const int c = cb + i;
+          if (c >= ng) break;
+          const int s = c % S;
+          stage_free(c, s);
+          const uint2 qc = q[i];
+          const float scale = sc[i] * up;
+          fetch(c + kPD, q[i], sc[i]);
+          dequant(smem + (size_t)s * kStageA, qc, scale);
+          stage_full(s);
+        }
+      }
+    }
+  } else if (warp == kTc5Threads / 32 + 1) {
+    // ---- the copy warp: the activation halves of each group by two bulk copies
+    if (lane != 0) {
+      if (pdl) asm volatile("griddepcontrol.wait;" ::: "memory");
+      side(lane);
+    } else {
+      if (pdl) asm volatile("griddepcontrol.wait;" ::: "memory");  // the activations come from the previous kernel
+      if constexpr (XRES)
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&xfull)),
+                     "r"(2u * xbytes * (uint32_t)ng)
                      : "memory");
-        const size_t src = ((size_t)g * T8 + t0 / 8) * 256;  // in halves
+      for (int c = 0; c < ng; ++c) {
+        uint32_t bar, dst;
+        if constexpr (XRES) {  // every group at once, all on one barrier
+          bar = su32(&xfull);
+          dst = su32(xs + (size_t)c * 2 * kB);
+        } else {  // a ring: wait until the MMAs of S groups ago released the stage
+          const int s = c % S;
+          if (ok && c >= S && !bar_wait(su32(&empty[s]), ((c / S) - 1) & 1, limit)) {
+            atomicExch(err, 1);
+            ok = false;
+          }
+          bar = su32(&full[s]);
+          dst = su32(xs + (size_t)s * 2 * kB);
+          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2u * xbytes) : "memory");
+        }
+        const size_t src = ((size_t)(g0 + c) * T8 + t0 / 8) * 256;  // in halves
         asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                         st + 2 * kTc5ABytes),
-                     "l"(xh + src), "r"(xbytes), "r"(full_s)
+                         dst),
+                     "l"(xh + src), "r"(xbytes), "r"(bar)
                      : "memory");
         asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                         st + 2 * kTc5ABytes + kB),
-                     "l"(xl + src), "r"(xbytes), "r"(full_s)
+                         dst + kB),
+                     "l"(xl + src), "r"(xbytes), "r"(bar)
                      : "memory");
       }
     }
   } else if (lane == 0) {
-    // ---- the MMA warp: per group, wait until full, issue w_hi x_hi + w_hi x_lo + w_lo x_hi, release
+    // ---- the MMA warp: per stage, wait until full, issue w_hi x_hi + w_hi x_lo + w_lo x_hi for each of
+    // its groups, release the stage
     const uint32_t idesc = idesc_f16(N), idesc2 = idesc_f16(kAcc);
-    for (int c = 0; c < NG && ok; ++c) {
-      const int s = c % S;
-      if (!bar_wait(su32(&full[s]), (c / S) & 1, limit)) {
+    if (XRES && !bar_wait(su32(&xfull), 0, limit)) {
+      atomicExch(err, 1);
+      ok = false;
+    }
+    for (int k = 0; k < nst && ok; ++k) {
+      const int s = k % S;
+      if (!bar_wait(su32(&full[s]), (k / S) & 1, limit)) {
         atomicExch(err, 1);
         ok = false;
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t st = su32(smem + (size_t)s * kStage);
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {  // two K = 16 steps of the group
-        const uint64_t ah = sdesc(st + j * 2 * kTc5Lbo), al = sdesc(st + kTc5ABytes + j * 2 * kTc5Lbo);
-        const uint64_t bh = sdesc(st + 2 * kTc5ABytes + j * 2 * kTc5Lbo);
-        const uint64_t bl = sdesc(st + 2 * kTc5ABytes + kB + j * 2 * kTc5Lbo);
-        if constexpr (kMerge) {
-          mma_f16(dtmem, ah, bh, idesc2, (c > 0 || j > 0) ? 1u : 0u);  // columns [0, N): x_hi, [N, 2N): x_lo
-          mma_f16(dtmem, al, bh, idesc, 1u);
-        } else {
-          mma_f16(dtmem, ah, bh, idesc, (c > 0 || j > 0) ? 1u : 0u);
-          mma_f16(dtmem, ah, bl, idesc, 1u);
-          mma_f16(dtmem, al, bh, idesc, 1u);
+      for (int u = 0; u < G; ++u) {
+        const int c = G * k + u;
+        if (c >= ng) break;
+        const uint32_t st = su32(smem + (size_t)s * kStageA + u * 2 * kTc5ABytes);
+        const uint32_t xb = su32(xs + (size_t)(XRES ? c : s) * 2 * kB);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {  // two K = 16 steps of the group: 32 bytes into each 64-byte row
+          const uint64_t ah = sdesc(st + j * 32), al = sdesc(st + kTc5ABytes + j * 32);
+          const uint64_t bh = sdesc(xb + j * 32);
+          const uint64_t bl = sdesc(xb + kB + j * 32);
+          if constexpr (kMerge) {
+            mma_f16(dtmem, ah, bh, idesc2, (c > 0 || j > 0) ? 1u : 0u);  // columns [0, N): x_hi, [N, 2N): x_lo
+            mma_f16(dtmem, al, bh, idesc, 1u);
+          } else {
+            mma_f16(dtmem, ah, bh, idesc, (c > 0 || j > 0) ? 1u : 0u);
+            mma_f16(dtmem, ah, bl, idesc, 1u);
+            mma_f16(dtmem, al, bh, idesc, 1u);
+          }
         }
       }
       mma_commit(su32(&empty[s]));
@@ -304,25 +463,39 @@ __device__ __forceinline__ Tc5Acc tc5_tile(const uint8_t* __restrict__ W, const 
     mma_commit(su32(&done));  // arrives once every MMA issued above has finished
   }
   __syncwarp();
-  // ---- epilogue: every MMA has finished
-  if (!bar_wait(su32(&done), 0, limit)) {
+  // ---- epilogue: every MMA has finished (one lane per warp waits)
+  if (lane == 0 && !bar_wait(su32(&done), 0, limit)) {
     atomicExch(err, 1);
     ok = false;
   }
   if (tid == kTc5Threads + 32) {
-    // no bulk copy of this CTA is left in flight: the last use of each stage has completed (at once,
-    // unless the MMA warp stopped early)
-    for (int s = 0; s < S && s < NG; ++s) {
-      const int gl = s + ((NG - 1 - s) / S) * S;
-      if (!bar_wait(su32(&full[s]), (gl / S) & 1, limit)) {
+    // no bulk copy of this CTA is left in flight (at once, unless a wait above ran out)
+    if constexpr (XRES) {
+      if (!bar_wait(su32(&xfull), 0, limit) || !bar_wait(su32(&wfull), 0, limit)) {
         atomicExch(err, 1);
         ok = false;
+      }
+    } else {
+      for (int s = 0; s < S && s < ng; ++s) {  // the last use of each stage
+        const int gl = s + ((ng - 1 - s) / S) * S;
+        if (!bar_wait(su32(&full[s]), (gl / S) & 1, limit)) {
+          atomicExch(err, 1);
+          ok = false;
+        }
       }
     }
   }
   ok = __syncthreads_and(ok);
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   return Tc5Acc{dtmem, down, ok};
+}
+
+// The whole K range of rows r0 .. r0 + 127 of an R x K matrix, activations in the ring form.
+template <int N, int S>
+__device__ __forceinline__ Tc5Acc tc5_tile(const uint8_t* __restrict__ W, const float* __restrict__ Sc,
+                                           const __half* __restrict__ xh, const __half* __restrict__ xl, int R, int K,
+                                           int T8, int r0, int t0, uint8_t* smem, bool pdl, int* err) {
+  return tc5_tile_rows<N, S, false>(Tc5Linear{W, Sc, R, K, r0}, xh, xl, T8, t0, 0, K / 32, smem, pdl, err);
 }
 
 // N <= 128 keeps x_hi and x_lo products in separate column halves of the accumulator.

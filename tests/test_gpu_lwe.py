@@ -121,6 +121,37 @@ def test_batch_wide_w13_prefill(cuda_ok):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("name", ["tiny-llama", "ref-llama"])
+def test_layer_gemms_on_tcgen05(cuda_ok, name):
+    """MLLM_LWE_GEMM_TC5=1: forwards of >= 32 rows run every layer GEMM (QKV, proj + residual, w1/w3 +
+    SiLU, w2 + residual) on the tcgen05 tile with the tiled activation layout.  A 100-token prompt's
+    logits of every row within the logits bar of the oracle; 48 sequences (batched prefill and 48-row
+    decode steps) equal the mma.sync engine's streams and the oracle's."""
+    data = _data(name)
+    om = O.OracleModel(data)
+    eng = _engine(data, env={"MLLM_LWE_GEMM_TC5": "1"}, max_slots=48)
+    ref_eng = _engine(data, max_slots=48)
+    try:
+        V = eng.cfg["vocabSize"]
+        ids = pkg().seeded_prompt(100, V, 41)
+        eng.resetCache()
+        g, _ = eng.forward(ids, 0, logits_each=True)
+        r = np.asarray(om.forward(ids, 0, logits_each=True))
+        err = float(np.abs(g - r).max())
+        assert err <= LOGIT_TOL, err
+        seqs = _prompts(V, [1 + (5 * i) % 37 for i in range(48)], 700)
+        res, st = eng.generateBatch(seqs, maxNewTokens=10, eosId=-1)
+        res0, _ = ref_eng.generateBatch(seqs, maxNewTokens=10, eosId=-1)
+        for i, (q, a, b) in enumerate(zip(seqs, res, res0)):
+            assert a["generatedIds"] == b["generatedIds"], i
+            if i % 6 == 0:
+                assert a["generatedIds"] == om.generate(q, 10, eos=-1)["generatedIds"], i
+    finally:
+        eng.destroy()
+        ref_eng.destroy()
+
+
+@pytest.mark.gpu
 def test_batch_single_sequence_equals_generate(batch_models):
     data, eng, om = batch_models["ref-llama"]
     ids = pkg().seeded_prompt(20, eng.cfg["vocabSize"], 50)
