@@ -437,6 +437,50 @@ def gemv_points(torch, P, steps: int, shapes=GEMV_SHAPES, ms=(1, 5, 9, 16), mode
     return rows, launches
 
 
+def gemv_dense_points(torch, P, steps: int, R: int = 49152, C: int = 576, ms=(1, 16)):
+    """mllm_gemv (f32 / f16 / bf16 / q8 storage, engine/infer.js:10-86) on the lm_head shape, cold L2
+    (rotating copies larger than 2x L2, a CUDA graph of back-to-back launches).  GB/s counts the stored
+    weight bytes (+ the q8 row scales) per launch.  Returns (points, kernel launches)."""
+    rng = np.random.default_rng(1)
+    st = torch.cuda.Stream()
+    out, launches = [], 0
+    w = rng.standard_normal((R, C), dtype=np.float32) * np.float32(0.02)
+    for dt, esize in (("f32", 4), ("f16", 2), ("bf16", 2), ("q8", 1)):
+        nbytes = R * C * esize + (R * 4 if dt == "q8" else 0)
+        ncopy = max(1, -(-2 * L2_BYTES // nbytes))
+        wt = torch.empty((ncopy, R * C * esize), dtype=torch.uint8, device="cuda")
+        wt.random_(0, 256)
+        if dt in ("f16", "bf16"):  # finite 16-bit words (the top bits of N(0, 0.02) values)
+            wt.view(torch.int16).copy_(torch.from_numpy(w.astype(np.float16).view(np.int16)).cuda().reshape(-1))
+        elif dt == "f32":
+            wt.view(torch.float32).copy_(torch.from_numpy(w).cuda().reshape(-1))
+        sc = torch.full((R,), 1e-3, device="cuda")
+        for M in ms:
+            x = torch.from_numpy(rng.standard_normal((M, C), dtype=np.float32)).cuda()
+            y = torch.empty((M, R), device="cuda")
+            n = min(ncopy, 4096)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                for i in range(n):
+                    P.gemv_device(dt, wt[i].data_ptr(), sc.data_ptr(), x.data_ptr(), y.data_ptr(), R, C, M,
+                                  torch.cuda.current_stream().cuda_stream)
+            g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                g.replay()
+            e1.record()
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (steps * n)
+            launches += steps * n + n
+            out.append({"dtype": dt, "shape": f"{R}x{C}", "M": M, "weight_bytes": nbytes, "cold_us": us,
+                        "cold_gbs": nbytes / (us * 1e-6) / 1e9})
+            del g
+        del wt
+    return out, launches
+
+
 def gemv_e2e(torch, P, steps: int):
     """The headline GEMV point (lm_head 49152x576, M = 1) through the C ABI with host buffers: every
     step copies x from pinned host memory, runs mllm_gemv_q4 and reads y back; events around it."""
@@ -506,6 +550,9 @@ def gemv_line(torch, P, steps: int, full: bool, cpu: bool) -> dict:
                      "kernel": "gemv_q4_bulk_kernel<1,2,2,2> (mllm_gemv_q4 on 49152x576, M=1; two CTAs per SM)"},
         "gpu_launches": launches, "points": rows,
     }
+    dense, dl = gemv_dense_points(torch, P, steps)
+    out["dense_points"] = dense  # the other PGW storage kinds (mllm_gemv), same shape, cold L2
+    out["gpu_launches"] += dl
     if cpu:
         threads = os.cpu_count() or 1
         v, n = cpu_baseline_gemv(P, threads)

@@ -34,6 +34,9 @@ typedef enum {
 
 typedef enum { MLLM_STOP_EOS = 0, MLLM_STOP_MAX_NEW = 1, MLLM_STOP_CONTEXT = 2 } mllm_stop;
 
+/* PGW1 storage kinds: the dtype byte of the header and each tensor's storage (engine/weights.js:3). */
+typedef enum { MLLM_DTYPE_F32 = 0, MLLM_DTYPE_F16 = 1, MLLM_DTYPE_BF16 = 2, MLLM_DTYPE_Q8 = 3, MLLM_DTYPE_Q4 = 4 } mllm_dtype;
+
 /* Result of a generate call: engine/infer.js:617-645 and engine/webgpu.js:1272-1281. */
 typedef struct {
   int32_t n_generated;  /* ids written to out_ids */
@@ -174,6 +177,19 @@ int mllm_selftest_timeout(mllm_engine* e, int wait_ms);
  */
 int mllm_gemv_q4(const uint8_t* d_packed, const float* d_scales, const float* d_x, float* d_y, int rows, int cols,
                  int n_act, void* stream);
+
+/*
+ * Matrix-vector / skinny-matrix product for the other PGW storage kinds: gemvF32, gemvF16, gemvBf16
+ * and gemvQ8 (engine/infer.js:10-86, bound per tensor storage at engine/infer.js:314-345).
+ * y[m][r] = sum_k W[r][k] x[m][k] for m < n_act, with W in storage `dtype` on the device: f32
+ * [rows][cols]; f16 or bf16 as 16-bit words [rows][cols]; q8 as int8 [rows][cols] with d_scales f32
+ * [rows], applied after the row sum as gemvQ8 does (d_scales is ignored for the other kinds).
+ * fp32 accumulation.  n_act <= 16; a row must be whole 16-byte chunks (cols x element bytes a multiple
+ * of 16, cols a multiple of 4) and d_w, d_x 16-byte aligned, else MLLM_ERR_ARG.  MLLM_DTYPE_Q4 returns
+ * MLLM_ERR_UNSUPPORTED: its packed layout goes to mllm_gemv_q4.
+ */
+int mllm_gemv(int dtype, const void* d_w, const float* d_scales, const float* d_x, float* d_y, int rows, int cols,
+              int n_act, void* stream);
 
 /*
  * The same product for any number of activation rows on the tensor cores: n_act >= 1 rows of f32

@@ -25,7 +25,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr", "-Xptxas", "-v"]
 if os.environ.get("MLLM_FAST_BUILD"):  # development: only the PetitGPT-shape instantiation
     CUFLAGS += ["-DMLLM_FAST_BUILD"]
-SOURCES = ["engine.cu", "decode.cu", "decode1.cu", "cdec.cu", "gemv.cu", "gemm.cu", "gemm_tc5.cu", "lwe.cu", "pgw.cpp"]
+SOURCES = ["engine.cu", "decode.cu", "decode1.cu", "cdec.cu", "gemv.cu", "gemv_dense.cu", "gemm.cu", "gemm_tc5.cu", "lwe.cu",
+           "pgw.cpp"]
 HEADERS = ["cdec.cuh", "device_common.cuh", "engine.cuh", "lwe.cuh", "pgw.hpp", "q4mma.cuh", "tc5.cuh"]
 
 

@@ -31,7 +31,7 @@ EXPORTS = ["mllm_create", "mllm_destroy", "mllm_last_error", "mllm_config", "mll
            "mllm_cache_len", "mllm_forward", "mllm_generate", "mllm_generate_stream", "mllm_generate_device",
            "mllm_generate_batch",
            "mllm_selftest_timeout",
-           "mllm_gemv_q4", "mllm_gemm_q4", "mllm_gemm_q4_noalloc"]
+           "mllm_gemv_q4", "mllm_gemv", "mllm_gemm_q4", "mllm_gemm_q4_noalloc"]
 
 
 class MllmError(RuntimeError):
@@ -84,6 +84,7 @@ def load_library(path: str = LIB_PATH):
     L.mllm_generate_stream.argtypes = [P, I, P, I, I, ctypes.c_int32, I, I, P, ctypes.POINTER(Stats), TOKEN_FN, P]
     L.mllm_generate_batch.argtypes = [P, I, P, P, I, ctypes.c_int32, P, P, P, ctypes.POINTER(BatchStats)]
     L.mllm_gemv_q4.argtypes = [P, P, P, P, I, I, I, P]
+    L.mllm_gemv.argtypes = [I, P, P, P, P, I, I, I, P]
     L.mllm_gemm_q4.argtypes = [P, P, P, P, I, I, I, P]
     L.mllm_gemm_q4_noalloc.argtypes = [P, P, P, P, I, I, I, P]
     L.mllm_selftest_timeout.argtypes = [P, I]
@@ -102,6 +103,19 @@ def gemv_q4_device(packed_ptr: int, scales_ptr: int, x_ptr: int, y_ptr: int, row
     rc = load_library().mllm_gemv_q4(packed_ptr, scales_ptr, x_ptr, y_ptr, rows, cols, n_act, stream or None)
     if rc:
         raise MllmError(rc, "mllm_gemv_q4 rejected its arguments")
+
+
+DTYPES = {"f32": 0, "f16": 1, "bf16": 2, "q8": 3, "q4": 4}  # engine/weights.js:3 (mllm_dtype)
+
+
+def gemv_device(dtype: str, w_ptr: int, scales_ptr: int, x_ptr: int, y_ptr: int, rows: int, cols: int, n_act: int,
+                stream: int = 0) -> None:
+    """GEMV for the f32 / f16 / bf16 / q8 storage kinds on device pointers (mllm_gemv):
+    y[n_act][rows] = x[n_act][cols] . W^T (q8: times the row scales)."""
+    rc = load_library().mllm_gemv(DTYPES[dtype], w_ptr, scales_ptr or None, x_ptr, y_ptr, rows, cols, n_act,
+                                  stream or None)
+    if rc:
+        raise MllmError(rc, "mllm_gemv rejected its arguments")
 
 
 def gemm_q4_device(packed_ptr: int, scales_ptr: int, x_ptr: int, y_ptr: int, rows: int, cols: int, n_act: int,

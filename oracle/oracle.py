@@ -99,6 +99,36 @@ def gemv_q4_f32acc(packed, scales, x, group: int = 32) -> np.ndarray:
     return y
 
 
+def f16_bits_to_f32(u16: np.ndarray) -> np.ndarray:
+    """f16ToF32 (engine/weights.js:159): IEEE half to float, exact."""
+    return np.ascontiguousarray(u16, np.uint16).view(np.float16).astype(np.float32)
+
+
+def bf16_bits_to_f32(u16: np.ndarray) -> np.ndarray:
+    """The bf16 conversion of gemvBf16 (engine/infer.js:66-77): the 16 bits become the top of an f32."""
+    return (np.ascontiguousarray(u16, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def gemv_dense(dtype: str, w: np.ndarray, scales, x: np.ndarray) -> np.ndarray:
+    """gemvF32 / gemvF16 / gemvBf16 / gemvQ8 (engine/infer.js:10-86): y[r] = sum_k W[r][k] x[k] in f64
+    (the JS `let s` accumulator), stored as f32; q8 multiplies the row sum by the row scale.  w holds
+    f32 values, uint16 words (f16 / bf16) or int8 values; x is one activation row."""
+    if dtype == "f32":
+        wf = np.asarray(w, np.float32).astype(np.float64)
+    elif dtype == "f16":
+        wf = f16_bits_to_f32(w).astype(np.float64)
+    elif dtype == "bf16":
+        wf = bf16_bits_to_f32(w).astype(np.float64)
+    elif dtype == "q8":
+        wf = np.asarray(w, np.int8).astype(np.float64)
+    else:
+        raise ValueError(dtype)
+    y = wf @ np.asarray(x, np.float32).astype(np.float64)
+    if dtype == "q8":
+        y = y * np.asarray(scales, np.float32).astype(np.float64)
+    return y.astype(np.float32)
+
+
 def lookup_draft(seq, k: int, n: int):
     """engine/webgpu.js:846-865"""
     s = np.ascontiguousarray(seq, np.int32)

@@ -117,3 +117,47 @@ def test_spec_generate_equals_greedy():
         assert s["generatedIds"] == g["generatedIds"], k
         assert s["specTries"] == s["forwards"]
         assert len(s["generatedIds"]) == s["forwards"] + 1 + s["specHits"]
+
+
+def _js_gemv_row(wrow, x, conv):
+    """One row of gemvF32 / gemvF16 / gemvBf16 / gemvQ8 as the JS loops write it (engine/infer.js:10-86):
+    a double accumulator, gemvF32's 8-way unrolled body and tail loop, per-element conversion."""
+    n = len(x)
+    s = 0.0
+    k = 0
+    while k < n - 7:
+        for j in range(8):
+            s += float(conv(wrow[k + j])) * float(x[k + j])
+        k += 8
+    while k < n:
+        s += float(conv(wrow[k])) * float(x[k])
+        k += 1
+    return s
+
+
+def test_gemv_dense_oracle_matches_the_js_loops():
+    """The vectorised dense / q8 GEMV oracle against a scalar restatement of the JS row loops, including
+    f16 subnormals and infinities-free extremes, bf16 bit patterns and negative int8."""
+    rng = np.random.default_rng(5)
+    rows, cols = 6, 44
+    x = rng.standard_normal(cols).astype(np.float32)
+    f32 = (rng.standard_normal((rows, cols)) * 0.05).astype(np.float32)
+    f16 = (rng.standard_normal((rows, cols)) * 0.05).astype(np.float16)
+    f16[0, :4] = np.array([6e-8, -3e-6, 65504.0, -0.0], np.float16)  # subnormal, tiny, largest finite
+    f16w = f16.view(np.uint16)
+    bf = rng.integers(0, 1 << 16, size=(rows, cols), dtype=np.uint16)
+    bf[(bf & 0x7F80) == 0x7F80] &= 0xBFFF  # no inf / nan patterns
+    q8 = rng.integers(-128, 128, size=(rows, cols)).astype(np.int8)
+    sc = (rng.random(rows) * 0.01).astype(np.float32)
+    cases = [("f32", f32, None, lambda v: np.float32(v)),
+             ("f16", f16w, None, lambda v: np.uint16(v).view(np.float16).astype(np.float32)),
+             ("bf16", bf, None, lambda v: np.array([np.uint32(v) << np.uint32(16)], np.uint32).view(np.float32)[0]),
+             ("q8", q8, sc, lambda v: np.float32(v))]
+    for dt, w, s, conv in cases:
+        got = O.gemv_dense(dt, w, s, x)
+        for r in range(rows):
+            want = _js_gemv_row(w[r], x, conv)
+            if dt == "q8":
+                want *= float(s[r])
+            assert np.float32(want) == got[r] or abs(float(got[r]) - want) <= 1e-6 * max(1.0, abs(want)), (dt, r)
+
