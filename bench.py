@@ -47,11 +47,13 @@ DECODE_TRAFFIC_PER_LAUNCH = {("config1 petitgpt b1 p64 n128", "decode1"): 187_88
 # sm__pipe_tensor_cycles_active (% of peak, active cycles) of the decode-step GEMMs of config 5, one
 # single-kernel ncu --set full capture each on `bench.py --case batched --seqs 128 --prompt 8 --new 3`
 # (the first decode step's launch; mma.sync.m16n8k16 tiles): the share of the tensor pipe they keep busy.
-BATCHED_TENSOR_PIPE = {"source": "ncu single-kernel captures, 128-row decode step", "unit": "% of peak",
+BATCHED_TENSOR_PIPE = {"source": "ncu single-kernel captures: the mma.sync GEMMs and attention on a 128-row decode "
+                                 "step; the tcgen05 lm_head (the default) on a 128-row forward "
+                                 "(profiles/lwe_lm_tc5_smollm2_135m.md)", "unit": "% of peak",
                        "lwe_gemm_qkv<2,4>": 11.9, "lwe_gemm_w13<2,1>": 20.9, "lwe_gemm_resid<2,4>": 5.0,
-                       "lwe_gemm_lm_wide<8,3>": 43.0, "lwe_attention<3,1>": 0.0}
+                       "lwe_lm_tc5<128,6>": 27.6, "lwe_attention<3,1>": 0.0}
 # dram__bytes_read.sum + dram__bytes_write.sum of one cold gemv_q4_bulk_kernel launch on the lm_head
-# shape (49152 x 576, M = 1), from an ncu capture of `microllm-lab_b200/profile_case.py gemv`: exactly the
+# shape (49152 x 576, M = 1), from an ncu capture of `bench.py --case gemv`: exactly the
 # 17,694,720 bytes of nibbles and scales plus the activations.
 GEMV_LM_TRAFFIC_PER_LAUNCH = 17_712_384
 
