@@ -20,7 +20,7 @@ def test_gemv_q4_matches_oracle(rows, cols, cuda_ok):
     packed, sc = P.quant_q4(w)
     dp = torch.from_numpy(packed).cuda()
     ds = torch.from_numpy(sc).cuda()
-    for m in (1, 5, 9, 16):
+    for m in (1, 2, 4, 5, 9, 16):
         x = rng.standard_normal((m, cols), dtype=np.float32)
         dx = torch.from_numpy(x).cuda()
         dy = torch.empty((m, rows), dtype=torch.float32, device="cuda")
