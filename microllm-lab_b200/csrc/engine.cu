@@ -838,6 +838,25 @@ int mllm_create(int device, const uint8_t* buf, size_t len, int max_slots, int k
     w.kc = kc;
     w.vc = vc;
   }
+  if (e->lh.gemm_tc5 && md.arch == 0 && e->lwe_ok) {
+    // the layer matrices expanded once into the tcgen05 tile's group images (fp16 hi/lo, swizzled)
+    e->lh.pre.resize((size_t)L * kPreMats);
+    for (int l = 0; l < L; ++l) {
+      const LayerDev& Ld = layers[l];
+      const Q4* mw[kPreMats] = {&Ld.qkv, &Ld.proj, &Ld.w1, &Ld.w2};
+      const Q4* m3[kPreMats] = {nullptr, nullptr, &Ld.w3, nullptr};
+      const int mr[kPreMats] = {md.QKV, D, FF, D}, mk[kPreMats] = {D, D, D, FF};
+      for (int m = 0; m < kPreMats; ++m) {
+        Tc5Pre& p = e->lh.pre[(size_t)l * kPreMats + m];
+        const bool paired = m3[m] != nullptr;
+        if ((rc = dev_alloc(E, &p.img, tc5_pre_bytes(mr[m], mk[m], paired))) ||
+            (rc = dev_alloc(E, &p.down, (size_t)tc5_pre_tiles(mr[m], paired) * 4)))
+          return relay(rc);
+        if (tc5_expand(*mw[m], m3[m], mr[m], mk[m], p, 0) != cudaSuccess)
+          return bad(MLLM_ERR_CUDA, "weight expansion for the tcgen05 GEMMs failed");
+      }
+    }
+  }
   if (const char* v = getenv("MLLM_POLL_SLEEP_NS")) e->poll_sleep_ns = atoi(v);
   if (const char* v = getenv("MLLM_WEIGHT_EVICT_LAST")) e->weight_policy = atoi(v) ? 1 : 0;
   if (const char* v = getenv("MLLM_L2_PREFETCH")) e->l2_prefetch = atoi(v) ? 1 : 0;

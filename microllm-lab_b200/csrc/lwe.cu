@@ -1381,7 +1381,8 @@ __global__ void __launch_bounds__(tc5::kTc5Threads + 64, 1) lwe_lm_tc5(const __g
 }
 
 // ---------------------------------------------------------------------------------------------
-// Layer GEMMs of a llama forward on the tcgen05 tile (tc5.cuh, resident form).
+// Layer GEMMs of a llama forward on the tcgen05 tile (tc5.cuh), fed by the load-time group images of the
+// matrix (tc5_tile_pre).
 // grid (row tiles, ceil(T / N), kz): CTA (b, y, z) multiplies 128 tile rows by tokens N y .. N y + N - 1
 // over its share of the K groups (split-K when kz > 1: each CTA leaves its fp32 partial tile in
 // a.skws, the last one of a tile (counter a.skctr) adds them in split order and runs the epilogue).
@@ -1416,7 +1417,7 @@ __device__ __forceinline__ int tc5_fold_token(int lane) {
 template <int N, int S, int EPI>
 __global__ void __launch_bounds__(tc5::kTc5Threads + 64, 1)
     lwe_tc5_gemm(const __grid_constant__ LweArgs a, int T, Q4 w, Q4 w3, const float* bias, int R, int K,
-                 const __half* xh, const __half* xl, const float* gn, __half* nh, __half* nl) {
+                 const __half* xh, const __half* xl, const float* gn, __half* nh, __half* nl, Tc5Pre pre) {
   using namespace tc5;
   static_assert(N >= 32 && N % 32 == 0, "two column halves of 16-token chunks");
   extern __shared__ __align__(128) uint8_t smem[];
@@ -1432,15 +1433,9 @@ __global__ void __launch_bounds__(tc5::kTc5Threads + 64, 1)
     if (EPI != kTc5Resid)
       for (int i = lane - 1; i < N; i += 31) sinv[i] = t0 + i < T ? fold_inv(a, t0 + i) : 1.f;
   };
-  Tc5Acc acc;
-  if constexpr (EPI == kTc5W13) {
-    const Tc5Paired rows{reinterpret_cast<const uint8_t*>(w.w), w.s, reinterpret_cast<const uint8_t*>(w3.w), w3.s,
-                         R, K, (int)blockIdx.x * 64};
-    acc = tc5_tile_rows<N, S, true>(rows, xh, xl, T8, t0, g0, ng, smem, true, a.err, side);
-  } else {
-    const Tc5Linear rows{reinterpret_cast<const uint8_t*>(w.w), w.s, R, K, (int)blockIdx.x * kTc5Rows};
-    acc = tc5_tile_rows<N, S, true>(rows, xh, xl, T8, t0, g0, ng, smem, true, a.err, side);
-  }
+  // the matrix's group images from the load-time expansion (the Q4 pointers w / w3 are not read here)
+  const Tc5Acc acc = tc5_tile_pre<N, S>(pre.img + ((size_t)blockIdx.x * NG + g0) * kTc5GroupImage,
+                                        pre.down[blockIdx.x], xh, xl, T8, t0, g0, ng, smem, true, a.err, side);
   pdl_enter();  // the previous kernel's x, ss and activation buffers are complete
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool epi_warp = warp < kTc5Threads / 32;
@@ -1770,15 +1765,31 @@ static void launch_lm_tc5(const LweArgs& a, int T, const float* norm_f, const in
 // the SMs or the 64-token tile's resident activations would not fit, else 64.  The K groups are split
 // over several CTAs as far as the resident activations need to fit, and further (up to 4) while the
 // grid stays within one wave and each CTA keeps >= 12 groups.
-constexpr int kTc5GemmStages = 3;
+constexpr int kTc5PreStages = 4;  // stages of one group image
 static int g_tc5_gemm_cap = 0;  // dynamic shared memory granted to lwe_tc5_gemm (0: not set up)
 static int g_sms = 0;
 template <int N, int EPI>
 static void tc5_gemm_attr() {
-  if (smem_attr(lwe_tc5_gemm<N, kTc5GemmStages, EPI>, g_tc5_gemm_cap) != cudaSuccess) {
+  if (smem_attr(lwe_tc5_gemm<N, kTc5PreStages, EPI>, g_tc5_gemm_cap) != cudaSuccess) {
     (void)cudaGetLastError();
     g_tc5_gemm_cap = 0;
   }
+}
+int tc5_pre_tiles(int R, bool paired) { return paired ? (R + 63) / 64 : (R + tc5::kTc5Rows - 1) / tc5::kTc5Rows; }
+size_t tc5_pre_bytes(int R, int K, bool paired) {
+  return (size_t)tc5_pre_tiles(R, paired) * (K / 32) * tc5::kTc5GroupImage;
+}
+cudaError_t tc5_expand(const Q4& w, const Q4* w3, int R, int K, const Tc5Pre& p, cudaStream_t st) {
+  using namespace tc5;
+  const dim3 grid(tc5_pre_tiles(R, w3 != nullptr), K / 32);
+  if (w3)
+    tc5_expand_kernel<<<grid, 256, 0, st>>>(Tc5Paired{reinterpret_cast<const uint8_t*>(w.w), w.s,
+                                                      reinterpret_cast<const uint8_t*>(w3->w), w3->s, R, K, 0},
+                                            K / 32, p.img, p.down);
+  else
+    tc5_expand_kernel<<<grid, 256, 0, st>>>(Tc5Linear{reinterpret_cast<const uint8_t*>(w.w), w.s, R, K, 0}, K / 32,
+                                            p.img, p.down);
+  return cudaGetLastError();
 }
 struct Tc5Shape {
   int N, tt, kz, ngz;
@@ -1788,12 +1799,10 @@ static bool tc5_gemm_shape(int T, int rtiles, int K, Tc5Shape* sh) {
   using namespace tc5;
   if (g_tc5_gemm_cap <= 0 || K % 32) return false;
   const int NG = K / 32, sms = g_sms > 0 ? g_sms : 148;
-  // resident bytes (tc5_smem_resident): the stages, the per-row pads and the alignment slack, then per
-  // group N x 128 of activations, 16 x 128 of raw nibbles and 4 x 128 of scales
-  const int fixed = kTc5GemmStages * kTc5StageGroups * 2 * kTc5ABytes + kTc5Rows * 20 + 1024;
-  auto max_groups = [&](int n) {
-    return std::min(kTc5MaxGroups, (g_tc5_gemm_cap - fixed) / (n * 128 + kTc5Rows * 20));
-  };
+  // shared memory (tc5_smem_pre): the image ring and the alignment slack, then N x 128 bytes of
+  // activation halves per group
+  const int fixed = kTc5PreStages * kTc5GroupImage + 1024;
+  auto max_groups = [&](int n) { return (g_tc5_gemm_cap - fixed) / (n * 128); };
   // 64-token tiles only where the 32-token grid would take more than one wave and no K split is needed
   const int N = (long)rtiles * ((T + 31) / 32) <= sms || NG > max_groups(64) ? 32 : 64;
   const int tt = (T + N - 1) / N, tiles = rtiles * tt;
@@ -1804,7 +1813,7 @@ static bool tc5_gemm_shape(int T, int rtiles, int K, Tc5Shape* sh) {
   const int ngz = (NG + kz - 1) / kz;
   kz = (NG + ngz - 1) / ngz;  // every split keeps at least one group
   if (kz > 1 && (tiles > kLweSplitKTiles || (size_t)tiles * kz * kTc5Rows * N * 4 > kLweSkwsBytes)) return false;
-  const size_t sm = tc5_smem_resident(N, kTc5GemmStages, ngz);
+  const size_t sm = tc5_smem_pre(N, kTc5PreStages, ngz);
   if (sm > (size_t)g_tc5_gemm_cap) return false;
   *sh = Tc5Shape{N, tt, kz, ngz, sm};
   return true;
@@ -1821,16 +1830,16 @@ static bool tc5_gemms_fit(const ModelDev& md, int T) {
 template <int EPI>
 static void launch_tc5_gemm(const LweArgs& a, int T, int rtiles, int R, int K, Q4 w, Q4 w3, const float* bias,
                             const __half* xh, const __half* xl, const float* gn, __half* nh, __half* nl,
-                            cudaStream_t st) {
+                            const Tc5Pre& pre, cudaStream_t st) {
   Tc5Shape sh;
   (void)tc5_gemm_shape(T, rtiles, K, &sh);  // tc5_gemms_fit checked it for the forward
   const dim3 grid(rtiles, sh.tt, sh.kz), block(tc5::kTc5Threads + 64);
   if (sh.N == 32)
-    lwe_launch(lwe_tc5_gemm<32, kTc5GemmStages, EPI>, grid, block, sh.smem, st, a, T, w, w3, bias, R, K, xh, xl, gn, nh,
-               nl);
+    lwe_launch(lwe_tc5_gemm<32, kTc5PreStages, EPI>, grid, block, sh.smem, st, a, T, w, w3, bias, R, K, xh, xl, gn, nh,
+               nl, pre);
   else
-    lwe_launch(lwe_tc5_gemm<64, kTc5GemmStages, EPI>, grid, block, sh.smem, st, a, T, w, w3, bias, R, K, xh, xl, gn, nh,
-               nl);
+    lwe_launch(lwe_tc5_gemm<64, kTc5PreStages, EPI>, grid, block, sh.smem, st, a, T, w, w3, bias, R, K, xh, xl, gn, nh,
+               nl, pre);
   lwe_debug_check("lwe_tc5_gemm", sh.N, EPI, rtiles, T, sh.kz, sh.smem);
 }
 
@@ -1904,7 +1913,9 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
   const bool fold = md.arch == 0 && h.fold_norm;
   a.fold = fold ? 1 : 0;
   // llama forwards of many rows: every layer GEMM on the tcgen05 tile, GEMM inputs in the tiled layout
-  const bool tc = fold && h.gemm_tc5 && T >= kTc5GemmRows && !a.skip && tc5_gemms_fit(md, T);
+  // (the matrices were expanded into the tile's group images at load when MLLM_LWE_GEMM_TC5 is set)
+  const bool tc = fold && h.gemm_tc5 && (int)h.pre.size() == nl * kPreMats && T >= kTc5GemmRows && !a.skip &&
+                  tc5_gemms_fit(md, T);
   a.tiled = tc ? 1 : 0;
   g_lwe_pdl = h.pdl != 0;
   lwe_launch(lwe_embed, dim3(T), dim3(128), 0, st, a, T, h.layers[0].norm1);  // + norm1 of layer 0
@@ -1917,9 +1928,10 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
     const bool rope_epi = !one_per_slot && h.rope_epi && T <= kLweSplitAttnRows;
     const Q4 none{nullptr, nullptr};
     const int dt = (md.D + tc5::kTc5Rows - 1) / tc5::kTc5Rows;
+    auto pm = [&](int m) -> const Tc5Pre& { return h.pre[(size_t)l * kPreMats + m]; };
     if (tc)
       launch_tc5_gemm<kTc5Qkv>(a, T, (md.QKV + tc5::kTc5Rows - 1) / tc5::kTc5Rows, md.QKV, md.D, L.qkv, none, L.qkv_b,
-                               a.xh, a.xl, nullptr, nullptr, nullptr, st);
+                               a.xh, a.xl, nullptr, nullptr, nullptr, pm(kPreQkv), st);
     else
       LWE_GEMM(lwe_gemm_qkv, kGemmRows, md.QKV, md.D, T, a, T, l, rope_epi ? 1 : 0);
     if (one_per_slot) {
@@ -1941,7 +1953,8 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
       n2.xh = a.xh3;
       n2.xl = a.xl3;
       if (tc)
-        launch_tc5_gemm<kTc5Resid>(a, T, dt, md.D, md.D, L.proj, none, L.proj_b, a.xh, a.xl, L.norm2, a.xh3, a.xl3, st);
+        launch_tc5_gemm<kTc5Resid>(a, T, dt, md.D, md.D, L.proj, none, L.proj_b, a.xh, a.xl, L.norm2, a.xh3, a.xl3,
+                                   pm(kPreProj), st);
       else
         LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.D, T, a, T, L.proj, L.proj_b, md.D, L.norm2, a.xh3, a.xl3, a.ldx);
     } else {
@@ -1952,7 +1965,7 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
       // long forwards (prefill chunks): the persistent wide GEMM, activations read once per CTA
       if (tc)
         launch_tc5_gemm<kTc5W13>(a, T, (md.FF + 63) / 64, md.FF, md.D, L.w1, L.w3, nullptr, a.xh3, a.xl3, nullptr,
-                                 nullptr, nullptr, st);
+                                 nullptr, nullptr, pm(kPreW13), st);
       else if (!(T >= kW13WideRows && h.w13_wide && launch_w13_wide(n2, T, l, st)))
         LWE_GEMM(lwe_gemm_w13, 32, md.FF, md.D, T, n2, T, l);
     } else
@@ -1965,7 +1978,8 @@ cudaError_t lwe_forward(LweArgs a, const LweHost& h, int T, int lm_T, bool lm_fr
     const float* ng = l + 1 < nl ? h.layers[l + 1].norm1 : nullptr;
     if (fold) {
       if (tc)
-        launch_tc5_gemm<kTc5Resid>(a, T, dt, md.D, md.FF, L.w2, none, L.mproj_b, a.xh2, a.xl2, ng, a.xh, a.xl, st);
+        launch_tc5_gemm<kTc5Resid>(a, T, dt, md.D, md.FF, L.w2, none, L.mproj_b, a.xh2, a.xl2, ng, a.xh, a.xl,
+                                   pm(kPreW2), st);
       else
         LWE_GEMM(lwe_gemm_resid, kGemmRows, md.D, md.FF, T, b, T, L.w2, L.mproj_b, md.FF, ng, a.xh, a.xl, a.ldx);
     } else {

@@ -52,6 +52,18 @@ constexpr int kLweSplitAttnRows = 16;  // forwards of at most this many tokens u
 constexpr int kLweSplitKTiles = 16384;
 constexpr int kTc5GemmRows = 32;  // token rows from which the layer GEMMs run on the tcgen05 tile
 
+// A layer matrix expanded once at load into the tcgen05 tile's group images (tc5::tc5_expand_kernel):
+// img [row tiles][groups][16 KB], down [row tiles] (each tile's 2^-E).
+struct Tc5Pre {
+  uint8_t* img = nullptr;
+  float* down = nullptr;
+};
+enum { kPreQkv = 0, kPreProj = 1, kPreW13 = 2, kPreW2 = 3, kPreMats = 4 };
+// Row tiles and bytes of one matrix's images (paired: w1/w3 interleaved, 64 FF rows a tile).
+int tc5_pre_tiles(int R, bool paired);
+size_t tc5_pre_bytes(int R, int K, bool paired);
+cudaError_t tc5_expand(const Q4& w, const Q4* w3, int R, int K, const Tc5Pre& p, cudaStream_t st);
+
 // Host-side copies of the per-layer descriptors the launches pass by value.
 struct LweHost {
   std::vector<LayerDev> layers;
@@ -63,6 +75,7 @@ struct LweHost {
   int pdl = 1;         // programmatic dependent launch between the forward's kernels (MLLM_LWE_PDL=0: off)
   int lm_wide = 1;     // persistent lm_head GEMM for many rows without logits (MLLM_LWE_LM_WIDE=0: off)
   int lm_tc5 = 1;      // the same on the tcgen05 tile, ahead of lm_wide (MLLM_LWE_LM_TC5=0: off)
+  std::vector<Tc5Pre> pre;  // [layer * kPreMats + matrix] when the layer GEMMs run on the tcgen05 tile
   int gemm_tc5 = 0;    // llama forwards of >= kTc5GemmRows rows: every layer GEMM on the tcgen05 tile
                        // (MLLM_LWE_GEMM_TC5=1; off by default: measured slower than the mma.sync tiles
                        // at these shapes)

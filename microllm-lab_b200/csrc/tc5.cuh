@@ -7,12 +7,13 @@
 // One CTA computes a 128-row x N-token tile with three roles and no CTA-wide barrier inside the K loop.
 //   - Eight producer warps walk the Q4 groups (32 columns).  Two threads dequantise each weight row's
 //     group into a stage of shared memory; each warp then arrives once on the stage's full mbarrier.
-//   - One copy thread brings the activation halves (N tokens x 32 columns, hi and lo) by bulk copies:
-//     per stage into a ring (counted on the stage's barrier), or (the resident form) every group at
-//     the start, counted on one barrier.
+//   - One copy thread brings the activation halves (N tokens x 32 columns, hi and lo) by two bulk copies
+//     per stage, counted on the stage's barrier.
 //   - One MMA thread waits for a full stage, issues its MMAs and releases the stage with
-//     tcgen05.commit onto its empty mbarrier, which the producers (and in the ring form the copy thread)
-//     wait for before they refill it.
+//     tcgen05.commit onto its empty mbarrier, which the producers and the copy thread wait for before
+//     they refill it.
+// tc5_tile_pre is the same tile for matrices expanded at load into these stage images: no producer
+// warps, the copy thread brings one image per group and every group's activation halves up front.
 //
 // Precision.  The group scale is folded into the weights, w = (q - 8) s 2^E.  The per-CTA 2^E puts the
 // tile's largest |w| near 2^14, so that the fp16 parts below stay normal.  The scale is split as
@@ -129,21 +130,12 @@ constexpr size_t tc5_smem_bytes() {
   return (size_t)S * (2 * kTc5ABytes + 2 * N * 64) + 1024;
 }
 
-// The resident form of the tile (tc5_tile_rows<N, S, true>): stages of kTc5StageGroups groups, and per
-// group the activation halves, the raw nibbles (16 bytes a row, one 16-byte pad per row) and the scales
-// of the tile's 128 rows, all in shared memory for the whole K loop.
-constexpr int kTc5StageGroups = 2;
-constexpr int kTc5MaxGroups = 64;  // K columns per CTA <= 2,048 in the resident form
-__host__ __device__ constexpr size_t tc5_smem_resident(int N, int S, int ng) {
-  return (size_t)S * kTc5StageGroups * 2 * kTc5ABytes + (size_t)ng * 2 * N * 64 + (size_t)kTc5Rows * 16 * (ng + 1) +
-         (size_t)kTc5Rows * 4 * (ng + 1) + 1024;
-}
-
 // Row sources of a tile: tile row lr (0 .. 127) -> its packed Q4 row and scales, false past the matrix.
 struct Tc5Linear {  // rows r0 .. r0 + 127 of an R x K matrix
   const uint8_t* W;
   const float* S;
   int R, K, r0;
+  __host__ __device__ Tc5Linear at_tile(int tile) const { return Tc5Linear{W, S, R, K, tile * kTc5Rows}; }
   __device__ __forceinline__ bool row(int lr, const uint8_t*& w, const float*& s) const {
     const int r = r0 + lr;
     if (r >= R) return false;
@@ -161,6 +153,7 @@ struct Tc5Paired {
   const uint8_t* W3;
   const float* S3;
   int F, K, f0;
+  __host__ __device__ Tc5Paired at_tile(int tile) const { return Tc5Paired{W1, S1, W3, S3, F, K, tile * 64}; }
   __device__ __forceinline__ bool row(int lr, const uint8_t*& w, const float*& s) const {
     const int j = lr & 31, f = f0 + 16 * (lr >> 5) + (j & 15);
     if (f >= F) return false;
@@ -183,26 +176,21 @@ struct Tc5NoSide {
 
 // One 128-row x N-token tile over the Q4 groups g0 .. g0 + ng - 1, run by kTc5Threads + 64 threads
 // (see the top of this file): the tile rows of `rows` against tokens t0 .. t0 + N - 1 of the tiled
-// activation halves xh / xl (T8 8-token blocks, tiled_at).
-//   - Ring form (XRES false, tc5_smem_bytes<N, S>()): S one-group stages of weights and activations;
-//     each producer thread fetches its nibbles and scales kPD groups ahead into registers.
-//   - Resident form (XRES, tc5_smem_resident(N, S, ng), ng <= kTc5MaxGroups): every group's activation
-//     halves come in at the start on one barrier, the tile's raw Q4 rows by one bulk copy per row and
-//     its scales by one pass of loads; the producers dequantise kTc5StageGroups groups per stage from
-//     shared memory, so that a stage costs one wait and one arrival per warp for two groups.
-// With pdl the copy warp waits for the previous kernel (griddepcontrol.wait) before its activation
-// copies; the weights need no wait.  Lanes 1 .. 31 of the copy warp then run side(lane) during the K
-// loop: epilogue inputs that the previous kernel wrote can be staged there.  A wait that runs out its
-// limit sets *err and turns ok false.  Every thread must then call tc5_release.
-template <int N, int S, bool XRES, class Rows, class Side = Tc5NoSide>
+// activation halves xh / xl (T8 8-token blocks, tiled_at), through S one-group stages of weights and
+// activations (tc5_smem_bytes<N, S>()); each producer thread fetches its nibbles and scales kPD groups
+// ahead into registers.  With pdl the copy thread waits for the previous kernel (griddepcontrol.wait)
+// before its first activation copy; the weights need no wait.  Lanes 1 .. 31 of the copy warp run
+// side(lane) during the K loop (after the same wait when pdl): epilogue inputs that the previous kernel
+// wrote can be staged there.  A wait that runs out its limit sets *err and turns ok false.  Every thread
+// must then call tc5_release.
+template <int N, int S, class Rows, class Side = Tc5NoSide>
 __device__ __forceinline__ Tc5Acc tc5_tile_rows(const Rows& rows, const __half* __restrict__ xh,
                                                 const __half* __restrict__ xl, int T8, int t0, int g0, int ng,
                                                 uint8_t* smem, bool pdl, int* err, const Side& side = Tc5NoSide{}) {
   constexpr int kB = N * 64;                    // one fp16 half of a group's activations
-  constexpr int kPD = 8;                        // ring form: groups each producer thread requests ahead
-  constexpr int G = XRES ? kTc5StageGroups : 1;  // groups per stage
-  constexpr int kStageA = G * 2 * kTc5ABytes;   // a stage's weights: per group [w_hi 8 KB][w_lo 8 KB]
-  __shared__ __align__(8) uint64_t full[S], empty[S], done, xfull, wfull;
+  constexpr int kPD = 8;                        // groups each producer thread requests ahead
+  constexpr int kStageA = 2 * kTc5ABytes;       // a stage's weights: [w_hi 8 KB][w_lo 8 KB]
+  __shared__ __align__(8) uint64_t full[S], empty[S], done;
   __shared__ uint32_t tmem_base;
   __shared__ float smax[kTc5Threads / 32];
   smem += (1024u - (su32(smem) & 1023u)) & 1023u;  // swizzle atoms on 1024-byte boundaries
@@ -220,11 +208,7 @@ __device__ __forceinline__ Tc5Acc tc5_tile_rows(const Rows& rows, const __half* 
   constexpr uint32_t kCols = kAcc < 32 ? 32 : kAcc;  // tensor-memory columns (a power of 2 >= 32)
   // activation bytes per group: the 8-token blocks of this tile that exist (the last may be padding)
   const uint32_t xbytes = (uint32_t)min(N / 8, T8 - t0 / 8) * 512u;
-  const int nst = (ng + G - 1) / G;  // stages of the K loop
-  uint8_t* const xs = smem + (size_t)S * kStageA;  // activations: S ring stages, or every group
-  const int rs = 16 * (ng + 1);                    // resident raw rows [128][rs] and scales [128][ng + 1]
-  uint8_t* const wraw = xs + (size_t)(XRES ? ng : S) * 2 * kB;
-  float* const sraw = reinterpret_cast<float*>(wraw + (size_t)kTc5Rows * rs);
+  uint8_t* const xs = smem + (size_t)S * kStageA;  // activations: S ring stages
 
   // ---- tensor memory for the accumulator (warp 0), barriers, the tile's power-of-two weight scale
   if (warp == 0) {
@@ -235,19 +219,15 @@ __device__ __forceinline__ Tc5Acc tc5_tile_rows(const Rows& rows, const __half* 
   }
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      // one arrival per producer warp, plus (ring form) the copy thread's arrival with the copies' bytes
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&full[s])),
-                   "r"(kTc5Threads / 32 + (XRES ? 0 : 1))
+      // one arrival per producer warp, plus the copy thread's arrival with the copies' bytes
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&full[s])), "r"(kTc5Threads / 32 + 1)
                    : "memory");
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&empty[s])) : "memory");
     }
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&done)) : "memory");
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&xfull)) : "memory");
-    // one arrival per tile row (with the byte count of its copy when the row exists)
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&wfull)), "r"(kTc5Rows) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // ring form: this thread's nibbles and scales of the first kPD groups, requested before the scale
+  // this thread's nibbles and scales of the first kPD groups, requested before the scale
   // pass so that both round trips overlap (volatile loads: issued where written)
   uint2 q[kPD];
   float sc[kPD];
@@ -261,38 +241,13 @@ __device__ __forceinline__ Tc5Acc tc5_tile_rows(const Rows& rows, const __half* 
     }
   };
   float m = 0.f;
-  if constexpr (XRES) {
-    __syncthreads();  // the barriers are initialised
-    if (producer && half == 0) {  // the row's nibbles of groups g0 .. g0 + ng - 1: one bulk copy
-      const uint32_t wb = su32(&wfull);
-      if (row_ok) {
-        const uint32_t bytes = 16u * (uint32_t)ng;
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(wb), "r"(bytes) : "memory");
-        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                         su32(wraw + (size_t)lr * rs)),
-                     "l"(wrow + 16 * g0), "r"(bytes), "r"(wb)
-                     : "memory");
-      } else {
-        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(wb) : "memory");
-      }
-    }
-    if (producer) {
-#pragma unroll 8
-      for (int g = half; g < ng; g += 2) {
-        const float v = row_ok ? __ldg(srow + g0 + g) : 0.f;
-        sraw[lr * (ng + 1) + g] = v;
-        m = fmaxf(m, fabsf(v));
-      }
-    }
-  } else {
-    if (producer) {
+  if (producer) {
 #pragma unroll
-      for (int i = 0; i < kPD; ++i) fetch(i, q[i], sc[i]);
-    }
-    if (row_ok) {
+    for (int i = 0; i < kPD; ++i) fetch(i, q[i], sc[i]);
+  }
+  if (row_ok) {
 #pragma unroll 8
-      for (int g = half; g < ng; g += 2) m = fmaxf(m, fabsf(__ldg(srow + g0 + g)));
-    }
+    for (int g = half; g < ng; g += 2) m = fmaxf(m, fabsf(__ldg(srow + g0 + g)));
   }
   m = warp_max(m);
   if (lane == 0 && producer) smax[warp] = m;
@@ -348,40 +303,20 @@ __device__ __forceinline__ Tc5Acc tc5_tile_rows(const Rows& rows, const __half* 
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&full[s])) : "memory");
     };
-    if constexpr (XRES) {
-      if (!bar_wait(su32(&wfull), 0, limit)) {  // the raw rows have landed (every thread observes it)
-        atomicExch(err, 1);
-        ok = false;
-      }
-      for (int k = 0; k < nst; ++k) {
-        const int s = k % S;
-        stage_free(k, s);
-        uint8_t* st = smem + (size_t)s * kStageA;
+    // the nibbles and scales of group c + kPD are requested while group c is dequantised, so that the
+    // global-load latency overlaps the groups in between (rows past the matrix hold weight 0)
+    for (int cb = 0; cb < ng; cb += kPD) {
 #pragma unroll
-        for (int u = 0; u < G; ++u) {
-          const int c = G * k + u;
-          if (c >= ng) break;
-          dequant(st + u * 2 * kTc5ABytes, *reinterpret_cast<const uint2*>(wraw + (size_t)lr * rs + 16 * c + 8 * half),
-                  sraw[lr * (ng + 1) + c] * up);
-        }
+      for (int i = 0; i < kPD; ++i) {
+        const int c = cb + i;
+        if (c >= ng) break;
+        const int s = c % S;
+        stage_free(c, s);
+        const uint2 qc = q[i];
+        const float scale = sc[i] * up;
+        fetch(c + kPD, q[i], sc[i]);
+        dequant(smem + (size_t)s * kStageA, qc, scale);
         stage_full(s);
-      }
-    } else {
-      // the nibbles and scales of group c + kPD are requested while group c is dequantised, so that the
-      // global-load latency overlaps the groups in between (rows past the matrix hold weight 0)
-      for (int cb = 0; cb < ng; cb += kPD) {
-#pragma unroll
-        for (int i = 0; i < kPD; ++i) {
-          const int c = cb + i;
-          if (c >= ng) break;
-          const int s = c % S;
-          stage_free(c, s);
-          const uint2 qc = q[i];
-          const float scale = sc[i] * up;
-          fetch(c + kPD, q[i], sc[i]);
-          dequant(smem + (size_t)s * kStageA, qc, scale);
-          stage_full(s);
-        }
       }
     }
   } else if (warp == kTc5Threads / 32 + 1) {
@@ -391,25 +326,15 @@ __device__ __forceinline__ Tc5Acc tc5_tile_rows(const Rows& rows, const __half* 
       side(lane);
     } else {
       if (pdl) asm volatile("griddepcontrol.wait;" ::: "memory");  // the activations come from the previous kernel
-      if constexpr (XRES)
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&xfull)),
-                     "r"(2u * xbytes * (uint32_t)ng)
-                     : "memory");
       for (int c = 0; c < ng; ++c) {
-        uint32_t bar, dst;
-        if constexpr (XRES) {  // every group at once, all on one barrier
-          bar = su32(&xfull);
-          dst = su32(xs + (size_t)c * 2 * kB);
-        } else {  // a ring: wait until the MMAs of S groups ago released the stage
-          const int s = c % S;
-          if (ok && c >= S && !bar_wait(su32(&empty[s]), ((c / S) - 1) & 1, limit)) {
-            atomicExch(err, 1);
-            ok = false;
-          }
-          bar = su32(&full[s]);
-          dst = su32(xs + (size_t)s * 2 * kB);
-          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2u * xbytes) : "memory");
+        // a ring: wait until the MMAs of S groups ago released the stage
+        const int s = c % S;
+        if (ok && c >= S && !bar_wait(su32(&empty[s]), ((c / S) - 1) & 1, limit)) {
+          atomicExch(err, 1);
+          ok = false;
         }
+        const uint32_t bar = su32(&full[s]), dst = su32(xs + (size_t)s * 2 * kB);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2u * xbytes) : "memory");
         const size_t src = ((size_t)(g0 + c) * T8 + t0 / 8) * 256;  // in halves
         asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                          dst),
@@ -422,40 +347,30 @@ __device__ __forceinline__ Tc5Acc tc5_tile_rows(const Rows& rows, const __half* 
       }
     }
   } else if (lane == 0) {
-    // ---- the MMA warp: per stage, wait until full, issue w_hi x_hi + w_hi x_lo + w_lo x_hi for each of
-    // its groups, release the stage
+    // ---- the MMA warp: per group, wait until full, issue w_hi x_hi + w_hi x_lo + w_lo x_hi, release
     const uint32_t idesc = idesc_f16(N), idesc2 = idesc_f16(kAcc);
-    if (XRES && !bar_wait(su32(&xfull), 0, limit)) {
-      atomicExch(err, 1);
-      ok = false;
-    }
-    for (int k = 0; k < nst && ok; ++k) {
-      const int s = k % S;
-      if (!bar_wait(su32(&full[s]), (k / S) & 1, limit)) {
+    for (int c = 0; c < ng && ok; ++c) {
+      const int s = c % S;
+      if (!bar_wait(su32(&full[s]), (c / S) & 1, limit)) {
         atomicExch(err, 1);
         ok = false;
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t st = su32(smem + (size_t)s * kStageA);
+      const uint32_t xb = su32(xs + (size_t)s * 2 * kB);
 #pragma unroll
-      for (int u = 0; u < G; ++u) {
-        const int c = G * k + u;
-        if (c >= ng) break;
-        const uint32_t st = su32(smem + (size_t)s * kStageA + u * 2 * kTc5ABytes);
-        const uint32_t xb = su32(xs + (size_t)(XRES ? c : s) * 2 * kB);
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {  // two K = 16 steps of the group: 32 bytes into each 64-byte row
-          const uint64_t ah = sdesc(st + j * 32), al = sdesc(st + kTc5ABytes + j * 32);
-          const uint64_t bh = sdesc(xb + j * 32);
-          const uint64_t bl = sdesc(xb + kB + j * 32);
-          if constexpr (kMerge) {
-            mma_f16(dtmem, ah, bh, idesc2, (c > 0 || j > 0) ? 1u : 0u);  // columns [0, N): x_hi, [N, 2N): x_lo
-            mma_f16(dtmem, al, bh, idesc, 1u);
-          } else {
-            mma_f16(dtmem, ah, bh, idesc, (c > 0 || j > 0) ? 1u : 0u);
-            mma_f16(dtmem, ah, bl, idesc, 1u);
-            mma_f16(dtmem, al, bh, idesc, 1u);
-          }
+      for (int j = 0; j < 2; ++j) {  // two K = 16 steps of the group: 32 bytes into each 64-byte row
+        const uint64_t ah = sdesc(st + j * 32), al = sdesc(st + kTc5ABytes + j * 32);
+        const uint64_t bh = sdesc(xb + j * 32);
+        const uint64_t bl = sdesc(xb + kB + j * 32);
+        if constexpr (kMerge) {
+          mma_f16(dtmem, ah, bh, idesc2, (c > 0 || j > 0) ? 1u : 0u);  // columns [0, N): x_hi, [N, 2N): x_lo
+          mma_f16(dtmem, al, bh, idesc, 1u);
+        } else {
+          mma_f16(dtmem, ah, bh, idesc, (c > 0 || j > 0) ? 1u : 0u);
+          mma_f16(dtmem, ah, bl, idesc, 1u);
+          mma_f16(dtmem, al, bh, idesc, 1u);
         }
       }
       mma_commit(su32(&empty[s]));
@@ -470,18 +385,208 @@ __device__ __forceinline__ Tc5Acc tc5_tile_rows(const Rows& rows, const __half* 
   }
   if (tid == kTc5Threads + 32) {
     // no bulk copy of this CTA is left in flight (at once, unless a wait above ran out)
-    if constexpr (XRES) {
-      if (!bar_wait(su32(&xfull), 0, limit) || !bar_wait(su32(&wfull), 0, limit)) {
+    for (int s = 0; s < S && s < ng; ++s) {  // the last use of each stage
+      const int gl = s + ((ng - 1 - s) / S) * S;
+      if (!bar_wait(su32(&full[s]), (gl / S) & 1, limit)) {
         atomicExch(err, 1);
         ok = false;
       }
+    }
+  }
+  ok = __syncthreads_and(ok);
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  return Tc5Acc{dtmem, down, ok};
+}
+
+// ---- Pre-expanded weights.  tc5_expand_kernel writes, once at load, every (128-row tile, group) of a Q4
+// matrix as the exact shared-memory image the producers would build: [w_hi 8 KB][w_lo 8 KB] in the
+// swizzled layout, with the tile's 2^E factor applied (E from the largest |scale| of the tile's rows over
+// all groups), and the tile's 2^-E in `down`.  The values equal those of tc5_tile_rows (whose E spans the
+// CTA's groups only), so a tile computes the same products, now fed by one bulk copy per group.
+constexpr int kTc5GroupImage = 2 * kTc5ABytes;  // bytes of one (tile, group) image
+template <class Rows>
+__global__ void __launch_bounds__(256) tc5_expand_kernel(Rows rows, int NG, uint8_t* __restrict__ out,
+                                                         float* __restrict__ down) {
+  __shared__ float smax[8];
+  const int tile = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, lr = tid >> 1, half = tid & 1;
+  const uint8_t* wrow = nullptr;
+  const float* srow = nullptr;
+  const bool ok = rows.at_tile(tile).row(lr, wrow, srow);
+  float m = 0.f;
+  if (ok)
+    for (int k = half; k < NG; k += 2) m = fmaxf(m, fabsf(srow[k]));
+  m = warp_max(m);
+  if ((tid & 31) == 0) smax[tid >> 5] = m;
+  __syncthreads();
+  m = 0.f;
+  for (int w = 0; w < 8; ++w) m = fmaxf(m, smax[w]);
+  int e2 = 0;
+  if (m > 0.f) (void)frexpf(8.f * m, &e2);
+  const int E = 14 - e2;
+  const float up = ldexpf(1.f, E);
+  if (g == 0 && tid == 0) down[tile] = ldexpf(1.f, -E);
+  uint2 q = make_uint2(0x88888888u, 0x88888888u);
+  float scale = 0.f;
+  if (ok) {
+    q = *reinterpret_cast<const uint2*>(wrow + 16 * g + 8 * half);
+    scale = srow[g] * up;
+  }
+  const float sh = __uint_as_float(__float_as_uint(scale) & 0xFFFF0000u), sl = scale - sh;
+  const __half2 mh = __floats2half2_rn(sh, sh * 0.0625f), ml = __floats2half2_rn(sl, sl * 0.0625f);
+  uint8_t* img = out + ((size_t)tile * NG + g) * kTc5GroupImage;
+  const uint32_t qw[2] = {q.x, q.y};
+#pragma unroll
+  for (int cc = 0; cc < 2; ++cc) {
+    __half2 hi[4], lo[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const __half2 v = nib_pair(qw[cc], (uint32_t)(p | (4 << 4) | (p << 8) | (4 << 12)));
+      hi[p] = __hmul2(v, mh);
+      lo[p] = __hmul2(v, ml);
+    }
+    const int rb = sw64_at(lr, 2 * half + cc);
+    *reinterpret_cast<uint4*>(img + rb) = *reinterpret_cast<const uint4*>(hi);
+    *reinterpret_cast<uint4*>(img + kTc5ABytes + rb) = *reinterpret_cast<const uint4*>(lo);
+  }
+}
+
+// Shared-memory bytes of tc5_tile_pre<N, S> over ng groups: S group images and every group's
+// activation halves.
+__host__ __device__ constexpr size_t tc5_smem_pre(int N, int S, int ng) {
+  return (size_t)S * kTc5GroupImage + (size_t)ng * 2 * N * 64 + 1024;
+}
+
+// One 128-row x N-token tile over groups g0 .. g0 + ng - 1 of a pre-expanded matrix: img points at the
+// tile's first group image, down is its 2^-E.  No producer warps: the copy thread brings the group images
+// through an S-stage ring (the first S before the wait for the previous kernel, which the weights do not
+// need) and every group's activation halves at once; the MMA thread is the one of tc5_tile_rows.  Lanes
+// 1 .. 31 of the copy warp run side(lane) as there.  Waits are bounded; every thread must then call
+// tc5_release.
+template <int N, int S, class Side = Tc5NoSide>
+__device__ __forceinline__ Tc5Acc tc5_tile_pre(const uint8_t* __restrict__ img, float down,
+                                               const __half* __restrict__ xh, const __half* __restrict__ xl, int T8,
+                                               int t0, int g0, int ng, uint8_t* smem, bool pdl, int* err,
+                                               const Side& side = Tc5NoSide{}) {
+  constexpr int kB = N * 64;
+  __shared__ __align__(8) uint64_t full[S], empty[S], done, xfull;
+  __shared__ uint32_t tmem_base;
+  smem += (1024u - (su32(smem) & 1023u)) & 1023u;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint64_t limit = kWaitNs;
+  constexpr bool kMerge = N <= 128;
+  constexpr int kAcc = kMerge ? 2 * N : N;
+  constexpr uint32_t kCols = kAcc < 32 ? 32 : kAcc;
+  const uint32_t xbytes = (uint32_t)min(N / 8, T8 - t0 / 8) * 512u;
+  uint8_t* const xs = smem + (size_t)S * kTc5GroupImage;
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base)),
+                 "r"(kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&full[s])) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&empty[s])) : "memory");
+    }
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&done)) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&xfull)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t dtmem = tmem_base;
+  bool ok = true;
+  auto load_image = [&](int c) {
+    const uint32_t bar = su32(&full[c % S]);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"((uint32_t)kTc5GroupImage)
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     su32(smem + (size_t)(c % S) * kTc5GroupImage)),
+                 "l"(img + (size_t)c * kTc5GroupImage), "r"((uint32_t)kTc5GroupImage), "r"(bar)
+                 : "memory");
+  };
+  if (warp == kTc5Threads / 32 + 1) {
+    if (lane != 0) {
+      if (pdl) asm volatile("griddepcontrol.wait;" ::: "memory");
+      side(lane);
     } else {
-      for (int s = 0; s < S && s < ng; ++s) {  // the last use of each stage
-        const int gl = s + ((ng - 1 - s) / S) * S;
-        if (!bar_wait(su32(&full[s]), (gl / S) & 1, limit)) {
+      for (int c = 0; c < ng && c < S; ++c) load_image(c);  // weights: no wait for the previous kernel
+      if (pdl) asm volatile("griddepcontrol.wait;" ::: "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&xfull)),
+                   "r"(2u * xbytes * (uint32_t)ng)
+                   : "memory");
+      for (int c = 0; c < ng; ++c) {
+        const size_t src = ((size_t)(g0 + c) * T8 + t0 / 8) * 256;  // in halves
+        const uint32_t dst = su32(xs + (size_t)c * 2 * kB), bar = su32(&xfull);
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         dst),
+                     "l"(xh + src), "r"(xbytes), "r"(bar)
+                     : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         dst + kB),
+                     "l"(xl + src), "r"(xbytes), "r"(bar)
+                     : "memory");
+      }
+      for (int c = S; c < ng; ++c) {  // the ring: a stage is refilled once its MMAs are done
+        if (!bar_wait(su32(&empty[c % S]), ((c / S) - 1) & 1, limit)) {
           atomicExch(err, 1);
           ok = false;
+          break;
         }
+        load_image(c);
+      }
+    }
+  } else if (warp == kTc5Threads / 32 && lane == 0) {
+    const uint32_t idesc = idesc_f16(N), idesc2 = idesc_f16(kAcc);
+    if (!bar_wait(su32(&xfull), 0, limit)) {
+      atomicExch(err, 1);
+      ok = false;
+    }
+    for (int c = 0; c < ng && ok; ++c) {
+      const int s = c % S;
+      if (!bar_wait(su32(&full[s]), (c / S) & 1, limit)) {
+        atomicExch(err, 1);
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t st = su32(smem + (size_t)s * kTc5GroupImage);
+      const uint32_t xb = su32(xs + (size_t)c * 2 * kB);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint64_t ah = sdesc(st + j * 32), al = sdesc(st + kTc5ABytes + j * 32);
+        const uint64_t bh = sdesc(xb + j * 32);
+        const uint64_t bl = sdesc(xb + kB + j * 32);
+        if constexpr (kMerge) {
+          mma_f16(dtmem, ah, bh, idesc2, (c > 0 || j > 0) ? 1u : 0u);
+          mma_f16(dtmem, al, bh, idesc, 1u);
+        } else {
+          mma_f16(dtmem, ah, bh, idesc, (c > 0 || j > 0) ? 1u : 0u);
+          mma_f16(dtmem, ah, bl, idesc, 1u);
+          mma_f16(dtmem, al, bh, idesc, 1u);
+        }
+      }
+      mma_commit(su32(&empty[s]));
+    }
+    mma_commit(su32(&done));
+  }
+  __syncwarp();
+  if (lane == 0 && !bar_wait(su32(&done), 0, limit)) {
+    atomicExch(err, 1);
+    ok = false;
+  }
+  if (tid == kTc5Threads + 32) {  // no bulk copy of this CTA is left in flight
+    if (!bar_wait(su32(&xfull), 0, limit)) {
+      atomicExch(err, 1);
+      ok = false;
+    }
+    for (int s = 0; s < S && s < ng; ++s) {  // the last image copied into each stage
+      const int gl = s + ((ng - 1 - s) / S) * S;
+      if (!bar_wait(su32(&full[s]), (gl / S) & 1, limit)) {
+        atomicExch(err, 1);
+        ok = false;
       }
     }
   }
@@ -495,7 +600,7 @@ template <int N, int S>
 __device__ __forceinline__ Tc5Acc tc5_tile(const uint8_t* __restrict__ W, const float* __restrict__ Sc,
                                            const __half* __restrict__ xh, const __half* __restrict__ xl, int R, int K,
                                            int T8, int r0, int t0, uint8_t* smem, bool pdl, int* err) {
-  return tc5_tile_rows<N, S, false>(Tc5Linear{W, Sc, R, K, r0}, xh, xl, T8, t0, 0, K / 32, smem, pdl, err);
+  return tc5_tile_rows<N, S>(Tc5Linear{W, Sc, R, K, r0}, xh, xl, T8, t0, 0, K / 32, smem, pdl, err);
 }
 
 // N <= 128 keeps x_hi and x_lo products in separate column halves of the accumulator.
