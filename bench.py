@@ -368,11 +368,12 @@ def run_reference(args):
         "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": wall / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f64-accumulate/f32-store", "data": DATA_TEXT,
-        "config": config_of(W, 1),
+        "config": config_of(W, ws),  # the CUDA arm's dict at the same N (same_config)
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": f"every step the whole workload: {W['prompt']}-token prefill + {W['new'] - 1} "
-                                   f"greedy decode steps (oracle/, the C restatement of engine/infer.js; "
-                                   f"{threads} threads inside each forward)"},
+                         "sample": f"every step the whole workload of one replica: {W['prompt']}-token prefill + "
+                                   f"{W['new'] - 1} greedy decode steps (oracle/, the C restatement of "
+                                   f"engine/infer.js; {threads} threads inside each forward; the host's cores "
+                                   f"serve all {ws} replicas in turn at this rate)"},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
