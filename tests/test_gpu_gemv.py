@@ -86,6 +86,32 @@ def test_gemv_dense_matches_oracle(dtype, rows, cols, cuda_ok):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16", "q8"])
+def test_gemv_dense_ragged_rows(dtype, cuda_ok):
+    """Row counts that leave a warp's last rows empty (13, 1) and activation counts below the kernel's
+    tile (3 of 4, 7 of 8, 11 of 16), against the oracle."""
+    import torch
+    P = pkg()
+    rng = np.random.default_rng(9)
+    for rows, cols in ((13, 64), (1, 32), (37, 96)):
+        w, sc = _dense_weights(dtype, rows, cols, rng)
+        dw = torch.from_numpy(np.ascontiguousarray(w)).cuda()
+        ds = torch.from_numpy(sc).cuda() if sc is not None else None
+        for m in (3, 7, 11):
+            x = rng.standard_normal((m, cols), dtype=np.float32)
+            dx = torch.from_numpy(x).cuda()
+            dy = torch.full((m, rows), float("nan"), dtype=torch.float32, device="cuda")
+            P.gemv_device(dtype, dw.data_ptr(), ds.data_ptr() if ds is not None else 0, dx.data_ptr(),
+                          dy.data_ptr(), rows, cols, m)
+            torch.cuda.synchronize()
+            y = dy.cpu().numpy()
+            for i in range(m):
+                ref = O.gemv_dense(dtype, w, sc, x[i])
+                err = np.abs(y[i] - ref).max()
+                assert err <= 1e-4 * np.abs(ref).max() + 1e-6, (dtype, rows, cols, m, i, err)
+
+
+@pytest.mark.gpu
 def test_gemv_dense_rejects_bad_arguments(cuda_ok):
     import torch
     P = pkg()
