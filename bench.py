@@ -48,8 +48,8 @@ DECODE_TRAFFIC_PER_LAUNCH = {("config1 petitgpt b1 p64 n128", "decode1"): 187_88
 # single-kernel ncu --set full capture each on `bench.py --case batched --seqs 128 --prompt 8 --new 3`
 # (the first decode step's launch; mma.sync.m16n8k16 tiles): the share of the tensor pipe they keep busy.
 BATCHED_TENSOR_PIPE = {"source": "ncu single-kernel captures: the mma.sync GEMMs and attention on a 128-row decode "
-                                 "step; the tcgen05 lm_head (the default) on a 128-row forward "
-                                 "(profiles/lwe_lm_tc5_smollm2_135m.md)", "unit": "% of peak",
+                                 "step; the tcgen05 lm_head (the default) on a 128-row forward of "
+                                 "`bench.py --case batched --seqs 256 --prompt 8 --new 3`", "unit": "% of peak",
                        "lwe_gemm_qkv<2,4>": 11.9, "lwe_gemm_w13<2,1>": 20.9, "lwe_gemm_resid<2,4>": 5.0,
                        "lwe_lm_tc5<128,6>": 27.6, "lwe_attention<3,1>": 0.0}
 # dram__bytes_read.sum + dram__bytes_write.sum of one cold gemv_q4_bulk_kernel launch on the lm_head
