@@ -58,13 +58,22 @@ class Bundle:
         return np.frombuffer(self.buffer, np.float32, t["scaleNbytes"] // 4, self.payload_off + t["scaleOffset"])
 
     def dequant(self, name: str) -> np.ndarray:
-        """engine/weights.js:74-126 (q4 and f32 branches), as float32 [rows, cols]."""
+        """engine/weights.js:74-126, as float32 [rows, cols]."""
         t = self.tensors[name]
         rows, cols = (1, t["shape"][0]) if len(t["shape"]) == 1 else t["shape"]
-        if t["storage"] == "f32":
+        st = t["storage"]
+        if st == "f32":
             return self.f32(name).reshape(rows, cols).copy()
-        if t["storage"] != "q4":
-            raise ValueError(t["storage"])
+        if st in ("f16", "bf16"):
+            u = np.frombuffer(self.buffer, np.uint16, t["nbytes"] // 2, self.payload_off + t["offset"])
+            if st == "f16":
+                return u.view(np.float16).astype(np.float32).reshape(rows, cols)
+            return (u.astype(np.uint32) << 16).view(np.float32).reshape(rows, cols)
+        if st == "q8":
+            q = np.frombuffer(self.buffer, np.int8, t["nbytes"], self.payload_off + t["offset"]).reshape(rows, cols)
+            return (q.astype(np.float32) * self.scales(name).reshape(rows, 1)).astype(np.float32)
+        if st != "q4":
+            raise ValueError(st)
         return dequant_q4(self.u8(name).reshape(rows, cols // 2), self.scales(name).reshape(rows, -1),
                           t.get("group") or GROUP)
 
@@ -131,6 +140,16 @@ def dequant_q4(packed: np.ndarray, scales: np.ndarray, group: int = GROUP) -> np
     return (q.reshape(rows, ng, group) * scales.reshape(rows, ng, 1)).reshape(rows, -1).astype(np.float32)
 
 
+def quant_q8(mat: np.ndarray):
+    """Symmetric per-row int8 (the layout engine/weights.js:96-105 reads): scale = amax / 127,
+    q = clip(rint(w / scale), -127, 127).  Rows of zeros get scale 1."""
+    mat = np.ascontiguousarray(mat, dtype=np.float32)
+    amax = np.abs(mat).max(axis=1)
+    scales = np.where(amax > 0, amax / np.float32(127.0), np.float32(1.0)).astype(np.float32)
+    q = np.clip(np.rint(mat / scales[:, None]), -127, 127).astype(np.int8)
+    return q, scales
+
+
 def _entries_and_payload(tensors):
     """tools/convert_hf_to_pgw.py:37-72 — returns (table entries, payload bytes)."""
     entries, blobs = [], bytearray()
@@ -164,15 +183,39 @@ def _entries_and_payload(tensors):
                 "offset": off,
                 "nbytes": data.nbytes,
             })
+        elif storage in ("f16", "bf16"):  # 16-bit words, read as engine/weights.js:82-95 does
+            a = np.ascontiguousarray(arr, dtype=np.float32)
+            if storage == "f16":
+                words = a.astype(np.float16).view(np.uint16)
+            else:  # round to nearest even on the top 16 bits
+                u = a.view(np.uint32).astype(np.uint64)
+                words = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+            off = len(blobs)
+            blobs += words.tobytes()
+            entries.append({"name": name, "shape": list(a.shape), "kind": storage, "storage": storage,
+                            "offset": off, "nbytes": words.nbytes})
+        elif storage == "q8":  # int8 rows and one f32 scale per row (engine/weights.js:96-105)
+            if isinstance(arr, tuple):
+                q, scales = arr
+            else:
+                q, scales = quant_q8(np.asarray(arr))
+            scale_off = len(blobs)
+            blobs += scales.tobytes()
+            data_off = len(blobs)
+            blobs += q.tobytes()
+            entries.append({"name": name, "shape": [int(q.shape[0]), int(q.shape[1])], "kind": "q8",
+                            "storage": "q8", "scaleOffset": scale_off, "scaleNbytes": scales.nbytes,
+                            "offset": data_off, "nbytes": q.nbytes})
         else:
             raise ValueError(storage)
     return entries, bytes(blobs)
 
 
-def write_pgw(cfg: dict, tensors, path: str | None = None) -> bytes:
-    """Serialise a PGW1 Q4 file (tools/convert_hf_to_pgw.py:123-144; GPT-2 header
+def write_pgw(cfg: dict, tensors, path: str | None = None, kind: str = "q4") -> bytes:
+    """Serialise a PGW1 file (tools/convert_hf_to_pgw.py:123-144; GPT-2 header
     tools/convert_gpt2_to_pgw.py:171-178).  ``tensors`` is a list of (name, array, storage) where a
-    q4 array may also be a precomputed (packed, scales) tuple."""
+    q4 array may also be a precomputed (packed, scales) tuple and a q8 array a (q, scales) tuple;
+    ``kind`` is the header's dtype byte (engine/weights.js:14)."""
     entries, payload = _entries_and_payload(tensors)
     table = json.dumps(entries, separators=(",", ":")).encode("utf-8")
     table_off = 256
@@ -181,7 +224,7 @@ def write_pgw(cfg: dict, tensors, path: str | None = None) -> bytes:
     gpt2 = cfg.get("arch") == "gpt2"
     header = bytearray(256)
     header[0:4] = b"PGW1"
-    header[4] = 4
+    header[4] = {v: k for k, v in DTYPE_CODE.items()}[kind]
     header[5] = 1 if gpt2 else 0
     struct.pack_into("<8I", header, 8, cfg["vocabSize"], cfg["nLayers"], cfg["dModel"], cfg["nHeads"],
                      cfg["nKvHeads"], cfg["dFf"], cfg["maxSeqLen"], 1 if gpt2 else GROUP)
@@ -230,54 +273,58 @@ def _normal(rng, shape, std=0.02):
     return rng.standard_normal(shape, dtype=np.float32) * np.float32(std)
 
 
-def llama_tensor_list(cfg: dict, seed: int, std: float = 0.02):
-    """Tensors in tools/convert_hf_to_pgw.py:104-122 order, N(0, std) weights, unit norm gains."""
+def llama_tensor_list(cfg: dict, seed: int, std: float = 0.02, storage: str = "q4"):
+    """Tensors in tools/convert_hf_to_pgw.py:104-122 order, N(0, std) weights stored as ``storage``,
+    unit norm gains."""
     rng = np.random.default_rng(seed)
     d, ff, V = cfg["dModel"], cfg["dFf"], cfg["vocabSize"]
     hd = d // cfg["nHeads"]
     kv = cfg["nKvHeads"] * hd
-    out = [("lm_head", _normal(rng, (V, d), std), "q4")]
+    out = [("lm_head", _normal(rng, (V, d), std), storage)]
     ones = np.ones(d, np.float32)
     for i in range(cfg["nLayers"]):
         out.append((f"blocks.{i}.norm1", ones, "f32"))
-        out.append((f"blocks.{i}.attn.qkv", _normal(rng, (d + 2 * kv, d), std), "q4"))
-        out.append((f"blocks.{i}.attn.proj", _normal(rng, (d, d), std), "q4"))
+        out.append((f"blocks.{i}.attn.qkv", _normal(rng, (d + 2 * kv, d), std), storage))
+        out.append((f"blocks.{i}.attn.proj", _normal(rng, (d, d), std), storage))
         out.append((f"blocks.{i}.norm2", ones, "f32"))
-        out.append((f"blocks.{i}.mlp.w1", _normal(rng, (ff, d), std), "q4"))
-        out.append((f"blocks.{i}.mlp.w3", _normal(rng, (ff, d), std), "q4"))
-        out.append((f"blocks.{i}.mlp.w2", _normal(rng, (d, ff), std), "q4"))
+        out.append((f"blocks.{i}.mlp.w1", _normal(rng, (ff, d), std), storage))
+        out.append((f"blocks.{i}.mlp.w3", _normal(rng, (ff, d), std), storage))
+        out.append((f"blocks.{i}.mlp.w2", _normal(rng, (d, ff), std), storage))
     out.append(("norm_f", ones, "f32"))
     return out
 
 
-def gpt2_tensor_list(cfg: dict, seed: int, std: float = 0.02):
-    """Tensors in tools/convert_gpt2_to_pgw.py:134-164 order; scale_factors 1, LN [1; 0], biases 0."""
+def gpt2_tensor_list(cfg: dict, seed: int, std: float = 0.02, storage: str = "q4"):
+    """Tensors in tools/convert_gpt2_to_pgw.py:134-164 order (weights stored as ``storage``);
+    scale_factors 1, LN [1; 0], biases 0."""
     rng = np.random.default_rng(seed)
     d, ff, V, ms = cfg["dModel"], cfg["dFf"], cfg["vocabSize"], cfg["maxSeqLen"]
     ln = np.concatenate([np.ones(d, np.float32), np.zeros(d, np.float32)])
     out = [("scale_factors", np.ones(d, np.float32), "f32"),
-           ("lm_head", _normal(rng, (V, d), std), "q4"),
+           ("lm_head", _normal(rng, (V, d), std), storage),
            ("wpe", _normal(rng, (ms, d), std), "f32"),
            ("ln_f", ln, "f32")]
     for i in range(cfg["nLayers"]):
         out.append((f"blocks.{i}.ln1", ln, "f32"))
-        out.append((f"blocks.{i}.attn.qkv", _normal(rng, (3 * d, d), std), "q4"))
+        out.append((f"blocks.{i}.attn.qkv", _normal(rng, (3 * d, d), std), storage))
         out.append((f"blocks.{i}.attn.qkv_bias", np.zeros(3 * d, np.float32), "f32"))
-        out.append((f"blocks.{i}.attn.proj", _normal(rng, (d, d), std), "q4"))
+        out.append((f"blocks.{i}.attn.proj", _normal(rng, (d, d), std), storage))
         out.append((f"blocks.{i}.attn.proj_bias", np.zeros(d, np.float32), "f32"))
         out.append((f"blocks.{i}.ln2", ln, "f32"))
-        out.append((f"blocks.{i}.mlp.fc", _normal(rng, (ff, d), std), "q4"))
+        out.append((f"blocks.{i}.mlp.fc", _normal(rng, (ff, d), std), storage))
         out.append((f"blocks.{i}.mlp.fc_bias", np.zeros(ff, np.float32), "f32"))
-        out.append((f"blocks.{i}.mlp.proj", _normal(rng, (d, ff), std), "q4"))
+        out.append((f"blocks.{i}.mlp.proj", _normal(rng, (d, ff), std), storage))
         out.append((f"blocks.{i}.mlp.proj_bias", np.zeros(d, np.float32), "f32"))
     return out
 
 
-def synthetic_pgw(name_or_cfg, seed: int, cache_dir: str | None = None) -> bytes:
-    """Seeded synthetic PGW1 Q4 file for a named config (see CONFIGS) or an explicit cfg dict.
-    When ``cache_dir`` is given the file is cached there under a hash of (cfg, seed)."""
+def synthetic_pgw(name_or_cfg, seed: int, cache_dir: str | None = None, storage: str = "q4") -> bytes:
+    """Seeded synthetic PGW1 file for a named config (see CONFIGS) or an explicit cfg dict, its matrices
+    stored as ``storage`` (q4 by default; f32 / f16 / bf16 / q8 for the other kinds).  When
+    ``cache_dir`` is given the file is cached there under a hash of (cfg, seed, storage)."""
     cfg = dict(CONFIGS[name_or_cfg]) if isinstance(name_or_cfg, str) else dict(name_or_cfg)
-    key = hashlib.sha1(json.dumps([cfg, seed], sort_keys=True).encode()).hexdigest()[:16]
+    key = hashlib.sha1(json.dumps([cfg, seed] if storage == "q4" else [cfg, seed, storage],
+                                  sort_keys=True).encode()).hexdigest()[:16]
     path = None
     if cache_dir:
         os.makedirs(cache_dir, exist_ok=True)
@@ -286,8 +333,9 @@ def synthetic_pgw(name_or_cfg, seed: int, cache_dir: str | None = None) -> bytes
             with open(path, "rb") as f:
                 return f.read()
     std = float(cfg.get("std", 0.02))
-    tl = gpt2_tensor_list(cfg, seed, std) if cfg["arch"] == "gpt2" else llama_tensor_list(cfg, seed, std)
-    data = write_pgw(cfg, tl)
+    tl = (gpt2_tensor_list(cfg, seed, std, storage) if cfg["arch"] == "gpt2"
+          else llama_tensor_list(cfg, seed, std, storage))
+    data = write_pgw(cfg, tl, kind=storage)
     if path:
         tmp = path + f".tmp{os.getpid()}"
         with open(tmp, "wb") as f:

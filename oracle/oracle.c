@@ -43,14 +43,15 @@
 #define EPS 1e-6    /* engine/infer.js:8 */
 #define LN_EPS 1e-5 /* engine/infer.js:145 */
 
-enum { ST_F32 = 0, ST_Q4 = 4 };
+/* PGW1 storage kinds (engine/weights.js:3) */
+enum { ST_F32 = 0, ST_F16 = 1, ST_BF16 = 2, ST_Q8 = 3, ST_Q4 = 4 };
 
 typedef struct {
   char name[64];
-  int storage; /* ST_F32 or ST_Q4 */
+  int storage; /* ST_* */
   int rows, cols, group;
-  const uint8_t* data;   /* q4 packed bytes or f32 values */
-  const float* scale;    /* q4 only */
+  const uint8_t* data;   /* f32 values, 16-bit words (f16 / bf16), int8 (q8) or q4 packed bytes */
+  const float* scale;    /* q8: one per row; q4: one per group */
 } otensor;
 
 typedef struct {
@@ -236,11 +237,87 @@ void oracle_gemv_q4_f32acc(int m, int n, const uint8_t* packed, const float* sca
   }
 }
 
+/* engine/weights.js:129-158 (_rawF16ToF32, the F16_LUT entries): IEEE half to float, exact */
+static float f16_to_f32(uint16_t h) {
+  const uint32_t s = (uint32_t)(h & 0x8000) << 16;
+  int e = (h >> 10) & 0x1f;
+  uint32_t f = h & 0x3ff, bits;
+  if (e == 0) {
+    if (f == 0) {
+      bits = s;
+    } else {
+      e = 1;
+      while ((f & 0x400) == 0) {
+        f <<= 1;
+        e -= 1;
+      }
+      f &= 0x3ff;
+      bits = s | ((uint32_t)(e + 127 - 15) << 23) | (f << 13);
+    }
+  } else if (e == 31) {
+    bits = s | 0x7f800000u | (f << 13);
+  } else {
+    bits = s | ((uint32_t)(e + 127 - 15) << 23) | (f << 13);
+  }
+  float v;
+  memcpy(&v, &bits, 4);
+  return v;
+}
+/* gemvBf16's conversion (engine/infer.js:66-77): the 16 bits become the top of an f32 */
+static float bf16_to_f32(uint16_t h) {
+  const uint32_t bits = (uint32_t)h << 16;
+  float v;
+  memcpy(&v, &bits, 4);
+  return v;
+}
+
+/* gemvF32 / gemvF16 / gemvBf16 / gemvQ8 (engine/infer.js:10-86): a double accumulator (the JS `let s`)
+   per row, products of f32 values in double, gemvF32's 8-way unrolled order, q8's row scale after the
+   sum; each row stored as f32. */
+static void gemv_dense(const otensor* w, const float* x, float* y) {
+  const int n = w->cols;
+  for (int i = 0; i < w->rows; i++) {
+    double s = 0;
+    if (w->storage == ST_F32) {
+      const float* r = (const float*)w->data + (size_t)i * n;
+      int k = 0;
+      for (; k < n - 7; k += 8) {
+        s += (double)r[k] * x[k];
+        s += (double)r[k + 1] * x[k + 1];
+        s += (double)r[k + 2] * x[k + 2];
+        s += (double)r[k + 3] * x[k + 3];
+        s += (double)r[k + 4] * x[k + 4];
+        s += (double)r[k + 5] * x[k + 5];
+        s += (double)r[k + 6] * x[k + 6];
+        s += (double)r[k + 7] * x[k + 7];
+      }
+      for (; k < n; k++) s += (double)r[k] * x[k];
+    } else if (w->storage == ST_F16) {
+      const uint16_t* r = (const uint16_t*)w->data + (size_t)i * n;
+      for (int k = 0; k < n; k++) s += (double)f16_to_f32(r[k]) * x[k];
+    } else if (w->storage == ST_BF16) {
+      const uint16_t* r = (const uint16_t*)w->data + (size_t)i * n;
+      for (int k = 0; k < n; k++) s += (double)bf16_to_f32(r[k]) * x[k];
+    } else { /* ST_Q8 */
+      const int8_t* r = (const int8_t*)w->data + (size_t)i * n;
+      for (int k = 0; k < n; k++) s += (double)r[k] * x[k];
+      s = s * w->scale[i];
+    }
+    y[i] = (float)s;
+  }
+}
+
+/* engine/infer.js:337-345 (gemv, dispatched on the tensor's storage) */
+static void gemv_any(const oracle_model* m, const otensor* w, const float* x, float* y) {
+  if (w->storage == ST_Q4)
+    gemv_q4_pool(m->pool, w->rows, w->cols, w->data, w->scale, w->group, x, y);
+  else
+    gemv_dense(w, x, y);
+}
+
 /* engine/infer.js:118-132 — t independent GEMVs */
 static void gemm_q4(const oracle_model* m, const otensor* w, int t, const float* x, float* y) {
-  for (int i = 0; i < t; i++)
-    gemv_q4_pool(m->pool, w->rows, w->cols, w->data, w->scale, w->group, x + (size_t)i * w->cols,
-                 y + (size_t)i * w->rows);
+  for (int i = 0; i < t; i++) gemv_any(m, w, x + (size_t)i * w->cols, y + (size_t)i * w->rows);
 }
 
 /* ------------------------------------------------------------------------------------------ */
@@ -503,7 +580,7 @@ oracle_model* oracle_create(const int* cfg_i, const double* cfg_d, int n_tensors
 
 /* Returns 0 when every tensor the forward needs is present. */
 int oracle_check(const oracle_model* m) {
-  if (!m->lm_head || m->lm_head->storage != ST_Q4 || !m->norm_f) return -1;
+  if (!m->lm_head || !m->norm_f) return -1;
   for (int l = 0; l < m->c.n_layers; l++) {
     if (!m->qkv[l] || !m->proj[l] || !m->w1[l] || !m->w2[l] || !m->norm1[l] || !m->norm2[l]) return -2 - l;
     if (m->c.arch == 0 && !m->w3[l]) return -2 - l;
@@ -546,10 +623,17 @@ void oracle_reset(oracle_model* m) {
 int oracle_cache_len(const oracle_model* m) { return m->cache_len; }
 void oracle_set_cache_len(oracle_model* m, int n) { m->cache_len = n; }
 
-/* engine/infer.js:395-420 (q4 branch) */
+/* engine/infer.js:395-420 (q8 and q4 branches) */
 static void embed_row_quant(const oracle_model* m, int id, float* row) {
   const otensor* w = m->lm_head;
-  const int n = m->c.d_model, group = w->group, ng = n / group, packedRow = n / 2;
+  const int n = m->c.d_model, group = w->group, packedRow = n / 2;
+  int ng = n / group;
+  if (w->storage == ST_Q8) {
+    const float sc = w->scale[id];
+    const int8_t* q = (const int8_t*)w->data + (size_t)id * n;
+    for (int i = 0; i < n; i++) row[i] = (float)((double)q[i] * sc);
+    ng = 0;
+  }
   for (int g = 0; g < ng; g++) {
     const float sc = w->scale[(size_t)id * ng + g];
     const uint8_t* base = w->data + (size_t)id * packedRow + g * (group / 2);
@@ -566,7 +650,20 @@ static void embed_row_quant(const oracle_model* m, int id, float* row) {
 /* engine/infer.js:360-393 */
 static void embed(const oracle_model* m, const int32_t* ids, int t, float* out, int pos0) {
   const int d = m->c.d_model;
-  for (int i = 0; i < t; i++) embed_row_quant(m, ids[i], out + (size_t)i * d);
+  const otensor* w = m->lm_head;
+  for (int i = 0; i < t; i++) {
+    float* row = out + (size_t)i * d;
+    const size_t off = (size_t)ids[i] * d;
+    if (w->storage == ST_F32) {
+      memcpy(row, (const float*)w->data + off, (size_t)d * sizeof(float));
+    } else if (w->storage == ST_F16) {
+      for (int k = 0; k < d; k++) row[k] = f16_to_f32(((const uint16_t*)w->data)[off + k]);
+    } else if (w->storage == ST_BF16) {
+      for (int k = 0; k < d; k++) row[k] = bf16_to_f32(((const uint16_t*)w->data)[off + k]);
+    } else {
+      embed_row_quant(m, ids[i], row);
+    }
+  }
   if (m->c.arch == 1) {
     const int maxSeq = m->c.max_seq ? m->c.max_seq : 1024;
     for (int i = 0; i < t; i++) {
@@ -720,11 +817,9 @@ int oracle_forward(oracle_model* m, const int32_t* ids, int t, int pastLen, int 
   else rms_norm(s.x, m->norm_f, s.xn, d, t);
   const otensor* lm = m->lm_head;
   if (logits_each) {
-    for (int i = 0; i < t; i++)
-      gemv_q4_pool(m->pool, lm->rows, lm->cols, lm->data, lm->scale, lm->group, s.xn + (size_t)i * d,
-                   logits + (size_t)i * c->vocab);
+    for (int i = 0; i < t; i++) gemv_any(m, lm, s.xn + (size_t)i * d, logits + (size_t)i * c->vocab);
   } else {
-    gemv_q4_pool(m->pool, lm->rows, lm->cols, lm->data, lm->scale, lm->group, s.xn + (size_t)(t - 1) * d, logits);
+    gemv_any(m, lm, s.xn + (size_t)(t - 1) * d, logits);
   }
   scratch_free(&s);
   return 0;

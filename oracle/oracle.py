@@ -153,17 +153,18 @@ class OracleModel:
         self.cfg = cfg
         names, st, rows, cols, grp, data, scale = [], [], [], [], [], [], []
         base = self._buf.ctypes.data
+        codes = {"f32": 0, "f16": 1, "bf16": 2, "q8": 3, "q4": 4}  # engine/weights.js:3
         for e in table:
-            if e["storage"] not in ("f32", "q4"):
-                raise ValueError(f"oracle supports f32/q4 tensors, got {e['storage']}")
+            if e["storage"] not in codes:
+                raise ValueError(f"unknown tensor storage {e['storage']}")
             names.append(e["name"].encode())
-            st.append(4 if e["storage"] == "q4" else 0)
+            st.append(codes[e["storage"]])
             shp = e["shape"]
             rows.append(shp[0] if len(shp) == 2 else 1)
             cols.append(shp[1] if len(shp) == 2 else shp[0])
             grp.append(e.get("group") or 32)
             data.append(base + poff + e["offset"])
-            scale.append(base + poff + e["scaleOffset"] if e["storage"] == "q4" else 0)
+            scale.append(base + poff + e["scaleOffset"] if e["storage"] in ("q4", "q8") else 0)
         n = len(names)
         cfg_i = np.array([cfg["arch"], cfg["vocab"], cfg["n_layers"], cfg["d_model"], cfg["n_heads"],
                           cfg["n_kv_heads"], cfg["d_ff"], cfg["max_seq"]], np.int32)
