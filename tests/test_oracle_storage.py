@@ -83,3 +83,53 @@ def test_pgw_storage_kinds_decode_as_the_reference_reads_them():
             assert np.abs(got - w).max() <= np.abs(w).max() / 127.0
         np.testing.assert_array_equal(got, want.astype(np.float32))
         assert b.kind == storage
+
+
+GPT2_CFG = dict(arch="gpt2", vocabSize=80, nLayers=2, dModel=128, nHeads=2, nKvHeads=2, dFf=512, maxSeqLen=64,
+                std=0.1)
+
+
+@pytest.mark.parametrize("storage", ["f16", "q8"])
+def test_oracle_gpt2_storage_kinds_match_hf_float64(storage):
+    """The GPT-2 path (LayerNorm, biases, tanh GELU, wpe; engine/infer.js:383-392) on f16 and q8 files:
+    the embedding takes the stored lm_head row (q8: times its row scale, then / scale_factors)."""
+    import torch
+    from transformers import GPT2Config, GPT2LMHeadModel
+    P = pkg()
+    c = GPT2_CFG
+    data = P.synthetic_pgw(c, 17, storage=storage)
+    b = P.parse_pgw(data)
+    d = c["dModel"]
+    sf = b.f32("scale_factors").astype(np.float64)
+    hc = GPT2Config(vocab_size=c["vocabSize"], n_embd=d, n_head=c["nHeads"], n_layer=c["nLayers"],
+                    n_positions=c["maxSeqLen"], tie_word_embeddings=False)
+    m = GPT2LMHeadModel(hc).double().eval()
+    F = lambda n: torch.from_numpy(b.f32(n).astype(np.float64))
+    dq = lambda n: torch.from_numpy(b.dequant(n).astype(np.float64))
+    with torch.no_grad():
+        lm = dq("lm_head")
+        m.lm_head.weight.copy_(lm)
+        m.transformer.wte.weight.copy_(lm / torch.from_numpy(sf)[None, :] if storage == "q8" else lm)
+        m.transformer.wpe.weight.copy_(F("wpe").reshape(-1, d))
+        lnf = F("ln_f")
+        m.transformer.ln_f.weight.copy_(lnf[:d])
+        m.transformer.ln_f.bias.copy_(lnf[d:])
+        for i, blk in enumerate(m.transformer.h):
+            ln1, ln2 = F(f"blocks.{i}.ln1"), F(f"blocks.{i}.ln2")
+            blk.ln_1.weight.copy_(ln1[:d])
+            blk.ln_1.bias.copy_(ln1[d:])
+            blk.ln_2.weight.copy_(ln2[:d])
+            blk.ln_2.bias.copy_(ln2[d:])
+            blk.attn.c_attn.weight.copy_(dq(f"blocks.{i}.attn.qkv").T)
+            blk.attn.c_attn.bias.copy_(F(f"blocks.{i}.attn.qkv_bias"))
+            blk.attn.c_proj.weight.copy_(dq(f"blocks.{i}.attn.proj").T)
+            blk.attn.c_proj.bias.copy_(F(f"blocks.{i}.attn.proj_bias"))
+            blk.mlp.c_fc.weight.copy_(dq(f"blocks.{i}.mlp.fc").T)
+            blk.mlp.c_fc.bias.copy_(F(f"blocks.{i}.mlp.fc_bias"))
+            blk.mlp.c_proj.weight.copy_(dq(f"blocks.{i}.mlp.proj").T)
+            blk.mlp.c_proj.bias.copy_(F(f"blocks.{i}.mlp.proj_bias"))
+        prompt = P.seeded_prompt(9, c["vocabSize"], 23)
+        hf = m(torch.from_numpy(prompt.astype(np.int64))[None]).logits[0].numpy()
+    om = O.OracleModel(data)
+    lg = om.forward(prompt, 0, logits_each=True)
+    np.testing.assert_allclose(np.asarray(lg), hf, atol=5e-5, rtol=0)
